@@ -1,0 +1,66 @@
+// Library-level C-ABI entry points: version, error messages, device status,
+// and the programmatic-dependent-launch switch shared by every launcher.
+#include <cstdlib>
+#include <cstring>
+#include <cstdio>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "capi_util.h"
+
+namespace omni {
+
+static thread_local char g_last_error[512] = "";
+
+int set_error(int code, const char* msg) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s", msg ? msg : "");
+  return code;
+}
+
+int check_launch(cudaError_t e) {
+  if (e == cudaSuccess) return OMNI_OK;
+  std::snprintf(g_last_error, sizeof(g_last_error), "CUDA launch failed: %s", cudaGetErrorString(e));
+  return OMNI_ERR_CUDA;
+}
+
+static std::vector<StatusReader>& readers() {
+  static std::vector<StatusReader> r;
+  return r;
+}
+static std::mutex& readers_mu() {
+  static std::mutex m;
+  return m;
+}
+
+int register_status_reader(StatusReader r) {
+  std::lock_guard<std::mutex> g(readers_mu());
+  readers().push_back(r);
+  return (int)readers().size();
+}
+
+// OMNI_PDL=0 disables programmatic dependent launch (every launch then waits
+// for its predecessor in the stream, as a plain launch does).
+bool pdl_enabled() {
+  static int enabled = [] {
+    const char* v = std::getenv("OMNI_PDL");
+    return (v && v[0] == '0') ? 0 : 1;
+  }();
+  return enabled != 0;
+}
+
+}  // namespace omni
+
+extern "C" OMNI_API const char* omni_version(void) { return "omni_b200 0.1.0 sm_100a"; }
+
+extern "C" OMNI_API const char* omni_last_error(void) { return omni::g_last_error; }
+
+extern "C" OMNI_API unsigned int omni_device_status(int reset) {
+  std::lock_guard<std::mutex> g(omni::readers_mu());
+  unsigned int v = 0;
+  for (auto r : omni::readers()) {
+    unsigned int s = r(reset);
+    if (s && !v) v = s;
+  }
+  return v;
+}

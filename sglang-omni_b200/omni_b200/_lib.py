@@ -1,0 +1,124 @@
+"""ctypes binding of libomni_b200.so (the C ABI declared in include/omni_b200.h).
+
+The library is the only compute path: if it is missing or fails to load on a
+machine with a GPU, every op raises.  There is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libomni_b200.so"
+
+OMNI_OK = 0
+OMNI_ERR_UNSUPPORTED = 1
+OMNI_ERR_INVALID = 2
+OMNI_ERR_CAPACITY = 3
+OMNI_ERR_CUDA = 4
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int32
+_F32 = ctypes.c_float
+_U32 = ctypes.c_uint32
+
+# name -> argument types (all entry points return int unless listed in _RESTYPES)
+SIGNATURES: dict[str, list] = {
+    "omni_version": [],
+    "omni_last_error": [],
+    "omni_device_status": [ctypes.c_int],
+    "omni_sample_topk_topp": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I32, _I32, _P, _P],
+    "omni_predictor_sample_step": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _I32, _I32, _I32,
+                                   _P, _I64, _P, _I64, _P, _P, _P],
+    "omni_sample_sorted_seeded": [_P, _P, _I64, _I64, _P, _P, _P, _P],
+    "omni_codebook_step": [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P],
+    "omni_gather_embedding_add": [_P, _I32, _I64, _P, _I64, _P, _P, _P, _I64, _P, _P],
+    "omni_layer0_sample": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P],
+}
+_RESTYPES = {
+    "omni_version": ctypes.c_char_p,
+    "omni_last_error": ctypes.c_char_p,
+    "omni_device_status": ctypes.c_uint,
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class OmniUnsupported(Exception):
+    """The call is outside the kernel's contract (the reference returns None/False)."""
+
+
+def load() -> ctypes.CDLL:
+    """Load the CUDA library; raise if it is absent (no fallback path exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            if os.environ.get("OMNI_B200_AUTOBUILD", "1") != "0":
+                import importlib.util
+
+                spec = importlib.util.spec_from_file_location(
+                    "omni_b200_build", LIB_PATH.parent.parent / "build.py"
+                )
+                mod = importlib.util.module_from_spec(spec)
+                spec.loader.exec_module(mod)
+                mod.build()
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"omni_b200 CUDA library not found at {LIB_PATH}; build it with "
+                    "`python sglang-omni_b200/build.py`"
+                )
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = _RESTYPES.get(name, ctypes.c_int)
+        _lib = lib
+        return lib
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)
+
+
+def last_error() -> str:
+    return load().omni_last_error().decode()
+
+
+def check(rc: int, name: str) -> None:
+    """Raise the Python exception matching an OMNI_* return code."""
+    if rc == OMNI_OK:
+        return
+    msg = f"{name}: {last_error()}"
+    if rc == OMNI_ERR_UNSUPPORTED:
+        raise OmniUnsupported(msg)
+    if rc == OMNI_ERR_INVALID:
+        raise ValueError(msg)
+    if rc == OMNI_ERR_CAPACITY:
+        raise RuntimeError(msg)
+    raise RuntimeError(f"CUDA error in {msg}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args), name)
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def device_status(reset: bool = False) -> int:
+    return int(load().omni_device_status(1 if reset else 0))
