@@ -123,6 +123,115 @@ OMNI_API int omni_layer0_sample(const float* logits, int64_t rows, int64_t vocab
                                 const float* min_ps, const int64_t* seeds, const int64_t* positions,
                                 int32_t max_top_k, int64_t* out, void* stream);
 
+
+/* ======================================================================== */
+/* Projections (tcgen05 tensor cores)                                       */
+/* ======================================================================== */
+
+#define OMNI_EPI_STORE 0    /* y = bf16(x W^T)                                   */
+#define OMNI_EPI_RESIDUAL 1 /* y = bf16(x W^T + residual) (residual may alias y) */
+#define OMNI_EPI_SWIGLU 2   /* W = [gate; up] (2I x K): y[:, :I] = silu(g) * u   */
+#define OMNI_EPI_F32 3      /* y = x W^T in f32 (logits)                          */
+
+/* Bytes of split-K workspace omni_linear needs for this shape (0 = none).
+ * splits = 0 lets the library choose. */
+OMNI_API int64_t omni_linear_workspace_bytes(int64_t rows, int64_t k, int64_t n, int32_t epilogue, int32_t splits);
+
+/* y[rows, N] = epilogue(x[rows, K] . w[N, K]^T): the decode-step linears
+ * (QKVParallelLinear / RowParallelLinear / MergedColumnParallelLinear +
+ * SiluAndMul / codec_head / lm_head of thinker_model.py:152-402,
+ * talker.py:216-247, sglang_model.py:1294-1302, 2101-2152).
+ *   x, w, residual bf16; y bf16 (f32 for OMNI_EPI_F32); K % 64 == 0, N % 128 == 0.
+ *   workspace: >= omni_linear_workspace_bytes, 256-byte aligned, ZERO-FILLED
+ *   before first use (the kernel leaves its counters at zero again). */
+OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n,
+                         int32_t epilogue, const void* residual, int64_t residual_stride, void* y, int64_t y_stride,
+                         void* workspace, int64_t workspace_bytes, int32_t splits, void* stream);
+
+/* ======================================================================== */
+/* Norms and rotary embedding                                               */
+/* ======================================================================== */
+
+/* out = RMSNorm(s) * weight with s = x (addend == NULL) or s = bf16(x + addend)
+ * (written to residual_out when given): sglang RMSNorm(x) / RMSNorm(x, residual)
+ * (vendor/sglang/layers.py:57-98; add_rmsnorm_rounded, predictor_layers.py:603-622).
+ * hidden = 256 * {1,2,4,8,16,32}; bf16 rows 16-byte aligned. */
+OMNI_API int omni_rmsnorm(const void* x, int64_t x_stride, const void* addend, int64_t addend_stride,
+                          void* residual_out, int64_t residual_stride, const void* weight, float eps, void* out,
+                          int64_t out_stride, int64_t rows, int64_t hidden, void* stream);
+
+/* Per-head q/k RMSNorm, neox rotary embedding and the KV store
+ * (apply_qk_norm + rotary_emb with FusedSetKVBufferArg, thinker_model.py:272-345;
+ * predictor_cached_self_attention, sglang_model.py:2168-2233).
+ *   qkv bf16 [rows, (Hq + 2 Hkv) head_dim]; cos_sin_cache f32 [max_position, head_dim]
+ *   (cos in the first half, sin in the second).
+ *   positions / cache_loc i64 [rows], or both NULL for the predictor layout:
+ *   row r = (request r / T, token r % T), position = slot_base + r % T,
+ *   slot = (r / T) * slot_stride + position.
+ *   q_out bf16 [rows, Hq head_dim]; k_cache, v_cache bf16 [slots, Hkv, head_dim]. */
+OMNI_API int omni_qknorm_rope_store(const void* qkv, int64_t qkv_stride, int64_t rows, int32_t num_q_heads,
+                                    int32_t num_kv_heads, int32_t head_dim, const void* q_norm_weight,
+                                    const void* k_norm_weight, float eps, const float* cos_sin_cache,
+                                    int64_t max_position, const int64_t* positions, const int64_t* cache_loc,
+                                    int32_t tokens_per_req, int32_t slot_stride, int32_t slot_base, void* q_out,
+                                    int64_t q_stride, void* k_cache, void* v_cache, void* stream);
+
+/* ======================================================================== */
+/* Attention                                                                */
+/* ======================================================================== */
+
+OMNI_API int64_t omni_paged_attention_workspace_bytes(int64_t rows, int32_t num_kv_heads, int64_t work_capacity);
+
+/* Paged-KV GQA decode attention (RadixAttention decode, thinker_model.py:373-379).
+ *   q bf16 [rows, Hq, 128]; k_cache, v_cache bf16 [slots, Hkv, 128], page size 16;
+ *   page_indptr i32 [rows+1] / page_indices i32 (page ids); seq_lens i64 [rows];
+ *   work_indptr i32 [rows+1]: cumulative ceil(pages / pages_per_chunk) (from
+ *   omni_decode_prepare); work_capacity bounds its last entry.
+ *   workspace: omni_paged_attention_workspace_bytes, 256-byte aligned, zero-filled
+ *   before first use.  out bf16 [rows, Hq, 128]. */
+OMNI_API int omni_paged_decode_attention(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                                         const int32_t* page_indptr, const int32_t* page_indices,
+                                         const int64_t* seq_lens, const int32_t* work_indptr, int64_t rows,
+                                         int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                         int32_t page_size, int32_t pages_per_chunk, int64_t work_capacity,
+                                         float sm_scale, void* out, int64_t out_stride, void* workspace,
+                                         int64_t workspace_bytes, int32_t grid_ctas, void* stream);
+
+/* The code predictor's attention over its per-request cache slots
+ * (predictor_gqa_attention / decode_attention_kernel, sglang_model.py:113-150,
+ * predictor_layers.py:336-396).  Row r = (request r / T, token r % T) attends to
+ * slots [0, slot_base + r % T] of its request (causal for the opening pair). */
+OMNI_API int omni_predictor_attention(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                                      int64_t rows, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                      int32_t tokens_per_req, int32_t slot_stride, int32_t slot_base, float sm_scale,
+                                      void* out, int64_t out_stride, void* stream);
+
+/* ======================================================================== */
+/* Batch packing                                                            */
+/* ======================================================================== */
+
+/* prepare_for_decode + ForwardBatch metadata (omni_scheduler.py:2000-2022,
+ * model_runner/base.py:577-623, talker_scheduler.py:198-225): seq_lens += 1, one
+ * KV slot per row (a new page from free_pages[*free_head...] when
+ * (seq_len - 1) % page_size == 0, pages taken in row order), req_to_token written,
+ * positions = seq_len - 1, kv_indptr / kv_indices (token level, nullable),
+ * page_indptr / page_indices, work_indptr (attention chunks, nullable).
+ * status (nullable) becomes 1 if the free list ran dry. */
+OMNI_API int omni_decode_prepare(int64_t rows, int64_t* seq_lens, const int64_t* req_pool_indices,
+                                 int32_t* req_to_token, int64_t max_ctx, int32_t page_size, const int32_t* free_pages,
+                                 int64_t num_free, int64_t* free_head, int64_t* out_cache_loc, int64_t* positions,
+                                 int32_t* kv_indptr, int32_t* kv_indices, int32_t* page_indptr,
+                                 int32_t* page_indices, int32_t* work_indptr, int32_t pages_per_chunk,
+                                 int32_t* status, void* stream);
+
+/* rollback_decode_prep_after_skip (talker_scheduler.py:198-225): free the pages
+ * this step opened (their slots listed in freed_slots, count in num_freed),
+ * seq_lens -= 1, req_to_token cleared at the rolled-back position. */
+OMNI_API int omni_decode_rollback(int64_t rows, int64_t* seq_lens, const int64_t* req_pool_indices,
+                                  int32_t* req_to_token, int64_t max_ctx, int32_t page_size,
+                                  const int64_t* out_cache_loc, int64_t* free_head, int64_t* freed_slots,
+                                  int64_t* num_freed, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

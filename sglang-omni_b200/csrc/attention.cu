@@ -1,0 +1,435 @@
+// Attention kernels of the decode step.
+//
+// paged_decode_attention_kernel — GQA decode over the paged KV pool (L1:
+//   RadixAttention decode, thinker_model.py:373-379).  One work item is
+//   (request row, chunk of up to `pages_per_chunk` pages) x one KV head; the
+//   work list is built once per step by the packing kernel and shared by every
+//   layer.  Each warp streams whole pages (16 tokens x head_dim, K and V) with
+//   16-byte cp.async into a swizzled double buffer and runs
+//   S = Q K^T and O += P V on mma.sync m16n8k16 (the 8 query heads of the
+//   group in the M tile), with an online base-2 softmax.  Warps combine in
+//   shared memory; chunks of one row are merged by the last CTA of the row to
+//   finish (deterministic order, no spinning).
+//
+// predictor_attention_kernel — the code predictor's attention over its <= G+1
+//   per-request cache slots (predictor_cached_self_attention,
+//   sglang_model.py:2168-2233; decode_attention_kernel,
+//   predictor_layers.py:336-396): one warp per (row, query head), causal for
+//   the opening pair.
+#include "capi_util.h"
+#include "common.cuh"
+
+namespace omni {
+namespace {
+
+constexpr int kAttnWarps = 4;
+constexpr int kPage = 16;
+constexpr int kD = 128;       // head_dim of the talker
+constexpr int kGroup = 8;     // query heads per KV head
+constexpr int kPageBytes = kPage * kD * 2;  // one head's K (or V) page: 4 KB
+
+OMNI_DEVINL void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+OMNI_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+OMNI_DEVINL void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+OMNI_DEVINL void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+OMNI_DEVINL void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+OMNI_DEVINL void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Swizzled offset of (token row, 16-byte chunk) inside a 16 x 256-byte page tile.
+OMNI_DEVINL uint32_t swz(int row, int chunk) { return (uint32_t)(row * 256 + ((chunk ^ (row & 7)) << 4)); }
+
+struct PagedAttnParams {
+  const uint16_t* q;  // [B, Hq, D] row stride q_stride
+  int64_t q_stride;
+  const uint16_t* k_cache;  // [slots, Hkv, D]
+  const uint16_t* v_cache;
+  const int32_t* page_indptr;  // [B + 1]
+  const int32_t* page_indices;
+  const int64_t* seq_lens;     // [B]
+  const int32_t* work_indptr;  // [B + 1] chunks per row (prefix)
+  int rows, hkv, pages_per_chunk;
+  float scale_log2;  // softmax scale * log2(e)
+  uint16_t* out;     // [B, Hq, D]
+  int64_t out_stride;
+  float* part_o;     // [work capacity][Hkv][8][D]
+  float* part_lse;   // [work capacity][Hkv][8]
+  int* counters;     // [B][Hkv]
+  int work_capacity;
+};
+
+__global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_attention_kernel(const __grid_constant__ PagedAttnParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_last;
+  griddep_wait();
+  griddep_launch();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int h = blockIdx.y;
+  const int num_work = p.work_indptr[p.rows];
+  uint8_t* wbuf = smem + warp * (2 * 2 * kPageBytes);  // [stage][K|V][4 KB]
+
+  for (int it = blockIdx.x; it < num_work; it += gridDim.x) {
+    // row of this item: last b with work_indptr[b] <= it
+    int lo = 0, hi = p.rows - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.work_indptr[mid] <= it) lo = mid;
+      else hi = mid - 1;
+    }
+    const int b = lo;
+    const int c = it - p.work_indptr[b];
+    const int nchunks = p.work_indptr[b + 1] - p.work_indptr[b];
+    const int pg_begin = p.page_indptr[b];
+    const int p0 = pg_begin + c * p.pages_per_chunk;
+    const int p1 = min(p0 + p.pages_per_chunk, p.page_indptr[b + 1]);
+    const int seq_len = (int)p.seq_lens[b];
+
+    // Q fragments of the 8 heads of this group (rows 8..15 of the M tile are zero)
+    uint32_t qa[8][2];
+    const uint16_t* qrow = p.q + (int64_t)b * p.q_stride + (int64_t)(h * kGroup + g) * kD;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 2 * t);
+      qa[ks][1] = *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * t);
+    }
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m = -INFINITY, l = 0.0f;
+
+    auto issue = [&](int pg, int stage) {
+      const int64_t page = p.page_indices[pg];
+      const uint16_t* kbase = p.k_cache + (page * kPage * p.hkv + h) * kD;
+      const uint16_t* vbase = p.v_cache + (page * kPage * p.hkv + h) * kD;
+      uint8_t* kd = wbuf + stage * 2 * kPageBytes;
+      uint8_t* vd = kd + kPageBytes;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int id = i * 32 + lane;
+        const int row = id >> 4, ch = id & 15;
+        const int64_t goff = (int64_t)row * p.hkv * kD + ch * 8;
+        cp_async16(kd + swz(row, ch), kbase + goff);
+        cp_async16(vd + swz(row, ch), vbase + goff);
+      }
+      cp_async_commit();
+    };
+
+    int pg = p0 + warp;
+    int stage = 0;
+    if (pg < p1) issue(pg, 0);
+    for (; pg < p1; pg += kAttnWarps) {
+      const int nxt = pg + kAttnWarps;
+      if (nxt < p1) {
+        issue(nxt, stage ^ 1);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncwarp();
+      const int tok_base = (pg - pg_begin) * kPage;
+      if (seq_len - tok_base < kPage) {
+        // slots past the sequence end hold stale values: zero their V rows so
+        // that P = 0 never meets a non-finite value in P V
+        uint8_t* vd = wbuf + stage * 2 * kPageBytes + kPageBytes;
+        const int first = max(seq_len - tok_base, 0);
+        for (int id = first * 16 + lane; id < kPage * 16; id += 32)
+          *reinterpret_cast<uint4*>(vd + swz(id >> 4, id & 15)) = make_uint4(0, 0, 0, 0);
+        __syncwarp();
+      }
+      const uint32_t kb = smem_u32(wbuf + stage * 2 * kPageBytes);
+      const uint32_t vb = kb + kPageBytes;
+      // S = Q K^T over the page's 16 tokens (two n-tiles of 8)
+      float s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int tok = ((lane >> 4) << 3) + (lane & 7);
+        const int ch = 2 * ks + ((lane >> 3) & 1);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(kb + swz(tok, ch), r0, r1, r2, r3);
+        mma_bf16_16816(s[0], qa[ks][0], 0u, qa[ks][1], 0u, r0, r1);
+        mma_bf16_16816(s[1], qa[ks][0], 0u, qa[ks][1], 0u, r2, r3);
+      }
+      float sv[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int tok = tok_base + 8 * j + 2 * t + e;
+          sv[2 * j + e] = tok < seq_len ? s[j][e] * p.scale_log2 : -INFINITY;
+        }
+      float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+      const float m_new = fmaxf(m, mx);
+      const float alpha = (m == -INFINITY) ? 0.0f : exp2f(m - m_new);
+      float pv[4], rs = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        pv[e] = (sv[e] == -INFINITY) ? 0.0f : exp2f(sv[e] - m_new);
+        rs += pv[e];
+      }
+      rs += __shfl_xor_sync(0xFFFFFFFFu, rs, 1);
+      rs += __shfl_xor_sync(0xFFFFFFFFu, rs, 2);
+      l = l * alpha + rs;
+      m = m_new;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        o[n][0] *= alpha;
+        o[n][1] *= alpha;
+      }
+      const uint32_t pa0 = pack_bf2(pv[0], pv[1]);
+      const uint32_t pa2 = pack_bf2(pv[2], pv[3]);
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const int tok = ((lane >> 3) & 1) * 8 + (lane & 7);
+        const int ch = 2 * jj + (lane >> 4);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_t(vb + swz(tok, ch), r0, r1, r2, r3);
+        mma_bf16_16816(o[2 * jj], pa0, 0u, pa2, 0u, r0, r1);
+        mma_bf16_16816(o[2 * jj + 1], pa0, 0u, pa2, 0u, r2, r3);
+      }
+      __syncwarp();
+      stage ^= 1;
+    }
+
+    // ---- combine the warps of this CTA ----
+    __syncthreads();
+    float* wm = reinterpret_cast<float*>(smem);
+    float* wl = wm + kAttnWarps * kGroup;
+    float* wo = wl + kAttnWarps * kGroup;  // [warp][8][128]
+    if (t == 0) {
+      wm[warp * kGroup + g] = m;
+      wl[warp * kGroup + g] = l;
+    }
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      wo[(warp * kGroup + g) * kD + 8 * n + 2 * t] = o[n][0];
+      wo[(warp * kGroup + g) * kD + 8 * n + 2 * t + 1] = o[n][1];
+    }
+    __syncthreads();
+    {
+      const int hg = threadIdx.x >> 4;          // head within group
+      const int d0 = (threadIdx.x & 15) * 8;    // 8 dims
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w * kGroup + hg]);
+      float L = 0.0f, acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float lw = wl[w * kGroup + hg];
+        if (lw == 0.0f) continue;
+        const float sc = exp2f(wm[w * kGroup + hg] - M);
+        L += lw * sc;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += wo[(w * kGroup + hg) * kD + d0 + e] * sc;
+      }
+      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+      if (nchunks == 1) {
+        uint16_t* dst = p.out + (int64_t)b * p.out_stride + (int64_t)(h * kGroup + hg) * kD + d0;
+        uint4 v = make_uint4(pack_bf2(acc[0] * inv, acc[1] * inv), pack_bf2(acc[2] * inv, acc[3] * inv),
+                             pack_bf2(acc[4] * inv, acc[5] * inv), pack_bf2(acc[6] * inv, acc[7] * inv));
+        *reinterpret_cast<uint4*>(dst) = v;
+      } else {
+        float* po = p.part_o + (((int64_t)it * p.hkv + h) * kGroup + hg) * kD + d0;
+        *reinterpret_cast<float4*>(po) = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+        *reinterpret_cast<float4*>(po + 4) = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
+        if ((threadIdx.x & 15) == 0) p.part_lse[((int64_t)it * p.hkv + h) * kGroup + hg] = M + log2f(L);
+      }
+    }
+    if (nchunks > 1) {
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        int* ctr = p.counters + b * p.hkv + h;
+        const int old = atomicAdd(ctr, 1);
+        s_last = old == nchunks - 1;
+        if (s_last) *ctr = 0;
+      }
+      __syncthreads();
+      if (s_last) {
+        __threadfence();
+        const int hg = threadIdx.x >> 4;
+        const int d0 = (threadIdx.x & 15) * 8;
+        const int w0 = p.work_indptr[b];
+        float M = -INFINITY;
+        for (int cc = 0; cc < nchunks; ++cc)
+          M = fmaxf(M, __ldcg(p.part_lse + ((int64_t)(w0 + cc) * p.hkv + h) * kGroup + hg));
+        float W = 0.0f, acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int cc = 0; cc < nchunks; ++cc) {
+          const int64_t base = ((int64_t)(w0 + cc) * p.hkv + h) * kGroup + hg;
+          const float lse = __ldcg(p.part_lse + base);
+          const float wgt = lse == -INFINITY ? 0.0f : exp2f(lse - M);
+          W += wgt;
+          const float* po = p.part_o + base * kD + d0;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += __ldcg(po + e) * wgt;
+        }
+        const float inv = W > 0.0f ? 1.0f / W : 0.0f;
+        uint16_t* dst = p.out + (int64_t)b * p.out_stride + (int64_t)(h * kGroup + hg) * kD + d0;
+        *reinterpret_cast<uint4*>(dst) =
+            make_uint4(pack_bf2(acc[0] * inv, acc[1] * inv), pack_bf2(acc[2] * inv, acc[3] * inv),
+                       pack_bf2(acc[4] * inv, acc[5] * inv), pack_bf2(acc[6] * inv, acc[7] * inv));
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Predictor attention: rows laid out (request, token); a row attends to the
+// request's slots [0, base + t] (t = the row's token index within the request).
+// ---------------------------------------------------------------------------
+template <int E>  // head_dim = 32 * E
+__global__ void __launch_bounds__(128) predictor_attention_kernel(const uint16_t* __restrict__ q, int64_t q_stride,
+                                                                  const uint16_t* __restrict__ k_cache,
+                                                                  const uint16_t* __restrict__ v_cache, int rows,
+                                                                  int hq, int hkv, int tokens_per_req,
+                                                                  int slot_stride, int slot_base, float scale,
+                                                                  uint16_t* __restrict__ out, int64_t out_stride) {
+  griddep_wait();
+  griddep_launch();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int item = blockIdx.x * 4 + warp;
+  if (item >= rows * hq) return;
+  const int row = item / hq, head = item % hq;
+  const int req = row / tokens_per_req, tk = row % tokens_per_req;
+  const int kvh = head / (hq / hkv);
+  constexpr int D = 32 * E;
+  float qv[E], acc[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    qv[j] = bf2f(q[row * q_stride + head * D + E * lane + j]) * scale;
+    acc[j] = 0.0f;
+  }
+  float m = -INFINITY, l = 0.0f;
+  const int last = slot_base + tk;
+  const int64_t slot0 = (int64_t)req * slot_stride;
+  for (int s = 0; s <= last; ++s) {
+    const int64_t off = ((slot0 + s) * hkv + kvh) * D + E * lane;
+    float d = 0.0f;
+#pragma unroll
+    for (int j = 0; j < E; ++j) d = __fmaf_rn(qv[j], bf2f(k_cache[off + j]), d);
+#pragma unroll
+    for (int o2 = 16; o2 >= 1; o2 >>= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, o2);
+    const float mn = fmaxf(m, d);
+    const float a = expf(m - mn);
+    const float pr = expf(d - mn);
+    l = l * a + pr;
+#pragma unroll
+    for (int j = 0; j < E; ++j) acc[j] = acc[j] * a + pr * bf2f(v_cache[off + j]);
+    m = mn;
+  }
+  const float inv = 1.0f / l;
+#pragma unroll
+  for (int j = 0; j < E; ++j) out[row * out_stride + head * D + E * lane + j] = f2bf(acc[j] * inv);
+}
+
+}  // namespace
+}  // namespace omni
+
+using namespace omni;
+
+extern "C" OMNI_API int64_t omni_paged_attention_workspace_bytes(int64_t rows, int32_t num_kv_heads,
+                                                                 int64_t work_capacity) {
+  const int64_t ctr = (rows * num_kv_heads * 4 + 255) / 256 * 256;
+  const int64_t lse = (work_capacity * num_kv_heads * kGroup * 4 + 255) / 256 * 256;
+  return ctr + lse + work_capacity * num_kv_heads * kGroup * kD * 4;
+}
+
+extern "C" OMNI_API int omni_paged_decode_attention(const void* q, int64_t q_stride, const void* k_cache,
+                                                    const void* v_cache, const int32_t* page_indptr,
+                                                    const int32_t* page_indices, const int64_t* seq_lens,
+                                                    const int32_t* work_indptr, int64_t rows, int32_t num_q_heads,
+                                                    int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                                                    int32_t pages_per_chunk, int64_t work_capacity, float sm_scale,
+                                                    void* out, int64_t out_stride, void* workspace,
+                                                    int64_t workspace_bytes, int32_t grid_ctas, void* stream) {
+  if (rows < 0 || num_kv_heads <= 0 || pages_per_chunk <= 0) return set_error(OMNI_ERR_INVALID, "bad attention shape");
+  if (head_dim != kD || page_size != kPage || num_q_heads != num_kv_heads * kGroup)
+    return set_error(OMNI_ERR_UNSUPPORTED, "paged attention supports head_dim 128, page 16, 8 query heads per KV head");
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || out_stride % 8 || (reinterpret_cast<uintptr_t>(q) & 3) ||
+      q_stride % 2 || (reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15))
+    return set_error(OMNI_ERR_UNSUPPORTED, "misaligned attention operands");
+  if (workspace_bytes < omni_paged_attention_workspace_bytes(rows, num_kv_heads, work_capacity) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return set_error(OMNI_ERR_CAPACITY, "attention workspace too small or misaligned");
+  if (rows == 0) return OMNI_OK;
+  PagedAttnParams p{};
+  p.q = static_cast<const uint16_t*>(q);
+  p.q_stride = q_stride;
+  p.k_cache = static_cast<const uint16_t*>(k_cache);
+  p.v_cache = static_cast<const uint16_t*>(v_cache);
+  p.page_indptr = page_indptr;
+  p.page_indices = page_indices;
+  p.seq_lens = seq_lens;
+  p.work_indptr = work_indptr;
+  p.rows = (int)rows;
+  p.hkv = num_kv_heads;
+  p.pages_per_chunk = pages_per_chunk;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.out = static_cast<uint16_t*>(out);
+  p.out_stride = out_stride;
+  p.work_capacity = (int)work_capacity;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int64_t ctr = (rows * num_kv_heads * 4 + 255) / 256 * 256;
+  const int64_t lse = (work_capacity * num_kv_heads * kGroup * 4 + 255) / 256 * 256;
+  p.counters = reinterpret_cast<int*>(ws);
+  p.part_lse = reinterpret_cast<float*>(ws + ctr);
+  p.part_o = reinterpret_cast<float*>(ws + ctr + lse);
+  const size_t smem = (size_t)kAttnWarps * 2 * 2 * kPageBytes;  // 64 KB
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(paged_decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return check_launch(e);
+    attr = true;
+  }
+  int gx = grid_ctas > 0 ? grid_ctas : 296;
+  if (gx > work_capacity) gx = (int)work_capacity;
+  if (gx < 1) gx = 1;
+  return check_launch(launch(paged_decode_attention_kernel, dim3((unsigned)gx, (unsigned)num_kv_heads),
+                             dim3(kAttnWarps * 32), smem, static_cast<cudaStream_t>(stream), p));
+}
+
+extern "C" OMNI_API int omni_predictor_attention(const void* q, int64_t q_stride, const void* k_cache,
+                                                 const void* v_cache, int64_t rows, int32_t num_q_heads,
+                                                 int32_t num_kv_heads, int32_t head_dim, int32_t tokens_per_req,
+                                                 int32_t slot_stride, int32_t slot_base, float sm_scale, void* out,
+                                                 int64_t out_stride, void* stream) {
+  if (rows < 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0 || tokens_per_req <= 0 ||
+      slot_base < 0 || slot_base + tokens_per_req > slot_stride)
+    return set_error(OMNI_ERR_INVALID, "bad predictor attention shape");
+  if (rows % tokens_per_req != 0) return set_error(OMNI_ERR_INVALID, "rows must be whole requests");
+  if (head_dim != 64 && head_dim != 128) return set_error(OMNI_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (rows == 0) return OMNI_OK;
+  dim3 g((unsigned)((rows * num_q_heads + 3) / 4)), b(128);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto Q = static_cast<const uint16_t*>(q);
+  auto K = static_cast<const uint16_t*>(k_cache);
+  auto V = static_cast<const uint16_t*>(v_cache);
+  auto O = static_cast<uint16_t*>(out);
+  if (head_dim == 64)
+    return check_launch(launch(predictor_attention_kernel<2>, g, b, 0, st, Q, q_stride, K, V, (int)rows, num_q_heads,
+                               num_kv_heads, tokens_per_req, slot_stride, slot_base, sm_scale, O, out_stride));
+  return check_launch(launch(predictor_attention_kernel<4>, g, b, 0, st, Q, q_stride, K, V, (int)rows, num_q_heads,
+                             num_kv_heads, tokens_per_req, slot_stride, slot_base, sm_scale, O, out_stride));
+}

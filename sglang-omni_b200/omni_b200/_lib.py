@@ -39,11 +39,24 @@ SIGNATURES: dict[str, list] = {
     "omni_codebook_step": [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P],
     "omni_gather_embedding_add": [_P, _I32, _I64, _P, _I64, _P, _P, _P, _I64, _P, _P],
     "omni_layer0_sample": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P],
+    "omni_linear_workspace_bytes": [_I64, _I64, _I64, _I32, _I32],
+    "omni_linear": [_P, _I64, _I64, _I64, _P, _I64, _I32, _P, _I64, _P, _I64, _P, _I64, _I32, _P],
+    "omni_rmsnorm": [_P, _I64, _P, _I64, _P, _I64, _P, _F32, _P, _I64, _I64, _I64, _P],
+    "omni_qknorm_rope_store": [_P, _I64, _I64, _I32, _I32, _I32, _P, _P, _F32, _P, _I64, _P, _P, _I32, _I32, _I32,
+                               _P, _I64, _P, _P, _P],
+    "omni_paged_attention_workspace_bytes": [_I64, _I32, _I64],
+    "omni_paged_decode_attention": [_P, _I64, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _I64, _F32,
+                                    _P, _I64, _P, _I64, _I32, _P],
+    "omni_predictor_attention": [_P, _I64, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _F32, _P, _I64, _P],
+    "omni_decode_prepare": [_I64, _P, _P, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P],
+    "omni_decode_rollback": [_I64, _P, _P, _P, _I64, _I32, _P, _P, _P, _P, _P],
 }
 _RESTYPES = {
     "omni_version": ctypes.c_char_p,
     "omni_last_error": ctypes.c_char_p,
     "omni_device_status": ctypes.c_uint,
+    "omni_linear_workspace_bytes": ctypes.c_int64,
+    "omni_paged_attention_workspace_bytes": ctypes.c_int64,
 }
 
 _lock = threading.Lock()
