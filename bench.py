@@ -1,0 +1,338 @@
+"""Benchmark of the continuous-batching talker decode step (codec frames/s).
+
+Workload: 64 live streams per GPU; a random-init
+(seed 0) 20-layer dense talker (hidden 1024, 16 q / 2 kv heads, head_dim 128,
+SwiGLU 3072, codec vocab 3072) decoding one codec frame per stream per step
+over a paged KV cache (page 16, pages randomly permuted in the pool, context
+lengths log-normal(6, 0.8) clipped to [16, 8192]), followed by the config-0
+code predictor (5 layers, 15 residual codebooks of 2048, T 0.9, top-k 50,
+top-p 0.8) for all 64 streams.  One step = one CUDA graph replay of packing +
+talker + layer-0 draw + predictor.  Synthetic data: seeded random weights,
+KV contents and text rows.
+
+The step streams ~3 GB (weights + KV) per step, far above the 126 MB L2, so
+no L2 flush is needed between timed steps.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Under torchrun each rank runs an independent replica of the workload (data
+parallel by request, no collective on the hot path); rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "sglang-omni_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "codec frames/s per GPU (ragged talker+codebook decode step); p50 step µs"
+UNIT = "frames/s"
+STREAMS = 64
+
+
+def context_lengths(n: int, seed: int, headroom: int) -> list[int]:
+    rng = np.random.default_rng(seed)
+    lens = np.clip(np.round(np.exp(rng.normal(6.0, 0.8, n))), 16, 8192).astype(int)
+    return [int(min(L, 8192 - headroom)) for L in lens]
+
+
+def measured_peaks() -> tuple[float, float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples: list[list[str]] = []
+        self._stop = threading.Event()
+        self._thread: threading.Thread | None = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                if out.returncode == 0 and out.stdout.strip():
+                    self.samples.append([x.strip() for x in out.stdout.strip().split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for s in self.samples for n, v in zip(names, s[5:9]) if v.strip().lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the oracle restatement of the same step on the host cores
+# ---------------------------------------------------------------------------
+def cpu_step_rate(steps: int, warmup: int, seed: int = 0) -> tuple[float, dict, list[float]]:
+    """Times the CPU restatement of the config-1 step (64 streams, 20 layers, 15
+    codebooks) on the host cores; returns (frames/s, description, per-step seconds)."""
+    from oracle.model import OracleTalker, rb  # noqa: F401  (test infrastructure: the CPU baseline)
+    from omni_b200.config import CONFIG1_DENSE
+    from omni_b200.predictor import init_predictor_weights
+    from omni_b200.talker import init_talker_weights
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = CONFIG1_DENSE
+    tw = init_talker_weights(cfg, seed=seed, device="cpu")
+    pw = init_predictor_weights(cfg.predictor, seed=seed + 1, device="cpu")
+    o = OracleTalker(cfg, tw, pw)
+    lens = context_lengths(STREAMS, seed, headroom=steps + warmup + 8)
+    B = STREAMS
+    P = cfg.page_size
+    total_slots = sum(L + steps + warmup + 1 for L in lens)
+    L_ = cfg.num_hidden_layers
+    g = torch.Generator().manual_seed(seed + 7)
+    kpool = torch.randn(L_, total_slots, cfg.num_key_value_heads, cfg.head_dim, generator=g).bfloat16().float()
+    vpool = torch.randn(L_, total_slots, cfg.num_key_value_heads, cfg.head_dim, generator=g).bfloat16().float()
+    r2t = torch.zeros(B, max(lens) + steps + warmup + 2, dtype=torch.int32)
+    off = 0
+    for i, L in enumerate(lens):
+        n = L + steps + warmup + 1
+        r2t[i, :n] = torch.arange(off, off + n, dtype=torch.int32)
+        off += n
+    seq = torch.tensor(lens)
+    feedback = torch.zeros(B, cfg.hidden_size).bfloat16()
+    text = torch.randn(B, cfg.hidden_size, generator=g).bfloat16()
+    l0 = dict(penalties=np.full(B, 1.05, np.float32), rep_mask=np.zeros((B, cfg.vocab_size), np.uint8),
+              suppress_mask=np.zeros((B, cfg.vocab_size), np.uint8), temperature=np.full(B, 0.9, np.float32),
+              top_k=np.full(B, 50), top_p=np.full(B, 0.8, np.float32), min_p=np.zeros(B, np.float32),
+              seed=np.arange(B) + 1, max_top_k=50)
+    sub = dict(temperature=np.full(B, 0.9, np.float32), top_k=np.full(B, 50), top_p=np.full(B, 0.8, np.float32),
+               seed=np.arange(B) + 100, do_sample=np.ones(B, np.uint8), max_top_k=50, has_top_p=True)
+    times = []
+    for it in range(warmup + steps):
+        t0 = time.perf_counter()
+        seq = seq + 1
+        pos = seq - 1
+        loc = r2t[torch.arange(B), pos].long()
+        logits, hidden = o.talker_forward(feedback, text, pos, loc, seq, r2t, kpool, vpool)
+        l0["positions"] = pos.numpy()
+        c0 = torch.from_numpy(o.layer0(logits, l0))
+        codes, summed, _ = o.code_predictor(c0, hidden, pos, sub)
+        feedback = torch.from_numpy(summed.view(np.int16)).view(torch.bfloat16)
+        if it >= warmup:
+            times.append(time.perf_counter() - t0)
+    rate = B * len(times) / sum(times)
+    desc = {"cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(times)} full config-1 steps (64 streams, 20 layers, 15 codebooks) of the CPU "
+                      f"restatement, fp32 on {torch.get_num_threads()} threads, after {warmup} warm-up steps"}
+    return rate, desc, times
+
+
+# ---------------------------------------------------------------------------
+def run_reference_arm(args, rank: int) -> None:
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 5))
+    warmup = 1
+    rate, desc, times = cpu_step_rate(steps, warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+        "warmup": warmup, "ms_per_step": 1000 * float(np.median(times)), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config1: dense talker decode, 64 streams + config-0 predictor",
+                   "streams": STREAMS, "layers": 20, "codebooks": 15},
+        "cpu_baseline": {"value": rate, "unit": UNIT, **desc},
+        "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def time_kernel(fn, iters: int) -> float:
+    """Average device time (s) of fn() launched back to back on the current stream."""
+    st = torch.cuda.current_stream()
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(iters):
+        fn()
+    e1.record(st)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1000.0 / iters
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-steps", type=int, default=2)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    from omni_b200 import _lib, ops
+    from omni_b200.config import CONFIG1_DENSE
+    from omni_b200.model_runner import TalkerDecodeRunner
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = CONFIG1_DENSE
+    W, K = max(3, args.warmup), args.steps
+    total_steps = 2 * (W + K) + 4
+    lens = context_lengths(STREAMS, seed=rank, headroom=total_steps + 8)
+    P = cfg.page_size
+    pages = int(sum(math.ceil((L + total_steps) / P) for L in lens) * 1.25) + STREAMS
+    runner = TalkerDecodeRunner(cfg, max_batch=STREAMS, num_pages=pages, seed=0, device=dev)
+    runner.admit(lens, seed=rank)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    runner.text_embeds.normal_(generator=g)
+    n0 = _lib.launch_count()
+    runner.capture(warmup=1)
+    launches_per_step = (_lib.launch_count() - n0) // 2  # one eager warm-up step + the captured step
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident leg ----
+    for _ in range(W):
+        runner.step()
+    barrier()
+    st = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)]
+    with ClockSampler(local_rank) as clocks:
+        ev[0].record(st)
+        for i in range(K):
+            runner.step()
+            ev[i + 1].record(st)
+        barrier()
+    step_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(K)]
+    total_ms = ev[0].elapsed_time(ev[K])
+
+    # ---- end-to-end leg: pinned host text rows in, host codes out, every step ----
+    H = cfg.hidden_size
+    G = cfg.predictor.num_code_groups
+    text_host = torch.randn(STREAMS, H).to(torch.bfloat16).pin_memory()
+    codes_host = torch.empty((STREAMS, G), dtype=torch.long).pin_memory()
+    for _ in range(W):
+        runner.decode(text_host, codes_host)
+    barrier()
+    t_e0 = torch.cuda.Event(enable_timing=True)
+    t_e1 = torch.cuda.Event(enable_timing=True)
+    t_e0.record(st)
+    for _ in range(K):
+        runner.decode(text_host, codes_host)
+    t_e1.record(st)
+    barrier()
+    e2e_ms = t_e0.elapsed_time(t_e1)
+
+    # ---- dominant kernel: paged decode attention of one layer, timed in isolation ----
+    fb = runner.forward_batch()
+    t = runner.talker
+    attn_args = dict(page_indptr=fb.page_indptr, page_indices=fb.page_indices, seq_lens=fb.seq_lens,
+                     work_indptr=fb.work_indptr, num_q_heads=cfg.num_attention_heads,
+                     num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim, page_size=P,
+                     pages_per_chunk=fb.pages_per_chunk, work_capacity=fb.work_capacity, sm_scale=t.scale,
+                     out=t.attn[:STREAMS], workspace=t.attn_workspace)
+    kc, vc = runner.kv.k_buffer[0], runner.kv.v_buffer[0]
+    attn_s = time_kernel(lambda: ops.paged_decode_attention(t.q[:STREAMS], kc, vc, **attn_args), 50)
+    seq_now = runner.seq_lens[:STREAMS].cpu().numpy()
+    attn_bytes = float(seq_now.sum()) * cfg.num_key_value_heads * cfg.head_dim * 2 * 2 \
+        + STREAMS * cfg.num_attention_heads * cfg.head_dim * 2 * 2
+
+    # ---- gather over ranks ----
+    frames = STREAMS * K
+    stats = torch.tensor([total_ms, e2e_ms, frames], dtype=torch.float64, device=dev)
+    if dist is not None:
+        t_max = stats.clone()
+        dist.all_reduce(t_max[:2], op=dist.ReduceOp.MAX)
+        f_sum = stats[2:].clone()
+        dist.all_reduce(f_sum, op=dist.ReduceOp.SUM)
+        total_ms, e2e_ms, frames = float(t_max[0]), float(t_max[1]), float(f_sum[0])
+    if rank == 0:
+        hbm, tflops, peak_kind = measured_peaks()
+        value = frames / (total_ms / 1000.0)
+        e2e = frames / (e2e_ms / 1000.0)
+        achieved = attn_bytes / attn_s / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": total_ms / K, "p50_step_us": 1000 * float(np.median(step_ms)),
+            "p99_step_us": 1000 * float(np.percentile(step_ms, 99)), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config1: dense talker decode (20 layers, 64 streams, paged KV page 16, "
+                                   "ctx lognormal(6,0.8) clip [16,8192]) + config-0 predictor (15 codebooks)",
+                       "streams_per_gpu": STREAMS, "parallelism": f"dp{world} replicas (no collective)",
+                       "sum_ctx_rank0": int(sum(lens)), "l2": "inputs > L2 (~3 GB streamed per step)"},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": STREAMS * H * 2,
+                    "d2h_bytes_per_step": STREAMS * G * 8},
+            "gpu_launches": launches_per_step * K,
+            "roofline": {"bound": "hbm", "kernel": "paged_decode_attention_kernel", "achieved": achieved,
+                         "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                         "peak_kind": peak_kind},
+            "clocks": clocks.summary(),
+        }
+        if not args.no_cpu:
+            rate, desc, _ = cpu_step_rate(args.cpu_steps, 1)
+            line["cpu_baseline"] = {"value": rate, "unit": UNIT, **desc}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        runner.graph = None
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

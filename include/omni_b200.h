@@ -116,12 +116,24 @@ OMNI_API int omni_gather_embedding_add(const void* token_ids, int32_t token_is_i
  *   logits f32 [rows, vocab] row stride logits_stride; vocab % 4 == 0, <= 8192
  *   penalties f32 [rows]; rep_mask, suppress_mask u8 [rows, vocab] or NULL
  *   temperatures, top_ps, min_ps (nullable) f32 [rows]; top_ks, seeds, positions i64 [rows]
- *   max_top_k <= 1024: the widest top_k of the batch. */
+ *   max_top_k <= 1024: the widest top_k of the batch.
+ *   rep_mask_update u8 [rows, vocab] or NULL: the drawn token is marked 1 (the
+ *   next step's repetition mask: prepare_decode_buffers, talker.py:1065-1215). */
 OMNI_API int omni_layer0_sample(const float* logits, int64_t rows, int64_t vocab, int64_t logits_stride,
                                 const float* penalties, const uint8_t* rep_mask, const uint8_t* suppress_mask,
                                 const float* temperatures, const int64_t* top_ks, const float* top_ps,
                                 const float* min_ps, const int64_t* seeds, const int64_t* positions,
-                                int32_t max_top_k, int64_t* out, void* stream);
+                                int32_t max_top_k, int64_t* out, uint8_t* rep_mask_update, void* stream);
+
+/* First pass of the code predictor for one frame (code_predictor_forward_incremental,
+ * sglang_model.py:1784-1813): codes[row * codes_stride] = layer0_codes[row];
+ * e = table[layer0_codes[row]]; summed[row] = e; pair rows 2 row and 2 row + 1 =
+ * (talker_hidden[row], e), the opening two-token pass input.
+ *   layer0_codes i64 [rows]; talker_hidden bf16 [rows, hidden] row stride hidden_stride;
+ *   table bf16 [vocab, hidden]; pair bf16 [2 rows, hidden]; summed bf16 [rows, hidden]. */
+OMNI_API int omni_predictor_pair_inputs(const int64_t* layer0_codes, const void* talker_hidden, int64_t hidden_stride,
+                                        const void* table, int64_t rows, int64_t hidden, void* pair, void* summed,
+                                        int64_t* codes, int64_t codes_stride, void* stream);
 
 
 /* ======================================================================== */

@@ -1,0 +1,201 @@
+"""CPU restatement of the talker decode step — TEST INFRASTRUCTURE ONLY.
+
+fp32 PyTorch-CPU arithmetic on the bf16 weights, rounding to bf16 where the
+reference's plain path keeps bf16 tensors (outputs of every projection, norm,
+rotary and attention; the residual stream), following:
+
+- talker layer: Qwen3OmniMoeThinkerTextAttention + dense MLP
+  (sglang_omni/models/qwen3_omni/components/thinker_model.py:152-402,
+  talker.py:216-247), decode forward talker.py:438-491;
+- paged GQA decode attention over req_to_token slots (RadixAttention decode,
+  thinker_model.py:373-379), softmax in fp32;
+- layer-0 draw: omni_oracle.c orc_layer0_sample (talker.py:1376-1412);
+- code predictor: code_predictor_forward_incremental
+  (sglang_model.py:1743-1879), predictor_forward_tokens (:2036-2098),
+  predictor_cached_self_attention (:2168-2233), seeded residual sampler
+  omni_oracle.c orc_sample_topk_topp.
+
+Also the CPU baseline that bench.py times on the host cores.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from oracle import sampler as orc
+
+BF16 = torch.bfloat16
+
+
+def rb(x: torch.Tensor) -> torch.Tensor:
+    """Round an fp32 tensor to bf16 and back (a bf16 storage point)."""
+    return x.to(BF16).float()
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+
+
+def rope_cache(max_pos: int, d: int, theta: float) -> torch.Tensor:
+    inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+    f = torch.outer(torch.arange(max_pos, dtype=torch.float32), inv)
+    return torch.cat([f.cos(), f.sin()], -1)
+
+
+def rope_neox(x: torch.Tensor, cs: torch.Tensor) -> torch.Tensor:
+    """x [..., heads, d]; cs [..., d] broadcast over heads."""
+    d = x.shape[-1]
+    cos, sin = cs[..., None, : d // 2], cs[..., None, d // 2:]
+    a, b = x[..., : d // 2], x[..., d // 2:]
+    return torch.cat([a * cos - b * sin, b * cos + a * sin], -1)
+
+
+def to_f32(weights) -> dict | list | torch.Tensor:
+    if isinstance(weights, dict):
+        return {k: to_f32(v) for k, v in weights.items()}
+    if isinstance(weights, list):
+        return [to_f32(v) for v in weights]
+    return weights.detach().float().cpu()
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+class OracleTalker:
+    """fp32 CPU decode step of the dense talker + code predictor."""
+
+    def __init__(self, cfg, talker_w: dict, predictor_w: dict):
+        self.cfg = cfg
+        self.w = to_f32(talker_w)
+        self.pw = to_f32(predictor_w)
+        self.cs = rope_cache(cfg.max_context, cfg.head_dim, cfg.rope_theta)
+        pc = cfg.predictor
+        self.pcs = rope_cache(pc.cache_len, pc.head_dim, pc.rope_theta)
+
+    # ------------------------------------------------------------------
+    def talker_forward(self, feedback, text, positions, out_cache_loc, seq_lens, req_to_token, k_pool, v_pool):
+        """One decode forward; k_pool/v_pool: fp32 [L, slots, hkv, d] updated in place.
+        Returns (logits fp32 [B, V], hidden bf16-rounded [B, H])."""
+        cfg = self.cfg
+        H, D = cfg.hidden_size, cfg.head_dim
+        hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        eps = cfg.rms_norm_eps
+        B = feedback.shape[0]
+        x = rb(feedback.float() + (text.float() if text is not None else 0.0))
+        cs = self.cs[positions]
+        scale = 1.0 / math.sqrt(D)
+        for li, lw in enumerate(self.w["layers"]):
+            n = rb(rmsnorm(x, lw["input_layernorm"], eps))
+            qkv = rb(n @ lw["qkv_proj"].t())
+            q = qkv[:, : hq * D].view(B, hq, D)
+            k = qkv[:, hq * D: (hq + hkv) * D].view(B, hkv, D)
+            v = qkv[:, (hq + hkv) * D:].view(B, hkv, D)
+            q = rb(rmsnorm(q, lw["q_norm"], eps))
+            k = rb(rmsnorm(k, lw["k_norm"], eps))
+            q = rb(rope_neox(q, cs))
+            k = rb(rope_neox(k, cs))
+            k_pool[li, out_cache_loc] = k
+            v_pool[li, out_cache_loc] = v
+            att = torch.empty(B, hq, D)
+            for b in range(B):
+                L = int(seq_lens[b])
+                slots = req_to_token[b, :L].long()
+                kk = k_pool[li, slots]  # [L, hkv, D]
+                vv = v_pool[li, slots]
+                qb = q[b].view(hkv, hq // hkv, D)
+                s = torch.einsum("hgd,lhd->hgl", qb, kk) * scale
+                p = torch.softmax(s, -1)
+                att[b] = torch.einsum("hgl,lhd->hgd", p, vv).reshape(hq, D)
+            att = rb(att.reshape(B, hq * D))
+            x = rb(x + att @ lw["o_proj"].t())
+            n = rb(rmsnorm(x, lw["post_attention_layernorm"], eps))
+            gu = n @ lw["gate_up_proj"].t()
+            I = gu.shape[1] // 2
+            a = rb(torch.nn.functional.silu(rb(gu[:, :I])) * rb(gu[:, I:]))
+            x = rb(x + a @ lw["down_proj"].t())
+        hidden = rb(rmsnorm(x, self.w["norm"], eps))
+        logits = hidden @ self.w["codec_head"].t()
+        return logits, hidden
+
+    # ------------------------------------------------------------------
+    def predictor_tokens(self, x, k_cache, v_cache, *, batch, tokens, cache_len):
+        """x [batch*tokens, H] rows (request, token) at slots cache_len..; caches fp32
+        [L, batch, S, hkv, d] updated in place; returns final-normed rows."""
+        pc = self.cfg.predictor
+        D, hq, hkv, eps = pc.head_dim, pc.num_attention_heads, pc.num_key_value_heads, pc.rms_norm_eps
+        rows = batch * tokens
+        pos = cache_len + torch.arange(tokens).repeat(batch)
+        cs = self.pcs[pos]
+        scale = 1.0 / math.sqrt(D)
+        h = x
+        for li, lw in enumerate(self.pw["layers"]):
+            n = rb(rmsnorm(h, lw["input_layernorm"], eps))
+            qkv = rb(n @ lw["qkv_proj"].t())
+            q = qkv[:, : hq * D].view(rows, hq, D)
+            k = qkv[:, hq * D: (hq + hkv) * D].view(rows, hkv, D)
+            v = qkv[:, (hq + hkv) * D:].view(rows, hkv, D)
+            q = rb(rope_neox(rb(rmsnorm(q, lw["q_norm"], eps)), cs))
+            k = rb(rope_neox(rb(rmsnorm(k, lw["k_norm"], eps)), cs))
+            k_cache[li, :, cache_len: cache_len + tokens] = k.view(batch, tokens, hkv, D)
+            v_cache[li, :, cache_len: cache_len + tokens] = v.view(batch, tokens, hkv, D)
+            end = cache_len + tokens
+            kk = k_cache[li, :, :end].transpose(1, 2).repeat_interleave(hq // hkv, 1)  # [b, hq, end, D]
+            vv = v_cache[li, :, :end].transpose(1, 2).repeat_interleave(hq // hkv, 1)
+            qq = q.view(batch, tokens, hq, D).transpose(1, 2)
+            s = qq @ kk.transpose(-1, -2) * scale
+            mask = torch.arange(end)[None, :] > (cache_len + torch.arange(tokens))[:, None]
+            s = s.masked_fill(mask, float("-inf"))
+            att = rb((torch.softmax(s, -1) @ vv).transpose(1, 2).reshape(rows, hq * D))
+            h = rb(h + att @ lw["o_proj"].t())
+            n = rb(rmsnorm(h, lw["post_attention_layernorm"], eps))
+            gu = n @ lw["gate_up_proj"].t()
+            I = gu.shape[1] // 2
+            a = rb(torch.nn.functional.silu(rb(gu[:, :I])) * rb(gu[:, I:]))
+            h = rb(h + a @ lw["down_proj"].t())
+        return rb(rmsnorm(h, self.pw["norm"], eps))
+
+    def code_predictor(self, c0, talker_hidden, semantic_positions, sampling, *, forced_codes=None):
+        """Returns (codes [B, G] i64, summed bf16 bits [B, H], lm_head logits [G-1, B, V] fp32).
+        With forced_codes [B, G], the loop feeds those codes instead of its own draws
+        (teacher forcing), so every pass sees the same inputs as the device run."""
+        pc = self.cfg.predictor
+        G, H = pc.num_code_groups, pc.hidden_size
+        B = c0.shape[0]
+        S, hkv, D = pc.cache_len, pc.num_key_value_heads, pc.head_dim
+        kc = torch.zeros(pc.num_hidden_layers, B, S, hkv, D)
+        vc = torch.zeros_like(kc)
+        table0 = self.w["codec_embedding"]
+        e0 = table0[c0]
+        summed = bits(e0.to(BF16))
+        codes = np.zeros((B, G), np.int64)
+        codes[:, 0] = c0.numpy()
+        pair = torch.stack([talker_hidden.float(), e0], 1).reshape(2 * B, H)
+        out = self.predictor_tokens(pair, kc, vc, batch=B, tokens=2, cache_len=0)
+        last = out.view(B, 2, H)[:, 1]
+        all_logits = torch.zeros(G - 1, B, pc.vocab_size)
+        for j in range(G - 1):
+            logits = rb(last @ self.pw["lm_head"][j].t())
+            all_logits[j] = logits
+            pos = semantic_positions.numpy() * (G - 1) + (j + 1)
+            drawn = orc.sample_topk_topp(bits(logits.to(BF16)), sampling["temperature"], sampling["top_k"],
+                                         sampling["top_p"], sampling["seed"], pos,
+                                         max_top_k=sampling["max_top_k"], has_top_p=sampling["has_top_p"])
+            am = np.argmax(logits.numpy(), axis=1)  # first NaN, else first maximum (torch.argmax)
+            drawn = np.where(np.asarray(sampling["do_sample"], bool), drawn, am)
+            code = drawn if forced_codes is None else forced_codes[:, j + 1]
+            codes[:, j + 1] = code
+            table = bits(self.pw["codec_embedding"][j].to(BF16))
+            gathered, summed = orc.gather_add(code, table, summed)
+            if j < G - 2:
+                nxt = orc.bf16_bits_to_f32(gathered)
+                last = self.predictor_tokens(torch.from_numpy(nxt), kc, vc, batch=B, tokens=1, cache_len=2 + j)
+        return codes, summed, all_logits
+
+    def layer0(self, logits, state):
+        return orc.layer0_sample(logits.numpy(), state["penalties"], state["rep_mask"], state["suppress_mask"],
+                                 state["temperature"], state["top_k"], state["top_p"], state["min_p"], state["seed"],
+                                 state["positions"], max_top_k=state["max_top_k"])

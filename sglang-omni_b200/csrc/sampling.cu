@@ -657,6 +657,7 @@ struct Layer0Params {
   const int64_t* positions;
   int block_k;
   int64_t* out;
+  uint8_t* rep_mask_update;  // nullable: marks the drawn token as seen
 };
 
 template <int J, int C>
@@ -795,7 +796,10 @@ __global__ void __launch_bounds__(kThreads) layer0_sample_kernel(const __grid_co
         best_id = oid;
       }
     }
-    if (lane == 0) p.out[row] = (int64_t)best_id;
+    if (lane == 0) {
+      p.out[row] = (int64_t)best_id;
+      if (p.rep_mask_update) p.rep_mask_update[row * (int64_t)p.vocab + best_id] = 1;
+    }
   }
 }
 
@@ -963,7 +967,7 @@ extern "C" OMNI_API int omni_layer0_sample(const float* logits, int64_t rows, in
                                            const uint8_t* suppress_mask, const float* temperatures,
                                            const int64_t* top_ks, const float* top_ps, const float* min_ps,
                                            const int64_t* seeds, const int64_t* positions, int32_t max_top_k,
-                                           int64_t* out, void* stream) {
+                                           int64_t* out, uint8_t* rep_mask_update, void* stream) {
   if (rows < 0) return set_error(OMNI_ERR_INVALID, "rows must be >= 0");
   if (vocab < 32 || vocab > 8192 || vocab % 4 != 0)
     return set_error(OMNI_ERR_UNSUPPORTED, "vocab must be a multiple of 4 in [32, 8192]");
@@ -976,7 +980,7 @@ extern "C" OMNI_API int omni_layer0_sample(const float* logits, int64_t rows, in
     return set_error(OMNI_ERR_UNSUPPORTED, "logits rows must be 16-byte aligned");
   if (rows == 0) return OMNI_OK;
   Layer0Params p = {logits, logits_stride, (int)vocab, penalties, rep_mask, suppress_mask, temperatures, top_ks,
-                    top_ps, min_ps, seeds, positions, bk, out};
+                    top_ps, min_ps, seeds, positions, bk, out, rep_mask_update};
   const int J = (int)((vocab + 1023) / 1024);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   dim3 g((unsigned)rows), b(kThreads);
@@ -1013,4 +1017,53 @@ extern "C" OMNI_API int omni_layer0_sample(const float* logits, int64_t rows, in
     }
   }
   return set_error(OMNI_ERR_UNSUPPORTED, "unsupported layer-0 vocab");
+}
+
+// ---------------------------------------------------------------------------
+// Opening inputs of the code predictor for one frame.
+// ---------------------------------------------------------------------------
+namespace omni {
+namespace {
+__global__ void __launch_bounds__(128) predictor_pair_inputs_kernel(const int64_t* __restrict__ c0,
+                                                                   const uint16_t* __restrict__ hidden,
+                                                                   int64_t hidden_stride,
+                                                                   const uint16_t* __restrict__ table, int H,
+                                                                   uint16_t* __restrict__ pair,
+                                                                   uint16_t* __restrict__ summed,
+                                                                   int64_t* __restrict__ codes, int64_t codes_stride) {
+  griddep_wait();
+  griddep_launch();
+  const int row = blockIdx.x;
+  const int64_t code = c0[row];
+  if (threadIdx.x == 0) codes[row * codes_stride] = code;
+  const uint4* e = reinterpret_cast<const uint4*>(table + code * H);
+  const uint4* hs = reinterpret_cast<const uint4*>(hidden + row * hidden_stride);
+  uint4* p0 = reinterpret_cast<uint4*>(pair + (int64_t)(2 * row) * H);
+  uint4* p1 = reinterpret_cast<uint4*>(pair + (int64_t)(2 * row + 1) * H);
+  uint4* sm = reinterpret_cast<uint4*>(summed + (int64_t)row * H);
+  for (int v = threadIdx.x; v < H / 8; v += 128) {
+    const uint4 w = e[v];
+    p0[v] = hs[v];
+    p1[v] = w;
+    sm[v] = w;
+  }
+}
+}  // namespace
+}  // namespace omni
+
+extern "C" OMNI_API int omni_predictor_pair_inputs(const int64_t* layer0_codes, const void* talker_hidden,
+                                                   int64_t hidden_stride, const void* table, int64_t rows,
+                                                   int64_t hidden, void* pair, void* summed, int64_t* codes,
+                                                   int64_t codes_stride, void* stream) {
+  if (rows < 0 || hidden <= 0) return omni::set_error(OMNI_ERR_INVALID, "bad shape");
+  auto mis = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
+  if (hidden % 8 || hidden_stride % 8 || mis(talker_hidden) || mis(table) || mis(pair) || mis(summed))
+    return omni::set_error(OMNI_ERR_UNSUPPORTED, "rows must be 16-byte aligned");
+  if (rows == 0) return OMNI_OK;
+  return omni::check_launch(omni::launch(omni::predictor_pair_inputs_kernel, dim3((unsigned)rows), dim3(128), 0,
+                                         static_cast<cudaStream_t>(stream), layer0_codes,
+                                         static_cast<const uint16_t*>(talker_hidden), hidden_stride,
+                                         static_cast<const uint16_t*>(table), (int)hidden,
+                                         static_cast<uint16_t*>(pair), static_cast<uint16_t*>(summed), codes,
+                                         codes_stride));
 }

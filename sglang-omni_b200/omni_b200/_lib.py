@@ -38,7 +38,8 @@ SIGNATURES: dict[str, list] = {
     "omni_sample_sorted_seeded": [_P, _P, _I64, _I64, _P, _P, _P, _P],
     "omni_codebook_step": [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P],
     "omni_gather_embedding_add": [_P, _I32, _I64, _P, _I64, _P, _P, _P, _I64, _P, _P],
-    "omni_layer0_sample": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P],
+    "omni_layer0_sample": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P, _P],
+    "omni_predictor_pair_inputs": [_P, _P, _I64, _P, _I64, _I64, _P, _P, _P, _I64, _P],
     "omni_linear_workspace_bytes": [_I64, _I64, _I64, _I32, _I32],
     "omni_linear": [_P, _I64, _I64, _I64, _P, _I64, _I32, _P, _I64, _P, _I64, _P, _I64, _I32, _P],
     "omni_rmsnorm": [_P, _I64, _P, _I64, _P, _I64, _P, _F32, _P, _I64, _I64, _I64, _P],
@@ -121,8 +122,22 @@ def check(rc: int, name: str) -> None:
     raise RuntimeError(f"CUDA error in {msg}")
 
 
+# Entry points that launch kernels (counted by launch_counter()).
+_LAUNCHERS = {n for n in SIGNATURES if not n.endswith("_bytes") and n not in (
+    "omni_version", "omni_last_error", "omni_device_status")}
+_launches = 0
+
+
+def launch_count() -> int:
+    """Number of kernel-launching C-ABI calls made by this process so far."""
+    return _launches
+
+
 def call(name: str, *args) -> None:
+    global _launches
     check(getattr(load(), name)(*args), name)
+    if name in _LAUNCHERS:
+        _launches += 1
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

@@ -1,0 +1,226 @@
+"""The B200 talker model runner: one continuous-batching decode step as a single
+CUDA graph.
+
+Plugs in where the reference's ModelRunner hook protocol lets a subclass own
+the forward (sglang_omni/model_runner/base.py:839-1020):
+``custom_decode_forward(forward_batch, schedule_batch, requests)`` returns the
+batch result (next_token_ids, logits, hidden) and leaves the frame's codes and
+summed embeddings in ``output_codes`` / ``output_embeds`` as the reference's
+talkers do (sglang_model.py:1023-1160).
+
+One step on the device, in order:
+  1. omni_decode_prepare: seq_lens += 1, page/slot allocation, positions, page
+     table and the attention work list (prepare_for_decode + build_forward_batch);
+  2. talker forward over the decode rows, input = previous frame's summed codec
+     embeddings + the text row (write_feedback_buffers);
+  3. layer-0 codec draw (repetition penalty, suppression, seeded top-k/top-p);
+  4. the code predictor: 15 residual codebooks, each fused sample + gather.
+The host touches nothing inside the step: it copies the text rows in and the
+codes out around the graph replay.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from omni_b200 import ops
+from omni_b200.config import SamplingParams, TalkerConfig
+from omni_b200.kv_cache import PageAllocator, PagedKVPool, ReqToTokenPool
+from omni_b200.predictor import CodePredictor, init_predictor_weights
+from omni_b200.seed import derive_sampling_seed
+from omni_b200.talker import DecodeForwardBatch, DenseTalker, init_talker_weights
+
+
+@dataclass
+class GenerationBatchResult:
+    """What custom_decode_forward hands back (base.py:879-890, 649-655)."""
+
+    next_token_ids: torch.Tensor   # layer-0 codes [B]
+    next_token_logits: torch.Tensor  # fp32 [B, V0]
+    hidden_states: torch.Tensor    # [B, H]
+    codes: torch.Tensor            # [B, G] all codebooks of the frame
+    summed_embeds: torch.Tensor    # [B, H] feedback for the next frame
+
+
+class TalkerDecodeRunner:
+    def __init__(self, cfg: TalkerConfig, *, max_batch: int, num_pages: int, seed: int = 0, device="cuda",
+                 pages_per_chunk: int = 8, weights: dict | None = None, predictor_weights: dict | None = None):
+        if cfg.moe is not None:
+            raise NotImplementedError("the MoE talker runs through MoETalkerDecodeRunner")
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.max_batch = max_batch
+        self.pages_per_chunk = pages_per_chunk
+        self.w = weights if weights is not None else init_talker_weights(cfg, seed=seed, device=self.device)
+        pw = predictor_weights if predictor_weights is not None else init_predictor_weights(
+            cfg.predictor, seed=seed + 1, device=self.device)
+        self.kv = PagedKVPool(num_layers=cfg.num_hidden_layers, num_pages=num_pages, page_size=cfg.page_size,
+                              num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim, device=self.device)
+        self.r2t = ReqToTokenPool(max_reqs=max_batch, max_context=cfg.max_context, device=self.device)
+        self.talker = DenseTalker(cfg, self.w, max_batch=max_batch, device=self.device, kv_pool=self.kv)
+        self.predictor = CodePredictor(cfg.predictor, pw, max_batch=max_batch, device=self.device,
+                                       layer0_embedding=self.w["codec_embedding"])
+        B = max_batch
+        i64 = dict(dtype=torch.long, device=self.device)
+        i32 = dict(dtype=torch.int32, device=self.device)
+        self.seq_lens = torch.zeros(B, **i64)
+        self.req_pool_indices = torch.arange(B, **i64)
+        self.out_cache_loc = torch.zeros(B, **i64)
+        self.positions = torch.zeros(B, **i64)
+        self.page_indptr = torch.zeros(B + 1, **i32)
+        self.page_indices = torch.zeros(num_pages + B, **i32)
+        self.work_indptr = torch.zeros(B + 1, **i32)
+        self.work_capacity = (num_pages + pages_per_chunk - 1) // pages_per_chunk + B
+        self.status = torch.zeros(1, **i32)
+        self.text_embeds = torch.zeros(B, cfg.hidden_size, dtype=torch.bfloat16, device=self.device)
+        self.allocator: PageAllocator | None = None
+        self.batch_size = 0
+        self.host_seq_lens: list[int] = []
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.talker.ensure_attention_workspace(self.work_capacity)
+
+    # ------------------------------------------------------------------
+    # request admission (synthetic prefill: random KV contents)
+    # ------------------------------------------------------------------
+    def admit(self, context_lens: list[int], *, sampling: SamplingParams = SamplingParams(), seed: int = 0,
+              request_seeds: list[int] | None = None, fill_kv: bool = True) -> None:
+        """Admit len(context_lens) streams whose first context_lens[i] tokens are in the
+        KV pool (pages randomly permuted in the pool), with seeded random KV contents."""
+        cfg = self.cfg
+        B = len(context_lens)
+        if B > self.max_batch:
+            raise RuntimeError("batch exceeds max_batch")
+        P = cfg.page_size
+        rng = np.random.default_rng(seed)
+        num_pages = self.kv.num_pages
+        perm = torch.from_numpy(rng.permutation(num_pages).astype(np.int32))
+        self.allocator = PageAllocator(perm, self.device)
+        need = [(L + P - 1) // P for L in context_lens]
+        r2t = torch.zeros(B, cfg.max_context, dtype=torch.int32)
+        pages = self.allocator.alloc_prefix(sum(need)).cpu()
+        off = 0
+        for i, (L, n) in enumerate(zip(context_lens, need)):
+            if L + 1 > cfg.max_context:
+                raise ValueError("context exceeds max_context")
+            pg = pages[off: off + n].long()
+            off += n
+            slots = (pg[:, None] * P + torch.arange(P)[None, :]).reshape(-1)[:L]
+            r2t[i, :L] = slots.to(torch.int32)
+        self.r2t.req_to_token[:B].copy_(r2t.to(self.device))
+        self.seq_lens[:B].copy_(torch.tensor(context_lens, dtype=torch.long))
+        self.host_seq_lens = list(context_lens)
+        self.batch_size = B
+        if fill_kv:
+            g = torch.Generator(device=self.device).manual_seed(seed + 7)
+            for li in range(cfg.num_hidden_layers):
+                self.kv.k_buffer[li].normal_(generator=g)
+                self.kv.v_buffer[li].normal_(generator=g)
+        # sampling state
+        t = self.talker
+        t.repetition_penalties[:B].fill_(sampling.repetition_penalty)
+        t.repetition_mask[:B].zero_()
+        t.suppress_mask[:B].zero_()
+        t.sampling_temperatures[:B].fill_(sampling.temperature)
+        t.sampling_top_ks[:B].fill_(sampling.top_k)
+        t.sampling_top_ps[:B].fill_(sampling.top_p)
+        t.sampling_min_ps[:B].fill_(sampling.min_p)
+        ladder = (4, 8, 16, 32, 50, 64, 128, 256, 512, 1024)
+        t.max_top_k = next(w for w in ladder if w >= sampling.top_k)
+        seeds = request_seeds or [derive_sampling_seed("omni-b200", seed, f"req{i}") for i in range(B)]
+        t.sampling_seeds[:B].copy_(torch.tensor([derive_sampling_seed("semantic", s) for s in seeds]))
+        self.predictor.set_sampling(
+            temperature=[sampling.subtalker_temperature] * B, top_k=[sampling.subtalker_top_k] * B,
+            top_p=[sampling.subtalker_top_p] * B,
+            seeds=[derive_sampling_seed("subtalker", s) for s in seeds],
+            do_sample=[sampling.subtalker_dosample] * B, batch=B)
+        self.predictor.output_embeds[:B].zero_()
+        self.graph = None
+
+    # ------------------------------------------------------------------
+    def forward_batch(self) -> DecodeForwardBatch:
+        B = self.batch_size
+        return DecodeForwardBatch(
+            batch_size=B, positions=self.positions[:B], seq_lens=self.seq_lens[:B],
+            out_cache_loc=self.out_cache_loc[:B], req_pool_indices=self.req_pool_indices[:B],
+            page_indptr=self.page_indptr[: B + 1], page_indices=self.page_indices, work_indptr=self.work_indptr[: B + 1],
+            work_capacity=self.work_capacity, pages_per_chunk=self.pages_per_chunk)
+
+    def prepare_decode(self) -> DecodeForwardBatch:
+        """Device-side prepare_for_decode + ForwardBatch packing."""
+        B = self.batch_size
+        ops.decode_prepare(seq_lens=self.seq_lens[:B], req_pool_indices=self.req_pool_indices[:B],
+                           req_to_token=self.r2t.req_to_token, page_size=self.cfg.page_size,
+                           free_pages=self.allocator.free_pages, free_head=self.allocator.free_head,
+                           out_cache_loc=self.out_cache_loc[:B], positions=self.positions[:B],
+                           page_indptr=self.page_indptr[: B + 1], page_indices=self.page_indices,
+                           work_indptr=self.work_indptr[: B + 1], pages_per_chunk=self.pages_per_chunk,
+                           status=self.status)
+        return self.forward_batch()
+
+    def run_step(self) -> None:
+        """The whole decode step on the current stream (capturable)."""
+        fb = self.prepare_decode()
+        self.custom_decode_forward(fb, None, None)
+
+    def custom_decode_forward(self, forward_batch: DecodeForwardBatch, schedule_batch, requests):
+        """The hook that owns the decode forward (base.py:879-890)."""
+        B = forward_batch.batch_size
+        # the previous frame's summed codec embeddings are this frame's feedback input
+        feedback = self.predictor.output_embeds[:B]
+        logits = self.talker.forward(feedback, self.text_embeds[:B], forward_batch)
+        c0 = self.talker.sample_decode_tokens(logits, forward_batch)
+        codes, summed = self.predictor.code_predictor_forward(c0, self.talker.hidden[:B], forward_batch.positions)
+        return GenerationBatchResult(next_token_ids=c0, next_token_logits=logits, hidden_states=self.talker.hidden[:B],
+                                     codes=codes[:, :, 0], summed_embeds=summed[:, 0])
+
+    # ------------------------------------------------------------------
+    def _host_reserve(self) -> None:
+        self.allocator.reserve_host(self.host_seq_lens, self.cfg.page_size)
+        self.host_seq_lens = [L + 1 for L in self.host_seq_lens]
+        if max(self.host_seq_lens) >= self.cfg.max_context:
+            raise RuntimeError("a stream reached max_context")
+
+    def step(self, use_graph: bool = True) -> None:
+        """One decode step on device-resident inputs (text rows already in text_embeds)."""
+        self._host_reserve()
+        if use_graph:
+            if self.graph is None:
+                raise RuntimeError("capture() first")
+            self.graph.replay()
+        else:
+            self.run_step()
+
+    def capture(self, warmup: int = 1) -> None:
+        """Warm up eagerly (consuming `warmup` steps) and capture one step as a CUDA graph."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self._host_reserve()
+                self.run_step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        # recording executes nothing: the device state is unchanged by capture
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self.run_step()
+        torch.cuda.synchronize(self.device)
+        self.graph = g
+
+    # ------------------------------------------------------------------
+    # public end-to-end API: host text rows in, host codes out
+    # ------------------------------------------------------------------
+    def decode(self, text_embeds_host: torch.Tensor, codes_host: torch.Tensor | None = None) -> torch.Tensor:
+        """One frame for every live stream: copy the text rows in (pinned host -> HBM),
+        replay the step graph, copy the frame's codes out.  Returns codes [B, G] on the host."""
+        B = self.batch_size
+        self.text_embeds[:B].copy_(text_embeds_host, non_blocking=True)
+        self.step(use_graph=self.graph is not None)
+        if codes_host is None:
+            codes_host = torch.empty((B, self.cfg.predictor.num_code_groups), dtype=torch.long, pin_memory=True)
+        codes_host.copy_(self.predictor.output_codes[:B], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return codes_host

@@ -1,0 +1,216 @@
+"""The code predictor ("subtalker") of the Qwen3 talkers on sm_100a.
+
+Mirrors Qwen3TTSCodePredictor / Qwen3TTSTalker.code_predictor_forward
+(sglang_omni/models/qwen3_tts/sglang_model.py:447-490, 1317-1346, 1743-1879)
+and the Qwen3-Omni greedy variant (talker.py:1633-1732): per frame, one
+two-token pass [talker hidden, embedding of the layer-0 code] at cache slots
+0 and 1, then for each residual codebook j: lm_head[j] -> sample (or argmax)
+code j+1 -> gather its embedding (summed += it) -> a one-token pass at slot
+j + 2.  Every launch goes to libomni_b200.so; all buffers are allocated once
+for max_batch rows so the loop can be captured in a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from omni_b200 import ops
+from omni_b200.config import PredictorConfig
+from omni_b200.sampling_kernels import fused_raw_logit_block_k, predictor_sample_step
+
+
+def init_predictor_weights(cfg: PredictorConfig, *, seed: int, device, dtype=torch.bfloat16) -> dict:
+    """Seeded random weights: linears N(0, 0.02^2), norm gains 1 + N(0, 0.05^2)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    H, D = cfg.hidden_size, cfg.head_dim
+    hq, hkv, I, V = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.intermediate_size, cfg.vocab_size
+
+    def lin(*shape):
+        return (torch.randn(*shape, generator=g, device=device) * 0.02).to(dtype)
+
+    def gain(n):
+        return (1.0 + 0.05 * torch.randn(n, generator=g, device=device)).to(dtype)
+
+    layers = []
+    for _ in range(cfg.num_hidden_layers):
+        layers.append({
+            "input_layernorm": gain(H),
+            "qkv_proj": lin((hq + 2 * hkv) * D, H),
+            "q_norm": gain(D),
+            "k_norm": gain(D),
+            "o_proj": lin(H, hq * D),
+            "post_attention_layernorm": gain(H),
+            "gate_up_proj": lin(2 * I, H),
+            "down_proj": lin(H, I),
+        })
+    G = cfg.num_code_groups
+    return {
+        "layers": layers,
+        "norm": gain(H),
+        "lm_head": lin(G - 1, V, H),
+        "codec_embedding": lin(G - 1, V, H),
+    }
+
+
+class CodePredictor:
+    """Predictor stack + residual-codebook loop with persistent buffers."""
+
+    def __init__(self, cfg: PredictorConfig, weights: dict, *, max_batch: int, device, layer0_embedding: torch.Tensor):
+        self.cfg = cfg
+        self.w = weights
+        self.device = torch.device(device)
+        self.max_batch = max_batch
+        self.layer0_embedding = layer0_embedding  # the talker's codec embedding [V0, H]
+        H, D = cfg.hidden_size, cfg.head_dim
+        hq, hkv, I = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.intermediate_size
+        G, S = cfg.num_code_groups, cfg.cache_len
+        R = 2 * max_batch
+        bf = dict(device=self.device, dtype=torch.bfloat16)
+        self.cos_sin = ops.rope_cos_sin_cache(S, D, cfg.rope_theta, self.device)
+        L = cfg.num_hidden_layers
+        self.k_cache = torch.zeros(L, max_batch * S, hkv, D, **bf)
+        self.v_cache = torch.zeros(L, max_batch * S, hkv, D, **bf)
+        self.pair = torch.zeros(R, H, **bf)
+        self.h = torch.zeros(R, H, **bf)
+        self.normed = torch.zeros(R, H, **bf)
+        self.qkv = torch.zeros(R, (hq + 2 * hkv) * D, **bf)
+        self.q = torch.zeros(R, hq * D, **bf)
+        self.attn = torch.zeros(R, hq * D, **bf)
+        self.act = torch.zeros(R, I, **bf)
+        self.out = torch.zeros(R, H, **bf)
+        self.next_in = torch.zeros(max_batch, H, **bf)
+        self.logits = torch.zeros(G - 1, max_batch, cfg.vocab_size, **bf)
+        self.output_codes = torch.zeros(max_batch, G, dtype=torch.long, device=self.device)
+        self.output_embeds = torch.zeros(max_batch, H, **bf)
+        # per-row residual sampling state (sub_*_tensor of sglang_model.py:1115-1140)
+        self.sub_temperature_tensor = torch.full((max_batch,), 0.9, dtype=torch.float32, device=self.device)
+        self.sub_top_k_tensor = torch.full((max_batch,), 50, dtype=torch.long, device=self.device)
+        self.sub_top_p_tensor = torch.ones(max_batch, dtype=torch.float32, device=self.device)
+        self.sub_sampling_seed_tensor = torch.zeros(max_batch, dtype=torch.long, device=self.device)
+        self.sub_do_sample_tensor = torch.ones(max_batch, dtype=torch.uint8, device=self.device)
+        self.sub_sampled_max_top_k = 50
+        self.sub_sampled_has_top_p = True
+        self.sub_has_sampled_rows = True
+        self.sub_has_argmax_rows = False
+        ws = 0
+        for rows in (max_batch, R):
+            for k, n, e in ((H, (hq + 2 * hkv) * D, 0), (hq * D, H, 1), (H, 2 * I, 2), (I, H, 1),
+                            (H, cfg.vocab_size, 0)):
+                ws = max(ws, ops.linear_workspace_bytes(rows, k, n, e))
+        self.workspace = torch.zeros(max(ws, 256), dtype=torch.uint8, device=self.device)
+        self.scale = 1.0 / math.sqrt(D)
+
+    # ------------------------------------------------------------------
+    def set_sampling(self, *, temperature, top_k, top_p, seeds, do_sample, batch: int) -> None:
+        """Stage per-row residual sampling parameters (prepare_decode_buffers)."""
+        dev = self.device
+        self.sub_temperature_tensor[:batch].copy_(torch.as_tensor(temperature, dtype=torch.float32), non_blocking=True)
+        self.sub_top_k_tensor[:batch].copy_(torch.as_tensor(top_k, dtype=torch.long), non_blocking=True)
+        self.sub_top_p_tensor[:batch].copy_(torch.as_tensor(top_p, dtype=torch.float32), non_blocking=True)
+        self.sub_sampling_seed_tensor[:batch].copy_(torch.as_tensor(seeds, dtype=torch.long), non_blocking=True)
+        ds = torch.as_tensor(do_sample, dtype=torch.uint8)
+        self.sub_do_sample_tensor[:batch].copy_(ds, non_blocking=True)
+        top_k_list = [int(k) for k in torch.as_tensor(top_k).reshape(-1).tolist()]
+        top_p_list = [float(p) for p in torch.as_tensor(top_p).reshape(-1).tolist()]
+        ds_list = [bool(v) for v in ds.reshape(-1).tolist()]
+        sampled = [i for i, d in enumerate(ds_list) if d]
+        self.sub_has_sampled_rows = bool(sampled)
+        self.sub_has_argmax_rows = len(sampled) != len(ds_list)
+        bounded = [top_k_list[i] for i in sampled if 0 < top_k_list[i] < self.cfg.vocab_size]
+        if len(bounded) != len(sampled):
+            raise ValueError("unbounded subtalker top_k is outside the fused sampler's contract")
+        widest = max(bounded, default=4)
+        ladder = (4, 8, 16, 32, 50, 64, 128, 256, 512, 1024)
+        self.sub_sampled_max_top_k = next(w for w in ladder if w >= widest)
+        self.sub_sampled_has_top_p = any(0.0 < top_p_list[i] < 1.0 for i in sampled)
+        assert fused_raw_logit_block_k(self.sub_sampled_max_top_k) is not None
+        del dev
+
+    # ------------------------------------------------------------------
+    def forward_tokens(self, x: torch.Tensor, *, batch: int, tokens: int, cache_len: int) -> torch.Tensor:
+        """The predictor stack on rows (request, token) at slots cache_len.. ;
+        returns the final-normed rows (predictor_forward_tokens, sglang_model.py:2036-2098)."""
+        cfg = self.cfg
+        rows = batch * tokens
+        H, D = cfg.hidden_size, cfg.head_dim
+        hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        eps = cfg.rms_norm_eps
+        h, normed, qkv, q, attn, act = (self.h[:rows], self.normed[:rows], self.qkv[:rows], self.q[:rows],
+                                        self.attn[:rows], self.act[:rows])
+        ws = self.workspace
+        resid = x
+        for li, lw in enumerate(self.w["layers"]):
+            ops.rmsnorm(resid, lw["input_layernorm"], eps, out=normed)
+            ops.linear(normed, lw["qkv_proj"], out=qkv, workspace=ws)
+            ops.qknorm_rope_store(qkv, num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=lw["q_norm"],
+                                  k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin, q_out=q,
+                                  k_cache=self.k_cache[li], v_cache=self.v_cache[li], tokens_per_req=tokens,
+                                  slot_stride=cfg.cache_len, slot_base=cache_len)
+            ops.predictor_attention(q, self.k_cache[li], self.v_cache[li], num_q_heads=hq, num_kv_heads=hkv,
+                                    head_dim=D, tokens_per_req=tokens, slot_stride=cfg.cache_len,
+                                    slot_base=cache_len, sm_scale=self.scale, out=attn)
+            ops.linear(attn, lw["o_proj"], epilogue=ops.EPI_RESIDUAL, residual=resid, out=h, workspace=ws)
+            resid = h
+            ops.rmsnorm(h, lw["post_attention_layernorm"], eps, out=normed)
+            ops.linear(normed, lw["gate_up_proj"], epilogue=ops.EPI_SWIGLU, out=act, workspace=ws)
+            ops.linear(act, lw["down_proj"], epilogue=ops.EPI_RESIDUAL, residual=h, out=h, workspace=ws)
+        out = self.out[:rows]
+        ops.rmsnorm(h, self.w["norm"], eps, out=out)
+        return out
+
+    def code_predictor_forward(
+        self,
+        layer0_codes: torch.Tensor,
+        talker_hidden: torch.Tensor,
+        semantic_positions: torch.Tensor | None = None,
+    ) -> tuple[torch.Tensor, torch.Tensor]:
+        """(layer0_codes [B, 1] i64, talker_hidden [B, 1, H] bf16, semantic_positions [B])
+        -> (codes [B, G, 1] i64, summed [B, 1, H] bf16) (sglang_model.py:1317-1346)."""
+        cfg = self.cfg
+        if layer0_codes.ndim == 2:
+            layer0_codes = layer0_codes[:, 0]
+        if talker_hidden.ndim == 3:
+            talker_hidden = talker_hidden[:, 0]
+        B = layer0_codes.shape[0]
+        if B > self.max_batch:
+            raise RuntimeError("code predictor buffers are too small for this batch")
+        H, G = cfg.hidden_size, cfg.num_code_groups
+        if semantic_positions is None:
+            semantic_positions = torch.zeros(B, dtype=torch.long, device=self.device)
+        codes = self.output_codes[:B]
+        summed = self.output_embeds[:B]
+        pair = self.pair[: 2 * B]
+        from omni_b200 import _lib
+
+        _lib.call("omni_predictor_pair_inputs", layer0_codes.data_ptr(), talker_hidden.data_ptr(),
+                  talker_hidden.stride(0), self.layer0_embedding.data_ptr(), B, H, pair.data_ptr(), summed.data_ptr(),
+                  codes.data_ptr(), codes.stride(0), _lib.stream_of(self.device))
+        out = self.forward_tokens(pair, batch=B, tokens=2, cache_len=0)
+        last = out[1::2]  # the layer-0 token's row of each request (row stride 2H)
+        argmax_all = not self.sub_has_sampled_rows
+        for j in range(G - 1):
+            logits = self.logits[j, :B]
+            ops.linear(last, self.w["lm_head"][j], out=logits, workspace=self.workspace)
+            predictor_sample_step(
+                logits,
+                temperatures=self.sub_temperature_tensor[:B],
+                top_ks=self.sub_top_k_tensor[:B],
+                top_ps=self.sub_top_p_tensor[:B],
+                seeds=self.sub_sampling_seed_tensor[:B],
+                positions=semantic_positions,
+                pos_mul=G - 1,
+                pos_add=j + 1,
+                do_sample=self.sub_do_sample_tensor[:B] if self.sub_has_argmax_rows else None,
+                argmax_all=argmax_all,
+                max_top_k=self.sub_sampled_max_top_k,
+                has_top_p=self.sub_sampled_has_top_p,
+                codes=codes[:, j + 1],
+                table=self.w["codec_embedding"][j],
+                gathered=self.next_in[:B],
+                summed=summed,
+            )
+            if j < G - 2:
+                last = self.forward_tokens(self.next_in[:B], batch=B, tokens=1, cache_len=2 + j)
+        return codes.unsqueeze(-1), summed.unsqueeze(1)

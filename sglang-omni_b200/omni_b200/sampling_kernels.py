@@ -223,6 +223,7 @@ def layer0_sample(
     positions: torch.Tensor,
     max_top_k: int,
     out: torch.Tensor | None = None,
+    rep_mask_update: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Layer-0 codec token draw from fp32 logits [rows, vocab]: repetition penalty,
     suppression, temperature, top-k/top-p/min-p and the seeded Gumbel draw
@@ -251,6 +252,7 @@ def layer0_sample(
         positions.data_ptr(),
         int(max_top_k),
         out.data_ptr(),
+        _lib.ptr(u8(rep_mask_update)),
         _lib.stream_of(logits.device),
     )
     return out

@@ -1,0 +1,179 @@
+"""The dense Qwen3 talker decode forward on sm_100a.
+
+Mirrors Qwen3TTSTalker.forward / Qwen3OmniTalker.forward at decode
+(sglang_omni/models/qwen3_tts/sglang_model.py:1273-1302;
+sglang_omni/models/qwen3_omni/components/talker.py:1259-1340): the decode
+input row (feedback embedding + text embedding) through L decoder layers
+(RMSNorm -> QKV -> q/k RMSNorm -> neox RoPE + paged KV store -> paged GQA decode
+attention -> o_proj + residual -> RMSNorm -> SwiGLU MLP + residual), the final
+RMSNorm and the codec head in fp32, then the layer-0 codec token draw
+(sample_decode_tokens, talker.py:1376-1412).
+
+Per layer the forward is 8 launches: rmsnorm, qkv GEMM, qknorm_rope_store,
+paged attention, o_proj GEMM (+residual), rmsnorm, gate_up GEMM (+SwiGLU),
+down GEMM (+residual); GEMMs run on the tcgen05 tensor cores.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from omni_b200 import ops
+from omni_b200.config import TalkerConfig
+from omni_b200.kv_cache import PagedKVPool
+from omni_b200.sampling_kernels import layer0_sample
+
+
+def init_talker_weights(cfg: TalkerConfig, *, seed: int, device, dtype=torch.bfloat16) -> dict:
+    """Seeded random weights: linears and embeddings N(0, 0.02^2), norm gains 1 + N(0, 0.05^2)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    H, D = cfg.hidden_size, cfg.head_dim
+    hq, hkv, I, V = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.intermediate_size, cfg.vocab_size
+
+    def lin(*shape):
+        return (torch.randn(*shape, generator=g, device=device) * 0.02).to(dtype)
+
+    def gain(n):
+        return (1.0 + 0.05 * torch.randn(n, generator=g, device=device)).to(dtype)
+
+    layers = []
+    for _ in range(cfg.num_hidden_layers):
+        layers.append({
+            "input_layernorm": gain(H),
+            "qkv_proj": lin((hq + 2 * hkv) * D, H),
+            "q_norm": gain(D),
+            "k_norm": gain(D),
+            "o_proj": lin(H, hq * D),
+            "post_attention_layernorm": gain(H),
+            "gate_up_proj": lin(2 * I, H),
+            "down_proj": lin(H, I),
+        })
+    return {"layers": layers, "norm": gain(H), "codec_head": lin(V, H), "codec_embedding": lin(V, H)}
+
+
+@dataclass
+class DecodeForwardBatch:
+    """Device tensors of one packed decode batch (ForwardBatch.init_new at decode)."""
+
+    batch_size: int
+    positions: torch.Tensor       # i64 [B]
+    seq_lens: torch.Tensor        # i64 [B] (after this step's token)
+    out_cache_loc: torch.Tensor   # i64 [B]
+    req_pool_indices: torch.Tensor
+    page_indptr: torch.Tensor     # i32 [B + 1]
+    page_indices: torch.Tensor    # i32
+    work_indptr: torch.Tensor     # i32 [B + 1]
+    work_capacity: int
+    pages_per_chunk: int
+
+
+class DenseTalker:
+    def __init__(self, cfg: TalkerConfig, weights: dict, *, max_batch: int, device, kv_pool: PagedKVPool):
+        self.cfg = cfg
+        self.w = weights
+        self.device = torch.device(device)
+        self.max_batch = max_batch
+        self.kv = kv_pool
+        H, D = cfg.hidden_size, cfg.head_dim
+        hq, hkv, I, V = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.intermediate_size, cfg.vocab_size
+        bf = dict(device=self.device, dtype=torch.bfloat16)
+        B = max_batch
+        self.cos_sin = ops.rope_cos_sin_cache(cfg.max_context, D, cfg.rope_theta, self.device)
+        self.h = torch.zeros(B, H, **bf)
+        self.normed = torch.zeros(B, H, **bf)
+        self.qkv = torch.zeros(B, (hq + 2 * hkv) * D, **bf)
+        self.q = torch.zeros(B, hq * D, **bf)
+        self.attn = torch.zeros(B, hq * D, **bf)
+        self.act = torch.zeros(B, I, **bf)
+        self.hidden = torch.zeros(B, H, **bf)
+        self.logits = torch.zeros(B, V, dtype=torch.float32, device=self.device)
+        self.sampled_token_ids = torch.zeros(B, dtype=torch.long, device=self.device)
+        ws = 0
+        for k, n, e in ((H, (hq + 2 * hkv) * D, 0), (hq * D, H, 1), (H, 2 * I, 2), (I, H, 1), (H, V, 3)):
+            ws = max(ws, ops.linear_workspace_bytes(B, k, n, e))
+        self.workspace = torch.zeros(max(ws, 256), dtype=torch.uint8, device=self.device)
+        self.attn_workspace: torch.Tensor | None = None
+        self.scale = 1.0 / math.sqrt(D)
+        # layer-0 sampling state (talker.py:836-1010 buffers)
+        f32 = dict(device=self.device, dtype=torch.float32)
+        self.repetition_penalties = torch.ones(B, **f32)
+        self.repetition_mask = torch.zeros(B, V, dtype=torch.uint8, device=self.device)
+        self.suppress_mask = torch.zeros(B, V, dtype=torch.uint8, device=self.device)
+        self.sampling_temperatures = torch.ones(B, **f32)
+        self.sampling_top_ks = torch.full((B,), 50, dtype=torch.long, device=self.device)
+        self.sampling_top_ps = torch.ones(B, **f32)
+        self.sampling_min_ps = torch.zeros(B, **f32)
+        self.sampling_seeds = torch.zeros(B, dtype=torch.long, device=self.device)
+        self.max_top_k = 50
+
+    def ensure_attention_workspace(self, work_capacity: int) -> None:
+        need = ops.paged_attention_workspace_bytes(self.max_batch, self.cfg.num_key_value_heads, work_capacity)
+        if self.attn_workspace is None or self.attn_workspace.numel() < need:
+            self.attn_workspace = torch.zeros(need, dtype=torch.uint8, device=self.device)
+
+    def forward(self, feedback: torch.Tensor, text: torch.Tensor | None, fb: DecodeForwardBatch) -> torch.Tensor:
+        """Decode forward of B rows whose input is feedback (+ text); fills self.logits
+        (fp32) and self.hidden and returns the logits [B, V]."""
+        cfg = self.cfg
+        B = fb.batch_size
+        H, D = cfg.hidden_size, cfg.head_dim
+        hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        eps = cfg.rms_norm_eps
+        h, normed, qkv, q, attn, act = (self.h[:B], self.normed[:B], self.qkv[:B], self.q[:B], self.attn[:B],
+                                        self.act[:B])
+        ws = self.workspace
+        self.ensure_attention_workspace(fb.work_capacity)
+        for li, lw in enumerate(self.w["layers"]):
+            if li == 0:
+                if text is not None:
+                    ops.rmsnorm(feedback, lw["input_layernorm"], eps, addend=text, residual_out=h, out=normed)
+                else:
+                    h.copy_(feedback)
+                    ops.rmsnorm(h, lw["input_layernorm"], eps, out=normed)
+            else:
+                ops.rmsnorm(h, lw["input_layernorm"], eps, out=normed)
+            ops.linear(normed, lw["qkv_proj"], out=qkv, workspace=ws)
+            kc, vc = self.kv.k_buffer[li], self.kv.v_buffer[li]
+            ops.qknorm_rope_store(qkv, num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=lw["q_norm"],
+                                  k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin, q_out=q, k_cache=kc,
+                                  v_cache=vc, positions=fb.positions, cache_loc=fb.out_cache_loc)
+            ops.paged_decode_attention(q, kc, vc, page_indptr=fb.page_indptr, page_indices=fb.page_indices,
+                                       seq_lens=fb.seq_lens, work_indptr=fb.work_indptr, num_q_heads=hq,
+                                       num_kv_heads=hkv, head_dim=D, page_size=cfg.page_size,
+                                       pages_per_chunk=fb.pages_per_chunk, work_capacity=fb.work_capacity,
+                                       sm_scale=self.scale, out=attn, workspace=self.attn_workspace)
+            ops.linear(attn, lw["o_proj"], epilogue=ops.EPI_RESIDUAL, residual=h, out=h, workspace=ws)
+            ops.rmsnorm(h, lw["post_attention_layernorm"], eps, out=normed)
+            ops.linear(normed, lw["gate_up_proj"], epilogue=ops.EPI_SWIGLU, out=act, workspace=ws)
+            ops.linear(act, lw["down_proj"], epilogue=ops.EPI_RESIDUAL, residual=h, out=h, workspace=ws)
+        hidden = self.hidden[:B]
+        ops.rmsnorm(h, self.w["norm"], eps, out=hidden)
+        logits = self.logits[:B]
+        ops.linear(hidden, self.w["codec_head"], epilogue=ops.EPI_F32, out=logits, workspace=ws)
+        return logits
+
+    def sample_decode_tokens(self, logits: torch.Tensor, fb: DecodeForwardBatch) -> torch.Tensor:
+        """Repetition penalty, suppression and the seeded layer-0 draw
+        (sample_decode_tokens, talker.py:1376-1412); marks the drawn token in the
+        repetition mask for the next step."""
+        B = fb.batch_size
+        out = self.sampled_token_ids[:B]
+        layer0_sample(
+            logits,
+            penalties=self.repetition_penalties[:B],
+            repetition_mask=self.repetition_mask[:B],
+            suppress_mask=self.suppress_mask[:B],
+            temperatures=self.sampling_temperatures[:B],
+            top_ks=self.sampling_top_ks[:B],
+            top_ps=self.sampling_top_ps[:B],
+            min_ps=self.sampling_min_ps[:B],
+            seeds=self.sampling_seeds[:B],
+            positions=fb.positions,
+            max_top_k=self.max_top_k,
+            out=out,
+            rep_mask_update=self.repetition_mask[:B],
+        )
+        return out

@@ -1,0 +1,181 @@
+"""One full decode step (packing -> talker -> layer-0 draw -> code predictor) on
+the GPU against the CPU oracle.
+
+- packing (positions, slots, page table): bit-exact;
+- talker logits and final hidden: cosine >= 0.999, max-abs <= 2e-2 x scale
+  (bf16 tolerance of the north-star contract);
+- every drawn token (layer 0 and 15 residual codebooks): bit-exact against the
+  oracle sampler applied to the device's own logits;
+- predictor lm_head logits with the device's codes fed back (teacher forcing):
+  bf16 tolerance; summed codec embeddings: bit-exact;
+- CUDA-graph replay == eager, bit for bit; rows never mix (batch invariance).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import sampler as orc
+from oracle.model import OracleTalker, bits
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def cos_err(a: torch.Tensor, b: torch.Tensor):
+    a, b = a.float().flatten().cpu(), b.float().flatten().cpu()
+    cos = torch.nn.functional.cosine_similarity(a, b, dim=0).item()
+    return cos, (a - b).abs().max().item(), b.abs().max().item()
+
+
+def make_runner(layers=2, lens=(16, 1, 33, 100, 200, 15, 64, 17), seed=0, max_batch=8, sampling=None):
+    from omni_b200.config import SamplingParams, TalkerConfig
+    from omni_b200.model_runner import TalkerDecodeRunner
+
+    cfg = TalkerConfig(num_hidden_layers=layers, max_context=1024)
+    pages = sum((L + 16) // 16 for L in lens) + 32
+    r = TalkerDecodeRunner(cfg, max_batch=max_batch, num_pages=pages, seed=seed)
+    r.admit(list(lens), sampling=sampling or SamplingParams(), seed=seed + 5)
+    g = torch.Generator(device=DEV).manual_seed(seed + 11)
+    r.text_embeds.normal_(generator=g)
+    r.predictor.output_embeds.normal_(generator=g)
+    return r
+
+
+@pytest.mark.parametrize("dosample", [True, False])
+def test_decode_step_matches_oracle(dosample):
+    from omni_b200.config import SamplingParams
+
+    sp = SamplingParams(subtalker_dosample=dosample)
+    r = make_runner(sampling=sp)
+    B = r.batch_size
+    cfg = r.cfg
+    # snapshot the pre-step state for the oracle
+    seq0 = r.seq_lens[:B].cpu().numpy()
+    r2t0 = r.r2t.req_to_token[:B].cpu().numpy()
+    free = r.allocator.free_pages.cpu().numpy()
+    head0 = int(r.allocator.free_head.item())
+    kpool = r.kv.k_buffer.float().cpu()
+    vpool = r.kv.v_buffer.float().cpu()
+    feedback = r.predictor.output_embeds[:B].clone().cpu()
+    text = r.text_embeds[:B].clone().cpu()
+    t = r.talker
+    l0_state = dict(penalties=t.repetition_penalties[:B].cpu().numpy(), rep_mask=t.repetition_mask[:B].cpu().numpy(),
+                    suppress_mask=t.suppress_mask[:B].cpu().numpy(), temperature=t.sampling_temperatures[:B].cpu().numpy(),
+                    top_k=t.sampling_top_ks[:B].cpu().numpy(), top_p=t.sampling_top_ps[:B].cpu().numpy(),
+                    min_p=t.sampling_min_ps[:B].cpu().numpy(), seed=t.sampling_seeds[:B].cpu().numpy(),
+                    max_top_k=t.max_top_k)
+    p = r.predictor
+    sub = dict(temperature=p.sub_temperature_tensor[:B].cpu().numpy(), top_k=p.sub_top_k_tensor[:B].cpu().numpy(),
+               top_p=p.sub_top_p_tensor[:B].cpu().numpy(), seed=p.sub_sampling_seed_tensor[:B].cpu().numpy(),
+               do_sample=p.sub_do_sample_tensor[:B].cpu().numpy(), max_top_k=p.sub_sampled_max_top_k,
+               has_top_p=p.sub_sampled_has_top_p)
+
+    r.step(use_graph=False)
+    torch.cuda.synchronize()
+
+    # ---- packing: bit-exact ----
+    sl, r2t1, loc, pos, _, _, pgp, pgi, head1 = orc.decode_prepare(seq0, np.arange(B), r2t0, cfg.page_size, free,
+                                                                   free_head=head0)
+    assert r.seq_lens[:B].cpu().numpy().tolist() == sl.tolist()
+    assert r.out_cache_loc[:B].cpu().numpy().tolist() == loc.tolist()
+    assert r.positions[:B].cpu().numpy().tolist() == pos.tolist()
+    assert r.page_indptr[: B + 1].cpu().numpy().tolist() == pgp.tolist()
+    assert r.page_indices[: pgp[-1]].cpu().numpy().tolist() == pgi.tolist()
+    assert np.array_equal(r.r2t.req_to_token[:B].cpu().numpy(), r2t1)
+    assert int(r.allocator.free_head.item()) == head1
+
+    # ---- talker: bf16 tolerance ----
+    o = OracleTalker(cfg, r.w, r.predictor.w)
+    logits_o, hidden_o = o.talker_forward(feedback, text, torch.from_numpy(pos), torch.from_numpy(loc),
+                                          torch.from_numpy(sl), torch.from_numpy(r2t1), kpool, vpool)
+    cos, err, scale = cos_err(t.hidden[:B], hidden_o)
+    assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0), (cos, err, scale)
+    cos, err, scale = cos_err(t.logits[:B], logits_o)
+    assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0), (cos, err, scale)
+    # K/V written at the new slots
+    kdev = r.kv.k_buffer[:, torch.from_numpy(loc).to(DEV)].float().cpu()
+    cos, err, scale = cos_err(kdev, kpool[:, torch.from_numpy(loc)])
+    assert cos >= 0.999, cos
+
+    # ---- layer-0 draw: bit-exact given the device logits ----
+    l0_state["positions"] = pos
+    c0 = t.sampled_token_ids[:B].cpu()
+    assert o.layer0(t.logits[:B].cpu(), l0_state).tolist() == c0.tolist()
+    # the drawn token is marked in the repetition mask
+    assert t.repetition_mask[torch.arange(B, device=DEV), c0.to(DEV)].all()
+
+    # ---- predictor: teacher-forced logits within tolerance, draws bit-exact ----
+    codes = p.output_codes[:B].cpu().numpy()
+    assert codes[:, 0].tolist() == c0.tolist()
+    codes_o, summed_o, logits_po = o.code_predictor(c0, t.hidden[:B].cpu(), torch.from_numpy(pos), sub,
+                                                    forced_codes=codes)
+    G = cfg.predictor.num_code_groups
+    for j in range(G - 1):
+        lg = p.logits[j, :B]
+        cos, err, scale = cos_err(lg, logits_po[j])
+        assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0), (j, cos, err, scale)
+        drawn = orc.sample_topk_topp(bits(lg), sub["temperature"], sub["top_k"], sub["top_p"], sub["seed"],
+                                     pos * (G - 1) + (j + 1), max_top_k=sub["max_top_k"], has_top_p=sub["has_top_p"])
+        am = np.argmax(lg.float().cpu().numpy(), axis=1)
+        want = np.where(sub["do_sample"].astype(bool), drawn, am)
+        assert codes[:, j + 1].tolist() == want.tolist(), j
+    assert np.array_equal(bits(p.output_embeds[:B]), summed_o)
+
+
+def test_graph_replay_is_bit_identical_to_eager():
+    a = make_runner(seed=1)
+    b = make_runner(seed=1)
+    b.capture(warmup=1)
+    a.step(use_graph=False)  # the same number of steps as b's warm-up
+    for _ in range(3):
+        a.step(use_graph=False)
+        b.step(use_graph=True)
+        torch.cuda.synchronize()
+        assert torch.equal(a.predictor.output_codes, b.predictor.output_codes)
+        assert torch.equal(a.talker.logits, b.talker.logits)
+        assert torch.equal(a.predictor.output_embeds, b.predictor.output_embeds)
+        assert torch.equal(a.seq_lens, b.seq_lens)
+
+
+def test_rows_never_mix():
+    """A row's frame does not depend on the other rows of the batch."""
+    lens = (16, 1, 33, 100, 200, 15, 64, 17)
+    full = make_runner(lens=lens, seed=2)
+    full.step(use_graph=False)
+    part = make_runner(lens=lens[:4], seed=2)
+    # same per-row inputs: copy the full runner's initial feedback/text rows of the first 4 streams
+    ref = make_runner(lens=lens, seed=2)
+    part.text_embeds[:4].copy_(ref.text_embeds[:4])
+    part.predictor.output_embeds[:4].copy_(ref.predictor.output_embeds[:4])
+    part.talker.sampling_seeds[:4].copy_(ref.talker.sampling_seeds[:4])
+    part.predictor.sub_sampling_seed_tensor[:4].copy_(ref.predictor.sub_sampling_seed_tensor[:4])
+    # KV pool contents of the first 4 streams' slots
+    n4 = sum((L + 15) // 16 for L in lens[:4])
+    slots_full = ref.r2t.req_to_token[:4]
+    slots_part = part.r2t.req_to_token[:4]
+    for i, L in enumerate(lens[:4]):
+        part.kv.k_buffer[:, slots_part[i, :L].long()] = ref.kv.k_buffer[:, slots_full[i, :L].long()]
+        part.kv.v_buffer[:, slots_part[i, :L].long()] = ref.kv.v_buffer[:, slots_full[i, :L].long()]
+    del n4
+    part.step(use_graph=False)
+    torch.cuda.synchronize()
+    assert torch.equal(part.predictor.output_codes[:4], full.predictor.output_codes[:4])
+    assert torch.equal(part.talker.logits[:4], full.talker.logits[:4])
+
+
+def test_public_decode_api_round_trip():
+    r = make_runner(seed=4)
+    r.capture(warmup=1)
+    B = r.batch_size
+    text = torch.randn(B, r.cfg.hidden_size).to(torch.bfloat16).pin_memory()
+    codes = r.decode(text)
+    assert codes.shape == (B, r.cfg.predictor.num_code_groups)
+    assert (codes[:, 0] < r.cfg.vocab_size).all() and (codes[:, 1:] < r.cfg.predictor.vocab_size).all()
+    assert torch.equal(codes, r.predictor.output_codes[:B].cpu())
+    from omni_b200 import device_status
+
+    assert device_status() == 0
