@@ -145,8 +145,8 @@ OMNI_API int omni_predictor_pair_inputs(const int64_t* layer0_codes, const void*
 #define OMNI_EPI_SWIGLU 2   /* W = [gate; up] (2I x K): y[:, :I] = silu(g) * u   */
 #define OMNI_EPI_F32 3      /* y = x W^T in f32 (logits)                          */
 
-/* Bytes of split-K workspace omni_linear needs for this shape (0 = none).
- * splits = 0 lets the library choose. */
+/* Bytes of global workspace omni_linear needs for this shape: always 0 (the
+ * split-K partials are reduced in the cluster's distributed shared memory). */
 OMNI_API int64_t omni_linear_workspace_bytes(int64_t rows, int64_t k, int64_t n, int32_t epilogue, int32_t splits);
 
 /* y[rows, N] = epilogue(x[rows, K] . w[N, K]^T): the decode-step linears
@@ -154,8 +154,9 @@ OMNI_API int64_t omni_linear_workspace_bytes(int64_t rows, int64_t k, int64_t n,
  * SiluAndMul / codec_head / lm_head of thinker_model.py:152-402,
  * talker.py:216-247, sglang_model.py:1294-1302, 2101-2152).
  *   x, w, residual bf16; y bf16 (f32 for OMNI_EPI_F32); K % 64 == 0, N % 128 == 0.
- *   workspace: >= omni_linear_workspace_bytes, 256-byte aligned, ZERO-FILLED
- *   before first use (the kernel leaves its counters at zero again). */
+ *   splits: K-splits per 128-feature tile (one thread-block cluster each),
+ *   0 = chosen by the library so that one wave covers the GPU, else 1..16.
+ *   workspace / workspace_bytes: unused (may be NULL / 0). */
 OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n,
                          int32_t epilogue, const void* residual, int64_t residual_stride, void* y, int64_t y_stride,
                          void* workspace, int64_t workspace_bytes, int32_t splits, void* stream);

@@ -7,9 +7,13 @@
 // sit on the MMA's M axis (TMEM lanes), and up to 256 activation rows, which
 // sit on its N axis (TMEM columns).  W tiles (128 x 64, bf16, 128-byte
 // swizzle) stream from HBM through a TMA pipeline; X tiles come from L2.
-// Split-K spreads each feature tile over several CTAs so that one wave fills
-// the 148 SMs; the partial tiles are reduced in split order by the last CTA
-// of the tile to arrive (deterministic, no spinning).
+//
+// Split-K: the S CTAs that share a feature tile form one thread-block cluster
+// (S <= 16, chosen so that every cluster of the grid is co-resident).  Each
+// CTA stages its fp32 partial tile in its own shared memory; after a hardware
+// cluster barrier, CTA c reduces rows c, c + S, ... of the tile by reading all
+// S partials over distributed shared memory in split order (deterministic),
+// applies the epilogue and stores the result.  No global scratch memory.
 //
 // Programmatic dependent launch: weights never depend on the previous kernel,
 // so the producer issues the first stages' weight loads before
@@ -51,9 +55,30 @@ struct GemmParams {
   int64_t res_stride;
   void* y;
   int64_t y_stride;
-  float* partials;    // [tiles][row tiles][splits][row_tile][128]
-  int* counters;      // [tiles][row tiles]
 };
+
+OMNI_DEVINL uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+OMNI_DEVINL void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+OMNI_DEVINL uint32_t map_cluster(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+OMNI_DEVINL float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
 
 OMNI_DEVINL float silu(float g) { return g / (1.0f + expf(-g)); }
 
@@ -73,7 +98,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   uint64_t* empty = full + kMaxStages;
   uint64_t* mma_done = empty + kMaxStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
-  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort, [1] last
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, rtile = blockIdx.y, split = blockIdx.z;
@@ -196,79 +221,73 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
-  if (aborted) return;
 
-  // ---- split-K: publish the partial tile, the last CTA of the tile reduces ----
-  const int nrt = gridDim.y;
-  const size_t tile_elems = (size_t)Rt * kTileN;
-  const bool split_k = p.splits > 1;
-  float* part_base = nullptr;
-  if (split_k) {
-    part_base = p.partials + ((size_t)(tile * nrt + rtile) * p.splits) * tile_elems;
-    float4* dst = reinterpret_cast<float4*>(part_base + (size_t)split * tile_elems);
-    const float4* src = reinterpret_cast<const float4*>(stage);
-    for (int i = threadIdx.x; i < (int)(tile_elems / 4); i += kThreadsG) dst[i] = src[i];
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int* ctr = p.counters + tile * nrt + rtile;
-      const int old = atomicAdd(ctr, 1);
-      const int last = old == p.splits - 1;
-      if (last) *ctr = 0;  // restore for the next launch (graph replays)
-      flags[1] = last;
+  // ---- split-K reduction over the cluster's shared memory ----
+  // Every CTA takes part in both cluster barriers, aborted or not.
+  const int S = p.splits;
+  if (S > 1) cluster_sync();  // all partial tiles staged and visible cluster-wide
+  const uint32_t crank = S > 1 ? cluster_ctarank() : 0u;
+  const uint32_t stage_local = smem_u32(stage);
+  const bool any_abort = aborted;
+  const int rows_here = min(Rt, p.rows - row0);
+  // partial of split s, row r, features f..f+3 (s in split order)
+  auto acc4 = [&](int r, int f) -> float4 {
+    const uint32_t off = (uint32_t)((r * kTileN + f) * 4);
+    if (S == 1) return *reinterpret_cast<const float4*>(stage + r * kTileN + f);
+    float4 a = ld_cluster_f4(map_cluster(stage_local + off, 0));
+    for (int q = 1; q < S; ++q) {
+      const float4 b = ld_cluster_f4(map_cluster(stage_local + off, (uint32_t)q));
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
     }
-    __syncthreads();
-    if (!flags[1]) return;
-    __threadfence();
-  }
-
-  auto acc_at = [&](int r, int f) -> float {
-    if (!split_k) return stage[r * kTileN + f];
-    float a = __ldcg(part_base + (size_t)r * kTileN + f);
-    for (int s = 1; s < p.splits; ++s) a = a + __ldcg(part_base + (size_t)s * tile_elems + (size_t)r * kTileN + f);
     return a;
   };
-
-  const int rows_here = min(Rt, p.rows - row0);
-  if (EPI == kEpiSwiGLU) {
-    // features 0..63: gate, 64..127: up, for outputs tile*64 .. tile*64+63
-    uint16_t* Y = static_cast<uint16_t*>(p.y);
-    for (int idx = threadIdx.x; idx < rows_here * 16; idx += kThreadsG) {
-      const int r = idx >> 4, g = (idx & 15) * 4;
-      float o[4];
+  if (!any_abort) {
+    if (EPI == kEpiSwiGLU) {
+      // features 0..63: gate, 64..127: up, for outputs tile*64 .. tile*64+63
+      uint16_t* Y = static_cast<uint16_t*>(p.y);
+      const int nr = (rows_here - (int)crank + S - 1) / S;
+      for (int idx = threadIdx.x; idx < nr * 16; idx += kThreadsG) {
+        const int r = (int)crank + (idx >> 4) * S;
+        const int g = (idx & 15) * 4;
+        const float4 gt = acc4(r, g), up = acc4(r, 64 + g);
+        const float gg[4] = {gt.x, gt.y, gt.z, gt.w}, uu[4] = {up.x, up.y, up.z, up.w};
+        float o[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float gt = bf2f(f2bf(acc_at(r, g + j)));
-        const float up = bf2f(f2bf(acc_at(r, 64 + g + j)));
-        o[j] = silu(gt) * up;
-      }
-      uint2 v = make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
-      *reinterpret_cast<uint2*>(Y + (int64_t)(row0 + r) * p.y_stride + tile * 64 + g) = v;
-    }
-  } else {
-    for (int idx = threadIdx.x; idx < rows_here * 32; idx += kThreadsG) {
-      const int r = idx >> 5, f = (idx & 31) * 4;
-      const int64_t col = (int64_t)tile * kTileN + f;
-      float o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) o[j] = acc_at(r, f + j);
-      if (EPI == kEpiF32) {
-        float* Y = static_cast<float*>(p.y);
-        *reinterpret_cast<float4*>(Y + (int64_t)(row0 + r) * p.y_stride + col) = make_float4(o[0], o[1], o[2], o[3]);
-      } else {
-        if (EPI == kEpiResidual) {
-          const uint2 rv = *reinterpret_cast<const uint2*>(p.residual + (int64_t)(row0 + r) * p.res_stride + col);
-          o[0] += bf_lo(rv.x);
-          o[1] += bf_hi(rv.x);
-          o[2] += bf_lo(rv.y);
-          o[3] += bf_hi(rv.y);
-        }
-        uint16_t* Y = static_cast<uint16_t*>(p.y);
-        *reinterpret_cast<uint2*>(Y + (int64_t)(row0 + r) * p.y_stride + col) =
+        for (int j = 0; j < 4; ++j) o[j] = silu(bf2f(f2bf(gg[j]))) * bf2f(f2bf(uu[j]));
+        *reinterpret_cast<uint2*>(Y + (int64_t)(row0 + r) * p.y_stride + tile * 64 + g) =
             make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
+      }
+    } else {
+      // rows crank, crank + S, ...: 32 threads per row, 4 features each
+      const int nr = (rows_here - (int)crank + S - 1) / S;
+      for (int idx = threadIdx.x; idx < nr * 32; idx += kThreadsG) {
+        const int r = (int)crank + (idx >> 5) * S;
+        const int f = (idx & 31) * 4;
+        const int64_t col = (int64_t)tile * kTileN + f;
+        const float4 a = acc4(r, f);
+        float o[4] = {a.x, a.y, a.z, a.w};
+        if (EPI == kEpiF32) {
+          float* Y = static_cast<float*>(p.y);
+          *reinterpret_cast<float4*>(Y + (int64_t)(row0 + r) * p.y_stride + col) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
+          if (EPI == kEpiResidual) {
+            const uint2 rv = *reinterpret_cast<const uint2*>(p.residual + (int64_t)(row0 + r) * p.res_stride + col);
+            o[0] += bf_lo(rv.x);
+            o[1] += bf_hi(rv.x);
+            o[2] += bf_lo(rv.y);
+            o[3] += bf_hi(rv.y);
+          }
+          uint16_t* Y = static_cast<uint16_t*>(p.y);
+          *reinterpret_cast<uint2*>(Y + (int64_t)(row0 + r) * p.y_stride + col) =
+              make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
+        }
       }
     }
   }
+  if (S > 1) cluster_sync();  // no CTA leaves while a peer still reads its partial
 }
 
 // ---------------------------------------------------------------------------
@@ -315,7 +334,71 @@ int num_sms() {
   return n;
 }
 
-Plan make_plan(int64_t rows, int64_t k, int64_t n, int epi, int splits_req) {
+constexpr int kMaxSplits = 16;
+
+template <int EPI>
+void set_kernel_attrs() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  });
+}
+
+// Co-resident clusters of S CTAs with this much shared memory (cached).
+template <int EPI>
+int max_active_clusters(int S, size_t smem) {
+  static std::mutex mu;
+  static int cache[kMaxSplits + 1][64];  // [S][smem KB / 4]
+  static bool init = false;
+  std::lock_guard<std::mutex> g(mu);
+  if (!init) {
+    for (auto& row : cache)
+      for (int& v : row) v = -1;
+    init = true;
+  }
+  const int key = (int)((smem + 4095) / 4096);
+  if (key >= 64) return 0;
+  int& slot = cache[S][key];
+  if (slot >= 0) return slot;
+  set_kernel_attrs<EPI>();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, (unsigned)S);
+  cfg.blockDim = dim3(kThreadsG);
+  cfg.dynamicSmemBytes = (size_t)key * 4096;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)S;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<EPI>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  slot = n;
+  return n;
+}
+
+size_t plan_smem(int row_tile, int stages) {
+  const size_t stage_bytes = (size_t)kTileN * kBK * 2 + (size_t)row_tile * kBK * 2;
+  return 1024 + (size_t)stages * stage_bytes + 2 * kMaxStages * 8 + 8 + 16;
+}
+
+int plan_stages(int row_tile, int kb_per) {
+  const size_t stage_bytes = (size_t)kTileN * kBK * 2 + (size_t)row_tile * kBK * 2;
+  int st = kb_per < 4 ? kb_per : 4;
+  if (st < 1) st = 1;
+  // the epilogue staging [row_tile][128] fp32 reuses the stage buffers
+  const size_t staging = (size_t)row_tile * kTileN * 4;
+  while ((size_t)st * stage_bytes < staging && st < kMaxStages) ++st;
+  return st;
+}
+
+template <int EPI>
+Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
   Plan pl{};
   int nrt = (int)((rows + kMaxRows - 1) / kMaxRows);
   if (nrt < 1) nrt = 1;
@@ -326,81 +409,45 @@ Plan make_plan(int64_t rows, int64_t k, int64_t n, int epi, int splits_req) {
   // every row tile starts inside the activation rows
   pl.num_rt = (int)((rows + pl.row_tile - 1) / pl.row_tile);
   if (pl.num_rt < 1) pl.num_rt = 1;
-  pl.tiles = (int)(epi == kEpiSwiGLU ? (n / 2) / (kTileN / 2) : n / kTileN);
+  pl.tiles = (int)(EPI == kEpiSwiGLU ? (n / 2) / (kTileN / 2) : n / kTileN);
   pl.num_kb = (int)(k / kBK);
-  const int ctas = pl.tiles * pl.num_rt;
-  int s = splits_req > 0 ? splits_req : num_sms() / (ctas > 0 ? ctas : 1);
-  if (s < 1) s = 1;
-  if (s > pl.num_kb) s = pl.num_kb;
-  pl.splits = s;
-  const int kb_per = (pl.num_kb + s - 1) / s;
-  const size_t stage_bytes = (size_t)kTileN * kBK * 2 + (size_t)pl.row_tile * kBK * 2;
-  int st = kb_per < 4 ? kb_per : 4;
-  if (st < 1) st = 1;
-  // the epilogue staging [row_tile][128] fp32 reuses the stage buffers
-  const size_t staging = (size_t)pl.row_tile * kTileN * 4;
-  while ((size_t)st * stage_bytes < staging && st < kMaxStages) ++st;
-  pl.stages = st;
+  const int clusters = pl.tiles * pl.num_rt;
+  int best = 1;
+  if (splits_req > 0) {
+    best = splits_req;
+  } else {
+    // the widest split whose clusters all fit in one wave, preferring more busy SMs
+    long best_busy = 0;
+    for (int S = 1; S <= kMaxSplits && S <= pl.num_kb; ++S) {
+      const int st = plan_stages(pl.row_tile, (pl.num_kb + S - 1) / S);
+      const int fit = S == 1 ? num_sms() : max_active_clusters<EPI>(S, plan_smem(pl.row_tile, st));
+      if (clusters > fit) continue;
+      const long busy = (long)clusters * S;
+      if (busy > best_busy) {
+        best_busy = busy;
+        best = S;
+      }
+    }
+  }
+  if (best > pl.num_kb) best = pl.num_kb;
+  if (best < 1) best = 1;
+  pl.splits = best;
+  pl.stages = plan_stages(pl.row_tile, (pl.num_kb + best - 1) / best);
   int tc = 32;
   while (tc < pl.row_tile) tc <<= 1;
   pl.tmem_cols = tc;
-  pl.smem = 1024 + (size_t)st * stage_bytes + 2 * kMaxStages * 8 + 8 + 16;
+  pl.smem = plan_smem(pl.row_tile, pl.stages);
   return pl;
 }
 
-size_t workspace_bytes(const Plan& pl) {
-  if (pl.splits <= 1) return 0;
-  const size_t counters = ((size_t)pl.tiles * pl.num_rt * 4 + 255) / 256 * 256;
-  return counters + (size_t)pl.tiles * pl.num_rt * pl.splits * pl.row_tile * kTileN * 4;
-}
-
 template <int EPI>
-int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmParams& gp, const Plan& pl, cudaStream_t st) {
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  });
-  if (attr_err != cudaSuccess) return check_launch(attr_err);
-  dim3 grid((unsigned)pl.tiles, (unsigned)pl.num_rt, (unsigned)pl.splits);
-  return check_launch(launch(gemm_kernel<EPI>, grid, dim3(kThreadsG), pl.smem, st, tw, tx, gp));
-}
-
-}  // namespace
-}  // namespace omni
-
-using namespace omni;
-
-extern "C" OMNI_API int64_t omni_linear_workspace_bytes(int64_t rows, int64_t k, int64_t n, int32_t epilogue,
-                                                        int32_t splits) {
-  if (rows <= 0 || k <= 0 || n <= 0) return 0;
-  return (int64_t)workspace_bytes(make_plan(rows, k, n, epilogue, splits));
-}
-
-extern "C" OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w,
-                                    int64_t n, int32_t epilogue, const void* residual, int64_t residual_stride,
-                                    void* y, int64_t y_stride, void* workspace, int64_t workspace_bytes_avail,
-                                    int32_t splits, void* stream) {
-  if (rows < 0 || k <= 0 || n <= 0) return set_error(OMNI_ERR_INVALID, "bad GEMM shape");
-  if (epilogue < 0 || epilogue > 3) return set_error(OMNI_ERR_INVALID, "unknown epilogue");
-  if (k % kBK != 0) return set_error(OMNI_ERR_UNSUPPORTED, "K must be a multiple of 64");
-  if (epilogue == kEpiSwiGLU ? (n % 128 != 0) : (n % kTileN != 0))
-    return set_error(OMNI_ERR_UNSUPPORTED, "N must be a multiple of 128");
-  auto mis16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
-  if (mis16(x) || mis16(w) || (x_stride % 8) != 0 || mis16(y) || (y_stride % 4) != 0)
-    return set_error(OMNI_ERR_UNSUPPORTED, "operands must be 16-byte aligned with 16-byte row strides");
-  if (epilogue == kEpiResidual && (residual == nullptr || (residual_stride % 4) != 0 ||
-                                   (reinterpret_cast<uintptr_t>(residual) & 7) != 0))
-    return set_error(OMNI_ERR_INVALID, "residual epilogue needs an 8-byte aligned residual");
-  if (rows == 0) return OMNI_OK;
-  Plan pl = make_plan(rows, k, n, epilogue, splits);
-  const size_t need = workspace_bytes(pl);
-  if ((size_t)workspace_bytes_avail < need || (need > 0 && workspace == nullptr))
-    return set_error(OMNI_ERR_CAPACITY, "GEMM workspace too small");
-  if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
-    return set_error(OMNI_ERR_INVALID, "workspace must be 256-byte aligned");
+int launch_gemm(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n,
+                const void* residual, int64_t residual_stride, void* y, int64_t y_stride, int splits_req,
+                cudaStream_t st) {
+  const Plan pl = make_plan<EPI>(rows, k, n, splits_req);
+  if (pl.splits > kMaxSplits) return set_error(OMNI_ERR_UNSUPPORTED, "at most 16 K-splits");
   CUtensorMap tw, tx;
-  const int wbox = epilogue == kEpiSwiGLU ? kTileN / 2 : kTileN;
+  const int wbox = EPI == kEpiSwiGLU ? kTileN / 2 : kTileN;
   if (!make_tmap(&tw, w, n, k, k, wbox) || !make_tmap(&tx, x, rows, k, x_stride, pl.row_tile))
     return set_error(OMNI_ERR_UNSUPPORTED, "tensor map encoding failed");
   GemmParams gp{};
@@ -417,16 +464,65 @@ extern "C" OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int6
   gp.res_stride = residual_stride;
   gp.y = y;
   gp.y_stride = y_stride;
-  if (need > 0) {
-    const size_t counters = ((size_t)pl.tiles * pl.num_rt * 4 + 255) / 256 * 256;
-    gp.counters = static_cast<int*>(workspace);
-    gp.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
+  set_kernel_attrs<EPI>();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)pl.tiles, (unsigned)pl.num_rt, (unsigned)pl.splits);
+  cfg.blockDim = dim3(kThreadsG);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pl.splits > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = (unsigned)pl.splits;
+    ++na;
   }
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return check_launch(cudaLaunchKernelEx(&cfg, gemm_kernel<EPI>, tw, tx, gp));
+}
+
+}  // namespace
+}  // namespace omni
+
+using namespace omni;
+
+extern "C" OMNI_API int64_t omni_linear_workspace_bytes(int64_t rows, int64_t k, int64_t n, int32_t epilogue,
+                                                        int32_t splits) {
+  (void)rows, (void)k, (void)n, (void)epilogue, (void)splits;
+  return 0;  // split-K partials are reduced in distributed shared memory
+}
+
+extern "C" OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w,
+                                    int64_t n, int32_t epilogue, const void* residual, int64_t residual_stride,
+                                    void* y, int64_t y_stride, void* workspace, int64_t workspace_bytes_avail,
+                                    int32_t splits, void* stream) {
+  (void)workspace, (void)workspace_bytes_avail;
+  if (rows < 0 || k <= 0 || n <= 0) return set_error(OMNI_ERR_INVALID, "bad GEMM shape");
+  if (epilogue < 0 || epilogue > 3) return set_error(OMNI_ERR_INVALID, "unknown epilogue");
+  if (splits < 0 || splits > kMaxSplits) return set_error(OMNI_ERR_INVALID, "splits must be in [0, 16]");
+  if (k % kBK != 0) return set_error(OMNI_ERR_UNSUPPORTED, "K must be a multiple of 64");
+  if (n % kTileN != 0) return set_error(OMNI_ERR_UNSUPPORTED, "N must be a multiple of 128");
+  auto mis16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
+  if (mis16(x) || mis16(w) || (x_stride % 8) != 0 || mis16(y) || (y_stride % 4) != 0)
+    return set_error(OMNI_ERR_UNSUPPORTED, "operands must be 16-byte aligned with 16-byte row strides");
+  if (epilogue == kEpiResidual && (residual == nullptr || (residual_stride % 4) != 0 ||
+                                   (reinterpret_cast<uintptr_t>(residual) & 7) != 0))
+    return set_error(OMNI_ERR_INVALID, "residual epilogue needs an 8-byte aligned residual");
+  if (rows == 0) return OMNI_OK;
+  if (splits > k / kBK) splits = (int32_t)(k / kBK);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (epilogue) {
-    case kEpiStore: return launch_gemm<kEpiStore>(tw, tx, gp, pl, st);
-    case kEpiResidual: return launch_gemm<kEpiResidual>(tw, tx, gp, pl, st);
-    case kEpiSwiGLU: return launch_gemm<kEpiSwiGLU>(tw, tx, gp, pl, st);
-    default: return launch_gemm<kEpiF32>(tw, tx, gp, pl, st);
+    case kEpiStore: return launch_gemm<kEpiStore>(x, rows, k, x_stride, w, n, residual, residual_stride, y, y_stride, splits, st);
+    case kEpiResidual: return launch_gemm<kEpiResidual>(x, rows, k, x_stride, w, n, residual, residual_stride, y, y_stride, splits, st);
+    case kEpiSwiGLU: return launch_gemm<kEpiSwiGLU>(x, rows, k, x_stride, w, n, residual, residual_stride, y, y_stride, splits, st);
+    default: return launch_gemm<kEpiF32>(x, rows, k, x_stride, w, n, residual, residual_stride, y, y_stride, splits, st);
   }
 }

@@ -49,7 +49,7 @@ GEMM_CASES = [
 
 
 @pytest.mark.parametrize("rows,k,n,epi", GEMM_CASES)
-@pytest.mark.parametrize("splits", [0, 1, 3])
+@pytest.mark.parametrize("splits", [0, 1, 3, 16])
 def test_linear_matches_fp32(rows, k, n, epi, splits):
     from omni_b200 import ops
 
