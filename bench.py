@@ -180,17 +180,108 @@ def run_reference_arm(args, rank: int) -> None:
 
 
 def time_kernel(fn, iters: int) -> float:
-    """Average device time (s) of fn() launched back to back on the current stream."""
+    """Average device time (s) of one fn() launch: `iters` launches are captured in a
+    CUDA graph (so host-side launch cost is excluded) and the replay is timed with
+    CUDA events on the capturing stream."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(iters):
+            fn()
     st = torch.cuda.current_stream()
-    fn()
+    g.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
-    for _ in range(iters):
-        fn()
+    g.replay()
     e1.record(st)
     e1.synchronize()
+    del g
     return e0.elapsed_time(e1) / 1000.0 / iters
+
+
+def kernel_table(runner, iters: int = 50) -> list[dict]:
+    """Steady-state device time of every distinct launch of the step (back-to-back
+    launches on the current stream, CUDA events), with algorithmic bytes moved."""
+    from omni_b200 import ops
+    from omni_b200.sampling_kernels import predictor_sample_step
+
+    cfg = runner.cfg
+    t, p = runner.talker, runner.predictor
+    B = runner.batch_size
+    fb = runner.forward_batch()
+    pc = cfg.predictor
+    rows_out = []
+
+    def add(name, fn, nbytes, count_per_step):
+        s = time_kernel(fn, iters)
+        rows_out.append({"kernel": name, "us": s * 1e6, "bytes": nbytes, "gbs": nbytes / s / 1e9,
+                         "per_step": count_per_step})
+
+    lw = t.w["layers"][0]
+    H = cfg.hidden_size
+    L = cfg.num_hidden_layers
+    wb = lambda w: w.numel() * 2  # noqa: E731
+    add("talker rmsnorm", lambda: ops.rmsnorm(t.h[:B], lw["input_layernorm"], 1e-6, out=t.normed[:B]), 4 * B * H, 2 * L + 1)
+    add("talker qkv gemm", lambda: ops.linear(t.normed[:B], lw["qkv_proj"], out=t.qkv[:B]), wb(lw["qkv_proj"]), L)
+    add("talker qknorm_rope_store", lambda: ops.qknorm_rope_store(
+        t.qkv[:B], num_q_heads=cfg.num_attention_heads, num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
+        q_norm=lw["q_norm"], k_norm=lw["k_norm"], eps=1e-6, cos_sin=t.cos_sin, q_out=t.q[:B],
+        k_cache=runner.kv.k_buffer[0], v_cache=runner.kv.v_buffer[0], positions=fb.positions,
+        cache_loc=fb.out_cache_loc), 2 * B * t.qkv.shape[1] * 2, L)
+    seq_now = runner.seq_lens[:B].cpu().numpy()
+    kv_bytes = float(seq_now.sum()) * cfg.num_key_value_heads * cfg.head_dim * 2 * 2
+    add("talker paged attention", lambda: ops.paged_decode_attention(
+        t.q[:B], runner.kv.k_buffer[0], runner.kv.v_buffer[0], page_indptr=fb.page_indptr,
+        page_indices=fb.page_indices, seq_lens=fb.seq_lens, work_indptr=fb.work_indptr,
+        num_q_heads=cfg.num_attention_heads, num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
+        page_size=cfg.page_size, pages_per_chunk=fb.pages_per_chunk, work_capacity=fb.work_capacity,
+        sm_scale=t.scale, out=t.attn[:B], workspace=t.attn_workspace), kv_bytes, L)
+    add("talker o_proj gemm", lambda: ops.linear(t.attn[:B], lw["o_proj"], epilogue=1, residual=t.h[:B], out=t.h[:B]),
+        wb(lw["o_proj"]), L)
+    add("talker gate_up gemm", lambda: ops.linear(t.normed[:B], lw["gate_up_proj"], epilogue=2, out=t.act[:B]),
+        wb(lw["gate_up_proj"]), L)
+    add("talker down gemm", lambda: ops.linear(t.act[:B], lw["down_proj"], epilogue=1, residual=t.h[:B], out=t.h[:B]),
+        wb(lw["down_proj"]), L)
+    add("talker codec_head gemm", lambda: ops.linear(t.hidden[:B], t.w["codec_head"], epilogue=3, out=t.logits[:B]),
+        wb(t.w["codec_head"]), 1)
+    add("layer0 sampler", lambda: t.sample_decode_tokens(t.logits[:B], fb), B * cfg.vocab_size * 4, 1)
+    plw = p.w["layers"][0]
+    for rows, label, per in ((2 * B, "pair", 1), (B, "single", pc.num_code_groups - 2)):
+        n5 = pc.num_hidden_layers
+        add(f"predictor[{label}] rmsnorm", lambda rows=rows: ops.rmsnorm(p.h[:rows], plw["input_layernorm"], 1e-6,
+                                                                         out=p.normed[:rows]), 4 * rows * H, per * (2 * n5 + 1))
+        add(f"predictor[{label}] qkv gemm", lambda rows=rows: ops.linear(p.normed[:rows], plw["qkv_proj"],
+                                                                         out=p.qkv[:rows]), wb(plw["qkv_proj"]), per * n5)
+        add(f"predictor[{label}] attention", lambda rows=rows: ops.predictor_attention(
+            p.q[:rows], p.k_cache[0], p.v_cache[0], num_q_heads=pc.num_attention_heads,
+            num_kv_heads=pc.num_key_value_heads, head_dim=pc.head_dim, tokens_per_req=rows // B,
+            slot_stride=pc.cache_len, slot_base=0 if rows == 2 * B else 8, sm_scale=p.scale, out=p.attn[:rows]),
+            rows * (pc.cache_len // 2) * pc.num_key_value_heads * pc.head_dim * 4, per * n5)
+        add(f"predictor[{label}] o_proj gemm", lambda rows=rows: ops.linear(p.attn[:rows], plw["o_proj"], epilogue=1,
+                                                                            residual=p.h[:rows], out=p.h[:rows]),
+            wb(plw["o_proj"]), per * n5)
+        add(f"predictor[{label}] gate_up gemm", lambda rows=rows: ops.linear(p.normed[:rows], plw["gate_up_proj"],
+                                                                             epilogue=2, out=p.act[:rows]),
+            wb(plw["gate_up_proj"]), per * n5)
+        add(f"predictor[{label}] down gemm", lambda rows=rows: ops.linear(p.act[:rows], plw["down_proj"], epilogue=1,
+                                                                          residual=p.h[:rows], out=p.h[:rows]),
+            wb(plw["down_proj"]), per * n5)
+    add("predictor lm_head gemm", lambda: ops.linear(p.out[:B], p.w["lm_head"][0], out=p.logits[0, :B]),
+        wb(p.w["lm_head"][0]), pc.num_code_groups - 1)
+    add("predictor sample+gather", lambda: predictor_sample_step(
+        p.logits[0, :B], temperatures=p.sub_temperature_tensor[:B], top_ks=p.sub_top_k_tensor[:B],
+        top_ps=p.sub_top_p_tensor[:B], seeds=p.sub_sampling_seed_tensor[:B], positions=fb.positions, pos_mul=15,
+        pos_add=1, do_sample=None, argmax_all=False, max_top_k=p.sub_sampled_max_top_k,
+        has_top_p=p.sub_sampled_has_top_p, codes=p.output_codes[:B, 1], table=p.w["codec_embedding"][0],
+        gathered=p.next_in[:B], summed=p.output_embeds[:B]), B * pc.vocab_size * 2 + 3 * B * H * 2,
+        pc.num_code_groups - 1)
+    return rows_out
 
 
 def main() -> None:
@@ -201,6 +292,7 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernels", action="store_true", help="print the per-kernel time table and exit")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -238,6 +330,17 @@ def main() -> None:
     runner.admit(lens, seed=rank)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     runner.text_embeds.normal_(generator=g)
+    if args.kernels:
+        runner.step(use_graph=False)
+        torch.cuda.synchronize()
+        table = kernel_table(runner)
+        if rank == 0:
+            tot = sum(r["us"] * r["per_step"] for r in table)
+            for r in table:
+                print(f'{r["kernel"]:34s} {r["us"]:8.2f} us  x{r["per_step"]:3d}/step  {r["gbs"]:8.1f} GB/s  '
+                      f'{100 * r["us"] * r["per_step"] / tot:5.1f}% of kernel time')
+            print(f"sum of isolated kernel times per step: {tot:.1f} us")
+        return
     n0 = _lib.launch_count()
     runner.capture(warmup=1)
     launches_per_step = (_lib.launch_count() - n0) // 2  # one eager warm-up step + the captured step
