@@ -210,6 +210,25 @@ OMNI_API int omni_paged_decode_attention(const void* q, int64_t q_stride, const 
                                          float sm_scale, void* out, int64_t out_stride, void* workspace,
                                          int64_t workspace_bytes, int32_t grid_ctas, void* stream);
 
+/* omni_paged_decode_attention without a caller workspace; this entry point has
+ * no counterpart in the reference.  For callers that may not allocate device
+ * memory (a host that owns and budgets all device memory, or a real-time
+ * audio thread that must not block in cudaMalloc): the scratch comes from an
+ * 8 MiB array built into the library, one per GPU that loads it, held until
+ * process exit.  Calls needing more than 8 MiB of scratch
+ * (omni_paged_attention_workspace_bytes) fail with OMNI_ERR_CAPACITY.  All
+ * calls on a device share the array: calls that overlap on the GPU race.
+ * Each call zeroes the merge counters on its stream before the kernel.  The
+ * first call on a device resolves the array's address (cudaGetSymbolAddress)
+ * with that device current; make it before any stream capture. */
+OMNI_API int omni_paged_decode_attention_noalloc(const void* q, int64_t q_stride, const void* k_cache,
+                                                 const void* v_cache, const int32_t* page_indptr,
+                                                 const int32_t* page_indices, const int64_t* seq_lens,
+                                                 const int32_t* work_indptr, int64_t rows, int32_t num_q_heads,
+                                                 int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                                                 int32_t pages_per_chunk, int64_t work_capacity, float sm_scale,
+                                                 void* out, int64_t out_stride, int32_t grid_ctas, void* stream);
+
 /* The code predictor's attention over its per-request cache slots
  * (predictor_gqa_attention / decode_attention_kernel, sglang_model.py:113-150,
  * predictor_layers.py:336-396).  Row r = (request r / T, token r % T) attends to

@@ -16,6 +16,8 @@
 //   sglang_model.py:2168-2233; decode_attention_kernel,
 //   predictor_layers.py:336-396): one warp per (row, query head), causal for
 //   the opening pair.
+#include <mutex>
+
 #include "capi_util.h"
 #include "common.cuh"
 
@@ -432,4 +434,79 @@ extern "C" OMNI_API int omni_predictor_attention(const void* q, int64_t q_stride
                                num_kv_heads, tokens_per_req, slot_stride, slot_base, sm_scale, O, out_stride));
   return check_launch(launch(predictor_attention_kernel<4>, g, b, 0, st, Q, q_stride, K, V, (int)rows, num_q_heads,
                              num_kv_heads, tokens_per_req, slot_stride, slot_base, sm_scale, O, out_stride));
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot allocate device memory: a host process that owns and
+// budgets every byte of device memory (a serving runtime with its own pool),
+// or a thread on the real-time audio path that must not call cudaMalloc,
+// whose implicit device-wide synchronisation would stall the streams of the
+// other live speakers.  For them, this variant takes its scratch (the
+// per-chunk partial outputs, their log-sum-exps and the per-row merge
+// counters) from a fixed array compiled into the library instead of a
+// caller-provided workspace.
+//
+// Limits and sharing:
+//   - the array holds kNoAllocScratchBytes (8 MiB); a call whose scratch need
+//     (omni_paged_attention_workspace_bytes(rows, num_kv_heads, work_capacity))
+//     exceeds it is rejected with OMNI_ERR_CAPACITY before any launch;
+//   - every GPU that loads the library keeps its own copy of the array until
+//     the process exits;
+//   - all calls on a device share the array, so calls whose kernels overlap on
+//     the GPU (different streams without ordering) race on it; serialise them;
+//   - each call clears the merge counters (the part that must start at zero)
+//     with cudaMemsetAsync on the call's stream before its kernel.
+// The first call on each device looks up the array's device address with
+// cudaGetSymbolAddress while that device is current and caches it; make that
+// first call before any stream capture on the device.
+// ---------------------------------------------------------------------------
+namespace omni {
+namespace {
+constexpr size_t kNoAllocScratchBytes = 8u << 20;
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) unsigned char g_noalloc_attn_scratch[kNoAllocScratchBytes];
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+}  // namespace
+}  // namespace omni
+
+extern "C" OMNI_API int omni_paged_decode_attention_noalloc(
+    const void* q, int64_t q_stride, const void* k_cache, const void* v_cache, const int32_t* page_indptr,
+    const int32_t* page_indices, const int64_t* seq_lens, const int32_t* work_indptr, int64_t rows,
+    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t page_size, int32_t pages_per_chunk,
+    int64_t work_capacity, float sm_scale, void* out, int64_t out_stride, int32_t grid_ctas, void* stream) {
+  if (rows < 0 || num_kv_heads <= 0 || work_capacity < 0) return set_error(OMNI_ERR_INVALID, "bad attention shape");
+  const int64_t need = omni_paged_attention_workspace_bytes(rows, num_kv_heads, work_capacity);
+  if (need > (int64_t)kNoAllocScratchBytes)
+    return set_error(OMNI_ERR_CAPACITY,
+                     "scratch need exceeds the 8 MiB built-in array of the allocation-free attention entry point");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return check_launch(e);
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return set_error(OMNI_ERR_UNSUPPORTED, "device ordinal out of range");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_attn_scratch);
+      if (e != cudaSuccess || p == nullptr) {
+        set_error(OMNI_ERR_CUDA, "cudaGetSymbolAddress of the built-in attention scratch failed");
+        return OMNI_ERR_CUDA;
+      }
+      g_noalloc_ptr[dev] = p;
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  // the merge counters sit at the front of the scratch and must start at zero
+  const size_t counter_bytes = (size_t)((rows * num_kv_heads * 4 + 255) / 256 * 256);
+  if (rows > 0) {
+    e = cudaMemsetAsync(scratch, 0, counter_bytes, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return check_launch(e);
+  }
+  return omni_paged_decode_attention(q, q_stride, k_cache, v_cache, page_indptr, page_indices, seq_lens, work_indptr,
+                                     rows, num_q_heads, num_kv_heads, head_dim, page_size, pages_per_chunk,
+                                     work_capacity, sm_scale, out, out_stride, scratch, need, grid_ctas, stream);
 }

@@ -48,6 +48,8 @@ SIGNATURES: dict[str, list] = {
     "omni_paged_attention_workspace_bytes": [_I64, _I32, _I64],
     "omni_paged_decode_attention": [_P, _I64, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _I64, _F32,
                                     _P, _I64, _P, _I64, _I32, _P],
+    "omni_paged_decode_attention_noalloc": [_P, _I64, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32,
+                                            _I64, _F32, _P, _I64, _I32, _P],
     "omni_predictor_attention": [_P, _I64, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _F32, _P, _I64, _P],
     "omni_decode_prepare": [_I64, _P, _P, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P],
     "omni_decode_rollback": [_I64, _P, _P, _P, _I64, _I32, _P, _P, _P, _P, _P],
