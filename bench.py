@@ -206,8 +206,8 @@ def time_kernel(fn, iters: int) -> float:
 
 
 def kernel_table(runner, iters: int = 50) -> list[dict]:
-    """Steady-state device time of every distinct launch of the step (back-to-back
-    launches on the current stream, CUDA events), with algorithmic bytes moved."""
+    """Steady-state device time of every distinct launch of the step (each replayed
+    `iters` times back to back from a CUDA graph, CUDA events), with algorithmic bytes."""
     from omni_b200 import ops
     from omni_b200.sampling_kernels import predictor_sample_step
 
@@ -216,71 +216,81 @@ def kernel_table(runner, iters: int = 50) -> list[dict]:
     B = runner.batch_size
     fb = runner.forward_batch()
     pc = cfg.predictor
+    H = cfg.hidden_size
+    L = cfg.num_hidden_layers
+    eps = cfg.rms_norm_eps
     rows_out = []
 
     def add(name, fn, nbytes, count_per_step):
-        s = time_kernel(fn, iters)
-        rows_out.append({"kernel": name, "us": s * 1e6, "bytes": nbytes, "gbs": nbytes / s / 1e9,
+        sec = time_kernel(fn, iters)
+        rows_out.append({"kernel": name, "us": sec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9,
                          "per_step": count_per_step})
 
-    lw = t.w["layers"][0]
-    H = cfg.hidden_size
-    L = cfg.num_hidden_layers
     wb = lambda w: w.numel() * 2  # noqa: E731
-    add("talker rmsnorm", lambda: ops.rmsnorm(t.h[:B], lw["input_layernorm"], 1e-6, out=t.normed[:B]), 4 * B * H, 2 * L + 1)
-    add("talker qkv gemm", lambda: ops.linear(t.normed[:B], lw["qkv_proj"], out=t.qkv[:B]), wb(lw["qkv_proj"]), L)
-    add("talker qknorm_rope_store", lambda: ops.qknorm_rope_store(
-        t.qkv[:B], num_q_heads=cfg.num_attention_heads, num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
-        q_norm=lw["q_norm"], k_norm=lw["k_norm"], eps=1e-6, cos_sin=t.cos_sin, q_out=t.q[:B],
-        k_cache=runner.kv.k_buffer[0], v_cache=runner.kv.v_buffer[0], positions=fb.positions,
-        cache_loc=fb.out_cache_loc), 2 * B * t.qkv.shape[1] * 2, L)
+    lw, fw = t.w["layers"][0], t.folded[0]
+    kc, vc = runner.kv.k_buffer[0], runner.kv.v_buffer[0]
+    qkv_geo = dict(num_q_heads=cfg.num_attention_heads, num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
+                   q_norm=lw["q_norm"], k_norm=lw["k_norm"], eps=eps, cos_sin=t.cos_sin, positions=fb.positions,
+                   cache_loc=fb.out_cache_loc, k_cache=kc, v_cache=vc)
+    add("talker input add+sumsq", lambda: ops.add_sumsq(p.output_embeds[:B], runner.text_embeds[:B], t.h[:B], t.ss[0]),
+        3 * B * H * 2, 1)
+    add("talker qkv gemm (+norm,rope,kv)", lambda: ops.linear_fused(
+        t.h[:B], fw["qkv"], t.q[:B], epilogue=ops.EPI_QKV_ROPE, ss_in=t.ss, ss_in_parts=8, norm_eps=eps,
+        qkv=qkv_geo), wb(fw["qkv"]), L)
     seq_now = runner.seq_lens[:B].cpu().numpy()
     kv_bytes = float(seq_now.sum()) * cfg.num_key_value_heads * cfg.head_dim * 2 * 2
     add("talker paged attention", lambda: ops.paged_decode_attention(
-        t.q[:B], runner.kv.k_buffer[0], runner.kv.v_buffer[0], page_indptr=fb.page_indptr,
-        page_indices=fb.page_indices, seq_lens=fb.seq_lens, work_indptr=fb.work_indptr,
-        num_q_heads=cfg.num_attention_heads, num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
-        page_size=cfg.page_size, pages_per_chunk=fb.pages_per_chunk, work_capacity=fb.work_capacity,
-        sm_scale=t.scale, out=t.attn[:B], workspace=t.attn_workspace), kv_bytes, L)
-    add("talker o_proj gemm", lambda: ops.linear(t.attn[:B], lw["o_proj"], epilogue=1, residual=t.h[:B], out=t.h[:B]),
+        t.q[:B], kc, vc, page_indptr=fb.page_indptr, page_indices=fb.page_indices, seq_lens=fb.seq_lens,
+        work_indptr=fb.work_indptr, num_q_heads=cfg.num_attention_heads, num_kv_heads=cfg.num_key_value_heads,
+        head_dim=cfg.head_dim, page_size=cfg.page_size, pages_per_chunk=fb.pages_per_chunk,
+        work_capacity=fb.work_capacity, sm_scale=t.scale, out=t.attn[:B], workspace=t.attn_workspace), kv_bytes, L)
+    add("talker o_proj gemm (+res,ss)", lambda: ops.linear_fused(
+        t.attn[:B], lw["o_proj"], t.h[:B], epilogue=ops.EPI_RESIDUAL, residual=t.h[:B], ss_out=t.ss),
         wb(lw["o_proj"]), L)
-    add("talker gate_up gemm", lambda: ops.linear(t.normed[:B], lw["gate_up_proj"], epilogue=2, out=t.act[:B]),
-        wb(lw["gate_up_proj"]), L)
-    add("talker down gemm", lambda: ops.linear(t.act[:B], lw["down_proj"], epilogue=1, residual=t.h[:B], out=t.h[:B]),
+    add("talker gate_up gemm (+norm,swiglu)", lambda: ops.linear_fused(
+        t.h[:B], fw["gate_up"], t.act[:B], epilogue=ops.EPI_SWIGLU, ss_in=t.ss, ss_in_parts=8, norm_eps=eps),
+        wb(fw["gate_up"]), L)
+    add("talker down gemm (+res,ss)", lambda: ops.linear_fused(
+        t.act[:B], lw["down_proj"], t.h[:B], epilogue=ops.EPI_RESIDUAL, residual=t.h[:B], ss_out=t.ss),
         wb(lw["down_proj"]), L)
-    add("talker codec_head gemm", lambda: ops.linear(t.hidden[:B], t.w["codec_head"], epilogue=3, out=t.logits[:B]),
-        wb(t.w["codec_head"]), 1)
+    add("talker codec_head gemm (+norm)", lambda: ops.linear_fused(
+        t.h[:B], t.codec_head_folded, t.logits[:B], epilogue=ops.EPI_F32, ss_in=t.ss, ss_in_parts=8, norm_eps=eps),
+        wb(t.codec_head_folded), 1)
     add("layer0 sampler", lambda: t.sample_decode_tokens(t.logits[:B], fb), B * cfg.vocab_size * 4, 1)
-    plw = p.w["layers"][0]
-    for rows, label, per in ((2 * B, "pair", 1), (B, "single", pc.num_code_groups - 2)):
-        n5 = pc.num_hidden_layers
-        add(f"predictor[{label}] rmsnorm", lambda rows=rows: ops.rmsnorm(p.h[:rows], plw["input_layernorm"], 1e-6,
-                                                                         out=p.normed[:rows]), 4 * rows * H, per * (2 * n5 + 1))
-        add(f"predictor[{label}] qkv gemm", lambda rows=rows: ops.linear(p.normed[:rows], plw["qkv_proj"],
-                                                                         out=p.qkv[:rows]), wb(plw["qkv_proj"]), per * n5)
-        add(f"predictor[{label}] attention", lambda rows=rows: ops.predictor_attention(
+    plw, pfw = p.w["layers"][0], p.folded[0]
+    n5 = pc.num_hidden_layers
+    for rows, label, per, base in ((2 * B, "pair", 1, 0), (B, "single", pc.num_code_groups - 2, 8)):
+        T = rows // B
+        geo = dict(num_q_heads=pc.num_attention_heads, num_kv_heads=pc.num_key_value_heads, head_dim=pc.head_dim,
+                   q_norm=plw["q_norm"], k_norm=plw["k_norm"], eps=eps, cos_sin=p.cos_sin, tokens_per_req=T,
+                   slot_stride=pc.cache_len, slot_base=base, k_cache=p.k_cache[0], v_cache=p.v_cache[0])
+        add(f"predictor[{label}] qkv gemm (+norm,rope,kv)", lambda rows=rows, geo=geo: ops.linear_fused(
+            p.h[:rows], pfw["qkv"], p.q[:rows], epilogue=ops.EPI_QKV_ROPE, ss_in=p.ss, ss_in_parts=8, norm_eps=eps,
+            qkv=geo), wb(pfw["qkv"]), per * n5)
+        add(f"predictor[{label}] attention", lambda rows=rows, T=T, base=base: ops.predictor_attention(
             p.q[:rows], p.k_cache[0], p.v_cache[0], num_q_heads=pc.num_attention_heads,
-            num_kv_heads=pc.num_key_value_heads, head_dim=pc.head_dim, tokens_per_req=rows // B,
-            slot_stride=pc.cache_len, slot_base=0 if rows == 2 * B else 8, sm_scale=p.scale, out=p.attn[:rows]),
+            num_kv_heads=pc.num_key_value_heads, head_dim=pc.head_dim, tokens_per_req=T, slot_stride=pc.cache_len,
+            slot_base=base, sm_scale=p.scale, out=p.attn[:rows]),
             rows * (pc.cache_len // 2) * pc.num_key_value_heads * pc.head_dim * 4, per * n5)
-        add(f"predictor[{label}] o_proj gemm", lambda rows=rows: ops.linear(p.attn[:rows], plw["o_proj"], epilogue=1,
-                                                                            residual=p.h[:rows], out=p.h[:rows]),
+        add(f"predictor[{label}] o_proj gemm (+res,ss)", lambda rows=rows: ops.linear_fused(
+            p.attn[:rows], plw["o_proj"], p.h[:rows], epilogue=ops.EPI_RESIDUAL, residual=p.h[:rows], ss_out=p.ss),
             wb(plw["o_proj"]), per * n5)
-        add(f"predictor[{label}] gate_up gemm", lambda rows=rows: ops.linear(p.normed[:rows], plw["gate_up_proj"],
-                                                                             epilogue=2, out=p.act[:rows]),
-            wb(plw["gate_up_proj"]), per * n5)
-        add(f"predictor[{label}] down gemm", lambda rows=rows: ops.linear(p.act[:rows], plw["down_proj"], epilogue=1,
-                                                                          residual=p.h[:rows], out=p.h[:rows]),
-            wb(plw["down_proj"]), per * n5)
-    add("predictor lm_head gemm", lambda: ops.linear(p.out[:B], p.w["lm_head"][0], out=p.logits[0, :B]),
-        wb(p.w["lm_head"][0]), pc.num_code_groups - 1)
+        add(f"predictor[{label}] gate_up gemm (+norm,swiglu)", lambda rows=rows: ops.linear_fused(
+            p.h[:rows], pfw["gate_up"], p.act[:rows], epilogue=ops.EPI_SWIGLU, ss_in=p.ss, ss_in_parts=8,
+            norm_eps=eps), wb(pfw["gate_up"]), per * n5)
+        add(f"predictor[{label}] down gemm (+res,ss)", lambda rows=rows: ops.linear_fused(
+            p.act[:rows], plw["down_proj"], p.h[:rows], epilogue=ops.EPI_RESIDUAL, residual=p.h[:rows],
+            ss_out=p.ss), wb(plw["down_proj"]), per * n5)
+    add("predictor lm_head gemm (+norm)", lambda: ops.linear_fused(
+        p.h[:B], p.lm_head_folded[1], p.logits[1, :B], epilogue=ops.EPI_STORE, ss_in=p.ss, ss_in_parts=8,
+        norm_eps=eps), wb(p.lm_head_folded[1]), pc.num_code_groups - 1)
     add("predictor sample+gather", lambda: predictor_sample_step(
-        p.logits[0, :B], temperatures=p.sub_temperature_tensor[:B], top_ks=p.sub_top_k_tensor[:B],
+        p.logits[1, :B], temperatures=p.sub_temperature_tensor[:B], top_ks=p.sub_top_k_tensor[:B],
         top_ps=p.sub_top_p_tensor[:B], seeds=p.sub_sampling_seed_tensor[:B], positions=fb.positions, pos_mul=15,
-        pos_add=1, do_sample=None, argmax_all=False, max_top_k=p.sub_sampled_max_top_k,
-        has_top_p=p.sub_sampled_has_top_p, codes=p.output_codes[:B, 1], table=p.w["codec_embedding"][0],
-        gathered=p.next_in[:B], summed=p.output_embeds[:B]), B * pc.vocab_size * 2 + 3 * B * H * 2,
-        pc.num_code_groups - 1)
+        pos_add=2, do_sample=None, argmax_all=False, max_top_k=p.sub_sampled_max_top_k,
+        has_top_p=p.sub_sampled_has_top_p, codes=p.output_codes[:B, 2], table=p.w["codec_embedding"][1],
+        gathered=p.next_in[:B], summed=p.output_embeds[:B], gathered_ss=p.next_ss[:B]),
+        B * pc.vocab_size * 2 + 3 * B * H * 2, pc.num_code_groups - 1)
     return rows_out
 
 

@@ -73,14 +73,16 @@ OMNI_API int omni_sample_topk_topp(const void* logits, int64_t rows, int64_t voc
  * The seed position of a row is positions[row] * pos_mul + pos_add
  * (sub_seed_positions, sglang_model.py:1908-1916).
  *   do_sample  u8 [rows] or NULL (all rows sampled); argmax_all != 0 takes argmax on every row
- *   table      bf16 [vocab, hidden]; gathered, summed bf16 [rows, hidden] or NULL */
+ *   table      bf16 [vocab, hidden]; gathered, summed bf16 [rows, hidden] or NULL
+ *   gathered_ss f32 [rows] or NULL: sum of squares of each gathered row (the
+ *   next pass's folded RMSNorm input, see omni_linear_fused) */
 OMNI_API int omni_predictor_sample_step(const void* logits, int64_t rows, int64_t vocab, int64_t logits_stride,
                                         const float* temperatures, const int64_t* top_ks, const float* top_ps,
                                         const int64_t* seeds, const int64_t* positions, int64_t pos_mul,
                                         int64_t pos_add, const uint8_t* do_sample, int32_t argmax_all,
                                         int32_t max_top_k, int32_t has_top_p, int64_t* codes, int64_t codes_stride,
                                         const void* table, int64_t hidden, void* gathered, void* summed,
-                                        void* stream);
+                                        float* gathered_ss, void* stream);
 
 /* Seeded Gumbel-max over pre-sorted fp32 log-probabilities.
  * Replaces sample_from_sorted_logprobs_with_seed_small_k
@@ -126,14 +128,20 @@ OMNI_API int omni_layer0_sample(const float* logits, int64_t rows, int64_t vocab
                                 int32_t max_top_k, int64_t* out, uint8_t* rep_mask_update, void* stream);
 
 /* First pass of the code predictor for one frame (code_predictor_forward_incremental,
- * sglang_model.py:1784-1813): codes[row * codes_stride] = layer0_codes[row];
- * e = table[layer0_codes[row]]; summed[row] = e; pair rows 2 row and 2 row + 1 =
- * (talker_hidden[row], e), the opening two-token pass input.
- *   layer0_codes i64 [rows]; talker_hidden bf16 [rows, hidden] row stride hidden_stride;
- *   table bf16 [vocab, hidden]; pair bf16 [2 rows, hidden]; summed bf16 [rows, hidden]. */
-OMNI_API int omni_predictor_pair_inputs(const int64_t* layer0_codes, const void* talker_hidden, int64_t hidden_stride,
+ * sglang_model.py:1784-1813) with the talker's final RMSNorm
+ * (talker.py:482-491) applied on the way: hidden = bf16(h * rstd * final_norm)
+ * where rstd comes from the per-row sums of squares ss_in of the talker's last
+ * residual h (ss_parts parts, see omni_linear_fused); hidden goes to
+ * hidden_out (nullable) and to pair row 2 r; e = table[layer0_codes[r]] goes
+ * to pair row 2 r + 1 and to summed; codes[r * codes_stride] = layer0_codes[r];
+ * pair_ss[2 r], pair_ss[2 r + 1] = the pair rows' sums of squares.
+ *   talker_residual bf16 [rows, hidden]; table bf16 [vocab, hidden];
+ *   pair bf16 [2 rows, hidden]; summed, hidden_out bf16 [rows, hidden]. */
+OMNI_API int omni_predictor_pair_inputs(const int64_t* layer0_codes, const void* talker_residual,
+                                        int64_t residual_stride, const void* final_norm_weight, const float* ss_in,
+                                        int32_t ss_parts, int64_t ss_stride, float eps, void* hidden_out,
                                         const void* table, int64_t rows, int64_t hidden, void* pair, void* summed,
-                                        int64_t* codes, int64_t codes_stride, void* stream);
+                                        float* pair_ss, int64_t* codes, int64_t codes_stride, void* stream);
 
 
 /* ======================================================================== */
@@ -161,6 +169,55 @@ OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_strid
                          int32_t epilogue, const void* residual, int64_t residual_stride, void* y, int64_t y_stride,
                          void* workspace, int64_t workspace_bytes, int32_t splits, void* stream);
 
+#define OMNI_EPI_QKV_ROPE 4 /* qkv projection + per-head RMSNorm + neox RoPE + KV store */
+
+/* Arguments of omni_linear_fused (unused fields zero).  Replaces, in one launch,
+ * the chain RMSNorm -> linear [-> residual add] of the decoder layers
+ * (thinker_model.py:259-402, talker.py:216-247, predictor_forward_tokens
+ * sglang_model.py:2036-2098) and, with OMNI_EPI_QKV_ROPE, also apply_qk_norm +
+ * rotary_emb(FusedSetKVBufferArg) (thinker_model.py:272-345):
+ *   - folded RMSNorm: w holds the layer's weight times the norm gain (column
+ *     scaled); the accumulator of row r is scaled by
+ *     rsqrt(sum_p ss_in[p * ss_in_stride + r] / norm_dim + norm_eps);
+ *   - ss_out (store / residual epilogues): per-row sum of squares of the bf16
+ *     output, one part per 128-feature tile (part t at ss_out + t * ss_out_stride),
+ *     the next folded RMSNorm's ss_in;
+ *   - OMNI_EPI_QKV_ROPE: y receives q [rows, Hq * head_dim]; k and v go to
+ *     k_cache / v_cache [slots, Hkv, head_dim] at cache_loc (or the implicit
+ *     predictor slots, as omni_qknorm_rope_store). */
+typedef struct OmniLinearArgs {
+  const void* x;
+  int64_t rows, k, x_stride;
+  const void* w;
+  int64_t n;
+  int32_t epilogue;
+  int32_t splits;
+  const float* ss_in;
+  int32_t ss_in_parts;
+  int64_t ss_in_stride;
+  int32_t norm_dim;
+  float norm_eps;
+  const void* residual;
+  int64_t residual_stride;
+  void* y;
+  int64_t y_stride;
+  float* ss_out;
+  int64_t ss_out_stride;
+  int32_t num_q_heads, num_kv_heads, head_dim;
+  const void* q_norm;
+  const void* k_norm;
+  float qk_eps;
+  const float* cos_sin;
+  int64_t max_position;
+  const int64_t* positions;
+  const int64_t* cache_loc;
+  int32_t tokens_per_req, slot_stride, slot_base;
+  void* k_cache;
+  void* v_cache;
+} OmniLinearArgs;
+
+OMNI_API int omni_linear_fused(const OmniLinearArgs* args, void* stream);
+
 /* ======================================================================== */
 /* Norms and rotary embedding                                               */
 /* ======================================================================== */
@@ -172,6 +229,13 @@ OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_strid
 OMNI_API int omni_rmsnorm(const void* x, int64_t x_stride, const void* addend, int64_t addend_stride,
                           void* residual_out, int64_t residual_stride, const void* weight, float eps, void* out,
                           int64_t out_stride, int64_t rows, int64_t hidden, void* stream);
+
+/* sum = bf16(a + b) (b nullable: a copy of a) and ss_out[r] = sum of squares of
+ * row r of sum: the decode input row (write_feedback_buffers,
+ * talker_model_runner.py:564-606: feedback embedding + text row) ahead of a
+ * folded first RMSNorm.  hidden = 256 * {1,2,4,8}. */
+OMNI_API int omni_add_sumsq(const void* a, int64_t a_stride, const void* b, int64_t b_stride, void* sum,
+                            int64_t sum_stride, float* ss_out, int64_t rows, int64_t hidden, void* stream);
 
 /* Per-head q/k RMSNorm, neox rotary embedding and the KV store
  * (apply_qk_norm + rotary_emb with FusedSetKVBufferArg, thinker_model.py:272-345;

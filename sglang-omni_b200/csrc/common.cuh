@@ -116,6 +116,26 @@ OMNI_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// Bounded wait with cluster-scope acquire: for barriers completed by peer CTAs'
+// remote stores (st.async), whose data must be visible after the wait.
+OMNI_DEVINL bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+OMNI_DEVINL bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+  }
+  return false;
+}
+
 // TMA: 2D tiled load global -> shared, completion on an mbarrier.
 OMNI_DEVINL void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar, int x, int y) {
   asm volatile(

@@ -11,9 +11,11 @@
 // Split-K: the S CTAs that share a feature tile form one thread-block cluster
 // (S <= 16, chosen so that every cluster of the grid is co-resident).  Each
 // CTA stages its fp32 partial tile in its own shared memory; after a hardware
-// cluster barrier, CTA c reduces rows c, c + S, ... of the tile by reading all
-// S partials over distributed shared memory in split order (deterministic),
-// applies the epilogue and stores the result.  No global scratch memory.
+// cluster barrier, CTA c reduces the c-th contiguous block of the tile's rows
+// by reading the S partials over distributed shared memory in split order
+// (deterministic), applies the epilogue and stores.  The epilogue operands of
+// the owned rows (RMSNorm scale, rotary position, KV slot, residual) are
+// fetched while the MMAs run.  No global scratch memory.
 //
 // Programmatic dependent launch: weights never depend on the previous kernel,
 // so the producer issues the first stages' weight loads before
@@ -38,8 +40,9 @@ constexpr int kTileN = 128;    // output features per CTA (MMA M)
 constexpr int kMaxRows = 256;  // activation rows per CTA (MMA N)
 constexpr int kMaxStages = 6;
 constexpr int kThreadsG = 128;
+constexpr int kMaxSplits = 16;
 
-enum Epilogue : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiF32 = 3 };
+enum Epilogue : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiF32 = 3, kEpiQKV = 4 };
 
 struct GemmParams {
   int rows;         // total activation rows
@@ -55,6 +58,27 @@ struct GemmParams {
   int64_t res_stride;
   void* y;
   int64_t y_stride;
+  // folded RMSNorm: acc *= rsqrt(sum_p ss_in[p * ss_in_stride + row] / norm_dim + eps)
+  const float* ss_in;
+  int ss_in_parts;
+  int64_t ss_in_stride;
+  int norm_dim;
+  float norm_eps;
+  // per-row sum of squares of the bf16 output, one part per 128-feature tile
+  float* ss_out;
+  int64_t ss_out_stride;
+  // qkv epilogue: per-head RMSNorm, neox rotary, q to y, k and v to their cache slot
+  int hq, hkv, head_dim;
+  const uint16_t* q_norm;
+  const uint16_t* k_norm;
+  float qk_eps;
+  const float* cos_sin;
+  int64_t max_pos;
+  const int64_t* positions;
+  const int64_t* cache_loc;
+  int tokens_per_req, slot_stride, slot_base;
+  uint16_t* k_cache;
+  uint16_t* v_cache;
 };
 
 OMNI_DEVINL uint32_t cluster_ctarank() {
@@ -71,16 +95,28 @@ OMNI_DEVINL uint32_t map_cluster(uint32_t local, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
   return r;
 }
+// Reads of peers' partial tiles between two cluster barriers (which order them).
 OMNI_DEVINL float4 ld_cluster_f4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
+               : "r"(addr));
   return v;
 }
 
 OMNI_DEVINL float silu(float g) { return g / (1.0f + expf(-g)); }
+
+// Rows of the tile owned (reduced and stored) by cluster rank q: a contiguous block.
+struct RowBlock {
+  int per, begin, count;
+};
+OMNI_DEVINL RowBlock row_block(int rows_here, int S, int q) {
+  RowBlock b;
+  b.per = (rows_here + S - 1) / S;
+  b.begin = q * b.per;
+  b.count = max(0, min(b.per, rows_here - b.begin));
+  return b;
+}
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreadsG, 1)
@@ -90,22 +126,30 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int ST = p.stages;
   const int Rt = p.row_tile;
+  const int S = p.splits;
   const uint32_t a_bytes = kTileN * kBK * 2;
   const uint32_t b_bytes = (uint32_t)Rt * kBK * 2;
-  uint8_t* a_smem = smem;
-  uint8_t* b_smem = smem + ST * a_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(b_smem + ST * b_bytes);
-  uint64_t* empty = full + kMaxStages;
-  uint64_t* mma_done = empty + kMaxStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
-  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, rtile = blockIdx.y, split = blockIdx.z;
-  const int kb_begin = (int)(((int64_t)p.num_kb * split) / p.splits);
-  const int kb_end = (int)(((int64_t)p.num_kb * (split + 1)) / p.splits);
-  const int nk = kb_end - kb_begin;
   const int row0 = rtile * Rt;
+  const int rows_here = min(Rt, p.rows - row0);
+  const uint32_t crank = S > 1 ? cluster_ctarank() : 0u;
+  const RowBlock mine = row_block(rows_here, S, (int)crank);
+  // shared memory: [stages A][stages B][row info][barriers]; the fp32 partial tile
+  // [rows][128] is staged over the drained stage buffers after the main loop
+  uint8_t* a_smem = smem;
+  uint8_t* b_smem = smem + ST * a_bytes;
+  float* row_info = reinterpret_cast<float*>(b_smem + ST * b_bytes);  // [per] rstd, [per] position, [per] slot
+  uint64_t* full = reinterpret_cast<uint64_t*>(row_info + 3 * ((mine.per + 1) & ~1));
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* mma_done = empty + kMaxStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 2);
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort
+  float* stage = reinterpret_cast<float*>(smem);
+
+  const int kb_begin = (int)(((int64_t)p.num_kb * split) / S);
+  const int kb_end = (int)(((int64_t)p.num_kb * (split + 1)) / S);
+  const int nk = kb_end - kb_begin;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
@@ -114,7 +158,6 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     }
     mbar_init(mma_done, 1);
     flags[0] = 0;
-    flags[1] = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
@@ -128,7 +171,6 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // Weight tile coordinates of k-block kb into stage s.
   auto load_w = [&](int s, int kb) {
     uint8_t* dst = a_smem + s * a_bytes;
     const int kx = kb * kBK;
@@ -187,11 +229,36 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     }
     if (ok) tc_commit(mma_done);
     else mbar_arrive(mma_done);
+  } else if (warp >= 2) {
+    // while the MMAs run: per-row epilogue operands of the rows this CTA owns
+    for (int i = threadIdx.x - 64; i < mine.count; i += kThreadsG - 64) {
+      const int64_t grow = row0 + mine.begin + i;
+      float rs = 1.0f;
+      if (p.ss_in != nullptr) {
+        float ssum = 0.0f;
+        for (int q = 0; q < p.ss_in_parts; ++q) ssum += p.ss_in[q * p.ss_in_stride + grow];
+        rs = rsqrtf(ssum / (float)p.norm_dim + p.norm_eps);
+      }
+      row_info[i] = rs;
+      if (EPI == kEpiQKV) {
+        int64_t pos, loc;
+        if (p.positions) {
+          pos = p.positions[grow];
+          loc = p.cache_loc[grow];
+        } else {
+          const int t = (int)(grow % p.tokens_per_req);
+          pos = p.slot_base + t;
+          loc = (grow / p.tokens_per_req) * p.slot_stride + p.slot_base + t;
+        }
+        if (pos < 0 || pos >= p.max_pos) pos = 0;
+        reinterpret_cast<int*>(row_info)[mine.per + i] = (int)pos;
+        reinterpret_cast<int*>(row_info)[2 * mine.per + i] = (int)loc;
+      }
+    }
   }
   __syncwarp();
 
-  // ---- epilogue: TMEM -> smem staging [Rt][128] fp32 ----
-  float* stage = reinterpret_cast<float*>(smem);  // reuses the drained pipeline buffers
+  // ---- accumulators: TMEM -> smem staging [rows][128] fp32 ----
   const bool have_acc = nk > 0;
   if (have_acc) {
     if (!mbar_wait(mma_done, 0)) {
@@ -202,9 +269,22 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   tc_fence_after();
   __syncthreads();
   const bool aborted = flags[0] != 0;
+  // the residual rows this thread will add, fetched ahead of the reduction
+  constexpr int kPre = 4;
+  uint2 res_pre[kPre];
+  if (EPI == kEpiResidual && !aborted) {
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      const int idx = threadIdx.x + u * kThreadsG;
+      if (idx < mine.count * 32)
+        res_pre[u] = *reinterpret_cast<const uint2*>(p.residual + (int64_t)(row0 + mine.begin + (idx >> 5)) *
+                                                                         p.res_stride +
+                                                     (int64_t)tile * kTileN + (idx & 31) * 4);
+    }
+  }
   if (!aborted) {
     const int f = warp * 32 + lane;
-    for (int c0 = 0; c0 < Rt; c0 += 32) {
+    for (int c0 = 0; c0 < rows_here; c0 += 32) {
       uint32_t r[32];
       if (have_acc) {
         tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
@@ -215,75 +295,138 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       }
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (c0 + j < Rt) stage[(c0 + j) * kTileN + f] = __uint_as_float(r[j]);
+        if (c0 + j < rows_here) stage[(c0 + j) * kTileN + f] = __uint_as_float(r[j]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
-
-  // ---- split-K reduction over the cluster's shared memory ----
   // Every CTA takes part in both cluster barriers, aborted or not.
-  const int S = p.splits;
   if (S > 1) cluster_sync();  // all partial tiles staged and visible cluster-wide
-  const uint32_t crank = S > 1 ? cluster_ctarank() : 0u;
+  if (aborted) {
+    if (S > 1) cluster_sync();
+    return;
+  }
+
+  // ---- reduce the owned rows over the cluster, in split order, and apply the epilogue ----
   const uint32_t stage_local = smem_u32(stage);
-  const bool any_abort = aborted;
-  const int rows_here = min(Rt, p.rows - row0);
-  // partial of split s, row r, features f..f+3 (s in split order)
-  auto acc4 = [&](int r, int f) -> float4 {
-    const uint32_t off = (uint32_t)((r * kTileN + f) * 4);
+  auto acc4 = [&](int i, int f) -> float4 {
+    const int r = mine.begin + i;
     if (S == 1) return *reinterpret_cast<const float4*>(stage + r * kTileN + f);
-    float4 a = ld_cluster_f4(map_cluster(stage_local + off, 0));
-    for (int q = 1; q < S; ++q) {
-      const float4 b = ld_cluster_f4(map_cluster(stage_local + off, (uint32_t)q));
-      a.x += b.x;
-      a.y += b.y;
-      a.z += b.z;
-      a.w += b.w;
-    }
+    const uint32_t off = stage_local + (uint32_t)((r * kTileN + f) * 4);
+    float4 v[kMaxSplits];
+#pragma unroll
+    for (int q = 0; q < kMaxSplits; ++q)
+      if (q < S) v[q] = ld_cluster_f4(map_cluster(off, (uint32_t)q));
+    float4 a = v[0];
+#pragma unroll
+    for (int q = 1; q < kMaxSplits; ++q)
+      if (q < S) {
+        a.x += v[q].x;
+        a.y += v[q].y;
+        a.z += v[q].z;
+        a.w += v[q].w;
+      }
     return a;
   };
-  if (!any_abort) {
-    if (EPI == kEpiSwiGLU) {
-      // features 0..63: gate, 64..127: up, for outputs tile*64 .. tile*64+63
-      uint16_t* Y = static_cast<uint16_t*>(p.y);
-      const int nr = (rows_here - (int)crank + S - 1) / S;
-      for (int idx = threadIdx.x; idx < nr * 16; idx += kThreadsG) {
-        const int r = (int)crank + (idx >> 4) * S;
-        const int g = (idx & 15) * 4;
-        const float4 gt = acc4(r, g), up = acc4(r, 64 + g);
-        const float gg[4] = {gt.x, gt.y, gt.z, gt.w}, uu[4] = {up.x, up.y, up.z, up.w};
-        float o[4];
+  if (EPI == kEpiSwiGLU) {
+    // features 0..63: gate, 64..127: up, for outputs tile*64 .. tile*64+63
+    uint16_t* Y = static_cast<uint16_t*>(p.y);
+    for (int idx = threadIdx.x; idx < mine.count * 16; idx += kThreadsG) {
+      const int i = idx >> 4;
+      const int g = (idx & 15) * 4;
+      const float sc = row_info[i];
+      const float4 gt = acc4(i, g), up = acc4(i, 64 + g);
+      const float gg[4] = {gt.x, gt.y, gt.z, gt.w}, uu[4] = {up.x, up.y, up.z, up.w};
+      float o[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) o[j] = silu(bf2f(f2bf(gg[j]))) * bf2f(f2bf(uu[j]));
-        *reinterpret_cast<uint2*>(Y + (int64_t)(row0 + r) * p.y_stride + tile * 64 + g) =
+      for (int j = 0; j < 4; ++j) o[j] = silu(bf2f(f2bf(gg[j] * sc))) * bf2f(f2bf(uu[j] * sc));
+      *reinterpret_cast<uint2*>(Y + (int64_t)(row0 + mine.begin + i) * p.y_stride + tile * 64 + g) =
+          make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
+    }
+    if (S > 1) cluster_sync();  // no CTA leaves while a peer still reads its partial
+    return;
+  }
+  // one warp per owned row, lane l holds features 4l..4l+3
+  for (int idx = threadIdx.x, u = 0; idx < mine.count * 32; idx += kThreadsG, ++u) {
+    const int i = idx >> 5;
+    const int ln = idx & 31;
+    const int f = ln * 4;
+    const int64_t grow = row0 + mine.begin + i;
+    const int64_t col = (int64_t)tile * kTileN + f;
+    const float sc = row_info[i];
+    const float4 a = acc4(i, f);
+    float o[4] = {a.x * sc, a.y * sc, a.z * sc, a.w * sc};
+    if (EPI == kEpiF32) {
+      float* Y = static_cast<float*>(p.y);
+      *reinterpret_cast<float4*>(Y + grow * p.y_stride + col) = make_float4(o[0], o[1], o[2], o[3]);
+    } else if (EPI == kEpiQKV) {
+      const int D = p.head_dim;
+      const int gh = (int)(col / D);  // global head of these 4 features
+      const int d = (int)(col % D);   // first dimension within the head
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = bf2f(f2bf(o[j]));  // the qkv projection's bf16 output
+      const int64_t pos = reinterpret_cast<const int*>(row_info)[mine.per + i];
+      const int64_t loc = reinterpret_cast<const int*>(row_info)[2 * mine.per + i];
+      const bool is_q = gh < p.hq, is_k = !is_q && gh < p.hq + p.hkv;
+      // lanes sharing a head: D/4 consecutive lanes (the whole warp for D = 128)
+      const int head_lanes = D / 4;
+      float ss = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ss = __fmaf_rn(o[j], o[j], ss);
+      for (int off = 1; off < head_lanes; off <<= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
+      if (is_q || is_k) {
+        const uint16_t* gw = is_q ? p.q_norm : p.k_norm;
+        const float hr = rsqrtf(ss / (float)D + p.qk_eps);
+        const uint2 wv = *reinterpret_cast<const uint2*>(gw + d);
+        const float gw4[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = bf2f(f2bf(o[j] * hr * gw4[j]));
+      }
+      // neox rotation pairs d with d + D/2, held by lane ^ (D/8); every lane joins the shuffle
+      const int half = D / 2;
+      const float* cs = p.cos_sin + pos * D;
+      float y4[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float other = __shfl_xor_sync(0xFFFFFFFFu, o[j], D / 8);
+        const int dd = d + j;
+        const int ii = dd % half;
+        const float c = cs[ii], sn = cs[half + ii];
+        y4[j] = dd < half ? o[j] * c - other * sn : o[j] * c + other * sn;
+      }
+      const uint2 packed_rot = make_uint2(pack_bf2(y4[0], y4[1]), pack_bf2(y4[2], y4[3]));
+      if (is_q) {
+        uint16_t* Y = static_cast<uint16_t*>(p.y);
+        *reinterpret_cast<uint2*>(Y + grow * p.y_stride + col) = packed_rot;
+      } else if (is_k) {
+        const int kh = gh - p.hq;
+        *reinterpret_cast<uint2*>(p.k_cache + (loc * p.hkv + kh) * D + d) = packed_rot;
+      } else {
+        const int vh = gh - p.hq - p.hkv;
+        *reinterpret_cast<uint2*>(p.v_cache + (loc * p.hkv + vh) * D + d) =
             make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
       }
     } else {
-      // rows crank, crank + S, ...: 32 threads per row, 4 features each
-      const int nr = (rows_here - (int)crank + S - 1) / S;
-      for (int idx = threadIdx.x; idx < nr * 32; idx += kThreadsG) {
-        const int r = (int)crank + (idx >> 5) * S;
-        const int f = (idx & 31) * 4;
-        const int64_t col = (int64_t)tile * kTileN + f;
-        const float4 a = acc4(r, f);
-        float o[4] = {a.x, a.y, a.z, a.w};
-        if (EPI == kEpiF32) {
-          float* Y = static_cast<float*>(p.y);
-          *reinterpret_cast<float4*>(Y + (int64_t)(row0 + r) * p.y_stride + col) = make_float4(o[0], o[1], o[2], o[3]);
-        } else {
-          if (EPI == kEpiResidual) {
-            const uint2 rv = *reinterpret_cast<const uint2*>(p.residual + (int64_t)(row0 + r) * p.res_stride + col);
-            o[0] += bf_lo(rv.x);
-            o[1] += bf_hi(rv.x);
-            o[2] += bf_lo(rv.y);
-            o[3] += bf_hi(rv.y);
-          }
-          uint16_t* Y = static_cast<uint16_t*>(p.y);
-          *reinterpret_cast<uint2*>(Y + (int64_t)(row0 + r) * p.y_stride + col) =
-              make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
-        }
+      if (EPI == kEpiResidual) {
+        const uint2 rv = u < kPre ? res_pre[u]
+                                  : *reinterpret_cast<const uint2*>(p.residual + grow * p.res_stride + col);
+        o[0] += bf_lo(rv.x);
+        o[1] += bf_hi(rv.x);
+        o[2] += bf_lo(rv.y);
+        o[3] += bf_hi(rv.y);
+      }
+      uint16_t* Y = static_cast<uint16_t*>(p.y);
+      const uint2 packed = make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
+      *reinterpret_cast<uint2*>(Y + grow * p.y_stride + col) = packed;
+      if (p.ss_out) {
+        float ss = 0.0f;
+        const float q4[4] = {bf_lo(packed.x), bf_hi(packed.x), bf_lo(packed.y), bf_hi(packed.y)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ss = __fmaf_rn(q4[j], q4[j], ss);
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
+        if (ln == 0) p.ss_out[tile * p.ss_out_stride + grow] = ss;
       }
     }
   }
@@ -334,8 +477,6 @@ int num_sms() {
   return n;
 }
 
-constexpr int kMaxSplits = 16;
-
 template <int EPI>
 void set_kernel_attrs() {
   static std::once_flag once;
@@ -382,18 +523,23 @@ int max_active_clusters(int S, size_t smem) {
   return n;
 }
 
-size_t plan_smem(int row_tile, int stages) {
+size_t plan_smem(int row_tile, int stages, int splits) {
   const size_t stage_bytes = (size_t)kTileN * kBK * 2 + (size_t)row_tile * kBK * 2;
-  return 1024 + (size_t)stages * stage_bytes + 2 * kMaxStages * 8 + 8 + 16;
+  const int per = (row_tile + splits - 1) / splits;
+  const size_t info = (size_t)3 * ((per + 1) & ~1) * 4;
+  return 1024 + (size_t)stages * stage_bytes + info + (2 * kMaxStages + 2) * 8 + 16;
 }
 
-int plan_stages(int row_tile, int kb_per) {
+int plan_stages(int row_tile, int kb_per, int splits) {
   const size_t stage_bytes = (size_t)kTileN * kBK * 2 + (size_t)row_tile * kBK * 2;
   int st = kb_per < 4 ? kb_per : 4;
   if (st < 1) st = 1;
-  // the epilogue staging [row_tile][128] fp32 reuses the stage buffers
+  // the partial tile [row_tile][128] fp32 is staged over the stage buffers
   const size_t staging = (size_t)row_tile * kTileN * 4;
   while ((size_t)st * stage_bytes < staging && st < kMaxStages) ++st;
+  while (st > 1 && plan_smem(row_tile, st, splits) > 227 * 1024 &&
+         (size_t)(st - 1) * stage_bytes >= staging)
+    --st;
   return st;
 }
 
@@ -419,8 +565,10 @@ Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
     // the widest split whose clusters all fit in one wave, preferring more busy SMs
     long best_busy = 0;
     for (int S = 1; S <= kMaxSplits && S <= pl.num_kb; ++S) {
-      const int st = plan_stages(pl.row_tile, (pl.num_kb + S - 1) / S);
-      const int fit = S == 1 ? num_sms() : max_active_clusters<EPI>(S, plan_smem(pl.row_tile, st));
+      const int st = plan_stages(pl.row_tile, (pl.num_kb + S - 1) / S, S);
+      const size_t sm = plan_smem(pl.row_tile, st, S);
+      if (sm > 227 * 1024) continue;
+      const int fit = S == 1 ? num_sms() : max_active_clusters<EPI>(S, sm);
       if (clusters > fit) continue;
       const long busy = (long)clusters * S;
       if (busy > best_busy) {
@@ -432,25 +580,24 @@ Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
   if (best > pl.num_kb) best = pl.num_kb;
   if (best < 1) best = 1;
   pl.splits = best;
-  pl.stages = plan_stages(pl.row_tile, (pl.num_kb + best - 1) / best);
+  pl.stages = plan_stages(pl.row_tile, (pl.num_kb + best - 1) / best, best);
   int tc = 32;
   while (tc < pl.row_tile) tc <<= 1;
   pl.tmem_cols = tc;
-  pl.smem = plan_smem(pl.row_tile, pl.stages);
+  pl.smem = plan_smem(pl.row_tile, pl.stages, best);
   return pl;
 }
 
 template <int EPI>
-int launch_gemm(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n,
-                const void* residual, int64_t residual_stride, void* y, int64_t y_stride, int splits_req,
-                cudaStream_t st) {
+int launch_gemm(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n, GemmParams gp,
+                int splits_req, cudaStream_t st) {
   const Plan pl = make_plan<EPI>(rows, k, n, splits_req);
   if (pl.splits > kMaxSplits) return set_error(OMNI_ERR_UNSUPPORTED, "at most 16 K-splits");
+  if (pl.smem > 227 * 1024) return set_error(OMNI_ERR_UNSUPPORTED, "GEMM tile does not fit in shared memory");
   CUtensorMap tw, tx;
   const int wbox = EPI == kEpiSwiGLU ? kTileN / 2 : kTileN;
   if (!make_tmap(&tw, w, n, k, k, wbox) || !make_tmap(&tx, x, rows, k, x_stride, pl.row_tile))
     return set_error(OMNI_ERR_UNSUPPORTED, "tensor map encoding failed");
-  GemmParams gp{};
   gp.rows = (int)rows;
   gp.K = (int)k;
   gp.N = (int)n;
@@ -460,10 +607,6 @@ int launch_gemm(const void* x, int64_t rows, int64_t k, int64_t x_stride, const 
   gp.stages = pl.stages;
   gp.tmem_cols = pl.tmem_cols;
   gp.swiglu_half = (int)(n / 2);
-  gp.residual = static_cast<const uint16_t*>(residual);
-  gp.res_stride = residual_stride;
-  gp.y = y;
-  gp.y_stride = y_stride;
   set_kernel_attrs<EPI>();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)pl.tiles, (unsigned)pl.num_rt, (unsigned)pl.splits);
@@ -489,6 +632,47 @@ int launch_gemm(const void* x, int64_t rows, int64_t k, int64_t x_stride, const 
   return check_launch(cudaLaunchKernelEx(&cfg, gemm_kernel<EPI>, tw, tx, gp));
 }
 
+int run_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n, int epilogue,
+               const GemmParams& gp, int splits, cudaStream_t st) {
+  if (rows < 0 || k <= 0 || n <= 0) return set_error(OMNI_ERR_INVALID, "bad GEMM shape");
+  if (epilogue < 0 || epilogue > 4) return set_error(OMNI_ERR_INVALID, "unknown epilogue");
+  if (splits < 0 || splits > kMaxSplits) return set_error(OMNI_ERR_INVALID, "splits must be in [0, 16]");
+  if (k % kBK != 0) return set_error(OMNI_ERR_UNSUPPORTED, "K must be a multiple of 64");
+  if (n % kTileN != 0) return set_error(OMNI_ERR_UNSUPPORTED, "N must be a multiple of 128");
+  auto mis16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
+  if (mis16(x) || mis16(w) || (x_stride % 8) != 0 || mis16(gp.y) || (gp.y_stride % 4) != 0)
+    return set_error(OMNI_ERR_UNSUPPORTED, "operands must be 16-byte aligned with 16-byte row strides");
+  if (epilogue == kEpiResidual && (gp.residual == nullptr || (gp.res_stride % 4) != 0 ||
+                                   (reinterpret_cast<uintptr_t>(gp.residual) & 7) != 0))
+    return set_error(OMNI_ERR_INVALID, "residual epilogue needs an 8-byte aligned residual");
+  if (gp.ss_in && (gp.ss_in_parts <= 0 || gp.ss_in_parts > 64 || gp.norm_dim <= 0))
+    return set_error(OMNI_ERR_INVALID, "ss_in needs 1..64 parts and norm_dim > 0");
+  if (gp.ss_out && (epilogue == kEpiSwiGLU || epilogue == kEpiF32 || epilogue == kEpiQKV))
+    return set_error(OMNI_ERR_UNSUPPORTED, "ss_out is produced by the store and residual epilogues only");
+  if (epilogue == kEpiQKV) {
+    if (gp.head_dim != 64 && gp.head_dim != 128)
+      return set_error(OMNI_ERR_UNSUPPORTED, "qkv epilogue supports head_dim 64 or 128");
+    if (gp.hq <= 0 || gp.hkv <= 0 || (int64_t)(gp.hq + 2 * gp.hkv) * gp.head_dim != n)
+      return set_error(OMNI_ERR_INVALID, "qkv epilogue: N must be (Hq + 2 Hkv) * head_dim");
+    if ((gp.positions == nullptr) != (gp.cache_loc == nullptr))
+      return set_error(OMNI_ERR_INVALID, "positions and cache_loc are given together");
+    if (gp.positions == nullptr && (gp.tokens_per_req <= 0 || gp.slot_stride <= 0 || gp.slot_base < 0 ||
+                                    gp.slot_base + gp.tokens_per_req > gp.max_pos))
+      return set_error(OMNI_ERR_INVALID, "implicit slots need tokens_per_req, slot_stride > 0 within the rotary table");
+    if (!gp.q_norm || !gp.k_norm || !gp.cos_sin || !gp.k_cache || !gp.v_cache)
+      return set_error(OMNI_ERR_INVALID, "qkv epilogue needs norms, cos/sin table and caches");
+  }
+  if (rows == 0) return OMNI_OK;
+  if (splits > k / kBK) splits = (int)(k / kBK);
+  switch (epilogue) {
+    case kEpiStore: return launch_gemm<kEpiStore>(x, rows, k, x_stride, w, n, gp, splits, st);
+    case kEpiResidual: return launch_gemm<kEpiResidual>(x, rows, k, x_stride, w, n, gp, splits, st);
+    case kEpiSwiGLU: return launch_gemm<kEpiSwiGLU>(x, rows, k, x_stride, w, n, gp, splits, st);
+    case kEpiQKV: return launch_gemm<kEpiQKV>(x, rows, k, x_stride, w, n, gp, splits, st);
+    default: return launch_gemm<kEpiF32>(x, rows, k, x_stride, w, n, gp, splits, st);
+  }
+}
+
 }  // namespace
 }  // namespace omni
 
@@ -505,24 +689,44 @@ extern "C" OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int6
                                     void* y, int64_t y_stride, void* workspace, int64_t workspace_bytes_avail,
                                     int32_t splits, void* stream) {
   (void)workspace, (void)workspace_bytes_avail;
-  if (rows < 0 || k <= 0 || n <= 0) return set_error(OMNI_ERR_INVALID, "bad GEMM shape");
-  if (epilogue < 0 || epilogue > 3) return set_error(OMNI_ERR_INVALID, "unknown epilogue");
-  if (splits < 0 || splits > kMaxSplits) return set_error(OMNI_ERR_INVALID, "splits must be in [0, 16]");
-  if (k % kBK != 0) return set_error(OMNI_ERR_UNSUPPORTED, "K must be a multiple of 64");
-  if (n % kTileN != 0) return set_error(OMNI_ERR_UNSUPPORTED, "N must be a multiple of 128");
-  auto mis16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
-  if (mis16(x) || mis16(w) || (x_stride % 8) != 0 || mis16(y) || (y_stride % 4) != 0)
-    return set_error(OMNI_ERR_UNSUPPORTED, "operands must be 16-byte aligned with 16-byte row strides");
-  if (epilogue == kEpiResidual && (residual == nullptr || (residual_stride % 4) != 0 ||
-                                   (reinterpret_cast<uintptr_t>(residual) & 7) != 0))
-    return set_error(OMNI_ERR_INVALID, "residual epilogue needs an 8-byte aligned residual");
-  if (rows == 0) return OMNI_OK;
-  if (splits > k / kBK) splits = (int32_t)(k / kBK);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (epilogue) {
-    case kEpiStore: return launch_gemm<kEpiStore>(x, rows, k, x_stride, w, n, residual, residual_stride, y, y_stride, splits, st);
-    case kEpiResidual: return launch_gemm<kEpiResidual>(x, rows, k, x_stride, w, n, residual, residual_stride, y, y_stride, splits, st);
-    case kEpiSwiGLU: return launch_gemm<kEpiSwiGLU>(x, rows, k, x_stride, w, n, residual, residual_stride, y, y_stride, splits, st);
-    default: return launch_gemm<kEpiF32>(x, rows, k, x_stride, w, n, residual, residual_stride, y, y_stride, splits, st);
-  }
+  if (epilogue == kEpiQKV) return set_error(OMNI_ERR_INVALID, "the qkv epilogue is reached through omni_linear_fused");
+  GemmParams gp{};
+  gp.residual = static_cast<const uint16_t*>(residual);
+  gp.res_stride = residual_stride;
+  gp.y = y;
+  gp.y_stride = y_stride;
+  return run_linear(x, rows, k, x_stride, w, n, epilogue, gp, splits, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" OMNI_API int omni_linear_fused(const OmniLinearArgs* a, void* stream) {
+  if (a == nullptr) return set_error(OMNI_ERR_INVALID, "null arguments");
+  GemmParams gp{};
+  gp.residual = static_cast<const uint16_t*>(a->residual);
+  gp.res_stride = a->residual_stride;
+  gp.y = a->y;
+  gp.y_stride = a->y_stride;
+  gp.ss_in = a->ss_in;
+  gp.ss_in_parts = a->ss_in_parts;
+  gp.ss_in_stride = a->ss_in_stride;
+  gp.norm_dim = a->norm_dim;
+  gp.norm_eps = a->norm_eps;
+  gp.ss_out = a->ss_out;
+  gp.ss_out_stride = a->ss_out_stride;
+  gp.hq = a->num_q_heads;
+  gp.hkv = a->num_kv_heads;
+  gp.head_dim = a->head_dim;
+  gp.q_norm = static_cast<const uint16_t*>(a->q_norm);
+  gp.k_norm = static_cast<const uint16_t*>(a->k_norm);
+  gp.qk_eps = a->qk_eps;
+  gp.cos_sin = a->cos_sin;
+  gp.max_pos = a->max_position;
+  gp.positions = a->positions;
+  gp.cache_loc = a->cache_loc;
+  gp.tokens_per_req = a->tokens_per_req;
+  gp.slot_stride = a->slot_stride;
+  gp.slot_base = a->slot_base;
+  gp.k_cache = static_cast<uint16_t*>(a->k_cache);
+  gp.v_cache = static_cast<uint16_t*>(a->v_cache);
+  return run_linear(a->x, a->rows, a->k, a->x_stride, a->w, a->n, a->epilogue, gp, a->splits,
+                    static_cast<cudaStream_t>(stream));
 }

@@ -158,10 +158,71 @@ __global__ void __launch_bounds__(128) qknorm_rope_store_kernel(const __grid_con
   }
 }
 
+// ---------------------------------------------------------------------------
+// sum = bf16(a + b) (or a copy of a) and its per-row sum of squares: the input
+// row of a decoder stack whose first RMSNorm is folded into the next GEMM.
+// ---------------------------------------------------------------------------
+template <int CHUNKS>
+__global__ void __launch_bounds__(128) add_sumsq_kernel(const uint16_t* __restrict__ a, int64_t a_stride,
+                                                        const uint16_t* __restrict__ b, int64_t b_stride,
+                                                        uint16_t* __restrict__ sum, int64_t s_stride,
+                                                        float* __restrict__ ss_out, int rows) {
+  griddep_wait();
+  griddep_launch();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + warp;
+  if (row >= rows) return;
+  float acc = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CHUNKS; ++c) {
+    const int col = 256 * c + 8 * lane;
+    uint4 x = *reinterpret_cast<const uint4*>(a + row * a_stride + col);
+    uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+    if (b) {
+      uint4 y = *reinterpret_cast<const uint4*>(b + row * b_stride + col);
+      uint32_t ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) xs[q] = pack_bf2(bf_lo(xs[q]) + bf_lo(ys[q]), bf_hi(xs[q]) + bf_hi(ys[q]));
+    }
+    *reinterpret_cast<uint4*>(sum + row * s_stride + col) = make_uint4(xs[0], xs[1], xs[2], xs[3]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      acc = __fmaf_rn(bf_lo(xs[q]), bf_lo(xs[q]), acc);
+      acc = __fmaf_rn(bf_hi(xs[q]), bf_hi(xs[q]), acc);
+    }
+  }
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
+  if (lane == 0) ss_out[row] = acc;
+}
+
 }  // namespace
 }  // namespace omni
 
 using namespace omni;
+
+extern "C" OMNI_API int omni_add_sumsq(const void* a, int64_t a_stride, const void* b, int64_t b_stride, void* sum,
+                                       int64_t sum_stride, float* ss_out, int64_t rows, int64_t hidden,
+                                       void* stream) {
+  if (rows < 0 || hidden <= 0 || sum == nullptr || ss_out == nullptr) return set_error(OMNI_ERR_INVALID, "bad shape");
+  if (hidden % 256 != 0 || hidden > 8192) return set_error(OMNI_ERR_UNSUPPORTED, "hidden must be 256k, <= 8192");
+  auto mis = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
+  if (mis(a) || mis(sum) || (b && mis(b)) || a_stride % 8 || sum_stride % 8 || (b && b_stride % 8))
+    return set_error(OMNI_ERR_UNSUPPORTED, "rows must be 16-byte aligned");
+  if (rows == 0) return OMNI_OK;
+  dim3 g((unsigned)((rows + 3) / 4)), bl(128);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto A = static_cast<const uint16_t*>(a);
+  auto B = static_cast<const uint16_t*>(b);
+  auto S = static_cast<uint16_t*>(sum);
+  switch (hidden / 256) {
+    case 1: return check_launch(launch(add_sumsq_kernel<1>, g, bl, 0, st, A, a_stride, B, b_stride, S, sum_stride, ss_out, (int)rows));
+    case 2: return check_launch(launch(add_sumsq_kernel<2>, g, bl, 0, st, A, a_stride, B, b_stride, S, sum_stride, ss_out, (int)rows));
+    case 4: return check_launch(launch(add_sumsq_kernel<4>, g, bl, 0, st, A, a_stride, B, b_stride, S, sum_stride, ss_out, (int)rows));
+    case 8: return check_launch(launch(add_sumsq_kernel<8>, g, bl, 0, st, A, a_stride, B, b_stride, S, sum_stride, ss_out, (int)rows));
+  }
+  return set_error(OMNI_ERR_UNSUPPORTED, "hidden must be 256 x {1,2,4,8}");
+}
 
 extern "C" OMNI_API int omni_rmsnorm(const void* x, int64_t x_stride, const void* addend, int64_t addend_stride,
                                      void* residual_out, int64_t residual_stride, const void* weight, float eps,

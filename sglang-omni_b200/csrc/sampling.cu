@@ -437,12 +437,20 @@ OMNI_DEVINL int block_argmax(const float (&v)[EPT], const bool (&valid)[EPT], in
   return bi;
 }
 
-// Fused embedding epilogue: gathered[row] = table[token]; summed[row] += it.
-OMNI_DEVINL void gather_add_row(const uint16_t* __restrict__ table, int hidden, int64_t token,
-                                uint16_t* __restrict__ gathered, uint16_t* __restrict__ summed) {
+// Fused embedding epilogue: gathered[row] = table[token]; summed[row] += it;
+// returns this thread's part of the gathered row's sum of squares.
+OMNI_DEVINL float gather_add_row(const uint16_t* __restrict__ table, int hidden, int64_t token,
+                                 uint16_t* __restrict__ gathered, uint16_t* __restrict__ summed) {
   const uint4* src = reinterpret_cast<const uint4*>(table + token * (int64_t)hidden);
+  float ss = 0.0f;
   for (int v = threadIdx.x; v < hidden / 8; v += kThreads) {
     uint4 w = src[v];
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      ss = __fmaf_rn(bf_lo(ws[q]), bf_lo(ws[q]), ss);
+      ss = __fmaf_rn(bf_hi(ws[q]), bf_hi(ws[q]), ss);
+    }
     if (gathered) reinterpret_cast<uint4*>(gathered)[v] = w;
     if (summed) {
       uint4 s = reinterpret_cast<uint4*>(summed)[v];
@@ -453,6 +461,7 @@ OMNI_DEVINL void gather_add_row(const uint16_t* __restrict__ table, int hidden, 
       reinterpret_cast<uint4*>(summed)[v] = s;
     }
   }
+  return ss;
 }
 
 struct ResidualParams {
@@ -474,6 +483,7 @@ struct ResidualParams {
   int hidden;
   uint16_t* gathered;
   uint16_t* summed;
+  float* gathered_ss;  // nullable: sum of squares of each gathered row
 };
 
 // Loads EPT consecutive bf16 logits of a row: thread t holds [t*EPT, t*EPT+EPT).
@@ -575,9 +585,21 @@ __global__ void __launch_bounds__(kThreads) residual_sample_kernel(const __grid_
     token = sm.token;
   }
   if (tid == 0) p.out[row * p.out_stride] = token;
-  if (p.table != nullptr)
-    gather_add_row(p.table, p.hidden, token, p.gathered ? p.gathered + (int64_t)row * p.hidden : nullptr,
-                   p.summed ? p.summed + (int64_t)row * p.hidden : nullptr);
+  if (p.table != nullptr) {
+    float ss = gather_add_row(p.table, p.hidden, token, p.gathered ? p.gathered + (int64_t)row * p.hidden : nullptr,
+                              p.summed ? p.summed + (int64_t)row * p.hidden : nullptr);
+    if (p.gathered_ss) {
+      ss = warp_sum_xor(ss);
+      __syncthreads();
+      if (lane == 0) sm.fred[warp] = ss;
+      __syncthreads();
+      if (tid == 0) {
+        float t = sm.fred[0];
+        for (int w = 1; w < kWarps; ++w) t += sm.fred[w];
+        p.gathered_ss[row] = t;
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -891,7 +913,7 @@ extern "C" OMNI_API int omni_predictor_sample_step(const void* logits, int64_t r
                                                    const uint8_t* do_sample, int32_t argmax_all, int32_t max_top_k,
                                                    int32_t has_top_p, int64_t* codes, int64_t codes_stride,
                                                    const void* table, int64_t hidden, void* gathered, void* summed,
-                                                   void* stream) {
+                                                   float* gathered_ss, void* stream) {
   ResidualParams p = {};
   p.logits = static_cast<const uint16_t*>(logits);
   p.stride = logits_stride;
@@ -912,6 +934,7 @@ extern "C" OMNI_API int omni_predictor_sample_step(const void* logits, int64_t r
   p.hidden = (int)hidden;
   p.gathered = static_cast<uint16_t*>(gathered);
   p.summed = static_cast<uint16_t*>(summed);
+  p.gathered_ss = gathered_ss;
   return run_residual(p, rows, (int)vocab, argmax_all ? 32 : max_top_k, !argmax_all,
                       static_cast<cudaStream_t>(stream));
 }
@@ -1020,50 +1043,87 @@ extern "C" OMNI_API int omni_layer0_sample(const float* logits, int64_t rows, in
 }
 
 // ---------------------------------------------------------------------------
-// Opening inputs of the code predictor for one frame.
+// Opening inputs of the code predictor for one frame.  The talker's final
+// RMSNorm is applied here (its gain and the per-row sums of squares of the
+// talker's last residual): hidden = bf16(h * rstd * gain) is written to the
+// caller's hidden rows and to pair row 2r; the layer-0 code's embedding goes
+// to pair row 2r + 1 and to summed; both pair rows' sums of squares are written.
 // ---------------------------------------------------------------------------
 namespace omni {
 namespace {
-__global__ void __launch_bounds__(128) predictor_pair_inputs_kernel(const int64_t* __restrict__ c0,
-                                                                   const uint16_t* __restrict__ hidden,
-                                                                   int64_t hidden_stride,
-                                                                   const uint16_t* __restrict__ table, int H,
-                                                                   uint16_t* __restrict__ pair,
-                                                                   uint16_t* __restrict__ summed,
-                                                                   int64_t* __restrict__ codes, int64_t codes_stride) {
+__global__ void __launch_bounds__(128) predictor_pair_inputs_kernel(
+    const int64_t* __restrict__ c0, const uint16_t* __restrict__ h, int64_t h_stride,
+    const uint16_t* __restrict__ final_norm, const float* __restrict__ ss_in, int ss_parts, int64_t ss_stride,
+    float eps, uint16_t* __restrict__ hidden_out, const uint16_t* __restrict__ table, int H,
+    uint16_t* __restrict__ pair, uint16_t* __restrict__ summed, float* __restrict__ pair_ss,
+    int64_t* __restrict__ codes, int64_t codes_stride) {
+  __shared__ float red[2][4];
   griddep_wait();
   griddep_launch();
   const int row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t code = c0[row];
   if (threadIdx.x == 0) codes[row * codes_stride] = code;
+  float tot = 0.0f;
+  for (int q = 0; q < ss_parts; ++q) tot += ss_in[q * ss_stride + row];
+  const float rstd = rsqrtf(tot / (float)H + eps);
   const uint4* e = reinterpret_cast<const uint4*>(table + code * H);
-  const uint4* hs = reinterpret_cast<const uint4*>(hidden + row * hidden_stride);
+  const uint4* hs = reinterpret_cast<const uint4*>(h + row * h_stride);
+  const uint4* gw = reinterpret_cast<const uint4*>(final_norm);
   uint4* p0 = reinterpret_cast<uint4*>(pair + (int64_t)(2 * row) * H);
   uint4* p1 = reinterpret_cast<uint4*>(pair + (int64_t)(2 * row + 1) * H);
   uint4* sm = reinterpret_cast<uint4*>(summed + (int64_t)row * H);
+  uint4* ho = hidden_out ? reinterpret_cast<uint4*>(hidden_out + (int64_t)row * H) : nullptr;
+  float ss0 = 0.0f, ss1 = 0.0f;
   for (int v = threadIdx.x; v < H / 8; v += 128) {
-    const uint4 w = e[v];
-    p0[v] = hs[v];
+    const uint4 hv = hs[v], gv = gw[v], w = e[v];
+    const uint32_t hx[4] = {hv.x, hv.y, hv.z, hv.w}, gx[4] = {gv.x, gv.y, gv.z, gv.w}, wx[4] = {w.x, w.y, w.z, w.w};
+    uint32_t nx[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      nx[q] = pack_bf2(bf_lo(hx[q]) * rstd * bf_lo(gx[q]), bf_hi(hx[q]) * rstd * bf_hi(gx[q]));
+      ss0 = __fmaf_rn(bf_lo(nx[q]), bf_lo(nx[q]), ss0);
+      ss0 = __fmaf_rn(bf_hi(nx[q]), bf_hi(nx[q]), ss0);
+      ss1 = __fmaf_rn(bf_lo(wx[q]), bf_lo(wx[q]), ss1);
+      ss1 = __fmaf_rn(bf_hi(wx[q]), bf_hi(wx[q]), ss1);
+    }
+    const uint4 n = make_uint4(nx[0], nx[1], nx[2], nx[3]);
+    p0[v] = n;
+    if (ho) ho[v] = n;
     p1[v] = w;
     sm[v] = w;
+  }
+  ss0 = warp_sum_xor(ss0);
+  ss1 = warp_sum_xor(ss1);
+  if (lane == 0) {
+    red[0][warp] = ss0;
+    red[1][warp] = ss1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    pair_ss[2 * row] = red[0][0] + red[0][1] + red[0][2] + red[0][3];
+    pair_ss[2 * row + 1] = red[1][0] + red[1][1] + red[1][2] + red[1][3];
   }
 }
 }  // namespace
 }  // namespace omni
 
-extern "C" OMNI_API int omni_predictor_pair_inputs(const int64_t* layer0_codes, const void* talker_hidden,
-                                                   int64_t hidden_stride, const void* table, int64_t rows,
-                                                   int64_t hidden, void* pair, void* summed, int64_t* codes,
-                                                   int64_t codes_stride, void* stream) {
-  if (rows < 0 || hidden <= 0) return omni::set_error(OMNI_ERR_INVALID, "bad shape");
+extern "C" OMNI_API int omni_predictor_pair_inputs(const int64_t* layer0_codes, const void* talker_residual,
+                                                   int64_t residual_stride, const void* final_norm_weight,
+                                                   const float* ss_in, int32_t ss_parts, int64_t ss_stride,
+                                                   float eps, void* hidden_out, const void* table, int64_t rows,
+                                                   int64_t hidden, void* pair, void* summed, float* pair_ss,
+                                                   int64_t* codes, int64_t codes_stride, void* stream) {
+  if (rows < 0 || hidden <= 0 || ss_parts <= 0 || !ss_in || !pair_ss) return omni::set_error(OMNI_ERR_INVALID, "bad shape");
   auto mis = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
-  if (hidden % 8 || hidden_stride % 8 || mis(talker_hidden) || mis(table) || mis(pair) || mis(summed))
+  if (hidden % 8 || residual_stride % 8 || mis(talker_residual) || mis(table) || mis(pair) || mis(summed) ||
+      mis(final_norm_weight) || (hidden_out && mis(hidden_out)))
     return omni::set_error(OMNI_ERR_UNSUPPORTED, "rows must be 16-byte aligned");
   if (rows == 0) return OMNI_OK;
-  return omni::check_launch(omni::launch(omni::predictor_pair_inputs_kernel, dim3((unsigned)rows), dim3(128), 0,
-                                         static_cast<cudaStream_t>(stream), layer0_codes,
-                                         static_cast<const uint16_t*>(talker_hidden), hidden_stride,
-                                         static_cast<const uint16_t*>(table), (int)hidden,
-                                         static_cast<uint16_t*>(pair), static_cast<uint16_t*>(summed), codes,
-                                         codes_stride));
+  return omni::check_launch(omni::launch(
+      omni::predictor_pair_inputs_kernel, dim3((unsigned)rows), dim3(128), 0, static_cast<cudaStream_t>(stream),
+      layer0_codes, static_cast<const uint16_t*>(talker_residual), residual_stride,
+      static_cast<const uint16_t*>(final_norm_weight), ss_in, (int)ss_parts, ss_stride, eps,
+      static_cast<uint16_t*>(hidden_out), static_cast<const uint16_t*>(table), (int)hidden,
+      static_cast<uint16_t*>(pair), static_cast<uint16_t*>(summed), pair_ss, codes, codes_stride));
 }

@@ -34,12 +34,15 @@ SIGNATURES: dict[str, list] = {
     "omni_device_status": [ctypes.c_int],
     "omni_sample_topk_topp": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I32, _I32, _P, _P],
     "omni_predictor_sample_step": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _I32, _I32, _I32,
-                                   _P, _I64, _P, _I64, _P, _P, _P],
+                                   _P, _I64, _P, _I64, _P, _P, _P, _P],
     "omni_sample_sorted_seeded": [_P, _P, _I64, _I64, _P, _P, _P, _P],
     "omni_codebook_step": [_P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P],
     "omni_gather_embedding_add": [_P, _I32, _I64, _P, _I64, _P, _P, _P, _I64, _P, _P],
     "omni_layer0_sample": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P, _P],
-    "omni_predictor_pair_inputs": [_P, _P, _I64, _P, _I64, _I64, _P, _P, _P, _I64, _P],
+    "omni_predictor_pair_inputs": [_P, _P, _I64, _P, _P, _I32, _I64, _F32, _P, _P, _I64, _I64, _P, _P, _P, _P, _I64,
+                                   _P],
+    "omni_add_sumsq": [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _P],
+    "omni_linear_fused": [_P, _P],
     "omni_linear_workspace_bytes": [_I64, _I64, _I64, _I32, _I32],
     "omni_linear": [_P, _I64, _I64, _I64, _P, _I64, _I32, _P, _I64, _P, _I64, _P, _I64, _I32, _P],
     "omni_rmsnorm": [_P, _I64, _P, _I64, _P, _I64, _P, _F32, _P, _I64, _I64, _I64, _P],

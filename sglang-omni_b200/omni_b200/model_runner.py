@@ -172,7 +172,10 @@ class TalkerDecodeRunner:
         feedback = self.predictor.output_embeds[:B]
         logits = self.talker.forward(feedback, self.text_embeds[:B], forward_batch)
         c0 = self.talker.sample_decode_tokens(logits, forward_batch)
-        codes, summed = self.predictor.code_predictor_forward(c0, self.talker.hidden[:B], forward_batch.positions)
+        t = self.talker
+        codes, summed = self.predictor.code_predictor_forward(
+            c0, t.h[:B], forward_batch.positions, final_norm=t.w["norm"], final_ss=t.ss, final_eps=self.cfg.rms_norm_eps,
+            hidden_out=t.hidden[:B])
         return GenerationBatchResult(next_token_ids=c0, next_token_logits=logits, hidden_states=self.talker.hidden[:B],
                                      codes=codes[:, :, 0], summed_embeds=summed[:, 0])
 

@@ -7,6 +7,8 @@ and must be zero-filled once before first use.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from omni_b200 import _lib
@@ -15,6 +17,99 @@ EPI_STORE = 0
 EPI_RESIDUAL = 1
 EPI_SWIGLU = 2
 EPI_F32 = 3
+EPI_QKV_ROPE = 4
+
+
+class OmniLinearArgs(ctypes.Structure):
+    """Mirror of OmniLinearArgs in include/omni_b200.h (same field order and types)."""
+
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("rows", ctypes.c_int64), ("k", ctypes.c_int64), ("x_stride", ctypes.c_int64),
+        ("w", ctypes.c_void_p), ("n", ctypes.c_int64), ("epilogue", ctypes.c_int32), ("splits", ctypes.c_int32),
+        ("ss_in", ctypes.c_void_p), ("ss_in_parts", ctypes.c_int32), ("ss_in_stride", ctypes.c_int64),
+        ("norm_dim", ctypes.c_int32), ("norm_eps", ctypes.c_float), ("residual", ctypes.c_void_p),
+        ("residual_stride", ctypes.c_int64), ("y", ctypes.c_void_p), ("y_stride", ctypes.c_int64),
+        ("ss_out", ctypes.c_void_p), ("ss_out_stride", ctypes.c_int64), ("num_q_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("q_norm", ctypes.c_void_p),
+        ("k_norm", ctypes.c_void_p), ("qk_eps", ctypes.c_float), ("cos_sin", ctypes.c_void_p),
+        ("max_position", ctypes.c_int64), ("positions", ctypes.c_void_p), ("cache_loc", ctypes.c_void_p),
+        ("tokens_per_req", ctypes.c_int32), ("slot_stride", ctypes.c_int32), ("slot_base", ctypes.c_int32),
+        ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+    ]
+
+
+def linear_fused(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    epilogue: int,
+    ss_in: torch.Tensor | None = None,
+    ss_in_parts: int = 0,
+    norm_eps: float = 1e-6,
+    residual: torch.Tensor | None = None,
+    ss_out: torch.Tensor | None = None,
+    qkv: dict | None = None,
+    splits: int = 0,
+) -> torch.Tensor:
+    """out = epilogue(rstd * (x @ w.T)) with the RMSNorm folded into w (gain already
+    multiplied into its columns) and rstd from ss_in [parts, rows_cap] sums of squares.
+    ss_out [parts, rows_cap] receives the output's per-tile sums of squares.
+    qkv: head geometry, norms, rotary table and caches for EPI_QKV_ROPE."""
+    a = OmniLinearArgs()
+    a.x = x.data_ptr()
+    a.rows, a.k = x.shape
+    a.x_stride = x.stride(0)
+    a.w = w.data_ptr()
+    a.n = w.shape[0]
+    a.epilogue = epilogue
+    a.splits = splits
+    if ss_in is not None:
+        a.ss_in = ss_in.data_ptr()
+        a.ss_in_parts = ss_in_parts
+        a.ss_in_stride = ss_in.stride(0) if ss_in.ndim == 2 else ss_in.shape[0]
+        a.norm_dim = x.shape[1]
+        a.norm_eps = norm_eps
+    if residual is not None:
+        a.residual = residual.data_ptr()
+        a.residual_stride = residual.stride(0)
+    a.y = out.data_ptr()
+    a.y_stride = out.stride(0)
+    if ss_out is not None:
+        a.ss_out = ss_out.data_ptr()
+        a.ss_out_stride = ss_out.stride(0)
+    if qkv is not None:
+        a.num_q_heads = qkv["num_q_heads"]
+        a.num_kv_heads = qkv["num_kv_heads"]
+        a.head_dim = qkv["head_dim"]
+        a.q_norm = qkv["q_norm"].data_ptr()
+        a.k_norm = qkv["k_norm"].data_ptr()
+        a.qk_eps = qkv.get("eps", 1e-6)
+        a.cos_sin = qkv["cos_sin"].data_ptr()
+        a.max_position = qkv["cos_sin"].shape[0]
+        if qkv.get("positions") is not None:
+            a.positions = qkv["positions"].data_ptr()
+            a.cache_loc = qkv["cache_loc"].data_ptr()
+        else:
+            a.tokens_per_req = qkv["tokens_per_req"]
+            a.slot_stride = qkv["slot_stride"]
+            a.slot_base = qkv["slot_base"]
+        a.k_cache = qkv["k_cache"].data_ptr()
+        a.v_cache = qkv["v_cache"].data_ptr()
+    _lib.call("omni_linear_fused", ctypes.addressof(a), _lib.stream_of(x.device))
+    return out
+
+
+def add_sumsq(a: torch.Tensor, b: torch.Tensor | None, out: torch.Tensor, ss_out: torch.Tensor) -> torch.Tensor:
+    """out = bf16(a + b) (or a copy of a); ss_out[r] = sum of squares of out[r]."""
+    _lib.call("omni_add_sumsq", a.data_ptr(), a.stride(0), _lib.ptr(b), 0 if b is None else b.stride(0),
+              out.data_ptr(), out.stride(0), ss_out.data_ptr(), a.shape[0], a.shape[1], _lib.stream_of(a.device))
+    return out
+
+
+def fold_norm(weight: torch.Tensor, gain: torch.Tensor) -> torch.Tensor:
+    """W * diag(gain) rounded to bf16: the weight of a GEMM whose input RMSNorm is folded."""
+    return (weight.float() * gain.float()[None, :]).to(torch.bfloat16).contiguous()
 
 
 def linear_workspace_bytes(rows: int, k: int, n: int, epilogue: int = EPI_STORE, splits: int = 0) -> int:

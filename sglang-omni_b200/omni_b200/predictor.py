@@ -81,7 +81,18 @@ class CodePredictor:
         self.act = torch.zeros(R, I, **bf)
         self.out = torch.zeros(R, H, **bf)
         self.next_in = torch.zeros(max_batch, H, **bf)
-        self.logits = torch.zeros(G - 1, max_batch, cfg.vocab_size, **bf)
+        # lm_head logits of codebook j; codebook 0 is computed on all 2B rows of the
+        # opening pair pass and read at the odd (layer-0 token) rows
+        self.logits = torch.zeros(G - 1, R, cfg.vocab_size, **bf)
+        f32 = dict(device=self.device, dtype=torch.float32)
+        self.ss = torch.zeros(H // 128, R, **f32)     # residual stream sums of squares per 128-feature tile
+        self.pair_ss = torch.zeros(R, **f32)           # opening pair rows
+        self.next_ss = torch.zeros(max_batch, **f32)   # gathered embedding rows
+        self.folded = [{"qkv": ops.fold_norm(lw["qkv_proj"], lw["input_layernorm"]),
+                        "gate_up": ops.fold_norm(lw["gate_up_proj"], lw["post_attention_layernorm"])}
+                       for lw in weights["layers"]]
+        self.lm_head_folded = torch.stack([ops.fold_norm(weights["lm_head"][j], weights["norm"])
+                                           for j in range(G - 1)])
         self.output_codes = torch.zeros(max_batch, G, dtype=torch.long, device=self.device)
         self.output_embeds = torch.zeros(max_batch, H, **bf)
         # per-row residual sampling state (sub_*_tensor of sglang_model.py:1115-1140)
@@ -129,45 +140,57 @@ class CodePredictor:
         del dev
 
     # ------------------------------------------------------------------
-    def forward_tokens(self, x: torch.Tensor, *, batch: int, tokens: int, cache_len: int) -> torch.Tensor:
-        """The predictor stack on rows (request, token) at slots cache_len.. ;
-        returns the final-normed rows (predictor_forward_tokens, sglang_model.py:2036-2098)."""
+    def forward_tokens(self, x: torch.Tensor, x_ss: torch.Tensor, *, batch: int, tokens: int,
+                       cache_len: int) -> torch.Tensor:
+        """The predictor stack on rows (request, token) at slots cache_len.. with input
+        sums of squares x_ss (one part); leaves the residual stream in self.h and its sums
+        of squares in self.ss, the input of the folded final norm of the lm_head
+        (predictor_forward_tokens, sglang_model.py:2036-2098)."""
         cfg = self.cfg
         rows = batch * tokens
         H, D = cfg.hidden_size, cfg.head_dim
         hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
         eps = cfg.rms_norm_eps
-        h, normed, qkv, q, attn, act = (self.h[:rows], self.normed[:rows], self.qkv[:rows], self.q[:rows],
-                                        self.attn[:rows], self.act[:rows])
-        ws = self.workspace
-        resid = x
+        h, q, attn, act = self.h[:rows], self.q[:rows], self.attn[:rows], self.act[:rows]
+        parts = H // 128
+        resid, ss_in, ss_parts = x, x_ss, 1
         for li, lw in enumerate(self.w["layers"]):
-            ops.rmsnorm(resid, lw["input_layernorm"], eps, out=normed)
-            ops.linear(normed, lw["qkv_proj"], out=qkv, workspace=ws)
-            ops.qknorm_rope_store(qkv, num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=lw["q_norm"],
-                                  k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin, q_out=q,
-                                  k_cache=self.k_cache[li], v_cache=self.v_cache[li], tokens_per_req=tokens,
-                                  slot_stride=cfg.cache_len, slot_base=cache_len)
+            ops.linear_fused(resid, self.folded[li]["qkv"], q, epilogue=ops.EPI_QKV_ROPE, ss_in=ss_in,
+                             ss_in_parts=ss_parts, norm_eps=eps,
+                             qkv=dict(num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=lw["q_norm"],
+                                      k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin, tokens_per_req=tokens,
+                                      slot_stride=cfg.cache_len, slot_base=cache_len, k_cache=self.k_cache[li],
+                                      v_cache=self.v_cache[li]))
             ops.predictor_attention(q, self.k_cache[li], self.v_cache[li], num_q_heads=hq, num_kv_heads=hkv,
                                     head_dim=D, tokens_per_req=tokens, slot_stride=cfg.cache_len,
                                     slot_base=cache_len, sm_scale=self.scale, out=attn)
-            ops.linear(attn, lw["o_proj"], epilogue=ops.EPI_RESIDUAL, residual=resid, out=h, workspace=ws)
-            resid = h
-            ops.rmsnorm(h, lw["post_attention_layernorm"], eps, out=normed)
-            ops.linear(normed, lw["gate_up_proj"], epilogue=ops.EPI_SWIGLU, out=act, workspace=ws)
-            ops.linear(act, lw["down_proj"], epilogue=ops.EPI_RESIDUAL, residual=h, out=h, workspace=ws)
-        out = self.out[:rows]
-        ops.rmsnorm(h, self.w["norm"], eps, out=out)
-        return out
+            ops.linear_fused(attn, lw["o_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=resid, ss_out=self.ss)
+            resid, ss_in, ss_parts = h, self.ss, parts
+            ops.linear_fused(h, self.folded[li]["gate_up"], act, epilogue=ops.EPI_SWIGLU, ss_in=self.ss,
+                             ss_in_parts=parts, norm_eps=eps)
+            ops.linear_fused(act, lw["down_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=self.ss)
+        return h
+
+    def codebook_logits(self, j: int, batch: int) -> torch.Tensor:
+        """The lm_head logits of residual codebook j + 1 for the batch's rows."""
+        return self.logits[0, 1: 2 * batch: 2] if j == 0 else self.logits[j, :batch]
 
     def code_predictor_forward(
         self,
         layer0_codes: torch.Tensor,
         talker_hidden: torch.Tensor,
         semantic_positions: torch.Tensor | None = None,
+        *,
+        final_norm: torch.Tensor,
+        final_ss: torch.Tensor,
+        final_eps: float = 1e-6,
+        hidden_out: torch.Tensor | None = None,
     ) -> tuple[torch.Tensor, torch.Tensor]:
-        """(layer0_codes [B, 1] i64, talker_hidden [B, 1, H] bf16, semantic_positions [B])
-        -> (codes [B, G, 1] i64, summed [B, 1, H] bf16) (sglang_model.py:1317-1346)."""
+        """(layer0_codes [B, 1] i64, talker residual [B, 1, H] bf16, semantic_positions [B])
+        -> (codes [B, G, 1] i64, summed [B, 1, H] bf16) (sglang_model.py:1317-1346).
+        The talker's final RMSNorm (gain final_norm, row sums of squares final_ss
+        [parts, rows]) is applied to talker_hidden on the way in; the normalized hidden
+        states are written to hidden_out when given."""
         cfg = self.cfg
         if layer0_codes.ndim == 2:
             layer0_codes = layer0_codes[:, 0]
@@ -185,16 +208,20 @@ class CodePredictor:
         from omni_b200 import _lib
 
         _lib.call("omni_predictor_pair_inputs", layer0_codes.data_ptr(), talker_hidden.data_ptr(),
-                  talker_hidden.stride(0), self.layer0_embedding.data_ptr(), B, H, pair.data_ptr(), summed.data_ptr(),
-                  codes.data_ptr(), codes.stride(0), _lib.stream_of(self.device))
-        out = self.forward_tokens(pair, batch=B, tokens=2, cache_len=0)
-        last = out[1::2]  # the layer-0 token's row of each request (row stride 2H)
+                  talker_hidden.stride(0), final_norm.data_ptr(), final_ss.data_ptr(), final_ss.shape[0],
+                  final_ss.stride(0), float(final_eps), _lib.ptr(hidden_out), self.layer0_embedding.data_ptr(), B, H,
+                  pair.data_ptr(), summed.data_ptr(), self.pair_ss.data_ptr(), codes.data_ptr(), codes.stride(0),
+                  _lib.stream_of(self.device))
+        h = self.forward_tokens(pair, self.pair_ss, batch=B, tokens=2, cache_len=0)
         argmax_all = not self.sub_has_sampled_rows
+        parts = H // 128
+        eps = cfg.rms_norm_eps
         for j in range(G - 1):
-            logits = self.logits[j, :B]
-            ops.linear(last, self.w["lm_head"][j], out=logits, workspace=self.workspace)
+            rows = 2 * B if j == 0 else B
+            ops.linear_fused(h[:rows], self.lm_head_folded[j], self.logits[j, :rows], epilogue=ops.EPI_STORE,
+                             ss_in=self.ss, ss_in_parts=parts, norm_eps=eps)
             predictor_sample_step(
-                logits,
+                self.codebook_logits(j, B),
                 temperatures=self.sub_temperature_tensor[:B],
                 top_ks=self.sub_top_k_tensor[:B],
                 top_ps=self.sub_top_p_tensor[:B],
@@ -210,7 +237,8 @@ class CodePredictor:
                 table=self.w["codec_embedding"][j],
                 gathered=self.next_in[:B],
                 summed=summed,
+                gathered_ss=self.next_ss[:B],
             )
             if j < G - 2:
-                last = self.forward_tokens(self.next_in[:B], batch=B, tokens=1, cache_len=2 + j)
+                h = self.forward_tokens(self.next_in[:B], self.next_ss[:B], batch=B, tokens=1, cache_len=2 + j)
         return codes.unsqueeze(-1), summed.unsqueeze(1)

@@ -176,6 +176,7 @@ def predictor_sample_step(
     table: torch.Tensor | None,
     gathered: torch.Tensor | None,
     summed: torch.Tensor | None,
+    gathered_ss: torch.Tensor | None = None,
 ) -> None:
     """One fused residual-codebook step of the code predictor: sample (or argmax)
     the code from lm_head logits, write codes[:, 0], gather its embedding row into
@@ -205,6 +206,7 @@ def predictor_sample_step(
         0 if table is None else table.shape[1],
         _lib.ptr(gathered),
         _lib.ptr(summed),
+        _lib.ptr(gathered_ss),
         _lib.stream_of(logits.device),
     )
 

@@ -9,9 +9,10 @@ attention -> o_proj + residual -> RMSNorm -> SwiGLU MLP + residual), the final
 RMSNorm and the codec head in fp32, then the layer-0 codec token draw
 (sample_decode_tokens, talker.py:1376-1412).
 
-Per layer the forward is 8 launches: rmsnorm, qkv GEMM, qknorm_rope_store,
-paged attention, o_proj GEMM (+residual), rmsnorm, gate_up GEMM (+SwiGLU),
-down GEMM (+residual); GEMMs run on the tcgen05 tensor cores.
+Per layer the forward is 5 launches, all but the attention tcgen05 GEMMs with
+fused epilogues: qkv (folded input RMSNorm + q/k RMSNorm + RoPE + KV store),
+paged attention, o_proj (+residual, row sums of squares), gate_up (folded
+post-attention RMSNorm + SwiGLU), down (+residual, row sums of squares).
 """
 
 from __future__ import annotations
@@ -108,6 +109,13 @@ class DenseTalker:
         self.sampling_min_ps = torch.zeros(B, **f32)
         self.sampling_seeds = torch.zeros(B, dtype=torch.long, device=self.device)
         self.max_top_k = 50
+        # folded RMSNorms: each norm's gain is multiplied into the columns of the GEMM it feeds;
+        # ss holds the per-row sums of squares of the residual stream (one part per 128 features)
+        self.folded = [{"qkv": ops.fold_norm(lw["qkv_proj"], lw["input_layernorm"]),
+                        "gate_up": ops.fold_norm(lw["gate_up_proj"], lw["post_attention_layernorm"])}
+                       for lw in self.w["layers"]]
+        self.codec_head_folded = ops.fold_norm(self.w["codec_head"], self.w["norm"])
+        self.ss = torch.zeros(H // 128, B, dtype=torch.float32, device=self.device)
 
     def ensure_attention_workspace(self, work_capacity: int) -> None:
         need = ops.paged_attention_workspace_bytes(self.max_batch, self.cfg.num_key_value_heads, work_capacity)
@@ -115,44 +123,44 @@ class DenseTalker:
             self.attn_workspace = torch.zeros(need, dtype=torch.uint8, device=self.device)
 
     def forward(self, feedback: torch.Tensor, text: torch.Tensor | None, fb: DecodeForwardBatch) -> torch.Tensor:
-        """Decode forward of B rows whose input is feedback (+ text); fills self.logits
-        (fp32) and self.hidden and returns the logits [B, V]."""
+        """Decode forward of B rows whose input is feedback (+ text); leaves the residual
+        stream in self.h (its sums of squares in self.ss, for the final norm applied by the
+        predictor's opening pass), fills self.logits (fp32) and returns them [B, V].
+
+        Per layer 4 projections + attention: the qkv GEMM carries the input RMSNorm (folded),
+        q/k RMSNorm, RoPE and the KV store; o_proj and down add the residual and emit the
+        sums of squares the next folded norm needs."""
         cfg = self.cfg
         B = fb.batch_size
         H, D = cfg.hidden_size, cfg.head_dim
         hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
         eps = cfg.rms_norm_eps
-        h, normed, qkv, q, attn, act = (self.h[:B], self.normed[:B], self.qkv[:B], self.q[:B], self.attn[:B],
-                                        self.act[:B])
-        ws = self.workspace
+        h, q, attn, act = self.h[:B], self.q[:B], self.attn[:B], self.act[:B]
+        ss = self.ss
+        parts = H // 128
         self.ensure_attention_workspace(fb.work_capacity)
+        ops.add_sumsq(feedback, text, h, ss[0])
+        ss_parts = 1
         for li, lw in enumerate(self.w["layers"]):
-            if li == 0:
-                if text is not None:
-                    ops.rmsnorm(feedback, lw["input_layernorm"], eps, addend=text, residual_out=h, out=normed)
-                else:
-                    h.copy_(feedback)
-                    ops.rmsnorm(h, lw["input_layernorm"], eps, out=normed)
-            else:
-                ops.rmsnorm(h, lw["input_layernorm"], eps, out=normed)
-            ops.linear(normed, lw["qkv_proj"], out=qkv, workspace=ws)
             kc, vc = self.kv.k_buffer[li], self.kv.v_buffer[li]
-            ops.qknorm_rope_store(qkv, num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=lw["q_norm"],
-                                  k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin, q_out=q, k_cache=kc,
-                                  v_cache=vc, positions=fb.positions, cache_loc=fb.out_cache_loc)
+            ops.linear_fused(h, self.folded[li]["qkv"], q, epilogue=ops.EPI_QKV_ROPE, ss_in=ss, ss_in_parts=ss_parts,
+                             norm_eps=eps, qkv=dict(num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=lw["q_norm"],
+                                                    k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin,
+                                                    positions=fb.positions, cache_loc=fb.out_cache_loc,
+                                                    k_cache=kc, v_cache=vc))
             ops.paged_decode_attention(q, kc, vc, page_indptr=fb.page_indptr, page_indices=fb.page_indices,
                                        seq_lens=fb.seq_lens, work_indptr=fb.work_indptr, num_q_heads=hq,
                                        num_kv_heads=hkv, head_dim=D, page_size=cfg.page_size,
                                        pages_per_chunk=fb.pages_per_chunk, work_capacity=fb.work_capacity,
                                        sm_scale=self.scale, out=attn, workspace=self.attn_workspace)
-            ops.linear(attn, lw["o_proj"], epilogue=ops.EPI_RESIDUAL, residual=h, out=h, workspace=ws)
-            ops.rmsnorm(h, lw["post_attention_layernorm"], eps, out=normed)
-            ops.linear(normed, lw["gate_up_proj"], epilogue=ops.EPI_SWIGLU, out=act, workspace=ws)
-            ops.linear(act, lw["down_proj"], epilogue=ops.EPI_RESIDUAL, residual=h, out=h, workspace=ws)
-        hidden = self.hidden[:B]
-        ops.rmsnorm(h, self.w["norm"], eps, out=hidden)
+            ops.linear_fused(attn, lw["o_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=ss)
+            ops.linear_fused(h, self.folded[li]["gate_up"], act, epilogue=ops.EPI_SWIGLU, ss_in=ss, ss_in_parts=parts,
+                             norm_eps=eps)
+            ops.linear_fused(act, lw["down_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=ss)
+            ss_parts = parts
         logits = self.logits[:B]
-        ops.linear(hidden, self.w["codec_head"], epilogue=ops.EPI_F32, out=logits, workspace=ws)
+        ops.linear_fused(h, self.codec_head_folded, logits, epilogue=ops.EPI_F32, ss_in=ss, ss_in_parts=parts,
+                         norm_eps=eps)
         return logits
 
     def sample_decode_tokens(self, logits: torch.Tensor, fb: DecodeForwardBatch) -> torch.Tensor:

@@ -333,3 +333,85 @@ def test_rollback_known_answer(golden):
     assert seq.tolist() == g["seq_lens_after"]
     assert r2t.tolist() == g["req_to_token_after"]
     assert free_head.item() == 9
+
+
+# ---------------------------------------------------------------------------
+# fused projections (folded RMSNorm, qkv epilogue, row sums of squares)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("rows", [1, 64, 128])
+def test_linear_fused_folded_norm_and_sumsq(rows):
+    from omni_b200 import ops
+
+    H, N = 1024, 3072
+    g = torch.Generator(device=DEV).manual_seed(rows)
+    x = (torch.randn(rows, H, device=DEV, generator=g) * 3).to(torch.bfloat16)
+    res = torch.randn(rows, H, device=DEV, generator=g).to(torch.bfloat16)
+    gain = (1 + 0.1 * torch.randn(H, device=DEV, generator=g)).to(torch.bfloat16)
+    w = (torch.randn(N, H, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    wo = (torch.randn(H, N, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    # input row + its sum of squares
+    s = torch.empty_like(x)
+    ss1 = torch.empty(rows, device=DEV)
+    ops.add_sumsq(x, res, s, ss1)
+    ref_s = (x.float() + res.float()).bfloat16()
+    assert torch.equal(s, ref_s)
+    torch.testing.assert_close(ss1, ref_s.float().pow(2).sum(1), rtol=1e-5, atol=1e-3)
+    # folded RMSNorm -> projection
+    y = torch.empty(rows, N, device=DEV, dtype=torch.bfloat16)
+    ops.linear_fused(s, ops.fold_norm(w, gain), y, epilogue=ops.EPI_STORE, ss_in=ss1, ss_in_parts=1, norm_eps=1e-6)
+    ref = ref_rmsnorm(ref_s, gain, 1e-6).bfloat16().float() @ w.float().t()
+    close(y, ref, rel=2e-2, cos_min=0.9995)
+    # residual epilogue emits per-tile sums of squares of its bf16 output
+    a = torch.randn(rows, N, device=DEV, generator=g).to(torch.bfloat16)
+    out = s.clone()
+    ss8 = torch.zeros(H // 128, rows, device=DEV)
+    ops.linear_fused(a, wo, out, epilogue=ops.EPI_RESIDUAL, residual=out, ss_out=ss8)
+    close(out, a.float() @ wo.float().t() + s.float())
+    torch.testing.assert_close(ss8.sum(0), out.float().pow(2).sum(1), rtol=1e-4, atol=1e-2)
+    torch.testing.assert_close(ss8[3], out[:, 384:512].float().pow(2).sum(1), rtol=1e-4, atol=1e-2)
+    # SwiGLU with the folded norm and 8-part sums of squares
+    wgu = (torch.randn(2 * N, H, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    act = torch.empty(rows, N, device=DEV, dtype=torch.bfloat16)
+    ops.linear_fused(out, ops.fold_norm(wgu, gain), act, epilogue=ops.EPI_SWIGLU, ss_in=ss8, ss_in_parts=8,
+                     norm_eps=1e-6)
+    gu = ref_rmsnorm(out, gain, 1e-6).bfloat16().float() @ wgu.float().t()
+    ref_act = torch.nn.functional.silu(gu[:, :N].bfloat16().float()) * gu[:, N:].bfloat16().float()
+    close(act, ref_act, rel=2e-2, cos_min=0.9995)
+
+
+@pytest.mark.parametrize("hq,hkv,d,implicit", [(16, 2, 128, False), (16, 8, 64, True)])
+def test_linear_fused_qkv_rope_store(hq, hkv, d, implicit):
+    from omni_b200 import ops
+
+    rows, H = 12, 1024
+    g = torch.Generator(device=DEV).manual_seed(d)
+    x = (torch.randn(rows, H, device=DEV, generator=g) * 2).to(torch.bfloat16)
+    ss = x.float().pow(2).sum(1).contiguous()
+    gain = (1 + 0.1 * torch.randn(H, device=DEV, generator=g)).to(torch.bfloat16)
+    w = (torch.randn((hq + 2 * hkv) * d, H, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(d, device=DEV, generator=g)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(d, device=DEV, generator=g)).to(torch.bfloat16)
+    if implicit:
+        G1, T, base = 17, 2, 0
+        cos_sin = ops.rope_cos_sin_cache(G1, d, 1e6, DEV)
+        pos = torch.arange(T, device=DEV).repeat(rows // T) + base
+        loc = torch.arange(rows // T, device=DEV).repeat_interleave(T) * G1 + pos
+        slots = (rows // T) * G1
+        geo = dict(tokens_per_req=T, slot_stride=G1, slot_base=base)
+    else:
+        cos_sin = ops.rope_cos_sin_cache(4096, d, 1e6, DEV)
+        pos = torch.randint(0, 4096, (rows,), device=DEV)
+        slots = 256
+        loc = torch.randperm(slots, device=DEV)[:rows]
+        geo = dict(positions=pos, cache_loc=loc)
+    kc = torch.zeros(slots, hkv, d, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    q = torch.empty(rows, hq * d, device=DEV, dtype=torch.bfloat16)
+    ops.linear_fused(x, ops.fold_norm(w, gain), q, epilogue=ops.EPI_QKV_ROPE, ss_in=ss, ss_in_parts=1, norm_eps=1e-6,
+                     qkv=dict(num_q_heads=hq, num_kv_heads=hkv, head_dim=d, q_norm=qn, k_norm=kn, eps=1e-6,
+                              cos_sin=cos_sin, k_cache=kc, v_cache=vc, **geo))
+    qkv_ref = (ref_rmsnorm(x, gain, 1e-6).bfloat16().float() @ w.float().t()).bfloat16()
+    rq, rk, rv = ref_qknorm_rope(qkv_ref, hq, hkv, d, qn, kn, 1e-6, cos_sin, pos)
+    close(q.view(rows, hq, d), rq, rel=3e-2, cos_min=0.999)
+    close(kc[loc], rk, rel=3e-2, cos_min=0.999)
+    close(vc[loc], rv, rel=3e-2, cos_min=0.999)

@@ -115,7 +115,7 @@ def test_decode_step_matches_oracle(dosample):
                                                     forced_codes=codes)
     G = cfg.predictor.num_code_groups
     for j in range(G - 1):
-        lg = p.logits[j, :B]
+        lg = p.codebook_logits(j, B)
         cos, err, scale = cos_err(lg, logits_po[j])
         assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0), (j, cos, err, scale)
         drawn = orc.sample_topk_topp(bits(lg), sub["temperature"], sub["top_k"], sub["top_p"], sub["seed"],
