@@ -14,8 +14,8 @@
 // predictor_attention_kernel — the code predictor's attention over its <= G+1
 //   per-request cache slots (predictor_cached_self_attention,
 //   sglang_model.py:2168-2233; decode_attention_kernel,
-//   predictor_layers.py:336-396): one warp per (row, query head), causal for
-//   the opening pair.
+//   predictor_layers.py:336-396): one warp per (row, KV head) serving the
+//   group's query heads, lanes = slots, causal for the opening pair.
 #include <mutex>
 
 #include "capi_util.h"
@@ -276,14 +276,36 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_attention_kernel
         for (int cc = 0; cc < nchunks; ++cc)
           M = fmaxf(M, __ldcg(p.part_lse + ((int64_t)(w0 + cc) * p.hkv + h) * kGroup + hg));
         float W = 0.0f, acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int cc = 0; cc < nchunks; ++cc) {
-          const int64_t base = ((int64_t)(w0 + cc) * p.hkv + h) * kGroup + hg;
-          const float lse = __ldcg(p.part_lse + base);
-          const float wgt = lse == -INFINITY ? 0.0f : exp2f(lse - M);
-          W += wgt;
-          const float* po = p.part_o + base * kD + d0;
+        // chunks in batches of 4 with every load of a batch in flight before the sums,
+        // summed in chunk order
+        for (int c0 = 0; c0 < nchunks; c0 += 4) {
+          float lse[4];
+          float4 lo[4], hi[4];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] += __ldcg(po + e) * wgt;
+          for (int u = 0; u < 4; ++u) {
+            if (c0 + u < nchunks) {
+              const int64_t base = ((int64_t)(w0 + c0 + u) * p.hkv + h) * kGroup + hg;
+              lse[u] = __ldcg(p.part_lse + base);
+              const float4* po = reinterpret_cast<const float4*>(p.part_o + base * kD + d0);
+              lo[u] = __ldcg(po);
+              hi[u] = __ldcg(po + 1);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (c0 + u < nchunks) {
+              const float wgt = lse[u] == -INFINITY ? 0.0f : exp2f(lse[u] - M);
+              W += wgt;
+              acc[0] += lo[u].x * wgt;
+              acc[1] += lo[u].y * wgt;
+              acc[2] += lo[u].z * wgt;
+              acc[3] += lo[u].w * wgt;
+              acc[4] += hi[u].x * wgt;
+              acc[5] += hi[u].y * wgt;
+              acc[6] += hi[u].z * wgt;
+              acc[7] += hi[u].w * wgt;
+            }
+          }
         }
         const float inv = W > 0.0f ? 1.0f / W : 0.0f;
         uint16_t* dst = p.out + (int64_t)b * p.out_stride + (int64_t)(h * kGroup + hg) * kD + d0;
@@ -299,50 +321,97 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_attention_kernel
 // ---------------------------------------------------------------------------
 // Predictor attention: rows laid out (request, token); a row attends to the
 // request's slots [0, base + t] (t = the row's token index within the request).
+// One warp per (row, KV head) serves the G query heads of the group: lane s
+// scores slot s (<= 32 slots) against every query head of the group, the
+// softmax runs across lanes, then lane l accumulates dimensions
+// [l*D/32, (l+1)*D/32) of P V over the slots.
 // ---------------------------------------------------------------------------
-template <int E>  // head_dim = 32 * E
+template <int E, int G>  // head_dim = 32 * E, G query heads per KV head
 __global__ void __launch_bounds__(128) predictor_attention_kernel(const uint16_t* __restrict__ q, int64_t q_stride,
                                                                   const uint16_t* __restrict__ k_cache,
                                                                   const uint16_t* __restrict__ v_cache, int rows,
                                                                   int hq, int hkv, int tokens_per_req,
                                                                   int slot_stride, int slot_base, float scale,
                                                                   uint16_t* __restrict__ out, int64_t out_stride) {
+  constexpr int D = 32 * E;
+  __shared__ float qs[4][G][D];
   griddep_wait();
   griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int item = blockIdx.x * 4 + warp;
-  if (item >= rows * hq) return;
-  const int row = item / hq, head = item % hq;
+  if (item >= rows * hkv) return;
+  const int row = item / hkv, kvh = item % hkv;
   const int req = row / tokens_per_req, tk = row % tokens_per_req;
-  const int kvh = head / (hq / hkv);
-  constexpr int D = 32 * E;
-  float qv[E], acc[E];
-#pragma unroll
-  for (int j = 0; j < E; ++j) {
-    qv[j] = bf2f(q[row * q_stride + head * D + E * lane + j]) * scale;
-    acc[j] = 0.0f;
-  }
-  float m = -INFINITY, l = 0.0f;
-  const int last = slot_base + tk;
+  const int last = slot_base + tk;  // inclusive
   const int64_t slot0 = (int64_t)req * slot_stride;
-  for (int s = 0; s <= last; ++s) {
-    const int64_t off = ((slot0 + s) * hkv + kvh) * D + E * lane;
-    float d = 0.0f;
+  // the group's query heads, scaled, into this warp's shared slice
 #pragma unroll
-    for (int j = 0; j < E; ++j) d = __fmaf_rn(qv[j], bf2f(k_cache[off + j]), d);
+  for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int o2 = 16; o2 >= 1; o2 >>= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, o2);
-    const float mn = fmaxf(m, d);
-    const float a = expf(m - mn);
-    const float pr = expf(d - mn);
-    l = l * a + pr;
+    for (int j = 0; j < E; ++j)
+      qs[warp][g][E * lane + j] = bf2f(q[row * q_stride + (kvh * G + g) * D + E * lane + j]) * scale;
+  __syncwarp();
+  // scores: lane = slot
+  float sc[G];
+  const bool valid = lane <= last;
+  if (valid) {
+    const uint4* krow = reinterpret_cast<const uint4*>(k_cache + ((slot0 + lane) * hkv + kvh) * D);
 #pragma unroll
-    for (int j = 0; j < E; ++j) acc[j] = acc[j] * a + pr * bf2f(v_cache[off + j]);
-    m = mn;
+    for (int g = 0; g < G; ++g) sc[g] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      const uint4 kv = krow[c];
+      const uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float k0 = bf_lo(w[e]), k1 = bf_hi(w[e]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          sc[g] = __fmaf_rn(qs[warp][g][8 * c + 2 * e], k0, sc[g]);
+          sc[g] = __fmaf_rn(qs[warp][g][8 * c + 2 * e + 1], k1, sc[g]);
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int g = 0; g < G; ++g) sc[g] = -INFINITY;
   }
-  const float inv = 1.0f / l;
+  float pr[G], inv[G];
 #pragma unroll
-  for (int j = 0; j < E; ++j) out[row * out_stride + head * D + E * lane + j] = f2bf(acc[j] * inv);
+  for (int g = 0; g < G; ++g) {
+    const float m = warp_max_xor(sc[g]);
+    pr[g] = valid ? expf(sc[g] - m) : 0.0f;
+    inv[g] = 1.0f / warp_sum_xor(pr[g]);
+  }
+  // P V: lane l owns dimensions E*l .. E*l+E-1
+  float acc[G][E];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < E; ++j) acc[g][j] = 0.0f;
+  for (int s = 0; s <= last; ++s) {
+    const uint16_t* vrow = v_cache + ((slot0 + s) * hkv + kvh) * D + E * lane;
+    float v[E];
+    if constexpr (E == 2) {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(vrow);
+      v[0] = bf_lo(w);
+      v[1] = bf_hi(w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[j] = bf2f(vrow[j]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float ps = __shfl_sync(0xFFFFFFFFu, pr[g], s);
+#pragma unroll
+      for (int j = 0; j < E; ++j) acc[g][j] = __fmaf_rn(ps, v[j], acc[g][j]);
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < E; ++j)
+      out[row * out_stride + (kvh * G + g) * D + E * lane + j] = f2bf(acc[g][j] * inv[g]);
 }
 
 }  // namespace
@@ -422,18 +491,31 @@ extern "C" OMNI_API int omni_predictor_attention(const void* q, int64_t q_stride
     return set_error(OMNI_ERR_INVALID, "bad predictor attention shape");
   if (rows % tokens_per_req != 0) return set_error(OMNI_ERR_INVALID, "rows must be whole requests");
   if (head_dim != 64 && head_dim != 128) return set_error(OMNI_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (slot_base + tokens_per_req > 32) return set_error(OMNI_ERR_UNSUPPORTED, "at most 32 cache slots");
+  const int G = num_q_heads / num_kv_heads;
+  if (G != 1 && G != 2 && G != 4) return set_error(OMNI_ERR_UNSUPPORTED, "1, 2 or 4 query heads per KV head");
+  if ((reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 3))
+    return set_error(OMNI_ERR_UNSUPPORTED, "misaligned caches");
   if (rows == 0) return OMNI_OK;
-  dim3 g((unsigned)((rows * num_q_heads + 3) / 4)), b(128);
+  dim3 g((unsigned)((rows * num_kv_heads + 3) / 4)), b(128);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto Q = static_cast<const uint16_t*>(q);
   auto K = static_cast<const uint16_t*>(k_cache);
   auto V = static_cast<const uint16_t*>(v_cache);
   auto O = static_cast<uint16_t*>(out);
-  if (head_dim == 64)
-    return check_launch(launch(predictor_attention_kernel<2>, g, b, 0, st, Q, q_stride, K, V, (int)rows, num_q_heads,
-                               num_kv_heads, tokens_per_req, slot_stride, slot_base, sm_scale, O, out_stride));
-  return check_launch(launch(predictor_attention_kernel<4>, g, b, 0, st, Q, q_stride, K, V, (int)rows, num_q_heads,
-                             num_kv_heads, tokens_per_req, slot_stride, slot_base, sm_scale, O, out_stride));
+#define OMNI_PA(EE, GG)                                                                                        \
+  return check_launch(launch(predictor_attention_kernel<EE, GG>, g, b, 0, st, Q, q_stride, K, V, (int)rows,     \
+                             num_q_heads, num_kv_heads, tokens_per_req, slot_stride, slot_base, sm_scale, O,    \
+                             out_stride))
+  if (head_dim == 64) {
+    if (G == 1) OMNI_PA(2, 1);
+    if (G == 2) OMNI_PA(2, 2);
+    OMNI_PA(2, 4);
+  }
+  if (G == 1) OMNI_PA(4, 1);
+  if (G == 2) OMNI_PA(4, 2);
+  OMNI_PA(4, 4);
+#undef OMNI_PA
 }
 
 // ---------------------------------------------------------------------------

@@ -274,6 +274,33 @@ OMNI_DEVINL void smem_bitonic_desc(unsigned long long* keys, int n) {
   }
 }
 
+// Descending bitonic sort of 64 keys held two per lane (element 2 lane + j),
+// entirely in registers; lane l ends with ranks 2l and 2l + 1.
+OMNI_DEVINL void warp_sort64_desc(unsigned long long& a0, unsigned long long& a1) {
+  const int lane = threadIdx.x & 31;
+  const int i0 = 2 * lane;
+#pragma unroll
+  for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const bool desc = (i0 & size) == 0;
+      if (stride == 1) {
+        if ((a0 < a1) == desc) {
+          const unsigned long long t = a0;
+          a0 = a1;
+          a1 = t;
+        }
+      } else {
+        const unsigned long long o0 = __shfl_xor_sync(0xFFFFFFFFu, a0, stride >> 1);
+        const unsigned long long o1 = __shfl_xor_sync(0xFFFFFFFFu, a1, stride >> 1);
+        const bool take_max = ((i0 & stride) == 0) == desc;
+        a0 = take_max ? (a0 > o0 ? a0 : o0) : (a0 < o0 ? a0 : o0);
+        a1 = take_max ? (a1 > o1 ? a1 : o1) : (a1 < o1 ? a1 : o1);
+      }
+    }
+  }
+}
+
 // torch.topk's 32-entry descending bitonic network over the gathered
 // candidates, one entry per lane (sampling_kernels.py:123-312).
 OMNI_DEVINL void warp_bitonic32_torch(float& sc, uint32_t& id, int max_top_k) {
@@ -564,13 +591,17 @@ __global__ void __launch_bounds__(kThreads) residual_sample_kernel(const __grid_
       if (pos >= 0 && pos < limit) sm.keys[pos] = key;
     }
     __syncthreads();
-    if (!small) smem_bitonic_desc(sm.keys, p.block_k);
+    if (!small && C != 2) smem_bitonic_desc(sm.keys, p.block_k);
     if (warp == 0) {
       float sc[C];
       uint32_t id[C];
+      unsigned long long kk[C];
+#pragma unroll
+      for (int j = 0; j < C; ++j) kk[j] = sm.keys[lane * C + j];
+      if constexpr (C == 2) warp_sort64_desc(kk[0], kk[1]);
 #pragma unroll
       for (int j = 0; j < C; ++j) {
-        const unsigned long long key = sm.keys[lane * C + j];
+        const unsigned long long key = kk[j];
         sc[j] = unordered_float((uint32_t)(key >> 32));
         id[j] = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu);
       }
@@ -767,14 +798,18 @@ __global__ void __launch_bounds__(kThreads) layer0_sample_kernel(const __grid_co
     if (pos >= 0 && pos < p.block_k) sm.keys[pos] = key;
   }
   __syncthreads();
-  smem_bitonic_desc(sm.keys, p.block_k);
+  if (C != 2) smem_bitonic_desc(sm.keys, p.block_k);
   if (warp == 0) {
     float pr[C], q[C];
     uint32_t id[C];
     float acc = 0.0f;
+    unsigned long long kk[C];
+#pragma unroll
+    for (int j = 0; j < C; ++j) kk[j] = sm.keys[lane * C + j];
+    if constexpr (C == 2) warp_sort64_desc(kk[0], kk[1]);
 #pragma unroll
     for (int j = 0; j < C; ++j) {
-      const unsigned long long key = sm.keys[lane * C + j];
+      const unsigned long long key = kk[j];
       const float sc = unordered_float((uint32_t)(key >> 32));
       id[j] = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu);
       pr[j] = __fdiv_rn(det_expf(__fsub_rn(sc, mx)), z);

@@ -47,7 +47,7 @@ class GenerationBatchResult:
 
 class TalkerDecodeRunner:
     def __init__(self, cfg: TalkerConfig, *, max_batch: int, num_pages: int, seed: int = 0, device="cuda",
-                 pages_per_chunk: int = 8, weights: dict | None = None, predictor_weights: dict | None = None):
+                 pages_per_chunk: int = 16, weights: dict | None = None, predictor_weights: dict | None = None):
         if cfg.moe is not None:
             raise NotImplementedError("the MoE talker runs through MoETalkerDecodeRunner")
         self.cfg = cfg

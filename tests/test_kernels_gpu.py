@@ -230,11 +230,12 @@ def test_paged_decode_attention(lens, ppc):
             close(out[b].cpu(), ref, rel=2e-2, cos_min=0.999)
 
 
+@pytest.mark.parametrize("hq,hkv,d", [(16, 8, 64), (8, 8, 128), (16, 4, 128)])
 @pytest.mark.parametrize("tokens,base", [(2, 0), (1, 5), (1, 15)])
-def test_predictor_attention(tokens, base):
+def test_predictor_attention(tokens, base, hq, hkv, d):
     from omni_b200 import ops
 
-    hq, hkv, d, G1, B = 16, 8, 64, 17, 6
+    G1, B = 17, 6
     rows = B * tokens
     q = torch.randn(rows, hq * d, device=DEV).to(torch.bfloat16)
     kc = torch.randn(B * G1, hkv, d, device=DEV).to(torch.bfloat16)

@@ -7,7 +7,8 @@ the GPU against the CPU oracle.
 - every drawn token (layer 0 and 15 residual codebooks): bit-exact against the
   oracle sampler applied to the device's own logits;
 - predictor lm_head logits with the device's codes fed back (teacher forcing):
-  bf16 tolerance; summed codec embeddings: bit-exact;
+  bf16 tolerance plus one bf16 ulp of output rounding (they are stored in bf16);
+  summed codec embeddings: bit-exact;
 - CUDA-graph replay == eager, bit for bit; rows never mix (batch invariance).
 """
 
@@ -117,7 +118,10 @@ def test_decode_step_matches_oracle(dosample):
     for j in range(G - 1):
         lg = p.codebook_logits(j, B)
         cos, err, scale = cos_err(lg, logits_po[j])
-        assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0), (j, cos, err, scale)
+        # these logits are stored in bf16: on top of the 2e-2 tolerance, one rounding
+        # of the output may land on the neighbouring bf16 value (one ulp at the scale)
+        ulp = 2.0 ** (np.floor(np.log2(max(scale, 1.0))) - 7)
+        assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0) + ulp, (j, cos, err, scale)
         drawn = orc.sample_topk_topp(bits(lg), sub["temperature"], sub["top_k"], sub["top_p"], sub["seed"],
                                      pos * (G - 1) + (j + 1), max_top_k=sub["max_top_k"], has_top_p=sub["has_top_p"])
         am = np.argmax(lg.float().cpu().numpy(), axis=1)
