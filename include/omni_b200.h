@@ -163,7 +163,8 @@ OMNI_API int64_t omni_linear_workspace_bytes(int64_t rows, int64_t k, int64_t n,
  * talker.py:216-247, sglang_model.py:1294-1302, 2101-2152).
  *   x, w, residual bf16; y bf16 (f32 for OMNI_EPI_F32); K % 64 == 0, N % 128 == 0.
  *   splits: K-splits per 128-feature tile (one thread-block cluster each),
- *   0 = chosen by the library so that one wave covers the GPU, else 1..16.
+ *   0 = chosen by the library so that one wave covers the GPU, else 1..16
+ *   (narrowed when the split partials of a wide row tile exceed shared memory).
  *   workspace / workspace_bytes: unused (may be NULL / 0). */
 OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n,
                          int32_t epilogue, const void* residual, int64_t residual_stride, void* y, int64_t y_stride,

@@ -9,20 +9,27 @@
 // swizzle) stream from HBM through a TMA pipeline; X tiles come from L2.
 //
 // Split-K: the S CTAs that share a feature tile form one thread-block cluster
-// (S <= 16, chosen so that every cluster of the grid is co-resident).  Each
-// CTA stages its fp32 partial tile in its own shared memory; after a hardware
-// cluster barrier, CTA c reduces the c-th contiguous block of the tile's rows
-// by reading the S partials over distributed shared memory in split order
-// (deterministic), applies the epilogue and stores.  The epilogue operands of
-// the owned rows (RMSNorm scale, rotary position, KV slot, residual) are
-// fetched while the MMAs run.  No global scratch memory.
+// (S <= 16, chosen so that every cluster of the grid is co-resident).  CTA c
+// owns the c-th contiguous block of the tile's rows.  Each CTA stages its fp32
+// partial tile in its own shared memory and sends every owner that owner's
+// block of rows with one bulk shared-to-shared copy into the owner's drained
+// pipeline buffers (completion on the owner's mbarrier); the owner sums the S
+// blocks in split order (deterministic), applies the epilogue and stores.  Two
+// split-phase cluster barriers order this: "buffers drained" (arrive before the
+// staging, wait before sending) and "all blocks received" (arrive before the
+// epilogue, wait before exit, so no CTA leaves while its partial is still being
+// copied).  The epilogue operands of the owned rows (RMSNorm scale, rotary
+// position, KV slot, residual) are fetched while the MMAs run.  No global
+// scratch memory.
 //
 // Programmatic dependent launch: weights never depend on the previous kernel,
 // so the producer issues the first stages' weight loads before
 // griddepcontrol.wait, overlapping them with the predecessor's tail.
 //
-// Roles (128 threads): warp 0 lane 0 = TMA producer, warp 1 lane 0 = MMA
-// issuer, all four warps = epilogue (warp w reads TMEM lanes 32w..32w+31).
+// Roles (256 threads): warp 0 lane 0 = TMA producer, warp 1 lane 0 = MMA
+// issuer, warps 2-7 = epilogue operands during the main loop; all eight warps
+// drain TMEM (warp w reads lanes 32 (w % 4) .. + 31, column half w / 4) and run
+// the epilogue.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -39,7 +46,7 @@ constexpr int kBK = 64;        // K elements per stage (one 128-byte swizzle row
 constexpr int kTileN = 128;    // output features per CTA (MMA M)
 constexpr int kMaxRows = 256;  // activation rows per CTA (MMA N)
 constexpr int kMaxStages = 6;
-constexpr int kThreadsG = 128;
+constexpr int kThreadsG = 256;
 constexpr int kMaxSplits = 16;
 
 enum Epilogue : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiF32 = 3, kEpiQKV = 4 };
@@ -53,6 +60,7 @@ struct GemmParams {
   int splits;       // CTAs per (feature tile, row tile)
   int stages;       // pipeline depth
   int tmem_cols;    // power of two >= row_tile
+  int region;       // bytes of the pipeline / partial-tile region (1024-aligned)
   int swiglu_half;  // I for SwiGLU (gate rows [0, I), up rows [I, 2I))
   const uint16_t* residual;
   int64_t res_stride;
@@ -86,22 +94,25 @@ OMNI_DEVINL uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-OMNI_DEVINL void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+OMNI_DEVINL void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+OMNI_DEVINL void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Generic-proxy shared-memory writes of this thread made visible to the bulk-copy engine.
+OMNI_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory to a peer's
+// (both addresses 16-byte aligned); completes `bytes` of transactions on the
+// peer's mbarrier.
+OMNI_DEVINL void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
+      : "memory");
 }
 // Address of the same shared-memory offset in CTA `rank` of the cluster.
 OMNI_DEVINL uint32_t map_cluster(uint32_t local, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
   return r;
-}
-// Reads of peers' partial tiles between two cluster barriers (which order them).
-OMNI_DEVINL float4 ld_cluster_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr));
-  return v;
 }
 
 OMNI_DEVINL float silu(float g) { return g / (1.0f + expf(-g)); }
@@ -135,17 +146,20 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   const int rows_here = min(Rt, p.rows - row0);
   const uint32_t crank = S > 1 ? cluster_ctarank() : 0u;
   const RowBlock mine = row_block(rows_here, S, (int)crank);
-  // shared memory: [stages A][stages B][row info][barriers]; the fp32 partial tile
-  // [rows][128] is staged over the drained stage buffers after the main loop
+  // shared memory: region [stages A][stages B], then [row info][barriers].  After
+  // the main loop the region holds this CTA's fp32 partial tile [rows][128] and,
+  // behind it, the S-1 peers' partials of the owned rows [S-1][per][128].
   uint8_t* a_smem = smem;
   uint8_t* b_smem = smem + ST * a_bytes;
-  float* row_info = reinterpret_cast<float*>(b_smem + ST * b_bytes);  // [per] rstd, [per] position, [per] slot
+  float* row_info = reinterpret_cast<float*>(smem + p.region);  // [per] rstd, [per] position, [per] slot
   uint64_t* full = reinterpret_cast<uint64_t*>(row_info + 3 * ((mine.per + 1) & ~1));
   uint64_t* empty = full + kMaxStages;
   uint64_t* mma_done = empty + kMaxStages;
+  uint64_t* recv_bar = mma_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 2);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort
   float* stage = reinterpret_cast<float*>(smem);
+  float* recv = stage + Rt * kTileN;
 
   const int kb_begin = (int)(((int64_t)p.num_kb * split) / S);
   const int kb_end = (int)(((int64_t)p.num_kb * (split + 1)) / S);
@@ -157,8 +171,11 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(mma_done, 1);
+    mbar_init(recv_bar, 1);
     flags[0] = 0;
     fence_barrier_init();
+    // the owned rows arrive from the S-1 peers (no phase to wait for when S == 1)
+    mbar_arrive_expect_tx(recv_bar, (uint32_t)((S - 1) * mine.count * kTileN * 4));
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
   }
@@ -268,7 +285,9 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   }
   tc_fence_after();
   __syncthreads();
-  const bool aborted = flags[0] != 0;
+  // the pipeline buffers are drained: peers may write this CTA's rows into them
+  if (S > 1) cluster_arrive();
+  bool aborted = flags[0] != 0;
   // the residual rows this thread will add, fetched ahead of the reduction
   constexpr int kPre = 4;
   uint2 res_pre[kPre];
@@ -283,41 +302,67 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     }
   }
   if (!aborted) {
-    const int f = warp * 32 + lane;
-    for (int c0 = 0; c0 < rows_here; c0 += 32) {
-      uint32_t r[32];
+    // warp w: TMEM lanes (features) 32 (w % 4) .., 32-column chunks w / 4, w / 4 + 2, ...
+    const int f = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    for (int c0 = (warp >> 2) * 32; c0 < rows_here; c0 += 128) {
+      // two 32-column loads in flight per wait
+      uint32_t r0[32], r1[32];
       if (have_acc) {
-        tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+        tmem_ld_32x32b_x32(lane_base + (uint32_t)c0, r0);
+        if (c0 + 64 < rows_here) tmem_ld_32x32b_x32(lane_base + (uint32_t)(c0 + 64), r1);
         tc_wait_ld();
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = 0u;
+        for (int j = 0; j < 32; ++j) r0[j] = r1[j] = 0u;
       }
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (c0 + j < rows_here) stage[(c0 + j) * kTileN + f] = __uint_as_float(r[j]);
+        if (c0 + j < rows_here) stage[(c0 + j) * kTileN + f] = __uint_as_float(r0[j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + 64 + j < rows_here) stage[(c0 + 64 + j) * kTileN + f] = __uint_as_float(r1[j]);
     }
   }
   tc_fence_before();
+  fence_proxy_async_smem();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
-  // Every CTA takes part in both cluster barriers, aborted or not.
-  if (S > 1) cluster_sync();  // all partial tiles staged and visible cluster-wide
-  if (aborted) {
-    if (S > 1) cluster_sync();
-    return;
+  if (S > 1) {
+    cluster_wait();  // every peer's buffers are drained and its barriers initialised
+    if (threadIdx.x == 0) {
+      // each owner gets its block of this partial, into slot (split index, skipping its own)
+      for (int q = 0; q < S; ++q) {
+        if (q == (int)crank) continue;
+        const RowBlock ob = row_block(rows_here, S, q);
+        if (ob.count == 0) continue;
+        const int slot = (int)crank < q ? (int)crank : (int)crank - 1;
+        const uint32_t dst = smem_u32(recv + (size_t)slot * ob.per * kTileN);
+        bulk_copy_to_peer(map_cluster(dst, (uint32_t)q), smem_u32(stage + (size_t)ob.begin * kTileN),
+                          (uint32_t)(ob.count * kTileN * 4), map_cluster(smem_u32(recv_bar), (uint32_t)q));
+      }
+    }
+    if (!mbar_wait(recv_bar, 0)) {
+      report_status(kDevTimeoutTma);
+      flags[0] = 1;
+    }
+    __syncthreads();
+    aborted = flags[0] != 0;
+    cluster_arrive();  // this CTA's rows are in; its copies out are complete once every owner arrives
   }
 
-  // ---- reduce the owned rows over the cluster, in split order, and apply the epilogue ----
-  const uint32_t stage_local = smem_u32(stage);
+  // ---- sum the owned rows' partials in split order and apply the epilogue ----
+  const float4* own4 = reinterpret_cast<const float4*>(stage);
+  const float4* recv4 = reinterpret_cast<const float4*>(recv);
   auto acc4 = [&](int i, int f) -> float4 {
     const int r = mine.begin + i;
-    if (S == 1) return *reinterpret_cast<const float4*>(stage + r * kTileN + f);
-    const uint32_t off = stage_local + (uint32_t)((r * kTileN + f) * 4);
     float4 v[kMaxSplits];
 #pragma unroll
     for (int q = 0; q < kMaxSplits; ++q)
-      if (q < S) v[q] = ld_cluster_f4(map_cluster(off, (uint32_t)q));
+      if (q < S) {
+        const int c = (int)crank;
+        v[q] = q == c ? own4[(r * kTileN + f) >> 2] : recv4[(((q < c ? q : q - 1) * mine.per + i) * kTileN + f) >> 2];
+      }
     float4 a = v[0];
 #pragma unroll
     for (int q = 1; q < kMaxSplits; ++q)
@@ -329,10 +374,11 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       }
     return a;
   };
+  const int items = aborted ? 0 : mine.count;
   if (EPI == kEpiSwiGLU) {
     // features 0..63: gate, 64..127: up, for outputs tile*64 .. tile*64+63
     uint16_t* Y = static_cast<uint16_t*>(p.y);
-    for (int idx = threadIdx.x; idx < mine.count * 16; idx += kThreadsG) {
+    for (int idx = threadIdx.x; idx < items * 16; idx += kThreadsG) {
       const int i = idx >> 4;
       const int g = (idx & 15) * 4;
       const float sc = row_info[i];
@@ -344,11 +390,28 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       *reinterpret_cast<uint2*>(Y + (int64_t)(row0 + mine.begin + i) * p.y_stride + tile * 64 + g) =
           make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
     }
-    if (S > 1) cluster_sync();  // no CTA leaves while a peer still reads its partial
+    if (S > 1) cluster_wait();
     return;
   }
-  // one warp per owned row, lane l holds features 4l..4l+3
-  for (int idx = threadIdx.x, u = 0; idx < mine.count * 32; idx += kThreadsG, ++u) {
+  // one warp per owned row, lane l holds features 4l..4l+3; kPre rows per thread per
+  // round, their residuals loaded together (the first round's ahead of the reduction)
+  for (int base = 0; base < items * 32; base += kThreadsG * kPre) {
+  uint2 rv[kPre];
+  if (EPI == kEpiResidual) {
+#pragma unroll
+    for (int u = 0; u < kPre; ++u) {
+      const int idx = base + threadIdx.x + u * kThreadsG;
+      if (idx < items * 32)
+        rv[u] = base == 0 ? res_pre[u]
+                          : *reinterpret_cast<const uint2*>(p.residual + (int64_t)(row0 + mine.begin + (idx >> 5)) *
+                                                                             p.res_stride +
+                                                            (int64_t)tile * kTileN + (idx & 31) * 4);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kPre; ++u) {
+    const int idx = base + threadIdx.x + u * kThreadsG;
+    if (idx >= items * 32) break;  // warp-uniform: items * 32 is a multiple of 32
     const int i = idx >> 5;
     const int ln = idx & 31;
     const int f = ln * 4;
@@ -409,12 +472,10 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       }
     } else {
       if (EPI == kEpiResidual) {
-        const uint2 rv = u < kPre ? res_pre[u]
-                                  : *reinterpret_cast<const uint2*>(p.residual + grow * p.res_stride + col);
-        o[0] += bf_lo(rv.x);
-        o[1] += bf_hi(rv.x);
-        o[2] += bf_lo(rv.y);
-        o[3] += bf_hi(rv.y);
+        o[0] += bf_lo(rv[u].x);
+        o[1] += bf_hi(rv[u].x);
+        o[2] += bf_lo(rv[u].y);
+        o[3] += bf_hi(rv[u].y);
       }
       uint16_t* Y = static_cast<uint16_t*>(p.y);
       const uint2 packed = make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
@@ -430,7 +491,8 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       }
     }
   }
-  if (S > 1) cluster_sync();  // no CTA leaves while a peer still reads its partial
+  }
+  if (S > 1) cluster_wait();  // every owner has its rows: no copy still reads this CTA's partial
 }
 
 // ---------------------------------------------------------------------------
@@ -464,7 +526,7 @@ bool make_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int
 }
 
 struct Plan {
-  int row_tile, num_rt, tiles, num_kb, splits, stages, tmem_cols;
+  int row_tile, num_rt, tiles, num_kb, splits, stages, tmem_cols, region;
   size_t smem;
 };
 
@@ -523,23 +585,27 @@ int max_active_clusters(int S, size_t smem) {
   return n;
 }
 
-size_t plan_smem(int row_tile, int stages, int splits) {
+// Bytes of the region that holds the pipeline stages during the main loop and,
+// after it, the partial tile [row_tile][128] fp32 plus the peers' partials of
+// the owned rows [splits - 1][per][128] fp32.
+size_t plan_region(int row_tile, int stages, int splits) {
   const size_t stage_bytes = (size_t)kTileN * kBK * 2 + (size_t)row_tile * kBK * 2;
   const int per = (row_tile + splits - 1) / splits;
+  const size_t partials = (size_t)row_tile * kTileN * 4 + (size_t)(splits - 1) * per * kTileN * 4;
+  const size_t r = (size_t)stages * stage_bytes > partials ? (size_t)stages * stage_bytes : partials;
+  return (r + 1023) & ~(size_t)1023;
+}
+
+size_t plan_smem(int row_tile, int stages, int splits) {
+  const int per = (row_tile + splits - 1) / splits;
   const size_t info = (size_t)3 * ((per + 1) & ~1) * 4;
-  return 1024 + (size_t)stages * stage_bytes + info + (2 * kMaxStages + 2) * 8 + 16;
+  return 1024 + plan_region(row_tile, stages, splits) + info + (2 * kMaxStages + 2) * 8 + 16;
 }
 
 int plan_stages(int row_tile, int kb_per, int splits) {
-  const size_t stage_bytes = (size_t)kTileN * kBK * 2 + (size_t)row_tile * kBK * 2;
   int st = kb_per < 4 ? kb_per : 4;
   if (st < 1) st = 1;
-  // the partial tile [row_tile][128] fp32 is staged over the stage buffers
-  const size_t staging = (size_t)row_tile * kTileN * 4;
-  while ((size_t)st * stage_bytes < staging && st < kMaxStages) ++st;
-  while (st > 1 && plan_smem(row_tile, st, splits) > 227 * 1024 &&
-         (size_t)(st - 1) * stage_bytes >= staging)
-    --st;
+  while (st > 1 && plan_smem(row_tile, st, splits) > 227 * 1024) --st;
   return st;
 }
 
@@ -560,7 +626,11 @@ Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
   const int clusters = pl.tiles * pl.num_rt;
   int best = 1;
   if (splits_req > 0) {
+    // the requested split, narrowed until the partials fit in shared memory
     best = splits_req;
+    while (best > 1 && plan_smem(pl.row_tile, plan_stages(pl.row_tile, (pl.num_kb + best - 1) / best, best), best) >
+                           227 * 1024)
+      --best;
   } else {
     // the widest split whose clusters all fit in one wave, preferring more busy SMs
     long best_busy = 0;
@@ -585,6 +655,7 @@ Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
   while (tc < pl.row_tile) tc <<= 1;
   pl.tmem_cols = tc;
   pl.smem = plan_smem(pl.row_tile, pl.stages, best);
+  pl.region = (int)plan_region(pl.row_tile, pl.stages, best);
   return pl;
 }
 
@@ -606,6 +677,7 @@ int launch_gemm(const void* x, int64_t rows, int64_t k, int64_t x_stride, const 
   gp.splits = pl.splits;
   gp.stages = pl.stages;
   gp.tmem_cols = pl.tmem_cols;
+  gp.region = pl.region;
   gp.swiglu_half = (int)(n / 2);
   set_kernel_attrs<EPI>();
   cudaLaunchConfig_t cfg = {};
@@ -681,7 +753,7 @@ using namespace omni;
 extern "C" OMNI_API int64_t omni_linear_workspace_bytes(int64_t rows, int64_t k, int64_t n, int32_t epilogue,
                                                         int32_t splits) {
   (void)rows, (void)k, (void)n, (void)epilogue, (void)splits;
-  return 0;  // split-K partials are reduced in distributed shared memory
+  return 0;  // split-K partials are reduced in the cluster's shared memory
 }
 
 extern "C" OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w,
