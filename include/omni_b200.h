@@ -171,6 +171,7 @@ OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_strid
                          void* workspace, int64_t workspace_bytes, int32_t splits, void* stream);
 
 #define OMNI_EPI_QKV_ROPE 4 /* qkv projection + per-head RMSNorm + neox RoPE + KV store */
+#define OMNI_EPI_ROUTER 5   /* MoE router: bf16 logits + softmax, top-k, renormalise   */
 
 /* Arguments of omni_linear_fused (unused fields zero).  Replaces, in one launch,
  * the chain RMSNorm -> linear [-> residual add] of the decoder layers
@@ -215,6 +216,13 @@ typedef struct OmniLinearArgs {
   int32_t tokens_per_req, slot_stride, slot_base;
   void* k_cache;
   void* v_cache;
+  /* OMNI_EPI_ROUTER (N = 128 experts): y receives the bf16 router logits;
+   * topk_ids [rows, top_k] int32 and topk_weights [rows, top_k] f32 the
+   * experts by (softmax prob desc, index asc) and their renormalised probs
+   * (TopK with renormalize, thinker_model.py:428-433, fused_topk). */
+  int32_t* topk_ids;
+  float* topk_weights;
+  int32_t top_k;
 } OmniLinearArgs;
 
 OMNI_API int omni_linear_fused(const OmniLinearArgs* args, void* stream);
@@ -328,6 +336,63 @@ OMNI_API int omni_decode_rollback(int64_t rows, int64_t* seq_lens, const int64_t
                                   int32_t* req_to_token, int64_t max_ctx, int32_t page_size,
                                   const int64_t* out_cache_loc, int64_t* free_head, int64_t* freed_slots,
                                   int64_t* num_freed, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * MoE block (a9): Qwen3OmniMoeTalkerSparseMoeBlock.forward (talker.py:325-351)
+ * over Qwen3OmniMoeThinkerTextSparseMoeBlock (thinker_model.py:405-470) with
+ * block-FP8 experts (quantization.py:124-167).  The router is omni_linear_fused
+ * with OMNI_EPI_ROUTER (gate + TopK(renormalize), thinker_model.py:428-433).
+ * ------------------------------------------------------------------------- */
+
+/* post_attention_layernorm (decoder layer, thinker_model.py) followed by
+ * per_token_group_quant_fp8 (group 128) of its output, as FusedMoE's block-FP8
+ * path does on entry: x = bf16(h * rsqrt(sum_p ss[p][row] / hidden + eps) *
+ * gain); xq e4m3 [rows, hidden]; xs [rows, hidden / 128] f32 with
+ * scale = max(amax, 1e-10) / 448.  hidden % 1024 == 0. */
+OMNI_API int omni_moe_rmsnorm_quant(const void* h, int64_t h_stride, const float* ss, int32_t ss_parts,
+                                    int64_t ss_stride, const void* gain, float eps, int64_t rows, int32_t hidden,
+                                    void* x, int64_t x_stride, void* xq, float* xs, void* stream);
+
+/* Work-list capacity (chunks of <= 64 rows) for tokens x top_k pairs. */
+OMNI_API int64_t omni_moe_chunk_capacity(int64_t tokens, int32_t top_k, int32_t experts);
+
+/* moe_align_block_size + the activation permute of FusedMoE: pairs (t, k)
+ * sorted by expert, stable by token; slot_of [tokens, top_k] = row of the pair
+ * in the sorted order; expert_offsets [experts + 1]; chunks int4 {expert,
+ * first row, rows, 0} [chunk_capacity] and *n_chunks; permuted_q / permuted_s
+ * receive the pairs' e4m3 rows and scales.  tokens <= 1024, top_k <= 8,
+ * experts <= 256. */
+OMNI_API int omni_moe_align_gather(const int32_t* topk_ids, int64_t tokens, int32_t top_k, int32_t experts,
+                                   const void* xq, const float* xs, int32_t hidden, void* permuted_q,
+                                   float* permuted_s, int32_t* slot_of, int32_t* expert_offsets, void* chunks,
+                                   int64_t chunk_capacity, int32_t* n_chunks, void* stream);
+
+/* FusedMoE w13 GEMM + SiluAndMul + per_token_group_quant_fp8 of the
+ * activation, per sorted row: w13 e4m3 [experts][2 inter][hidden] (gate rows
+ * then up rows), w13_scale f32 [experts][2 inter / 128][hidden / 128];
+ * act_q e4m3 [rows_cap, inter], act_s f32 [rows_cap, inter / 128].
+ * hidden <= 1024, both multiples of 128. */
+OMNI_API int omni_moe_gate_up_fp8(const void* permuted_q, const float* permuted_s, int64_t rows_cap, int32_t hidden,
+                                  const void* w13, const float* w13_scale, int32_t experts, int32_t inter,
+                                  const void* chunks, const int32_t* n_chunks, void* act_q, float* act_s,
+                                  void* stream);
+
+/* FusedMoE w2 GEMM per sorted row: w2 e4m3 [experts][hidden][inter],
+ * w2_scale f32 [experts][hidden / 128][inter / 128]; y bf16 [rows_cap, hidden]. */
+OMNI_API int omni_moe_down_fp8(const void* act_q, const float* act_s, int64_t rows_cap, int32_t inter,
+                               const void* w2, const float* w2_scale, int32_t experts, int32_t hidden,
+                               const void* chunks, const int32_t* n_chunks, void* y, int64_t y_stride,
+                               void* stream);
+
+/* moe_sum of the routed outputs + the gated shared expert (talker.py:341-350)
+ * + the decoder layer's residual add: h = bf16(h + bf16(bf16(sum_k w_k y[slot])
+ * + bf16(shared * sigmoid(bf16(x . shared_gate_weight))))); ss_out
+ * [hidden / 128, rows] (stride ss_stride) the new rows' per-128-feature sums
+ * of squares (nullable). */
+OMNI_API int omni_moe_combine(const void* y, int64_t y_stride, const int32_t* slot_of, const float* topk_weights,
+                              int32_t top_k, const void* x, int64_t x_stride, const void* shared_gate_weight,
+                              const void* shared_out, int64_t shared_stride, void* h, int64_t h_stride,
+                              float* ss_out, int64_t ss_stride, int64_t rows, int32_t hidden, void* stream);
 
 #ifdef __cplusplus
 }

@@ -7,6 +7,11 @@ rotary and attention; the residual stream), following:
 - talker layer: Qwen3OmniMoeThinkerTextAttention + dense MLP
   (sglang_omni/models/qwen3_omni/components/thinker_model.py:152-402,
   talker.py:216-247), decode forward talker.py:438-491;
+- MoE layer (moe_block): router gate + TopK(renormalize) + block-FP8 FusedMoE +
+  sigmoid-gated shared expert (talker.py:325-351, thinker_model.py:405-470,
+  quantization.py:124-167), with the routing and the e4m3 quantisation done by
+  omni_oracle.c (orc_moe_route, orc_quant_fp8_group) and the expert GEMMs in
+  fp32 on the dequantised operands;
 - paged GQA decode attention over req_to_token slots (RadixAttention decode,
   thinker_model.py:373-379), softmax in fp32;
 - layer-0 draw: omni_oracle.c orc_layer0_sample (talker.py:1376-1412);
@@ -54,11 +59,59 @@ def rope_neox(x: torch.Tensor, cs: torch.Tensor) -> torch.Tensor:
 
 
 def to_f32(weights) -> dict | list | torch.Tensor:
+    """fp32 CPU copies; e4m3 codes (uint8) and their scales are copied unchanged."""
     if isinstance(weights, dict):
         return {k: to_f32(v) for k, v in weights.items()}
     if isinstance(weights, list):
         return [to_f32(v) for v in weights]
+    if weights.dtype == torch.uint8:
+        return weights.detach().cpu()
     return weights.detach().float().cpu()
+
+
+def dequant_rows(q: np.ndarray, scales: np.ndarray, group: int = 128) -> torch.Tensor:
+    """e4m3 codes [rows, cols] with per-row group scales [rows, cols / group] -> fp32."""
+    v = orc.e4m3_to_f32(q)
+    return torch.from_numpy(v * np.repeat(scales, group, axis=1))
+
+
+def dequant_expert(q: torch.Tensor, scale: torch.Tensor, block: int = 128) -> torch.Tensor:
+    """One expert's e4m3 weight [R, C] with its 128x128 block scales [R/128, C/128] -> fp32."""
+    v = torch.from_numpy(orc.e4m3_to_f32(q.numpy()))
+    s = scale.repeat_interleave(block, 0).repeat_interleave(block, 1)
+    return v * s
+
+
+def moe_block(x: torch.Tensor, w: dict, top_k: int):
+    """MoE block output (bf16-rounded fp32 [B, H]) for the normed rows x, plus the
+    router logits (bf16-rounded), top-k ids and weights."""
+    B, H = x.shape
+    logits = rb(x @ w["gate"].t())
+    ids, tw = orc.moe_route(logits.numpy(), top_k)
+    xq, xs = orc.quant_fp8_group(x.numpy())
+    xd = dequant_rows(xq, xs)
+    I = w["w13"].shape[1] // 2
+    y = torch.zeros(B, top_k, H)
+    for e in np.unique(ids):
+        tok, slot = np.nonzero(ids == e)
+        w13 = dequant_expert(w["w13"][e], w["w13_scale"][e])
+        w2 = dequant_expert(w["w2"][e], w["w2_scale"][e])
+        gu = xd[tok] @ w13.t()
+        a = rb(torch.nn.functional.silu(rb(gu[:, :I])) * rb(gu[:, I:]))
+        aq, as_ = orc.quant_fp8_group(a.numpy())
+        y[tok, slot] = rb(dequant_rows(aq, as_) @ w2.t())
+    routed = torch.zeros(B, H)
+    twt = torch.from_numpy(tw)
+    for kk in range(top_k):
+        routed = routed + twt[:, kk: kk + 1] * y[:, kk]
+    routed = rb(routed)
+    sg = rb(x @ w["shared_expert_gate"].t())
+    gus = x @ w["shared_gate_up"].t()
+    Is = gus.shape[1] // 2
+    sa = rb(torch.nn.functional.silu(rb(gus[:, :Is])) * rb(gus[:, Is:]))
+    so = rb(sa @ w["shared_down"].t())
+    shared = rb(so * torch.sigmoid(sg))
+    return rb(routed + shared), logits, ids, tw
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
@@ -113,6 +166,10 @@ class OracleTalker:
             att = rb(att.reshape(B, hq * D))
             x = rb(x + att @ lw["o_proj"].t())
             n = rb(rmsnorm(x, lw["post_attention_layernorm"], eps))
+            if "moe" in lw:
+                out, _, _, _ = moe_block(n, lw["moe"], cfg.moe.num_experts_per_tok)
+                x = rb(x + out)
+                continue
             gu = n @ lw["gate_up_proj"].t()
             I = gu.shape[1] // 2
             a = rb(torch.nn.functional.silu(rb(gu[:, :I])) * rb(gu[:, I:]))

@@ -631,9 +631,9 @@ ORC_API int64_t orc_decode_rollback(int64_t rows, int64_t* seq_lens, const int64
 /* ------------------------------------------------------------------------ */
 /* MoE routing (a9): softmax over experts (fp32), top-k by (prob desc, index */
 /* asc), renormalised (norm_topk_prob).  thinker_model.py:428-433;           */
-/* hf_config.py:299-304.  Reductions: 32 lanes, lane l holds experts         */
-/* l, l+32, l+64, ... folded in that order; xor butterfly 16..1; the top-k   */
-/* weights are summed in selection order.                                    */
+/* hf_config.py:299-304.  Reductions: 32 lanes, lane l holds the contiguous  */
+/* experts [l*E/32, (l+1)*E/32) folded in index order; xor butterfly 16..1;  */
+/* the top-k weights are summed in selection order.                          */
 /* ------------------------------------------------------------------------ */
 ORC_API int orc_moe_route(const float* router_logits, int64_t tokens, int64_t experts, int64_t top_k,
                           int renormalize, int32_t* topk_ids, float* topk_weights) {
@@ -647,8 +647,8 @@ ORC_API int orc_moe_route(const float* router_logits, int64_t tokens, int64_t ex
         int per = (int)(experts / 32);
         float v[32], nv[32];
         for (int l = 0; l < 32; ++l) {
-            float acc = orc_expf(lg[l] - mx);
-            for (int j = 1; j < per; ++j) acc = acc + orc_expf(lg[l + 32 * j] - mx);
+            float acc = orc_expf(lg[l * per] - mx);
+            for (int j = 1; j < per; ++j) acc = acc + orc_expf(lg[l * per + j] - mx);
             v[l] = acc;
         }
         for (int off = 16; off >= 1; off >>= 1) {
@@ -686,5 +686,70 @@ ORC_API int orc_moe_permute(const int32_t* topk_ids, int64_t tokens, int64_t top
     for (int64_t e = 0; e < experts; ++e) fill[e] = expert_offsets[e];
     for (int64_t i = 0; i < tokens * top_k; ++i) sorted_pairs[fill[topk_ids[i]]++] = (int32_t)i;
     free(fill);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* FP8 e4m3 (OCP "e4m3fn": bias 7, no infinities, max 448) and the per-token */
+/* 128-group activation quantisation of the block-FP8 MoE path               */
+/* (sglang per_token_group_quant_fp8, called from FusedMoE with              */
+/* quantization.py:124-167's block config):                                  */
+/*   amax = max(max|x_g|, 1e-10); scale = amax / 448;                        */
+/*   q = e4m3(clamp(x / scale, -448, 448)), round to nearest even.           */
+/* ------------------------------------------------------------------------ */
+ORC_API uint8_t orc_e4m3_from_f32(float x) {
+    uint32_t u = f2u(x);
+    uint8_t sign = (uint8_t)((u >> 24) & 0x80);
+    if (x != x) return (uint8_t)(sign | 0x7F);
+    float a = fabsf(x);
+    if (a >= 448.0f) return (uint8_t)(sign | 0x7E); /* saturate */
+    if (a < 0.015625f) {                             /* below 2^-6: subnormal, quantum 2^-9 */
+        float q = a * 512.0f;                        /* exact (power-of-two scale) */
+        float r = rintf(q);                          /* nearest even */
+        int m = (int)r;                              /* 0..8; 8 is the smallest normal */
+        return (uint8_t)(sign | (uint8_t)m);
+    }
+    int e;
+    frexpf(a, &e);                                   /* a = f * 2^e, f in [0.5, 1) */
+    int E = e - 1;                                   /* a in [2^E, 2^(E+1)) */
+    float q = ldexpf(a, 3 - E);                      /* [8, 16): exact */
+    float r = rintf(q);
+    int m = (int)r;
+    if (m == 16) { m = 8; E += 1; }
+    if (E > 8) return (uint8_t)(sign | 0x7E);
+    uint8_t bits = (uint8_t)(((E + 7) << 3) | (m - 8));
+    if (bits > 0x7E) bits = 0x7E;
+    return (uint8_t)(sign | bits);
+}
+
+ORC_API float orc_e4m3_to_f32(uint8_t b) {
+    float s = (b & 0x80) ? -1.0f : 1.0f;
+    int E = (b >> 3) & 0xF, m = b & 7;
+    if (E == 15 && m == 7) return NAN;
+    if (E == 0) return s * ldexpf((float)m, -9);
+    return s * ldexpf((float)(8 + m), E - 10);
+}
+
+/* x: rows x cols fp32 (bf16 values); group divides cols.  q: rows x cols
+ * e4m3 bytes; scales: rows x (cols / group) fp32. */
+ORC_API int orc_quant_fp8_group(const float* x, int64_t rows, int64_t cols, int64_t group, uint8_t* q,
+                                float* scales) {
+    if (group <= 0 || cols % group != 0) return 1;
+    for (int64_t r = 0; r < rows; ++r) {
+        for (int64_t g = 0; g < cols / group; ++g) {
+            const float* xs = x + r * cols + g * group;
+            float amax = 0.0f;
+            for (int64_t i = 0; i < group; ++i) { float a = fabsf(xs[i]); if (a > amax) amax = a; }
+            if (amax < 1e-10f) amax = 1e-10f;
+            const float sc = amax / 448.0f;
+            scales[r * (cols / group) + g] = sc;
+            for (int64_t i = 0; i < group; ++i) {
+                float v = xs[i] / sc;
+                if (v > 448.0f) v = 448.0f;
+                if (v < -448.0f) v = -448.0f;
+                q[r * cols + g * group + i] = orc_e4m3_from_f32(v);
+            }
+        }
+    }
     return 0;
 }

@@ -41,6 +41,11 @@ def lib() -> ctypes.CDLL:
         l.orc_decode_rollback.argtypes = [_I64, _P, _P, _P, _I64, _I64, _P, _P]
         l.orc_moe_route.argtypes = [_P, _I64, _I64, _I64, ctypes.c_int, _P, _P]
         l.orc_moe_permute.argtypes = [_P, _I64, _I64, _I64, _P, _P]
+        l.orc_e4m3_from_f32.restype = ctypes.c_uint8
+        l.orc_e4m3_from_f32.argtypes = [ctypes.c_float]
+        l.orc_e4m3_to_f32.restype = ctypes.c_float
+        l.orc_e4m3_to_f32.argtypes = [ctypes.c_uint8]
+        l.orc_quant_fp8_group.argtypes = [_P, _I64, _I64, _I64, _P, _P]
         _lib = l
     return _lib
 
@@ -194,6 +199,35 @@ def moe_permute(topk_ids, experts: int):
     pairs = np.zeros(tokens * k, np.int32)
     lib().orc_moe_permute(_p(ids), tokens, k, experts, _p(offsets), _p(pairs))
     return offsets, pairs
+
+
+def e4m3_from_f32(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    f = lib().orc_e4m3_from_f32
+    return np.array([f(float(v)) for v in x], np.uint8)
+
+
+_E4M3_TABLE = None
+
+
+def e4m3_to_f32(b) -> np.ndarray:
+    """Decodes e4m3 bytes through the oracle's decoder (as a 256-entry table)."""
+    global _E4M3_TABLE
+    if _E4M3_TABLE is None:
+        f = lib().orc_e4m3_to_f32
+        _E4M3_TABLE = np.array([f(i) for i in range(256)], np.float32)
+    return _E4M3_TABLE[np.asarray(b, np.uint8)]
+
+
+def quant_fp8_group(x, group: int = 128):
+    """Per-row, per-group e4m3 quantisation: returns (q uint8 [rows, cols], scales f32 [rows, cols/group])."""
+    xs = _c(x, np.float32)
+    rows, cols = xs.shape
+    q = np.zeros((rows, cols), np.uint8)
+    sc = np.zeros((rows, cols // group), np.float32)
+    if lib().orc_quant_fp8_group(_p(xs), rows, cols, int(group), _p(q), _p(sc)) != 0:
+        raise ValueError("oracle: group must divide the row length")
+    return q, sc
 
 
 # ---------------------------------------------------------------------------

@@ -37,6 +37,7 @@
 
 #include "capi_util.h"
 #include "common.cuh"
+#include "detmath.cuh"
 
 namespace omni {
 namespace {
@@ -49,7 +50,7 @@ constexpr int kMaxStages = 6;
 constexpr int kThreadsG = 256;
 constexpr int kMaxSplits = 16;
 
-enum Epilogue : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiF32 = 3, kEpiQKV = 4 };
+enum Epilogue : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiF32 = 3, kEpiQKV = 4, kEpiRouter = 5 };
 
 struct GemmParams {
   int rows;         // total activation rows
@@ -87,6 +88,10 @@ struct GemmParams {
   int tokens_per_req, slot_stride, slot_base;
   uint16_t* k_cache;
   uint16_t* v_cache;
+  // router epilogue: top_k experts per row by (prob desc, index asc), renormalised
+  int32_t* topk_ids;
+  float* topk_w;
+  int top_k;
 };
 
 OMNI_DEVINL uint32_t cluster_ctarank() {
@@ -423,6 +428,58 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     if (EPI == kEpiF32) {
       float* Y = static_cast<float*>(p.y);
       *reinterpret_cast<float4*>(Y + grow * p.y_stride + col) = make_float4(o[0], o[1], o[2], o[3]);
+    } else if (EPI == kEpiRouter) {
+      // bf16 router logits (the gate projection's output), then the fp32 softmax over
+      // the 128 experts of the row: lane l holds experts 4l..4l+3, partial sums in index
+      // order, xor butterfly 16..1; top-k by (prob desc, index asc); weights renormalised
+      // by their sum in selection order
+      const uint2 packed = make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
+      uint16_t* Y = static_cast<uint16_t*>(p.y);
+      *reinterpret_cast<uint2*>(Y + grow * p.y_stride + col) = packed;
+      const float lg[4] = {bf_lo(packed.x), bf_hi(packed.x), bf_lo(packed.y), bf_hi(packed.y)};
+      float mx = fmaxf(fmaxf(lg[0], lg[1]), fmaxf(lg[2], lg[3]));
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+      float ex[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ex[j] = det_expf(__fsub_rn(lg[j], mx));
+      float z = __fadd_rn(__fadd_rn(__fadd_rn(ex[0], ex[1]), ex[2]), ex[3]);
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) z = __fadd_rn(z, __shfl_xor_sync(0xFFFFFFFFu, z, off));
+      unsigned long long key[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t pb = __float_as_uint(__fdiv_rn(ex[j], z));
+        const uint32_t ord = (pb >> 31) ? ~pb : (pb | 0x80000000u);
+        key[j] = ((unsigned long long)ord << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)(f + j));
+      }
+      float wsum = 0.0f, wsel = 0.0f;
+      int idsel = 0;
+      for (int kk = 0; kk < p.top_k; ++kk) {
+        unsigned long long best = 0ull;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) best = key[j] > best ? key[j] : best;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+          const unsigned long long o2 = __shfl_xor_sync(0xFFFFFFFFu, best, off);
+          best = o2 > best ? o2 : best;
+        }
+        const int e = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu));
+        const uint32_t ob = (uint32_t)(best >> 32);
+        const float pe = __uint_as_float((ob >> 31) ? (ob & 0x7FFFFFFFu) : ~ob);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (f + j == e) key[j] = 0ull;
+        wsum = kk == 0 ? pe : __fadd_rn(wsum, pe);
+        if (ln == kk) {
+          wsel = pe;
+          idsel = e;
+        }
+      }
+      if (ln < p.top_k) {
+        p.topk_ids[grow * p.top_k + ln] = idsel;
+        p.topk_w[grow * p.top_k + ln] = __fdiv_rn(wsel, wsum);
+      }
     } else if (EPI == kEpiQKV) {
       const int D = p.head_dim;
       const int gh = (int)(col / D);  // global head of these 4 features
@@ -707,7 +764,7 @@ int launch_gemm(const void* x, int64_t rows, int64_t k, int64_t x_stride, const 
 int run_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n, int epilogue,
                const GemmParams& gp, int splits, cudaStream_t st) {
   if (rows < 0 || k <= 0 || n <= 0) return set_error(OMNI_ERR_INVALID, "bad GEMM shape");
-  if (epilogue < 0 || epilogue > 4) return set_error(OMNI_ERR_INVALID, "unknown epilogue");
+  if (epilogue < 0 || epilogue > 5) return set_error(OMNI_ERR_INVALID, "unknown epilogue");
   if (splits < 0 || splits > kMaxSplits) return set_error(OMNI_ERR_INVALID, "splits must be in [0, 16]");
   if (k % kBK != 0) return set_error(OMNI_ERR_UNSUPPORTED, "K must be a multiple of 64");
   if (n % kTileN != 0) return set_error(OMNI_ERR_UNSUPPORTED, "N must be a multiple of 128");
@@ -719,7 +776,7 @@ int run_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const v
     return set_error(OMNI_ERR_INVALID, "residual epilogue needs an 8-byte aligned residual");
   if (gp.ss_in && (gp.ss_in_parts <= 0 || gp.ss_in_parts > 64 || gp.norm_dim <= 0))
     return set_error(OMNI_ERR_INVALID, "ss_in needs 1..64 parts and norm_dim > 0");
-  if (gp.ss_out && (epilogue == kEpiSwiGLU || epilogue == kEpiF32 || epilogue == kEpiQKV))
+  if (gp.ss_out && (epilogue == kEpiSwiGLU || epilogue == kEpiF32 || epilogue == kEpiQKV || epilogue == kEpiRouter))
     return set_error(OMNI_ERR_UNSUPPORTED, "ss_out is produced by the store and residual epilogues only");
   if (epilogue == kEpiQKV) {
     if (gp.head_dim != 64 && gp.head_dim != 128)
@@ -734,6 +791,9 @@ int run_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const v
     if (!gp.q_norm || !gp.k_norm || !gp.cos_sin || !gp.k_cache || !gp.v_cache)
       return set_error(OMNI_ERR_INVALID, "qkv epilogue needs norms, cos/sin table and caches");
   }
+  if (epilogue == kEpiRouter &&
+      (n != kTileN || gp.top_k < 1 || gp.top_k > 32 || gp.topk_ids == nullptr || gp.topk_w == nullptr))
+    return set_error(OMNI_ERR_UNSUPPORTED, "router epilogue: 128 experts, 1 <= top_k <= 32, top-k outputs given");
   if (rows == 0) return OMNI_OK;
   if (splits > k / kBK) splits = (int)(k / kBK);
   switch (epilogue) {
@@ -741,6 +801,7 @@ int run_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const v
     case kEpiResidual: return launch_gemm<kEpiResidual>(x, rows, k, x_stride, w, n, gp, splits, st);
     case kEpiSwiGLU: return launch_gemm<kEpiSwiGLU>(x, rows, k, x_stride, w, n, gp, splits, st);
     case kEpiQKV: return launch_gemm<kEpiQKV>(x, rows, k, x_stride, w, n, gp, splits, st);
+    case kEpiRouter: return launch_gemm<kEpiRouter>(x, rows, k, x_stride, w, n, gp, splits, st);
     default: return launch_gemm<kEpiF32>(x, rows, k, x_stride, w, n, gp, splits, st);
   }
 }
@@ -761,7 +822,8 @@ extern "C" OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int6
                                     void* y, int64_t y_stride, void* workspace, int64_t workspace_bytes_avail,
                                     int32_t splits, void* stream) {
   (void)workspace, (void)workspace_bytes_avail;
-  if (epilogue == kEpiQKV) return set_error(OMNI_ERR_INVALID, "the qkv epilogue is reached through omni_linear_fused");
+  if (epilogue == kEpiQKV || epilogue == kEpiRouter)
+    return set_error(OMNI_ERR_INVALID, "the qkv and router epilogues are reached through omni_linear_fused");
   GemmParams gp{};
   gp.residual = static_cast<const uint16_t*>(residual);
   gp.res_stride = residual_stride;
@@ -799,6 +861,9 @@ extern "C" OMNI_API int omni_linear_fused(const OmniLinearArgs* a, void* stream)
   gp.slot_base = a->slot_base;
   gp.k_cache = static_cast<uint16_t*>(a->k_cache);
   gp.v_cache = static_cast<uint16_t*>(a->v_cache);
+  gp.topk_ids = a->topk_ids;
+  gp.topk_w = a->topk_weights;
+  gp.top_k = a->top_k;
   return run_linear(a->x, a->rows, a->k, a->x_stride, a->w, a->n, a->epilogue, gp, a->splits,
                     static_cast<cudaStream_t>(stream));
 }

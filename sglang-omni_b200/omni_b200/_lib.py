@@ -56,6 +56,12 @@ SIGNATURES: dict[str, list] = {
     "omni_predictor_attention": [_P, _I64, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _F32, _P, _I64, _P],
     "omni_decode_prepare": [_I64, _P, _P, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P],
     "omni_decode_rollback": [_I64, _P, _P, _P, _I64, _I32, _P, _P, _P, _P, _P],
+    "omni_moe_rmsnorm_quant": [_P, _I64, _P, _I32, _I64, _P, _F32, _I64, _I32, _P, _I64, _P, _P, _P],
+    "omni_moe_chunk_capacity": [_I64, _I32, _I32],
+    "omni_moe_align_gather": [_P, _I64, _I32, _I32, _P, _P, _I32, _P, _P, _P, _P, _P, _I64, _P, _P],
+    "omni_moe_gate_up_fp8": [_P, _P, _I64, _I32, _P, _P, _I32, _I32, _P, _P, _P, _P, _P],
+    "omni_moe_down_fp8": [_P, _P, _I64, _I32, _P, _P, _I32, _I32, _P, _P, _P, _I64, _P],
+    "omni_moe_combine": [_P, _I64, _P, _P, _I32, _P, _I64, _P, _P, _I64, _P, _I64, _P, _I64, _I64, _I32, _P],
 }
 _RESTYPES = {
     "omni_version": ctypes.c_char_p,
@@ -63,6 +69,7 @@ _RESTYPES = {
     "omni_device_status": ctypes.c_uint,
     "omni_linear_workspace_bytes": ctypes.c_int64,
     "omni_paged_attention_workspace_bytes": ctypes.c_int64,
+    "omni_moe_chunk_capacity": ctypes.c_int64,
 }
 
 _lock = threading.Lock()

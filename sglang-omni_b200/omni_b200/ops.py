@@ -18,6 +18,7 @@ EPI_RESIDUAL = 1
 EPI_SWIGLU = 2
 EPI_F32 = 3
 EPI_QKV_ROPE = 4
+EPI_ROUTER = 5
 
 
 class OmniLinearArgs(ctypes.Structure):
@@ -35,6 +36,7 @@ class OmniLinearArgs(ctypes.Structure):
         ("max_position", ctypes.c_int64), ("positions", ctypes.c_void_p), ("cache_loc", ctypes.c_void_p),
         ("tokens_per_req", ctypes.c_int32), ("slot_stride", ctypes.c_int32), ("slot_base", ctypes.c_int32),
         ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+        ("topk_ids", ctypes.c_void_p), ("topk_weights", ctypes.c_void_p), ("top_k", ctypes.c_int32),
     ]
 
 
@@ -50,12 +52,15 @@ def linear_fused(
     residual: torch.Tensor | None = None,
     ss_out: torch.Tensor | None = None,
     qkv: dict | None = None,
+    router: dict | None = None,
     splits: int = 0,
 ) -> torch.Tensor:
     """out = epilogue(rstd * (x @ w.T)) with the RMSNorm folded into w (gain already
     multiplied into its columns) and rstd from ss_in [parts, rows_cap] sums of squares.
     ss_out [parts, rows_cap] receives the output's per-tile sums of squares.
-    qkv: head geometry, norms, rotary table and caches for EPI_QKV_ROPE."""
+    qkv: head geometry, norms, rotary table and caches for EPI_QKV_ROPE.
+    router: {"topk_ids": i32 [rows, k], "topk_weights": f32 [rows, k]} for EPI_ROUTER
+    (out receives the bf16 router logits)."""
     a = OmniLinearArgs()
     a.x = x.data_ptr()
     a.rows, a.k = x.shape
@@ -96,6 +101,10 @@ def linear_fused(
             a.slot_base = qkv["slot_base"]
         a.k_cache = qkv["k_cache"].data_ptr()
         a.v_cache = qkv["v_cache"].data_ptr()
+    if router is not None:
+        a.topk_ids = router["topk_ids"].data_ptr()
+        a.topk_weights = router["topk_weights"].data_ptr()
+        a.top_k = router["topk_ids"].shape[1]
     _lib.call("omni_linear_fused", ctypes.addressof(a), _lib.stream_of(x.device))
     return out
 
@@ -401,3 +410,56 @@ def rope_cos_sin_cache(max_position: int, head_dim: int, theta: float, device) -
     t = torch.arange(max_position, dtype=torch.float32)
     freqs = torch.outer(t, inv_freq)
     return torch.cat([freqs.cos(), freqs.sin()], dim=-1).contiguous().to(device)
+
+
+# ---------------------------------------------------------------------------
+# MoE block (block-FP8 experts)
+# ---------------------------------------------------------------------------
+def moe_rmsnorm_quant(h: torch.Tensor, ss: torch.Tensor, ss_parts: int, gain: torch.Tensor, eps: float,
+                      x: torch.Tensor, xq: torch.Tensor, xs: torch.Tensor) -> None:
+    """x = RMSNorm(h) (bf16) with rstd from ss [parts, rows_cap]; xq/xs its per-row
+    128-group e4m3 codes (uint8) and f32 scales."""
+    rows, hidden = h.shape
+    _lib.call("omni_moe_rmsnorm_quant", h.data_ptr(), h.stride(0), ss.data_ptr(), ss_parts, ss.stride(0),
+              gain.data_ptr(), eps, rows, hidden, x.data_ptr(), x.stride(0), xq.data_ptr(), xs.data_ptr(),
+              _lib.stream_of(h.device))
+
+
+def moe_chunk_capacity(tokens: int, top_k: int, experts: int) -> int:
+    return int(_lib.load().omni_moe_chunk_capacity(tokens, top_k, experts))
+
+
+def moe_align_gather(topk_ids: torch.Tensor, experts: int, xq: torch.Tensor, xs: torch.Tensor,
+                     permuted_q: torch.Tensor, permuted_s: torch.Tensor, slot_of: torch.Tensor,
+                     expert_offsets: torch.Tensor, chunks: torch.Tensor, n_chunks: torch.Tensor) -> None:
+    tokens, top_k = topk_ids.shape
+    _lib.call("omni_moe_align_gather", topk_ids.data_ptr(), tokens, top_k, experts, xq.data_ptr(), xs.data_ptr(),
+              xq.shape[1], permuted_q.data_ptr(), permuted_s.data_ptr(), slot_of.data_ptr(),
+              expert_offsets.data_ptr(), chunks.data_ptr(), chunks.shape[0], n_chunks.data_ptr(),
+              _lib.stream_of(topk_ids.device))
+
+
+def moe_gate_up_fp8(permuted_q: torch.Tensor, permuted_s: torch.Tensor, w13: torch.Tensor, w13_scale: torch.Tensor,
+                    chunks: torch.Tensor, n_chunks: torch.Tensor, act_q: torch.Tensor, act_s: torch.Tensor) -> None:
+    experts, two_i, hidden = w13.shape
+    _lib.call("omni_moe_gate_up_fp8", permuted_q.data_ptr(), permuted_s.data_ptr(), permuted_q.shape[0], hidden,
+              w13.data_ptr(), w13_scale.data_ptr(), experts, two_i // 2, chunks.data_ptr(), n_chunks.data_ptr(),
+              act_q.data_ptr(), act_s.data_ptr(), _lib.stream_of(w13.device))
+
+
+def moe_down_fp8(act_q: torch.Tensor, act_s: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor,
+                 chunks: torch.Tensor, n_chunks: torch.Tensor, y: torch.Tensor) -> None:
+    experts, hidden, inter = w2.shape
+    _lib.call("omni_moe_down_fp8", act_q.data_ptr(), act_s.data_ptr(), act_q.shape[0], inter, w2.data_ptr(),
+              w2_scale.data_ptr(), experts, hidden, chunks.data_ptr(), n_chunks.data_ptr(), y.data_ptr(),
+              y.stride(0), _lib.stream_of(w2.device))
+
+
+def moe_combine(y: torch.Tensor, slot_of: torch.Tensor, topk_weights: torch.Tensor, x: torch.Tensor,
+                shared_gate_weight: torch.Tensor, shared_out: torch.Tensor, h: torch.Tensor,
+                ss_out: torch.Tensor | None) -> None:
+    rows, hidden = h.shape
+    _lib.call("omni_moe_combine", y.data_ptr(), y.stride(0), slot_of.data_ptr(), topk_weights.data_ptr(),
+              slot_of.shape[1], x.data_ptr(), x.stride(0), shared_gate_weight.data_ptr(), shared_out.data_ptr(),
+              shared_out.stride(0), h.data_ptr(), h.stride(0), _lib.ptr(ss_out),
+              0 if ss_out is None else ss_out.stride(0), rows, hidden, _lib.stream_of(h.device))

@@ -12,7 +12,9 @@ RMSNorm and the codec head in fp32, then the layer-0 codec token draw
 Per layer the forward is 5 launches, all but the attention tcgen05 GEMMs with
 fused epilogues: qkv (folded input RMSNorm + q/k RMSNorm + RoPE + KV store),
 paged attention, o_proj (+residual, row sums of squares), gate_up (folded
-post-attention RMSNorm + SwiGLU), down (+residual, row sums of squares).
+post-attention RMSNorm + SwiGLU), down (+residual, row sums of squares).  With
+cfg.moe the MLP is the sparse MoE block (omni_b200.moe.MoEBlock,
+Qwen3OmniMoeTalkerSparseMoeBlock, talker.py:325-351).
 """
 
 from __future__ import annotations
@@ -25,6 +27,7 @@ import torch
 from omni_b200 import ops
 from omni_b200.config import TalkerConfig
 from omni_b200.kv_cache import PagedKVPool
+from omni_b200.moe import MoEBlock, init_moe_weights
 from omni_b200.sampling_kernels import layer0_sample
 
 
@@ -42,16 +45,20 @@ def init_talker_weights(cfg: TalkerConfig, *, seed: int, device, dtype=torch.bfl
 
     layers = []
     for _ in range(cfg.num_hidden_layers):
-        layers.append({
+        layer = {
             "input_layernorm": gain(H),
             "qkv_proj": lin((hq + 2 * hkv) * D, H),
             "q_norm": gain(D),
             "k_norm": gain(D),
             "o_proj": lin(H, hq * D),
             "post_attention_layernorm": gain(H),
-            "gate_up_proj": lin(2 * I, H),
-            "down_proj": lin(H, I),
-        })
+        }
+        if cfg.moe is None:
+            layer["gate_up_proj"] = lin(2 * I, H)
+            layer["down_proj"] = lin(H, I)
+        else:
+            layer["moe"] = init_moe_weights(cfg.moe, H, generator=g, device=device)
+        layers.append(layer)
     return {"layers": layers, "norm": gain(H), "codec_head": lin(V, H), "codec_embedding": lin(V, H)}
 
 
@@ -112,8 +119,10 @@ class DenseTalker:
         # folded RMSNorms: each norm's gain is multiplied into the columns of the GEMM it feeds;
         # ss holds the per-row sums of squares of the residual stream (one part per 128 features)
         self.folded = [{"qkv": ops.fold_norm(lw["qkv_proj"], lw["input_layernorm"]),
-                        "gate_up": ops.fold_norm(lw["gate_up_proj"], lw["post_attention_layernorm"])}
+                        "gate_up": (ops.fold_norm(lw["gate_up_proj"], lw["post_attention_layernorm"])
+                                    if "gate_up_proj" in lw else None)}
                        for lw in self.w["layers"]]
+        self.moe = MoEBlock(cfg.moe, H, max_batch=B, device=self.device) if cfg.moe is not None else None
         self.codec_head_folded = ops.fold_norm(self.w["codec_head"], self.w["norm"])
         self.ss = torch.zeros(H // 128, B, dtype=torch.float32, device=self.device)
 
@@ -154,9 +163,12 @@ class DenseTalker:
                                        pages_per_chunk=fb.pages_per_chunk, work_capacity=fb.work_capacity,
                                        sm_scale=self.scale, out=attn, workspace=self.attn_workspace)
             ops.linear_fused(attn, lw["o_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=ss)
-            ops.linear_fused(h, self.folded[li]["gate_up"], act, epilogue=ops.EPI_SWIGLU, ss_in=ss, ss_in_parts=parts,
-                             norm_eps=eps)
-            ops.linear_fused(act, lw["down_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=ss)
+            if "moe" in lw:
+                self.moe.forward(h, ss, parts, lw["post_attention_layernorm"], eps, lw["moe"])
+            else:
+                ops.linear_fused(h, self.folded[li]["gate_up"], act, epilogue=ops.EPI_SWIGLU, ss_in=ss,
+                                 ss_in_parts=parts, norm_eps=eps)
+                ops.linear_fused(act, lw["down_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=ss)
             ss_parts = parts
         logits = self.logits[:B]
         ops.linear_fused(h, self.codec_head_folded, logits, epilogue=ops.EPI_F32, ss_in=ss, ss_in_parts=parts,

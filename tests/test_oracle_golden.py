@@ -150,3 +150,36 @@ def test_moe_route_renormalised_topk():
     assert offsets[-1] == 16 * 8
     flat = ids.reshape(-1)
     assert np.all(np.diff(flat[pairs]) >= 0)
+
+
+def test_e4m3_codes_match_torch_float8():
+    """The oracle's e4m3 encoder/decoder against torch.float8_e4m3fn, the dtype the
+    reference's block-FP8 path quantises into (clamped to +-448 first)."""
+    import torch
+
+    rng = np.random.default_rng(7)
+    mags = np.float32(10.0) ** rng.uniform(-4, 3, 4000).astype(np.float32)
+    vals = np.concatenate([rng.standard_normal(4000).astype(np.float32) * mags,
+                           np.array([0.0, -0.0, 448, -448, 449, 464, 465, 1e9, 2**-9, 2**-10, 3 * 2**-11, 2**-6,
+                                     0.0009765625, 240, 248, 256, 272], np.float32)])
+    want = torch.from_numpy(vals).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(orc.e4m3_from_f32(vals), want)
+    dec = orc.e4m3_to_f32(np.arange(256))
+    tdec = torch.arange(256, dtype=torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    assert np.array_equal(np.nan_to_num(dec, nan=-1.0), np.nan_to_num(tdec, nan=-1.0))
+
+
+def test_group_quant_matches_torch_restatement():
+    """per_token_group_quant_fp8: scale = max(amax, 1e-10) / 448, q = e4m3(clamp(x / scale))."""
+    import torch
+
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((5, 384)).astype(np.float32)
+    x[2, 128:256] = 0.0  # an all-zero group takes the 1e-10 floor
+    q, s = orc.quant_fp8_group(x, 128)
+    xt = torch.from_numpy(x).view(5, 3, 128)
+    amax = xt.abs().amax(-1, keepdim=True).clamp_min(1e-10)
+    ts = amax / 448.0
+    tq = (xt / ts).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8).view(5, 384).numpy()
+    assert np.array_equal(q, tq)
+    assert np.array_equal(s, ts.view(5, 3).numpy())
