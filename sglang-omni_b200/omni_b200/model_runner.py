@@ -12,9 +12,10 @@ One step on the device, in order:
   1. omni_decode_prepare: seq_lens += 1, page/slot allocation, positions, page
      table and the attention work list (prepare_for_decode + build_forward_batch);
   2. talker forward over the decode rows, input = previous frame's summed codec
-     embeddings + the text row (write_feedback_buffers);
+     embeddings + the text row (write_feedback_buffers); dense SwiGLU or, with
+     cfg.moe, the block-FP8 MoE block per layer;
   3. layer-0 codec draw (repetition penalty, suppression, seeded top-k/top-p);
-  4. the code predictor: 15 residual codebooks, each fused sample + gather.
+  4. the code predictor: G - 1 residual codebooks, each fused sample + gather.
 The host touches nothing inside the step: it copies the text rows in and the
 codes out around the graph replay.
 """
@@ -48,8 +49,6 @@ class GenerationBatchResult:
 class TalkerDecodeRunner:
     def __init__(self, cfg: TalkerConfig, *, max_batch: int, num_pages: int, seed: int = 0, device="cuda",
                  pages_per_chunk: int = 16, weights: dict | None = None, predictor_weights: dict | None = None):
-        if cfg.moe is not None:
-            raise NotImplementedError("the MoE talker runs through MoETalkerDecodeRunner")
         self.cfg = cfg
         self.device = torch.device(device)
         self.max_batch = max_batch

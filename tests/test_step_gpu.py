@@ -32,11 +32,15 @@ def cos_err(a: torch.Tensor, b: torch.Tensor):
     return cos, (a - b).abs().max().item(), b.abs().max().item()
 
 
-def make_runner(layers=2, lens=(16, 1, 33, 100, 200, 15, 64, 17), seed=0, max_batch=8, sampling=None):
-    from omni_b200.config import SamplingParams, TalkerConfig
+def make_runner(layers=2, lens=(16, 1, 33, 100, 200, 15, 64, 17), seed=0, max_batch=8, sampling=None, moe=False):
+    from omni_b200.config import MoEConfig, PredictorConfig, SamplingParams, TalkerConfig
     from omni_b200.model_runner import TalkerDecodeRunner
 
-    cfg = TalkerConfig(num_hidden_layers=layers, max_context=1024)
+    if moe:  # the config-3 geometry: 128 experts top-8, 31 residual codebooks of 1024
+        cfg = TalkerConfig(num_hidden_layers=layers, max_context=1024, moe=MoEConfig(),
+                           predictor=PredictorConfig(vocab_size=1024, num_code_groups=32))
+    else:
+        cfg = TalkerConfig(num_hidden_layers=layers, max_context=1024)
     pages = sum((L + 16) // 16 for L in lens) + 32
     r = TalkerDecodeRunner(cfg, max_batch=max_batch, num_pages=pages, seed=seed)
     r.admit(list(lens), sampling=sampling or SamplingParams(), seed=seed + 5)
@@ -46,12 +50,12 @@ def make_runner(layers=2, lens=(16, 1, 33, 100, 200, 15, 64, 17), seed=0, max_ba
     return r
 
 
-@pytest.mark.parametrize("dosample", [True, False])
-def test_decode_step_matches_oracle(dosample):
+@pytest.mark.parametrize("dosample,moe", [(True, False), (False, False), (True, True)])
+def test_decode_step_matches_oracle(dosample, moe):
     from omni_b200.config import SamplingParams
 
     sp = SamplingParams(subtalker_dosample=dosample)
-    r = make_runner(sampling=sp)
+    r = make_runner(sampling=sp, moe=moe)
     B = r.batch_size
     cfg = r.cfg
     # snapshot the pre-step state for the oracle
@@ -130,9 +134,10 @@ def test_decode_step_matches_oracle(dosample):
     assert np.array_equal(bits(p.output_embeds[:B]), summed_o)
 
 
-def test_graph_replay_is_bit_identical_to_eager():
-    a = make_runner(seed=1)
-    b = make_runner(seed=1)
+@pytest.mark.parametrize("moe", [False, True])
+def test_graph_replay_is_bit_identical_to_eager(moe):
+    a = make_runner(seed=1, moe=moe)
+    b = make_runner(seed=1, moe=moe)
     b.capture(warmup=1)
     a.step(use_graph=False)  # the same number of steps as b's warm-up
     for _ in range(3):
@@ -145,14 +150,16 @@ def test_graph_replay_is_bit_identical_to_eager():
         assert torch.equal(a.seq_lens, b.seq_lens)
 
 
-def test_rows_never_mix():
-    """A row's frame does not depend on the other rows of the batch."""
+@pytest.mark.parametrize("moe", [False, True])
+def test_rows_never_mix(moe):
+    """A row's frame does not depend on the other rows of the batch (with MoE: nor on
+    which rows share its experts)."""
     lens = (16, 1, 33, 100, 200, 15, 64, 17)
-    full = make_runner(lens=lens, seed=2)
+    full = make_runner(lens=lens, seed=2, moe=moe)
     full.step(use_graph=False)
-    part = make_runner(lens=lens[:4], seed=2)
+    part = make_runner(lens=lens[:4], seed=2, moe=moe)
     # same per-row inputs: copy the full runner's initial feedback/text rows of the first 4 streams
-    ref = make_runner(lens=lens, seed=2)
+    ref = make_runner(lens=lens, seed=2, moe=moe)
     part.text_embeds[:4].copy_(ref.text_embeds[:4])
     part.predictor.output_embeds[:4].copy_(ref.predictor.output_embeds[:4])
     part.talker.sampling_seeds[:4].copy_(ref.talker.sampling_seeds[:4])
