@@ -247,12 +247,45 @@ def kernel_table(runner, iters: int = 50) -> list[dict]:
     add("talker o_proj gemm (+res,ss)", lambda: ops.linear_fused(
         t.attn[:B], lw["o_proj"], t.h[:B], epilogue=ops.EPI_RESIDUAL, residual=t.h[:B], ss_out=t.ss),
         wb(lw["o_proj"]), L)
-    add("talker gate_up gemm (+norm,swiglu)", lambda: ops.linear_fused(
-        t.h[:B], fw["gate_up"], t.act[:B], epilogue=ops.EPI_SWIGLU, ss_in=t.ss, ss_in_parts=8, norm_eps=eps),
-        wb(fw["gate_up"]), L)
-    add("talker down gemm (+res,ss)", lambda: ops.linear_fused(
-        t.act[:B], lw["down_proj"], t.h[:B], epilogue=ops.EPI_RESIDUAL, residual=t.h[:B], ss_out=t.ss),
-        wb(lw["down_proj"]), L)
+    if cfg.moe is None:
+        add("talker gate_up gemm (+norm,swiglu)", lambda: ops.linear_fused(
+            t.h[:B], fw["gate_up"], t.act[:B], epilogue=ops.EPI_SWIGLU, ss_in=t.ss, ss_in_parts=8, norm_eps=eps),
+            wb(fw["gate_up"]), L)
+        add("talker down gemm (+res,ss)", lambda: ops.linear_fused(
+            t.act[:B], lw["down_proj"], t.h[:B], epilogue=ops.EPI_RESIDUAL, residual=t.h[:B], ss_out=t.ss),
+            wb(lw["down_proj"]), L)
+    else:
+        m, mw, mc = t.moe, lw["moe"], cfg.moe
+        E, k = mc.num_experts, mc.num_experts_per_tok
+        gain = lw["post_attention_layernorm"]
+        ids, tw = m.topk_ids[:B], m.topk_weights[:B]
+        ops.moe_rmsnorm_quant(t.h[:B], t.ss, 8, gain, eps, m.x[:B], m.xq[:B], m.xs[:B])
+        ops.linear_fused(m.x[:B], mw["gate"], m.router_logits[:B], epilogue=ops.EPI_ROUTER,
+                         router={"topk_ids": ids, "topk_weights": tw})
+        torch.cuda.synchronize()
+        used = int(torch.unique(ids).numel())
+        add("moe rmsnorm+fp8 quant", lambda: ops.moe_rmsnorm_quant(t.h[:B], t.ss, 8, gain, eps, m.x[:B], m.xq[:B],
+                                                                  m.xs[:B]), B * H * 5, L)
+        add("moe router gemm (+softmax,top-k)", lambda: ops.linear_fused(
+            m.x[:B], mw["gate"], m.router_logits[:B], epilogue=ops.EPI_ROUTER,
+            router={"topk_ids": ids, "topk_weights": tw}), wb(mw["gate"]), L)
+        add("moe align+gather", lambda: ops.moe_align_gather(
+            ids, E, m.xq[:B], m.xs[:B], m.permuted_q, m.permuted_s, m.slot_of[:B], m.expert_offsets, m.chunks,
+            m.n_chunks), 2 * B * k * H, L)
+        add("moe gate_up fp8 grouped gemm (+swiglu,quant)", lambda: ops.moe_gate_up_fp8(
+            m.permuted_q, m.permuted_s, mw["w13"], mw["w13_scale"], m.chunks, m.n_chunks, m.act_q, m.act_s),
+            used * mw["w13"][0].numel(), L)
+        add("moe down fp8 grouped gemm", lambda: ops.moe_down_fp8(
+            m.act_q, m.act_s, mw["w2"], mw["w2_scale"], m.chunks, m.n_chunks, m.y), used * mw["w2"][0].numel(), L)
+        add("moe shared gate_up gemm (swiglu)", lambda: ops.linear_fused(
+            m.x[:B], mw["shared_gate_up"], m.shared_act[:B], epilogue=ops.EPI_SWIGLU), wb(mw["shared_gate_up"]), L)
+        add("moe shared down gemm", lambda: ops.linear_fused(
+            m.shared_act[:B], mw["shared_down"], m.shared_out[:B], epilogue=ops.EPI_STORE), wb(mw["shared_down"]), L)
+        h_copy = t.h[:B].clone()
+        ss_copy = t.ss.clone()
+        add("moe combine (+res,ss)", lambda: ops.moe_combine(
+            m.y, m.slot_of[:B], tw, m.x[:B], mw["shared_expert_gate"], m.shared_out[:B], h_copy, ss_copy),
+            B * k * H * 2 + 4 * B * H * 2, L)
     add("talker codec_head gemm (+norm)", lambda: ops.linear_fused(
         t.h[:B], t.codec_head_folded, t.logits[:B], epilogue=ops.EPI_F32, ss_in=t.ss, ss_in_parts=8, norm_eps=eps),
         wb(t.codec_head_folded), 1)
@@ -286,7 +319,7 @@ def kernel_table(runner, iters: int = 50) -> list[dict]:
         norm_eps=eps), wb(p.lm_head_folded[1]), pc.num_code_groups - 1)
     add("predictor sample+gather", lambda: predictor_sample_step(
         p.logits[1, :B], temperatures=p.sub_temperature_tensor[:B], top_ks=p.sub_top_k_tensor[:B],
-        top_ps=p.sub_top_p_tensor[:B], seeds=p.sub_sampling_seed_tensor[:B], positions=fb.positions, pos_mul=15,
+        top_ps=p.sub_top_p_tensor[:B], seeds=p.sub_sampling_seed_tensor[:B], positions=fb.positions, pos_mul=pc.num_code_groups - 1,
         pos_add=2, do_sample=None, argmax_all=False, max_top_k=p.sub_sampled_max_top_k,
         has_top_p=p.sub_sampled_has_top_p, codes=p.output_codes[:B, 2], table=p.w["codec_embedding"][1],
         gathered=p.next_in[:B], summed=p.output_embeds[:B], gathered_ss=p.next_ss[:B]),
@@ -303,6 +336,8 @@ def main() -> None:
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kernels", action="store_true", help="print the per-kernel time table and exit")
+    ap.add_argument("--config", type=int, default=1, choices=[1, 3],
+                    help="1: dense talker, 64 streams (the headline); 3: MoE talker with FP8 experts, 256 streams")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -325,12 +360,16 @@ def main() -> None:
         return
 
     from omni_b200 import _lib, ops
-    from omni_b200.config import CONFIG1_DENSE
+    from omni_b200.config import CONFIG1_DENSE, CONFIG3_MOE
     from omni_b200.model_runner import TalkerDecodeRunner
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    cfg = CONFIG1_DENSE
+    global STREAMS
+    if args.config == 3:
+        cfg, STREAMS = CONFIG3_MOE, 256
+    else:
+        cfg = CONFIG1_DENSE
     W, K = max(3, args.warmup), args.steps
     total_steps = 2 * (W + K) + 4
     lens = context_lengths(STREAMS, seed=rank, headroom=total_steps + 8)
@@ -425,8 +464,12 @@ def main() -> None:
             "ms_per_step": total_ms / K, "p50_step_us": 1000 * float(np.median(step_ms)),
             "p99_step_us": 1000 * float(np.percentile(step_ms, 99)), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "config1: dense talker decode (20 layers, 64 streams, paged KV page 16, "
-                                   "ctx lognormal(6,0.8) clip [16,8192]) + config-0 predictor (15 codebooks)",
+            "config": {"workload": ("config1: dense talker decode (20 layers, 64 streams, paged KV page 16, "
+                                    "ctx lognormal(6,0.8) clip [16,8192]) + config-0 predictor (15 codebooks)")
+                       if args.config == 1 else
+                       ("config3: MoE talker decode (20 layers, 128 experts top-8 inter 384 FP8 e4m3 "
+                        "128x128 block scales + shared expert 1536, 256 streams, paged KV page 16, "
+                        "ctx lognormal(6,0.8) clip [16,8192]) + predictor (31 codebooks of 1024)"),
                        "streams_per_gpu": STREAMS, "parallelism": f"dp{world} replicas (no collective)",
                        "sum_ctx_rank0": int(sum(lens)), "l2": "inputs > L2 (~3 GB streamed per step)"},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": STREAMS * H * 2,
@@ -437,7 +480,7 @@ def main() -> None:
                          "peak_kind": peak_kind},
             "clocks": clocks.summary(),
         }
-        if not args.no_cpu:
+        if not args.no_cpu and args.config == 1:
             rate, desc, _ = cpu_step_rate(args.cpu_steps, 1)
             line["cpu_baseline"] = {"value": rate, "unit": UNIT, **desc}
         print(json.dumps(line), flush=True)

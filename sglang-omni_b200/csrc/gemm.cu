@@ -666,19 +666,39 @@ int plan_stages(int row_tile, int kb_per, int splits) {
   return st;
 }
 
+// Rows per CTA.  Splitting the rows into several tiles re-reads the weights
+// from L2 once per tile but shrinks each CTA's partial tile and epilogue;
+// split-K instead shrinks each CTA's weight stream.  Measured on B200 over the
+// decode-step shapes (rows 64..512, K 1024 / 3072, 1..48 feature tiles): aim
+// for about 48 (feature tile, row tile) pairs when K <= 1024 and 32 beyond,
+// with power-of-two row tiles of at least 32 rows (64 when K > 1024) and at
+// most 256.
+int plan_row_tile(int64_t rows, int64_t k, int tiles) {
+  const int min_rt = k > 1024 ? 64 : 32;
+  const int target = k > 1024 ? 32 : 48;
+  int64_t rt;
+  if (rows <= min_rt) {
+    rt = rows;
+  } else {
+    const int nrt = (target + tiles - 1) / tiles;
+    const int64_t want = (rows + nrt - 1) / nrt;
+    rt = min_rt;
+    while (rt * 2 <= want && rt * 2 <= kMaxRows) rt *= 2;
+  }
+  rt = (rt + 15) / 16 * 16;
+  if (rt < 16) rt = 16;
+  if (rt > kMaxRows) rt = kMaxRows;
+  return (int)rt;
+}
+
 template <int EPI>
 Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
   Plan pl{};
-  int nrt = (int)((rows + kMaxRows - 1) / kMaxRows);
-  if (nrt < 1) nrt = 1;
-  int64_t per = (rows + nrt - 1) / nrt;
-  pl.row_tile = (int)((per + 15) / 16 * 16);
-  if (pl.row_tile < 16) pl.row_tile = 16;
-  if (pl.row_tile > kMaxRows) pl.row_tile = kMaxRows;
+  pl.tiles = (int)(EPI == kEpiSwiGLU ? (n / 2) / (kTileN / 2) : n / kTileN);
+  pl.row_tile = plan_row_tile(rows, k, pl.tiles);
   // every row tile starts inside the activation rows
   pl.num_rt = (int)((rows + pl.row_tile - 1) / pl.row_tile);
   if (pl.num_rt < 1) pl.num_rt = 1;
-  pl.tiles = (int)(EPI == kEpiSwiGLU ? (n / 2) / (kTileN / 2) : n / kTileN);
   pl.num_kb = (int)(k / kBK);
   const int clusters = pl.tiles * pl.num_rt;
   int best = 1;
