@@ -205,7 +205,7 @@ def time_kernel(fn, iters: int) -> float:
     return e0.elapsed_time(e1) / 1000.0 / iters
 
 
-def kernel_table(runner, iters: int = 50) -> list[dict]:
+def kernel_table(runner, iters: int = 50, only: str | None = None) -> list[dict]:
     """Steady-state device time of every distinct launch of the step (each replayed
     `iters` times back to back from a CUDA graph, CUDA events), with algorithmic bytes."""
     from omni_b200 import ops
@@ -222,6 +222,8 @@ def kernel_table(runner, iters: int = 50) -> list[dict]:
     rows_out = []
 
     def add(name, fn, nbytes, count_per_step):
+        if only is not None and only not in name:
+            return
         sec = time_kernel(fn, iters)
         rows_out.append({"kernel": name, "us": sec * 1e6, "bytes": nbytes, "gbs": nbytes / sec / 1e9,
                          "per_step": count_per_step})
@@ -239,8 +241,17 @@ def kernel_table(runner, iters: int = 50) -> list[dict]:
         qkv=qkv_geo), wb(fw["qkv"]), L)
     seq_now = runner.seq_lens[:B].cpu().numpy()
     kv_bytes = float(seq_now.sum()) * cfg.num_key_value_heads * cfg.head_dim * 2 * 2
+    # each timed launch reads another layer's KV pool (as the step does), so the
+    # KV of a launch is not resident in L2 from the previous one
+    layer_cycle = {"i": 0}
+
+    def next_layer_kv():
+        li = layer_cycle["i"] % L
+        layer_cycle["i"] += 1
+        return runner.kv.k_buffer[li], runner.kv.v_buffer[li]
+
     add("talker paged attention", lambda: ops.paged_decode_attention(
-        t.q[:B], kc, vc, page_indptr=fb.page_indptr, page_indices=fb.page_indices, seq_lens=fb.seq_lens,
+        t.q[:B], *next_layer_kv(), page_indptr=fb.page_indptr, page_indices=fb.page_indices, seq_lens=fb.seq_lens,
         work_indptr=fb.work_indptr, num_q_heads=cfg.num_attention_heads, num_kv_heads=cfg.num_key_value_heads,
         head_dim=cfg.head_dim, page_size=cfg.page_size, pages_per_chunk=fb.pages_per_chunk,
         work_capacity=fb.work_capacity, sm_scale=t.scale, out=t.attn[:B], workspace=t.attn_workspace), kv_bytes, L)
@@ -336,6 +347,7 @@ def main() -> None:
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kernels", action="store_true", help="print the per-kernel time table and exit")
+    ap.add_argument("--only", default=None, help="with --kernels: only the rows whose name contains this text")
     ap.add_argument("--config", type=int, default=1, choices=[1, 3],
                     help="1: dense talker, 64 streams (the headline); 3: MoE talker with FP8 experts, 256 streams")
     args = ap.parse_args()
@@ -382,9 +394,9 @@ def main() -> None:
     if args.kernels:
         runner.step(use_graph=False)
         torch.cuda.synchronize()
-        table = kernel_table(runner)
+        table = kernel_table(runner, only=args.only)
         if rank == 0:
-            tot = sum(r["us"] * r["per_step"] for r in table)
+            tot = max(1e-9, sum(r["us"] * r["per_step"] for r in table))
             for r in table:
                 print(f'{r["kernel"]:34s} {r["us"]:8.2f} us  x{r["per_step"]:3d}/step  {r["gbs"]:8.1f} GB/s  '
                       f'{100 * r["us"] * r["per_step"] / tot:5.1f}% of kernel time')
@@ -439,8 +451,15 @@ def main() -> None:
                      num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim, page_size=P,
                      pages_per_chunk=fb.pages_per_chunk, work_capacity=fb.work_capacity, sm_scale=t.scale,
                      out=t.attn[:STREAMS], workspace=t.attn_workspace)
-    kc, vc = runner.kv.k_buffer[0], runner.kv.v_buffer[0]
-    attn_s = time_kernel(lambda: ops.paged_decode_attention(t.q[:STREAMS], kc, vc, **attn_args), 50)
+    # 20 layers' KV pools in turn (each ~37 MB; together far beyond L2), as in the step
+    cyc = {"i": 0}
+
+    def attn_next():
+        li = cyc["i"] % cfg.num_hidden_layers
+        cyc["i"] += 1
+        ops.paged_decode_attention(t.q[:STREAMS], runner.kv.k_buffer[li], runner.kv.v_buffer[li], **attn_args)
+
+    attn_s = time_kernel(attn_next, 60)
     seq_now = runner.seq_lens[:STREAMS].cpu().numpy()
     attn_bytes = float(seq_now.sum()) * cfg.num_key_value_heads * cfg.head_dim * 2 * 2 \
         + STREAMS * cfg.num_attention_heads * cfg.head_dim * 2 * 2

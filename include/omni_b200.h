@@ -353,7 +353,7 @@ OMNI_API int omni_moe_rmsnorm_quant(const void* h, int64_t h_stride, const float
                                     int64_t ss_stride, const void* gain, float eps, int64_t rows, int32_t hidden,
                                     void* x, int64_t x_stride, void* xq, float* xs, void* stream);
 
-/* Work-list capacity (chunks of <= 64 rows) for tokens x top_k pairs. */
+/* Work-list capacity (chunks of <= 32 rows) for tokens x top_k pairs. */
 OMNI_API int64_t omni_moe_chunk_capacity(int64_t tokens, int32_t top_k, int32_t experts);
 
 /* moe_align_block_size + the activation permute of FusedMoE: pairs (t, k)

@@ -4,8 +4,9 @@
 //   RadixAttention decode, thinker_model.py:373-379).  One work item is
 //   (request row, chunk of up to `pages_per_chunk` pages) x one KV head; the
 //   work list is built once per step by the packing kernel and shared by every
-//   layer.  Each warp streams whole pages (16 tokens x head_dim, K and V) with
-//   16-byte cp.async into a swizzled double buffer and runs
+//   layer.  The 4 warps of a CTA take the item's pages in turn; each warp
+//   streams whole pages (16 tokens x head_dim, K and V) with 16-byte cp.async
+//   into a swizzled double buffer and runs
 //   S = Q K^T and O += P V on mma.sync m16n8k16 (the 8 query heads of the
 //   group in the M tile), with an online base-2 softmax.  Warps combine in
 //   shared memory; chunks of one row are merged by the last CTA of the row to
@@ -29,6 +30,7 @@ constexpr int kPage = 16;
 constexpr int kD = 128;       // head_dim of the talker
 constexpr int kGroup = 8;     // query heads per KV head
 constexpr int kPageBytes = kPage * kD * 2;  // one head's K (or V) page: 4 KB
+constexpr int kMaxRowsInSmem = 1024;
 
 OMNI_DEVINL void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
@@ -81,25 +83,31 @@ struct PagedAttnParams {
 __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_attention_kernel(const __grid_constant__ PagedAttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_last;
+  __shared__ int s_work[kMaxRowsInSmem + 1];  // work_indptr, when the batch fits
   griddep_wait();
   griddep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int h = blockIdx.y;
-  const int num_work = p.work_indptr[p.rows];
+  const bool work_in_smem = p.rows <= kMaxRowsInSmem;
+  if (work_in_smem)
+    for (int i = threadIdx.x; i <= p.rows; i += blockDim.x) s_work[i] = p.work_indptr[i];
+  __syncthreads();
+  const int* work = work_in_smem ? s_work : p.work_indptr;
+  const int num_work = work[p.rows];
   uint8_t* wbuf = smem + warp * (2 * 2 * kPageBytes);  // [stage][K|V][4 KB]
 
   for (int it = blockIdx.x; it < num_work; it += gridDim.x) {
-    // row of this item: last b with work_indptr[b] <= it
+    // row of this item: last b with work_indptr[b] <= it (a search in shared memory)
     int lo = 0, hi = p.rows - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if (p.work_indptr[mid] <= it) lo = mid;
+      if (work[mid] <= it) lo = mid;
       else hi = mid - 1;
     }
     const int b = lo;
-    const int c = it - p.work_indptr[b];
-    const int nchunks = p.work_indptr[b + 1] - p.work_indptr[b];
+    const int c = it - work[b];
+    const int nchunks = work[b + 1] - work[b];
     const int pg_begin = p.page_indptr[b];
     const int p0 = pg_begin + c * p.pages_per_chunk;
     const int p1 = min(p0 + p.pages_per_chunk, p.page_indptr[b + 1]);
@@ -118,8 +126,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_attention_kernel
     for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
     float m = -INFINITY, l = 0.0f;
 
+    // the item's page ids, one per lane (all loads in flight together)
+    const int pid_lane = p0 + lane < p1 ? p.page_indices[p0 + lane] : 0;
     auto issue = [&](int pg, int stage) {
-      const int64_t page = p.page_indices[pg];
+      const int64_t page = pg - p0 < 32 ? __shfl_sync(0xFFFFFFFFu, pid_lane, pg - p0) : p.page_indices[pg];
       const uint16_t* kbase = p.k_cache + (page * kPage * p.hkv + h) * kD;
       const uint16_t* vbase = p.v_cache + (page * kPage * p.hkv + h) * kD;
       uint8_t* kd = wbuf + stage * 2 * kPageBytes;
@@ -228,7 +238,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_attention_kernel
       wo[(warp * kGroup + g) * kD + 8 * n + 2 * t + 1] = o[n][1];
     }
     __syncthreads();
-    {
+    if (threadIdx.x < kGroup * 16) {
       const int hg = threadIdx.x >> 4;          // head within group
       const int d0 = (threadIdx.x & 15) * 8;    // 8 dims
       float M = -INFINITY;
@@ -267,22 +277,22 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_attention_kernel
         if (s_last) *ctr = 0;
       }
       __syncthreads();
-      if (s_last) {
+      if (s_last && threadIdx.x < kGroup * 16) {
         __threadfence();
         const int hg = threadIdx.x >> 4;
         const int d0 = (threadIdx.x & 15) * 8;
-        const int w0 = p.work_indptr[b];
+        const int w0 = work[b];
         float M = -INFINITY;
         for (int cc = 0; cc < nchunks; ++cc)
           M = fmaxf(M, __ldcg(p.part_lse + ((int64_t)(w0 + cc) * p.hkv + h) * kGroup + hg));
         float W = 0.0f, acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        // chunks in batches of 4 with every load of a batch in flight before the sums,
+        // chunks in batches of 8 with every load of a batch in flight before the sums,
         // summed in chunk order
-        for (int c0 = 0; c0 < nchunks; c0 += 4) {
-          float lse[4];
-          float4 lo[4], hi[4];
+        for (int c0 = 0; c0 < nchunks; c0 += 8) {
+          float lse[8];
+          float4 lo[8], hi[8];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < 8; ++u) {
             if (c0 + u < nchunks) {
               const int64_t base = ((int64_t)(w0 + c0 + u) * p.hkv + h) * kGroup + hg;
               lse[u] = __ldcg(p.part_lse + base);
@@ -292,7 +302,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_attention_kernel
             }
           }
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < 8; ++u) {
             if (c0 + u < nchunks) {
               const float wgt = lse[u] == -INFINITY ? 0.0f : exp2f(lse[u] - M);
               W += wgt;
@@ -474,7 +484,14 @@ extern "C" OMNI_API int omni_paged_decode_attention(const void* q, int64_t q_str
     if (e != cudaSuccess) return check_launch(e);
     attr = true;
   }
-  int gx = grid_ctas > 0 ? grid_ctas : 296;
+  // two CTAs per SM along the work list (x), one grid row per KV head (y)
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0, v = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    sms = v;
+  }
+  int gx = grid_ctas > 0 ? grid_ctas : 2 * sms;
   if (gx > work_capacity) gx = (int)work_capacity;
   if (gx < 1) gx = 1;
   return check_launch(launch(paged_decode_attention_kernel, dim3((unsigned)gx, (unsigned)num_kv_heads),

@@ -14,7 +14,8 @@
 //                   gathered into that order
 //   grouped GEMMs   persistent tcgen05 kind::f8f6f4 kernels over the work
 //                   list: gate/up (two accumulators, SwiGLU, e4m3 re-quant of
-//                   the activation) and down (bf16 rows per pair)
+//                   the activation) and down (bf16 rows per pair), over
+//                   work items of <= 32 rows of one expert
 //   combine         h += bf16(bf16(sum_k w_k y_k) + bf16(shared * sigmoid(g)))
 //                   and the residual stream's per-128-feature sums of squares
 //
@@ -36,9 +37,9 @@ namespace {
 OMNI_DEFINE_STATUS(moe)
 
 constexpr int kBlk = 128;       // quantisation group = K-block = feature tile
-constexpr int kChunk = 64;      // activation rows per work item (MMA N <= 64)
+constexpr int kChunk = 32;      // activation rows per work item (MMA N <= 32)
 constexpr int kMaxKBlocks = 8;  // K <= 1024 for the gate/up GEMM
-constexpr int kGroupedThreads = 192;
+constexpr int kGroupedThreads = 320;
 constexpr int kMaxStagesG = 8;
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTokens = 1024;
@@ -51,10 +52,6 @@ OMNI_DEVINL uint16_t e4m3x2(float lo, float hi) {
   return r;
 }
 
-OMNI_DEVINL float silu_f(float g) { return g / (1.0f + expf(-g)); }
-
-OMNI_DEVINL void named_sync(int id, int threads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory"); }
-
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::f8f6f4 (e4m3 inputs, fp32 accumulate).
 OMNI_DEVINL void tc_mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
   asm volatile(
@@ -64,6 +61,16 @@ OMNI_DEVINL void tc_mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
       : "memory");
 }
+// Bounded mbarrier wait that also gives up as soon as another role of the CTA
+// has raised the abort flag.
+OMNI_DEVINL bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 255 && *abort_flag) return false;
+  }
+  return false;
+}
+
 // kind::f8f6f4 instruction descriptor: A = B = e4m3 (format 0), D = f32, K-major.
 __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -130,7 +137,7 @@ __global__ void __launch_bounds__(128) rmsnorm_quant_kernel(const uint16_t* __re
 // CTA rebuilds the expert membership bitmaps from topk_ids in shared memory
 // (tokens x experts bits) and gathers the e4m3 rows and scales of its own
 // tokens into their rows; CTA 0 also writes the expert offsets and the work
-// list of row chunks (expert, first row, rows <= 64).
+// list of row chunks (expert, first row, rows <= 32).
 // ---------------------------------------------------------------------------
 struct AlignParams {
   const int32_t* topk_ids;
@@ -253,8 +260,11 @@ __global__ void __launch_bounds__(1024) moe_align_gather_kernel(const __grid_con
 //   mode 1 (down):     W = w2 [E][N][K]; work item = (chunk, tile < N/128);
 //     output y [rows][N] bf16.
 //
-// Roles (192 threads): warp 0 lane 0 = TMA producer, warp 1 lane 0 = MMA
-// issuer, warps 2-5 = epilogue (TMEM lane quarter = warp % 4).
+// Roles (320 threads): warp 0 lane 0 = TMA producer, warp 1 lane 0 = MMA
+// issuer, warps 2-5 and 6-9 = two epilogue groups (TMEM lane quarter = warp %
+// 4) taking the CTA's work items alternately, so that one group's closing
+// epilogue (SwiGLU, re-quantisation, stores) overlaps the other group's
+// accumulation of the next item.  Only the chunk's row columns are read.
 // ---------------------------------------------------------------------------
 struct GroupedParams {
   int mode;
@@ -291,13 +301,18 @@ __global__ void __launch_bounds__(kGroupedThreads, 1)
   const int NS = p.slots;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* stage_base = smem;
-  uint16_t* act = reinterpret_cast<uint16_t*>(smem + ST * kStageBytes);            // [64][128] bf16 (mode 0)
-  float* sa = reinterpret_cast<float*>(smem + ST * kStageBytes + kChunk * kBlk * 2);  // [kMaxKBlocks][64]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sa + kMaxKBlocks * kChunk);
+  // per epilogue group: act [64][128] bf16 (mode 0) and the chunk's activation scales [kb][64]
+  uint16_t* act_all = reinterpret_cast<uint16_t*>(smem + ST * kStageBytes);
+  float* sa_all = reinterpret_cast<float*>(smem + ST * kStageBytes + 2 * kChunk * kBlk * 2);
+  // barriers: smem stages full/empty; TMEM slots full (one set per epilogue group, so
+  // that each group waits on every phase of its own barriers) and empty; per group
+  // "scales ready", "activation staged" and "item done" (128 arrivals each)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sa_all + 2 * kMaxKBlocks * kChunk);
   uint64_t* empty = full + kMaxStagesG;
-  uint64_t* tfull = empty + kMaxStagesG;
-  uint64_t* tempty = tfull + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 8);
+  uint64_t* tfull = empty + kMaxStagesG;  // [2][8]
+  uint64_t* tempty = tfull + 16;          // [8]
+  uint64_t* gbar = tempty + 8;            // [2][3]: sa ready, act staged, item done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbar + 6);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   if (threadIdx.x == 0) {
@@ -307,8 +322,10 @@ __global__ void __launch_bounds__(kGroupedThreads, 1)
     }
     for (int s = 0; s < NS; ++s) {
       mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], 4);  // one arrive per epilogue warp
+      mbar_init(&tfull[8 + s], 1);
+      mbar_init(&tempty[s], 4);  // one arrive per warp of the consuming group
     }
+    for (int b = 0; b < 6; ++b) mbar_init(&gbar[b], 128);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmap_w);
@@ -337,7 +354,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1)
         const int wrow = c.x * p.w_rows + tile * kBlk;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % ST;
-          if (it >= ST && !mbar_wait(&empty[s], ((it / ST) - 1) & 1)) {
+          if (it >= ST && !mbar_wait_or_abort(&empty[s], ((it / ST) - 1) & 1, abort_flag)) {
             report_status(kDevTimeoutMma);
             *abort_flag = 1;
             break;
@@ -352,15 +369,16 @@ __global__ void __launch_bounds__(kGroupedThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      int it = 0, bt = 0;
-      for (int w = blockIdx.x; w < n_items && !*abort_flag; w += gridDim.x) {
+      int it = 0, bt = 0, li = 0;
+      for (int w = blockIdx.x; w < n_items && !*abort_flag; w += gridDim.x, ++li) {
         const int4 c = p.chunks[w / p.tiles];
         const int N = (c.z + 15) & ~15;
         const uint32_t idesc = idesc_e4m3_f32(kBlk, N);
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb, ++it, ++bt) {
           const int s = it % ST, ts = bt % NS;
-          if (!mbar_wait(&full[s], (it / ST) & 1) || (bt >= NS && !mbar_wait(&tempty[ts], ((bt / NS) - 1) & 1))) {
+          if (!mbar_wait_or_abort(&full[s], (it / ST) & 1, abort_flag) ||
+              (bt >= NS && !mbar_wait_or_abort(&tempty[ts], ((bt / NS) - 1) & 1, abort_flag))) {
             report_status(kDevTimeoutTma);
             *abort_flag = 1;
             ok = false;
@@ -380,66 +398,96 @@ __global__ void __launch_bounds__(kGroupedThreads, 1)
               tc_mma_f8(d0 + kChunk, au + 2 * kk, bd + 2 * kk, idesc, kk > 0 ? 1u : 0u);
           }
           tc_commit(&empty[s]);
-          tc_commit(&tfull[ts]);
+          tc_commit(&tfull[(li & 1) * 8 + ts]);
         }
         if (!ok) break;
       }
     }
   } else {
-    // epilogue warps: TMEM lane quarter q = warp % 4, feature f = 32 q + lane of the tile
+    // epilogue group gi takes the CTA's items gi, gi + 2, ...; TMEM lane quarter q =
+    // warp % 4, feature f = 32 q + lane of the tile
+    const int gi = (warp - 2) >> 2;
     const int q = warp & 3;
     const int f = q * 32 + lane;
-    const int et = threadIdx.x - 64;  // 0..127
+    const int et = ((warp - 2) & 3) * 32 + lane;  // 0..127 within the group
+    uint16_t* act = act_all + gi * kChunk * kBlk;
+    float* sa = sa_all + gi * kMaxKBlocks * kChunk;
+    uint64_t* g_sa = &gbar[3 * gi];
+    uint64_t* g_act = &gbar[3 * gi + 1];
+    uint64_t* g_done = &gbar[3 * gi + 2];
+    uint64_t* my_tfull = &tfull[8 * gi];
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    int bt = 0;
-    for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
+    // bounded group-wide wait; on timeout every later wait of this thread is skipped
+    auto gwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+      if (*abort_flag) return false;
+      if (mbar_wait_or_abort(bar, parity, abort_flag)) return true;
+      report_status(kDevTimeoutFlag);
+      *abort_flag = 1;
+      return false;
+    };
+    // completed phases of this group's TMEM-full barriers, one bit per slot: the slot
+    // of a block depends on the CTA-wide block index, so a group's uses of a slot are
+    // counted here rather than derived from its own item count
+    uint32_t tphase = 0;
+    for (int li = gi; blockIdx.x + li * gridDim.x < n_items; li += 2) {
+      const int w = blockIdx.x + li * gridDim.x;
+      const int k = li >> 1;  // this group's item count so far
+      // the group's previous item has finished reading sa and act
+      if (k > 0 && !gwait(g_done, (k - 1) & 1)) break;
       const int4 c = p.chunks[w / p.tiles];
       const int tile = w % p.tiles;
       const int e = c.x, r0 = c.y, nr = c.z;
+      const int N = (nr + 15) & ~15;
       // per-row activation scales of the chunk, [kb][row]
       for (int i = et; i < KB * kChunk; i += 128) {
-        const int kb = i / kChunk, j = i % kChunk;
-        sa[kb * kChunk + j] = j < nr ? p.a_scale[(int64_t)(r0 + j) * KB + kb] : 0.0f;
+        const int kb = i / kChunk, jr = i % kChunk;
+        sa[kb * kChunk + jr] = jr < nr ? p.a_scale[(int64_t)(r0 + jr) * KB + kb] : 0.0f;
       }
       const float* swg = p.w_scale + ((int64_t)e * wtile_rows + tile) * KB;
       const float* swu = p.w_scale + ((int64_t)e * wtile_rows + p.half / kBlk + tile) * KB;
-      named_sync(1, 128);
+      mbar_arrive(g_sa);
+      if (!gwait(g_sa, k & 1)) break;
       float accg[kChunk], accu[MODE == 0 ? kChunk : 1];
 #pragma unroll
-      for (int j = 0; j < kChunk; ++j) accg[j] = 0.0f;
+      for (int jj = 0; jj < kChunk; ++jj) accg[jj] = 0.0f;
 #pragma unroll
-      for (int j = 0; j < (MODE == 0 ? kChunk : 1); ++j) accu[j] = 0.0f;
+      for (int jj = 0; jj < (MODE == 0 ? kChunk : 1); ++jj) accu[jj] = 0.0f;
       bool ok = true;
-      for (int kb = 0; kb < KB; ++kb, ++bt) {
-        const int ts = bt % NS;
+      for (int kb = 0; kb < KB; ++kb) {
+        const int bt = li * KB + kb, ts = bt % NS;
         const float wg = swg[kb], wu = MODE == 0 ? swu[kb] : 0.0f;
-        if (!mbar_wait(&tfull[ts], (bt / NS) & 1)) {
-          report_status(kDevTimeoutMma);
-          *abort_flag = 1;
+        // the group's blocks in slot ts complete my_tfull[ts] once each, in order: the
+        // MMA refills a slot only after its previous block has been drained
+        if (!gwait(&my_tfull[ts], (tphase >> ts) & 1u)) {
           ok = false;
           break;
         }
+        tphase ^= 1u << ts;
         tc_fence_after();
         const uint32_t base = tmem + lane_off + (uint32_t)(ts * p.slot_cols);
         uint32_t r[32];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          tmem_ld_32x32b_x32(base + (uint32_t)(32 * h), r);
-          tc_wait_ld();
+        for (int h = 0; h < kChunk / 32; ++h) {
+          if (32 * h < N) {
+            tmem_ld_32x32b_x32(base + (uint32_t)(32 * h), r);
+            tc_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            accg[32 * h + j] = __fmaf_rn(__uint_as_float(r[j]), wg * sa[kb * kChunk + 32 * h + j],
-                                         accg[32 * h + j]);
+            for (int jj = 0; jj < 32; ++jj)
+              accg[32 * h + jj] = __fmaf_rn(__uint_as_float(r[jj]), wg * sa[kb * kChunk + 32 * h + jj],
+                                            accg[32 * h + jj]);
+          }
         }
         if (MODE == 0) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            tmem_ld_32x32b_x32(base + (uint32_t)(kChunk + 32 * h), r);
-            tc_wait_ld();
+          for (int h = 0; h < kChunk / 32; ++h) {
+            if (32 * h < N) {
+              tmem_ld_32x32b_x32(base + (uint32_t)(kChunk + 32 * h), r);
+              tc_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              accu[32 * h + j] = __fmaf_rn(__uint_as_float(r[j]), wu * sa[kb * kChunk + 32 * h + j],
-                                           accu[32 * h + j]);
+              for (int jj = 0; jj < 32; ++jj)
+                accu[32 * h + jj] = __fmaf_rn(__uint_as_float(r[jj]), wu * sa[kb * kChunk + 32 * h + jj],
+                                              accu[32 * h + jj]);
+            }
           }
         }
         tc_fence_before();
@@ -450,14 +498,17 @@ __global__ void __launch_bounds__(kGroupedThreads, 1)
       if (MODE == 0) {
         // act = bf16(silu(bf16(g)) * bf16(u)), staged [row][feature] for the per-row quantisation
 #pragma unroll
-        for (int j = 0; j < kChunk; ++j) {
-          const float g = bf2f(f2bf(accg[j])), u = bf2f(f2bf(accu[j]));
-          act[j * kBlk + f] = f2bf(silu_f(g) * u);
+        for (int jj = 0; jj < kChunk; ++jj) {
+          if (jj < nr) {
+            const float g = bf2f(f2bf(accg[jj])), u = bf2f(f2bf(accu[jj]));
+            act[jj * kBlk + f] = f2bf(__fdividef(g, 1.0f + __expf(-g)) * u);
+          }
         }
-        named_sync(1, 128);
-        // warp q' = et / 32 quantises rows q', q' + 4, ...: lane l holds features 4l..4l+3
-        for (int j = et >> 5; j < nr; j += 4) {
-          const uint2 a2 = *reinterpret_cast<const uint2*>(act + j * kBlk + 4 * lane);
+        mbar_arrive(g_act);
+        if (!gwait(g_act, k & 1)) break;
+        // warp et / 32 of the group quantises rows et / 32, + 4, ...: lane l holds features 4l..4l+3
+        for (int jr = et >> 5; jr < nr; jr += 4) {
+          const uint2 a2 = *reinterpret_cast<const uint2*>(act + jr * kBlk + 4 * lane);
           const float v[4] = {bf_lo(a2.x), bf_hi(a2.x), bf_lo(a2.y), bf_hi(a2.y)};
           float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
 #pragma unroll
@@ -465,16 +516,16 @@ __global__ void __launch_bounds__(kGroupedThreads, 1)
           const float sc = __fdiv_rn(fmaxf(amax, 1e-10f), 448.0f);
           const uint32_t lo = e4m3x2(__fdiv_rn(v[0], sc), __fdiv_rn(v[1], sc));
           const uint32_t hi = e4m3x2(__fdiv_rn(v[2], sc), __fdiv_rn(v[3], sc));
-          *reinterpret_cast<uint32_t*>(p.out_q + (int64_t)(r0 + j) * p.out_cols + tile * kBlk + 4 * lane) =
+          *reinterpret_cast<uint32_t*>(p.out_q + (int64_t)(r0 + jr) * p.out_cols + tile * kBlk + 4 * lane) =
               lo | (hi << 16);
-          if (lane == 0) p.out_s[(int64_t)(r0 + j) * (p.out_cols / kBlk) + tile] = sc;
+          if (lane == 0) p.out_s[(int64_t)(r0 + jr) * (p.out_cols / kBlk) + tile] = sc;
         }
-        named_sync(1, 128);  // act and sa are rewritten by the next item
+        mbar_arrive(g_done);  // act and sa are rewritten by this group's next item
       } else {
 #pragma unroll
-        for (int j = 0; j < kChunk; ++j)
-          if (j < nr) p.y[(int64_t)(r0 + j) * p.y_stride + tile * kBlk + f] = f2bf(accg[j]);
-        named_sync(1, 128);  // sa is rewritten by the next item
+        for (int jj = 0; jj < kChunk; ++jj)
+          if (jj < nr) p.y[(int64_t)(r0 + jj) * p.y_stride + tile * kBlk + f] = f2bf(accg[jj]);
+        mbar_arrive(g_done);  // sa is rewritten by this group's next item
       }
     }
   }
@@ -612,7 +663,8 @@ int launch_grouped(const void* a_q, int64_t rows_cap, int64_t k, const void* w, 
   if (!make_tmap_u8(&tw, w, experts * w_rows, k, kBlk) || !make_tmap_u8(&ta, a_q, rows_cap, k, kChunk))
     return set_error(OMNI_ERR_UNSUPPORTED, "tensor map encoding failed");
   const size_t stage_bytes = (MODE == 0 ? 2 : 1) * kBlk * kBlk + kChunk * kBlk;
-  const size_t fixed = 1024 + (size_t)kChunk * kBlk * 2 + kMaxKBlocks * kChunk * 4 + (2 * kMaxStagesG + 16) * 8 + 16;
+  const size_t fixed =
+      1024 + 2 * ((size_t)kChunk * kBlk * 2 + kMaxKBlocks * kChunk * 4) + (2 * kMaxStagesG + 16 + 8 + 6) * 8 + 16;
   int st = kMaxStagesG;
   while (st > 2 && fixed + st * stage_bytes > 227 * 1024) --st;
   gp.stages = st;

@@ -48,7 +48,7 @@ class GenerationBatchResult:
 
 class TalkerDecodeRunner:
     def __init__(self, cfg: TalkerConfig, *, max_batch: int, num_pages: int, seed: int = 0, device="cuda",
-                 pages_per_chunk: int = 16, weights: dict | None = None, predictor_weights: dict | None = None):
+                 pages_per_chunk: int = 32, weights: dict | None = None, predictor_weights: dict | None = None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.max_batch = max_batch

@@ -108,7 +108,7 @@ def test_align_gather_bit_exact(tokens, skew):
     cfg, w, blk, h, gain, ss = make_block(tokens, seed=2)
     rng = np.random.default_rng(tokens)
     E, k = cfg.num_experts, cfg.num_experts_per_tok
-    if skew:  # every token picks experts 0..7: one expert holds 256 rows (4 chunks)
+    if skew:  # every token picks experts 0..7: each of them holds 256 rows (8 chunks of 32)
         ids_np = np.tile(np.arange(k, dtype=np.int32), (tokens, 1))
     else:
         ids_np = np.stack([rng.permutation(E)[:k] for _ in range(tokens)]).astype(np.int32)
@@ -130,7 +130,7 @@ def test_align_gather_bit_exact(tokens, skew):
     n = int(blk.n_chunks.item())
     ch = blk.chunks[:n].cpu().numpy()
     cnt = np.diff(offsets)
-    want_ch = [(e, offsets[e] + c * 64, min(64, cnt[e] - c * 64)) for e in range(E) for c in range((cnt[e] + 63) // 64)]
+    want_ch = [(e, offsets[e] + c * 32, min(32, cnt[e] - c * 32)) for e in range(E) for c in range((cnt[e] + 31) // 32)]
     assert [tuple(r[:3]) for r in ch] == want_ch
 
 
