@@ -38,6 +38,12 @@ sys.path.insert(0, str(ROOT / "sglang-omni_b200"))
 sys.path.insert(0, str(ROOT))
 
 METRIC = "codec frames/s per GPU (ragged talker+codebook decode step); p50 step µs"
+# DRAM traffic of the roofline kernels per algorithmic byte, from one ncu capture of the
+# same kernel on the same workload (dram__bytes_read.sum + dram__bytes_write.sum over the
+# algorithmic bytes of the captured launch; see profiles/).  The bench scales it to the
+# timed launch by its algorithmic bytes (the traffic grows with the rows / tokens processed).
+GEMM_TRAFFIC_RATIO: dict[int, float] = {1: 6_883_840 / (1024 * 3072 * 2 + 64 * 3072 * 2 + 2 * 64 * 1024 * 2 + 8 * 64 * 4)}
+ATTN_TRAFFIC_RATIO: dict[int, float] = {1: (37_133_312 + 16_384) / (35_473 * 1024 + 64 * 16 * 128 * 2 * 2)}
 UNIT = "frames/s"
 STREAMS = 64
 
@@ -207,7 +213,10 @@ def time_kernel(fn, iters: int) -> float:
 
 def kernel_table(runner, iters: int = 50, only: str | None = None) -> list[dict]:
     """Steady-state device time of every distinct launch of the step (each replayed
-    `iters` times back to back from a CUDA graph, CUDA events), with algorithmic bytes."""
+    `iters` times back to back from a CUDA graph, CUDA events), with algorithmic bytes.
+    Launches of one row cycle through the layers (the talker's 20, the predictor's 5),
+    as the step does, so a launch does not find its weights or KV left in L2 by the
+    previous launch of the same row."""
     from omni_b200 import ops
     from omni_b200.sampling_kernels import predictor_sample_step
 
@@ -229,6 +238,17 @@ def kernel_table(runner, iters: int = 50, only: str | None = None) -> list[dict]
                          "per_step": count_per_step})
 
     wb = lambda w: w.numel() * 2  # noqa: E731
+
+    class Cycle:
+        def __init__(self, n):
+            self.n, self.i = n, 0
+
+        def __call__(self):
+            v = self.i % self.n
+            self.i += 1
+            return v
+
+    tl = Cycle(L)  # talker layer of the next launch
     lw, fw = t.w["layers"][0], t.folded[0]
     kc, vc = runner.kv.k_buffer[0], runner.kv.v_buffer[0]
     qkv_geo = dict(num_q_heads=cfg.num_attention_heads, num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
@@ -237,7 +257,7 @@ def kernel_table(runner, iters: int = 50, only: str | None = None) -> list[dict]
     add("talker input add+sumsq", lambda: ops.add_sumsq(p.output_embeds[:B], runner.text_embeds[:B], t.h[:B], t.ss[0]),
         3 * B * H * 2, 1)
     add("talker qkv gemm (+norm,rope,kv)", lambda: ops.linear_fused(
-        t.h[:B], fw["qkv"], t.q[:B], epilogue=ops.EPI_QKV_ROPE, ss_in=t.ss, ss_in_parts=8, norm_eps=eps,
+        t.h[:B], t.folded[tl()]["qkv"], t.q[:B], epilogue=ops.EPI_QKV_ROPE, ss_in=t.ss, ss_in_parts=8, norm_eps=eps,
         qkv=qkv_geo), wb(fw["qkv"]), L)
     seq_now = runner.seq_lens[:B].cpu().numpy()
     kv_bytes = float(seq_now.sum()) * cfg.num_key_value_heads * cfg.head_dim * 2 * 2
@@ -256,15 +276,15 @@ def kernel_table(runner, iters: int = 50, only: str | None = None) -> list[dict]
         head_dim=cfg.head_dim, page_size=cfg.page_size, pages_per_chunk=fb.pages_per_chunk,
         work_capacity=fb.work_capacity, sm_scale=t.scale, out=t.attn[:B], workspace=t.attn_workspace), kv_bytes, L)
     add("talker o_proj gemm (+res,ss)", lambda: ops.linear_fused(
-        t.attn[:B], lw["o_proj"], t.h[:B], epilogue=ops.EPI_RESIDUAL, residual=t.h[:B], ss_out=t.ss),
-        wb(lw["o_proj"]), L)
+        t.attn[:B], t.w["layers"][tl()]["o_proj"], t.h[:B], epilogue=ops.EPI_RESIDUAL, residual=t.h[:B],
+        ss_out=t.ss), wb(lw["o_proj"]), L)
     if cfg.moe is None:
         add("talker gate_up gemm (+norm,swiglu)", lambda: ops.linear_fused(
-            t.h[:B], fw["gate_up"], t.act[:B], epilogue=ops.EPI_SWIGLU, ss_in=t.ss, ss_in_parts=8, norm_eps=eps),
-            wb(fw["gate_up"]), L)
+            t.h[:B], t.folded[tl()]["gate_up"], t.act[:B], epilogue=ops.EPI_SWIGLU, ss_in=t.ss, ss_in_parts=8,
+            norm_eps=eps), wb(fw["gate_up"]), L)
         add("talker down gemm (+res,ss)", lambda: ops.linear_fused(
-            t.act[:B], lw["down_proj"], t.h[:B], epilogue=ops.EPI_RESIDUAL, residual=t.h[:B], ss_out=t.ss),
-            wb(lw["down_proj"]), L)
+            t.act[:B], t.w["layers"][tl()]["down_proj"], t.h[:B], epilogue=ops.EPI_RESIDUAL, residual=t.h[:B],
+            ss_out=t.ss), wb(lw["down_proj"]), L)
     else:
         m, mw, mc = t.moe, lw["moe"], cfg.moe
         E, k = mc.num_experts, mc.num_experts_per_tok
@@ -303,30 +323,32 @@ def kernel_table(runner, iters: int = 50, only: str | None = None) -> list[dict]
     add("layer0 sampler", lambda: t.sample_decode_tokens(t.logits[:B], fb), B * cfg.vocab_size * 4, 1)
     plw, pfw = p.w["layers"][0], p.folded[0]
     n5 = pc.num_hidden_layers
+    pl = Cycle(n5)  # predictor layer of the next launch
+    hl = Cycle(pc.num_code_groups - 1)  # lm_head of the next launch
     for rows, label, per, base in ((2 * B, "pair", 1, 0), (B, "single", pc.num_code_groups - 2, 8)):
         T = rows // B
         geo = dict(num_q_heads=pc.num_attention_heads, num_kv_heads=pc.num_key_value_heads, head_dim=pc.head_dim,
                    q_norm=plw["q_norm"], k_norm=plw["k_norm"], eps=eps, cos_sin=p.cos_sin, tokens_per_req=T,
                    slot_stride=pc.cache_len, slot_base=base, k_cache=p.k_cache[0], v_cache=p.v_cache[0])
         add(f"predictor[{label}] qkv gemm (+norm,rope,kv)", lambda rows=rows, geo=geo: ops.linear_fused(
-            p.h[:rows], pfw["qkv"], p.q[:rows], epilogue=ops.EPI_QKV_ROPE, ss_in=p.ss, ss_in_parts=8, norm_eps=eps,
-            qkv=geo), wb(pfw["qkv"]), per * n5)
+            p.h[:rows], p.folded[pl()]["qkv"], p.q[:rows], epilogue=ops.EPI_QKV_ROPE, ss_in=p.ss, ss_in_parts=8,
+            norm_eps=eps, qkv=geo), wb(pfw["qkv"]), per * n5)
         add(f"predictor[{label}] attention", lambda rows=rows, T=T, base=base: ops.predictor_attention(
             p.q[:rows], p.k_cache[0], p.v_cache[0], num_q_heads=pc.num_attention_heads,
             num_kv_heads=pc.num_key_value_heads, head_dim=pc.head_dim, tokens_per_req=T, slot_stride=pc.cache_len,
             slot_base=base, sm_scale=p.scale, out=p.attn[:rows]),
             rows * (pc.cache_len // 2) * pc.num_key_value_heads * pc.head_dim * 4, per * n5)
         add(f"predictor[{label}] o_proj gemm (+res,ss)", lambda rows=rows: ops.linear_fused(
-            p.attn[:rows], plw["o_proj"], p.h[:rows], epilogue=ops.EPI_RESIDUAL, residual=p.h[:rows], ss_out=p.ss),
-            wb(plw["o_proj"]), per * n5)
+            p.attn[:rows], p.w["layers"][pl()]["o_proj"], p.h[:rows], epilogue=ops.EPI_RESIDUAL,
+            residual=p.h[:rows], ss_out=p.ss), wb(plw["o_proj"]), per * n5)
         add(f"predictor[{label}] gate_up gemm (+norm,swiglu)", lambda rows=rows: ops.linear_fused(
-            p.h[:rows], pfw["gate_up"], p.act[:rows], epilogue=ops.EPI_SWIGLU, ss_in=p.ss, ss_in_parts=8,
-            norm_eps=eps), wb(pfw["gate_up"]), per * n5)
+            p.h[:rows], p.folded[pl()]["gate_up"], p.act[:rows], epilogue=ops.EPI_SWIGLU, ss_in=p.ss,
+            ss_in_parts=8, norm_eps=eps), wb(pfw["gate_up"]), per * n5)
         add(f"predictor[{label}] down gemm (+res,ss)", lambda rows=rows: ops.linear_fused(
-            p.act[:rows], plw["down_proj"], p.h[:rows], epilogue=ops.EPI_RESIDUAL, residual=p.h[:rows],
-            ss_out=p.ss), wb(plw["down_proj"]), per * n5)
+            p.act[:rows], p.w["layers"][pl()]["down_proj"], p.h[:rows], epilogue=ops.EPI_RESIDUAL,
+            residual=p.h[:rows], ss_out=p.ss), wb(plw["down_proj"]), per * n5)
     add("predictor lm_head gemm (+norm)", lambda: ops.linear_fused(
-        p.h[:B], p.lm_head_folded[1], p.logits[1, :B], epilogue=ops.EPI_STORE, ss_in=p.ss, ss_in_parts=8,
+        p.h[:B], p.lm_head_folded[hl()], p.logits[1, :B], epilogue=ops.EPI_STORE, ss_in=p.ss, ss_in_parts=8,
         norm_eps=eps), wb(p.lm_head_folded[1]), pc.num_code_groups - 1)
     add("predictor sample+gather", lambda: predictor_sample_step(
         p.logits[1, :B], temperatures=p.sub_temperature_tensor[:B], top_ks=p.sub_top_k_tensor[:B],
@@ -348,6 +370,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kernels", action="store_true", help="print the per-kernel time table and exit")
     ap.add_argument("--only", default=None, help="with --kernels: only the rows whose name contains this text")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="with --kernels: talker layers to build (0 = the config's 20); for small profiling runs")
     ap.add_argument("--config", type=int, default=1, choices=[1, 3],
                     help="1: dense talker, 64 streams (the headline); 3: MoE talker with FP8 experts, 256 streams")
     args = ap.parse_args()
@@ -382,6 +406,10 @@ def main() -> None:
         cfg, STREAMS = CONFIG3_MOE, 256
     else:
         cfg = CONFIG1_DENSE
+    if args.layers and args.kernels:
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, num_hidden_layers=args.layers)
     W, K = max(3, args.warmup), args.steps
     total_steps = 2 * (W + K) + 4
     lens = context_lengths(STREAMS, seed=rank, headroom=total_steps + 8)
@@ -443,9 +471,27 @@ def main() -> None:
     barrier()
     e2e_ms = t_e0.elapsed_time(t_e1)
 
-    # ---- dominant kernel: paged decode attention of one layer, timed in isolation ----
+    # ---- the dominant kernel (the residual-epilogue GEMM, gemm_kernel<1>: 34.6% of the
+    # step's device time in the launch list) and the paged attention, each timed in
+    # isolation over the 20 layers in turn (weights / KV far beyond L2), as in the step ----
     fb = runner.forward_batch()
     t = runner.talker
+    gcyc = {"i": 0}
+    dense = cfg.moe is None
+    gw = [lw["down_proj"] if dense else lw["o_proj"] for lw in t.w["layers"]]
+    g_in = t.act[:STREAMS] if dense else t.attn[:STREAMS]
+    g_name = ("gemm_kernel<1>: talker down projection + residual + row sums of squares" if dense else
+              "gemm_kernel<1>: talker o_proj + residual + row sums of squares")
+
+    def gemm_next():
+        li = gcyc["i"] % cfg.num_hidden_layers
+        gcyc["i"] += 1
+        ops.linear_fused(g_in, gw[li], t.h[:STREAMS], epilogue=ops.EPI_RESIDUAL, residual=t.h[:STREAMS], ss_out=t.ss)
+
+    gemm_s = time_kernel(gemm_next, 60)
+    gk, gn = g_in.shape[1], gw[0].shape[0]
+    # weights + activations in + residual in + output + per-128-feature sums of squares
+    gemm_bytes = gn * gk * 2 + STREAMS * gk * 2 + 2 * STREAMS * gn * 2 + (gn // 128) * STREAMS * 4
     attn_args = dict(page_indptr=fb.page_indptr, page_indices=fb.page_indices, seq_lens=fb.seq_lens,
                      work_indptr=fb.work_indptr, num_q_heads=cfg.num_attention_heads,
                      num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim, page_size=P,
@@ -478,6 +524,7 @@ def main() -> None:
         value = frames / (total_ms / 1000.0)
         e2e = frames / (e2e_ms / 1000.0)
         achieved = attn_bytes / attn_s / 1e9
+        g_achieved = gemm_bytes / gemm_s / 1e9
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": total_ms / K, "p50_step_us": 1000 * float(np.median(step_ms)),
@@ -494,9 +541,17 @@ def main() -> None:
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": STREAMS * H * 2,
                     "d2h_bytes_per_step": STREAMS * G * 8},
             "gpu_launches": launches_per_step * K,
-            "roofline": {"bound": "hbm", "kernel": "paged_decode_attention_kernel", "achieved": achieved,
-                         "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
-                         "peak_kind": peak_kind},
+            "roofline": {"bound": "hbm", "kernel": g_name, "achieved": g_achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": g_achieved / hbm,
+                         "traffic": (GEMM_TRAFFIC_RATIO[args.config] * gemm_bytes
+                                     if args.config in GEMM_TRAFFIC_RATIO else None),
+                         "algorithmic_bytes": gemm_bytes, "launch_us": gemm_s * 1e6, "peak_kind": peak_kind},
+            "roofline_attention": {"bound": "hbm", "kernel": "paged_decode_attention_kernel", "achieved": achieved,
+                                   "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                                   "traffic": (ATTN_TRAFFIC_RATIO[args.config] * attn_bytes
+                                               if args.config in ATTN_TRAFFIC_RATIO else None),
+                                   "algorithmic_bytes": attn_bytes,
+                                   "launch_us": attn_s * 1e6, "peak_kind": peak_kind},
             "clocks": clocks.summary(),
         }
         if not args.no_cpu and args.config == 1:
