@@ -510,15 +510,10 @@ def main() -> None:
     attn_bytes = float(seq_now.sum()) * cfg.num_key_value_heads * cfg.head_dim * 2 * 2 \
         + STREAMS * cfg.num_attention_heads * cfg.head_dim * 2 * 2
 
-    # ---- gather over ranks ----
-    frames = STREAMS * K
-    stats = torch.tensor([total_ms, e2e_ms, frames], dtype=torch.float64, device=dev)
-    if dist is not None:
-        t_max = stats.clone()
-        dist.all_reduce(t_max[:2], op=dist.ReduceOp.MAX)
-        f_sum = stats[2:].clone()
-        dist.all_reduce(f_sum, op=dist.ReduceOp.SUM)
-        total_ms, e2e_ms, frames = float(t_max[0]), float(t_max[1]), float(f_sum[0])
+    # ---- gather over ranks: max of the device times, sum of the frames ----
+    from omni_b200.replicas import aggregate_step_times
+
+    total_ms, e2e_ms, frames = aggregate_step_times(total_ms, e2e_ms, STREAMS * K, dist, dev)
     if rank == 0:
         hbm, tflops, peak_kind = measured_peaks()
         value = frames / (total_ms / 1000.0)
