@@ -134,8 +134,11 @@ OMNI_DEVINL RowBlock row_block(int rows_here, int S, int q) {
   return b;
 }
 
+// Two CTAs fit on an SM (<= 128 registers a thread) for the epilogues that need no
+// more, so that with programmatic dependent launch the next GEMM's CTAs can start,
+// and stream their weights, beside the CTAs of the current one.
 template <int EPI>
-__global__ void __launch_bounds__(kThreadsG, 1)
+__global__ void __launch_bounds__(kThreadsG, (EPI == kEpiSwiGLU || EPI == kEpiF32) ? 1 : 2)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
