@@ -379,6 +379,10 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        # the CPU arm needs no process group: rank 0 runs and prints, the others exit
+        run_reference_arm(args, rank)
+        return
     dist = None
     if world > 1:
         import datetime
@@ -388,12 +392,6 @@ def main() -> None:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    if args.impl == "reference":
-        run_reference_arm(args, rank)
-        if dist is not None:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
 
     from omni_b200 import _lib, ops
     from omni_b200.config import CONFIG1_DENSE, CONFIG3_MOE
