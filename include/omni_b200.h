@@ -360,7 +360,7 @@ OMNI_API int64_t omni_moe_chunk_capacity(int64_t tokens, int32_t top_k, int32_t 
  * sorted by expert, stable by token; slot_of [tokens, top_k] = row of the pair
  * in the sorted order; expert_offsets [experts + 1]; chunks int4 {expert,
  * first row, rows, 0} [chunk_capacity] and *n_chunks; permuted_q / permuted_s
- * receive the pairs' e4m3 rows and scales.  tokens <= 1024, top_k <= 8,
+ * receive the pairs' e4m3 rows and scales.  tokens <= 4096, top_k <= 8,
  * experts <= 256. */
 OMNI_API int omni_moe_align_gather(const int32_t* topk_ids, int64_t tokens, int32_t top_k, int32_t experts,
                                    const void* xq, const float* xs, int32_t hidden, void* permuted_q,
@@ -393,6 +393,31 @@ OMNI_API int omni_moe_combine(const void* y, int64_t y_stride, const int32_t* sl
                               int32_t top_k, const void* x, int64_t x_stride, const void* shared_gate_weight,
                               const void* shared_out, int64_t shared_stride, void* h, int64_t h_stride,
                               float* ss_out, int64_t ss_stride, int64_t rows, int32_t hidden, void* stream);
+
+/* omni_moe_align_gather over strided inputs (rows of a receive buffer that packs
+ * each token's e4m3 row, scales and local expert ids): ids_stride in int32
+ * elements, xq_stride in bytes, xs_stride in floats.  An expert id of -1 marks an
+ * entry with no local expert: skipped, slot_of -1.  tokens <= 4096. */
+OMNI_API int omni_moe_align_gather_strided(const int32_t* topk_ids, int64_t ids_stride, int64_t tokens,
+                                           int32_t top_k, int32_t experts, const void* xq, int64_t xq_stride,
+                                           const float* xs, int64_t xs_stride, int32_t hidden, void* permuted_q,
+                                           float* permuted_s, int32_t* slot_of, int32_t* expert_offsets,
+                                           void* chunks, int64_t chunk_capacity, int32_t* n_chunks, void* stream);
+
+/* Expert-parallel dispatch/combine (SURVEY-described EP variant of FusedMoE):
+ * the partial routed sum of one received row over the experts this rank holds,
+ * out[r] = bf16(sum_k w[r][k] * y[slot_of[r][k]]) over slot_of >= 0 (k order),
+ * zero when none. */
+OMNI_API int omni_moe_partial_sum(const void* y, int64_t y_stride, const int32_t* slot_of, const float* weights,
+                                  int64_t weights_stride, int32_t top_k, int64_t rows, int32_t hidden, void* out,
+                                  int64_t out_stride, void* stream);
+
+/* omni_moe_combine with the routed sum given as up to n_parts bf16 partial rows per
+ * token (parts row part_index[t][p], -1 = none), summed in p order. */
+OMNI_API int omni_moe_combine_parts(const void* parts, int64_t parts_stride, const int32_t* part_index,
+                                    int32_t n_parts, const void* x, int64_t x_stride, const void* shared_gate_weight,
+                                    const void* shared_out, int64_t shared_stride, void* h, int64_t h_stride,
+                                    float* ss_out, int64_t ss_stride, int64_t rows, int32_t hidden, void* stream);
 
 #ifdef __cplusplus
 }

@@ -42,7 +42,7 @@ constexpr int kMaxKBlocks = 8;  // K <= 1024 for the gate/up GEMM
 constexpr int kGroupedThreads = 320;
 constexpr int kMaxStagesG = 8;
 constexpr int kMaxExperts = 256;
-constexpr int kMaxTokens = 1024;
+constexpr int kMaxTokens = 4096;
 
 // Two fp32 values to two e4m3 codes (round to nearest even, saturating to
 // +-448): lo in the low byte.
@@ -137,13 +137,18 @@ __global__ void __launch_bounds__(128) rmsnorm_quant_kernel(const uint16_t* __re
 // CTA rebuilds the expert membership bitmaps from topk_ids in shared memory
 // (tokens x experts bits) and gathers the e4m3 rows and scales of its own
 // tokens into their rows; CTA 0 also writes the expert offsets and the work
-// list of row chunks (expert, first row, rows <= 32).
+// list of row chunks (expert, first row, rows <= 32).  An expert id of -1 marks a
+// (token, k) entry with no local expert (expert-parallel receive buffers): it is
+// skipped and its slot_of entry is -1.
 // ---------------------------------------------------------------------------
 struct AlignParams {
   const int32_t* topk_ids;
+  int64_t ids_stride;  // int32 elements between rows of topk_ids
   int tokens, top_k, experts;
   const uint8_t* xq;
+  int64_t xq_stride;   // bytes between e4m3 rows
   const float* xs;
+  int64_t xs_stride;   // floats between scale rows
   int hidden, groups;
   uint8_t* pq;
   float* ps;
@@ -164,12 +169,13 @@ __global__ void __launch_bounds__(1024) moe_align_gather_kernel(const __grid_con
   for (int i = tid; i < p.experts * W; i += blockDim.x) mask[i] = 0u;
   __syncthreads();
   for (int i = tid; i < p.tokens * p.top_k; i += blockDim.x) {
-    const int e = p.topk_ids[i];
+    const int t = i / p.top_k;
+    const int e = p.topk_ids[t * p.ids_stride + i % p.top_k];
+    if (e == -1) continue;
     if (e < 0 || e >= p.experts) {
       report_status(kDevBadIndex);
       continue;
     }
-    const int t = i / p.top_k;
     atomicOr(&mask[e * W + (t >> 5)], 1u << (t & 31));
   }
   __syncthreads();
@@ -232,8 +238,11 @@ __global__ void __launch_bounds__(1024) moe_align_gather_kernel(const __grid_con
   const int t_end = min(p.tokens, (int)(blockIdx.x + 1) * per_cta);
   for (int t = blockIdx.x * per_cta + warp; t < t_end; t += blockDim.x / 32) {
     for (int kk = 0; kk < p.top_k; ++kk) {
-      const int e = p.topk_ids[t * p.top_k + kk];
-      if (e < 0 || e >= p.experts) continue;
+      const int e = p.topk_ids[t * p.ids_stride + kk];
+      if (e < 0 || e >= p.experts) {
+        if (lane == 0) p.slot_of[t * p.top_k + kk] = -1;
+        continue;
+      }
       // rank of t among the tokens choosing e: whole mask words below t's word
       // (lane-strided, summed across the warp) plus the lower bits of its word
       int part = 0;
@@ -242,10 +251,10 @@ __global__ void __launch_bounds__(1024) moe_align_gather_kernel(const __grid_con
       for (int o = 16; o >= 1; o >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, o);
       const int slot = off[e] + __popc(mask[e * W + (t >> 5)] & ((1u << (t & 31)) - 1u)) + part;
       if (lane == 0) p.slot_of[t * p.top_k + kk] = slot;
-      const uint4* src = reinterpret_cast<const uint4*>(p.xq + (int64_t)t * p.hidden);
+      const uint4* src = reinterpret_cast<const uint4*>(p.xq + (int64_t)t * p.xq_stride);
       uint4* dst = reinterpret_cast<uint4*>(p.pq + (int64_t)slot * p.hidden);
       for (int v = lane; v < p.hidden / 16; v += 32) dst[v] = src[v];
-      for (int g = lane; g < p.groups; g += 32) p.ps[(int64_t)slot * p.groups + g] = p.xs[(int64_t)t * p.groups + g];
+      for (int g = lane; g < p.groups; g += 32) p.ps[(int64_t)slot * p.groups + g] = p.xs[(int64_t)t * p.xs_stride + g];
     }
   }
 }
@@ -543,11 +552,15 @@ __global__ void __launch_bounds__(kGroupedThreads, 1)
 // and ss_out[part][t] = sum over the part's 128 features of h^2.
 // One CTA of 128 threads per token, 8 features a thread.
 // ---------------------------------------------------------------------------
+// parts != nullptr: the routed sum arrives as up to top_k bf16 partial rows per token
+// (expert-parallel: one per rank that holds some of the token's experts), parts rows
+// slot_of[t][k] (or -1), summed in k order; topk_w is unused.
 __global__ void __launch_bounds__(128) moe_combine_kernel(
     const uint16_t* __restrict__ y, int64_t y_stride, const int32_t* __restrict__ slot_of,
     const float* __restrict__ topk_w, int top_k, const uint16_t* __restrict__ x, int64_t x_stride,
     const uint16_t* __restrict__ w_sg, const uint16_t* __restrict__ shared, int64_t sh_stride,
-    uint16_t* __restrict__ h, int64_t h_stride, float* __restrict__ ss_out, int64_t ss_stride, int hidden) {
+    uint16_t* __restrict__ h, int64_t h_stride, float* __restrict__ ss_out, int64_t ss_stride, int hidden,
+    int parts_mode) {
   __shared__ float red[4];
   griddep_wait();
   griddep_launch();
@@ -574,8 +587,8 @@ __global__ void __launch_bounds__(128) moe_combine_kernel(
   float wk[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    slot[k] = k < top_k ? slot_of[t * top_k + k] : 0;
-    wk[k] = k < top_k ? topk_w[t * top_k + k] : 0.0f;
+    slot[k] = k < top_k ? slot_of[t * top_k + k] : -1;
+    wk[k] = (k < top_k && !parts_mode) ? topk_w[t * top_k + k] : 1.0f;
   }
   for (int c0 = threadIdx.x * 8; c0 < hidden; c0 += 1024) {
     float acc[8];
@@ -583,7 +596,7 @@ __global__ void __launch_bounds__(128) moe_combine_kernel(
     for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      if (k < top_k) {
+      if (k < top_k && slot[k] >= 0) {
         const uint4 yv = *reinterpret_cast<const uint4*>(y + (int64_t)slot[k] * y_stride + c0);
         const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
 #pragma unroll
@@ -615,6 +628,46 @@ __global__ void __launch_bounds__(128) moe_combine_kernel(
 #pragma unroll
     for (int off = 8; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
     if (ss_out && (lane & 15) == 0) ss_out[(int64_t)(c0 / kBlk) * ss_stride + t] = ss;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Expert-parallel partial routed sum of one received row: out[r] = bf16(sum over
+// its k entries with slot >= 0 of w[r][k] * y[slot]) in k order (fp32), zero when
+// none.  One CTA of 128 threads per row, 8 features a thread.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) moe_partial_sum_kernel(const uint16_t* __restrict__ y, int64_t y_stride,
+                                                              const int32_t* __restrict__ slot_of,
+                                                              const float* __restrict__ w, int64_t w_stride,
+                                                              int top_k, int hidden, uint16_t* __restrict__ out,
+                                                              int64_t out_stride) {
+  griddep_wait();
+  griddep_launch();
+  const int r = blockIdx.x;
+  int slot[8];
+  float wk[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    slot[k] = k < top_k ? slot_of[(int64_t)r * top_k + k] : -1;
+    wk[k] = k < top_k ? w[(int64_t)r * w_stride + k] : 0.0f;
+  }
+  for (int c0 = threadIdx.x * 8; c0 < hidden; c0 += 1024) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (slot[k] >= 0) {
+        const uint4 yv = *reinterpret_cast<const uint4*>(y + (int64_t)slot[k] * y_stride + c0);
+        const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[2 * q] = __fmaf_rn(wk[k], bf_lo(yw[q]), acc[2 * q]);
+          acc[2 * q + 1] = __fmaf_rn(wk[k], bf_hi(yw[q]), acc[2 * q + 1]);
+        }
+      }
+    }
+    *reinterpret_cast<uint4*>(out + (int64_t)r * out_stride + c0) =
+        make_uint4(pack_bf2(acc[0], acc[1]), pack_bf2(acc[2], acc[3]), pack_bf2(acc[4], acc[5]),
+                   pack_bf2(acc[6], acc[7]));
   }
 }
 
@@ -708,25 +761,29 @@ extern "C" OMNI_API int64_t omni_moe_chunk_capacity(int64_t tokens, int32_t top_
   return experts + (tokens * top_k + kChunk - 1) / kChunk;
 }
 
-extern "C" OMNI_API int omni_moe_align_gather(const int32_t* topk_ids, int64_t tokens, int32_t top_k,
-                                              int32_t experts, const void* xq, const float* xs, int32_t hidden,
-                                              void* permuted_q, float* permuted_s, int32_t* slot_of,
-                                              int32_t* expert_offsets, void* chunks, int64_t chunk_capacity,
-                                              int32_t* n_chunks, void* stream) {
+extern "C" OMNI_API int omni_moe_align_gather_strided(
+    const int32_t* topk_ids, int64_t ids_stride, int64_t tokens, int32_t top_k, int32_t experts, const void* xq,
+    int64_t xq_stride, const float* xs, int64_t xs_stride, int32_t hidden, void* permuted_q, float* permuted_s,
+    int32_t* slot_of, int32_t* expert_offsets, void* chunks, int64_t chunk_capacity, int32_t* n_chunks,
+    void* stream) {
   if (tokens < 0 || tokens > kMaxTokens || top_k < 1 || top_k > 8 || experts < 1 || experts > kMaxExperts ||
-      top_k > experts)
-    return set_error(OMNI_ERR_UNSUPPORTED, "align: tokens <= 1024, 1 <= top_k <= 8, experts <= 256");
-  if (hidden % kBlk != 0 || !al16(xq) || !al16(permuted_q) || !al16(chunks))
+      top_k > experts || ids_stride < top_k)
+    return set_error(OMNI_ERR_UNSUPPORTED, "align: tokens <= 4096, 1 <= top_k <= 8, experts <= 256");
+  if (hidden % kBlk != 0 || !al16(xq) || xq_stride % 16 || xq_stride < hidden || xs_stride < hidden / kBlk ||
+      !al16(permuted_q) || !al16(chunks))
     return set_error(OMNI_ERR_UNSUPPORTED, "align: hidden a multiple of 128, 16-byte aligned rows");
   if (chunk_capacity < omni_moe_chunk_capacity(tokens, top_k, experts))
     return set_error(OMNI_ERR_CAPACITY, "align: chunk capacity too small");
   AlignParams p{};
   p.topk_ids = topk_ids;
+  p.ids_stride = ids_stride;
   p.tokens = (int)tokens;
   p.top_k = top_k;
   p.experts = experts;
   p.xq = static_cast<const uint8_t*>(xq);
+  p.xq_stride = xq_stride;
   p.xs = xs;
+  p.xs_stride = xs_stride;
   p.hidden = hidden;
   p.groups = hidden / kBlk;
   p.pq = static_cast<uint8_t*>(permuted_q);
@@ -747,6 +804,16 @@ extern "C" OMNI_API int omni_moe_align_gather(const int32_t* topk_ids, int64_t t
   const int grid = tokens > 0 ? (int)((tokens + 31) / 32) : 1;
   return check_launch(launch(moe_align_gather_kernel, dim3((unsigned)grid), dim3(1024), smem,
                              static_cast<cudaStream_t>(stream), p));
+}
+
+extern "C" OMNI_API int omni_moe_align_gather(const int32_t* topk_ids, int64_t tokens, int32_t top_k,
+                                              int32_t experts, const void* xq, const float* xs, int32_t hidden,
+                                              void* permuted_q, float* permuted_s, int32_t* slot_of,
+                                              int32_t* expert_offsets, void* chunks, int64_t chunk_capacity,
+                                              int32_t* n_chunks, void* stream) {
+  return omni_moe_align_gather_strided(topk_ids, top_k, tokens, top_k, experts, xq, hidden, xs, hidden / kBlk,
+                                       hidden, permuted_q, permuted_s, slot_of, expert_offsets, chunks,
+                                       chunk_capacity, n_chunks, stream);
 }
 
 extern "C" OMNI_API int omni_moe_gate_up_fp8(const void* permuted_q, const float* permuted_s, int64_t rows_cap,
@@ -810,5 +877,39 @@ extern "C" OMNI_API int omni_moe_combine(const void* y, int64_t y_stride, const 
                              static_cast<const uint16_t*>(x), x_stride,
                              static_cast<const uint16_t*>(shared_gate_weight),
                              static_cast<const uint16_t*>(shared_out), shared_stride, static_cast<uint16_t*>(h),
-                             h_stride, ss_out, ss_stride, (int)hidden));
+                             h_stride, ss_out, ss_stride, (int)hidden, 0));
+}
+
+extern "C" OMNI_API int omni_moe_combine_parts(const void* parts, int64_t parts_stride, const int32_t* part_index,
+                                               int32_t n_parts, const void* x, int64_t x_stride,
+                                               const void* shared_gate_weight, const void* shared_out,
+                                               int64_t shared_stride, void* h, int64_t h_stride, float* ss_out,
+                                               int64_t ss_stride, int64_t rows, int32_t hidden, void* stream) {
+  if (n_parts < 1 || n_parts > 8 || hidden % 1024 != 0)
+    return set_error(OMNI_ERR_UNSUPPORTED, "combine_parts: 1 <= parts <= 8, hidden a multiple of 1024");
+  if (!al16(parts) || !al16(x) || !al16(shared_gate_weight) || !al16(shared_out) || !al16(h) || parts_stride % 8 ||
+      x_stride % 8 || shared_stride % 8 || h_stride % 8)
+    return set_error(OMNI_ERR_UNSUPPORTED, "combine_parts: 16-byte aligned rows required");
+  if (rows == 0) return OMNI_OK;
+  return check_launch(launch(moe_combine_kernel, dim3((unsigned)rows), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                             static_cast<const uint16_t*>(parts), parts_stride, part_index,
+                             static_cast<const float*>(nullptr), (int)n_parts, static_cast<const uint16_t*>(x),
+                             x_stride, static_cast<const uint16_t*>(shared_gate_weight),
+                             static_cast<const uint16_t*>(shared_out), shared_stride, static_cast<uint16_t*>(h),
+                             h_stride, ss_out, ss_stride, (int)hidden, 1));
+}
+
+extern "C" OMNI_API int omni_moe_partial_sum(const void* y, int64_t y_stride, const int32_t* slot_of,
+                                             const float* weights, int64_t weights_stride, int32_t top_k,
+                                             int64_t rows, int32_t hidden, void* out, int64_t out_stride,
+                                             void* stream) {
+  if (top_k < 1 || top_k > 8 || hidden % 1024 != 0)
+    return set_error(OMNI_ERR_UNSUPPORTED, "partial_sum: 1 <= top_k <= 8, hidden a multiple of 1024");
+  if (!al16(y) || !al16(out) || y_stride % 8 || out_stride % 8)
+    return set_error(OMNI_ERR_UNSUPPORTED, "partial_sum: 16-byte aligned rows required");
+  if (rows == 0) return OMNI_OK;
+  return check_launch(launch(moe_partial_sum_kernel, dim3((unsigned)rows), dim3(128), 0,
+                             static_cast<cudaStream_t>(stream), static_cast<const uint16_t*>(y), y_stride, slot_of,
+                             weights, weights_stride, (int)top_k, (int)hidden, static_cast<uint16_t*>(out),
+                             out_stride));
 }

@@ -1,0 +1,162 @@
+"""Expert-parallel variant of the talker's MoE block across the GPUs of one node.
+
+Each of the W ranks holds E / W experts (rank d: experts [d E/W, (d+1) E/W)) and
+routes its own tokens with the replicated router.  Per layer:
+
+  dispatch  every token goes once to each rank that holds at least one of its
+            top-k experts: its e4m3 row, group scales, the k expert ids local to
+            that rank (-1 for the others) and the k routing weights travel as one
+            packed row; each rank sends a fixed block of `cap` rows to every peer
+            (unused rows carry no expert), one NCCL all-to-all over NVLink
+  compute   the received rows go through the same align/gather and grouped FP8
+            GEMMs as the single-GPU block, over the local experts only, and each
+            received row's partial routed sum (its local experts, k order) is
+            formed in bf16
+  combine   the partial rows return by a second all-to-all; each token sums its
+            partials in rank order, then adds the gated shared expert (computed
+            locally) and the residual, as the single-GPU combine does
+
+Fixed-size blocks keep every collective's split sizes constant, so no host
+synchronisation sits inside the layer.  The routed sum is rounded once per rank
+(the partial rows are bf16), so results agree with the single-GPU block within
+the bf16 tolerance, not bit for bit.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from omni_b200 import ops
+from omni_b200.config import MoEConfig
+from omni_b200.moe import MoEBlock
+
+
+def packed_row_bytes(hidden: int, top_k: int) -> int:
+    """Bytes of one dispatched row: e4m3 codes, group scales, k local ids, k weights (16-aligned)."""
+    b = hidden + 4 * (hidden // 128) + 8 * top_k
+    return (b + 15) // 16 * 16
+
+
+def dispatch_plan(topk_ids: torch.Tensor, world: int, experts_per_rank: int, cap: int):
+    """For tokens' global expert ids [T, k]: has[t, d] (token t goes to rank d), pos[t, d]
+    (its row in block d), flat[t, d] (row in the send buffer; world*cap = discarded) and
+    local_ids[t, d, k] (expert id on rank d, or -1)."""
+    T = topk_ids.shape[0]
+    dev = topk_ids.device
+    ranks = torch.arange(world, device=dev)
+    dest = torch.div(topk_ids.long(), experts_per_rank, rounding_mode="floor")  # [T, k]
+    onehot = dest.unsqueeze(-1) == ranks  # [T, k, W]
+    has = onehot.any(1)  # [T, W]
+    pos = torch.cumsum(has.to(torch.int32), 0) - 1  # [T, W]
+    flat = torch.where(has, ranks * cap + pos, torch.full_like(pos, world * cap))
+    local = topk_ids.long().unsqueeze(1) - (ranks * experts_per_rank).view(1, world, 1)  # [T, W, k]
+    local_ids = torch.where(onehot.permute(0, 2, 1), local, torch.full_like(local, -1)).to(torch.int32)
+    del T
+    return has, pos, flat, local_ids
+
+
+def pack_rows(send: torch.Tensor, hidden: int, top_k: int, xq: torch.Tensor, xs: torch.Tensor,
+              local_ids: torch.Tensor, weights: torch.Tensor, flat: torch.Tensor) -> None:
+    """Writes the dispatched rows into send [world*cap + 1, row_bytes] (uint8); rows no
+    token lands in carry expert ids -1."""
+    T, W = flat.shape
+    G = hidden // 128
+    idx = flat.reshape(-1)
+    q = send[:, :hidden]
+    s = send[:, hidden: hidden + 4 * G].view(torch.float32)
+    ids = send[:, hidden + 4 * G: hidden + 4 * G + 4 * top_k].view(torch.int32)
+    w = send[:, hidden + 4 * G + 4 * top_k: hidden + 4 * G + 8 * top_k].view(torch.float32)
+    ids.fill_(-1)
+    q.index_copy_(0, idx, xq.unsqueeze(1).expand(T, W, hidden).reshape(T * W, hidden))
+    s.index_copy_(0, idx, xs.unsqueeze(1).expand(T, W, G).reshape(T * W, G))
+    ids.index_copy_(0, idx, local_ids.reshape(T * W, top_k))
+    w.index_copy_(0, idx, weights.unsqueeze(1).expand(T, W, top_k).reshape(T * W, top_k))
+
+
+def part_index(has: torch.Tensor, pos: torch.Tensor, cap: int) -> torch.Tensor:
+    """Row of the returned partial of token t from rank d (or -1), [T, W] int32."""
+    W = has.shape[1]
+    ranks = torch.arange(W, device=has.device)
+    return torch.where(has, ranks * cap + pos, torch.full_like(pos, -1)).to(torch.int32).contiguous()
+
+
+class ExpertParallelMoE:
+    """One rank's share of the expert-parallel MoE block (buffers shared by the layers)."""
+
+    def __init__(self, cfg: MoEConfig, hidden: int, *, max_tokens: int, group=None, device=None):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if cfg.num_experts % self.world:
+            raise ValueError("experts must divide evenly over the ranks")
+        self.cfg = cfg
+        self.hidden = hidden
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.cap = max_tokens
+        self.e_local = cfg.num_experts // self.world
+        k = cfg.num_experts_per_tok
+        W, dev = self.world, self.device
+        self.row_bytes = packed_row_bytes(hidden, k)
+        # tokens of this rank: norm, codes, routing, shared expert (single-GPU block buffers)
+        self.local = MoEBlock(cfg, hidden, max_batch=max_tokens, device=dev)
+        self.send = torch.zeros(W * self.cap + 1, self.row_bytes, dtype=torch.uint8, device=dev)
+        self.recv = torch.zeros(W * self.cap, self.row_bytes, dtype=torch.uint8, device=dev)
+        n_recv = W * self.cap
+        pairs_cap = n_recv * k + 64
+        self.permuted_q = torch.zeros(pairs_cap, hidden, dtype=torch.uint8, device=dev)
+        self.permuted_s = torch.zeros(pairs_cap, hidden // 128, dtype=torch.float32, device=dev)
+        self.slot_of = torch.zeros(n_recv, k, dtype=torch.int32, device=dev)
+        self.expert_offsets = torch.zeros(self.e_local + 1, dtype=torch.int32, device=dev)
+        self.chunks = torch.zeros(ops.moe_chunk_capacity(n_recv, k, self.e_local), 4, dtype=torch.int32, device=dev)
+        self.n_chunks = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.act_q = torch.zeros(pairs_cap, cfg.moe_intermediate_size, dtype=torch.uint8, device=dev)
+        self.act_s = torch.zeros(pairs_cap, cfg.moe_intermediate_size // 128, dtype=torch.float32, device=dev)
+        self.y = torch.zeros(pairs_cap, hidden, dtype=torch.bfloat16, device=dev)
+        self.ret_send = torch.zeros(n_recv, hidden, dtype=torch.bfloat16, device=dev)
+        self.ret_recv = torch.zeros(n_recv, hidden, dtype=torch.bfloat16, device=dev)
+
+    def local_weights(self, w: dict) -> dict:
+        """This rank's slice of a full layer's MoE weights (experts r E/W .. (r+1) E/W)."""
+        e0, e1 = self.rank * self.e_local, (self.rank + 1) * self.e_local
+        out = dict(w)
+        for key in ("w13", "w13_scale", "w2", "w2_scale"):
+            out[key] = w[key][e0:e1].contiguous()
+        return out
+
+    def forward(self, h: torch.Tensor, ss: torch.Tensor, ss_parts: int, gain: torch.Tensor, eps: float,
+                w_local: dict) -> None:
+        """h [T, H] += MoE(RMSNorm(h)) in place for this rank's T tokens (T <= max_tokens);
+        w_local = local_weights(full layer weights).  Every rank calls it (collectives)."""
+        cfg, H, k = self.cfg, self.hidden, self.cfg.num_experts_per_tok
+        W, cap, G = self.world, self.cap, H // 128
+        T = h.shape[0]
+        m = self.local
+        x, xq, xs = m.x[:T], m.xq[:T], m.xs[:T]
+        ids, tw = m.topk_ids[:T], m.topk_weights[:T]
+        ops.moe_rmsnorm_quant(h, ss, ss_parts, gain, eps, x, xq, xs)
+        ops.linear_fused(x, w_local["gate"], m.router_logits[:T], epilogue=ops.EPI_ROUTER,
+                         router={"topk_ids": ids, "topk_weights": tw})
+        has, pos, flat, local_ids = dispatch_plan(ids, W, self.e_local, cap)
+        pack_rows(self.send, H, k, xq, xs, local_ids, tw, flat)
+        self.dist.all_to_all_single(self.recv, self.send[: W * cap], group=self.group)
+        rb = self.row_bytes
+        ids_view = self.recv[:, H + 4 * G:].view(torch.int32)
+        xs_view = self.recv[:, H:].view(torch.float32)
+        w_view = self.recv[:, H + 4 * G + 4 * k:].view(torch.float32)
+        n = W * cap
+        ops.moe_align_gather_strided(ids_view, n, k, self.e_local, self.recv, rb, xs_view, rb // 4, H,
+                                     self.permuted_q, self.permuted_s, self.slot_of, self.expert_offsets,
+                                     self.chunks, self.n_chunks, ids_stride=rb // 4)
+        ops.moe_gate_up_fp8(self.permuted_q, self.permuted_s, w_local["w13"], w_local["w13_scale"], self.chunks,
+                            self.n_chunks, self.act_q, self.act_s)
+        ops.moe_down_fp8(self.act_q, self.act_s, w_local["w2"], w_local["w2_scale"], self.chunks, self.n_chunks,
+                         self.y)
+        ops.moe_partial_sum(self.y, self.slot_of, w_view, rb // 4, self.ret_send)
+        self.dist.all_to_all_single(self.ret_recv, self.ret_send, group=self.group)
+        ops.linear_fused(x, w_local["shared_gate_up"], m.shared_act[:T], epilogue=ops.EPI_SWIGLU)
+        ops.linear_fused(m.shared_act[:T], w_local["shared_down"], m.shared_out[:T], epilogue=ops.EPI_STORE)
+        ops.moe_combine_parts(self.ret_recv, part_index(has, pos, cap), x, w_local["shared_expert_gate"],
+                              m.shared_out[:T], h, ss)

@@ -463,3 +463,33 @@ def moe_combine(y: torch.Tensor, slot_of: torch.Tensor, topk_weights: torch.Tens
               slot_of.shape[1], x.data_ptr(), x.stride(0), shared_gate_weight.data_ptr(), shared_out.data_ptr(),
               shared_out.stride(0), h.data_ptr(), h.stride(0), _lib.ptr(ss_out),
               0 if ss_out is None else ss_out.stride(0), rows, hidden, _lib.stream_of(h.device))
+
+
+def moe_align_gather_strided(topk_ids: torch.Tensor, tokens: int, top_k: int, experts: int, xq: torch.Tensor,
+                             xq_stride: int, xs: torch.Tensor, xs_stride: int, hidden: int,
+                             permuted_q: torch.Tensor, permuted_s: torch.Tensor, slot_of: torch.Tensor,
+                             expert_offsets: torch.Tensor, chunks: torch.Tensor, n_chunks: torch.Tensor,
+                             ids_stride: int) -> None:
+    """moe_align_gather over strided rows (ids_stride int32s, xq_stride bytes, xs_stride floats);
+    expert id -1 = no local expert for that entry."""
+    _lib.call("omni_moe_align_gather_strided", topk_ids.data_ptr(), ids_stride, tokens, top_k, experts,
+              xq.data_ptr(), xq_stride, xs.data_ptr(), xs_stride, hidden, permuted_q.data_ptr(),
+              permuted_s.data_ptr(), slot_of.data_ptr(), expert_offsets.data_ptr(), chunks.data_ptr(),
+              chunks.shape[0], n_chunks.data_ptr(), _lib.stream_of(permuted_q.device))
+
+
+def moe_partial_sum(y: torch.Tensor, slot_of: torch.Tensor, weights: torch.Tensor, weights_stride: int,
+                    out: torch.Tensor) -> None:
+    rows, top_k = slot_of.shape
+    _lib.call("omni_moe_partial_sum", y.data_ptr(), y.stride(0), slot_of.data_ptr(), weights.data_ptr(),
+              weights_stride, top_k, rows, out.shape[1], out.data_ptr(), out.stride(0), _lib.stream_of(y.device))
+
+
+def moe_combine_parts(parts: torch.Tensor, part_index: torch.Tensor, x: torch.Tensor,
+                      shared_gate_weight: torch.Tensor, shared_out: torch.Tensor, h: torch.Tensor,
+                      ss_out: torch.Tensor | None) -> None:
+    rows, hidden = h.shape
+    _lib.call("omni_moe_combine_parts", parts.data_ptr(), parts.stride(0), part_index.data_ptr(),
+              part_index.shape[1], x.data_ptr(), x.stride(0), shared_gate_weight.data_ptr(), shared_out.data_ptr(),
+              shared_out.stride(0), h.data_ptr(), h.stride(0), _lib.ptr(ss_out),
+              0 if ss_out is None else ss_out.stride(0), rows, hidden, _lib.stream_of(h.device))

@@ -1,0 +1,82 @@
+"""Expert-parallel MoE block on 2 GPUs (NCCL all-to-all over NVLink) against the
+single-GPU block on the same tokens: bf16 tolerance (cosine >= 0.999, max-abs <=
+2e-2 x scale).  Skipped with fewer than two GPUs."""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    for p in (str(ROOT), str(ROOT / "sglang-omni_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from omni_b200.config import MoEConfig
+        from omni_b200.moe import MoEBlock, init_moe_weights
+        from omni_b200.moe_ep import ExpertParallelMoE
+
+        cfg, H = MoEConfig(), 1024
+        g = torch.Generator(device=dev).manual_seed(0)  # identical weights on every rank
+        w = init_moe_weights(cfg, H, generator=g, device=dev)
+        T = 40 + 24 * rank  # uneven token counts
+        gt = torch.Generator(device=dev).manual_seed(100 + rank)
+        h = torch.randn(T, H, generator=gt, device=dev).to(torch.bfloat16)
+        gain = torch.ones(H, device=dev, dtype=torch.bfloat16)
+        ss = h.float().view(T, 8, 128).pow(2).sum(-1).t().contiguous()
+        ep = ExpertParallelMoE(cfg, H, max_tokens=64, device=dev)
+        h_ep, ss_ep = h.clone(), ss.clone()
+        ep.forward(h_ep, ss_ep, 8, gain, 1e-6, ep.local_weights(w))
+        single = MoEBlock(cfg, H, max_batch=T, device=dev)
+        h_1, ss_1 = h.clone(), ss.clone()
+        single.forward(h_1, ss_1, 8, gain, 1e-6, w)
+        torch.cuda.synchronize()
+        a, b = h_ep.float().flatten(), h_1.float().flatten()
+        cos = torch.nn.functional.cosine_similarity(a, b, dim=0).item()
+        err = (a - b).abs().max().item()
+        d_ep, d_1 = (h_ep.float() - h.float()).flatten(), (h_1.float() - h.float()).flatten()
+        cos_d = torch.nn.functional.cosine_similarity(d_ep, d_1, dim=0).item()
+        np.save(os.path.join(out_dir, f"ep{rank}.npy"),
+                np.array([cos, err, b.abs().max().item(), cos_d, int(torch.equal(ep.local.topk_ids[:T], single.topk_ids[:T]))]))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_moe_matches_single_gpu(tmp_path):
+    import torch.multiprocessing as mp
+
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    for r in range(world):
+        cos, err, scale, cos_d, same_route = np.load(tmp_path / f"ep{r}.npy")
+        assert same_route == 1
+        assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0), (r, cos, err, scale)
+        assert cos_d >= 0.99, (r, cos_d)
