@@ -370,6 +370,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kernels", action="store_true", help="print the per-kernel time table and exit")
     ap.add_argument("--only", default=None, help="with --kernels: only the rows whose name contains this text")
+    ap.add_argument("--ep", action="store_true",
+                    help="with --config 3 under torchrun: experts sharded over the ranks (NCCL all-to-all)")
     ap.add_argument("--layers", type=int, default=0,
                     help="with --kernels: talker layers to build (0 = the config's 20); for small profiling runs")
     ap.add_argument("--config", type=int, default=1, choices=[1, 3],
@@ -413,7 +415,8 @@ def main() -> None:
     lens = context_lengths(STREAMS, seed=rank, headroom=total_steps + 8)
     P = cfg.page_size
     pages = int(sum(math.ceil((L + total_steps) / P) for L in lens) * 1.25) + STREAMS
-    runner = TalkerDecodeRunner(cfg, max_batch=STREAMS, num_pages=pages, seed=0, device=dev)
+    ep = bool(args.ep and cfg.moe is not None and world > 1)
+    runner = TalkerDecodeRunner(cfg, max_batch=STREAMS, num_pages=pages, seed=0, device=dev, expert_parallel=ep)
     runner.admit(lens, seed=rank)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     runner.text_embeds.normal_(generator=g)
@@ -529,7 +532,9 @@ def main() -> None:
                        ("config3: MoE talker decode (20 layers, 128 experts top-8 inter 384 FP8 e4m3 "
                         "128x128 block scales + shared expert 1536, 256 streams, paged KV page 16, "
                         "ctx lognormal(6,0.8) clip [16,8192]) + predictor (31 codebooks of 1024)"),
-                       "streams_per_gpu": STREAMS, "parallelism": f"dp{world} replicas (no collective)",
+                       "streams_per_gpu": STREAMS,
+                       "parallelism": (f"ep{world}: experts sharded, NCCL all-to-all dispatch/combine per MoE layer"
+                                       if ep else f"dp{world} replicas (no collective)"),
                        "sum_ctx_rank0": int(sum(lens)), "l2": "inputs > L2 (~3 GB streamed per step)"},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": STREAMS * H * 2,
                     "d2h_bytes_per_step": STREAMS * G * 8},

@@ -48,7 +48,8 @@ class GenerationBatchResult:
 
 class TalkerDecodeRunner:
     def __init__(self, cfg: TalkerConfig, *, max_batch: int, num_pages: int, seed: int = 0, device="cuda",
-                 pages_per_chunk: int = 32, weights: dict | None = None, predictor_weights: dict | None = None):
+                 pages_per_chunk: int = 32, weights: dict | None = None, predictor_weights: dict | None = None,
+                 expert_parallel: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         self.max_batch = max_batch
@@ -59,7 +60,8 @@ class TalkerDecodeRunner:
         self.kv = PagedKVPool(num_layers=cfg.num_hidden_layers, num_pages=num_pages, page_size=cfg.page_size,
                               num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim, device=self.device)
         self.r2t = ReqToTokenPool(max_reqs=max_batch, max_context=cfg.max_context, device=self.device)
-        self.talker = DenseTalker(cfg, self.w, max_batch=max_batch, device=self.device, kv_pool=self.kv)
+        self.talker = DenseTalker(cfg, self.w, max_batch=max_batch, device=self.device, kv_pool=self.kv,
+                                  expert_parallel=expert_parallel)
         self.predictor = CodePredictor(cfg.predictor, pw, max_batch=max_batch, device=self.device,
                                        layer0_embedding=self.w["codec_embedding"])
         B = max_batch

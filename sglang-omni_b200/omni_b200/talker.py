@@ -79,7 +79,8 @@ class DecodeForwardBatch:
 
 
 class DenseTalker:
-    def __init__(self, cfg: TalkerConfig, weights: dict, *, max_batch: int, device, kv_pool: PagedKVPool):
+    def __init__(self, cfg: TalkerConfig, weights: dict, *, max_batch: int, device, kv_pool: PagedKVPool,
+                 expert_parallel: bool = False):
         self.cfg = cfg
         self.w = weights
         self.device = torch.device(device)
@@ -122,7 +123,16 @@ class DenseTalker:
                         "gate_up": (ops.fold_norm(lw["gate_up_proj"], lw["post_attention_layernorm"])
                                     if "gate_up_proj" in lw else None)}
                        for lw in self.w["layers"]]
-        self.moe = MoEBlock(cfg.moe, H, max_batch=B, device=self.device) if cfg.moe is not None else None
+        self.moe = None
+        self.moe_local_w = None
+        if cfg.moe is not None and expert_parallel:
+            # experts sharded over the ranks of the default process group (moe_ep)
+            from omni_b200.moe_ep import ExpertParallelMoE
+
+            self.moe = ExpertParallelMoE(cfg.moe, H, max_tokens=B, device=self.device)
+            self.moe_local_w = [self.moe.local_weights(lw["moe"]) for lw in self.w["layers"]]
+        elif cfg.moe is not None:
+            self.moe = MoEBlock(cfg.moe, H, max_batch=B, device=self.device)
         self.codec_head_folded = ops.fold_norm(self.w["codec_head"], self.w["norm"])
         self.ss = torch.zeros(H // 128, B, dtype=torch.float32, device=self.device)
 
@@ -164,7 +174,8 @@ class DenseTalker:
                                        sm_scale=self.scale, out=attn, workspace=self.attn_workspace)
             ops.linear_fused(attn, lw["o_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=ss)
             if "moe" in lw:
-                self.moe.forward(h, ss, parts, lw["post_attention_layernorm"], eps, lw["moe"])
+                mw = self.moe_local_w[li] if self.moe_local_w is not None else lw["moe"]
+                self.moe.forward(h, ss, parts, lw["post_attention_layernorm"], eps, mw)
             else:
                 ops.linear_fused(h, self.folded[li]["gate_up"], act, epilogue=ops.EPI_SWIGLU, ss_in=ss,
                                  ss_in_parts=parts, norm_eps=eps)
