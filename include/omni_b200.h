@@ -419,6 +419,31 @@ OMNI_API int omni_moe_combine_parts(const void* parts, int64_t parts_stride, con
                                     const void* shared_out, int64_t shared_stride, void* h, int64_t h_stride,
                                     float* ss_out, int64_t ss_stride, int64_t rows, int32_t hidden, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Extend (prefill) of new streams in a mixed batch (config 2's fused forward:
+ * ScheduleBatch.prepare_for_extend + ForwardBatch.init_new in extend mode,
+ * model_runner/base.py:577-623; compose_prefill_embeds talker_model_runner.py:
+ * 347-425 supplies the rows).  The scheduler has reserved the new tokens' slots
+ * in req_to_token; this packs seq_lens = prefix + extend, qo_indptr (cu_seqlens),
+ * each new token's out_cache_loc and position (prefix + j), the page lists and,
+ * with tile_indptr, the q-tile list of omni_prefill_attention (q_tile rows). */
+OMNI_API int omni_extend_prepare(int64_t rows, const int64_t* prefix_lens, const int64_t* extend_lens,
+                                 const int64_t* req_pool_indices, const int32_t* req_to_token, int64_t max_ctx,
+                                 int32_t page_size, int64_t* seq_lens, int32_t* qo_indptr, int64_t* out_cache_loc,
+                                 int64_t* positions, int32_t* page_indptr, int32_t* page_indices, int32_t* tile_indptr,
+                                 int32_t q_tile, int32_t* status, void* stream);
+
+/* Causal extend attention (RadixAttention extend, thinker_model.py:373-379) over
+ * the paged pool: the extend rows of stream s are q[qo_indptr[s] ..
+ * qo_indptr[s+1]) and query j sees keys [0, prefix + j] of the stream's pages;
+ * out has the rows of q.  Grid of max_tiles x Hq CTAs (tiles of 64 queries; the
+ * tiles past tile_indptr[streams] exit).  head_dim 128, page 16. */
+OMNI_API int omni_prefill_attention(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                                   const int32_t* qo_indptr, const int64_t* seq_lens, const int32_t* page_indptr,
+                                   const int32_t* page_indices, const int32_t* tile_indptr, int64_t streams,
+                                   int64_t max_tiles, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                   int32_t page_size, float sm_scale, void* out, int64_t out_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

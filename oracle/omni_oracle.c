@@ -753,3 +753,41 @@ ORC_API int orc_quant_fp8_group(const float* x, int64_t rows, int64_t cols, int6
     }
     return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Extend packing (prepare_for_extend + ForwardBatch.init_new in extend mode, */
+/* model_runner/base.py:577-623) for slots the scheduler reserved in         */
+/* req_to_token: seq_len = prefix + extend; qo_indptr = cumsum(extend);      */
+/* token j of row i: out_cache_loc = req_to_token[req, prefix + j],          */
+/* position = prefix + j; page list = req_to_token[req, k P] / P; q tiles of */
+/* q_tile rows: tile_indptr = cumsum(ceil(extend / q_tile)).                 */
+/* ------------------------------------------------------------------------ */
+ORC_API int orc_extend_prepare(int64_t rows, const int64_t* prefix_lens, const int64_t* extend_lens,
+                               const int64_t* req_pool_indices, const int32_t* req_to_token, int64_t max_ctx,
+                               int64_t page_size, int64_t q_tile, int64_t* seq_lens, int32_t* qo_indptr,
+                               int64_t* out_cache_loc, int64_t* positions, int32_t* page_indptr,
+                               int32_t* page_indices, int32_t* tile_indptr) {
+    int64_t q = 0, pg = 0, tl = 0;
+    for (int64_t i = 0; i < rows; ++i) {
+        const int64_t E = extend_lens[i], L = prefix_lens[i] + E;
+        if (E < 0 || L > max_ctx) return 1;
+        seq_lens[i] = L;
+        qo_indptr[i] = (int32_t)q;
+        page_indptr[i] = (int32_t)pg;
+        tile_indptr[i] = (int32_t)tl;
+        const int32_t* r2t = req_to_token + req_pool_indices[i] * max_ctx;
+        for (int64_t j = 0; j < E; ++j) {
+            out_cache_loc[q + j] = r2t[prefix_lens[i] + j];
+            positions[q + j] = prefix_lens[i] + j;
+        }
+        const int64_t np = (L + page_size - 1) / page_size;
+        for (int64_t k = 0; k < np; ++k) page_indices[pg + k] = r2t[k * page_size] / (int32_t)page_size;
+        q += E;
+        pg += np;
+        tl += (E + q_tile - 1) / q_tile;
+    }
+    qo_indptr[rows] = (int32_t)q;
+    page_indptr[rows] = (int32_t)pg;
+    tile_indptr[rows] = (int32_t)tl;
+    return 0;
+}

@@ -46,6 +46,7 @@ def lib() -> ctypes.CDLL:
         l.orc_e4m3_to_f32.restype = ctypes.c_float
         l.orc_e4m3_to_f32.argtypes = [ctypes.c_uint8]
         l.orc_quant_fp8_group.argtypes = [_P, _I64, _I64, _I64, _P, _P]
+        l.orc_extend_prepare.argtypes = [_I64, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P]
         _lib = l
     return _lib
 
@@ -179,6 +180,28 @@ def decode_rollback(seq_lens, req_pool_indices, req_to_token, page_size, out_cac
     n = lib().orc_decode_rollback(sl.shape[0], _p(sl), _p(rp), _p(r2t), r2t.shape[1], int(page_size), _p(loc),
                                   _p(freed))
     return sl, r2t, freed[:n]
+
+
+def extend_prepare(prefix_lens, extend_lens, req_pool_indices, req_to_token, page_size, q_tile=64):
+    """Returns (seq_lens, qo_indptr, out_cache_loc, positions, page_indptr, page_indices, tile_indptr)."""
+    pre = _c(prefix_lens, np.int64)
+    ext = _c(extend_lens, np.int64)
+    rp = _c(req_pool_indices, np.int64)
+    r2t = _c(req_to_token, np.int32)
+    rows = pre.shape[0]
+    total = int(ext.sum())
+    sl = np.zeros(rows, np.int64)
+    qo = np.zeros(rows + 1, np.int32)
+    loc = np.zeros(max(total, 1), np.int64)
+    pos = np.zeros(max(total, 1), np.int64)
+    pgp = np.zeros(rows + 1, np.int32)
+    npages = int(sum((pre + ext + page_size - 1) // page_size))
+    pgi = np.zeros(max(npages, 1), np.int32)
+    tp = np.zeros(rows + 1, np.int32)
+    if lib().orc_extend_prepare(rows, _p(pre), _p(ext), _p(rp), _p(r2t), r2t.shape[1], int(page_size), int(q_tile),
+                                _p(sl), _p(qo), _p(loc), _p(pos), _p(pgp), _p(pgi), _p(tp)) != 0:
+        raise ValueError("oracle: extend exceeds max_ctx")
+    return sl, qo, loc[:total], pos[:total], pgp, pgi[:npages], tp
 
 
 def moe_route(router_logits, top_k: int, renormalize: bool = True):

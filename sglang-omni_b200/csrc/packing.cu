@@ -10,6 +10,12 @@
 // rows (token level, optional), the page-level page_indptr / page_indices, and
 // the attention work list work_indptr = cumsum(ceil(pages / pages_per_chunk)).
 //
+// extend_prepare_kernel packs an extend (prefill) batch whose slots the
+// scheduler has already reserved in req_to_token (prepare_for_extend):
+// seq_len = prefix + extend, qo_indptr = cumsum(extend) (cu_seqlens),
+// out_cache_loc / positions of every new token (positions prefix + j), the
+// page list of each stream and the q-tile list of the prefill attention.
+//
 // rollback_kernel undoes one prepare (rollback_decode_prep_after_skip): it
 // returns the pages the step opened to the free list (the allocator is a
 // stack, so restoring its head returns exactly those pages), lists their
@@ -195,6 +201,93 @@ __global__ void __launch_bounds__(kPackThreads) decode_rollback_kernel(int rows,
   }
 }
 
+struct ExtendParams {
+  int rows;
+  const int64_t* prefix_lens;
+  const int64_t* extend_lens;
+  const int64_t* req_pool_indices;
+  const int32_t* req_to_token;
+  int64_t max_ctx;
+  int page_size;
+  int64_t* seq_lens;
+  int32_t* qo_indptr;
+  int64_t* out_cache_loc;
+  int64_t* positions;
+  int32_t* page_indptr;
+  int32_t* page_indices;
+  int32_t* tile_indptr;  // nullable
+  int q_tile;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kPackThreads) extend_prepare_kernel(const __grid_constant__ ExtendParams p) {
+  __shared__ int ws[33];
+  __shared__ int64_t carry_q, carry_pages, carry_tiles;
+  griddep_wait();
+  griddep_launch();
+  if (threadIdx.x == 0) {
+    carry_q = 0;
+    carry_pages = 0;
+    carry_tiles = 0;
+  }
+  __syncthreads();
+  for (int base = 0; base < p.rows; base += kPackThreads) {
+    const int i = base + threadIdx.x;
+    const bool in = i < p.rows;
+    int64_t E = 0, L = 0;
+    if (in) {
+      E = p.extend_lens[i];
+      L = p.prefix_lens[i] + E;
+      if (E < 0 || L > p.max_ctx) {
+        if (p.status) atomicExch(p.status, 2);
+        E = 0;
+        L = 0;
+      }
+      p.seq_lens[i] = L;
+    }
+    const int npages = (int)((L + p.page_size - 1) / p.page_size);
+    const int ntiles = p.tile_indptr ? (int)((E + p.q_tile - 1) / p.q_tile) : 0;
+    int tot_q, tot_pages, tot_tiles;
+    const int q_off = block_excl_scan((int)E, ws, tot_q);
+    const int pg_off = block_excl_scan(npages, ws, tot_pages);
+    const int t_off = block_excl_scan(ntiles, ws, tot_tiles);
+    if (in) {
+      p.qo_indptr[i] = (int32_t)(carry_q + q_off);
+      p.page_indptr[i] = (int32_t)(carry_pages + pg_off);
+      if (p.tile_indptr) p.tile_indptr[i] = (int32_t)(carry_tiles + t_off);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      carry_q += tot_q;
+      carry_pages += tot_pages;
+      carry_tiles += tot_tiles;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    p.qo_indptr[p.rows] = (int32_t)carry_q;
+    p.page_indptr[p.rows] = (int32_t)carry_pages;
+    if (p.tile_indptr) p.tile_indptr[p.rows] = (int32_t)carry_tiles;
+  }
+  __syncthreads();
+  // one warp per stream: its new tokens' slots and positions, and its page list
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = warp; i < p.rows; i += kPackThreads / 32) {
+    const int64_t req = p.req_pool_indices[i];
+    const int32_t* r2t = p.req_to_token + req * p.max_ctx;
+    const int64_t L = p.seq_lens[i];
+    const int q0 = p.qo_indptr[i], q1 = p.qo_indptr[i + 1];
+    const int64_t prefix = L - (q1 - q0);
+    for (int j = lane; j < q1 - q0; j += 32) {
+      p.out_cache_loc[q0 + j] = r2t[prefix + j];
+      p.positions[q0 + j] = prefix + j;
+    }
+    const int pbeg = p.page_indptr[i];
+    const int np = (int)((L + p.page_size - 1) / p.page_size);
+    for (int k = lane; k < np; k += 32) p.page_indices[pbeg + k] = r2t[(int64_t)k * p.page_size] / p.page_size;
+  }
+}
+
 }  // namespace
 }  // namespace omni
 
@@ -244,4 +337,34 @@ extern "C" OMNI_API int omni_decode_rollback(int64_t rows, int64_t* seq_lens, co
   return check_launch(launch(decode_rollback_kernel, dim3(1), dim3(kPackThreads), 0,
                              static_cast<cudaStream_t>(stream), (int)rows, seq_lens, req_pool_indices, req_to_token,
                              max_ctx, (int)page_size, out_cache_loc, free_head, freed_slots, num_freed));
+}
+
+extern "C" OMNI_API int omni_extend_prepare(int64_t rows, const int64_t* prefix_lens, const int64_t* extend_lens,
+                                            const int64_t* req_pool_indices, const int32_t* req_to_token,
+                                            int64_t max_ctx, int32_t page_size, int64_t* seq_lens,
+                                            int32_t* qo_indptr, int64_t* out_cache_loc, int64_t* positions,
+                                            int32_t* page_indptr, int32_t* page_indices, int32_t* tile_indptr,
+                                            int32_t q_tile, int32_t* status, void* stream) {
+  if (rows < 0 || max_ctx <= 0 || page_size <= 0) return set_error(OMNI_ERR_INVALID, "bad packing arguments");
+  if (tile_indptr && q_tile <= 0) return set_error(OMNI_ERR_INVALID, "q_tile must be > 0");
+  if (rows == 0) return OMNI_OK;
+  ExtendParams p{};
+  p.rows = (int)rows;
+  p.prefix_lens = prefix_lens;
+  p.extend_lens = extend_lens;
+  p.req_pool_indices = req_pool_indices;
+  p.req_to_token = req_to_token;
+  p.max_ctx = max_ctx;
+  p.page_size = page_size;
+  p.seq_lens = seq_lens;
+  p.qo_indptr = qo_indptr;
+  p.out_cache_loc = out_cache_loc;
+  p.positions = positions;
+  p.page_indptr = page_indptr;
+  p.page_indices = page_indices;
+  p.tile_indptr = tile_indptr;
+  p.q_tile = q_tile;
+  p.status = status;
+  return check_launch(
+      launch(extend_prepare_kernel, dim3(1), dim3(kPackThreads), 0, static_cast<cudaStream_t>(stream), p));
 }

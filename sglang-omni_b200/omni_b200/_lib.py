@@ -66,6 +66,9 @@ SIGNATURES: dict[str, list] = {
                                       _P, _P],
     "omni_moe_partial_sum": [_P, _I64, _P, _P, _I64, _I32, _I64, _I32, _P, _I64, _P],
     "omni_moe_combine_parts": [_P, _I64, _P, _I32, _P, _I64, _P, _P, _I64, _P, _I64, _P, _I64, _I64, _I32, _P],
+    "omni_extend_prepare": [_I64, _P, _P, _P, _P, _I64, _I32, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P],
+    "omni_prefill_attention": [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _I32, _F32, _P,
+                               _I64, _P],
 }
 _RESTYPES = {
     "omni_version": ctypes.c_char_p,

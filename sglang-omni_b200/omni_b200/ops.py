@@ -493,3 +493,28 @@ def moe_combine_parts(parts: torch.Tensor, part_index: torch.Tensor, x: torch.Te
               part_index.shape[1], x.data_ptr(), x.stride(0), shared_gate_weight.data_ptr(), shared_out.data_ptr(),
               shared_out.stride(0), h.data_ptr(), h.stride(0), _lib.ptr(ss_out),
               0 if ss_out is None else ss_out.stride(0), rows, hidden, _lib.stream_of(h.device))
+
+
+PREFILL_Q_TILE = 64
+
+
+def extend_prepare(*, prefix_lens, extend_lens, req_pool_indices, req_to_token, page_size, seq_lens, qo_indptr,
+                   out_cache_loc, positions, page_indptr, page_indices, tile_indptr=None, status=None) -> None:
+    """Packing of an extend batch whose slots are reserved in req_to_token (see include/omni_b200.h)."""
+    rows = prefix_lens.shape[0]
+    _lib.call("omni_extend_prepare", rows, prefix_lens.data_ptr(), extend_lens.data_ptr(),
+              req_pool_indices.data_ptr(), req_to_token.data_ptr(), req_to_token.shape[1], page_size,
+              seq_lens.data_ptr(), qo_indptr.data_ptr(), out_cache_loc.data_ptr(), positions.data_ptr(),
+              page_indptr.data_ptr(), page_indices.data_ptr(), _lib.ptr(tile_indptr), PREFILL_Q_TILE,
+              _lib.ptr(status), _lib.stream_of(prefix_lens.device))
+
+
+def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *, qo_indptr, seq_lens,
+                      page_indptr, page_indices, tile_indptr, max_tiles: int, num_q_heads: int, num_kv_heads: int,
+                      head_dim: int, page_size: int, sm_scale: float, out: torch.Tensor) -> torch.Tensor:
+    """Causal extend attention over the paged pool; q/out rows are the extend rows (cu_seqlens qo_indptr)."""
+    _lib.call("omni_prefill_attention", q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+              qo_indptr.data_ptr(), seq_lens.data_ptr(), page_indptr.data_ptr(), page_indices.data_ptr(),
+              tile_indptr.data_ptr(), qo_indptr.shape[0] - 1, max_tiles, num_q_heads, num_kv_heads, head_dim,
+              page_size, sm_scale, out.data_ptr(), out.stride(0), _lib.stream_of(q.device))
+    return out
