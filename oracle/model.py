@@ -133,37 +133,62 @@ class OracleTalker:
     def talker_forward(self, feedback, text, positions, out_cache_loc, seq_lens, req_to_token, k_pool, v_pool):
         """One decode forward; k_pool/v_pool: fp32 [L, slots, hkv, d] updated in place.
         Returns (logits fp32 [B, V], hidden bf16-rounded [B, H])."""
-        cfg = self.cfg
-        H, D = cfg.hidden_size, cfg.head_dim
-        hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
-        eps = cfg.rms_norm_eps
         B = feedback.shape[0]
         x = rb(feedback.float() + (text.float() if text is not None else 0.0))
-        cs = self.cs[positions]
+        ctx = [req_to_token[b, : int(seq_lens[b])].long() for b in range(B)]
+        x = self.forward_rows(x, positions, out_cache_loc, ctx, k_pool, v_pool)
+        hidden = rb(rmsnorm(x, self.w["norm"], self.cfg.rms_norm_eps))
+        return hidden @ self.w["codec_head"].t(), hidden
+
+    def mixed_forward(self, feedback, text, positions, out_cache_loc, seq_lens, req_to_token, prompt_embeds,
+                      ext_positions, ext_cache_loc, ext_ctx, select, k_pool, v_pool):
+        """A mixed batch: decode rows (as talker_forward) followed by extend rows (prompt
+        embeddings, positions, slots, and for each row the slots it attends, causal within its
+        stream) through the layers together; logits/hidden of the rows in `select`."""
+        B = feedback.shape[0]
+        xd = rb(feedback.float() + (text.float() if text is not None else 0.0))
+        x = torch.cat([xd, prompt_embeds.float()], 0)
+        ctx = [req_to_token[b, : int(seq_lens[b])].long() for b in range(B)] + list(ext_ctx)
+        pos = torch.cat([torch.as_tensor(positions), torch.as_tensor(ext_positions)])
+        loc = torch.cat([torch.as_tensor(out_cache_loc), torch.as_tensor(ext_cache_loc)])
+        x = self.forward_rows(x, pos, loc, ctx, k_pool, v_pool)
+        hidden = rb(rmsnorm(x[select], self.w["norm"], self.cfg.rms_norm_eps))
+        return hidden @ self.w["codec_head"].t(), hidden
+
+    def forward_rows(self, x, positions, cache_locs, ctx_slots, k_pool, v_pool):
+        """The decoder layers over rows x [R, H] (bf16-rounded fp32): row r sits at position
+        positions[r], writes its K/V at slot cache_locs[r] and attends the slots ctx_slots[r]
+        (its own slot included).  Returns the residual stream after the last layer."""
+        cfg = self.cfg
+        D = cfg.head_dim
+        hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        eps = cfg.rms_norm_eps
+        R = x.shape[0]
+        cs = self.cs[torch.as_tensor(positions).long()]
+        loc = torch.as_tensor(cache_locs).long()
         scale = 1.0 / math.sqrt(D)
         for li, lw in enumerate(self.w["layers"]):
             n = rb(rmsnorm(x, lw["input_layernorm"], eps))
             qkv = rb(n @ lw["qkv_proj"].t())
-            q = qkv[:, : hq * D].view(B, hq, D)
-            k = qkv[:, hq * D: (hq + hkv) * D].view(B, hkv, D)
-            v = qkv[:, (hq + hkv) * D:].view(B, hkv, D)
+            q = qkv[:, : hq * D].view(R, hq, D)
+            k = qkv[:, hq * D: (hq + hkv) * D].view(R, hkv, D)
+            v = qkv[:, (hq + hkv) * D:].view(R, hkv, D)
             q = rb(rmsnorm(q, lw["q_norm"], eps))
             k = rb(rmsnorm(k, lw["k_norm"], eps))
             q = rb(rope_neox(q, cs))
             k = rb(rope_neox(k, cs))
-            k_pool[li, out_cache_loc] = k
-            v_pool[li, out_cache_loc] = v
-            att = torch.empty(B, hq, D)
-            for b in range(B):
-                L = int(seq_lens[b])
-                slots = req_to_token[b, :L].long()
+            k_pool[li, loc] = k
+            v_pool[li, loc] = v
+            att = torch.empty(R, hq, D)
+            for r in range(R):
+                slots = ctx_slots[r]
                 kk = k_pool[li, slots]  # [L, hkv, D]
                 vv = v_pool[li, slots]
-                qb = q[b].view(hkv, hq // hkv, D)
-                s = torch.einsum("hgd,lhd->hgl", qb, kk) * scale
-                p = torch.softmax(s, -1)
-                att[b] = torch.einsum("hgl,lhd->hgd", p, vv).reshape(hq, D)
-            att = rb(att.reshape(B, hq * D))
+                qb = q[r].view(hkv, hq // hkv, D)
+                sc = torch.einsum("hgd,lhd->hgl", qb, kk) * scale
+                p = torch.softmax(sc, -1)
+                att[r] = torch.einsum("hgl,lhd->hgd", p, vv).reshape(hq, D)
+            att = rb(att.reshape(R, hq * D))
             x = rb(x + att @ lw["o_proj"].t())
             n = rb(rmsnorm(x, lw["post_attention_layernorm"], eps))
             if "moe" in lw:
@@ -174,9 +199,7 @@ class OracleTalker:
             I = gu.shape[1] // 2
             a = rb(torch.nn.functional.silu(rb(gu[:, :I])) * rb(gu[:, I:]))
             x = rb(x + a @ lw["down_proj"].t())
-        hidden = rb(rmsnorm(x, self.w["norm"], eps))
-        logits = hidden @ self.w["codec_head"].t()
-        return logits, hidden
+        return x
 
     # ------------------------------------------------------------------
     def predictor_tokens(self, x, k_cache, v_cache, *, batch, tokens, cache_len):

@@ -32,7 +32,7 @@ from omni_b200.config import SamplingParams, TalkerConfig
 from omni_b200.kv_cache import PageAllocator, PagedKVPool, ReqToTokenPool
 from omni_b200.predictor import CodePredictor, init_predictor_weights
 from omni_b200.seed import derive_sampling_seed
-from omni_b200.talker import DecodeForwardBatch, DenseTalker, init_talker_weights
+from omni_b200.talker import DecodeForwardBatch, DenseTalker, ExtendForwardBatch, init_talker_weights
 
 
 @dataclass
@@ -49,7 +49,9 @@ class GenerationBatchResult:
 class TalkerDecodeRunner:
     def __init__(self, cfg: TalkerConfig, *, max_batch: int, num_pages: int, seed: int = 0, device="cuda",
                  pages_per_chunk: int = 32, weights: dict | None = None, predictor_weights: dict | None = None,
-                 expert_parallel: bool = False):
+                 expert_parallel: bool = False, max_prefill_tokens: int = 0):
+        """max_batch: streams in a step (decode + newly admitted); max_prefill_tokens: extend rows of
+        a mixed step (0 = decode only)."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.max_batch = max_batch
@@ -61,7 +63,7 @@ class TalkerDecodeRunner:
                               num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim, device=self.device)
         self.r2t = ReqToTokenPool(max_reqs=max_batch, max_context=cfg.max_context, device=self.device)
         self.talker = DenseTalker(cfg, self.w, max_batch=max_batch, device=self.device, kv_pool=self.kv,
-                                  expert_parallel=expert_parallel)
+                                  expert_parallel=expert_parallel, max_rows=max_batch + max_prefill_tokens)
         self.predictor = CodePredictor(cfg.predictor, pw, max_batch=max_batch, device=self.device,
                                        layer0_embedding=self.w["codec_embedding"])
         B = max_batch
@@ -69,8 +71,14 @@ class TalkerDecodeRunner:
         i32 = dict(dtype=torch.int32, device=self.device)
         self.seq_lens = torch.zeros(B, **i64)
         self.req_pool_indices = torch.arange(B, **i64)
-        self.out_cache_loc = torch.zeros(B, **i64)
-        self.positions = torch.zeros(B, **i64)
+        # positions / slots of every row of a step: decode rows first, then extend rows
+        R = B + max_prefill_tokens
+        self.row_positions = torch.zeros(R, **i64)
+        self.row_cache_loc = torch.zeros(R, **i64)
+        self.out_cache_loc = self.row_cache_loc[:B]
+        self.positions = self.row_positions[:B]
+        self.max_prefill_tokens = max_prefill_tokens
+        self.extend: ExtendForwardBatch | None = None
         self.page_indptr = torch.zeros(B + 1, **i32)
         self.page_indices = torch.zeros(num_pages + B, **i32)
         self.work_indptr = torch.zeros(B + 1, **i32)
@@ -162,9 +170,13 @@ class TalkerDecodeRunner:
         return self.forward_batch()
 
     def run_step(self) -> None:
-        """The whole decode step on the current stream (capturable)."""
+        """The whole decode step on the current stream (capturable); a mixed step when
+        extend streams are admitted."""
         fb = self.prepare_decode()
-        self.custom_decode_forward(fb, None, None)
+        if self.extend is not None:
+            self.custom_mixed_forward(fb)
+        else:
+            self.custom_decode_forward(fb, None, None)
 
     def custom_decode_forward(self, forward_batch: DecodeForwardBatch, schedule_batch, requests):
         """The hook that owns the decode forward (base.py:879-890)."""
@@ -178,6 +190,107 @@ class TalkerDecodeRunner:
             c0, t.h[:B], forward_batch.positions, final_norm=t.w["norm"], final_ss=t.ss, final_eps=self.cfg.rms_norm_eps,
             hidden_out=t.hidden[:B])
         return GenerationBatchResult(next_token_ids=c0, next_token_logits=logits, hidden_states=self.talker.hidden[:B],
+                                     codes=codes[:, :, 0], summed_embeds=summed[:, 0])
+
+    # ------------------------------------------------------------------
+    # mixed step: new streams prefilled in the same forward as the decode rows
+    # ------------------------------------------------------------------
+    def admit_prefill(self, prompt_lens: list[int], *, seed: int = 0,
+                      sampling: SamplingParams = SamplingParams()) -> None:
+        """Admit len(prompt_lens) new streams (rows after the decode streams) whose prompts
+        (seeded N(0, 1) embeddings, the rows compose_prefill_embeds would produce) are
+        prefilled by every following step's fused forward, their slots reserved in
+        req_to_token (prepare_for_extend).  Each step then samples the layer-0 token of each
+        new stream from its last prompt row and runs the predictor for it."""
+        cfg, P = self.cfg, self.cfg.page_size
+        Bd, n = self.batch_size, len(prompt_lens)
+        if Bd + n > self.max_batch:
+            raise RuntimeError("decode + new streams exceed max_batch")
+        T = int(sum(prompt_lens))
+        if T > self.max_prefill_tokens:
+            raise RuntimeError("prompts exceed max_prefill_tokens")
+        if max(prompt_lens) >= cfg.max_context:
+            raise ValueError("prompt exceeds max_context")
+        dev = self.device
+        i64 = dict(dtype=torch.long, device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        need = [(L + P - 1) // P for L in prompt_lens]
+        pages = self.allocator.alloc_prefix(sum(need)).cpu()
+        r2t = torch.zeros(n, cfg.max_context, dtype=torch.int32)
+        off = 0
+        for i, (L, k) in enumerate(zip(prompt_lens, need)):
+            pg = pages[off: off + k].long()
+            off += k
+            r2t[i, :L] = (pg[:, None] * P + torch.arange(P)[None, :]).reshape(-1)[:L].to(torch.int32)
+        self.r2t.req_to_token[Bd: Bd + n].copy_(r2t.to(dev))
+        self.ext_req = torch.arange(Bd, Bd + n, **i64)
+        self.ext_prefix = torch.zeros(n, **i64)
+        self.ext_lens = torch.tensor(prompt_lens, **i64)
+        self.ext_seq_lens = torch.zeros(n, **i64)
+        self.ext_qo = torch.zeros(n + 1, **i32)
+        self.ext_page_indptr = torch.zeros(n + 1, **i32)
+        self.ext_page_indices = torch.zeros(sum(need) + 1, **i32)
+        self.ext_tiles = torch.zeros(n + 1, **i32)
+        max_tiles = sum((L + ops.PREFILL_Q_TILE - 1) // ops.PREFILL_Q_TILE for L in prompt_lens)
+        g = torch.Generator(device=dev).manual_seed(seed + 13)
+        self.prompt_embeds = torch.randn(T, cfg.hidden_size, generator=g, device=dev).to(torch.bfloat16)
+        last = np.cumsum(prompt_lens) - 1
+        self.select = torch.tensor(list(range(Bd)) + [Bd + int(x) for x in last], **i64)
+        self.extend = ExtendForwardBatch(streams=n, tokens=T, qo_indptr=self.ext_qo, seq_lens=self.ext_seq_lens,
+                                         page_indptr=self.ext_page_indptr, page_indices=self.ext_page_indices,
+                                         tile_indptr=self.ext_tiles, max_tiles=max_tiles)
+        self.sel_positions = torch.zeros(Bd + n, **i64)
+        # per-stream sampling state of the new rows
+        t = self.talker
+        rows = slice(Bd, Bd + n)
+        t.repetition_penalties[rows].fill_(sampling.repetition_penalty)
+        t.repetition_mask[rows].zero_()
+        t.suppress_mask[rows].zero_()
+        t.sampling_temperatures[rows].fill_(sampling.temperature)
+        t.sampling_top_ks[rows].fill_(sampling.top_k)
+        t.sampling_top_ps[rows].fill_(sampling.top_p)
+        t.sampling_min_ps[rows].fill_(sampling.min_p)
+        seeds = [derive_sampling_seed("omni-b200", seed, f"new{i}") for i in range(n)]
+        t.sampling_seeds[rows].copy_(torch.tensor([derive_sampling_seed("semantic", s_) for s_ in seeds]))
+        self.predictor.set_sampling(
+            temperature=[sampling.subtalker_temperature] * n, top_k=[sampling.subtalker_top_k] * n,
+            top_p=[sampling.subtalker_top_p] * n, seeds=[derive_sampling_seed("subtalker", s_) for s_ in seeds],
+            do_sample=[sampling.subtalker_dosample] * n, batch=n, row0=Bd)
+        self.graph = None
+
+    def prepare_extend(self) -> ExtendForwardBatch:
+        """Device-side prepare_for_extend packing of the admitted new streams."""
+        Bd = self.batch_size
+        T = self.extend.tokens
+        ops.extend_prepare(prefix_lens=self.ext_prefix, extend_lens=self.ext_lens, req_pool_indices=self.ext_req,
+                           req_to_token=self.r2t.req_to_token, page_size=self.cfg.page_size,
+                           seq_lens=self.ext_seq_lens, qo_indptr=self.ext_qo,
+                           out_cache_loc=self.row_cache_loc[Bd: Bd + T], positions=self.row_positions[Bd: Bd + T],
+                           page_indptr=self.ext_page_indptr, page_indices=self.ext_page_indices,
+                           tile_indptr=self.ext_tiles, status=self.status)
+        return self.extend
+
+    def custom_mixed_forward(self, fb: DecodeForwardBatch):
+        """custom_prefill_forward for a mixed batch (model_runner/base.py:866-877): decode rows and
+        the new streams' prompts in one forward, then the layer-0 draw and the code predictor for
+        every stream of the step (the decode rows and each new stream's first frame)."""
+        ext = self.prepare_extend()
+        Bd, n = fb.batch_size, self.select.shape[0]
+        t = self.talker
+        feedback = self.predictor.output_embeds[:Bd]
+        logits = t.forward_mixed(feedback, self.text_embeds[:Bd], fb, self.prompt_embeds, ext, self.row_positions,
+                                 self.row_cache_loc, self.select)
+        torch.index_select(self.row_positions, 0, self.select, out=self.sel_positions)
+        sel_fb = DecodeForwardBatch(batch_size=n, positions=self.sel_positions, seq_lens=fb.seq_lens,
+                                    out_cache_loc=fb.out_cache_loc, req_pool_indices=fb.req_pool_indices,
+                                    page_indptr=fb.page_indptr, page_indices=fb.page_indices,
+                                    work_indptr=fb.work_indptr, work_capacity=fb.work_capacity,
+                                    pages_per_chunk=fb.pages_per_chunk)
+        c0 = t.sample_decode_tokens(logits, sel_fb)
+        codes, summed = self.predictor.code_predictor_forward(
+            c0, t.h_sel[:n], self.sel_positions, final_norm=t.w["norm"], final_ss=t.ss_sel,
+            final_eps=self.cfg.rms_norm_eps, hidden_out=t.hidden[:n])
+        return GenerationBatchResult(next_token_ids=c0, next_token_logits=logits, hidden_states=t.hidden[:n],
                                      codes=codes[:, :, 0], summed_embeds=summed[:, 0])
 
     # ------------------------------------------------------------------

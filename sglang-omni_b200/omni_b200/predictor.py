@@ -114,15 +114,19 @@ class CodePredictor:
         self.scale = 1.0 / math.sqrt(D)
 
     # ------------------------------------------------------------------
-    def set_sampling(self, *, temperature, top_k, top_p, seeds, do_sample, batch: int) -> None:
-        """Stage per-row residual sampling parameters (prepare_decode_buffers)."""
+    def set_sampling(self, *, temperature, top_k, top_p, seeds, do_sample, batch: int, row0: int = 0) -> None:
+        """Stage per-row residual sampling parameters of rows row0 .. row0 + batch
+        (prepare_decode_buffers); with row0 > 0 the batch-wide flags widen to cover both."""
         dev = self.device
-        self.sub_temperature_tensor[:batch].copy_(torch.as_tensor(temperature, dtype=torch.float32), non_blocking=True)
-        self.sub_top_k_tensor[:batch].copy_(torch.as_tensor(top_k, dtype=torch.long), non_blocking=True)
-        self.sub_top_p_tensor[:batch].copy_(torch.as_tensor(top_p, dtype=torch.float32), non_blocking=True)
-        self.sub_sampling_seed_tensor[:batch].copy_(torch.as_tensor(seeds, dtype=torch.long), non_blocking=True)
+        rows = slice(row0, row0 + batch)
+        self.sub_temperature_tensor[rows].copy_(torch.as_tensor(temperature, dtype=torch.float32), non_blocking=True)
+        self.sub_top_k_tensor[rows].copy_(torch.as_tensor(top_k, dtype=torch.long), non_blocking=True)
+        self.sub_top_p_tensor[rows].copy_(torch.as_tensor(top_p, dtype=torch.float32), non_blocking=True)
+        self.sub_sampling_seed_tensor[rows].copy_(torch.as_tensor(seeds, dtype=torch.long), non_blocking=True)
         ds = torch.as_tensor(do_sample, dtype=torch.uint8)
-        self.sub_do_sample_tensor[:batch].copy_(ds, non_blocking=True)
+        self.sub_do_sample_tensor[rows].copy_(ds, non_blocking=True)
+        prev = (self.sub_has_sampled_rows, self.sub_has_argmax_rows, self.sub_sampled_max_top_k,
+                self.sub_sampled_has_top_p) if row0 > 0 else None
         top_k_list = [int(k) for k in torch.as_tensor(top_k).reshape(-1).tolist()]
         top_p_list = [float(p) for p in torch.as_tensor(top_p).reshape(-1).tolist()]
         ds_list = [bool(v) for v in ds.reshape(-1).tolist()]
@@ -136,6 +140,11 @@ class CodePredictor:
         ladder = (4, 8, 16, 32, 50, 64, 128, 256, 512, 1024)
         self.sub_sampled_max_top_k = next(w for w in ladder if w >= widest)
         self.sub_sampled_has_top_p = any(0.0 < top_p_list[i] < 1.0 for i in sampled)
+        if prev is not None:
+            self.sub_has_sampled_rows = self.sub_has_sampled_rows or prev[0]
+            self.sub_has_argmax_rows = self.sub_has_argmax_rows or prev[1]
+            self.sub_sampled_max_top_k = max(self.sub_sampled_max_top_k, prev[2])
+            self.sub_sampled_has_top_p = self.sub_sampled_has_top_p or prev[3]
         assert fused_raw_logit_block_k(self.sub_sampled_max_top_k) is not None
         del dev
 

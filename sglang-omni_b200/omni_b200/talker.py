@@ -63,6 +63,20 @@ def init_talker_weights(cfg: TalkerConfig, *, seed: int, device, dtype=torch.bfl
 
 
 @dataclass
+class ExtendForwardBatch:
+    """Device tensors of the extend part of a mixed batch (ForwardBatch.init_new, extend mode)."""
+
+    streams: int
+    tokens: int                  # total extend rows
+    qo_indptr: torch.Tensor      # i32 [streams + 1] (cu_seqlens)
+    seq_lens: torch.Tensor       # i64 [streams] prefix + extend
+    page_indptr: torch.Tensor    # i32 [streams + 1]
+    page_indices: torch.Tensor   # i32
+    tile_indptr: torch.Tensor    # i32 [streams + 1] query tiles of the prefill attention
+    max_tiles: int
+
+
+@dataclass
 class DecodeForwardBatch:
     """Device tensors of one packed decode batch (ForwardBatch.init_new at decode)."""
 
@@ -80,7 +94,7 @@ class DecodeForwardBatch:
 
 class DenseTalker:
     def __init__(self, cfg: TalkerConfig, weights: dict, *, max_batch: int, device, kv_pool: PagedKVPool,
-                 expert_parallel: bool = False):
+                 expert_parallel: bool = False, max_rows: int = 0):
         self.cfg = cfg
         self.w = weights
         self.device = torch.device(device)
@@ -90,20 +104,19 @@ class DenseTalker:
         hq, hkv, I, V = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.intermediate_size, cfg.vocab_size
         bf = dict(device=self.device, dtype=torch.bfloat16)
         B = max_batch
+        # rows of one forward: the decode rows plus, in a mixed step, the extend rows
+        R = max(max_rows, B)
+        self.max_rows = R
         self.cos_sin = ops.rope_cos_sin_cache(cfg.max_context, D, cfg.rope_theta, self.device)
-        self.h = torch.zeros(B, H, **bf)
-        self.normed = torch.zeros(B, H, **bf)
-        self.qkv = torch.zeros(B, (hq + 2 * hkv) * D, **bf)
-        self.q = torch.zeros(B, hq * D, **bf)
-        self.attn = torch.zeros(B, hq * D, **bf)
-        self.act = torch.zeros(B, I, **bf)
+        self.h = torch.zeros(R, H, **bf)
+        self.q = torch.zeros(R, hq * D, **bf)
+        self.attn = torch.zeros(R, hq * D, **bf)
+        self.act = torch.zeros(R, I, **bf)
         self.hidden = torch.zeros(B, H, **bf)
+        # the rows that produce logits in a mixed step (decode rows + last extend row of each stream)
+        self.h_sel = torch.zeros(B, H, **bf)
         self.logits = torch.zeros(B, V, dtype=torch.float32, device=self.device)
         self.sampled_token_ids = torch.zeros(B, dtype=torch.long, device=self.device)
-        ws = 0
-        for k, n, e in ((H, (hq + 2 * hkv) * D, 0), (hq * D, H, 1), (H, 2 * I, 2), (I, H, 1), (H, V, 3)):
-            ws = max(ws, ops.linear_workspace_bytes(B, k, n, e))
-        self.workspace = torch.zeros(max(ws, 256), dtype=torch.uint8, device=self.device)
         self.attn_workspace: torch.Tensor | None = None
         self.scale = 1.0 / math.sqrt(D)
         # layer-0 sampling state (talker.py:836-1010 buffers)
@@ -134,7 +147,8 @@ class DenseTalker:
         elif cfg.moe is not None:
             self.moe = MoEBlock(cfg.moe, H, max_batch=B, device=self.device)
         self.codec_head_folded = ops.fold_norm(self.w["codec_head"], self.w["norm"])
-        self.ss = torch.zeros(H // 128, B, dtype=torch.float32, device=self.device)
+        self.ss = torch.zeros(H // 128, R, dtype=torch.float32, device=self.device)
+        self.ss_sel = torch.zeros(H // 128, B, dtype=torch.float32, device=self.device)
 
     def ensure_attention_workspace(self, work_capacity: int) -> None:
         need = ops.paged_attention_workspace_bytes(self.max_batch, self.cfg.num_key_value_heads, work_capacity)
@@ -184,6 +198,59 @@ class DenseTalker:
         logits = self.logits[:B]
         ops.linear_fused(h, self.codec_head_folded, logits, epilogue=ops.EPI_F32, ss_in=ss, ss_in_parts=parts,
                          norm_eps=eps)
+        return logits
+
+    def forward_mixed(self, feedback: torch.Tensor, text: torch.Tensor | None, fb: DecodeForwardBatch,
+                      prompt_embeds: torch.Tensor, ext: "ExtendForwardBatch", positions: torch.Tensor,
+                      cache_loc: torch.Tensor, select: torch.Tensor) -> torch.Tensor:
+        """One fused forward of a mixed batch: fb.batch_size decode rows (input feedback +
+        text) followed by ext.tokens extend rows (input prompt_embeds, compose_prefill_embeds
+        talker_model_runner.py:347-425), through every layer together; decode rows attend over
+        their paged context, extend rows causally over their stream's pages (the extend forward
+        writes their KV into the pool, talker.py:438-491 in extend mode).  positions /
+        cache_loc cover all rows.  Logits of the rows in `select` (manual_extend_logits,
+        talker.py:1344-1360: decode rows and each stream's last extend row) are returned."""
+        cfg = self.cfg
+        Bd, Te = fb.batch_size, ext.tokens
+        R = Bd + Te
+        H, D = cfg.hidden_size, cfg.head_dim
+        hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        eps = cfg.rms_norm_eps
+        h, q, attn, act = self.h[:R], self.q[:R], self.attn[:R], self.act[:R]
+        ss = self.ss
+        parts = H // 128
+        self.ensure_attention_workspace(fb.work_capacity)
+        ops.add_sumsq(feedback, text, h[:Bd], ss[0, :Bd])
+        ops.add_sumsq(prompt_embeds, None, h[Bd:R], ss[0, Bd:R])
+        ss_parts = 1
+        for li, lw in enumerate(self.w["layers"]):
+            kc, vc = self.kv.k_buffer[li], self.kv.v_buffer[li]
+            ops.linear_fused(h, self.folded[li]["qkv"], q, epilogue=ops.EPI_QKV_ROPE, ss_in=ss, ss_in_parts=ss_parts,
+                             norm_eps=eps, qkv=dict(num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=lw["q_norm"],
+                                                    k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin,
+                                                    positions=positions[:R], cache_loc=cache_loc[:R],
+                                                    k_cache=kc, v_cache=vc))
+            ops.paged_decode_attention(q[:Bd], kc, vc, page_indptr=fb.page_indptr, page_indices=fb.page_indices,
+                                       seq_lens=fb.seq_lens, work_indptr=fb.work_indptr, num_q_heads=hq,
+                                       num_kv_heads=hkv, head_dim=D, page_size=cfg.page_size,
+                                       pages_per_chunk=fb.pages_per_chunk, work_capacity=fb.work_capacity,
+                                       sm_scale=self.scale, out=attn[:Bd], workspace=self.attn_workspace)
+            ops.prefill_attention(q[Bd:R], kc, vc, qo_indptr=ext.qo_indptr, seq_lens=ext.seq_lens,
+                                  page_indptr=ext.page_indptr, page_indices=ext.page_indices,
+                                  tile_indptr=ext.tile_indptr, max_tiles=ext.max_tiles, num_q_heads=hq,
+                                  num_kv_heads=hkv, head_dim=D, page_size=cfg.page_size, sm_scale=self.scale,
+                                  out=attn[Bd:R])
+            ops.linear_fused(attn, lw["o_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=ss)
+            ops.linear_fused(h, self.folded[li]["gate_up"], act, epilogue=ops.EPI_SWIGLU, ss_in=ss, ss_in_parts=parts,
+                             norm_eps=eps)
+            ops.linear_fused(act, lw["down_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=ss)
+            ss_parts = parts
+        n = select.shape[0]
+        torch.index_select(h, 0, select, out=self.h_sel[:n])
+        torch.index_select(ss[:, :R], 1, select, out=self.ss_sel[:, :n])
+        logits = self.logits[:n]
+        ops.linear_fused(self.h_sel[:n], self.codec_head_folded, logits, epilogue=ops.EPI_F32, ss_in=self.ss_sel,
+                         ss_in_parts=parts, norm_eps=eps)
         return logits
 
     def sample_decode_tokens(self, logits: torch.Tensor, fb: DecodeForwardBatch) -> torch.Tensor:

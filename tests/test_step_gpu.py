@@ -190,3 +190,70 @@ def test_public_decode_api_round_trip():
     from omni_b200 import device_status
 
     assert device_status() == 0
+
+
+def test_mixed_prefill_decode_step_matches_oracle():
+    """Config 2's fused forward at small size: 3 decode streams + 2 new streams (prompts of
+    20 and 70 rows) in one forward; logits / hidden of the decode rows and of each new
+    stream's last prompt row within the bf16 tolerance, the prompts' KV in the pool, the
+    layer-0 draws bit-exact given the device logits."""
+    from omni_b200.config import SamplingParams, TalkerConfig
+    from omni_b200.model_runner import TalkerDecodeRunner
+
+    lens, prompts = (16, 33, 100), (20, 70)
+    cfg = TalkerConfig(num_hidden_layers=2, max_context=1024)
+    pages = sum((L + 16) // 16 for L in lens) + sum((L + 15) // 16 for L in prompts) + 32
+    r = TalkerDecodeRunner(cfg, max_batch=5, num_pages=pages, seed=6, max_prefill_tokens=sum(prompts))
+    r.admit(list(lens), sampling=SamplingParams(), seed=7)
+    g = torch.Generator(device=DEV).manual_seed(8)
+    r.text_embeds.normal_(generator=g)
+    r.predictor.output_embeds.normal_(generator=g)
+    r.admit_prefill(list(prompts), seed=9)
+    B = r.batch_size
+    seq0 = r.seq_lens[:B].cpu().numpy()
+    r2t0 = r.r2t.req_to_token.cpu().numpy()
+    free = r.allocator.free_pages.cpu().numpy()
+    head0 = int(r.allocator.free_head.item())
+    kpool = r.kv.k_buffer.float().cpu()
+    vpool = r.kv.v_buffer.float().cpu()
+    feedback = r.predictor.output_embeds[:B].clone().cpu()
+    text = r.text_embeds[:B].clone().cpu()
+    prompt = r.prompt_embeds.clone().cpu()
+    t = r.talker
+    n = B + len(prompts)
+    l0_state = dict(penalties=t.repetition_penalties[:n].cpu().numpy(), rep_mask=t.repetition_mask[:n].cpu().numpy(),
+                    suppress_mask=t.suppress_mask[:n].cpu().numpy(), temperature=t.sampling_temperatures[:n].cpu().numpy(),
+                    top_k=t.sampling_top_ks[:n].cpu().numpy(), top_p=t.sampling_top_ps[:n].cpu().numpy(),
+                    min_p=t.sampling_min_ps[:n].cpu().numpy(), seed=t.sampling_seeds[:n].cpu().numpy(),
+                    max_top_k=t.max_top_k)
+    r.step(use_graph=False)
+    torch.cuda.synchronize()
+    assert int(r.status.item()) == 0
+    sl, r2t1, loc, pos, _, _, pgp, pgi, head1 = orc.decode_prepare(seq0, np.arange(B), r2t0[:B], cfg.page_size, free,
+                                                                   free_head=head0)
+    # extend rows: positions 0..L-1 at the reserved slots; token j attends its stream's first j+1 slots
+    ext_pos, ext_loc, ext_ctx = [], [], []
+    for i, L in enumerate(prompts):
+        slots = torch.from_numpy(r2t0[B + i, :L].astype(np.int64))
+        ext_pos += list(range(L))
+        ext_loc += slots.tolist()
+        ext_ctx += [slots[: j + 1] for j in range(L)]
+    assert r.row_positions[B: B + sum(prompts)].cpu().tolist() == ext_pos
+    assert r.row_cache_loc[B: B + sum(prompts)].cpu().tolist() == ext_loc
+    assert r.row_cache_loc[:B].cpu().numpy().tolist() == loc.tolist()
+    o = OracleTalker(cfg, r.w, r.predictor.w)
+    select = list(range(B)) + [B + int(x) for x in np.cumsum(prompts) - 1]
+    logits_o, hidden_o = o.mixed_forward(feedback, text, torch.from_numpy(pos), torch.from_numpy(loc),
+                                         torch.from_numpy(sl), torch.from_numpy(r2t1), prompt, ext_pos, ext_loc,
+                                         ext_ctx, torch.tensor(select), kpool, vpool)
+    cos, err, scale = cos_err(t.logits[:n], logits_o)
+    assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0), (cos, err, scale)
+    cos, err, scale = cos_err(t.hidden[:n], hidden_o)
+    assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0), (cos, err, scale)
+    kdev = r.kv.k_buffer[:, torch.tensor(ext_loc, device=DEV)].float().cpu()
+    cos, err, scale = cos_err(kdev, kpool[:, torch.tensor(ext_loc)])
+    assert cos >= 0.999, cos
+    l0_state["positions"] = np.array(pos.tolist() + [L - 1 for L in prompts])
+    c0 = t.sampled_token_ids[:n].cpu()
+    assert o.layer0(t.logits[:n].cpu(), l0_state).tolist() == c0.tolist()
+    assert r.predictor.output_codes[:n, 0].cpu().tolist() == c0.tolist()
