@@ -374,8 +374,9 @@ def main() -> None:
                     help="with --config 3 under torchrun: experts sharded over the ranks (NCCL all-to-all)")
     ap.add_argument("--layers", type=int, default=0,
                     help="with --kernels: talker layers to build (0 = the config's 20); for small profiling runs")
-    ap.add_argument("--config", type=int, default=1, choices=[1, 3],
-                    help="1: dense talker, 64 streams (the headline); 3: MoE talker with FP8 experts, 256 streams")
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3],
+                    help="1: dense talker, 64 streams (the headline); 2: mixed prefill (16 new streams, prompts "
+                         "U[64, 4096]) + 112 decode streams; 3: MoE talker with FP8 experts, 256 streams")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -402,8 +403,14 @@ def main() -> None:
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     global STREAMS
+    prompts: list[int] = []
     if args.config == 3:
         cfg, STREAMS = CONFIG3_MOE, 256
+    elif args.config == 2:
+        cfg = CONFIG1_DENSE
+        prng = np.random.default_rng(100 + rank)
+        prompts = [int(x) for x in prng.integers(64, 4097, 16)]
+        STREAMS = 112  # decode streams; every step also prefills the 16 prompts
     else:
         cfg = CONFIG1_DENSE
     if args.layers and args.kernels:
@@ -415,9 +422,14 @@ def main() -> None:
     lens = context_lengths(STREAMS, seed=rank, headroom=total_steps + 8)
     P = cfg.page_size
     pages = int(sum(math.ceil((L + total_steps) / P) for L in lens) * 1.25) + STREAMS
+    pages += sum(math.ceil(L / P) for L in prompts)
     ep = bool(args.ep and cfg.moe is not None and world > 1)
-    runner = TalkerDecodeRunner(cfg, max_batch=STREAMS, num_pages=pages, seed=0, device=dev, expert_parallel=ep)
+    runner = TalkerDecodeRunner(cfg, max_batch=STREAMS + len(prompts), num_pages=pages, seed=0, device=dev,
+                                expert_parallel=ep, max_prefill_tokens=sum(prompts))
     runner.admit(lens, seed=rank)
+    if prompts:
+        runner.admit_prefill(prompts, seed=rank)
+    frames_per_step = STREAMS + len(prompts)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     runner.text_embeds.normal_(generator=g)
     if args.kernels:
@@ -459,7 +471,7 @@ def main() -> None:
     H = cfg.hidden_size
     G = cfg.predictor.num_code_groups
     text_host = torch.randn(STREAMS, H).to(torch.bfloat16).pin_memory()
-    codes_host = torch.empty((STREAMS, G), dtype=torch.long).pin_memory()
+    codes_host = torch.empty((frames_per_step, G), dtype=torch.long).pin_memory()
     for _ in range(W):
         runner.decode(text_host, codes_host)
     barrier()
@@ -480,19 +492,40 @@ def main() -> None:
     gcyc = {"i": 0}
     dense = cfg.moe is None
     gw = [lw["down_proj"] if dense else lw["o_proj"] for lw in t.w["layers"]]
-    g_in = t.act[:STREAMS] if dense else t.attn[:STREAMS]
+    R = STREAMS + sum(prompts)  # rows of the talker forward (config 2: decode rows + prompt rows)
+    g_in = t.act[:R] if dense else t.attn[:R]
     g_name = ("gemm_kernel<1>: talker down projection + residual + row sums of squares" if dense else
               "gemm_kernel<1>: talker o_proj + residual + row sums of squares")
 
     def gemm_next():
         li = gcyc["i"] % cfg.num_hidden_layers
         gcyc["i"] += 1
-        ops.linear_fused(g_in, gw[li], t.h[:STREAMS], epilogue=ops.EPI_RESIDUAL, residual=t.h[:STREAMS], ss_out=t.ss)
+        ops.linear_fused(g_in, gw[li], t.h[:R], epilogue=ops.EPI_RESIDUAL, residual=t.h[:R], ss_out=t.ss)
 
-    gemm_s = time_kernel(gemm_next, 60)
+    gemm_s = time_kernel(gemm_next, 20 if prompts else 60)
     gk, gn = g_in.shape[1], gw[0].shape[0]
     # weights + activations in + residual in + output + per-128-feature sums of squares
-    gemm_bytes = gn * gk * 2 + STREAMS * gk * 2 + 2 * STREAMS * gn * 2 + (gn // 128) * STREAMS * 4
+    gemm_bytes = gn * gk * 2 + R * gk * 2 + 2 * R * gn * 2 + (gn // 128) * R * 4
+    gemm_flops = 2.0 * R * gk * gn
+    pf_s = pf_flops = None
+    if prompts:
+        ext = runner.extend
+        pcyc = {"i": 0}
+        Bd = STREAMS
+
+        def prefill_next():
+            li = pcyc["i"] % cfg.num_hidden_layers
+            pcyc["i"] += 1
+            ops.prefill_attention(t.q[Bd:R], runner.kv.k_buffer[li], runner.kv.v_buffer[li],
+                                  qo_indptr=ext.qo_indptr, seq_lens=ext.seq_lens, page_indptr=ext.page_indptr,
+                                  page_indices=ext.page_indices, tile_indptr=ext.tile_indptr,
+                                  max_tiles=ext.max_tiles, num_q_heads=cfg.num_attention_heads,
+                                  num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim, page_size=P,
+                                  sm_scale=t.scale, out=t.attn[Bd:R])
+
+        pf_s = time_kernel(prefill_next, 20)
+        # causal QK^T and PV: 2 x 2 x Hq x D x L (L + 1) / 2 per prompt
+        pf_flops = sum(2.0 * cfg.num_attention_heads * cfg.head_dim * L * (L + 1) for L in prompts)
     attn_args = dict(page_indptr=fb.page_indptr, page_indices=fb.page_indices, seq_lens=fb.seq_lens,
                      work_indptr=fb.work_indptr, num_q_heads=cfg.num_attention_heads,
                      num_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim, page_size=P,
@@ -514,30 +547,34 @@ def main() -> None:
     # ---- gather over ranks: max of the device times, sum of the frames ----
     from omni_b200.replicas import aggregate_step_times
 
-    total_ms, e2e_ms, frames = aggregate_step_times(total_ms, e2e_ms, STREAMS * K, dist, dev)
+    total_ms, e2e_ms, frames = aggregate_step_times(total_ms, e2e_ms, frames_per_step * K, dist, dev)
     if rank == 0:
         hbm, tflops, peak_kind = measured_peaks()
         value = frames / (total_ms / 1000.0)
         e2e = frames / (e2e_ms / 1000.0)
         achieved = attn_bytes / attn_s / 1e9
         g_achieved = gemm_bytes / gemm_s / 1e9
+        workload = {
+            1: "config1: dense talker decode (20 layers, 64 streams, paged KV page 16, ctx lognormal(6,0.8) "
+               "clip [16,8192]) + config-0 predictor (15 codebooks)",
+            2: "config2: one fused forward of 112 decode streams (config-1 contexts) + 16 new streams' prompts "
+               f"(U[64,4096], sum {sum(prompts)} rows, KV written to the paged pool) through the 20-layer talker, "
+               "then layer-0 draw + 15-codebook predictor for all 128 streams",
+            3: "config3: MoE talker decode (20 layers, 128 experts top-8 inter 384 FP8 e4m3 128x128 block scales "
+               "+ shared expert 1536, 256 streams, paged KV page 16, ctx lognormal(6,0.8) clip [16,8192]) + "
+               "predictor (31 codebooks of 1024)"}[args.config]
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": total_ms / K, "p50_step_us": 1000 * float(np.median(step_ms)),
             "p99_step_us": 1000 * float(np.percentile(step_ms, 99)), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": ("config1: dense talker decode (20 layers, 64 streams, paged KV page 16, "
-                                    "ctx lognormal(6,0.8) clip [16,8192]) + config-0 predictor (15 codebooks)")
-                       if args.config == 1 else
-                       ("config3: MoE talker decode (20 layers, 128 experts top-8 inter 384 FP8 e4m3 "
-                        "128x128 block scales + shared expert 1536, 256 streams, paged KV page 16, "
-                        "ctx lognormal(6,0.8) clip [16,8192]) + predictor (31 codebooks of 1024)"),
+            "config": {"workload": workload,
                        "streams_per_gpu": STREAMS,
                        "parallelism": (f"ep{world}: experts sharded, NCCL all-to-all dispatch/combine per MoE layer"
                                        if ep else f"dp{world} replicas (no collective)"),
                        "sum_ctx_rank0": int(sum(lens)), "l2": "inputs > L2 (~3 GB streamed per step)"},
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": STREAMS * H * 2,
-                    "d2h_bytes_per_step": STREAMS * G * 8},
+                    "d2h_bytes_per_step": frames_per_step * G * 8},
             "gpu_launches": launches_per_step * K,
             "roofline": {"bound": "hbm", "kernel": g_name, "achieved": g_achieved, "peak": hbm, "unit": "GB/s",
                          "frac": g_achieved / hbm,
@@ -552,6 +589,17 @@ def main() -> None:
                                    "launch_us": attn_s * 1e6, "peak_kind": peak_kind},
             "clocks": clocks.summary(),
         }
+        if prompts:
+            # the rows are many: the projections are tensor-bound
+            line["roofline"] = {"bound": "tensor", "kernel": g_name + f" ({R} rows)",
+                                "achieved": gemm_flops / gemm_s / 1e12, "peak": tflops, "unit": "TFLOP/s",
+                                "frac": gemm_flops / gemm_s / 1e12 / tflops, "traffic": None,
+                                "algorithmic_flops": gemm_flops, "launch_us": gemm_s * 1e6, "peak_kind": peak_kind}
+            line["roofline_prefill_attention"] = {
+                "bound": "tensor", "kernel": "prefill_attention_kernel (mma.sync)",
+                "achieved": pf_flops / pf_s / 1e12, "peak": tflops, "unit": "TFLOP/s",
+                "frac": pf_flops / pf_s / 1e12 / tflops, "algorithmic_flops": pf_flops, "launch_us": pf_s * 1e6,
+                "peak_kind": peak_kind}
         if not args.no_cpu and args.config == 1:
             rate, desc, _ = cpu_step_rate(args.cpu_steps, 1)
             line["cpu_baseline"] = {"value": rate, "unit": UNIT, **desc}

@@ -332,12 +332,14 @@ class TalkerDecodeRunner:
     # ------------------------------------------------------------------
     def decode(self, text_embeds_host: torch.Tensor, codes_host: torch.Tensor | None = None) -> torch.Tensor:
         """One frame for every live stream: copy the text rows in (pinned host -> HBM),
-        replay the step graph, copy the frame's codes out.  Returns codes [B, G] on the host."""
+        replay the step graph, copy the frame's codes out.  Returns codes [B, G] on the host
+        (in a mixed step also the new streams' first frames, after the decode rows)."""
         B = self.batch_size
+        n = B + (self.extend.streams if self.extend is not None else 0)  # + the new streams' first frames
         self.text_embeds[:B].copy_(text_embeds_host, non_blocking=True)
         self.step(use_graph=self.graph is not None)
         if codes_host is None:
-            codes_host = torch.empty((B, self.cfg.predictor.num_code_groups), dtype=torch.long, pin_memory=True)
-        codes_host.copy_(self.predictor.output_codes[:B], non_blocking=True)
+            codes_host = torch.empty((n, self.cfg.predictor.num_code_groups), dtype=torch.long, pin_memory=True)
+        codes_host.copy_(self.predictor.output_codes[:n], non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
         return codes_host
