@@ -99,7 +99,12 @@ OMNI_DEVINL uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-OMNI_DEVINL void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+// Relaxed arrive: neither cluster barrier of the kernel publishes generic-proxy data.
+// "Buffers drained" follows the MMA completion observed on an mbarrier, and "rows
+// received" follows the copy completion observed on an mbarrier; the barrier
+// initialisation is ordered by fence.mbarrier_init.release.cluster before it.
+// (A release arrive costs about 0.4 us per barrier here.)
+OMNI_DEVINL void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 OMNI_DEVINL void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 // Generic-proxy shared-memory writes of this thread made visible to the bulk-copy engine.
 OMNI_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
