@@ -4,6 +4,7 @@
 #include <cstring>
 #include <cstdio>
 #include <mutex>
+#include <unordered_set>
 #include <vector>
 
 #include "common.cuh"
@@ -47,6 +48,19 @@ bool pdl_enabled() {
     return (v && v[0] == '0') ? 0 : 1;
   }();
   return enabled != 0;
+}
+
+// Every kernel of the library asks for the largest shared-memory carveout, so
+// that all SMs keep one L1/shared split: an SM can only change its split while
+// it is idle, so kernels that prefer different splits cannot overlap through
+// programmatic dependent launch.
+void prefer_max_shared(const void* fn) {
+  static std::mutex mu;
+  static std::unordered_set<const void*> done;
+  std::lock_guard<std::mutex> g(mu);
+  if (!done.insert(fn).second) return;
+  cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+  cudaGetLastError();
 }
 
 }  // namespace omni

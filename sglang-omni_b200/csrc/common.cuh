@@ -46,6 +46,7 @@ OMNI_DEVINL void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memor
 OMNI_DEVINL void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 bool pdl_enabled();
+void prefer_max_shared(const void* fn);
 
 template <typename... KArgs, typename... Args>
 cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
@@ -60,6 +61,7 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  prefer_max_shared(reinterpret_cast<const void*>(kernel));
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 

@@ -10,17 +10,17 @@
 //
 // Split-K: the S CTAs that share a feature tile form one thread-block cluster
 // (S <= 16, chosen so that every cluster of the grid is co-resident).  CTA c
-// owns the c-th contiguous block of the tile's rows.  Each CTA stages its fp32
-// partial tile in its own shared memory and sends every owner that owner's
-// block of rows with one bulk shared-to-shared copy into the owner's drained
-// pipeline buffers (completion on the owner's mbarrier); the owner sums the S
-// blocks in split order (deterministic), applies the epilogue and stores.  Two
-// split-phase cluster barriers order this: "buffers drained" (arrive before the
-// staging, wait before sending) and "all blocks received" (arrive before the
-// epilogue, wait before exit, so no CTA leaves while its partial is still being
-// copied).  The epilogue operands of the owned rows (RMSNorm scale, rotary
-// position, KV slot, residual) are fetched while the MMAs run.  No global
-// scratch memory.
+// owns the c-th contiguous block of the tile's rows.  Each CTA reads its fp32
+// partial tile out of TMEM and stores every row straight into the owning CTA's
+// shared memory (distributed shared memory), into the owner's receive slot for
+// split c, over the owner's drained pipeline buffers; the owner sums its S
+// slots in split order (deterministic), applies the epilogue and stores.  Two
+// cluster barriers order this: "buffers drained" (split-phase: arrive once the
+// MMAs are complete, wait before the first remote store) and "all partials
+// stored" (release / acquire, before the reduction).  After the second no CTA
+// touches another's shared memory, so each leaves when its epilogue is done.
+// The epilogue operands of the owned rows (RMSNorm scale, rotary position, KV
+// slot, residual) are fetched while the MMAs run.  No global scratch memory.
 //
 // Programmatic dependent launch: weights never depend on the previous kernel,
 // so the producer issues the first stages' weight loads before
@@ -99,24 +99,15 @@ OMNI_DEVINL uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-// Relaxed arrive: neither cluster barrier of the kernel publishes generic-proxy data.
-// "Buffers drained" follows the MMA completion observed on an mbarrier, and "rows
-// received" follows the copy completion observed on an mbarrier; the barrier
-// initialisation is ordered by fence.mbarrier_init.release.cluster before it.
-// (A release arrive costs about 0.4 us per barrier here.)
+// Relaxed arrive for "buffers drained": no generic-proxy data crosses it (it follows
+// the MMA completion observed on an mbarrier).  (A release arrive costs about 0.4 us
+// here.)  "All partials stored" publishes the remote stores, so it releases.
 OMNI_DEVINL void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+OMNI_DEVINL void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 OMNI_DEVINL void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-// Generic-proxy shared-memory writes of this thread made visible to the bulk-copy engine.
-OMNI_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-// Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory to a peer's
-// (both addresses 16-byte aligned); completes `bytes` of transactions on the
-// peer's mbarrier.
-OMNI_DEVINL void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes, uint32_t bar_cluster) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst_cluster),
-      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
-      : "memory");
+// Store to a shared::cluster address (this CTA's own shared memory or a peer's).
+OMNI_DEVINL void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v));
 }
 // Address of the same shared-memory offset in CTA `rank` of the cluster.
 OMNI_DEVINL uint32_t map_cluster(uint32_t local, uint32_t rank) {
@@ -139,11 +130,12 @@ OMNI_DEVINL RowBlock row_block(int rows_here, int S, int q) {
   return b;
 }
 
-// Two CTAs fit on an SM (<= 128 registers a thread) for the epilogues that need no
-// more, so that with programmatic dependent launch the next GEMM's CTAs can start,
-// and stream their weights, beside the CTAs of the current one.
+// Two CTAs fit on an SM (<= 128 registers a thread) for every epilogue but the fp32
+// one (the codec head, once a step), so that with programmatic dependent launch the
+// next GEMM's CTAs can start, and stream their weights, beside the CTAs of the
+// current one.
 template <int EPI>
-__global__ void __launch_bounds__(kThreadsG, (EPI == kEpiSwiGLU || EPI == kEpiF32) ? 1 : 2)
+__global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                 const __grid_constant__ GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -160,19 +152,17 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiSwiGLU || EPI == kEpiF3
   const uint32_t crank = S > 1 ? cluster_ctarank() : 0u;
   const RowBlock mine = row_block(rows_here, S, (int)crank);
   // shared memory: region [stages A][stages B], then [row info][barriers].  After
-  // the main loop the region holds this CTA's fp32 partial tile [rows][128] and,
-  // behind it, the S-1 peers' partials of the owned rows [S-1][per][128].
+  // the main loop the region holds the S splits' fp32 partials of the owned rows,
+  // receive slots [S][per][128] (slot q written by cluster rank q).
   uint8_t* a_smem = smem;
   uint8_t* b_smem = smem + ST * a_bytes;
   float* row_info = reinterpret_cast<float*>(smem + p.region);  // [per] rstd, [per] position, [per] slot
   uint64_t* full = reinterpret_cast<uint64_t*>(row_info + 3 * ((mine.per + 1) & ~1));
   uint64_t* empty = full + kMaxStages;
   uint64_t* mma_done = empty + kMaxStages;
-  uint64_t* recv_bar = mma_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 2);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort
-  float* stage = reinterpret_cast<float*>(smem);
-  float* recv = stage + Rt * kTileN;
+  float* recv = reinterpret_cast<float*>(smem);
 
   const int kb_begin = (int)(((int64_t)p.num_kb * split) / S);
   const int kb_end = (int)(((int64_t)p.num_kb * (split + 1)) / S);
@@ -184,11 +174,8 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiSwiGLU || EPI == kEpiF3
       mbar_init(&empty[s], 1);
     }
     mbar_init(mma_done, 1);
-    mbar_init(recv_bar, 1);
     flags[0] = 0;
     fence_barrier_init();
-    // the owned rows arrive from the S-1 peers (no phase to wait for when S == 1)
-    mbar_arrive_expect_tx(recv_bar, (uint32_t)((S - 1) * mine.count * kTileN * 4));
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
   }
@@ -288,7 +275,7 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiSwiGLU || EPI == kEpiF3
   }
   __syncwarp();
 
-  // ---- accumulators: TMEM -> smem staging [rows][128] fp32 ----
+  // ---- accumulators: TMEM -> the owners' receive slots (distributed shared memory) ----
   const bool have_acc = nk > 0;
   if (have_acc) {
     if (!mbar_wait(mma_done, 0)) {
@@ -298,7 +285,7 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiSwiGLU || EPI == kEpiF3
   }
   tc_fence_after();
   __syncthreads();
-  // the pipeline buffers are drained: peers may write this CTA's rows into them
+  // the pipeline buffers are drained: peers may store their partials into them
   if (S > 1) cluster_arrive();
   bool aborted = flags[0] != 0;
   // the residual rows this thread will add, fetched ahead of the reduction
@@ -314,10 +301,27 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiSwiGLU || EPI == kEpiF3
                                                      (int64_t)tile * kTileN + (idx & 31) * 4);
     }
   }
+  if (S > 1) cluster_wait();  // every peer's buffers are drained
   if (!aborted) {
     // warp w: TMEM lanes (features) 32 (w % 4) .., 32-column chunks w / 4, w / 4 + 2, ...
     const int f = (warp & 3) * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    // feature f of this CTA's slot in every owner: [crank][rr][f], the same offset in each
+    const uint32_t slot_f = smem_u32(recv) + (uint32_t)(((int)crank * mine.per * kTileN + f) * 4);
+    // row r goes to owner r / per, row r % per of its block
+    auto send_rows = [&](int cb, const uint32_t(&r)[32]) {
+      int q = cb / mine.per, rr = cb - q * mine.per;
+      uint32_t dst = S > 1 ? map_cluster(slot_f, (uint32_t)q) : slot_f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (cb + j < rows_here) st_cluster_f32(dst + (uint32_t)(rr * kTileN * 4), __uint_as_float(r[j]));
+        if (++rr == mine.per) {
+          rr = 0;
+          ++q;
+          if (S > 1 && q < S) dst = map_cluster(slot_f, (uint32_t)q);
+        }
+      }
+    };
     for (int c0 = (warp >> 2) * 32; c0 < rows_here; c0 += 128) {
       // two 32-column loads in flight per wait
       uint32_t r0[32], r1[32];
@@ -329,53 +333,26 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiSwiGLU || EPI == kEpiF3
 #pragma unroll
         for (int j = 0; j < 32; ++j) r0[j] = r1[j] = 0u;
       }
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c0 + j < rows_here) stage[(c0 + j) * kTileN + f] = __uint_as_float(r0[j]);
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c0 + 64 + j < rows_here) stage[(c0 + 64 + j) * kTileN + f] = __uint_as_float(r1[j]);
+      send_rows(c0, r0);
+      if (c0 + 64 < rows_here) send_rows(c0 + 64, r1);
     }
   }
   tc_fence_before();
-  fence_proxy_async_smem();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
   if (S > 1) {
-    cluster_wait();  // every peer's buffers are drained and its barriers initialised
-    if (threadIdx.x == 0) {
-      // each owner gets its block of this partial, into slot (split index, skipping its own)
-      for (int q = 0; q < S; ++q) {
-        if (q == (int)crank) continue;
-        const RowBlock ob = row_block(rows_here, S, q);
-        if (ob.count == 0) continue;
-        const int slot = (int)crank < q ? (int)crank : (int)crank - 1;
-        const uint32_t dst = smem_u32(recv + (size_t)slot * ob.per * kTileN);
-        bulk_copy_to_peer(map_cluster(dst, (uint32_t)q), smem_u32(stage + (size_t)ob.begin * kTileN),
-                          (uint32_t)(ob.count * kTileN * 4), map_cluster(smem_u32(recv_bar), (uint32_t)q));
-      }
-    }
-    if (!mbar_wait(recv_bar, 0)) {
-      report_status(kDevTimeoutTma);
-      flags[0] = 1;
-    }
-    __syncthreads();
-    aborted = flags[0] != 0;
-    cluster_arrive();  // this CTA's rows are in; its copies out are complete once every owner arrives
+    // every split's partial of the owned rows is stored: after this barrier no CTA
+    // touches another's shared memory
+    cluster_arrive_release();
+    cluster_wait();
   }
 
   // ---- sum the owned rows' partials in split order and apply the epilogue ----
-  const float4* own4 = reinterpret_cast<const float4*>(stage);
-  const float4* recv4 = reinterpret_cast<const float4*>(recv);
   auto acc4 = [&](int i, int f) -> float4 {
-    const int r = mine.begin + i;
     float4 v[kMaxSplits];
 #pragma unroll
     for (int q = 0; q < kMaxSplits; ++q)
-      if (q < S) {
-        const int c = (int)crank;
-        v[q] = q == c ? own4[(r * kTileN + f) >> 2] : recv4[(((q < c ? q : q - 1) * mine.per + i) * kTileN + f) >> 2];
-      }
+      if (q < S) v[q] = *reinterpret_cast<const float4*>(recv + (q * mine.per + i) * kTileN + f);
     float4 a = v[0];
 #pragma unroll
     for (int q = 1; q < kMaxSplits; ++q)
@@ -395,7 +372,22 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiSwiGLU || EPI == kEpiF3
       const int i = idx >> 4;
       const int g = (idx & 15) * 4;
       const float sc = row_info[i];
-      const float4 gt = acc4(i, g), up = acc4(i, 64 + g);
+      // gate and up summed side by side in split order (two CTAs per SM leave no
+      // registers for all S slots of both in flight)
+      const float* slot = recv + i * kTileN + g;
+      float4 gt = *reinterpret_cast<const float4*>(slot), up = *reinterpret_cast<const float4*>(slot + 64);
+      for (int q = 1; q < S; ++q) {
+        const float4 a = *reinterpret_cast<const float4*>(slot + q * mine.per * kTileN);
+        const float4 b = *reinterpret_cast<const float4*>(slot + q * mine.per * kTileN + 64);
+        gt.x += a.x;
+        gt.y += a.y;
+        gt.z += a.z;
+        gt.w += a.w;
+        up.x += b.x;
+        up.y += b.y;
+        up.z += b.z;
+        up.w += b.w;
+      }
       const float gg[4] = {gt.x, gt.y, gt.z, gt.w}, uu[4] = {up.x, up.y, up.z, up.w};
       float o[4];
 #pragma unroll
@@ -403,7 +395,6 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiSwiGLU || EPI == kEpiF3
       *reinterpret_cast<uint2*>(Y + (int64_t)(row0 + mine.begin + i) * p.y_stride + tile * 64 + g) =
           make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
     }
-    if (S > 1) cluster_wait();
     return;
   }
   // one warp per owned row, lane l holds features 4l..4l+3; kPre rows per thread per
@@ -557,7 +548,6 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiSwiGLU || EPI == kEpiF3
     }
   }
   }
-  if (S > 1) cluster_wait();  // every owner has its rows: no copy still reads this CTA's partial
 }
 
 // ---------------------------------------------------------------------------
@@ -610,6 +600,7 @@ void set_kernel_attrs() {
   std::call_once(once, [] {
     cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    prefer_max_shared(reinterpret_cast<const void*>(gemm_kernel<EPI>));
   });
 }
 
@@ -651,12 +642,11 @@ int max_active_clusters(int S, size_t smem) {
 }
 
 // Bytes of the region that holds the pipeline stages during the main loop and,
-// after it, the partial tile [row_tile][128] fp32 plus the peers' partials of
-// the owned rows [splits - 1][per][128] fp32.
+// after it, the receive slots of the owned rows [splits][per][128] fp32.
 size_t plan_region(int row_tile, int stages, int splits) {
   const size_t stage_bytes = (size_t)kTileN * kBK * 2 + (size_t)row_tile * kBK * 2;
   const int per = (row_tile + splits - 1) / splits;
-  const size_t partials = (size_t)row_tile * kTileN * 4 + (size_t)(splits - 1) * per * kTileN * 4;
+  const size_t partials = (size_t)splits * per * kTileN * 4;
   const size_t r = (size_t)stages * stage_bytes > partials ? (size_t)stages * stage_bytes : partials;
   return (r + 1023) & ~(size_t)1023;
 }
