@@ -26,8 +26,9 @@
 // so the producer issues the first stages' weight loads before
 // griddepcontrol.wait, overlapping them with the predecessor's tail.
 //
-// Roles (256 threads): warp 0 lane 0 = TMA producer, warp 1 lane 0 = MMA
-// issuer, warps 2-7 = epilogue operands during the main loop; all eight warps
+// Roles (256 threads): warp 0 = TMA producer, warp 1 = MMA issuer (each warp
+// walks its loop together, one elected lane issues), warps 2-7 = epilogue
+// operands during the main loop; all eight warps
 // drain TMEM (warp w reads lanes 32 (w % 4) .. + 31, column half w / 4) and run
 // the epilogue.
 #include <cuda.h>
@@ -210,42 +211,69 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   griddep_wait();
   griddep_launch();
 
-  if (warp == 0 && lane == 0) {
-    // producer
-    for (int i = 0; i < pre; ++i) tma_load_2d(b_smem + i * b_bytes, &tmap_x, &full[i], (kb_begin + i) * kBK, row0);
+  if (warp == 0) {
+    // producer: the whole warp walks the stages (warp-uniform addresses and
+    // phases), one elected lane issues the copies
+    const bool leader = elect_one();
+    if (leader)
+      for (int i = 0; i < pre; ++i) tma_load_2d(b_smem + i * b_bytes, &tmap_x, &full[i], (kb_begin + i) * kBK, row0);
+    int s = 0;
+    uint32_t ph = 0;
     for (int i = pre; i < nk; ++i) {
-      const int s = i % ST;
-      if (!mbar_wait(&empty[s], ((i / ST) - 1) & 1)) {
-        report_status(kDevTimeoutMma);
-        flags[0] = 1;
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&empty[s], ph))) {
+        if (leader) {
+          report_status(kDevTimeoutMma);
+          flags[0] = 1;
+        }
         break;
       }
-      mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
-      load_w(s, kb_begin + i);
-      tma_load_2d(b_smem + s * b_bytes, &tmap_x, &full[s], (kb_begin + i) * kBK, row0);
+      if (leader) {
+        mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
+        load_w(s, kb_begin + i);
+        tma_load_2d(b_smem + s * b_bytes, &tmap_x, &full[s], (kb_begin + i) * kBK, row0);
+      }
+      __syncwarp();
+      if (++s == ST) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer
+  } else if (warp == 1) {
+    // MMA issuer: the whole warp waits, one elected lane issues
+    const bool leader = elect_one();
     const uint32_t idesc = idesc_bf16_f32(kTileN, Rt);
+    const uint64_t ad0 = smem_desc_sw128(a_smem), bd0 = smem_desc_sw128(b_smem);
     bool ok = true;
+    int s = 0;
+    uint32_t ph = 0;
     for (int i = 0; i < nk; ++i) {
-      const int s = i % ST;
-      if (!mbar_wait(&full[s], (i / ST) & 1)) {
-        report_status(kDevTimeoutTma);
-        flags[0] = 1;
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full[s], ph))) {
+        if (leader) {
+          report_status(kDevTimeoutTma);
+          flags[0] = 1;
+        }
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint64_t ad = smem_desc_sw128(a_smem + s * a_bytes);
-      const uint64_t bd = smem_desc_sw128(b_smem + s * b_bytes);
+      // descriptor start addresses advance by 16-byte units: a stage, then 32 bytes per K step
+      const uint64_t ad = ad0 + (uint64_t)(s * (a_bytes >> 4)), bd = bd0 + (uint64_t)(s * (b_bytes >> 4));
+      if (leader) {
 #pragma unroll
-      for (int kk = 0; kk < kBK / 16; ++kk)
-        tc_mma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-      tc_commit(&empty[s]);
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          tc_mma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&empty[s]);
+      }
+      __syncwarp();
+      if (++s == ST) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
-    if (ok) tc_commit(mma_done);
-    else mbar_arrive(mma_done);
+    if (leader) {
+      if (ok) tc_commit(mma_done);
+      else mbar_arrive(mma_done);
+    }
   } else if (warp >= 2) {
     // while the MMAs run: per-row epilogue operands of the rows this CTA owns
     for (int i = threadIdx.x - 64; i < mine.count; i += kThreadsG - 64) {
