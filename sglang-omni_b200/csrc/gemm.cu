@@ -3,18 +3,23 @@
 //   Y[rows, N] = epilogue( X[rows, K] . W[N, K]^T )        (nn.Linear layout)
 //
 // Decode-step projections have few activation rows (8-512) and many output
-// features, so the kernel is "swap-AB": a CTA owns 128 output features, which
-// sit on the MMA's M axis (TMEM lanes), and up to 256 activation rows, which
-// sit on its N axis (TMEM columns).  W tiles (128 x 64, bf16, 128-byte
-// swizzle) stream from HBM through a TMA pipeline; X tiles come from L2.
+// features.  A CTA owns 128 output features (the MMA's N axis, TMEM columns)
+// and up to 256 activation rows (the M axis, TMEM lanes, one or two M = 128
+// accumulators; rows past the tile are don't-care rows of the MMA that are
+// never read back).  W tiles (128 x 64, bf16, 128-byte swizzle) stream from HBM
+// through a TMA pipeline; X tiles come from L2.  With a row on each TMEM lane,
+// a thread drains 32 consecutive features of one row per load and moves them
+// with 16-byte stores.
 //
 // Split-K: the S CTAs that share a feature tile form one thread-block cluster
 // (S <= 16, chosen so that every cluster of the grid is co-resident).  CTA c
 // owns the c-th contiguous block of the tile's rows.  Each CTA reads its fp32
 // partial tile out of TMEM and stores every row straight into the owning CTA's
 // shared memory (distributed shared memory), into the owner's receive slot for
-// split c, over the owner's drained pipeline buffers; the owner sums its S
-// slots in split order (deterministic), applies the epilogue and stores.  Two
+// split c, over the owner's drained pipeline buffers (16-byte chunks of a row
+// XOR-swizzled by the row index, so that consecutive rows hit different
+// banks); the owner sums its S slots in split order (deterministic), applies
+// the epilogue and stores.  Two
 // cluster barriers order this: "buffers drained" (split-phase: arrive once the
 // MMAs are complete, wait before the first remote store) and "all partials
 // stored" (release / acquire, before the reduction).  After the second no CTA
@@ -61,7 +66,7 @@ struct GemmParams {
   int num_kb;       // K / 64
   int splits;       // CTAs per (feature tile, row tile)
   int stages;       // pipeline depth
-  int tmem_cols;    // power of two >= row_tile
+  int tmem_cols;    // 128 per 128-row accumulator
   int region;       // bytes of the pipeline / partial-tile region (1024-aligned)
   int swiglu_half;  // I for SwiGLU (gate rows [0, I), up rows [I, 2I))
   const uint16_t* residual;
@@ -106,9 +111,18 @@ OMNI_DEVINL uint32_t cluster_ctarank() {
 OMNI_DEVINL void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 OMNI_DEVINL void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 OMNI_DEVINL void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-// Store to a shared::cluster address (this CTA's own shared memory or a peer's).
-OMNI_DEVINL void st_cluster_f32(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v));
+// 16-byte store to a shared::cluster address (this CTA's own shared memory or a peer's).
+OMNI_DEVINL void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d));
+}
+// Byte offset of features 4c .. 4c + 3 in a received row rr: [rr][32 chunks of 16 B],
+// chunk index XOR (rr mod 8).
+OMNI_DEVINL uint32_t recv_off(int rr, int chunk) { return (uint32_t)(rr * kTileN * 4 + ((chunk ^ (rr & 7)) << 4)); }
+// Shared-memory load by shared-window address.
+OMNI_DEVINL float4 ld_shared_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
 }
 // Address of the same shared-memory offset in CTA `rank` of the cluster.
 OMNI_DEVINL uint32_t map_cluster(uint32_t local, uint32_t rank) {
@@ -241,8 +255,10 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   } else if (warp == 1) {
     // MMA issuer: the whole warp waits, one elected lane issues
     const bool leader = elect_one();
-    const uint32_t idesc = idesc_bf16_f32(kTileN, Rt);
-    const uint64_t ad0 = smem_desc_sw128(a_smem), bd0 = smem_desc_sw128(b_smem);
+    // A = X (rows on M, one accumulator per 128 rows), B = W (128 features on N)
+    const uint32_t idesc = idesc_bf16_f32(128, kTileN);
+    const uint64_t wd0 = smem_desc_sw128(a_smem), xd0 = smem_desc_sw128(b_smem);
+    const int halves = (Rt + 127) / 128;
     bool ok = true;
     int s = 0;
     uint32_t ph = 0;
@@ -257,11 +273,14 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
       }
       tc_fence_after();
       // descriptor start addresses advance by 16-byte units: a stage, then 32 bytes per K step
-      const uint64_t ad = ad0 + (uint64_t)(s * (a_bytes >> 4)), bd = bd0 + (uint64_t)(s * (b_bytes >> 4));
+      // (rows 128 h .. of the X stage sit 16 KB apart)
+      const uint64_t wd = wd0 + (uint64_t)(s * (a_bytes >> 4)), xd = xd0 + (uint64_t)(s * (b_bytes >> 4));
       if (leader) {
+        for (int h = 0; h < halves; ++h)
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)
-          tc_mma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc_mma_bf16(tmem + (uint32_t)(h * kTileN), xd + (uint64_t)(h * 1024) + 2 * kk, wd + 2 * kk, idesc,
+                        (i > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&empty[s]);
       }
       __syncwarp();
@@ -331,38 +350,32 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   }
   if (S > 1) cluster_wait();  // every peer's buffers are drained
   if (!aborted) {
-    // warp w: TMEM lanes (features) 32 (w % 4) .., 32-column chunks w / 4, w / 4 + 2, ...
-    const int f = (warp & 3) * 32 + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    // feature f of this CTA's slot in every owner: [crank][rr][f], the same offset in each
-    const uint32_t slot_f = smem_u32(recv) + (uint32_t)(((int)crank * mine.per * kTileN + f) * 4);
-    // row r goes to owner r / per, row r % per of its block
-    auto send_rows = [&](int cb, const uint32_t(&r)[32]) {
-      int q = cb / mine.per, rr = cb - q * mine.per;
-      uint32_t dst = S > 1 ? map_cluster(slot_f, (uint32_t)q) : slot_f;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (cb + j < rows_here) st_cluster_f32(dst + (uint32_t)(rr * kTileN * 4), __uint_as_float(r[j]));
-        if (++rr == mine.per) {
-          rr = 0;
-          ++q;
-          if (S > 1 && q < S) dst = map_cluster(slot_f, (uint32_t)q);
-        }
-      }
-    };
-    for (int c0 = (warp >> 2) * 32; c0 < rows_here; c0 += 128) {
-      // two 32-column loads in flight per wait
-      uint32_t r0[32], r1[32];
+    // warp w: TMEM lanes 32 (w % 4) .. + 31 (one row each) of every 128-row
+    // accumulator, features 64 (w / 4) .. + 63
+    const int sp = warp & 3, fh = warp >> 2;
+    const uint32_t slot_base = smem_u32(recv) + (uint32_t)((int)crank * mine.per * kTileN * 4);
+    for (int h = 0; h * 128 + sp * 32 < rows_here; ++h) {
+      uint32_t v[64];
+      const uint32_t taddr = tmem + ((uint32_t)(sp * 32) << 16) + (uint32_t)(h * kTileN + fh * 64);
       if (have_acc) {
-        tmem_ld_32x32b_x32(lane_base + (uint32_t)c0, r0);
-        if (c0 + 64 < rows_here) tmem_ld_32x32b_x32(lane_base + (uint32_t)(c0 + 64), r1);
+        tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tc_wait_ld();
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r0[j] = r1[j] = 0u;
+        for (int j = 0; j < 64; ++j) v[j] = 0u;
       }
-      send_rows(c0, r0);
-      if (c0 + 64 < rows_here) send_rows(c0 + 64, r1);
+      const int r = h * 128 + sp * 32 + lane;
+      if (r < rows_here) {
+        // row r goes to owner r / per, row r % per of its block, slot crank
+        const int q = r / mine.per, rr = r - q * mine.per;
+        const uint32_t local = slot_base + (uint32_t)(rr * kTileN * 4);
+        const uint32_t dst = S > 1 ? map_cluster(local, (uint32_t)q) : local;
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          st_cluster_v4(dst + (uint32_t)((((fh * 16 + c) ^ (rr & 7))) << 4), v[4 * c], v[4 * c + 1], v[4 * c + 2],
+                        v[4 * c + 3]);
+      }
     }
   }
   tc_fence_before();
@@ -376,11 +389,14 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   }
 
   // ---- sum the owned rows' partials in split order and apply the epilogue ----
+  const uint32_t recv_u32 = smem_u32(recv);
+  const uint32_t slot_bytes = (uint32_t)(mine.per * kTileN * 4);
   auto acc4 = [&](int i, int f) -> float4 {
     float4 v[kMaxSplits];
+    const uint32_t a0 = recv_u32 + recv_off(i, f >> 2);
 #pragma unroll
     for (int q = 0; q < kMaxSplits; ++q)
-      if (q < S) v[q] = *reinterpret_cast<const float4*>(recv + (q * mine.per + i) * kTileN + f);
+      if (q < S) v[q] = ld_shared_f4(a0 + (uint32_t)q * slot_bytes);
     float4 a = v[0];
 #pragma unroll
     for (int q = 1; q < kMaxSplits; ++q)
@@ -402,11 +418,11 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
       const float sc = row_info[i];
       // gate and up summed side by side in split order (two CTAs per SM leave no
       // registers for all S slots of both in flight)
-      const float* slot = recv + i * kTileN + g;
-      float4 gt = *reinterpret_cast<const float4*>(slot), up = *reinterpret_cast<const float4*>(slot + 64);
+      const uint32_t sg = recv_u32 + recv_off(i, g >> 2), su = recv_u32 + recv_off(i, (g >> 2) + 16);
+      float4 gt = ld_shared_f4(sg), up = ld_shared_f4(su);
       for (int q = 1; q < S; ++q) {
-        const float4 a = *reinterpret_cast<const float4*>(slot + q * mine.per * kTileN);
-        const float4 b = *reinterpret_cast<const float4*>(slot + q * mine.per * kTileN + 64);
+        const float4 a = ld_shared_f4(sg + (uint32_t)q * slot_bytes);
+        const float4 b = ld_shared_f4(su + (uint32_t)q * slot_bytes);
         gt.x += a.x;
         gt.y += a.y;
         gt.z += a.z;
@@ -673,9 +689,13 @@ int max_active_clusters(int S, size_t smem) {
 // after it, the receive slots of the owned rows [splits][per][128] fp32.
 size_t plan_region(int row_tile, int stages, int splits) {
   const size_t stage_bytes = (size_t)kTileN * kBK * 2 + (size_t)row_tile * kBK * 2;
+  // the MMA reads 128 rows of every X stage: behind the last stage of a tile
+  // shorter than 128 rows, a pad keeps those don't-care rows inside the region
+  const size_t pad = row_tile < 128 ? (size_t)(128 - row_tile) * kBK * 2 : 0;
   const int per = (row_tile + splits - 1) / splits;
   const size_t partials = (size_t)splits * per * kTileN * 4;
-  const size_t r = (size_t)stages * stage_bytes > partials ? (size_t)stages * stage_bytes : partials;
+  const size_t pipe = (size_t)stages * stage_bytes + pad;
+  const size_t r = pipe > partials ? pipe : partials;
   return (r + 1023) & ~(size_t)1023;
 }
 
@@ -754,9 +774,8 @@ Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
   if (best < 1) best = 1;
   pl.splits = best;
   pl.stages = plan_stages(pl.row_tile, (pl.num_kb + best - 1) / best, best);
-  int tc = 32;
-  while (tc < pl.row_tile) tc <<= 1;
-  pl.tmem_cols = tc;
+  // one 128-column fp32 accumulator (128 features) per 128 rows
+  pl.tmem_cols = pl.row_tile > 128 ? 256 : 128;
   pl.smem = plan_smem(pl.row_tile, pl.stages, best);
   pl.region = (int)plan_region(pl.row_tile, pl.stages, best);
   return pl;
