@@ -3,27 +3,24 @@
 //   Y[rows, N] = epilogue( X[rows, K] . W[N, K]^T )        (nn.Linear layout)
 //
 // Decode-step projections have few activation rows (8-512) and many output
-// features.  A CTA owns 128 output features (the MMA's N axis, TMEM columns)
-// and up to 256 activation rows (the M axis, TMEM lanes, one or two M = 128
-// accumulators; rows past the tile are don't-care rows of the MMA that are
-// never read back).  W tiles (128 x 64, bf16, 128-byte swizzle) stream from HBM
-// through a TMA pipeline; X tiles come from L2.  With a row on each TMEM lane,
-// a thread drains 32 consecutive features of one row per load and moves them
-// with 16-byte stores.
+// features, so the kernel is "swap-AB": a CTA owns 128 output features, which
+// sit on the MMA's M axis (TMEM lanes), and up to 256 activation rows, which
+// sit on its N axis (TMEM columns).  W tiles (128 x 64, bf16, 128-byte
+// swizzle) stream from HBM through a TMA pipeline; X tiles come from L2.
 //
 // Split-K: the S CTAs that share a feature tile form one thread-block cluster
 // (S <= 16, chosen so that every cluster of the grid is co-resident).  CTA c
-// owns the c-th contiguous block of the tile's rows.  Each CTA reads its fp32
-// partial tile out of TMEM and stores every row straight into the owning CTA's
-// shared memory (distributed shared memory), into the owner's receive slot for
-// split c, over the owner's drained pipeline buffers (16-byte chunks of a row
-// XOR-swizzled by the row index, so that consecutive rows hit different
-// banks); the owner sums its S slots in split order (deterministic), applies
-// the epilogue and stores.  Two
-// cluster barriers order this: "buffers drained" (split-phase: arrive once the
-// MMAs are complete, wait before the first remote store) and "all partials
-// stored" (release / acquire, before the reduction).  After the second no CTA
-// touches another's shared memory, so each leaves when its epilogue is done.
+// owns the c-th contiguous block of the tile's rows.  Each CTA writes its fp32
+// partial tile from TMEM into an L2-resident scratch slab ([rows][128], each
+// warp store one coalesced 128-byte row segment); after one cluster barrier
+// (release / acquire) each owner reads the S slabs' rows of its block in split
+// order (deterministic), applies the epilogue and stores.  The slabs live in a
+// static device array of the library, so GEMM launches that overlap on the GPU
+// (other than through programmatic dependent launch on one stream, where a
+// launch writes its slabs only after its predecessor has completed) must be
+// serialised.  A CTA without split (S = 1) keeps its partial in shared memory.
+// (Distributed shared memory moves about 12-16 bytes a cycle per SM here,
+// which made a shared-memory exchange of 32 KB per CTA cost about 1.5 us.)
 // The epilogue operands of the owned rows (RMSNorm scale, rotary position, KV
 // slot, residual) are fetched while the MMAs run.  No global scratch memory.
 //
@@ -66,7 +63,7 @@ struct GemmParams {
   int num_kb;       // K / 64
   int splits;       // CTAs per (feature tile, row tile)
   int stages;       // pipeline depth
-  int tmem_cols;    // 128 per 128-row accumulator
+  int tmem_cols;    // power of two >= row_tile
   int region;       // bytes of the pipeline / partial-tile region (1024-aligned)
   int swiglu_half;  // I for SwiGLU (gate rows [0, I), up rows [I, 2I))
   const uint16_t* residual;
@@ -105,31 +102,24 @@ OMNI_DEVINL uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-// Relaxed arrive for "buffers drained": no generic-proxy data crosses it (it follows
-// the MMA completion observed on an mbarrier).  (A release arrive costs about 0.4 us
-// here.)  "All partials stored" publishes the remote stores, so it releases.
-OMNI_DEVINL void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 OMNI_DEVINL void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 OMNI_DEVINL void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-// 16-byte store to a shared::cluster address (this CTA's own shared memory or a peer's).
-OMNI_DEVINL void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d));
-}
-// Byte offset of features 4c .. 4c + 3 in a received row rr: [rr][32 chunks of 16 B],
-// chunk index XOR (rr mod 8).
-OMNI_DEVINL uint32_t recv_off(int rr, int chunk) { return (uint32_t)(rr * kTileN * 4 + ((chunk ^ (rr & 7)) << 4)); }
 // Shared-memory load by shared-window address.
 OMNI_DEVINL float4 ld_shared_f4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
   return v;
 }
-// Address of the same shared-memory offset in CTA `rank` of the cluster.
-OMNI_DEVINL uint32_t map_cluster(uint32_t local, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-  return r;
+// Global load cached in L2 only (another SM wrote the line during this launch).
+OMNI_DEVINL float4 ld_cg_f4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
 }
+
+// Split-K partial slabs: [tile][row tile][split][row_tile][128] fp32.
+constexpr size_t kScratchFloats = size_t(6) << 20;  // 24 MiB
+__device__ __align__(16) float g_partials[kScratchFloats];
 
 OMNI_DEVINL float silu(float g) { return g / (1.0f + expf(-g)); }
 
@@ -175,6 +165,7 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   uint64_t* full = reinterpret_cast<uint64_t*>(row_info + 3 * ((mine.per + 1) & ~1));
   uint64_t* empty = full + kMaxStages;
   uint64_t* mma_done = empty + kMaxStages;
+  uint64_t* pre_bar = mma_done + 1;  // the stages resident before the main loop, as one group
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 2);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort
   float* recv = reinterpret_cast<float*>(smem);
@@ -189,6 +180,7 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
       mbar_init(&empty[s], 1);
     }
     mbar_init(mma_done, 1);
+    mbar_init(pre_bar, 1);
     flags[0] = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmap_w);
@@ -203,24 +195,25 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  auto load_w = [&](int s, int kb) {
+  auto load_w = [&](int s, int kb, uint64_t* bar) {
     uint8_t* dst = a_smem + s * a_bytes;
     const int kx = kb * kBK;
     if (EPI == kEpiSwiGLU) {
       const int g0 = tile * (kTileN / 2);
-      tma_load_2d(dst, &tmap_w, &full[s], kx, g0);
-      tma_load_2d(dst + (kTileN / 2) * kBK * 2, &tmap_w, &full[s], kx, p.swiglu_half + g0);
+      tma_load_2d(dst, &tmap_w, bar, kx, g0);
+      tma_load_2d(dst + (kTileN / 2) * kBK * 2, &tmap_w, bar, kx, p.swiglu_half + g0);
     } else {
-      tma_load_2d(dst, &tmap_w, &full[s], kx, tile * kTileN);
+      tma_load_2d(dst, &tmap_w, bar, kx, tile * kTileN);
     }
   };
 
+  // Stages 0 .. pre-1 fill before the main loop and complete together on pre_bar
+  // (one wait for the MMA warp); later stages cycle through the ring on full /
+  // empty, starting at phase 0.
   const int pre = nk < ST ? nk : ST;
   if (warp == 0 && lane == 0) {
-    for (int i = 0; i < pre; ++i) {
-      mbar_arrive_expect_tx(&full[i], a_bytes + b_bytes);
-      load_w(i, kb_begin + i);
-    }
+    mbar_arrive_expect_tx(pre_bar, (uint32_t)pre * (a_bytes + b_bytes));
+    for (int i = 0; i < pre; ++i) load_w(i, kb_begin + i, pre_bar);
   }
   griddep_wait();
   griddep_launch();
@@ -230,7 +223,7 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
     // phases), one elected lane issues the copies
     const bool leader = elect_one();
     if (leader)
-      for (int i = 0; i < pre; ++i) tma_load_2d(b_smem + i * b_bytes, &tmap_x, &full[i], (kb_begin + i) * kBK, row0);
+      for (int i = 0; i < pre; ++i) tma_load_2d(b_smem + i * b_bytes, &tmap_x, pre_bar, (kb_begin + i) * kBK, row0);
     int s = 0;
     uint32_t ph = 0;
     for (int i = pre; i < nk; ++i) {
@@ -243,7 +236,7 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
       }
       if (leader) {
         mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
-        load_w(s, kb_begin + i);
+        load_w(s, kb_begin + i, &full[s]);
         tma_load_2d(b_smem + s * b_bytes, &tmap_x, &full[s], (kb_begin + i) * kBK, row0);
       }
       __syncwarp();
@@ -255,15 +248,18 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   } else if (warp == 1) {
     // MMA issuer: the whole warp waits, one elected lane issues
     const bool leader = elect_one();
-    // A = X (rows on M, one accumulator per 128 rows), B = W (128 features on N)
-    const uint32_t idesc = idesc_bf16_f32(128, kTileN);
+    // A = W (128 features on M), B = X (the tile's rows on N)
+    const uint32_t idesc = idesc_bf16_f32(kTileN, Rt);
     const uint64_t wd0 = smem_desc_sw128(a_smem), xd0 = smem_desc_sw128(b_smem);
-    const int halves = (Rt + 127) / 128;
-    bool ok = true;
+    bool ok = nk == 0 || __all_sync(0xFFFFFFFFu, mbar_wait(pre_bar, 0));
+    if (!ok && leader) {
+      report_status(kDevTimeoutTma);
+      flags[0] = 1;
+    }
     int s = 0;
     uint32_t ph = 0;
-    for (int i = 0; i < nk; ++i) {
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full[s], ph))) {
+    for (int i = 0; ok && i < nk; ++i) {
+      if (i >= pre && !__all_sync(0xFFFFFFFFu, mbar_wait(&full[s], ph))) {
         if (leader) {
           report_status(kDevTimeoutTma);
           flags[0] = 1;
@@ -273,20 +269,18 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
       }
       tc_fence_after();
       // descriptor start addresses advance by 16-byte units: a stage, then 32 bytes per K step
-      // (rows 128 h .. of the X stage sit 16 KB apart)
       const uint64_t wd = wd0 + (uint64_t)(s * (a_bytes >> 4)), xd = xd0 + (uint64_t)(s * (b_bytes >> 4));
       if (leader) {
-        for (int h = 0; h < halves; ++h)
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            tc_mma_bf16(tmem + (uint32_t)(h * kTileN), xd + (uint64_t)(h * 1024) + 2 * kk, wd + 2 * kk, idesc,
-                        (i > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&empty[s]);
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          tc_mma_bf16(tmem, wd + 2 * kk, xd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        // the stage is refilled only when a later K block reuses it
+        if (i + ST < nk) tc_commit(&empty[s]);
       }
       __syncwarp();
       if (++s == ST) {
         s = 0;
-        ph ^= 1u;
+        if (i >= pre) ph ^= 1u;
       }
     }
     if (leader) {
@@ -322,7 +316,7 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   }
   __syncwarp();
 
-  // ---- accumulators: TMEM -> the owners' receive slots (distributed shared memory) ----
+  // ---- accumulators: TMEM -> this split's slab (S > 1) or shared memory (S = 1) ----
   const bool have_acc = nk > 0;
   if (have_acc) {
     if (!mbar_wait(mma_done, 0)) {
@@ -332,8 +326,6 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   }
   tc_fence_after();
   __syncthreads();
-  // the pipeline buffers are drained: peers may store their partials into them
-  if (S > 1) cluster_arrive();
   bool aborted = flags[0] != 0;
   // the residual rows this thread will add, fetched ahead of the reduction
   constexpr int kPre = 4;
@@ -348,55 +340,62 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
                                                      (int64_t)tile * kTileN + (idx & 31) * 4);
     }
   }
-  if (S > 1) cluster_wait();  // every peer's buffers are drained
+  // this launch's slabs: split q of the tile at slab + q * Rt * 128
+  float* slab = g_partials + ((size_t)(tile * gridDim.y + rtile) * S) * (size_t)Rt * kTileN;
   if (!aborted) {
-    // warp w: TMEM lanes 32 (w % 4) .. + 31 (one row each) of every 128-row
-    // accumulator, features 64 (w / 4) .. + 63
-    const int sp = warp & 3, fh = warp >> 2;
-    const uint32_t slot_base = smem_u32(recv) + (uint32_t)((int)crank * mine.per * kTileN * 4);
-    for (int h = 0; h * 128 + sp * 32 < rows_here; ++h) {
-      uint32_t v[64];
-      const uint32_t taddr = tmem + ((uint32_t)(sp * 32) << 16) + (uint32_t)(h * kTileN + fh * 64);
+    // warp w: TMEM lanes (features) 32 (w % 4) .., 32-column chunks w / 4, w / 4 + 2, ...
+    const int f = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    // S > 1: each warp store writes one coalesced 128-byte row segment of the slab
+    float* gdst = slab + (size_t)split * Rt * kTileN + f;
+    float* sdst = recv + f;
+    auto put_rows = [&](int cb, const uint32_t(&r)[32]) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (cb + j < rows_here) {
+          if (S > 1) gdst[(cb + j) * kTileN] = __uint_as_float(r[j]);
+          else sdst[(cb + j) * kTileN] = __uint_as_float(r[j]);
+        }
+    };
+    for (int c0 = (warp >> 2) * 32; c0 < rows_here; c0 += 128) {
+      // two 32-column loads in flight per wait
+      uint32_t r0[32], r1[32];
       if (have_acc) {
-        tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_ld_32x32b_x32(lane_base + (uint32_t)c0, r0);
+        if (c0 + 64 < rows_here) tmem_ld_32x32b_x32(lane_base + (uint32_t)(c0 + 64), r1);
         tc_wait_ld();
       } else {
 #pragma unroll
-        for (int j = 0; j < 64; ++j) v[j] = 0u;
+        for (int j = 0; j < 32; ++j) r0[j] = r1[j] = 0u;
       }
-      const int r = h * 128 + sp * 32 + lane;
-      if (r < rows_here) {
-        // row r goes to owner r / per, row r % per of its block, slot crank
-        const int q = r / mine.per, rr = r - q * mine.per;
-        const uint32_t local = slot_base + (uint32_t)(rr * kTileN * 4);
-        const uint32_t dst = S > 1 ? map_cluster(local, (uint32_t)q) : local;
-#pragma unroll
-        for (int c = 0; c < 16; ++c)
-          st_cluster_v4(dst + (uint32_t)((((fh * 16 + c) ^ (rr & 7))) << 4), v[4 * c], v[4 * c + 1], v[4 * c + 2],
-                        v[4 * c + 3]);
-      }
+      put_rows(c0, r0);
+      if (c0 + 64 < rows_here) put_rows(c0 + 64, r1);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
+  // every split's slab is written (the release orders the global stores for the
+  // cluster's readers)
   if (S > 1) {
-    // every split's partial of the owned rows is stored: after this barrier no CTA
-    // touches another's shared memory
     cluster_arrive_release();
     cluster_wait();
   }
 
   // ---- sum the owned rows' partials in split order and apply the epilogue ----
   const uint32_t recv_u32 = smem_u32(recv);
-  const uint32_t slot_bytes = (uint32_t)(mine.per * kTileN * 4);
+  const size_t slab_floats = (size_t)Rt * kTileN;
   auto acc4 = [&](int i, int f) -> float4 {
     float4 v[kMaxSplits];
-    const uint32_t a0 = recv_u32 + recv_off(i, f >> 2);
+    const int r = mine.begin + i;
+    if (S == 1) {
+      v[0] = ld_shared_f4(recv_u32 + (uint32_t)((r * kTileN + f) * 4));
+    } else {
+      const float* a0 = slab + r * kTileN + f;
 #pragma unroll
-    for (int q = 0; q < kMaxSplits; ++q)
-      if (q < S) v[q] = ld_shared_f4(a0 + (uint32_t)q * slot_bytes);
+      for (int q = 0; q < kMaxSplits; ++q)
+        if (q < S) v[q] = ld_cg_f4(a0 + q * slab_floats);
+    }
     float4 a = v[0];
 #pragma unroll
     for (int q = 1; q < kMaxSplits; ++q)
@@ -418,11 +417,19 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
       const float sc = row_info[i];
       // gate and up summed side by side in split order (two CTAs per SM leave no
       // registers for all S slots of both in flight)
-      const uint32_t sg = recv_u32 + recv_off(i, g >> 2), su = recv_u32 + recv_off(i, (g >> 2) + 16);
-      float4 gt = ld_shared_f4(sg), up = ld_shared_f4(su);
+      const int r = mine.begin + i;
+      float4 gt, up;
+      const float* sg = slab + r * kTileN + g;
+      if (S == 1) {
+        gt = ld_shared_f4(recv_u32 + (uint32_t)((r * kTileN + g) * 4));
+        up = ld_shared_f4(recv_u32 + (uint32_t)((r * kTileN + g + 64) * 4));
+      } else {
+        gt = ld_cg_f4(sg);
+        up = ld_cg_f4(sg + 64);
+      }
       for (int q = 1; q < S; ++q) {
-        const float4 a = ld_shared_f4(sg + (uint32_t)q * slot_bytes);
-        const float4 b = ld_shared_f4(su + (uint32_t)q * slot_bytes);
+        const float4 a = ld_cg_f4(sg + q * slab_floats);
+        const float4 b = ld_cg_f4(sg + q * slab_floats + 64);
         gt.x += a.x;
         gt.y += a.y;
         gt.z += a.z;
@@ -686,15 +693,12 @@ int max_active_clusters(int S, size_t smem) {
 }
 
 // Bytes of the region that holds the pipeline stages during the main loop and,
-// after it, the receive slots of the owned rows [splits][per][128] fp32.
+// after it, without split, the partial tile [row_tile][128] fp32.
 size_t plan_region(int row_tile, int stages, int splits) {
   const size_t stage_bytes = (size_t)kTileN * kBK * 2 + (size_t)row_tile * kBK * 2;
-  // the MMA reads 128 rows of every X stage: behind the last stage of a tile
-  // shorter than 128 rows, a pad keeps those don't-care rows inside the region
-  const size_t pad = row_tile < 128 ? (size_t)(128 - row_tile) * kBK * 2 : 0;
-  const int per = (row_tile + splits - 1) / splits;
-  const size_t partials = (size_t)splits * per * kTileN * 4;
-  const size_t pipe = (size_t)stages * stage_bytes + pad;
+  // without split the partial tile [row_tile][128] fp32 stays here
+  const size_t partials = splits == 1 ? (size_t)row_tile * kTileN * 4 : 0;
+  const size_t pipe = (size_t)stages * stage_bytes;
   const size_t r = pipe > partials ? pipe : partials;
   return (r + 1023) & ~(size_t)1023;
 }
@@ -747,12 +751,18 @@ Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
   if (pl.num_rt < 1) pl.num_rt = 1;
   pl.num_kb = (int)(k / kBK);
   const int clusters = pl.tiles * pl.num_rt;
+  // split partial slabs of the whole grid fit in the scratch array
+  auto slabs_fit = [&](int S) {
+    return S == 1 || (size_t)clusters * S * pl.row_tile * kTileN <= kScratchFloats;
+  };
   int best = 1;
   if (splits_req > 0) {
-    // the requested split, narrowed until the partials fit in shared memory
+    // the requested split, narrowed until the tile fits in shared memory and the
+    // slabs in the scratch array
     best = splits_req;
-    while (best > 1 && plan_smem(pl.row_tile, plan_stages(pl.row_tile, (pl.num_kb + best - 1) / best, best), best) >
-                           227 * 1024)
+    while (best > 1 && (plan_smem(pl.row_tile, plan_stages(pl.row_tile, (pl.num_kb + best - 1) / best, best), best) >
+                            227 * 1024 ||
+                        !slabs_fit(best)))
       --best;
   } else {
     // the widest split whose clusters all fit in one wave, preferring more busy SMs
@@ -760,7 +770,7 @@ Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
     for (int S = 1; S <= kMaxSplits && S <= pl.num_kb; ++S) {
       const int st = plan_stages(pl.row_tile, (pl.num_kb + S - 1) / S, S);
       const size_t sm = plan_smem(pl.row_tile, st, S);
-      if (sm > 227 * 1024) continue;
+      if (sm > 227 * 1024 || !slabs_fit(S)) continue;
       const int fit = S == 1 ? num_sms() : max_active_clusters<EPI>(S, sm);
       if (clusters > fit) continue;
       const long busy = (long)clusters * S;
@@ -774,8 +784,9 @@ Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
   if (best < 1) best = 1;
   pl.splits = best;
   pl.stages = plan_stages(pl.row_tile, (pl.num_kb + best - 1) / best, best);
-  // one 128-column fp32 accumulator (128 features) per 128 rows
-  pl.tmem_cols = pl.row_tile > 128 ? 256 : 128;
+  int tc = 32;
+  while (tc < pl.row_tile) tc <<= 1;
+  pl.tmem_cols = tc;
   pl.smem = plan_smem(pl.row_tile, pl.stages, best);
   pl.region = (int)plan_region(pl.row_tile, pl.stages, best);
   return pl;
