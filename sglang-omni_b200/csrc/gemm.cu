@@ -688,6 +688,17 @@ int max_active_clusters(int S, size_t smem) {
     cudaGetLastError();
     n = 0;
   }
+  // The cluster query counts one CTA per SM here, while two of these CTAs fit on an SM
+  // (and are placed so, measured): for cluster sizes that fit in any GPC (<= 8) count
+  // the per-SM occupancy instead.
+  int per_sm = 0;
+  if (S <= 8 && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_kernel<EPI>, kThreadsG,
+                                                              (size_t)key * 4096) == cudaSuccess) {
+    const int by_sm = per_sm * num_sms() / S;
+    if (by_sm > n) n = by_sm;
+  } else {
+    cudaGetLastError();
+  }
   slot = n;
   return n;
 }
@@ -719,16 +730,21 @@ int plan_stages(int row_tile, int kb_per, int splits) {
 // Rows per CTA.  Splitting the rows into several tiles re-reads the weights
 // from L2 once per tile but shrinks each CTA's partial tile and epilogue;
 // split-K instead shrinks each CTA's weight stream.  Measured on B200 over the
-// decode-step shapes (rows 64..512, K 1024 / 3072, 1..48 feature tiles): aim
-// for about 48 (feature tile, row tile) pairs when K <= 1024 and 32 beyond,
-// with power-of-two row tiles of at least 32 rows (64 when K > 1024) and at
-// most 256.
+// decode-step shapes (K 1024 / 3072, 8..48 feature tiles, every split): 32-row
+// tiles up to 64 rows, 64-row tiles up to 256 rows; beyond that (prefill-sized
+// batches) about 48 (feature tile, row tile) pairs when K <= 1024 and 32 beyond,
+// with power-of-two row tiles of at least 32 rows (64 when K > 1024) and at most
+// 256.
 int plan_row_tile(int64_t rows, int64_t k, int tiles) {
   const int min_rt = k > 1024 ? 64 : 32;
   const int target = k > 1024 ? 32 : 48;
   int64_t rt;
-  if (rows <= min_rt) {
+  if (rows <= 32) {
     rt = rows;
+  } else if (rows <= 64) {
+    rt = 32;
+  } else if (rows <= 256) {
+    rt = 64;
   } else {
     const int nrt = (target + tiles - 1) / tiles;
     const int64_t want = (rows + nrt - 1) / nrt;
