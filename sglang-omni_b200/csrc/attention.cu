@@ -34,12 +34,10 @@
 namespace omni {
 namespace {
 
-constexpr int kAttnWarps = 4;
 constexpr int kPage = 16;
 constexpr int kD = 128;       // head_dim of the talker
 constexpr int kGroup = 8;     // query heads per KV head
 constexpr int kPageBytes = kPage * kD * 2;  // one head's K (or V) page: 4 KB
-constexpr int kMaxRowsInSmem = 1024;
 
 OMNI_DEVINL void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
@@ -70,6 +68,12 @@ OMNI_DEVINL void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_
 // Swizzled offset of (token row, 16-byte chunk) inside a 16 x 256-byte page tile.
 OMNI_DEVINL uint32_t swz(int row, int chunk) { return (uint32_t)(row * 256 + ((chunk ^ (row & 7)) << 4)); }
 
+constexpr int kAttnWarps = 4;
+constexpr int kWarpStages = 3;                // pages in flight per warp
+constexpr int kCombStride = kD + 4;           // padded head stride of the combine area
+constexpr int kStageBytes = 2 * kPageBytes;   // K + V of one head's page: 8 KB
+constexpr int kMaxRowsInSmem = 512;
+
 struct PagedAttnParams {
   const uint16_t* q;  // [B, Hq, D] row stride q_stride
   int64_t q_stride;
@@ -78,263 +82,341 @@ struct PagedAttnParams {
   const int32_t* page_indptr;  // [B + 1]
   const int32_t* page_indices;
   const int64_t* seq_lens;     // [B]
-  const int32_t* work_indptr;  // [B + 1] chunks per row (prefix)
-  int rows, hkv, pages_per_chunk;
+  int rows, hkv, ctas;         // ctas: CTAs per KV head (grid x)
   float scale_log2;  // softmax scale * log2(e)
   uint16_t* out;     // [B, Hq, D]
   int64_t out_stride;
-  float* part_o;     // [work capacity][Hkv][8][D]
-  float* part_lse;   // [work capacity][Hkv][8]
+  float* part_o;     // [segments][Hkv][8][D]
+  float* part_lse;   // [segments][Hkv][8]
   int* counters;     // [B][Hkv]
-  int work_capacity;
 };
 
-__global__ void __launch_bounds__(kAttnWarps * 32) paged_decode_attention_kernel(const __grid_constant__ PagedAttnParams p) {
+// First page of CTA c's range: pages [bound(c), bound(c + 1)) of the flattened list.
+OMNI_DEVINL int range_bound(int c, int total, int ctas) { return (int)(((int64_t)total * c) / ctas); }
+// CTA whose range holds flattened page `pos` (ranges are non-empty: ctas <= total).
+OMNI_DEVINL int cta_of(int pos, int total, int ctas) {
+  int c = (int)(((int64_t)pos * ctas) / total);
+  while (c + 1 < ctas && range_bound(c + 1, total, ctas) <= pos) ++c;
+  while (c > 0 && range_bound(c, total, ctas) > pos) --c;
+  return c;
+}
+
+// Split-KV decode attention with a balanced split: the flattened page list of the batch
+// is cut into `ctas` equal ranges per KV head (two CTAs per SM over both heads); CTA c
+// walks the row pieces of its range in order.  The 4 warps take the pages of a piece in
+// turn, each keeping kWarpStages pages in flight (16-byte cp.async into a swizzled
+// per-warp ring).  Per page a warp computes S^T = K Q^T (16 tokens x the group's 8
+// query heads, mma.sync m16n8k16 with K as the A operand, so no padding rows), an online
+// base-2 softmax per head, and O^T += V^T P^T (V^T by transposed ldmatrix, P^T moved
+// into the B-operand layout by four shuffles).  The warps combine in shared memory; a
+// piece that is the whole row stores it, otherwise the piece's (o, lse) goes to segment
+// c + b and paged_attention_merge_kernel (the next launch) merges the row's segments in
+// order (deterministic).
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_kernel(
+    const __grid_constant__ PagedAttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int s_last;
-  __shared__ int s_work[kMaxRowsInSmem + 1];  // work_indptr, when the batch fits
-  griddep_wait();
-  griddep_launch();
+  __shared__ int s_ptr[kMaxRowsInSmem + 1];  // page_indptr, when the batch fits
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int h = blockIdx.y;
-  const bool work_in_smem = p.rows <= kMaxRowsInSmem;
-  if (work_in_smem)
-    for (int i = threadIdx.x; i <= p.rows; i += blockDim.x) s_work[i] = p.work_indptr[i];
+  const int h = blockIdx.y, c = blockIdx.x;
+  // The page table and sequence lengths are step metadata written before the previous
+  // kernel started: they are read before griddepcontrol.wait, overlapping the previous
+  // kernel's tail.  The queries and the KV pages (whose last page holds the token the
+  // previous kernel stored) are read after it.
+  const bool ptr_in_smem = p.rows <= kMaxRowsInSmem;
+  if (ptr_in_smem)
+    for (int i = threadIdx.x; i <= p.rows; i += blockDim.x) s_ptr[i] = p.page_indptr[i];
   __syncthreads();
-  const int* work = work_in_smem ? s_work : p.work_indptr;
-  const int num_work = work[p.rows];
-  uint8_t* wbuf = smem + warp * (2 * 2 * kPageBytes);  // [stage][K|V][4 KB]
+  const int* pptr = ptr_in_smem ? s_ptr : p.page_indptr;
+  const int total = pptr[p.rows];
+  // at most one CTA per page, so that every range is non-empty
+  const int ctas = min(p.ctas, total);
+  if (c >= ctas) {
+    griddep_wait();
+    griddep_launch();
+    return;
+  }
+  const int a0 = range_bound(c, total, ctas), a1 = range_bound(c + 1, total, ctas);
+  int lo = 0, hi = p.rows - 1;  // first row of the range: last b with page_indptr[b] <= a0
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (pptr[mid] <= a0) lo = mid;
+    else hi = mid - 1;
+  }
+  uint8_t* wring = smem + warp * (kWarpStages * kStageBytes);
+  // combine area over the rings: written once every warp is done with its pages
+  float* wo = reinterpret_cast<float*>(smem);                                           // [warp][8][kCombStride]
+  float* wm = wo + kAttnWarps * kGroup * kCombStride;                                   // [warp][8]
+  float* wl = wm + kAttnWarps * kGroup;                                                 // [warp][8]
 
-  for (int it = blockIdx.x; it < num_work; it += gridDim.x) {
-    // row of this item: last b with work_indptr[b] <= it (a search in shared memory)
-    int lo = 0, hi = p.rows - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (work[mid] <= it) lo = mid;
-      else hi = mid - 1;
+  // the next row piece of the range from row bb on: (b, r0, r1) with r0 < r1
+  auto find_piece = [&](int bb, int& b, int& r0, int& r1) -> bool {
+    for (b = bb; b < p.rows && pptr[b] < a1; ++b) {
+      r0 = max(a0, pptr[b]);
+      r1 = min(a1, pptr[b + 1]);
+      if (r0 < r1) return true;
     }
-    const int b = lo;
-    const int c = it - work[b];
-    const int nchunks = work[b + 1] - work[b];
-    const int pg_begin = p.page_indptr[b];
-    const int p0 = pg_begin + c * p.pages_per_chunk;
-    const int p1 = min(p0 + p.pages_per_chunk, p.page_indptr[b + 1]);
-    const int seq_len = (int)p.seq_lens[b];
+    return false;
+  };
+  // this warp's pages of a piece: r0 + warp + 4 i, i < nmine; ids one per lane
+  int pid_lane = 0, nmine = 0, cur_r0 = 0;
+  auto issue = [&](int i) {  // i-th page of this warp into stage i % kWarpStages
+    const int64_t page = i < 32 ? __shfl_sync(0xFFFFFFFFu, pid_lane, i)
+                                : p.page_indices[cur_r0 + warp + kAttnWarps * i];
+    const uint16_t* kbase = p.k_cache + (page * kPage * p.hkv + h) * kD;
+    const uint16_t* vbase = p.v_cache + (page * kPage * p.hkv + h) * kD;
+    uint8_t* kd = wring + (i % kWarpStages) * kStageBytes;
+    uint8_t* vd = kd + kPageBytes;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int id = u * 32 + lane;
+      const int row = id >> 4, ch = id & 15;
+      const int64_t goff = (int64_t)row * p.hkv * kD + ch * 8;
+      cp_async16(kd + swz(row, ch), kbase + goff);
+      cp_async16(vd + swz(row, ch), vbase + goff);
+    }
+    cp_async_commit();
+  };
+  auto piece_ids = [&](int r0, int r1) {
+    cur_r0 = r0;
+    const int npg = r1 - r0;
+    nmine = npg > warp ? (npg - warp + kAttnWarps - 1) / kAttnWarps : 0;
+    pid_lane = lane < nmine ? p.page_indices[r0 + warp + kAttnWarps * lane] : 0;
+  };
+  auto issue_first = [&]() {
+    const int first = nmine < kWarpStages ? nmine : kWarpStages;
+    for (int i = 0; i < first; ++i) issue(i);
+  };
 
-    // Q fragments of the 8 heads of this group (rows 8..15 of the M tile are zero)
-    uint32_t qa[8][2];
+  int b, r0, r1;
+  bool have = find_piece(lo, b, r0, r1);
+  if (have) piece_ids(r0, r1);
+  griddep_wait();
+  griddep_launch();
+  if (have) issue_first();
+  while (have) {
+    const int rp0 = pptr[b], rp1 = pptr[b + 1];
+    const int seq_len = (int)p.seq_lens[b];
+    // Q^T as the B operand: head g, dims 16 ks + 2t (+1) and + 8
+    uint32_t qb[8][2];
     const uint16_t* qrow = p.q + (int64_t)b * p.q_stride + (int64_t)(h * kGroup + g) * kD;
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
-      qa[ks][0] = *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 2 * t);
-      qa[ks][1] = *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * t);
+      qb[ks][0] = *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 2 * t);
+      qb[ks][1] = *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * t);
     }
-    float o[16][4];
+    // O^T accumulators: m-tile mt holds dims 16 mt + g (+ 8) for heads 2t, 2t + 1
+    float o[8][4];
 #pragma unroll
-    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-    float m = -INFINITY, l = 0.0f;
+    for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // heads 2t, 2t + 1
+    const int src_a = 8 * t + (g >> 1), src_b = src_a + 4;       // lanes holding P[g][2t], P[g][2t + 1]
 
-    // the item's page ids, one per lane (all loads in flight together)
-    const int pid_lane = p0 + lane < p1 ? p.page_indices[p0 + lane] : 0;
-    auto issue = [&](int pg, int stage) {
-      const int64_t page = pg - p0 < 32 ? __shfl_sync(0xFFFFFFFFu, pid_lane, pg - p0) : p.page_indices[pg];
-      const uint16_t* kbase = p.k_cache + (page * kPage * p.hkv + h) * kD;
-      const uint16_t* vbase = p.v_cache + (page * kPage * p.hkv + h) * kD;
-      uint8_t* kd = wbuf + stage * 2 * kPageBytes;
-      uint8_t* vd = kd + kPageBytes;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int id = i * 32 + lane;
-        const int row = id >> 4, ch = id & 15;
-        const int64_t goff = (int64_t)row * p.hkv * kD + ch * 8;
-        cp_async16(kd + swz(row, ch), kbase + goff);
-        cp_async16(vd + swz(row, ch), vbase + goff);
-      }
-      cp_async_commit();
-    };
-
-    int pg = p0 + warp;
-    int stage = 0;
-    if (pg < p1) issue(pg, 0);
-    for (; pg < p1; pg += kAttnWarps) {
-      const int nxt = pg + kAttnWarps;
-      if (nxt < p1) {
-        issue(nxt, stage ^ 1);
-        cp_async_wait<1>();
-      } else {
-        cp_async_wait<0>();
-      }
+    for (int i = 0; i < nmine; ++i) {
+      // page i is complete once at most (issued - i - 1) later groups are pending
+      const int pending = min(nmine, i + kWarpStages) - i - 1;
+      if (pending >= 2) cp_async_wait<2>();
+      else if (pending == 1) cp_async_wait<1>();
+      else cp_async_wait<0>();
       __syncwarp();
-      const int tok_base = (pg - pg_begin) * kPage;
+      uint8_t* kd = wring + (i % kWarpStages) * kStageBytes;
+      const int tok_base = (r0 - rp0 + warp + kAttnWarps * i) * kPage;
       if (seq_len - tok_base < kPage) {
         // slots past the sequence end hold stale values: zero their V rows so
         // that P = 0 never meets a non-finite value in P V
-        uint8_t* vd = wbuf + stage * 2 * kPageBytes + kPageBytes;
-        const int first = max(seq_len - tok_base, 0);
-        for (int id = first * 16 + lane; id < kPage * 16; id += 32)
+        uint8_t* vd = kd + kPageBytes;
+        const int f0 = max(seq_len - tok_base, 0);
+        for (int id = f0 * 16 + lane; id < kPage * 16; id += 32)
           *reinterpret_cast<uint4*>(vd + swz(id >> 4, id & 15)) = make_uint4(0, 0, 0, 0);
         __syncwarp();
       }
-      const uint32_t kb = smem_u32(wbuf + stage * 2 * kPageBytes);
+      const uint32_t kb = smem_u32(kd);
       const uint32_t vb = kb + kPageBytes;
-      // S = Q K^T over the page's 16 tokens (two n-tiles of 8)
-      float s[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+      // S^T = K Q^T: 16 tokens x 8 heads
+      float sacc[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        const int tok = ((lane >> 4) << 3) + (lane & 7);
-        const int ch = 2 * ks + ((lane >> 3) & 1);
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4(kb + swz(tok, ch), r0, r1, r2, r3);
-        mma_bf16_16816(s[0], qa[ks][0], 0u, qa[ks][1], 0u, r0, r1);
-        mma_bf16_16816(s[1], qa[ks][0], 0u, qa[ks][1], 0u, r2, r3);
+        const int tok = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int ch = 2 * ks + (lane >> 4);
+        uint32_t x0, x1, x2, x3;
+        ldsm_x4(kb + swz(tok, ch), x0, x1, x2, x3);
+        mma_bf16_16816(sacc, x0, x1, x2, x3, qb[ks][0], qb[ks][1]);
       }
-      float sv[4];
+      // sacc: [0] token g head 2t, [1] token g head 2t+1, [2] token g+8 head 2t, [3] token g+8 head 2t+1
+      const bool v_lo = tok_base + g < seq_len, v_hi = tok_base + g + 8 < seq_len;
+      const float s0 = v_lo ? sacc[0] * p.scale_log2 : -INFINITY;
+      const float s1 = v_lo ? sacc[1] * p.scale_log2 : -INFINITY;
+      const float s2 = v_hi ? sacc[2] * p.scale_log2 : -INFINITY;
+      const float s3 = v_hi ? sacc[3] * p.scale_log2 : -INFINITY;
+      float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int tok = tok_base + 8 * j + 2 * t + e;
-          sv[2 * j + e] = tok < seq_len ? s[j][e] * p.scale_log2 : -INFINITY;
-        }
-      float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
-      const float m_new = fmaxf(m, mx);
-      const float alpha = (m == -INFINITY) ? 0.0f : exp2f(m - m_new);
-      float pv[4], rs = 0.0f;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        pv[e] = (sv[e] == -INFINITY) ? 0.0f : exp2f(sv[e] - m_new);
-        rs += pv[e];
+      for (int off = 4; off <= 16; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, off));
       }
-      rs += __shfl_xor_sync(0xFFFFFFFFu, rs, 1);
-      rs += __shfl_xor_sync(0xFFFFFFFFu, rs, 2);
-      l = l * alpha + rs;
-      m = m_new;
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float al0 = (m0 == -INFINITY) ? 0.0f : exp2f(m0 - mn0);
+      const float al1 = (m1 == -INFINITY) ? 0.0f : exp2f(m1 - mn1);
+      const float p0 = s0 == -INFINITY ? 0.0f : exp2f(s0 - mn0);
+      const float p1 = s1 == -INFINITY ? 0.0f : exp2f(s1 - mn1);
+      const float p2 = s2 == -INFINITY ? 0.0f : exp2f(s2 - mn0);
+      const float p3 = s3 == -INFINITY ? 0.0f : exp2f(s3 - mn1);
+      float rs0 = p0 + p2, rs1 = p1 + p3;
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        o[n][0] *= alpha;
-        o[n][1] *= alpha;
+      for (int off = 4; off <= 16; off <<= 1) {
+        rs0 += __shfl_xor_sync(0xFFFFFFFFu, rs0, off);
+        rs1 += __shfl_xor_sync(0xFFFFFFFFu, rs1, off);
       }
-      const uint32_t pa0 = pack_bf2(pv[0], pv[1]);
-      const uint32_t pa2 = pack_bf2(pv[2], pv[3]);
+      l0 = l0 * al0 + rs0;
+      l1 = l1 * al1 + rs1;
+      m0 = mn0;
+      m1 = mn1;
 #pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int tok = ((lane >> 3) & 1) * 8 + (lane & 7);
-        const int ch = 2 * jj + (lane >> 4);
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4_t(vb + swz(tok, ch), r0, r1, r2, r3);
-        mma_bf16_16816(o[2 * jj], pa0, 0u, pa2, 0u, r0, r1);
-        mma_bf16_16816(o[2 * jj + 1], pa0, 0u, pa2, 0u, r2, r3);
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= al0;
+        o[mt][1] *= al1;
+        o[mt][2] *= al0;
+        o[mt][3] *= al1;
+      }
+      // P^T as the B operand: this lane needs P[head g][tokens 2t, 2t+1, 2t+8, 2t+9];
+      // lane 8t' + j holds tokens (2t' + (j >> 2)) of the pair-packed heads 2 (j & 3), + 1
+      const uint32_t x01 = pack_bf2(p0, p1), x23 = pack_bf2(p2, p3);
+      const uint32_t a01 = __shfl_sync(0xFFFFFFFFu, x01, src_a), b01 = __shfl_sync(0xFFFFFFFFu, x01, src_b);
+      const uint32_t a23 = __shfl_sync(0xFFFFFFFFu, x23, src_a), b23 = __shfl_sync(0xFFFFFFFFu, x23, src_b);
+      // head g is the low half of the pair when g is even
+      const uint32_t sel = (g & 1) ? 0x7632u : 0x5410u;
+      const uint32_t pb0 = __byte_perm(a01, b01, sel), pb1 = __byte_perm(a23, b23, sel);
+      // O^T += V^T P^T, 8 m-tiles of 16 dims
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int tok = (lane & 7) + ((lane >> 4) << 3);
+        const int ch = 2 * mt + ((lane >> 3) & 1);
+        uint32_t x0, x1, x2, x3;
+        ldsm_x4_t(vb + swz(tok, ch), x0, x1, x2, x3);
+        mma_bf16_16816(o[mt], x0, x1, x2, x3, pb0, pb1);
       }
       __syncwarp();
-      stage ^= 1;
+      if (i + kWarpStages < nmine) issue(i + kWarpStages);
     }
 
-    // ---- combine the warps of this CTA ----
-    __syncthreads();
-    float* wm = reinterpret_cast<float*>(smem);
-    float* wl = wm + kAttnWarps * kGroup;
-    float* wo = wl + kAttnWarps * kGroup;  // [warp][8][128]
-    if (t == 0) {
-      wm[warp * kGroup + g] = m;
-      wl[warp * kGroup + g] = l;
+    // ---- combine the warps ----
+    __syncthreads();  // every warp's pages are consumed: the rings become the combine area
+    if (g == 0) {
+      wm[warp * kGroup + 2 * t] = m0;
+      wm[warp * kGroup + 2 * t + 1] = m1;
+      wl[warp * kGroup + 2 * t] = l0;
+      wl[warp * kGroup + 2 * t + 1] = l1;
     }
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      wo[(warp * kGroup + g) * kD + 8 * n + 2 * t] = o[n][0];
-      wo[(warp * kGroup + g) * kD + 8 * n + 2 * t + 1] = o[n][1];
-    }
-    __syncthreads();
-    if (threadIdx.x < kGroup * 16) {
-      const int hg = threadIdx.x >> 4;          // head within group
-      const int d0 = (threadIdx.x & 15) * 8;    // 8 dims
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w * kGroup + hg]);
-      float L = 0.0f, acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) {
-        const float lw = wl[w * kGroup + hg];
-        if (lw == 0.0f) continue;
-        const float sc = exp2f(wm[w * kGroup + hg] - M);
-        L += lw * sc;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += wo[(w * kGroup + hg) * kD + d0 + e] * sc;
-      }
-      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-      if (nchunks == 1) {
-        uint16_t* dst = p.out + (int64_t)b * p.out_stride + (int64_t)(h * kGroup + hg) * kD + d0;
-        uint4 v = make_uint4(pack_bf2(acc[0] * inv, acc[1] * inv), pack_bf2(acc[2] * inv, acc[3] * inv),
-                             pack_bf2(acc[4] * inv, acc[5] * inv), pack_bf2(acc[6] * inv, acc[7] * inv));
-        *reinterpret_cast<uint4*>(dst) = v;
-      } else {
-        float* po = p.part_o + (((int64_t)it * p.hkv + h) * kGroup + hg) * kD + d0;
-        *reinterpret_cast<float4*>(po) = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
-        *reinterpret_cast<float4*>(po + 4) = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
-        if ((threadIdx.x & 15) == 0) p.part_lse[((int64_t)it * p.hkv + h) * kGroup + hg] = M + log2f(L);
-      }
-    }
-    if (nchunks > 1) {
-      __threadfence();
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        int* ctr = p.counters + b * p.hkv + h;
-        const int old = atomicAdd(ctr, 1);
-        s_last = old == nchunks - 1;
-        if (s_last) *ctr = 0;
-      }
-      __syncthreads();
-      if (s_last && threadIdx.x < kGroup * 16) {
-        __threadfence();
-        const int hg = threadIdx.x >> 4;
-        const int d0 = (threadIdx.x & 15) * 8;
-        const int w0 = work[b];
-        float M = -INFINITY;
-        for (int cc = 0; cc < nchunks; ++cc)
-          M = fmaxf(M, __ldcg(p.part_lse + ((int64_t)(w0 + cc) * p.hkv + h) * kGroup + hg));
-        float W = 0.0f, acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        // chunks in batches of 8 with every load of a batch in flight before the sums,
-        // summed in chunk order
-        for (int c0 = 0; c0 < nchunks; c0 += 8) {
-          float lse[8];
-          float4 lo[8], hi[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            if (c0 + u < nchunks) {
-              const int64_t base = ((int64_t)(w0 + c0 + u) * p.hkv + h) * kGroup + hg;
-              lse[u] = __ldcg(p.part_lse + base);
-              const float4* po = reinterpret_cast<const float4*>(p.part_o + base * kD + d0);
-              lo[u] = __ldcg(po);
-              hi[u] = __ldcg(po + 1);
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            if (c0 + u < nchunks) {
-              const float wgt = lse[u] == -INFINITY ? 0.0f : exp2f(lse[u] - M);
-              W += wgt;
-              acc[0] += lo[u].x * wgt;
-              acc[1] += lo[u].y * wgt;
-              acc[2] += lo[u].z * wgt;
-              acc[3] += lo[u].w * wgt;
-              acc[4] += hi[u].x * wgt;
-              acc[5] += hi[u].y * wgt;
-              acc[6] += hi[u].z * wgt;
-              acc[7] += hi[u].w * wgt;
-            }
-          }
-        }
-        const float inv = W > 0.0f ? 1.0f / W : 0.0f;
-        uint16_t* dst = p.out + (int64_t)b * p.out_stride + (int64_t)(h * kGroup + hg) * kD + d0;
-        *reinterpret_cast<uint4*>(dst) =
-            make_uint4(pack_bf2(acc[0] * inv, acc[1] * inv), pack_bf2(acc[2] * inv, acc[3] * inv),
-                       pack_bf2(acc[4] * inv, acc[5] * inv), pack_bf2(acc[6] * inv, acc[7] * inv));
-      }
+    for (int mt = 0; mt < 8; ++mt) {
+      float* w0 = wo + (warp * kGroup + 2 * t) * kCombStride + 16 * mt + g;
+      float* w1 = w0 + kCombStride;
+      w0[0] = o[mt][0];
+      w1[0] = o[mt][1];
+      w0[8] = o[mt][2];
+      w1[8] = o[mt][3];
     }
     __syncthreads();
+    const bool whole = r0 == rp0 && r1 == rp1;
+    const int seg = c + b;
+    const int hg = threadIdx.x >> 4;          // head within group
+    const int d0 = (threadIdx.x & 15) * 8;    // 8 dims
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float M = -INFINITY, L = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w * kGroup + hg]);
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float lw = wl[w * kGroup + hg];
+      if (lw == 0.0f) continue;
+      const float sc = exp2f(wm[w * kGroup + hg] - M);
+      L += lw * sc;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += wo[(w * kGroup + hg) * kCombStride + d0 + e] * sc;
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    // the next piece's page ids load while this piece is stored
+    int nb = 0, nr0 = 0, nr1 = 0;
+    const bool nhave = find_piece(b + 1, nb, nr0, nr1);
+    if (nhave) piece_ids(nr0, nr1);
+    if (whole) {
+      uint16_t* dst = p.out + (int64_t)b * p.out_stride + (int64_t)(h * kGroup + hg) * kD + d0;
+      *reinterpret_cast<uint4*>(dst) =
+          make_uint4(pack_bf2(acc[0] * inv, acc[1] * inv), pack_bf2(acc[2] * inv, acc[3] * inv),
+                     pack_bf2(acc[4] * inv, acc[5] * inv), pack_bf2(acc[6] * inv, acc[7] * inv));
+    } else {
+      float* po = p.part_o + (((int64_t)seg * p.hkv + h) * kGroup + hg) * kD + d0;
+      *reinterpret_cast<float4*>(po) = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+      *reinterpret_cast<float4*>(po + 4) = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
+      if ((threadIdx.x & 15) == 0)
+        p.part_lse[((int64_t)seg * p.hkv + h) * kGroup + hg] = L > 0.0f ? M + log2f(L) : -INFINITY;
+    }
+    __syncthreads();  // the combine area (the rings) is free for the next piece
+    if (nhave) issue_first();
+    have = nhave;
+    b = nb;
+    r0 = nr0;
+    r1 = nr1;
   }
+}
+
+// Rows whose pages span several CTA ranges: row b's segments are c_lo + b .. c_hi + b
+// (the ranges holding its first and last pages), merged in segment order with their
+// log-sum-exp weights.  Rows held by one range were stored by the attention kernel.
+__global__ void __launch_bounds__(kGroup * 16) paged_attention_merge_kernel(const __grid_constant__ PagedAttnParams p) {
+  const int b = blockIdx.x, h = blockIdx.y;
+  // step metadata, read before the wait (as in the attention kernel)
+  const int total = p.page_indptr[p.rows];
+  const int rp0 = p.page_indptr[b], rp1 = p.page_indptr[b + 1];
+  griddep_wait();
+  griddep_launch();
+  if (rp0 >= rp1) return;
+  const int ctas = min(p.ctas, total);
+  const int c_lo = cta_of(rp0, total, ctas), c_hi = cta_of(rp1 - 1, total, ctas);
+  const int nseg = c_hi - c_lo + 1;
+  if (nseg == 1) return;
+  const int hg = threadIdx.x >> 4;        // head within group
+  const int d0 = (threadIdx.x & 15) * 8;  // 8 dims
+  const int w0 = c_lo + b;
+  float M = -INFINITY;
+  for (int cc = 0; cc < nseg; ++cc) M = fmaxf(M, p.part_lse[((int64_t)(w0 + cc) * p.hkv + h) * kGroup + hg]);
+  float W = 0.0f, sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  // segments in batches of 8 with every load of a batch in flight before the sums,
+  // summed in segment order
+  for (int s0 = 0; s0 < nseg; s0 += 8) {
+    float lse[8];
+    float4 lo4[8], hi4[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (s0 + u < nseg) {
+        const int64_t base = ((int64_t)(w0 + s0 + u) * p.hkv + h) * kGroup + hg;
+        lse[u] = p.part_lse[base];
+        const float4* pp = reinterpret_cast<const float4*>(p.part_o + base * kD + d0);
+        lo4[u] = pp[0];
+        hi4[u] = pp[1];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (s0 + u < nseg) {
+        const float wgt = lse[u] == -INFINITY ? 0.0f : exp2f(lse[u] - M);
+        W += wgt;
+        sum[0] += lo4[u].x * wgt;
+        sum[1] += lo4[u].y * wgt;
+        sum[2] += lo4[u].z * wgt;
+        sum[3] += lo4[u].w * wgt;
+        sum[4] += hi4[u].x * wgt;
+        sum[5] += hi4[u].y * wgt;
+        sum[6] += hi4[u].z * wgt;
+        sum[7] += hi4[u].w * wgt;
+      }
+    }
+  }
+  const float iw = W > 0.0f ? 1.0f / W : 0.0f;
+  uint16_t* dst = p.out + (int64_t)b * p.out_stride + (int64_t)(h * kGroup + hg) * kD + d0;
+  *reinterpret_cast<uint4*>(dst) =
+      make_uint4(pack_bf2(sum[0] * iw, sum[1] * iw), pack_bf2(sum[2] * iw, sum[3] * iw),
+                 pack_bf2(sum[4] * iw, sum[5] * iw), pack_bf2(sum[6] * iw, sum[7] * iw));
 }
 
 // ---------------------------------------------------------------------------
@@ -674,6 +756,17 @@ extern "C" OMNI_API int omni_paged_decode_attention(const void* q, int64_t q_str
       (reinterpret_cast<uintptr_t>(workspace) & 255))
     return set_error(OMNI_ERR_CAPACITY, "attention workspace too small or misaligned");
   if (rows == 0) return OMNI_OK;
+  // one partial segment per (row, CTA page range) piece: at most ctas + rows - 1 of them
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0, v = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    sms = v;
+  }
+  // two CTAs per SM over all KV heads
+  int64_t ctas = grid_ctas > 0 ? grid_ctas : (2 * sms) / num_kv_heads;
+  if (ctas > work_capacity - rows + 1) ctas = work_capacity - rows + 1;
+  if (ctas < 1) return set_error(OMNI_ERR_CAPACITY, "attention work capacity below the row count");
   PagedAttnParams p{};
   p.q = static_cast<const uint16_t*>(q);
   p.q_stride = q_stride;
@@ -682,21 +775,19 @@ extern "C" OMNI_API int omni_paged_decode_attention(const void* q, int64_t q_str
   p.page_indptr = page_indptr;
   p.page_indices = page_indices;
   p.seq_lens = seq_lens;
-  p.work_indptr = work_indptr;
   p.rows = (int)rows;
   p.hkv = num_kv_heads;
-  p.pages_per_chunk = pages_per_chunk;
+  p.ctas = (int)ctas;
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.out = static_cast<uint16_t*>(out);
   p.out_stride = out_stride;
-  p.work_capacity = (int)work_capacity;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const int64_t ctr = (rows * num_kv_heads * 4 + 255) / 256 * 256;
   const int64_t lse = (work_capacity * num_kv_heads * kGroup * 4 + 255) / 256 * 256;
   p.counters = reinterpret_cast<int*>(ws);
   p.part_lse = reinterpret_cast<float*>(ws + ctr);
   p.part_o = reinterpret_cast<float*>(ws + ctr + lse);
-  const size_t smem = (size_t)kAttnWarps * 2 * 2 * kPageBytes;  // 64 KB
+  const size_t smem = (size_t)kAttnWarps * kWarpStages * kStageBytes;  // 96 KB of rings (+ combine area)
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(paged_decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -704,18 +795,13 @@ extern "C" OMNI_API int omni_paged_decode_attention(const void* q, int64_t q_str
     if (e != cudaSuccess) return check_launch(e);
     attr = true;
   }
-  // two CTAs per SM along the work list (x), one grid row per KV head (y)
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0, v = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    sms = v;
-  }
-  int gx = grid_ctas > 0 ? grid_ctas : 2 * sms;
-  if (gx > work_capacity) gx = (int)work_capacity;
-  if (gx < 1) gx = 1;
-  return check_launch(launch(paged_decode_attention_kernel, dim3((unsigned)gx, (unsigned)num_kv_heads),
-                             dim3(kAttnWarps * 32), smem, static_cast<cudaStream_t>(stream), p));
+  (void)work_indptr;
+  (void)pages_per_chunk;
+  const int rc = check_launch(launch(paged_decode_attention_kernel, dim3((unsigned)ctas, (unsigned)num_kv_heads),
+                                     dim3(kAttnWarps * 32), smem, static_cast<cudaStream_t>(stream), p));
+  if (rc != OMNI_OK) return rc;
+  return check_launch(launch(paged_attention_merge_kernel, dim3((unsigned)rows, (unsigned)num_kv_heads),
+                             dim3(kGroup * 16), 0, static_cast<cudaStream_t>(stream), p));
 }
 
 extern "C" OMNI_API int omni_predictor_attention(const void* q, int64_t q_stride, const void* k_cache,
@@ -818,12 +904,6 @@ extern "C" OMNI_API int omni_paged_decode_attention_noalloc(
       g_noalloc_ptr[dev] = p;
     }
     scratch = g_noalloc_ptr[dev];
-  }
-  // the merge counters sit at the front of the scratch and must start at zero
-  const size_t counter_bytes = (size_t)((rows * num_kv_heads * 4 + 255) / 256 * 256);
-  if (rows > 0) {
-    e = cudaMemsetAsync(scratch, 0, counter_bytes, static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) return check_launch(e);
   }
   return omni_paged_decode_attention(q, q_stride, k_cache, v_cache, page_indptr, page_indices, seq_lens, work_indptr,
                                      rows, num_q_heads, num_kv_heads, head_dim, page_size, pages_per_chunk,

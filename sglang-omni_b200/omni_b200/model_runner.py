@@ -82,7 +82,9 @@ class TalkerDecodeRunner:
         self.page_indptr = torch.zeros(B + 1, **i32)
         self.page_indices = torch.zeros(num_pages + B, **i32)
         self.work_indptr = torch.zeros(B + 1, **i32)
-        self.work_capacity = (num_pages + pages_per_chunk - 1) // pages_per_chunk + B
+        # attention partial segments: one per (row, CTA page range) piece, at most rows + CTAs
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.work_capacity = max((num_pages + pages_per_chunk - 1) // pages_per_chunk, sms) + B
         self.status = torch.zeros(1, **i32)
         self.text_embeds = torch.zeros(B, cfg.hidden_size, dtype=torch.bfloat16, device=self.device)
         self.allocator: PageAllocator | None = None
