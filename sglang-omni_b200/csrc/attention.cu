@@ -120,9 +120,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_ker
   const int g = lane >> 2, t = lane & 3;
   const int h = blockIdx.y, c = blockIdx.x;
   // The page table and sequence lengths are step metadata written before the previous
-  // kernel started: they are read before griddepcontrol.wait, overlapping the previous
-  // kernel's tail.  The queries and the KV pages (whose last page holds the token the
-  // previous kernel stored) are read after it.
+  // kernel started, and so is every KV slot but each row's newest token: the tables and
+  // the first pages are read before griddepcontrol.wait, overlapping the previous
+  // kernel's tail.  The queries and each row's last page are read after it.
   const bool ptr_in_smem = p.rows <= kMaxRowsInSmem;
   if (ptr_in_smem)
     for (int i = threadIdx.x; i <= p.rows; i += blockDim.x) s_ptr[i] = p.page_indptr[i];
@@ -190,10 +190,21 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_ker
 
   int b, r0, r1;
   bool have = find_piece(lo, b, r0, r1);
-  if (have) piece_ids(r0, r1);
+  // The first piece's pages stream in before the wait, up to its row's last page: only
+  // that page holds a token the previous kernel may have stored (the step's new KV).
+  int early = 0;
+  if (have) {
+    piece_ids(r0, r1);
+    const int first = nmine < kWarpStages ? nmine : kWarpStages;
+    const int last_pos = pptr[b + 1] - 1;
+    while (early < first && r0 + warp + kAttnWarps * early != last_pos) issue(early++);
+  }
   griddep_wait();
   griddep_launch();
-  if (have) issue_first();
+  if (have) {
+    const int first = nmine < kWarpStages ? nmine : kWarpStages;
+    for (int i = early; i < first; ++i) issue(i);
+  }
   while (have) {
     const int rp0 = pptr[b], rp1 = pptr[b + 1];
     const int seq_len = (int)p.seq_lens[b];
