@@ -154,7 +154,10 @@ OMNI_API int omni_predictor_pair_inputs(const int64_t* layer0_codes, const void*
 #define OMNI_EPI_F32 3      /* y = x W^T in f32 (logits)                          */
 
 /* Bytes of global workspace omni_linear needs for this shape: always 0 (the
- * split-K partials are reduced in the cluster's distributed shared memory). */
+ * split-K partials go through a 24 MiB scratch array inside the library, reduced
+ * by the owning CTA of each cluster; GEMM launches that overlap on the GPU, other
+ * than consecutive launches on one stream under programmatic dependent launch,
+ * must be serialised). */
 OMNI_API int64_t omni_linear_workspace_bytes(int64_t rows, int64_t k, int64_t n, int32_t epilogue, int32_t splits);
 
 /* y[rows, N] = epilogue(x[rows, K] . w[N, K]^T): the decode-step linears
@@ -164,7 +167,8 @@ OMNI_API int64_t omni_linear_workspace_bytes(int64_t rows, int64_t k, int64_t n,
  *   x, w, residual bf16; y bf16 (f32 for OMNI_EPI_F32); K % 64 == 0, N % 128 == 0.
  *   splits: K-splits per 128-feature tile (one thread-block cluster each),
  *   0 = chosen by the library so that one wave covers the GPU, else 1..16
- *   (narrowed when the split partials of a wide row tile exceed shared memory).
+ *   (narrowed when a wide row tile exceeds shared memory or the grid's split
+ *   partials exceed the scratch array).
  *   workspace / workspace_bytes: unused (may be NULL / 0). */
 OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n,
                          int32_t epilogue, const void* residual, int64_t residual_stride, void* y, int64_t y_stride,
@@ -271,10 +275,18 @@ OMNI_API int64_t omni_paged_attention_workspace_bytes(int64_t rows, int32_t num_
 /* Paged-KV GQA decode attention (RadixAttention decode, thinker_model.py:373-379).
  *   q bf16 [rows, Hq, 128]; k_cache, v_cache bf16 [slots, Hkv, 128], page size 16;
  *   page_indptr i32 [rows+1] / page_indices i32 (page ids); seq_lens i64 [rows];
- *   work_indptr i32 [rows+1]: cumulative ceil(pages / pages_per_chunk) (from
- *   omni_decode_prepare); work_capacity bounds its last entry.
- *   workspace: omni_paged_attention_workspace_bytes, 256-byte aligned, zero-filled
- *   before first use.  out bf16 [rows, Hq, 128]. */
+ *   out bf16 [rows, Hq, 128].
+ *   The flattened page list is split into grid_ctas equal ranges per KV head (0 = two
+ *   CTAs per SM over all KV heads); a row spread over several ranges is merged by a
+ *   second launch.  work_capacity = partial segments the workspace holds: at least
+ *   rows + ranges - 1 (fewer ranges are used when it is smaller).  workspace:
+ *   omni_paged_attention_workspace_bytes(rows, Hkv, work_capacity), 256-byte aligned.
+ *   work_indptr and pages_per_chunk (the chunk list of omni_decode_prepare) are accepted
+ *   for interface stability and not read.
+ *   Programmatic dependent launch: the page table, seq_lens and every KV slot except
+ *   each row's newest token are read before the kernel waits on its predecessor, so
+ *   they must have been written before the previous kernel on the stream started (the
+ *   previous kernel may store the new tokens' K/V and the queries). */
 OMNI_API int omni_paged_decode_attention(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
                                          const int32_t* page_indptr, const int32_t* page_indices,
                                          const int64_t* seq_lens, const int32_t* work_indptr, int64_t rows,
