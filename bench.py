@@ -42,8 +42,8 @@ METRIC = "codec frames/s per GPU (ragged talker+codebook decode step); p50 step 
 # same kernel on the same workload (dram__bytes_read.sum + dram__bytes_write.sum over the
 # algorithmic bytes of the captured launch; see profiles/).  The bench scales it to the
 # timed launch by its algorithmic bytes (the traffic grows with the rows / tokens processed).
-GEMM_TRAFFIC_RATIO: dict[int, float] = {1: 6_883_840 / (1024 * 3072 * 2 + 64 * 3072 * 2 + 2 * 64 * 1024 * 2 + 8 * 64 * 4)}
-ATTN_TRAFFIC_RATIO: dict[int, float] = {1: (37_133_312 + 16_384) / (35_473 * 1024 + 64 * 16 * 128 * 2 * 2)}
+GEMM_TRAFFIC_RATIO: dict[int, float] = {1: (6_881_536 + 0) / (1024 * 3072 * 2 + 64 * 3072 * 2 + 2 * 64 * 1024 * 2 + 8 * 64 * 4)}
+ATTN_TRAFFIC_RATIO: dict[int, float] = {1: (37_134_592 + 4_864) / (35_473 * 1024 + 64 * 16 * 128 * 2 * 2)}
 UNIT = "frames/s"
 STREAMS = 64
 

@@ -141,14 +141,16 @@ def check(rc: int, name: str) -> None:
     raise RuntimeError(f"CUDA error in {msg}")
 
 
-# Entry points that launch kernels (counted by launch_counter()).
+# Entry points that launch kernels (counted by launch_count()), one kernel each but
+# the paged decode attention (the attention and the merge of split rows).
 _LAUNCHERS = {n for n in SIGNATURES if not n.endswith("_bytes") and n not in (
     "omni_version", "omni_last_error", "omni_device_status")}
+_KERNELS_PER_CALL = {"omni_paged_decode_attention": 2, "omni_paged_decode_attention_noalloc": 2}
 _launches = 0
 
 
 def launch_count() -> int:
-    """Number of kernel-launching C-ABI calls made by this process so far."""
+    """Number of kernels launched through the C-ABI by this process so far."""
     return _launches
 
 
@@ -156,7 +158,7 @@ def call(name: str, *args) -> None:
     global _launches
     check(getattr(load(), name)(*args), name)
     if name in _LAUNCHERS:
-        _launches += 1
+        _launches += _KERNELS_PER_CALL.get(name, 1)
 
 
 def ptr(t: torch.Tensor | None) -> int | None:
