@@ -456,6 +456,59 @@ OMNI_API int omni_prefill_attention(const void* q, int64_t q_stride, const void*
                                    int64_t max_tiles, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                                    int32_t page_size, float sm_scale, void* out, int64_t out_stride, void* stream);
 
+/* ======================================================================== */
+/* Streaming vocoder (code2wav) step                                        */
+/* ======================================================================== */
+
+/* dtype codes of the vocoder entry points */
+#define OMNI_DTYPE_BF16 0
+#define OMNI_DTYPE_F16 1
+#define OMNI_DTYPE_F32 2
+
+/* out = SnakeBeta(conv_output + bias [+ residual]) with every intermediate rounded to
+ * the activations' dtype where the eager adds and SnakeBeta round; sum_out (nullable)
+ * receives the pre-activation sum.  Replaces fused_bias_snake_beta
+ * (sglang_omni/kernels/bias_snake_beta.py:100-151).
+ *   conv_output, out: [batch, length, channels] bf16 / fp16, rows contiguous, batch
+ *   strides given; residual, sum_out contiguous; bias, alpha_scale (exp(alpha)),
+ *   inverse_beta (1 / (exp(beta) + eps)): [channels]; channels % 8 == 0, 16-byte
+ *   aligned operands. */
+OMNI_API int omni_bias_snake_beta(const void* conv_output, int64_t conv_batch_stride, const void* bias,
+                                  const void* residual, void* sum_out, void* out, int64_t out_batch_stride,
+                                  const void* alpha_scale, const void* inverse_beta, int64_t batch, int64_t length,
+                                  int64_t channels, int32_t dtype, void* stream);
+
+/* out[b, 0, t] = clamp(bias + sum_{tap, c} padded[b, t + tap, c] * weight[0, c, tap], -1, 1)
+ * (NaN kept), accumulated in fp32 and rounded once; a position's bits do not depend on
+ * how positions are split across calls.  Replaces clamped_single_output_conv
+ * (sglang_omni/kernels/single_output_conv.py:68-102).
+ *   padded [batch, length + taps - 1, channels] channels-last, rows contiguous;
+ *   weight [1, channels, taps] with the given strides; out [batch, 1, length]. */
+OMNI_API int omni_clamped_single_output_conv(const void* padded, int64_t padded_batch_stride, const void* weight,
+                                             int64_t weight_channel_stride, int64_t weight_tap_stride,
+                                             const void* bias, void* out, int64_t batch, int64_t length,
+                                             int64_t channels, int32_t taps, int32_t dtype, void* stream);
+
+/* Causal-conv state: padded [rows, history + new + tail, channels] gets each row's slot
+ * history in front (zeros for a cold slot) and zeros after the new samples; the slot
+ * keeps the last `history` samples of (history ++ new).  history <= 64.  Replaces
+ * history_exchange (sglang_omni/kernels/codec_state.py:153-184). */
+OMNI_API int omni_history_exchange(void* padded, int64_t padded_row_stride, int64_t padded_sample_stride,
+                                   int64_t padded_channel_stride, void* history_pool, int64_t pool_slot_stride,
+                                   int64_t pool_sample_stride, int64_t pool_channel_stride, const int64_t* slot_index,
+                                   int64_t rows, int32_t history_samples, int32_t new_samples, int32_t tail_samples,
+                                   int32_t channels, int32_t is_cold, int32_t element_bytes, void* stream);
+
+/* Transposed-conv state: output [rows, emitted + overlap, channels]: the slot's overlap
+ * is added into the first samples (not for a cold slot, rounded once) and the samples
+ * past the emitted ones become the slot's overlap.  emitted >= overlap.  Replaces
+ * overlap_exchange (sglang_omni/kernels/codec_state.py:187-210). */
+OMNI_API int omni_overlap_exchange(void* output, int64_t output_row_stride, int64_t output_sample_stride,
+                                   int64_t output_channel_stride, void* overlap_pool, int64_t pool_slot_stride,
+                                   int64_t pool_sample_stride, int64_t pool_channel_stride, const int64_t* slot_index,
+                                   int64_t rows, int32_t overlap_samples, int32_t emitted_samples, int32_t channels,
+                                   int32_t is_cold, int32_t dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

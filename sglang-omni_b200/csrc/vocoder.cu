@@ -1,0 +1,385 @@
+// Kernels of the streaming vocoder (code2wav) step that consumes the decode step's codes:
+//
+// bias_snake_beta_kernel — SnakeBeta(conv + bias [+ residual]) over channels-last rows
+//   (fused_bias_snake_beta, sglang_omni/kernels/bias_snake_beta.py:100-151): every
+//   intermediate rounds to the activations' dtype where the eager adds and SnakeBeta
+//   round (conv + bias, + residual, x * exp(alpha), sin, its square, the 1 / beta
+//   scale, the final add), 16-byte vectors, parameters read at the vector's channel.
+// single_output_conv_kernel — a stride-one, undilated conv from channels-last rows to
+//   one output channel, + bias, clamped to [-1, 1] (NaN kept), accumulated in fp32 and
+//   rounded once (clamped_single_output_conv, sglang_omni/kernels/single_output_conv.py:
+//   68-102): one warp per output position, lanes over 16-byte channel vectors, the taps
+//   summed per lane and the lanes reduced by a fixed xor tree, so a position's bits do
+//   not depend on how the positions are split into calls.
+// history_exchange_kernel / overlap_exchange_kernel — the per-slot codec state of a
+//   causal conv (its history in front of the new samples, zeros after) and of a
+//   transposed conv (its overlap added into the next output) (history_exchange /
+//   overlap_exchange, sglang_omni/kernels/codec_state.py:153-210): one CTA per (row,
+//   channel block); every read of a slot's old state precedes every write of its new one.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "capi_util.h"
+#include "common.cuh"
+
+namespace omni {
+namespace {
+
+// dtype codes of these entry points
+constexpr int kBF16 = 0, kF16 = 1, kF32 = 2;
+
+template <int DT>
+struct Elem;
+template <>
+struct Elem<kBF16> {
+  using T = uint16_t;
+  static OMNI_DEVINL float load(T v) { return bf2f(v); }
+  static OMNI_DEVINL T store(float f) { return f2bf(f); }
+};
+template <>
+struct Elem<kF16> {
+  using T = uint16_t;
+  static OMNI_DEVINL float load(T v) {
+    __half h;
+    *reinterpret_cast<uint16_t*>(&h) = v;
+    return __half2float(h);
+  }
+  static OMNI_DEVINL T store(float f) {
+    __half h = __float2half_rn(f);
+    return *reinterpret_cast<uint16_t*>(&h);
+  }
+};
+template <>
+struct Elem<kF32> {
+  using T = float;
+  static OMNI_DEVINL float load(T v) { return v; }
+  static OMNI_DEVINL T store(float f) { return f; }
+};
+
+// rounds through the activations' dtype
+template <int DT>
+OMNI_DEVINL float rnd(float f) {
+  return Elem<DT>::load(Elem<DT>::store(f));
+}
+
+struct SnakeParams {
+  const void* conv;
+  int64_t conv_batch_stride;  // elements
+  const void* bias;
+  const void* residual;  // contiguous [B, L, C] or null
+  void* sum_out;         // contiguous [B, L, C] or null
+  void* out;
+  int64_t out_batch_stride;
+  const void* alpha_scale;   // [C]
+  const void* inverse_beta;  // [C]
+  int64_t row_vectors;       // L * C / vector elements
+  int channel_vectors;       // C / vector elements
+};
+
+template <int DT>
+__global__ void __launch_bounds__(256) bias_snake_beta_kernel(const __grid_constant__ SnakeParams p) {
+  using T = typename Elem<DT>::T;
+  constexpr int E = 16 / (int)sizeof(T);
+  const int64_t batch = blockIdx.y;
+  const int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  griddep_wait();
+  griddep_launch();
+  if (v >= p.row_vectors) return;
+  const int64_t ch0 = (v % p.channel_vectors) * E;
+  const int64_t off = v * E;
+  const uint4 cv = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.conv) + batch * p.conv_batch_stride + off);
+  const uint4 bv = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.bias) + ch0);
+  const uint4 av = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.alpha_scale) + ch0);
+  const uint4 iv = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.inverse_beta) + ch0);
+  const int64_t cbase = batch * p.row_vectors * E + off;  // contiguous [B, L, C]
+  uint4 rv = make_uint4(0, 0, 0, 0);
+  if (p.residual) rv = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.residual) + cbase);
+  const T* c = reinterpret_cast<const T*>(&cv);
+  const T* bb = reinterpret_cast<const T*>(&bv);
+  const T* a = reinterpret_cast<const T*>(&av);
+  const T* ib = reinterpret_cast<const T*>(&iv);
+  const T* r = reinterpret_cast<const T*>(&rv);
+  uint4 sv, ov;
+  T* s = reinterpret_cast<T*>(&sv);
+  T* o = reinterpret_cast<T*>(&ov);
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    float total = rnd<DT>(Elem<DT>::load(c[j]) + Elem<DT>::load(bb[j]));
+    if (p.residual) total = rnd<DT>(total + Elem<DT>::load(r[j]));
+    s[j] = Elem<DT>::store(total);
+    const float phase = rnd<DT>(total * Elem<DT>::load(a[j]));
+    const float sine = rnd<DT>(sinf(phase));
+    const float sq = rnd<DT>(sine * sine);
+    const float scaled = rnd<DT>(Elem<DT>::load(ib[j]) * sq);
+    o[j] = Elem<DT>::store(total + scaled);
+  }
+  if (p.sum_out) *reinterpret_cast<uint4*>(static_cast<T*>(p.sum_out) + cbase) = sv;
+  *reinterpret_cast<uint4*>(static_cast<T*>(p.out) + batch * p.out_batch_stride + off) = ov;
+}
+
+struct ConvParams {
+  const void* padded;  // [B, L + taps - 1, C] rows contiguous
+  int64_t padded_batch_stride;
+  const void* weight;  // [1, C, taps] with the given strides
+  int64_t w_channel_stride, w_tap_stride;
+  const void* bias;    // [1]
+  void* out;           // [B, 1, L] contiguous
+  int64_t length;
+  int channels, taps;
+};
+
+template <int DT>
+__global__ void __launch_bounds__(256) single_output_conv_kernel(const __grid_constant__ ConvParams p) {
+  using T = typename Elem<DT>::T;
+  constexpr int E = 16 / (int)sizeof(T);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t pos = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  const int64_t batch = blockIdx.y;
+  griddep_wait();
+  griddep_launch();
+  if (pos >= p.length) return;
+  const T* row0 = static_cast<const T*>(p.padded) + batch * p.padded_batch_stride + pos * p.channels;
+  const T* w = static_cast<const T*>(p.weight);
+  float acc = 0.0f;
+  // lane l: channel vectors l, l + 32, ...; every tap of a vector before the next vector
+  for (int cv = lane; cv * E < p.channels; cv += 32) {
+    const int c0 = cv * E;
+    float part[E];
+#pragma unroll
+    for (int j = 0; j < E; ++j) part[j] = 0.0f;
+    for (int tap = 0; tap < p.taps; ++tap) {
+      const uint4 xv = *reinterpret_cast<const uint4*>(row0 + (int64_t)tap * p.channels + c0);
+      const T* x = reinterpret_cast<const T*>(&xv);
+#pragma unroll
+      for (int j = 0; j < E; ++j)
+        part[j] = fmaf(Elem<DT>::load(x[j]),
+                       Elem<DT>::load(w[(int64_t)(c0 + j) * p.w_channel_stride + (int64_t)tap * p.w_tap_stride]),
+                       part[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < E; ++j) acc += part[j];
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
+  if (lane == 0) {
+    float v = acc + Elem<DT>::load(static_cast<const T*>(p.bias)[0]);
+    if (v == v) v = fminf(fmaxf(v, -1.0f), 1.0f);  // NaN passes through
+    static_cast<T*>(p.out)[batch * p.length + pos] = Elem<DT>::store(v);
+  }
+}
+
+constexpr int kChannelBlock = 64;
+constexpr int kMaxStateSamples = 64;  // history / overlap samples held per CTA
+
+struct HistoryParams {
+  void* padded;
+  int64_t pr, ps, pc;  // padded strides: row, sample, channel (elements)
+  void* pool;
+  int64_t qs_slot, qs_sample, qs_channel;  // pool strides
+  const int64_t* slot_index;
+  int history, new_samples, tail, channels, cold;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kChannelBlock * 4) history_exchange_kernel(const __grid_constant__ HistoryParams p) {
+  __shared__ T s_old[kMaxStateSamples][kChannelBlock];
+  __shared__ T s_new[kMaxStateSamples][kChannelBlock];
+  const int64_t row = blockIdx.x;
+  const int c = blockIdx.y * kChannelBlock + (threadIdx.x % kChannelBlock);
+  const int s0 = threadIdx.x / kChannelBlock, sstep = blockDim.x / kChannelBlock;
+  griddep_wait();
+  griddep_launch();
+  const int64_t slot = p.slot_index[row];
+  T* padded = static_cast<T*>(p.padded) + row * p.pr + (int64_t)c * p.pc;
+  T* pool = static_cast<T*>(p.pool) + slot * p.qs_slot + (int64_t)c * p.qs_channel;
+  const bool on = c < p.channels;
+  // reads: the slot's old history, and the new history (the last `history` samples of
+  // history + new samples)
+  for (int s = s0; s < p.history; s += sstep) {
+    T old = T(0), nh = T(0);
+    if (on) {
+      const int src = s + p.new_samples;  // position in (old history ++ new samples)
+      if (!p.cold) old = pool[(int64_t)s * p.qs_sample];
+      if (src >= p.history) nh = padded[(int64_t)src * p.ps];
+      else if (!p.cold) nh = pool[(int64_t)src * p.qs_sample];
+    }
+    s_old[s][threadIdx.x % kChannelBlock] = old;
+    s_new[s][threadIdx.x % kChannelBlock] = nh;
+  }
+  __syncthreads();
+  if (!on) return;
+  for (int s = s0; s < p.history; s += sstep) {
+    padded[(int64_t)s * p.ps] = s_old[s][threadIdx.x % kChannelBlock];
+    pool[(int64_t)s * p.qs_sample] = s_new[s][threadIdx.x % kChannelBlock];
+  }
+  for (int s = s0; s < p.tail; s += sstep) padded[(int64_t)(p.history + p.new_samples + s) * p.ps] = T(0);
+}
+
+struct OverlapParams {
+  void* output;
+  int64_t orow, osample, ochannel;
+  void* pool;
+  int64_t qs_slot, qs_sample, qs_channel;
+  const int64_t* slot_index;
+  int overlap, emitted, channels, cold;
+};
+
+template <int DT>
+__global__ void __launch_bounds__(kChannelBlock * 4) overlap_exchange_kernel(const __grid_constant__ OverlapParams p) {
+  using T = typename Elem<DT>::T;
+  const int64_t row = blockIdx.x;
+  const int c = blockIdx.y * kChannelBlock + (threadIdx.x % kChannelBlock);
+  const int s0 = threadIdx.x / kChannelBlock, sstep = blockDim.x / kChannelBlock;
+  griddep_wait();
+  griddep_launch();
+  if (c >= p.channels) return;
+  const int64_t slot = p.slot_index[row];
+  T* out = static_cast<T*>(p.output) + row * p.orow + (int64_t)c * p.ochannel;
+  T* pool = static_cast<T*>(p.pool) + slot * p.qs_slot + (int64_t)c * p.qs_channel;
+  // the ranges [0, overlap) and [emitted, emitted + overlap) are disjoint (emitted >= overlap)
+  for (int s = s0; s < p.overlap; s += sstep) {
+    const T tail = out[(int64_t)(p.emitted + s) * p.osample];
+    if (!p.cold) {
+      const T prev = pool[(int64_t)s * p.qs_sample];
+      T* h = out + (int64_t)s * p.osample;
+      *h = Elem<DT>::store(Elem<DT>::load(*h) + Elem<DT>::load(prev));
+    }
+    pool[(int64_t)s * p.qs_sample] = tail;
+  }
+}
+
+bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
+
+}  // namespace
+}  // namespace omni
+
+using namespace omni;
+
+extern "C" OMNI_API int omni_bias_snake_beta(const void* conv_output, int64_t conv_batch_stride, const void* bias,
+                                             const void* residual, void* sum_out, void* out,
+                                             int64_t out_batch_stride, const void* alpha_scale,
+                                             const void* inverse_beta, int64_t batch, int64_t length,
+                                             int64_t channels, int32_t dtype, void* stream) {
+  if (batch < 0 || length < 0 || channels <= 0) return set_error(OMNI_ERR_INVALID, "bad SnakeBeta shape");
+  if (dtype != kBF16 && dtype != kF16) return set_error(OMNI_ERR_UNSUPPORTED, "SnakeBeta runs on bf16 or fp16");
+  const int E = 8;
+  if (channels % E) return set_error(OMNI_ERR_UNSUPPORTED, "channels must split into 16-byte vectors");
+  if (!aligned16(conv_output) || !aligned16(out) || !aligned16(bias) || !aligned16(alpha_scale) ||
+      !aligned16(inverse_beta) || (residual && !aligned16(residual)) || (sum_out && !aligned16(sum_out)) ||
+      conv_batch_stride % E || out_batch_stride % E)
+    return set_error(OMNI_ERR_UNSUPPORTED, "SnakeBeta operands must be 16-byte aligned");
+  if (batch == 0 || length == 0) return OMNI_OK;
+  SnakeParams p{};
+  p.conv = conv_output;
+  p.conv_batch_stride = conv_batch_stride;
+  p.bias = bias;
+  p.residual = residual;
+  p.sum_out = sum_out;
+  p.out = out;
+  p.out_batch_stride = out_batch_stride;
+  p.alpha_scale = alpha_scale;
+  p.inverse_beta = inverse_beta;
+  p.row_vectors = length * channels / E;
+  p.channel_vectors = (int)(channels / E);
+  const dim3 grid((unsigned)((p.row_vectors + 255) / 256), (unsigned)batch);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return check_launch(dtype == kBF16 ? launch(bias_snake_beta_kernel<kBF16>, grid, dim3(256), 0, st, p)
+                                     : launch(bias_snake_beta_kernel<kF16>, grid, dim3(256), 0, st, p));
+}
+
+extern "C" OMNI_API int omni_clamped_single_output_conv(const void* padded, int64_t padded_batch_stride,
+                                                        const void* weight, int64_t weight_channel_stride,
+                                                        int64_t weight_tap_stride, const void* bias, void* out,
+                                                        int64_t batch, int64_t length, int64_t channels,
+                                                        int32_t taps, int32_t dtype, void* stream) {
+  if (batch < 0 || length < 0 || channels <= 0 || taps <= 0) return set_error(OMNI_ERR_INVALID, "bad conv shape");
+  if (dtype != kBF16 && dtype != kF16 && dtype != kF32) return set_error(OMNI_ERR_UNSUPPORTED, "unsupported dtype");
+  const int E = dtype == kF32 ? 4 : 8;
+  if (channels % E || padded_batch_stride % E || !aligned16(padded))
+    return set_error(OMNI_ERR_UNSUPPORTED, "channels-last rows must split into 16-byte vectors");
+  if (batch == 0 || length == 0) return OMNI_OK;
+  ConvParams p{};
+  p.padded = padded;
+  p.padded_batch_stride = padded_batch_stride;
+  p.weight = weight;
+  p.w_channel_stride = weight_channel_stride;
+  p.w_tap_stride = weight_tap_stride;
+  p.bias = bias;
+  p.out = out;
+  p.length = length;
+  p.channels = (int)channels;
+  p.taps = taps;
+  const dim3 grid((unsigned)((length + 7) / 8), (unsigned)batch);  // 8 positions (warps) per CTA
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == kBF16) return check_launch(launch(single_output_conv_kernel<kBF16>, grid, dim3(256), 0, st, p));
+  if (dtype == kF16) return check_launch(launch(single_output_conv_kernel<kF16>, grid, dim3(256), 0, st, p));
+  return check_launch(launch(single_output_conv_kernel<kF32>, grid, dim3(256), 0, st, p));
+}
+
+extern "C" OMNI_API int omni_history_exchange(void* padded, int64_t padded_row_stride, int64_t padded_sample_stride,
+                                              int64_t padded_channel_stride, void* history_pool,
+                                              int64_t pool_slot_stride, int64_t pool_sample_stride,
+                                              int64_t pool_channel_stride, const int64_t* slot_index, int64_t rows,
+                                              int32_t history_samples, int32_t new_samples, int32_t tail_samples,
+                                              int32_t channels, int32_t is_cold, int32_t element_bytes,
+                                              void* stream) {
+  if (rows < 0 || history_samples < 0 || new_samples < 0 || tail_samples < 0 || channels <= 0)
+    return set_error(OMNI_ERR_INVALID, "bad history exchange shape");
+  if (history_samples > kMaxStateSamples || tail_samples > (1 << 20))
+    return set_error(OMNI_ERR_UNSUPPORTED, "history longer than 64 samples");
+  if (element_bytes != 2 && element_bytes != 4) return set_error(OMNI_ERR_UNSUPPORTED, "2- or 4-byte elements");
+  if (rows == 0) return OMNI_OK;
+  HistoryParams p{};
+  p.padded = padded;
+  p.pr = padded_row_stride;
+  p.ps = padded_sample_stride;
+  p.pc = padded_channel_stride;
+  p.pool = history_pool;
+  p.qs_slot = pool_slot_stride;
+  p.qs_sample = pool_sample_stride;
+  p.qs_channel = pool_channel_stride;
+  p.slot_index = slot_index;
+  p.history = history_samples;
+  p.new_samples = new_samples;
+  p.tail = tail_samples;
+  p.channels = channels;
+  p.cold = is_cold;
+  const dim3 grid((unsigned)rows, (unsigned)((channels + kChannelBlock - 1) / kChannelBlock));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (element_bytes == 2)
+    return check_launch(launch(history_exchange_kernel<uint16_t>, grid, dim3(kChannelBlock * 4), 0, st, p));
+  return check_launch(launch(history_exchange_kernel<uint32_t>, grid, dim3(kChannelBlock * 4), 0, st, p));
+}
+
+extern "C" OMNI_API int omni_overlap_exchange(void* output, int64_t output_row_stride, int64_t output_sample_stride,
+                                              int64_t output_channel_stride, void* overlap_pool,
+                                              int64_t pool_slot_stride, int64_t pool_sample_stride,
+                                              int64_t pool_channel_stride, const int64_t* slot_index, int64_t rows,
+                                              int32_t overlap_samples, int32_t emitted_samples, int32_t channels,
+                                              int32_t is_cold, int32_t dtype, void* stream) {
+  if (rows < 0 || overlap_samples < 0 || emitted_samples < 0 || channels <= 0)
+    return set_error(OMNI_ERR_INVALID, "bad overlap exchange shape");
+  if (emitted_samples < overlap_samples)
+    return set_error(OMNI_ERR_INVALID, "emitted samples must cover the overlap");
+  if (dtype != kBF16 && dtype != kF16 && dtype != kF32) return set_error(OMNI_ERR_UNSUPPORTED, "unsupported dtype");
+  if (rows == 0 || overlap_samples == 0) return OMNI_OK;
+  OverlapParams p{};
+  p.output = output;
+  p.orow = output_row_stride;
+  p.osample = output_sample_stride;
+  p.ochannel = output_channel_stride;
+  p.pool = overlap_pool;
+  p.qs_slot = pool_slot_stride;
+  p.qs_sample = pool_sample_stride;
+  p.qs_channel = pool_channel_stride;
+  p.slot_index = slot_index;
+  p.overlap = overlap_samples;
+  p.emitted = emitted_samples;
+  p.channels = channels;
+  p.cold = is_cold;
+  const dim3 grid((unsigned)rows, (unsigned)((channels + kChannelBlock - 1) / kChannelBlock));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == kBF16) return check_launch(launch(overlap_exchange_kernel<kBF16>, grid, dim3(kChannelBlock * 4), 0, st, p));
+  if (dtype == kF16) return check_launch(launch(overlap_exchange_kernel<kF16>, grid, dim3(kChannelBlock * 4), 0, st, p));
+  return check_launch(launch(overlap_exchange_kernel<kF32>, grid, dim3(kChannelBlock * 4), 0, st, p));
+}
