@@ -360,6 +360,78 @@ def kernel_table(runner, iters: int = 50, only: str | None = None) -> list[dict]
     return rows_out
 
 
+def run_vocoder(args) -> None:
+    """One JSON line per vocoder-step kernel: device time (CUDA graph of launches, inputs
+    larger than L2 rotated through) and HBM bandwidth against the measured copy peak."""
+    from omni_b200.kernels.bias_snake_beta import SnakeBetaCoefficients, fused_bias_snake_beta
+    from omni_b200.kernels.codec_state import history_exchange, overlap_exchange
+    from omni_b200.kernels.single_output_conv import clamped_single_output_conv
+
+    hbm, _, kind = measured_peaks()
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    bf = torch.bfloat16
+    sets = 4  # input sets cycled through: every set is larger than L2 / sets
+    lines = []
+
+    class _Act:
+        def __init__(self, c):
+            self.alpha = (torch.randn(c, device=dev) * 0.5).to(bf)
+            self.beta = (torch.randn(c, device=dev) * 0.5).to(bf)
+            self.no_div_by_zero = 1e-9
+
+    # SnakeBeta over a code2wav block's conv output: 64 streams x 256 positions x 1536 channels
+    B, L, C = 64, 256, 1536
+    coef = SnakeBetaCoefficients.from_activation(_Act(C))
+    bias = torch.randn(C, device=dev, dtype=bf)
+    xs = [torch.randn(B, L, C, device=dev, dtype=bf) for _ in range(sets)]
+    rs = [torch.randn(B, L, C, device=dev, dtype=bf) for _ in range(sets)]
+    outs = [torch.empty(B, L, C, device=dev, dtype=bf) for _ in range(sets)]
+    sums = [torch.empty(B, L, C, device=dev, dtype=bf) for _ in range(sets)]
+    cyc = {"i": 0}
+
+    def snake():
+        i = cyc["i"] % sets
+        cyc["i"] += 1
+        fused_bias_snake_beta(xs[i], bias, coef, outs[i], residual=rs[i], sum_out=sums[i])
+
+    t = time_kernel(snake, 32)
+    nbytes = 4 * B * L * C * 2
+    lines.append(("bias_snake_beta (conv + bias + residual -> SnakeBeta, sum)", f"[{B}, {L}, {C}] bf16", t, nbytes))
+
+    # the last conv of code2wav: 96 channels, 7 taps, 64 streams x 4800 samples
+    B2, L2, C2, taps = 64, 4800, 96, 7
+    conv = torch.nn.Conv1d(C2, 1, taps).to(device=dev, dtype=bf)
+    pads = [torch.randn(B2, L2 + taps - 1, C2, device=dev, dtype=bf) for _ in range(sets)]
+
+    def sconv():
+        i = cyc["i"] % sets
+        cyc["i"] += 1
+        clamped_single_output_conv(pads[i], conv, L2)
+
+    with torch.inference_mode():
+        t = time_kernel(sconv, 32)
+    nbytes = B2 * (L2 + taps - 1) * C2 * 2 + B2 * L2 * 2
+    lines.append(("clamped_single_output_conv", f"[{B2}, {L2}+{taps - 1}, {C2}] bf16", t, nbytes))
+
+    # codec state of a causal conv (history 6) and a transposed conv (overlap 8), 1536 channels
+    R, H, N, O, E = 64, 6, 32, 8, 32
+    pool = torch.randn(R, H, C, device=dev, dtype=bf)
+    slot = torch.arange(R, device=dev)
+    padded = torch.randn(R, H + N, C, device=dev, dtype=bf)
+    opool = torch.randn(R, O, C, device=dev, dtype=bf)
+    out_t = torch.randn(R, E + O, C, device=dev, dtype=bf)
+    t = time_kernel(lambda: history_exchange(padded, pool, slot, N, False), 32)
+    lines.append(("history_exchange", f"{R} slots x {H} samples x {C} ch bf16", t, R * C * 2 * (3 * H)))
+    t = time_kernel(lambda: overlap_exchange(out_t, opool, slot, E, False), 32)
+    lines.append(("overlap_exchange", f"{R} slots x {O} samples x {C} ch bf16", t, R * C * 2 * (4 * O)))
+
+    for name, shape, secs, nbytes in lines:
+        gbs = nbytes / secs / 1e9
+        print(json.dumps({"kernel": name, "shape": shape, "us": secs * 1e6, "algorithmic_bytes": nbytes,
+                          "achieved_gbs": gbs, "peak_gbs": hbm, "frac": gbs / hbm, "peak_kind": kind}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -377,7 +449,12 @@ def main() -> None:
     ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3],
                     help="1: dense talker, 64 streams (the headline); 2: mixed prefill (16 new streams, prompts "
                          "U[64, 4096]) + 112 decode streams; 3: MoE talker with FP8 experts, 256 streams")
+    ap.add_argument("--vocoder", action="store_true",
+                    help="time the streaming vocoder step's kernels (one JSON line each) and exit")
     args = ap.parse_args()
+    if args.vocoder:
+        run_vocoder(args)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -8,9 +8,9 @@
 // single_output_conv_kernel — a stride-one, undilated conv from channels-last rows to
 //   one output channel, + bias, clamped to [-1, 1] (NaN kept), accumulated in fp32 and
 //   rounded once (clamped_single_output_conv, sglang_omni/kernels/single_output_conv.py:
-//   68-102): one warp per output position, lanes over 16-byte channel vectors, the taps
-//   summed per lane and the lanes reduced by a fixed xor tree, so a position's bits do
-//   not depend on how the positions are split into calls.
+//   68-102): a CTA stages 256 positions' input rows in shared memory and each thread
+//   sums one position in a fixed order, so a position's bits do not depend on how the
+//   positions are split into calls.
 // history_exchange_kernel / overlap_exchange_kernel — the per-slot codec state of a
 //   causal conv (its history in front of the new samples, zeros after) and of a
 //   transposed conv (its overlap added into the next output) (history_exchange /
@@ -128,44 +128,64 @@ struct ConvParams {
   int channels, taps;
 };
 
+constexpr int kConvPositions = 256;  // output positions per CTA (one per thread)
+constexpr int kConvMaxSmem = 200 * 1024;
+
+// Padded row stride of the staged tile, in 16-byte vectors: odd, so that the 8 threads of
+// a 16-byte access phase (consecutive rows) hit distinct bank groups.
+__host__ __device__ __forceinline__ int conv_row_vectors(int vecs) { return vecs + ((vecs & 1) ? 2 : 1); }
+
+// CTA: 256 consecutive output positions of one row.  Their input rows (256 + taps - 1,
+// channels-last) are staged in shared memory with 16-byte vectors at an odd padded
+// stride; the weights sit in shared memory too.  Thread p sums tap by tap over the
+// channels in a fixed order, so a position's bits do not depend on the split of the
+// positions into calls.
 template <int DT>
-__global__ void __launch_bounds__(256) single_output_conv_kernel(const __grid_constant__ ConvParams p) {
+__global__ void __launch_bounds__(kConvPositions) single_output_conv_kernel(const __grid_constant__ ConvParams p) {
   using T = typename Elem<DT>::T;
   constexpr int E = 16 / (int)sizeof(T);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t pos = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int C = p.channels, taps = p.taps;
+  const int rs = conv_row_vectors(C / E) * E;  // padded row stride (elements)
+  const int nrows = kConvPositions + taps - 1;
+  T* tile = reinterpret_cast<T*>(smem);
+  float* wsm = reinterpret_cast<float*>(smem + (size_t)nrows * rs * sizeof(T));  // [taps][C]
   const int64_t batch = blockIdx.y;
+  const int64_t pos0 = (int64_t)blockIdx.x * kConvPositions;
+  const T* w = static_cast<const T*>(p.weight);
+  // weights do not depend on the previous kernel
+  for (int i = threadIdx.x; i < taps * C; i += blockDim.x) {
+    const int tap = i / C, c = i % C;
+    wsm[i] = Elem<DT>::load(w[(int64_t)c * p.w_channel_stride + (int64_t)tap * p.w_tap_stride]);
+  }
   griddep_wait();
   griddep_launch();
+  const T* src = static_cast<const T*>(p.padded) + batch * p.padded_batch_stride;
+  const int64_t avail = p.length + taps - 1 - pos0;  // input rows left in this batch row
+  const int vecs = C / E;
+  for (int i = threadIdx.x; i < nrows * vecs; i += blockDim.x) {
+    const int r = i / vecs, v = i % vecs;
+    uint4 x = make_uint4(0, 0, 0, 0);
+    if (r < avail) x = *reinterpret_cast<const uint4*>(src + (pos0 + r) * C + v * E);
+    *reinterpret_cast<uint4*>(tile + r * rs + v * E) = x;
+  }
+  __syncthreads();
+  const int64_t pos = pos0 + threadIdx.x;
   if (pos >= p.length) return;
-  const T* row0 = static_cast<const T*>(p.padded) + batch * p.padded_batch_stride + pos * p.channels;
-  const T* w = static_cast<const T*>(p.weight);
   float acc = 0.0f;
-  // lane l: channel vectors l, l + 32, ...; every tap of a vector before the next vector
-  for (int cv = lane; cv * E < p.channels; cv += 32) {
-    const int c0 = cv * E;
-    float part[E];
-#pragma unroll
-    for (int j = 0; j < E; ++j) part[j] = 0.0f;
-    for (int tap = 0; tap < p.taps; ++tap) {
-      const uint4 xv = *reinterpret_cast<const uint4*>(row0 + (int64_t)tap * p.channels + c0);
+  for (int tap = 0; tap < taps; ++tap) {
+    const T* row = tile + (threadIdx.x + tap) * rs;
+    const float* wt = wsm + tap * C;
+    for (int v = 0; v < vecs; ++v) {
+      const uint4 xv = *reinterpret_cast<const uint4*>(row + v * E);
       const T* x = reinterpret_cast<const T*>(&xv);
 #pragma unroll
-      for (int j = 0; j < E; ++j)
-        part[j] = fmaf(Elem<DT>::load(x[j]),
-                       Elem<DT>::load(w[(int64_t)(c0 + j) * p.w_channel_stride + (int64_t)tap * p.w_tap_stride]),
-                       part[j]);
+      for (int j = 0; j < E; ++j) acc = fmaf(Elem<DT>::load(x[j]), wt[v * E + j], acc);
     }
-#pragma unroll
-    for (int j = 0; j < E; ++j) acc += part[j];
   }
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
-  if (lane == 0) {
-    float v = acc + Elem<DT>::load(static_cast<const T*>(p.bias)[0]);
-    if (v == v) v = fminf(fmaxf(v, -1.0f), 1.0f);  // NaN passes through
-    static_cast<T*>(p.out)[batch * p.length + pos] = Elem<DT>::store(v);
-  }
+  float y = acc + Elem<DT>::load(static_cast<const T*>(p.bias)[0]);
+  if (y == y) y = fminf(fmaxf(y, -1.0f), 1.0f);  // NaN passes through
+  static_cast<T*>(p.out)[batch * p.length + pos] = Elem<DT>::store(y);
 }
 
 constexpr int kChannelBlock = 64;
@@ -309,11 +329,18 @@ extern "C" OMNI_API int omni_clamped_single_output_conv(const void* padded, int6
   p.length = length;
   p.channels = (int)channels;
   p.taps = taps;
-  const dim3 grid((unsigned)((length + 7) / 8), (unsigned)batch);  // 8 positions (warps) per CTA
+  const size_t smem = (size_t)(kConvPositions + taps - 1) * conv_row_vectors((int)(channels / E)) * 16 +
+                      (size_t)taps * channels * 4;
+  if (smem > (size_t)kConvMaxSmem) return set_error(OMNI_ERR_UNSUPPORTED, "conv tile exceeds shared memory");
+  const dim3 grid((unsigned)((length + kConvPositions - 1) / kConvPositions), (unsigned)batch);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == kBF16) return check_launch(launch(single_output_conv_kernel<kBF16>, grid, dim3(256), 0, st, p));
-  if (dtype == kF16) return check_launch(launch(single_output_conv_kernel<kF16>, grid, dim3(256), 0, st, p));
-  return check_launch(launch(single_output_conv_kernel<kF32>, grid, dim3(256), 0, st, p));
+  auto go = [&](auto kernel) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kConvMaxSmem);
+    return check_launch(launch(kernel, grid, dim3(kConvPositions), smem, st, p));
+  };
+  if (dtype == kBF16) return go(single_output_conv_kernel<kBF16>);
+  if (dtype == kF16) return go(single_output_conv_kernel<kF16>);
+  return go(single_output_conv_kernel<kF32>);
 }
 
 extern "C" OMNI_API int omni_history_exchange(void* padded, int64_t padded_row_stride, int64_t padded_sample_stride,
