@@ -25,7 +25,9 @@
 //   per-request cache slots (predictor_cached_self_attention,
 //   sglang_model.py:2168-2233; decode_attention_kernel,
 //   predictor_layers.py:336-396): one warp per (row, KV head) serving the
-//   group's query heads, lanes = slots, causal for the opening pair.
+//   group's query heads, lanes = slots, causal for the opening pair; every K and V
+//   load is issued up front (the earlier passes' slots before the PDL wait), V rows
+//   into shared memory.
 #include <mutex>
 
 #include "capi_util.h"
@@ -657,16 +659,38 @@ __global__ void __launch_bounds__(128) predictor_attention_kernel(const uint16_t
                                                                   int slot_stride, int slot_base, float scale,
                                                                   uint16_t* __restrict__ out, int64_t out_stride) {
   constexpr int D = 32 * E;
+  constexpr int CH = D / 8;  // 16-byte chunks of a K or V row
   __shared__ float qs[4][G][D];
-  griddep_wait();
-  griddep_launch();
+  __shared__ __align__(16) uint16_t vs[4][32][D];  // this warp's V rows, slot-major
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int item = blockIdx.x * 4 + warp;
-  if (item >= rows * hkv) return;
-  const int row = item / hkv, kvh = item % hkv;
+  const bool live = item < rows * hkv;
+  const int row = live ? item / hkv : 0, kvh = live ? item % hkv : 0;
   const int req = row / tokens_per_req, tk = row % tokens_per_req;
   const int last = slot_base + tk;  // inclusive
   const int64_t slot0 = (int64_t)req * slot_stride;
+  const uint16_t* kbase = k_cache + (slot0 * hkv + kvh) * D;
+  const uint16_t* vbase = v_cache + (slot0 * hkv + kvh) * D;
+  // The slots before slot_base were stored by earlier passes: their K row (lane = slot)
+  // and V rows load before griddepcontrol.wait; the step's own slots (and q) after it.
+  uint4 kreg[CH];
+  if (live && lane < slot_base) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) kreg[c] = reinterpret_cast<const uint4*>(kbase + (int64_t)lane * hkv * D)[c];
+  }
+  if (live)
+    for (int idx = lane; idx < slot_base * CH; idx += 32)
+      cp_async16(&vs[warp][idx / CH][(idx % CH) * 8], vbase + (int64_t)(idx / CH) * hkv * D + (idx % CH) * 8);
+  griddep_wait();
+  griddep_launch();
+  if (!live) return;
+  if (lane >= slot_base && lane <= last) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) kreg[c] = reinterpret_cast<const uint4*>(kbase + (int64_t)lane * hkv * D)[c];
+  }
+  for (int idx = slot_base * CH + lane; idx < (last + 1) * CH; idx += 32)
+    cp_async16(&vs[warp][idx / CH][(idx % CH) * 8], vbase + (int64_t)(idx / CH) * hkv * D + (idx % CH) * 8);
+  cp_async_commit();
   // the group's query heads, scaled, into this warp's shared slice
 #pragma unroll
   for (int g = 0; g < G; ++g)
@@ -678,13 +702,11 @@ __global__ void __launch_bounds__(128) predictor_attention_kernel(const uint16_t
   float sc[G];
   const bool valid = lane <= last;
   if (valid) {
-    const uint4* krow = reinterpret_cast<const uint4*>(k_cache + ((slot0 + lane) * hkv + kvh) * D);
 #pragma unroll
     for (int g = 0; g < G; ++g) sc[g] = 0.0f;
 #pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      const uint4 kv = krow[c];
-      const uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
+    for (int c = 0; c < CH; ++c) {
+      const uint32_t w[4] = {kreg[c].x, kreg[c].y, kreg[c].z, kreg[c].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float k0 = bf_lo(w[e]), k1 = bf_hi(w[e]);
@@ -706,26 +728,31 @@ __global__ void __launch_bounds__(128) predictor_attention_kernel(const uint16_t
     pr[g] = valid ? expf(sc[g] - m) : 0.0f;
     inv[g] = 1.0f / warp_sum_xor(pr[g]);
   }
+  cp_async_wait<0>();
+  __syncwarp();
   // P V: lane l owns dimensions E*l .. E*l+E-1
   float acc[G][E];
 #pragma unroll
   for (int g = 0; g < G; ++g)
 #pragma unroll
     for (int j = 0; j < E; ++j) acc[g][j] = 0.0f;
-  for (int s = 0; s <= last; ++s) {
-    const uint16_t* vrow = v_cache + ((slot0 + s) * hkv + kvh) * D + E * lane;
+  for (int sl = 0; sl <= last; ++sl) {
+    const uint16_t* vrow = &vs[warp][sl][E * lane];
     float v[E];
     if constexpr (E == 2) {
       const uint32_t w = *reinterpret_cast<const uint32_t*>(vrow);
       v[0] = bf_lo(w);
       v[1] = bf_hi(w);
     } else {
-#pragma unroll
-      for (int j = 0; j < E; ++j) v[j] = bf2f(vrow[j]);
+      const uint2 w = *reinterpret_cast<const uint2*>(vrow);
+      v[0] = bf_lo(w.x);
+      v[1] = bf_hi(w.x);
+      v[2] = bf_lo(w.y);
+      v[3] = bf_hi(w.y);
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const float ps = __shfl_sync(0xFFFFFFFFu, pr[g], s);
+      const float ps = __shfl_sync(0xFFFFFFFFu, pr[g], sl);
 #pragma unroll
       for (int j = 0; j < E; ++j) acc[g][j] = __fmaf_rn(ps, v[j], acc[g][j]);
     }
@@ -828,7 +855,7 @@ extern "C" OMNI_API int omni_predictor_attention(const void* q, int64_t q_stride
   if (slot_base + tokens_per_req > 32) return set_error(OMNI_ERR_UNSUPPORTED, "at most 32 cache slots");
   const int G = num_q_heads / num_kv_heads;
   if (G != 1 && G != 2 && G != 4) return set_error(OMNI_ERR_UNSUPPORTED, "1, 2 or 4 query heads per KV head");
-  if ((reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 3))
+  if ((reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15))
     return set_error(OMNI_ERR_UNSUPPORTED, "misaligned caches");
   if (rows == 0) return OMNI_OK;
   dim3 g((unsigned)((rows * num_kv_heads + 3) / 4)), b(128);
