@@ -319,8 +319,25 @@ OMNI_DEVINL float warp_scan_incl(float v) {
 // winning token (valid in every lane).  Follows sample_sorted_top_k
 // (sampling_kernels.py:385-438) and the torch fallback (sglang_model.py:1987-2034).
 template <int C>
+OMNI_DEVINL int64_t warp_sample_sorted_g(const float (&sc)[C], const uint32_t (&id)[C], int64_t top_k, float top_p,
+                                         bool has_top_p, const double (&gum)[C]);
+// Gumbel noise of ranks lane * C + j (depends only on the seed and the position).
+template <int C>
+OMNI_DEVINL void rank_gumbels(uint32_t hash_prefix, double (&gum)[C]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < C; ++j) gum[j] = gumbel_of(mm3_finish(hash_prefix, (uint32_t)(lane * C + j)));
+}
+template <int C>
 OMNI_DEVINL int64_t warp_sample_sorted(const float (&sc)[C], const uint32_t (&id)[C], int64_t top_k, float top_p,
                                        bool has_top_p, uint32_t hash_prefix) {
+  double gum[C];
+  rank_gumbels<C>(hash_prefix, gum);
+  return warp_sample_sorted_g<C>(sc, id, top_k, top_p, has_top_p, gum);
+}
+template <int C>
+OMNI_DEVINL int64_t warp_sample_sorted_g(const float (&sc)[C], const uint32_t (&id)[C], int64_t top_k, float top_p,
+                                         bool has_top_p, const double (&gum)[C]) {
   const int lane = threadIdx.x & 31;
   float masked[C], e[C], p[C];
   float mx = __uint_as_float(0xFF800000u);
@@ -368,7 +385,7 @@ OMNI_DEVINL int64_t warp_sample_sorted(const float (&sc)[C], const uint32_t (&id
   for (int j = 0; j < C; ++j) {
     const int r = lane * C + j;
     float lp = keep[j] ? det_logf(p[j]) : __uint_as_float(0xFF800000u);
-    double v = __dadd_rn((double)lp, gumbel_of(mm3_finish(hash_prefix, (uint32_t)r)));
+    double v = __dadd_rn((double)lp, gum[j]);
     if (j == 0 || v > best) {
       best = v;
       best_rank = r;
@@ -435,7 +452,8 @@ OMNI_DEVINL int block_argmax(const float (&v)[EPT], const bool (&valid)[EPT], in
 // Fused embedding epilogue: gathered[row] = table[token]; summed[row] += it;
 // returns this thread's part of the gathered row's sum of squares.
 OMNI_DEVINL float gather_add_row(const uint16_t* __restrict__ table, int hidden, int64_t token,
-                                 uint16_t* __restrict__ gathered, uint16_t* __restrict__ summed) {
+                                 uint16_t* __restrict__ gathered, uint16_t* __restrict__ summed,
+                                 const uint4* summed_pre = nullptr) {
   const uint4* src = reinterpret_cast<const uint4*>(table + token * (int64_t)hidden);
   float ss = 0.0f;
   for (int v = threadIdx.x; v < hidden / 8; v += kThreads) {
@@ -448,7 +466,7 @@ OMNI_DEVINL float gather_add_row(const uint16_t* __restrict__ table, int hidden,
     }
     if (gathered) reinterpret_cast<uint4*>(gathered)[v] = w;
     if (summed) {
-      uint4 s = reinterpret_cast<uint4*>(summed)[v];
+      uint4 s = (summed_pre && v == (int)threadIdx.x) ? *summed_pre : reinterpret_cast<uint4*>(summed)[v];
       s.x = pack_bf2(__fadd_rn(bf_lo(s.x), bf_lo(w.x)), __fadd_rn(bf_hi(s.x), bf_hi(w.x)));
       s.y = pack_bf2(__fadd_rn(bf_lo(s.y), bf_lo(w.y)), __fadd_rn(bf_hi(s.y), bf_hi(w.y)));
       s.z = pack_bf2(__fadd_rn(bf_lo(s.z), bf_lo(w.z)), __fadd_rn(bf_hi(s.z), bf_hi(w.z)));
@@ -509,21 +527,37 @@ OMNI_DEVINL void load_bf16_row(const uint16_t* row, int vocab, float (&v)[EPT], 
 template <int EPT, int C>
 __global__ void __launch_bounds__(kThreads) residual_sample_kernel(const __grid_constant__ ResidualParams p) {
   __shared__ SelectSmem sm;
-  griddep_wait();
-  griddep_launch();
   const int row = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // Step metadata (the row's sampling parameters, seed and position) and the running sum
+  // of the frame's codec embeddings come from kernels before the previous one: they load,
+  // and the rank Gumbel noise is computed, before griddepcontrol.wait.  The logits (the
+  // previous kernel's output) are read after it.
+  const bool sample = !p.argmax_all && (p.do_sample == nullptr || p.do_sample[row] != 0);
+  float t_row = 1.0f, top_p_row = 1.0f;
+  int64_t top_k_row = 0;
+  double gum[C];
+  if (sample) {
+    t_row = p.temps[row];
+    top_k_row = p.top_ks[row];
+    top_p_row = p.top_ps[row];
+    if (warp == 0) rank_gumbels<C>(mm3_prefix(p.seeds[row], p.positions[row] * p.pos_mul + p.pos_add), gum);
+  }
+  uint4 summed_pre = make_uint4(0, 0, 0, 0);
+  const bool has_pre = p.table != nullptr && p.summed != nullptr && tid < p.hidden / 8;
+  if (has_pre) summed_pre = reinterpret_cast<const uint4*>(p.summed + (int64_t)row * p.hidden)[tid];
+  griddep_wait();
+  griddep_launch();
   float v[EPT];
   bool valid[EPT];
   load_bf16_row<EPT>(p.logits + row * p.stride, p.vocab, v, valid);
 
-  const bool sample = !p.argmax_all && (p.do_sample == nullptr || p.do_sample[row] != 0);
   int64_t token;
   if (!sample) {
     int idx = block_argmax<EPT>(v, valid, tid * EPT, sm);
     token = idx;
   } else {
-    float t = p.temps[row];
+    float t = t_row;
     if (!(t >= 1e-5f)) t = (t != t) ? t : 1e-5f;
     uint32_t o[EPT];
 #pragma unroll
@@ -576,8 +610,7 @@ __global__ void __launch_bounds__(kThreads) residual_sample_kernel(const __grid_
       if (small) {
         if constexpr (C == 1) warp_bitonic32_torch(sc[0], id[0], p.max_top_k);
       }
-      const uint32_t hp = mm3_prefix(p.seeds[row], p.positions[row] * p.pos_mul + p.pos_add);
-      int64_t tok = warp_sample_sorted<C>(sc, id, p.top_ks[row], p.top_ps[row], p.has_top_p != 0, hp);
+      int64_t tok = warp_sample_sorted_g<C>(sc, id, top_k_row, top_p_row, p.has_top_p != 0, gum);
       if (lane == 0) sm.token = tok;
     }
     __syncthreads();
@@ -586,7 +619,8 @@ __global__ void __launch_bounds__(kThreads) residual_sample_kernel(const __grid_
   if (tid == 0) p.out[row * p.out_stride] = token;
   if (p.table != nullptr) {
     float ss = gather_add_row(p.table, p.hidden, token, p.gathered ? p.gathered + (int64_t)row * p.hidden : nullptr,
-                              p.summed ? p.summed + (int64_t)row * p.hidden : nullptr);
+                              p.summed ? p.summed + (int64_t)row * p.hidden : nullptr,
+                              has_pre ? &summed_pre : nullptr);
     if (p.gathered_ss) {
       ss = warp_sum_xor(ss);
       __syncthreads();
