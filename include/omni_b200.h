@@ -349,6 +349,27 @@ OMNI_API int omni_decode_rollback(int64_t rows, int64_t* seq_lens, const int64_t
                                   const int64_t* out_cache_loc, int64_t* free_head, int64_t* freed_slots,
                                   int64_t* num_freed, void* stream);
 
+/* Batch compaction of the continuous-batching runner (the row moves of an
+ * omni_sched_plan, include/omni_sched.h): for every move m and tensor t, row
+ * dst[m] of tensor t becomes a copy of its row src[m].  bases / row_bytes /
+ * row_strides (bytes) describe up to 24 per-row state tensors; bases, src and
+ * dst are HOST arrays (passed by value to the kernel).  Sources and
+ * destinations must be disjoint row sets. */
+OMNI_API int omni_move_rows(void* const* bases, const int64_t* row_bytes, const int64_t* row_strides,
+                            int32_t num_tensors, const int32_t* src, const int32_t* dst, int32_t num_moves,
+                            void* stream);
+
+/* Admission of n streams planned by omni_sched_schedule (prepare_for_extend's
+ * req_to_token writes): stream i's req_to_token row slots[i] gets the slots of
+ * its first prompt_lens[i] tokens from its pages (page_indptr / pages, i32
+ * CSR), seq_lens[rows[i]] = prompt_lens[i], req_pool_indices[rows[i]] = slots[i].
+ * All arrays on the device.  status (nullable) becomes 2 on a stream whose
+ * pages cannot hold its prompt. */
+OMNI_API int omni_admit_streams(int64_t n, const int32_t* rows, const int32_t* slots, const int64_t* prompt_lens,
+                                const int32_t* page_indptr, const int32_t* pages, int32_t* req_to_token,
+                                int64_t max_ctx, int32_t page_size, int64_t* seq_lens, int64_t* req_pool_indices,
+                                int32_t* status, void* stream);
+
 /* ---------------------------------------------------------------------------
  * MoE block (a9): Qwen3OmniMoeTalkerSparseMoeBlock.forward (talker.py:325-351)
  * over Qwen3OmniMoeThinkerTextSparseMoeBlock (thinker_model.py:405-470) with

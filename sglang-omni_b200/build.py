@@ -1,6 +1,6 @@
 """Builds libomni_b200.so (sm_100a) in-tree with nvcc.
 
-Each csrc/*.cu compiles to an object under sglang-omni_b200/_build/ (in
+Each csrc/*.cu (and host-only csrc/*.cpp) compiles to an object under sglang-omni_b200/_build/ (in
 parallel, skipped when newer than its sources), then one shared library is
 linked into sglang-omni_b200/omni_b200/.  No torch dependency: the library
 links the static CUDA runtime and resolves driver entry points at run time.
@@ -65,7 +65,7 @@ def _compile(src: Path, extra: list[str]) -> Path:
 
 def build(verbose: bool = False, extra: list[str] | None = None) -> Path:
     BUILD.mkdir(exist_ok=True)
-    sources = sorted(CSRC.glob("*.cu"))
+    sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
     workers = max(1, min(len(sources), os.cpu_count() or 4))
     with concurrent.futures.ThreadPoolExecutor(workers) as pool:
         objs = list(pool.map(lambda s: _compile(s, extra or []), sources))

@@ -20,6 +20,8 @@
 // returns the pages the step opened to the free list (the allocator is a
 // stack, so restoring its head returns exactly those pages), lists their
 // slots, decrements seq_lens and clears req_to_token at the old position.
+#include <algorithm>
+
 #include "capi_util.h"
 #include "common.cuh"
 
@@ -288,6 +290,69 @@ __global__ void __launch_bounds__(kPackThreads) extend_prepare_kernel(const __gr
   }
 }
 
+// Row moves of the per-row state tensors (batch compaction): every move copies
+// row src to row dst of every tensor.  Sources and destinations are disjoint, so
+// the moves run in parallel: one CTA per (move, tensor).
+constexpr int kMoveThreads = 128;
+constexpr int kMaxMoveTensors = 24;
+constexpr int kMaxMovesPerLaunch = 384;
+
+struct MoveParams {
+  int num_tensors, num_moves;
+  uint8_t* base[kMaxMoveTensors];
+  int64_t row_bytes[kMaxMoveTensors];
+  int64_t stride[kMaxMoveTensors];
+  int32_t src[kMaxMovesPerLaunch];
+  int32_t dst[kMaxMovesPerLaunch];
+};
+
+__global__ void __launch_bounds__(kMoveThreads) move_rows_kernel(const __grid_constant__ MoveParams p) {
+  griddep_wait();
+  griddep_launch();
+  const int m = blockIdx.x, t = blockIdx.y;
+  const uint8_t* from = p.base[t] + (int64_t)p.src[m] * p.stride[t];
+  uint8_t* to = p.base[t] + (int64_t)p.dst[m] * p.stride[t];
+  const int64_t n = p.row_bytes[t];
+  const uintptr_t al = reinterpret_cast<uintptr_t>(from) | reinterpret_cast<uintptr_t>(to) | (uintptr_t)n;
+  if ((al & 15) == 0) {
+    for (int64_t i = threadIdx.x; i < n / 16; i += kMoveThreads)
+      reinterpret_cast<uint4*>(to)[i] = reinterpret_cast<const uint4*>(from)[i];
+  } else if ((al & 3) == 0) {
+    for (int64_t i = threadIdx.x; i < n / 4; i += kMoveThreads)
+      reinterpret_cast<uint32_t*>(to)[i] = reinterpret_cast<const uint32_t*>(from)[i];
+  } else {
+    for (int64_t i = threadIdx.x; i < n; i += kMoveThreads) to[i] = from[i];
+  }
+}
+
+// Admission of new streams: req_to_token rows from their page lists (token t of
+// stream i sits in slot pages[indptr[i] + t / P] * P + t % P), and the stream's
+// batch row gets seq_len = prompt_len and its request slot.  One CTA per stream.
+__global__ void __launch_bounds__(256) admit_streams_kernel(int n, const int32_t* rows, const int32_t* slots,
+                                                            const int64_t* prompt_lens, const int32_t* page_indptr,
+                                                            const int32_t* pages, int32_t* req_to_token,
+                                                            int64_t max_ctx, int page_size, int64_t* seq_lens,
+                                                            int64_t* req_pool_indices, int* status) {
+  griddep_wait();
+  griddep_launch();
+  const int i = blockIdx.x;
+  if (i >= n) return;
+  const int64_t L = prompt_lens[i];
+  const int64_t slot = slots[i];
+  const int p0 = page_indptr[i], p1 = page_indptr[i + 1];
+  if (L < 0 || L > max_ctx || (int64_t)(p1 - p0) * page_size < L) {
+    if (threadIdx.x == 0 && status) atomicExch(status, 2);
+    return;
+  }
+  int32_t* r2t = req_to_token + slot * max_ctx;
+  for (int64_t t = threadIdx.x; t < L; t += blockDim.x)
+    r2t[t] = pages[p0 + t / page_size] * page_size + (int32_t)(t % page_size);
+  if (threadIdx.x == 0) {
+    seq_lens[rows[i]] = L;
+    req_pool_indices[rows[i]] = slot;
+  }
+}
+
 }  // namespace
 }  // namespace omni
 
@@ -367,4 +432,48 @@ extern "C" OMNI_API int omni_extend_prepare(int64_t rows, const int64_t* prefix_
   p.status = status;
   return check_launch(
       launch(extend_prepare_kernel, dim3(1), dim3(kPackThreads), 0, static_cast<cudaStream_t>(stream), p));
+}
+
+extern "C" OMNI_API int omni_move_rows(void* const* bases, const int64_t* row_bytes, const int64_t* row_strides,
+                                       int32_t num_tensors, const int32_t* src, const int32_t* dst,
+                                       int32_t num_moves, void* stream) {
+  if (num_tensors < 0 || num_tensors > kMaxMoveTensors || num_moves < 0)
+    return set_error(OMNI_ERR_INVALID, "move_rows: at most 24 tensors");
+  if (num_moves == 0 || num_tensors == 0) return OMNI_OK;
+  if (!bases || !row_bytes || !row_strides || !src || !dst) return set_error(OMNI_ERR_INVALID, "move_rows: null array");
+  MoveParams p{};
+  p.num_tensors = num_tensors;
+  for (int t = 0; t < num_tensors; ++t) {
+    if (!bases[t] || row_bytes[t] < 0 || row_strides[t] < row_bytes[t])
+      return set_error(OMNI_ERR_INVALID, "move_rows: bad tensor descriptor");
+    p.base[t] = static_cast<uint8_t*>(bases[t]);
+    p.row_bytes[t] = row_bytes[t];
+    p.stride[t] = row_strides[t];
+  }
+  for (int m = 0; m < num_moves; ++m)
+    if (src[m] < 0 || dst[m] < 0) return set_error(OMNI_ERR_INVALID, "move_rows: negative row");
+  for (int m0 = 0; m0 < num_moves; m0 += kMaxMovesPerLaunch) {
+    const int k = std::min(kMaxMovesPerLaunch, num_moves - m0);
+    p.num_moves = k;
+    for (int m = 0; m < k; ++m) {
+      p.src[m] = src[m0 + m];
+      p.dst[m] = dst[m0 + m];
+    }
+    const int rc = check_launch(launch(move_rows_kernel, dim3(k, num_tensors), dim3(kMoveThreads), 0,
+                                       static_cast<cudaStream_t>(stream), p));
+    if (rc != OMNI_OK) return rc;
+  }
+  return OMNI_OK;
+}
+
+extern "C" OMNI_API int omni_admit_streams(int64_t n, const int32_t* rows, const int32_t* slots,
+                                           const int64_t* prompt_lens, const int32_t* page_indptr,
+                                           const int32_t* pages, int32_t* req_to_token, int64_t max_ctx,
+                                           int32_t page_size, int64_t* seq_lens, int64_t* req_pool_indices,
+                                           int32_t* status, void* stream) {
+  if (n < 0 || max_ctx <= 0 || page_size <= 0) return set_error(OMNI_ERR_INVALID, "bad admission arguments");
+  if (n == 0) return OMNI_OK;
+  return check_launch(launch(admit_streams_kernel, dim3((unsigned)n), dim3(256), 0,
+                             static_cast<cudaStream_t>(stream), (int)n, rows, slots, prompt_lens, page_indptr, pages,
+                             req_to_token, max_ctx, (int)page_size, seq_lens, req_pool_indices, status));
 }

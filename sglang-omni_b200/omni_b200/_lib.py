@@ -56,6 +56,20 @@ SIGNATURES: dict[str, list] = {
     "omni_predictor_attention": [_P, _I64, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _F32, _P, _I64, _P],
     "omni_decode_prepare": [_I64, _P, _P, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P],
     "omni_decode_rollback": [_I64, _P, _P, _P, _I64, _I32, _P, _P, _P, _P, _P],
+    "omni_move_rows": [_P, _P, _P, _I32, _P, _P, _I32, _P],
+    "omni_admit_streams": [_I64, _P, _P, _P, _P, _P, _P, _I64, _I32, _P, _P, _P, _P],
+    # host-only continuous-batching scheduler (include/omni_sched.h)
+    "omni_sched_create": [_P],
+    "omni_sched_destroy": [_P],
+    "omni_sched_add_request": [_P, _I64, _I64, _I64],
+    "omni_sched_abort": [_P, _I64],
+    "omni_sched_schedule": [_P, _I64, _P],
+    "omni_sched_commit": [_P, _P, _I64, _P, _P],
+    "omni_sched_rollback": [_P],
+    "omni_sched_stats": [_P, _P, _I32],
+    "omni_sched_row_rids": [_P, _P, _I64, _P],
+    "omni_sched_request_state": [_P, _I64, _P, _P, _P, _I64, _P],
+    "omni_sched_check": [_P],
     "omni_moe_rmsnorm_quant": [_P, _I64, _P, _I32, _I64, _P, _F32, _I64, _I32, _P, _I64, _P, _P, _P],
     "omni_moe_chunk_capacity": [_I64, _I32, _I32],
     "omni_moe_align_gather": [_P, _I64, _I32, _I32, _P, _P, _I32, _P, _P, _P, _P, _P, _I64, _P, _P],
@@ -83,6 +97,8 @@ _RESTYPES = {
     "omni_linear_workspace_bytes": ctypes.c_int64,
     "omni_paged_attention_workspace_bytes": ctypes.c_int64,
     "omni_moe_chunk_capacity": ctypes.c_int64,
+    "omni_sched_create": ctypes.c_void_p,
+    "omni_sched_destroy": None,
 }
 
 _lock = threading.Lock()
@@ -149,7 +165,7 @@ def check(rc: int, name: str) -> None:
 
 # Entry points that launch kernels (counted by launch_count()), one kernel each but
 # the paged decode attention (the attention and the merge of split rows).
-_LAUNCHERS = {n for n in SIGNATURES if not n.endswith("_bytes") and n not in (
+_LAUNCHERS = {n for n in SIGNATURES if not n.endswith("_bytes") and not n.startswith("omni_sched_") and n not in (
     "omni_version", "omni_last_error", "omni_device_status")}
 _KERNELS_PER_CALL = {"omni_paged_decode_attention": 2, "omni_paged_decode_attention_noalloc": 2}
 _launches = 0
