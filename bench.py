@@ -432,6 +432,138 @@ def run_vocoder(args) -> None:
                           "achieved_gbs": gbs, "peak_gbs": hbm, "frac": gbs / hbm, "peak_kind": kind}))
 
 
+def config4_trace(total: int, world: int, steady_per_gpu: int, frames_range: tuple[int, int], seed: int = 4242):
+    """Config 4's stream set: `total` streams with config-1/3 contexts as prompts
+    (lognormal(6, 0.8) clipped to [16, 8192]), frame counts U[frames_range], and
+    Poisson arrivals in step time at the rate that keeps `steady_per_gpu` streams live
+    per GPU (Little's law: rate = world x steady / mean frames).  Returns
+    [(rid, arrival_step, prompt_len, frames)]."""
+    rng = np.random.default_rng(seed)
+    prompts = np.clip(np.round(np.exp(rng.normal(6.0, 0.8, total))), 16, 8192).astype(int)
+    lo, hi = frames_range
+    frames = rng.integers(lo, hi + 1, total)
+    rate = world * steady_per_gpu / ((lo + hi) / 2.0)
+    out, rid, step = [], 0, 0
+    while rid < total:
+        for _ in range(int(rng.poisson(rate))):
+            if rid < total:
+                out.append((rid, step, int(prompts[rid]), int(frames[rid])))
+                rid += 1
+        step += 1
+    return out
+
+
+def run_config4(args, world: int, rank: int, local_rank: int, dist) -> None:
+    """Config 4: 2048 streams arriving by a Poisson process, sharded over the GPUs by
+    request (round-robin binding, no collective), each GPU running the continuous-
+    batching event loop (C++ scheduler: admission with the prefill-coalescing gate,
+    mixed decode + prefill steps, page allocation, compaction) over the MoE talker
+    of config 3 until every stream has all its frames.  The timed region is the whole
+    run, end to end through the public loop: text and prompt rows copied in from
+    pinned host memory, every step's codes copied out."""
+    import dataclasses
+
+    from omni_b200 import _lib
+    from omni_b200.config import CONFIG3_MOE
+    from omni_b200.continuous import ContinuousTalkerRunner
+    from omni_b200.model_runner import TalkerDecodeRunner
+    from omni_b200.replicas import shard_streams
+    from omni_b200.scheduler import MIXED, OmniScheduler, SchedulerConfig
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    frames_range = (64, 192)
+    cfg = dataclasses.replace(CONFIG3_MOE, max_context=8192 + frames_range[1])
+    max_batch, max_prefill = 320, 8192
+    trace = config4_trace(args.streams, world, 256, frames_range)
+    mine = set(shard_streams(args.streams, world, rank))
+    arrivals: dict[int, list] = {}
+    for rid, step, L, F in trace:
+        if rid in mine:
+            arrivals.setdefault(step, []).append((rid, L, F))
+    want_frames = sum(F for rid, _, _, F in trace if rid in mine)
+    num_pages = 32768
+    sc = SchedulerConfig(num_pages=num_pages, page_size=cfg.page_size, max_batch=max_batch,
+                         max_context=cfg.max_context, max_prefill_tokens=max_prefill,
+                         coalesce_requests=args.coalesce, coalesce_when_idle=False, coalesce_wait_us=40_000,
+                         reserve_ratio=1.0, page_seed=rank + 1)
+    runner = TalkerDecodeRunner(cfg, max_batch=max_batch + 1, num_pages=num_pages, seed=0, device=dev,
+                                max_prefill_tokens=max_prefill)
+    cr = ContinuousTalkerRunner(runner, OmniScheduler(sc), seed=rank)
+    cr.capture_buckets()  # warm-up: the decode graph of every bucket (start-up capture)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = _lib.launch_count()
+    step_s, rows_seen, mixed, idle = [], [], 0, 0
+    frames = 0
+    last = max(arrivals) if arrivals else 0
+    with ClockSampler(local_rank) as clocks:
+        e0.record(st)
+        t_start = time.perf_counter()
+        step = 0
+        while True:
+            for rid, L, F in arrivals.get(step, []):
+                cr.sched.add_request(rid, L, F)
+            t0 = time.perf_counter()
+            out = cr.step()
+            step += 1
+            if out is None:
+                idle += 1
+                if step > last and cr.sched.stats()["waiting"] == 0 and cr.sched.stats()["running"] == 0:
+                    break
+                continue
+            step_s.append(time.perf_counter() - t0)
+            rows_seen.append(len(out.rids))
+            frames += len(out.rids)
+            mixed += out.mode == MIXED
+        e1.record(st)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t_start
+    total_ms = e0.elapsed_time(e1)
+    launches = _lib.launch_count() - n0
+    st_sched = cr.sched.stats()
+    assert frames == want_frames and st_sched["finished"] == len(mine), "a stream did not get all its frames"
+    assert cr.device_status() == 0
+    steps = len(step_s)
+    h2d, d2h = cr.h2d_bytes, cr.d2h_bytes
+    from omni_b200.replicas import aggregate_step_times
+
+    total_ms_max, wall_ms_max, frames_all = aggregate_step_times(total_ms, wall * 1000.0, frames, dist, dev)
+    if rank == 0:
+        value = frames_all / (total_ms_max / 1000.0)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": 0,
+            "ms_per_step": total_ms / max(steps, 1), "p50_step_us": 1e6 * float(np.median(step_s)),
+            "p99_step_us": 1e6 * float(np.percentile(step_s, 99)), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"config4: {args.streams} streams (prompts lognormal(6,0.8) clip [16,8192], "
+                                   f"frames U[{frames_range[0]},{frames_range[1]}]) arriving by a seeded Poisson "
+                                   "process in step time at 256 live streams per GPU, sharded round-robin over the "
+                                   "GPUs; continuous batching (C++ scheduler, mixed decode + prefill steps, "
+                                   f"prefill-coalescing gate {args.coalesce} requests / 40 ms, decode graphs per "
+                                   "bucket) over the config-3 MoE talker + 31-codebook predictor, run to completion",
+                       "streams_rank0": len(mine), "parallelism": f"dp{world} replicas (no collective)",
+                       "warmup": "decode graphs of every bucket recorded before the timed region",
+                       "mixed_steps_rank0": mixed, "mean_rows_rank0": float(np.mean(rows_seen)),
+                       "graph_steps_rank0": cr.graph_steps, "eager_steps_rank0": cr.eager_steps,
+                       "retracted_rank0": st_sched["retracted"], "idle_iterations_rank0": idle,
+                       "l2": "inputs > L2 (MoE experts 3 GB + KV streamed per step)"},
+            "e2e": {"value": frames_all / (wall_ms_max / 1000.0), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d / max(steps, 1), "d2h_bytes_per_step": d2h / max(steps, 1),
+                    "note": "the timed loop is itself end to end (host scheduler, pinned copies in and out)"},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        cr.graphs.clear()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -446,9 +578,13 @@ def main() -> None:
                     help="with --config 3 under torchrun: experts sharded over the ranks (NCCL all-to-all)")
     ap.add_argument("--layers", type=int, default=0,
                     help="with --kernels: talker layers to build (0 = the config's 20); for small profiling runs")
-    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3],
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4],
                     help="1: dense talker, 64 streams (the headline); 2: mixed prefill (16 new streams, prompts "
-                         "U[64, 4096]) + 112 decode streams; 3: MoE talker with FP8 experts, 256 streams")
+                         "U[64, 4096]) + 112 decode streams; 3: MoE talker with FP8 experts, 256 streams; "
+                         "4: continuous batching of Poisson arrivals over the config-3 model")
+    ap.add_argument("--streams", type=int, default=2048, help="with --config 4: streams of the whole job")
+    ap.add_argument("--coalesce", type=int, default=8,
+                    help="with --config 4: prefill-coalescing gate (requests; <= 1 turns it off)")
     ap.add_argument("--vocoder", action="store_true",
                     help="time the streaming vocoder step's kernels (one JSON line each) and exit")
     args = ap.parse_args()
@@ -472,6 +608,10 @@ def main() -> None:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+
+    if args.config == 4:
+        run_config4(args, world, rank, local_rank, dist)
+        return
 
     from omni_b200 import _lib, ops
     from omni_b200.config import CONFIG1_DENSE, CONFIG3_MOE

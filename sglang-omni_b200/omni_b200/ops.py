@@ -403,6 +403,57 @@ def decode_rollback(
     )
 
 
+class RowTensors:
+    """Descriptor table of per-row state tensors (row = first dimension) for
+    move_rows; built once, the tensors stay at fixed addresses."""
+
+    def __init__(self, tensors: list[torch.Tensor]):
+        import ctypes
+
+        if len(tensors) > 24:
+            raise ValueError("move_rows takes at most 24 tensors")
+        for t in tensors:
+            if t.dim() < 1 or not t.is_contiguous():
+                raise ValueError("per-row state tensors must be contiguous with rows first")
+        self.tensors = list(tensors)
+        n = len(tensors)
+        self.bases = (ctypes.c_void_p * n)(*[t.data_ptr() for t in tensors])
+        self.row_bytes = (ctypes.c_int64 * n)(*[t[0].numel() * t.element_size() for t in tensors])
+        self.strides = (ctypes.c_int64 * n)(*[t.stride(0) * t.element_size() for t in tensors])
+        self.device = tensors[0].device
+
+
+def move_rows(table: RowTensors, src, dst) -> None:
+    """Row dst[m] of every tensor of the table becomes a copy of row src[m]
+    (batch compaction); src and dst are host int32 arrays of disjoint rows."""
+    import numpy as np
+
+    src = np.ascontiguousarray(src, dtype=np.int32)
+    dst = np.ascontiguousarray(dst, dtype=np.int32)
+    if src.shape != dst.shape:
+        raise ValueError("src and dst differ in length")
+    if src.size == 0:
+        return
+    rows = min(t.shape[0] for t in table.tensors)
+    if int(max(src.max(), dst.max())) >= rows or int(min(src.min(), dst.min())) < 0:
+        raise ValueError("row index outside the per-row tensors")
+    if set(src.tolist()) & set(dst.tolist()):
+        raise ValueError("move sources and destinations overlap")
+    _lib.call("omni_move_rows", table.bases, table.row_bytes, table.strides, len(table.tensors), src.ctypes.data,
+              dst.ctypes.data, src.shape[0], _lib.stream_of(table.device))
+
+
+def admit_streams(*, rows: torch.Tensor, slots: torch.Tensor, prompt_lens: torch.Tensor, page_indptr: torch.Tensor,
+                  pages: torch.Tensor, req_to_token: torch.Tensor, page_size: int, seq_lens: torch.Tensor,
+                  req_pool_indices: torch.Tensor, status: torch.Tensor | None = None) -> None:
+    """req_to_token rows of newly admitted streams from their page lists, and their
+    batch rows' seq_len and request slot (see include/omni_b200.h)."""
+    n = rows.shape[0]
+    _lib.call("omni_admit_streams", n, rows.data_ptr(), slots.data_ptr(), prompt_lens.data_ptr(),
+              page_indptr.data_ptr(), pages.data_ptr(), req_to_token.data_ptr(), req_to_token.shape[1], page_size,
+              seq_lens.data_ptr(), req_pool_indices.data_ptr(), _lib.ptr(status), _lib.stream_of(rows.device))
+
+
 def rope_cos_sin_cache(max_position: int, head_dim: int, theta: float, device) -> torch.Tensor:
     """fp32 [max_position, head_dim]: cos of the half-dim frequencies, then sin
     (sglang RotaryEmbedding._compute_cos_sin_cache: inv_freq = theta^(-2i/d))."""

@@ -145,7 +145,8 @@ class DenseTalker:
             self.moe = ExpertParallelMoE(cfg.moe, H, max_tokens=B, device=self.device)
             self.moe_local_w = [self.moe.local_weights(lw["moe"]) for lw in self.w["layers"]]
         elif cfg.moe is not None:
-            self.moe = MoEBlock(cfg.moe, H, max_batch=B, device=self.device)
+            # sized for a mixed step's rows (decode rows + prompt tokens)
+            self.moe = MoEBlock(cfg.moe, H, max_batch=R, device=self.device)
         self.codec_head_folded = ops.fold_norm(self.w["codec_head"], self.w["norm"])
         self.ss = torch.zeros(H // 128, R, dtype=torch.float32, device=self.device)
         self.ss_sel = torch.zeros(H // 128, B, dtype=torch.float32, device=self.device)
@@ -219,8 +220,13 @@ class DenseTalker:
         h, q, attn, act = self.h[:R], self.q[:R], self.attn[:R], self.act[:R]
         ss = self.ss
         parts = H // 128
+        if R > self.max_rows:
+            raise RuntimeError("mixed batch exceeds the talker's row capacity")
+        if self.moe is not None and self.moe_local_w is not None:
+            raise NotImplementedError("mixed prefill + decode with expert-parallel MoE")
         self.ensure_attention_workspace(fb.work_capacity)
-        ops.add_sumsq(feedback, text, h[:Bd], ss[0, :Bd])
+        if Bd > 0:
+            ops.add_sumsq(feedback, text, h[:Bd], ss[0, :Bd])
         ops.add_sumsq(prompt_embeds, None, h[Bd:R], ss[0, Bd:R])
         ss_parts = 1
         for li, lw in enumerate(self.w["layers"]):
@@ -230,20 +236,24 @@ class DenseTalker:
                                                     k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin,
                                                     positions=positions[:R], cache_loc=cache_loc[:R],
                                                     k_cache=kc, v_cache=vc))
-            ops.paged_decode_attention(q[:Bd], kc, vc, page_indptr=fb.page_indptr, page_indices=fb.page_indices,
-                                       seq_lens=fb.seq_lens, work_indptr=fb.work_indptr, num_q_heads=hq,
-                                       num_kv_heads=hkv, head_dim=D, page_size=cfg.page_size,
-                                       pages_per_chunk=fb.pages_per_chunk, work_capacity=fb.work_capacity,
-                                       sm_scale=self.scale, out=attn[:Bd], workspace=self.attn_workspace)
+            if Bd > 0:
+                ops.paged_decode_attention(q[:Bd], kc, vc, page_indptr=fb.page_indptr, page_indices=fb.page_indices,
+                                           seq_lens=fb.seq_lens, work_indptr=fb.work_indptr, num_q_heads=hq,
+                                           num_kv_heads=hkv, head_dim=D, page_size=cfg.page_size,
+                                           pages_per_chunk=fb.pages_per_chunk, work_capacity=fb.work_capacity,
+                                           sm_scale=self.scale, out=attn[:Bd], workspace=self.attn_workspace)
             ops.prefill_attention(q[Bd:R], kc, vc, qo_indptr=ext.qo_indptr, seq_lens=ext.seq_lens,
                                   page_indptr=ext.page_indptr, page_indices=ext.page_indices,
                                   tile_indptr=ext.tile_indptr, max_tiles=ext.max_tiles, num_q_heads=hq,
                                   num_kv_heads=hkv, head_dim=D, page_size=cfg.page_size, sm_scale=self.scale,
                                   out=attn[Bd:R])
             ops.linear_fused(attn, lw["o_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=ss)
-            ops.linear_fused(h, self.folded[li]["gate_up"], act, epilogue=ops.EPI_SWIGLU, ss_in=ss, ss_in_parts=parts,
-                             norm_eps=eps)
-            ops.linear_fused(act, lw["down_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=ss)
+            if "moe" in lw:
+                self.moe.forward(h, ss, parts, lw["post_attention_layernorm"], eps, lw["moe"])
+            else:
+                ops.linear_fused(h, self.folded[li]["gate_up"], act, epilogue=ops.EPI_SWIGLU, ss_in=ss,
+                                 ss_in_parts=parts, norm_eps=eps)
+                ops.linear_fused(act, lw["down_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=ss)
             ss_parts = parts
         n = select.shape[0]
         torch.index_select(h, 0, select, out=self.h_sel[:n])
