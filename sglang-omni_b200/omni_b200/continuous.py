@@ -96,7 +96,10 @@ class ContinuousTalkerRunner:
         self.pad_slot_h = torch.full((B,), self.dummy_slot, dtype=torch.long, **pin)
         # synthetic inputs on the host: the streams' text rows and prompt rows
         g = torch.Generator().manual_seed(seed + 101)
-        self.text_h = torch.randn(B, H, generator=g).to(torch.bfloat16).pin_memory()
+        # each stream's text rows (the thinker's chunk embeddings): a row of this pool
+        # chosen by the stream id, gathered into the step's staging rows
+        self.text_pool_h = torch.randn(4096, H, generator=g).to(torch.bfloat16)
+        self.text_h = torch.zeros(B, H, dtype=torch.bfloat16, **pin)
         P = max(prompt_pool_rows, sc.max_prefill_tokens + 4096)
         self.prompt_h = torch.randn(P, H, generator=g).to(torch.bfloat16).pin_memory()
         self.codes_h = torch.zeros(B, G, dtype=torch.long, **pin)
@@ -136,7 +139,6 @@ class ContinuousTalkerRunner:
                        do_sample=[sampling.subtalker_dosample] * B, batch=B)
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.graph_pool = None
-        self.row_rids: list[int] = []    # stream of each row, as the device has it
         self.eager_steps = 0
         self.graph_steps = 0
         self.h2d_bytes = 0
@@ -155,6 +157,12 @@ class ContinuousTalkerRunner:
     def _stream_seeds(self, rid: int) -> tuple[int, int]:
         base = derive_sampling_seed("omni-b200", self.seed, f"req{rid}")
         return derive_sampling_seed("semantic", base), derive_sampling_seed("subtalker", base)
+
+    def _stage_text(self, rids: list[int]) -> None:
+        n = len(rids)
+        if n:
+            idx = torch.tensor([rid % self.text_pool_h.shape[0] for rid in rids], dtype=torch.long)
+            torch.index_select(self.text_pool_h, 0, idx, out=self.text_h[:n])
 
     def _stage_pages(self, pages: np.ndarray) -> None:
         al = self.runner.allocator
@@ -301,6 +309,8 @@ class ContinuousTalkerRunner:
             return None
         self._stage_pages(plan.decode_pages)
         Bd = plan.decode_rows
+        rids = self.sched.row_rids()
+        self._stage_text(rids[:Bd])
         if plan.mode == MIXED:
             self._admit(plan)
             r.text_embeds[:Bd].copy_(self.text_h[:Bd], non_blocking=True)
@@ -318,7 +328,7 @@ class ContinuousTalkerRunner:
         self.codes_h[:rows].copy_(r.predictor.output_codes[:rows], non_blocking=True)
         self.d2h_bytes += rows * self.codes_h.shape[1] * 8
         torch.cuda.current_stream(self.device).synchronize()
-        rids = self.sched.row_rids()[:rows]
+        rids = rids[:rows]
         codes = self.codes_h[:rows].numpy().copy()
         finished = self.sched.process_batch_result(codes[:, 0])
         return StepOutput(plan.mode, rids, codes, finished)

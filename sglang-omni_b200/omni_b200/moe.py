@@ -63,6 +63,9 @@ def init_moe_weights(cfg: MoEConfig, hidden: int, *, generator: torch.Generator,
     }
 
 
+MAX_ALIGN_TOKENS = 4096  # omni_moe_align_gather's token limit
+
+
 class MoEBlock:
     """Fixed-address buffers for one talker's MoE layers (shared across layers)."""
 
@@ -77,6 +80,10 @@ class MoEBlock:
         dev = self.device
         bf = dict(device=dev, dtype=torch.bfloat16)
         self.max_batch = B
+        # the align/gather kernel takes at most MAX_ALIGN_TOKENS tokens: larger batches
+        # (the prompt rows of a mixed step) run through the block in chunks of rows
+        B = min(B, MAX_ALIGN_TOKENS)
+        self.chunk_rows = B
         self.rows_cap = B * k + 64  # the last 64-row activation box stays inside the buffer
         self.x = torch.zeros(B, H, **bf)
         self.xq = torch.zeros(B, H, dtype=torch.uint8, device=dev)
@@ -99,7 +106,17 @@ class MoEBlock:
     def forward(self, h: torch.Tensor, ss: torch.Tensor, ss_parts: int, gain: torch.Tensor, eps: float,
                 w: dict) -> None:
         """h [B, H] += MoE(RMSNorm(h)) in place; ss [H/128, B_cap] receives the new rows'
-        per-128-feature sums of squares.  ss holds h's sums of squares on entry."""
+        per-128-feature sums of squares.  ss holds h's sums of squares on entry.  Rows are
+        independent: more than chunk_rows rows go through in chunks."""
+        B = h.shape[0]
+        if B > self.max_batch:
+            raise RuntimeError("MoE block: more rows than its capacity")
+        for c in range(0, B, self.chunk_rows):
+            n = min(self.chunk_rows, B - c)
+            self._forward_rows(h[c:c + n], ss[:, c:c + n], ss_parts, gain, eps, w)
+
+    def _forward_rows(self, h: torch.Tensor, ss: torch.Tensor, ss_parts: int, gain: torch.Tensor, eps: float,
+                      w: dict) -> None:
         B = h.shape[0]
         x, xq, xs = self.x[:B], self.xq[:B], self.xs[:B]
         ids, tw = self.topk_ids[:B], self.topk_weights[:B]
