@@ -432,27 +432,6 @@ def run_vocoder(args) -> None:
                           "achieved_gbs": gbs, "peak_gbs": hbm, "frac": gbs / hbm, "peak_kind": kind}))
 
 
-def config4_trace(total: int, world: int, steady_per_gpu: int, frames_range: tuple[int, int], seed: int = 4242):
-    """Config 4's stream set: `total` streams with config-1/3 contexts as prompts
-    (lognormal(6, 0.8) clipped to [16, 8192]), frame counts U[frames_range], and
-    Poisson arrivals in step time at the rate that keeps `steady_per_gpu` streams live
-    per GPU (Little's law: rate = world x steady / mean frames).  Returns
-    [(rid, arrival_step, prompt_len, frames)]."""
-    rng = np.random.default_rng(seed)
-    prompts = np.clip(np.round(np.exp(rng.normal(6.0, 0.8, total))), 16, 8192).astype(int)
-    lo, hi = frames_range
-    frames = rng.integers(lo, hi + 1, total)
-    rate = world * steady_per_gpu / ((lo + hi) / 2.0)
-    out, rid, step = [], 0, 0
-    while rid < total:
-        for _ in range(int(rng.poisson(rate))):
-            if rid < total:
-                out.append((rid, step, int(prompts[rid]), int(frames[rid])))
-                rid += 1
-        step += 1
-    return out
-
-
 def run_config4(args, world: int, rank: int, local_rank: int, dist) -> None:
     """Config 4: 2048 streams arriving by a Poisson process, sharded over the GPUs by
     request (round-robin binding, no collective), each GPU running the continuous-
@@ -465,7 +444,7 @@ def run_config4(args, world: int, rank: int, local_rank: int, dist) -> None:
 
     from omni_b200 import _lib
     from omni_b200.config import CONFIG3_MOE
-    from omni_b200.continuous import ContinuousTalkerRunner
+    from omni_b200.continuous import ContinuousTalkerRunner, poisson_arrival_trace
     from omni_b200.model_runner import TalkerDecodeRunner
     from omni_b200.replicas import shard_streams
     from omni_b200.scheduler import MIXED, OmniScheduler, SchedulerConfig
@@ -475,7 +454,7 @@ def run_config4(args, world: int, rank: int, local_rank: int, dist) -> None:
     frames_range = (64, 192)
     cfg = dataclasses.replace(CONFIG3_MOE, max_context=8192 + frames_range[1])
     max_batch, max_prefill = 320, 8192
-    trace = config4_trace(args.streams, world, 256, frames_range)
+    trace = poisson_arrival_trace(args.streams, world, 256, frames_range)
     mine = set(shard_streams(args.streams, world, rank))
     arrivals: dict[int, list] = {}
     for rid, step, L, F in trace:

@@ -53,6 +53,29 @@ def decode_graph_buckets(max_bs: int) -> list[int]:
     return values
 
 
+def poisson_arrival_trace(total: int, world: int, steady_per_gpu: int, frames_range: tuple[int, int],
+                          seed: int = 4242):
+    """The config-4 stream set (synthetic, seeded): `total` streams with config-1/3
+    contexts as prompts (lognormal(6, 0.8) clipped to [16, 8192]), frame counts
+    U[frames_range], and
+    Poisson arrivals in step time at the rate that keeps `steady_per_gpu` streams live
+    per GPU (Little's law: rate = world x steady / mean frames).  Returns
+    [(rid, arrival_step, prompt_len, frames)]."""
+    rng = np.random.default_rng(seed)
+    prompts = np.clip(np.round(np.exp(rng.normal(6.0, 0.8, total))), 16, 8192).astype(int)
+    lo, hi = frames_range
+    frames = rng.integers(lo, hi + 1, total)
+    rate = world * steady_per_gpu / ((lo + hi) / 2.0)
+    out, rid, step = [], 0, 0
+    while rid < total:
+        for _ in range(int(rng.poisson(rate))):
+            if rid < total:
+                out.append((rid, step, int(prompts[rid]), int(frames[rid])))
+                rid += 1
+        step += 1
+    return out
+
+
 @dataclass
 class StepOutput:
     mode: int
