@@ -75,6 +75,8 @@ constexpr int kWarpStages = 3;                // pages in flight per warp
 constexpr int kCombStride = kD + 4;           // padded head stride of the combine area
 constexpr int kStageBytes = 2 * kPageBytes;   // K + V of one head's page: 8 KB
 constexpr int kMaxRowsInSmem = 512;
+constexpr int kCombSlot = kWarpStages - 1;    // the ring stage that holds a warp's combine partial
+static_assert((kGroup * kCombStride + 2 * kGroup) * 4 <= kStageBytes, "combine partial exceeds a ring stage");
 
 struct PagedAttnParams {
   const uint16_t* q;  // [B, Hq, D] row stride q_stride
@@ -110,7 +112,9 @@ OMNI_DEVINL int cta_of(int pos, int total, int ctas) {
 // per-warp ring).  Per page a warp computes S^T = K Q^T (16 tokens x the group's 8
 // query heads, mma.sync m16n8k16 with K as the A operand, so no padding rows), an online
 // base-2 softmax per head, and O^T += V^T P^T (V^T by transposed ldmatrix, P^T moved
-// into the B-operand layout by four shuffles).  The warps combine in shared memory; a
+// into the B-operand layout by four shuffles).  The warps combine in shared memory, each
+// warp's partial in the last stage of its ring, while the next piece's first pages
+// already stream into the other stages (no memory-latency bubble at row boundaries); a
 // piece that is the whole row stores it, otherwise the piece's (o, lse) goes to segment
 // c + b and paged_attention_merge_kernel (the next launch) merges the row's segments in
 // order (deterministic).
@@ -146,10 +150,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_ker
     else hi = mid - 1;
   }
   uint8_t* wring = smem + warp * (kWarpStages * kStageBytes);
-  // combine area over the rings: written once every warp is done with its pages
-  float* wo = reinterpret_cast<float*>(smem);                                           // [warp][8][kCombStride]
-  float* wm = wo + kAttnWarps * kGroup * kCombStride;                                   // [warp][8]
-  float* wl = wm + kAttnWarps * kGroup;                                                 // [warp][8]
+  // combine area of warp w: the last stage of its ring ([8][kCombStride] o, then m[8],
+  // l[8]); at a piece boundary the next piece's first pages already stream into the
+  // other stages while the warps combine
+  auto comb = [&](int w) { return reinterpret_cast<float*>(smem + (w * kWarpStages + kCombSlot) * kStageBytes); };
 
   // the next row piece of the range from row bb on: (b, r0, r1) with r0 < r1
   auto find_piece = [&](int bb, int& b, int& r0, int& r1) -> bool {
@@ -185,11 +189,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_ker
     nmine = npg > warp ? (npg - warp + kAttnWarps - 1) / kAttnWarps : 0;
     pid_lane = lane < nmine ? p.page_indices[r0 + warp + kAttnWarps * lane] : 0;
   };
-  auto issue_first = [&]() {
-    const int first = nmine < kWarpStages ? nmine : kWarpStages;
-    for (int i = 0; i < first; ++i) issue(i);
-  };
-
   int b, r0, r1;
   bool have = find_piece(lo, b, r0, r1);
   // The first piece's pages stream in before the wait, up to its row's last page: only
@@ -312,46 +311,55 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_ker
       if (i + kWarpStages < nmine) issue(i + kWarpStages);
     }
 
-    // ---- combine the warps ----
-    __syncthreads();  // every warp's pages are consumed: the rings become the combine area
-    if (g == 0) {
-      wm[warp * kGroup + 2 * t] = m0;
-      wm[warp * kGroup + 2 * t + 1] = m1;
-      wl[warp * kGroup + 2 * t] = l0;
-      wl[warp * kGroup + 2 * t + 1] = l1;
-    }
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      float* w0 = wo + (warp * kGroup + 2 * t) * kCombStride + 16 * mt + g;
-      float* w1 = w0 + kCombStride;
-      w0[0] = o[mt][0];
-      w1[0] = o[mt][1];
-      w0[8] = o[mt][2];
-      w1[8] = o[mt][3];
-    }
-    __syncthreads();
+    // ---- the next piece's first pages stream in during the combine ----
+    // (this warp's stages are all consumed; the combine slot is left out)
     const bool whole = r0 == rp0 && r1 == rp1;
     const int seg = c + b;
+    int nb = 0, nr0 = 0, nr1 = 0;
+    const bool nhave = find_piece(b + 1, nb, nr0, nr1);
+    if (nhave) {
+      piece_ids(nr0, nr1);
+      const int pre = nmine < kCombSlot ? nmine : kCombSlot;
+      for (int i = 0; i < pre; ++i) issue(i);
+    }
+    // ---- combine the warps ----
+    {
+      float* wo = comb(warp);
+      float* wm = wo + kGroup * kCombStride;
+      if (g == 0) {
+        wm[2 * t] = m0;
+        wm[2 * t + 1] = m1;
+        wm[kGroup + 2 * t] = l0;
+        wm[kGroup + 2 * t + 1] = l1;
+      }
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        float* w0 = wo + (2 * t) * kCombStride + 16 * mt + g;
+        float* w1 = w0 + kCombStride;
+        w0[0] = o[mt][0];
+        w1[0] = o[mt][1];
+        w0[8] = o[mt][2];
+        w1[8] = o[mt][3];
+      }
+    }
+    __syncthreads();
     const int hg = threadIdx.x >> 4;          // head within group
     const int d0 = (threadIdx.x & 15) * 8;    // 8 dims
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     float M = -INFINITY, L = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w * kGroup + hg]);
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, comb(w)[kGroup * kCombStride + hg]);
 #pragma unroll
     for (int w = 0; w < kAttnWarps; ++w) {
-      const float lw = wl[w * kGroup + hg];
+      const float* wo = comb(w);
+      const float lw = wo[kGroup * kCombStride + kGroup + hg];
       if (lw == 0.0f) continue;
-      const float sc = exp2f(wm[w * kGroup + hg] - M);
+      const float sc = exp2f(wo[kGroup * kCombStride + hg] - M);
       L += lw * sc;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += wo[(w * kGroup + hg) * kCombStride + d0 + e] * sc;
+      for (int e = 0; e < 8; ++e) acc[e] += wo[hg * kCombStride + d0 + e] * sc;
     }
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-    // the next piece's page ids load while this piece is stored
-    int nb = 0, nr0 = 0, nr1 = 0;
-    const bool nhave = find_piece(b + 1, nb, nr0, nr1);
-    if (nhave) piece_ids(nr0, nr1);
     if (whole) {
       uint16_t* dst = p.out + (int64_t)b * p.out_stride + (int64_t)(h * kGroup + hg) * kD + d0;
       *reinterpret_cast<uint4*>(dst) =
@@ -364,8 +372,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_ker
       if ((threadIdx.x & 15) == 0)
         p.part_lse[((int64_t)seg * p.hkv + h) * kGroup + hg] = L > 0.0f ? M + log2f(L) : -INFINITY;
     }
-    __syncthreads();  // the combine area (the rings) is free for the next piece
-    if (nhave) issue_first();
+    __syncthreads();  // the combine slots are free for the next piece
+    if (nhave)
+      for (int i = kCombSlot; i < (nmine < kWarpStages ? nmine : kWarpStages); ++i) issue(i);
     have = nhave;
     b = nb;
     r0 = nr0;
@@ -899,8 +908,8 @@ extern "C" OMNI_API int omni_predictor_attention(const void* q, int64_t q_stride
 //     the process exits;
 //   - all calls on a device share the array, so calls whose kernels overlap on
 //     the GPU (different streams without ordering) race on it; serialise them;
-//   - each call clears the merge counters (the part that must start at zero)
-//     with cudaMemsetAsync on the call's stream before its kernel.
+//   - the scratch also holds per-row counters that the current kernels do not
+//     use (the layout is shared with omni_paged_attention_workspace_bytes).
 // The first call on each device looks up the array's device address with
 // cudaGetSymbolAddress while that device is current and caches it; make that
 // first call before any stream capture on the device.
