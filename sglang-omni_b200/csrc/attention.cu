@@ -206,17 +206,24 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_ker
     const int first = nmine < kWarpStages ? nmine : kWarpStages;
     for (int i = early; i < first; ++i) issue(i);
   }
-  while (have) {
-    const int rp0 = pptr[b], rp1 = pptr[b + 1];
-    const int seq_len = (int)p.seq_lens[b];
-    // Q^T as the B operand: head g, dims 16 ks + 2t (+1) and + 8
-    uint32_t qb[8][2];
-    const uint16_t* qrow = p.q + (int64_t)b * p.q_stride + (int64_t)(h * kGroup + g) * kD;
+  // Q^T as the B operand: head g, dims 16 ks + 2t (+1) and + 8; the next piece's row
+  // is loaded at the piece boundary, during the combine
+  uint32_t qb[8][2];
+  auto load_q = [&](int row) {
+    const uint16_t* qrow = p.q + (int64_t)row * p.q_stride + (int64_t)(h * kGroup + g) * kD;
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       qb[ks][0] = *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 2 * t);
       qb[ks][1] = *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * t);
     }
+  };
+  int seq_len = 0;
+  if (have) {
+    load_q(b);
+    seq_len = (int)p.seq_lens[b];
+  }
+  while (have) {
+    const int rp0 = pptr[b], rp1 = pptr[b + 1];
     // O^T accumulators: m-tile mt holds dims 16 mt + g (+ 8) for heads 2t, 2t + 1
     float o[8][4];
 #pragma unroll
@@ -321,7 +328,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_ker
       piece_ids(nr0, nr1);
       const int pre = nmine < kCombSlot ? nmine : kCombSlot;
       for (int i = 0; i < pre; ++i) issue(i);
+      load_q(nb);
     }
+    const int seq_next = nhave ? (int)p.seq_lens[nb] : 0;
     // ---- combine the warps ----
     {
       float* wo = comb(warp);
@@ -376,6 +385,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_ker
     if (nhave)
       for (int i = kCombSlot; i < (nmine < kWarpStages ? nmine : kWarpStages); ++i) issue(i);
     have = nhave;
+    seq_len = seq_next;
     b = nb;
     r0 = nr0;
     r1 = nr1;
