@@ -465,7 +465,8 @@ def run_config4(args, world: int, rank: int, local_rank: int, dist) -> None:
     sc = SchedulerConfig(num_pages=num_pages, page_size=cfg.page_size, max_batch=max_batch,
                          max_context=cfg.max_context, max_prefill_tokens=max_prefill,
                          coalesce_requests=args.coalesce, coalesce_when_idle=False, coalesce_wait_us=40_000,
-                         reserve_ratio=1.0, page_seed=rank + 1)
+                         reserve_ratio=1.0, page_seed=rank + 1, emit_messages=True, codec_coalesce_frames=10,
+                         codec_coalesce_early_frames=10)
     runner = TalkerDecodeRunner(cfg, max_batch=max_batch + 1, num_pages=num_pages, seed=0, device=dev,
                                 max_prefill_tokens=max_prefill)
     cr = ContinuousTalkerRunner(runner, OmniScheduler(sc), seed=rank)
@@ -477,7 +478,7 @@ def run_config4(args, world: int, rank: int, local_rank: int, dist) -> None:
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n0 = _lib.launch_count()
     step_s, rows_seen, mixed, idle = [], [], 0, 0
-    frames = 0
+    frames = emitted = 0
     last = max(arrivals) if arrivals else 0
     with ClockSampler(local_rank) as clocks:
         e0.record(st)
@@ -494,9 +495,11 @@ def run_config4(args, world: int, rank: int, local_rank: int, dist) -> None:
                 if step > last and cr.sched.stats()["waiting"] == 0 and cr.sched.stats()["running"] == 0:
                     break
                 continue
+            msgs = cr.pop_messages()  # the code chunks handed to the vocoder stage
             step_s.append(time.perf_counter() - t0)
             rows_seen.append(len(out.rids))
             frames += len(out.rids)
+            emitted += sum(m[2].shape[0] for m in msgs)
             mixed += out.mode == MIXED
         e1.record(st)
         torch.cuda.synchronize()
@@ -505,6 +508,7 @@ def run_config4(args, world: int, rank: int, local_rank: int, dist) -> None:
     launches = _lib.launch_count() - n0
     st_sched = cr.sched.stats()
     assert frames == want_frames and st_sched["finished"] == len(mine), "a stream did not get all its frames"
+    assert emitted == want_frames, "a frame did not reach the vocoder queue"
     assert cr.device_status() == 0
     steps = len(step_s)
     h2d, d2h = cr.h2d_bytes, cr.d2h_bytes
@@ -523,7 +527,9 @@ def run_config4(args, world: int, rank: int, local_rank: int, dist) -> None:
                                    "process in step time at 256 live streams per GPU, sharded round-robin over the "
                                    "GPUs; continuous batching (C++ scheduler, mixed decode + prefill steps, "
                                    f"prefill-coalescing gate {args.coalesce} requests / 40 ms, decode graphs per "
-                                   "bucket) over the config-3 MoE talker + 31-codebook predictor, run to completion",
+                                   "bucket, frames to the vocoder queue in the talker's chunks: 10 single frames, "
+                                   "then 10 a chunk) over the config-3 MoE talker + 31-codebook predictor, run to "
+                                   "completion",
                        "streams_rank0": len(mine), "parallelism": f"dp{world} replicas (no collective)",
                        "warmup": "decode graphs of every bucket recorded before the timed region",
                        "mixed_steps_rank0": mixed, "mean_rows_rank0": float(np.mean(rows_seen)),

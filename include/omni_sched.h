@@ -52,6 +52,10 @@ typedef struct {
   int64_t eos_token;          /* layer-0 code that ends a stream, -1 = none          */
   uint64_t page_seed;         /* 0: pages handed out 1, 2, 3, ...; else a seeded     */
                               /* permutation (splitmix64 + Fisher-Yates)             */
+  int32_t emit_messages;      /* 1: committed frames go to the vocoder message queue */
+  int32_t codec_coalesce_frames;       /* <= 1: one message per frame             */
+  int32_t codec_coalesce_first_frames; /* size of the first coalesced chunk (0: same) */
+  int32_t codec_coalesce_early_frames; /* frames sent one by one before coalescing  */
 } omni_sched_config;
 
 typedef struct {
@@ -91,12 +95,22 @@ OMNI_API int omni_sched_abort(void* sched, int64_t rid);
 /* Plan the next step at host time now_us (the prefill gate's clock). */
 OMNI_API int omni_sched_schedule(void* sched, int64_t now_us, omni_sched_plan* plan);
 
-/* Close the planned step: layer0_codes [rows] are the step's layer-0 codes of
- * rows [0, decode_rows + new_rows) (rows must equal that count).  Streams that
- * reached max_frames or drew eos_token finish; their rids are written to
- * finished_rids (capacity max_batch), the count to num_finished. */
-OMNI_API int omni_sched_commit(void* sched, const int64_t* layer0_codes, int64_t rows, int64_t* finished_rids,
-                               int64_t* num_finished);
+/* Close the planned step: codes [rows, groups] are the step's frames of rows
+ * [0, decode_rows + new_rows) (rows must equal that count; column 0 is the layer-0
+ * code; groups = 1 passes layer-0 codes only).  Streams that reached max_frames or
+ * drew eos_token finish; their rids are written to finished_rids (capacity
+ * max_batch), the count to num_finished.  With emit_messages the frames enter the
+ * vocoder message queue (post_process_outputs / emit_code_chunks_and_feedback,
+ * qwen3_tts/model_runner.py:254-294, qwen3_omni/talker_model_runner.py:178-315). */
+OMNI_API int omni_sched_commit(void* sched, const int64_t* codes, int64_t rows, int32_t groups,
+                               int64_t* finished_rids, int64_t* num_finished);
+
+/* Pop the oldest vocoder message: stream rid, its frames first_frame ..
+ * first_frame + frames - 1 (1-based) as codes [frames, groups], final = 1 on the
+ * stream's last message.  frames = 0 when the queue is empty.  CAPACITY (nothing
+ * popped) when the message holds more than capacity codes. */
+OMNI_API int omni_sched_pop_message(void* sched, int64_t* rid, int64_t* first_frame, int32_t* frames,
+                                    int32_t* final, int64_t* codes, int64_t capacity);
 
 /* rollback_decode_prep_after_skip: undo a planned DECODE step that did not run
  * (its opened pages go back on the free stack, seq_len -= 1).  Row moves and
@@ -104,7 +118,8 @@ OMNI_API int omni_sched_commit(void* sched, const int64_t* layer0_codes, int64_t
 OMNI_API int omni_sched_rollback(void* sched);
 
 /* Counters: [waiting, running, free_pages, free_slots, steps, frames,
- * finished, retracted]; n <= 8 of them are written. */
+ * finished, retracted, queued messages, emitted frames]; n <= 10 of them are
+ * written. */
 OMNI_API int omni_sched_stats(void* sched, int64_t* out, int32_t n);
 
 /* rids of rows [0, B) (written to *rows); -1 marks a row freed since the

@@ -21,7 +21,10 @@ What it restates:
   page; pages come off a LIFO free stack in row order) and retract_decode's order
   (sort by (frames, -original prompt) descending, retract from the back);
 - rollback_decode_prep_after_skip, sglang_omni/models/qwen3_omni/
-  talker_scheduler.py:198-225 (opened pages back, seq_len - 1).
+  talker_scheduler.py:198-225 (opened pages back, seq_len - 1);
+- the vocoder emission of sglang_omni/models/qwen3_omni/talker_model_runner.py:
+  emit_code_chunks_and_feedback (:178-235), coalesce_threshold / flush_codec_rows
+  (:268-298) and on_request_finished (:300-315).
 Rows stay compact: the highest live rows fill the lowest holes.
 """
 
@@ -70,6 +73,9 @@ class _Stream:
     row: int = -1
     running: bool = False
     pages: list = field(default_factory=list)
+    frames_seen: int = 0
+    first_flush_done: bool = False
+    pending: list = field(default_factory=list)   # [(frame index, codes)]
 
 
 @dataclass
@@ -85,7 +91,8 @@ class OraclePlan:
 class OracleScheduler:
     def __init__(self, *, num_pages, page_size, max_batch, max_context, max_prefill_tokens, coalesce_requests=0,
                  coalesce_when_idle=False, coalesce_wait_us=0, prefill_decode_interval=0, reserve_ratio=1.0,
-                 eos_token=-1, page_seed=0):
+                 eos_token=-1, page_seed=0, emit_messages=False, codec_coalesce_frames=0,
+                 codec_coalesce_first_frames=0, codec_coalesce_early_frames=0):
         self.P = page_size
         self.num_pages = num_pages
         self.max_batch = max_batch
@@ -104,6 +111,11 @@ class OracleScheduler:
         self.rows: list[int] = []          # rid per row, -1 = hole
         self.interval_left = 0
         self.pending = None                # (mode, rows, opened rows, interval before)
+        self.emit_messages = emit_messages
+        self.coalesce = codec_coalesce_frames
+        self.first = codec_coalesce_first_frames
+        self.early = codec_coalesce_early_frames
+        self.messages: list = []           # (rid, first frame, [codes...], final)
 
     # ------------------------------------------------------------------
     def add_request(self, rid, prompt_len, max_frames):
@@ -239,6 +251,35 @@ class OracleScheduler:
             self.pending = (mode, len(self.rows), opened, interval_before)
         return OraclePlan(mode, B, moves, decode_pages, new, retracted)
 
+    def _flush(self, s, final=False):
+        if s.pending:
+            s.first_flush_done = True
+            self.messages.append((s.rid, s.pending[0][0], [c for _, c in s.pending], final))
+            s.pending = []
+
+    def _emit(self, s, frame, done):
+        idx = s.frames_done
+        if self.coalesce <= 1:
+            self.messages.append((s.rid, idx, [frame], done))
+            return
+        s.frames_seen += 1
+        if s.frames_seen <= self.early:
+            self.messages.append((s.rid, idx, [frame], done))
+            return
+        if self.early > 0:
+            ready = len(s.pending) >= self.coalesce
+        else:
+            threshold = self.first if (self.first > 0 and not s.first_flush_done) else self.coalesce
+            ready = len(s.pending) >= threshold
+        if ready:
+            self._flush(s)
+        s.pending.append((idx, frame))
+        if done:
+            last = s.pending.pop()
+            self._flush(s)
+            s.pending.append(last)
+            self._flush(s, final=True)
+
     def commit(self, codes):
         mode, n, _, _ = self.pending
         assert len(codes) == n
@@ -246,7 +287,11 @@ class OracleScheduler:
         for r in range(n):
             s = self.streams[self.rows[r]]
             s.frames_done += 1
-            if s.frames_done >= s.max_frames or (self.eos >= 0 and codes[r] == self.eos):
+            frame = list(codes[r]) if hasattr(codes[r], "__len__") else [codes[r]]
+            done = s.frames_done >= s.max_frames or (self.eos >= 0 and frame[0] == self.eos)
+            if self.emit_messages:
+                self._emit(s, frame, done)
+            if done:
                 finished.append(s.rid)
                 self.rows[r] = -1
                 self._release(s)

@@ -24,6 +24,13 @@
 //     opened and takes seq_len back by one.
 // Rows stay compact: after finishes, aborts and retractions the highest live
 // rows fill the lowest holes, and the plan lists those moves.
+// Committed frames go to the vocoder stage as messages, coalesced as the Qwen3-Omni
+// talker's emit_code_chunks_and_feedback does (models/qwen3_omni/
+// talker_model_runner.py:178-235, coalesce_threshold / flush_codec_rows :268-298,
+// on_request_finished :300-315): with coalescing off every frame is a message; with it
+// on, the first `early` frames go one by one, then frames are held and flushed in
+// chunks once `coalesce` (the first chunk: `first`) are pending, the newest frame always
+// held back; a finishing stream flushes its held frames and then its last frame alone.
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -52,6 +59,17 @@ struct Stream {
   int32_t row = -1;
   State state = kWaiting;
   std::vector<int32_t> pages;
+  // vocoder emission
+  int64_t frames_seen = 0;
+  bool first_flush_done = false;
+  int64_t pending_first = 0;         // frame index (1-based) of the first held frame
+  std::vector<int64_t> pending;      // held frames, groups codes each
+};
+
+struct Message {
+  int64_t rid, first_frame;
+  int32_t frames, final;
+  std::vector<int64_t> codes;
 };
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -261,16 +279,21 @@ class Scheduler {
     return OMNI_OK;
   }
 
-  int commit(const int64_t* codes, int64_t n, int64_t* finished, int64_t* num_finished) {
+  int commit(const int64_t* codes, int64_t n, int32_t groups, int64_t* finished, int64_t* num_finished) {
     if (committed_) return set_error(OMNI_ERR_INVALID, "no planned step to commit");
     if (n != last_rows_) return set_error(OMNI_ERR_INVALID, "commit rows differ from the planned step's rows");
+    if (groups < 1 || (cfg_.emit_messages && codes == nullptr))
+      return set_error(OMNI_ERR_INVALID, "commit needs codes (groups >= 1) when messages are emitted");
     int64_t nf = 0;
     for (int64_t r = 0; r < n; ++r) {
       Stream& s = streams_.at(rows_[(size_t)r]);
       s.frames_done += 1;
       ++frames_total_;
-      const bool eos = cfg_.eos_token >= 0 && codes != nullptr && codes[r] == cfg_.eos_token;
-      if (s.frames_done >= s.max_frames || eos) {
+      const int64_t* frame = codes != nullptr ? codes + r * groups : nullptr;
+      const bool eos = cfg_.eos_token >= 0 && frame != nullptr && frame[0] == cfg_.eos_token;
+      const bool done = s.frames_done >= s.max_frames || eos;
+      if (cfg_.emit_messages) emit(s, frame, groups, done);
+      if (done) {
         if (finished) finished[nf] = s.rid;
         ++nf;
         rows_[(size_t)r] = -1;
@@ -282,6 +305,21 @@ class Scheduler {
     if (num_finished) *num_finished = nf;
     ++steps_;
     committed_ = true;
+    return OMNI_OK;
+  }
+
+  int pop_message(int64_t* rid, int64_t* first_frame, int32_t* frames, int32_t* final, int64_t* codes,
+                  int64_t capacity) {
+    *frames = 0;
+    if (messages_.empty()) return OMNI_OK;
+    const Message& m = messages_.front();
+    if ((int64_t)m.codes.size() > capacity) return set_error(OMNI_ERR_CAPACITY, "message larger than the buffer");
+    *rid = m.rid;
+    *first_frame = m.first_frame;
+    *frames = m.frames;
+    *final = m.final;
+    std::copy(m.codes.begin(), m.codes.end(), codes);
+    messages_.pop_front();
     return OMNI_OK;
   }
 
@@ -302,9 +340,10 @@ class Scheduler {
 
   void stats(int64_t* out, int n) const {
     const int64_t live = (int64_t)std::count_if(rows_.begin(), rows_.end(), [](int64_t r) { return r >= 0; });
-    const int64_t v[8] = {(int64_t)waiting_.size(), live, (int64_t)free_pages_.size(),
-                          (int64_t)free_slots_.size(), steps_, frames_total_, finished_total_, retracted_total_};
-    for (int i = 0; i < n && i < 8; ++i) out[i] = v[i];
+    const int64_t v[10] = {(int64_t)waiting_.size(), live, (int64_t)free_pages_.size(),
+                           (int64_t)free_slots_.size(), steps_, frames_total_, finished_total_, retracted_total_,
+                           (int64_t)messages_.size(), frames_emitted_};
+    for (int i = 0; i < n && i < 10; ++i) out[i] = v[i];
   }
 
   int row_rids(int64_t* rids, int64_t cap, int64_t* n) const {
@@ -370,6 +409,50 @@ class Scheduler {
     return now_us - oldest >= cfg_.coalesce_wait_us;
   }
 
+  void push_message(const Stream& s, int64_t first, const int64_t* codes, int64_t n_codes, int32_t frames,
+                    bool final) {
+    Message m{s.rid, first, frames, final ? 1 : 0, std::vector<int64_t>(codes, codes + n_codes)};
+    messages_.push_back(std::move(m));
+    frames_emitted_ += frames;
+  }
+
+  void flush(Stream& s, int32_t groups, bool final) {
+    if (s.pending.empty()) return;
+    s.first_flush_done = true;
+    const int32_t k = (int32_t)(s.pending.size() / (size_t)groups);
+    push_message(s, s.pending_first, s.pending.data(), (int64_t)s.pending.size(), k, final);
+    s.pending.clear();
+  }
+
+  // One committed frame of stream s (frame index s.frames_done).
+  void emit(Stream& s, const int64_t* frame, int32_t groups, bool done) {
+    const int64_t idx = s.frames_done;
+    const int32_t coalesce = cfg_.codec_coalesce_frames;
+    if (coalesce <= 1) {
+      push_message(s, idx, frame, groups, 1, done);
+      return;
+    }
+    s.frames_seen += 1;
+    if (s.frames_seen <= cfg_.codec_coalesce_early_frames) {
+      push_message(s, idx, frame, groups, 1, done);
+      return;
+    }
+    const int64_t held = (int64_t)(s.pending.size() / (size_t)groups);
+    int64_t threshold = coalesce;
+    if (cfg_.codec_coalesce_early_frames <= 0 && cfg_.codec_coalesce_first_frames > 0 && !s.first_flush_done)
+      threshold = cfg_.codec_coalesce_first_frames;
+    if (held >= threshold) flush(s, groups, false);
+    if (s.pending.empty()) s.pending_first = idx;
+    s.pending.insert(s.pending.end(), frame, frame + groups);
+    if (done) {
+      // the held frames, then the last frame alone
+      std::vector<int64_t> last(s.pending.end() - groups, s.pending.end());
+      s.pending.resize(s.pending.size() - (size_t)groups);
+      flush(s, groups, false);
+      push_message(s, idx, last.data(), groups, 1, true);
+    }
+  }
+
   // The highest live rows fill the lowest holes.
   void compact() {
     size_t lo = 0, hi = rows_.size();
@@ -406,7 +489,8 @@ class Scheduler {
   int last_mode_ = OMNI_SCHED_IDLE;
   int64_t last_rows_ = 0;
   bool committed_ = true;
-  int64_t steps_ = 0, frames_total_ = 0, finished_total_ = 0, retracted_total_ = 0;
+  int64_t steps_ = 0, frames_total_ = 0, finished_total_ = 0, retracted_total_ = 0, frames_emitted_ = 0;
+  std::deque<Message> messages_;
 };
 
 Scheduler* as_sched(void* h) { return static_cast<Scheduler*>(h); }
@@ -420,7 +504,8 @@ using omni::set_error;
 extern "C" OMNI_API void* omni_sched_create(const omni_sched_config* c) {
   if (c == nullptr || c->num_pages < 2 || c->page_size <= 0 || c->max_batch <= 0 || c->max_context <= 0 ||
       c->max_prefill_tokens <= 0 || c->reserve_ratio < 0.0 || c->coalesce_wait_us < 0 ||
-      c->prefill_decode_interval < 0 || c->num_pages > INT32_MAX) {
+      c->prefill_decode_interval < 0 || c->num_pages > INT32_MAX || c->codec_coalesce_frames < 0 ||
+      c->codec_coalesce_first_frames < 0 || c->codec_coalesce_early_frames < 0) {
     set_error(OMNI_ERR_INVALID, "malformed scheduler config");
     return nullptr;
   }
@@ -446,10 +531,17 @@ extern "C" OMNI_API int omni_sched_schedule(void* sched, int64_t now_us, omni_sc
   return as_sched(sched)->schedule(now_us, plan);
 }
 
-extern "C" OMNI_API int omni_sched_commit(void* sched, const int64_t* layer0_codes, int64_t rows,
+extern "C" OMNI_API int omni_sched_commit(void* sched, const int64_t* codes, int64_t rows, int32_t groups,
                                           int64_t* finished_rids, int64_t* num_finished) {
   if (!sched) return set_error(OMNI_ERR_INVALID, "null scheduler");
-  return as_sched(sched)->commit(layer0_codes, rows, finished_rids, num_finished);
+  return as_sched(sched)->commit(codes, rows, groups, finished_rids, num_finished);
+}
+
+extern "C" OMNI_API int omni_sched_pop_message(void* sched, int64_t* rid, int64_t* first_frame, int32_t* frames,
+                                               int32_t* final, int64_t* codes, int64_t capacity) {
+  if (!sched || !rid || !first_frame || !frames || !final || (!codes && capacity > 0))
+    return set_error(OMNI_ERR_INVALID, "null scheduler or output");
+  return as_sched(sched)->pop_message(rid, first_frame, frames, final, codes, capacity);
 }
 
 extern "C" OMNI_API int omni_sched_rollback(void* sched) {

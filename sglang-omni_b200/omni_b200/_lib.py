@@ -64,7 +64,8 @@ SIGNATURES: dict[str, list] = {
     "omni_sched_add_request": [_P, _I64, _I64, _I64],
     "omni_sched_abort": [_P, _I64],
     "omni_sched_schedule": [_P, _I64, _P],
-    "omni_sched_commit": [_P, _P, _I64, _P, _P],
+    "omni_sched_commit": [_P, _P, _I64, _I32, _P, _P],
+    "omni_sched_pop_message": [_P, _P, _P, _P, _P, _P, _I64],
     "omni_sched_rollback": [_P],
     "omni_sched_stats": [_P, _P, _I32],
     "omni_sched_row_rids": [_P, _P, _I64, _P],

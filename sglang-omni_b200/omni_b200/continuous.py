@@ -18,9 +18,10 @@ Each iteration asks the C++ scheduler (omni_b200.scheduler) for a plan, then
      in, and runs the fused decode + prefill forward eagerly
      (custom_mixed_forward): the decode rows take a frame and every admitted
      stream its first frame;
-  3. copies the step's codes out and hands the layer-0 codes to
-     process_batch_result, which finishes streams (max_frames or the codec EOS)
-     and frees their pages.
+  3. copies the step's codes out and hands the frames to process_batch_result,
+     which finishes streams (max_frames or the codec EOS), frees their pages and,
+     with emit_messages, queues the frames for the vocoder stage in the talker's
+     coalesced chunks (pop_messages).
 Streams are independent rows: for one bucket size a stream's results do not
 depend on its row or on the other rows, which the GPU tests check by moving
 streams between rows.
@@ -353,8 +354,13 @@ class ContinuousTalkerRunner:
         torch.cuda.current_stream(self.device).synchronize()
         rids = rids[:rows]
         codes = self.codes_h[:rows].numpy().copy()
-        finished = self.sched.process_batch_result(codes[:, 0])
+        finished = self.sched.process_batch_result(codes)
         return StepOutput(plan.mode, rids, codes, finished)
+
+    def pop_messages(self) -> list[tuple[int, int, np.ndarray, bool]]:
+        """The code chunks ready for the vocoder stage (scheduler emit_messages on):
+        (rid, first frame, codes [frames, G], final), in emission order."""
+        return self.sched.pop_messages(self.runner.cfg.predictor.num_code_groups)
 
     def device_status(self) -> int:
         """The packing kernels' sticky status (0 = no page shortfall or bad length)."""

@@ -43,6 +43,10 @@ class _Config(ctypes.Structure):
         ("reserve_ratio", ctypes.c_double),
         ("eos_token", ctypes.c_int64),
         ("page_seed", ctypes.c_uint64),
+        ("emit_messages", ctypes.c_int32),
+        ("codec_coalesce_frames", ctypes.c_int32),
+        ("codec_coalesce_first_frames", ctypes.c_int32),
+        ("codec_coalesce_early_frames", ctypes.c_int32),
     ]
 
 
@@ -85,12 +89,19 @@ class SchedulerConfig:
     reserve_ratio: float = 1.0
     eos_token: int = -1
     page_seed: int = 0
+    # vocoder messages (the talker runner's codec_coalesce_* arguments,
+    # qwen3_omni/talker_model_runner.py:70-72)
+    emit_messages: bool = False
+    codec_coalesce_frames: int = 0
+    codec_coalesce_first_frames: int = 0
+    codec_coalesce_early_frames: int = 0
 
     def to_c(self) -> _Config:
         return _Config(self.num_pages, self.page_size, self.max_batch, self.max_context, self.max_prefill_tokens,
                        self.coalesce_requests, int(self.coalesce_when_idle), self.coalesce_wait_us,
                        self.prefill_decode_interval, 0, float(self.reserve_ratio), self.eos_token,
-                       self.page_seed & 0xFFFFFFFFFFFFFFFF)
+                       self.page_seed & 0xFFFFFFFFFFFFFFFF, int(self.emit_messages), self.codec_coalesce_frames,
+                       self.codec_coalesce_first_frames, self.codec_coalesce_early_frames)
 
 
 @dataclass
@@ -146,6 +157,7 @@ class OmniScheduler:
         for k, a in self._bufs.items():
             setattr(self._plan, k, a.ctypes.data)
         self._finished = np.zeros(B, np.int64)
+        self._msg_buf: np.ndarray | None = None
         self._t0 = time.perf_counter()
 
     def close(self) -> None:
@@ -185,22 +197,48 @@ class OmniScheduler:
             new_pages=b["new_pages"][: int(b["new_page_indptr"][n]) if n else 0].copy(),
             retracted=b["retracted_rid"][: p.num_retracted].copy(), new_tokens=int(p.new_tokens))
 
-    def process_batch_result(self, layer0_codes) -> list[int]:
-        """Close the step with the layer-0 codes of its rows; returns the finished rids."""
-        codes = np.ascontiguousarray(np.asarray(layer0_codes, dtype=np.int64).reshape(-1))
+    def process_batch_result(self, codes) -> list[int]:
+        """Close the step with its rows' codes: [rows] layer-0 codes or [rows, G] whole
+        frames (column 0 = layer 0; frames feed the vocoder messages); returns the
+        finished rids."""
+        c = np.asarray(codes, dtype=np.int64)
+        if c.ndim == 1:
+            c = c.reshape(-1, 1)
+        c = np.ascontiguousarray(c)
         nf = ctypes.c_int64(0)
-        self._call("omni_sched_commit", codes.ctypes.data, codes.shape[0], self._finished.ctypes.data,
+        self._call("omni_sched_commit", c.ctypes.data, c.shape[0], c.shape[1], self._finished.ctypes.data,
                    ctypes.byref(nf))
         return self._finished[: nf.value].tolist()
+
+    def pop_messages(self, groups: int) -> list[tuple[int, int, np.ndarray, bool]]:
+        """Drain the vocoder message queue: (rid, first frame, codes [frames, groups], final)."""
+        out = []
+        rid, first, frames, final = ctypes.c_int64(0), ctypes.c_int64(0), ctypes.c_int32(0), ctypes.c_int32(0)
+        buf = self._msg_buf
+        if buf is None or buf.shape[0] < 64 * groups:
+            buf = self._msg_buf = np.zeros(64 * groups, np.int64)
+        while True:
+            rc = self._lib.omni_sched_pop_message(self._h, ctypes.byref(rid), ctypes.byref(first),
+                                                  ctypes.byref(frames), ctypes.byref(final), buf.ctypes.data,
+                                                  buf.shape[0])
+            if rc == _lib.OMNI_ERR_CAPACITY:
+                buf = self._msg_buf = np.zeros(buf.shape[0] * 4, np.int64)
+                continue
+            _lib.check(rc, "omni_sched_pop_message")
+            if frames.value == 0:
+                return out
+            n = frames.value
+            out.append((rid.value, first.value, buf[: n * groups].reshape(n, groups).copy(), bool(final.value)))
 
     def rollback_decode_prep_after_skip(self) -> None:
         self._call("omni_sched_rollback")
 
     # ------------------------------------------------------------------
     def stats(self) -> dict:
-        out = np.zeros(8, np.int64)
-        self._call("omni_sched_stats", out.ctypes.data, 8)
-        keys = ("waiting", "running", "free_pages", "free_slots", "steps", "frames", "finished", "retracted")
+        out = np.zeros(10, np.int64)
+        self._call("omni_sched_stats", out.ctypes.data, 10)
+        keys = ("waiting", "running", "free_pages", "free_slots", "steps", "frames", "finished", "retracted",
+                "messages", "frames_emitted")
         return dict(zip(keys, (int(v) for v in out)))
 
     def row_rids(self) -> list[int]:

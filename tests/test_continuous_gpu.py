@@ -24,7 +24,7 @@ DEV = "cuda"
 
 
 def build(*, max_batch=16, layers=2, num_pages=256, max_prefill=512, use_graphs=True, seed=0, eos=-1, moe=False,
-          reserve_ratio=1.0, coalesce=0):
+          reserve_ratio=1.0, coalesce=0, emit=False):
     from omni_b200.config import MoEConfig, PredictorConfig, SamplingParams, TalkerConfig
     from omni_b200.continuous import ContinuousTalkerRunner
     from omni_b200.model_runner import TalkerDecodeRunner
@@ -37,7 +37,8 @@ def build(*, max_batch=16, layers=2, num_pages=256, max_prefill=512, use_graphs=
         cfg = TalkerConfig(num_hidden_layers=layers, max_context=1024)
     sc = SchedulerConfig(num_pages=num_pages, page_size=cfg.page_size, max_batch=max_batch, max_context=1024,
                          max_prefill_tokens=max_prefill, reserve_ratio=reserve_ratio, eos_token=eos,
-                         page_seed=seed + 3, coalesce_requests=coalesce)
+                         page_seed=seed + 3, coalesce_requests=coalesce, emit_messages=emit,
+                         codec_coalesce_frames=10 if emit else 0, codec_coalesce_early_frames=4 if emit else 0)
     runner = TalkerDecodeRunner(cfg, max_batch=max_batch + 1, num_pages=num_pages, seed=seed,
                                 max_prefill_tokens=max_prefill)
     return ContinuousTalkerRunner(runner, OmniScheduler(sc), sampling=SamplingParams(), seed=seed,
@@ -141,11 +142,19 @@ def poisson_trace(seed, streams, lam, max_prompt=120, frames=(2, 12)):
 
 
 def test_continuous_trace_runs_every_stream_to_its_end():
-    cr = build(max_batch=12, num_pages=96, max_prefill=400)
+    cr = build(max_batch=12, num_pages=96, max_prefill=400, emit=True)
     arrivals = poisson_trace(0, streams=30, lam=1.5)
     want = {rid: F for v in arrivals.values() for rid, _, F in v}
     frames = run_to_end(cr, arrivals, check_state=True)
     assert {rid: len(f) for rid, f in frames.items()} == want
+    # the vocoder messages carry every stream's frames, in order, the last one final
+    msgs: dict[int, list] = {}
+    for rid, first, codes, final in cr.pop_messages():
+        msgs.setdefault(rid, []).append((first, codes, final))
+    for rid, f in frames.items():
+        got = msgs[rid]
+        np.testing.assert_array_equal(np.concatenate([c for _, c, _ in got]), np.stack(f))
+        assert [fin for _, _, fin in got] == [False] * (len(got) - 1) + [True]
     G = cr.runner.cfg.predictor.num_code_groups
     for f in frames.values():
         c = np.stack(f)

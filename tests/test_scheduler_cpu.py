@@ -357,3 +357,126 @@ def test_plan_arrays_are_numpy():
     s.add_request(1, 3, 2)
     p = s.get_next_batch_to_run(0)
     assert isinstance(p.new_pages, np.ndarray) and p.new_pages.dtype == np.int32
+
+
+# ---------------------------------------------------------------------------
+# vocoder messages: the reference's codec-coalescing cases
+# (tests/unit_test/qwen3_omni/test_talker_codec_coalesce.py), restated on the C++
+# scheduler, plus random traces against the restatement
+# ---------------------------------------------------------------------------
+
+def emitter(n, frames, **kw):
+    """n streams of `frames` frames each, all admitted in the first step."""
+    cfg = dict(num_pages=256, page_size=4, max_batch=max(n, 2), max_context=512, max_prefill_tokens=64,
+               emit_messages=True)
+    cfg.update(kw)
+    s = OmniScheduler(SchedulerConfig(**cfg))
+    for r in range(n):
+        s.add_request(r, 3, frames)
+    return s
+
+
+def step_frames(s, step):
+    """One step; frame `step` of stream r is [r * 1000 + step, r + 100 + step]."""
+    p = s.get_next_batch_to_run(0)
+    rids = s.row_rids()[: p.rows]
+    codes = np.array([[r * 1000 + step, r + 100 + step] for r in rids], np.int64)
+    s.process_batch_result(codes)
+    return {r: codes[i] for i, r in enumerate(rids)}
+
+
+def test_messages_one_per_frame_when_coalescing_is_off():
+    s = emitter(2, 5)
+    for k in range(1, 6):
+        step_frames(s, k)
+    msgs = s.pop_messages(2)
+    assert len(msgs) == 10 and all(m[2].shape == (1, 2) for m in msgs)
+    assert [m[3] for m in msgs if m[0] == 0] == [False] * 4 + [True]
+
+
+def test_messages_coalesce_after_threshold_with_newest_held():
+    s = emitter(2, 100, codec_coalesce_frames=3)
+    seen = [step_frames(s, k) for k in range(1, 4)]
+    assert s.pop_messages(2) == []
+    seen.append(step_frames(s, 4))
+    msgs = s.pop_messages(2)
+    assert len(msgs) == 2
+    m0 = next(m for m in msgs if m[0] == 0)
+    assert m0[1] == 1 and m0[2].shape == (3, 2)
+    np.testing.assert_array_equal(m0[2], np.stack([f[0] for f in seen[:3]]))
+
+
+@pytest.mark.parametrize("steps", [1, 2, 3, 4])
+def test_finish_sends_the_last_frame_alone(steps):
+    s = emitter(1, steps, codec_coalesce_frames=3)
+    seen = [step_frames(s, k)[0] for k in range(1, steps + 1)]
+    msgs = s.pop_messages(2)
+    np.testing.assert_array_equal(msgs[-1][2], seen[-1][None])
+    assert msgs[-1][3] and not any(m[3] for m in msgs[:-1])
+    np.testing.assert_array_equal(np.concatenate([m[2] for m in msgs]), np.stack(seen))
+    # coalesce 3: [1..3] flushed when frame 4 arrives, so 4 steps give [1-3], [4]
+    assert len(msgs) == {1: 1, 2: 2, 3: 2, 4: 2}[steps]
+
+
+def test_first_flush_uses_the_smaller_threshold():
+    n, k, first = 2, 5, 2
+    s = emitter(n, 100, codec_coalesce_frames=k, codec_coalesce_first_frames=first)
+    for i in range(1, first + 2):
+        step_frames(s, i)
+    msgs = s.pop_messages(2)
+    assert len(msgs) == n and all(m[2].shape[0] == first for m in msgs)
+    for i in range(first + 2, first + 2 + k - 1):
+        step_frames(s, i)
+    assert s.pop_messages(2) == []
+    step_frames(s, first + 1 + k)
+    msgs = s.pop_messages(2)
+    assert len(msgs) == n and all(m[2].shape[0] == k for m in msgs)
+
+
+def test_early_frames_keep_the_vocoder_window_cadence():
+    s = emitter(1, 200, codec_coalesce_frames=10, codec_coalesce_early_frames=12)
+    ready_at, received = {}, 0
+    for step in range(1, 42):
+        step_frames(s, step)
+        received += sum(m[2].shape[0] for m in s.pop_messages(2))
+        for end in (2, 12, 22, 32):
+            if received >= end:
+                ready_at.setdefault(end, step)
+    assert ready_at == {2: 2, 12: 12, 22: 23, 32: 33}
+
+
+@pytest.mark.parametrize("early", [10, 12])
+@pytest.mark.parametrize("steps", [9, 10, 11, 12, 13, 20, 21, 22, 23])
+def test_early_frames_then_coalesced_tail_in_order(early, steps):
+    s = emitter(1, steps, codec_coalesce_frames=10, codec_coalesce_early_frames=early)
+    seen = [step_frames(s, k)[0] for k in range(1, steps + 1)]
+    msgs = s.pop_messages(2)
+    assert all(m[2].shape[0] == 1 for m in msgs[:early])
+    np.testing.assert_array_equal(np.concatenate([m[2] for m in msgs]), np.stack(seen))
+    assert [m[1] for m in msgs] == list(np.cumsum([1] + [m[2].shape[0] for m in msgs[:-1]]))
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_random_trace_messages_match_the_restatement(seed):
+    rng = random.Random(100 + seed)
+    kw = dict(num_pages=64, page_size=4, max_batch=6, max_context=256, max_prefill_tokens=48,
+              reserve_ratio=rng.choice([0.0, 1.0]), eos_token=rng.choice([-1, 2]), emit_messages=True,
+              codec_coalesce_frames=rng.choice([0, 1, 3, 5]), codec_coalesce_first_frames=rng.choice([0, 2]),
+              codec_coalesce_early_frames=rng.choice([0, 2, 4]))
+    s, o = make(**kw)
+    rid = 0
+    for step in range(200):
+        if rng.random() < 0.4:
+            L, F = rng.randint(1, 30), rng.randint(1, 25)
+            o.add_request(rid, L, F)
+            s.add_request(rid, L, F)
+            rid += 1
+        p, q = s.get_next_batch_to_run(step), o.schedule(step)
+        same_plan(p, q)
+        if p.is_idle():
+            continue
+        codes = [[rng.randint(0, 4), rng.randint(0, 99), rng.randint(0, 99)] for _ in range(p.rows)]
+        assert sorted(s.process_batch_result(codes)) == sorted(o.commit(codes))
+    got = [(r, f, c.tolist(), fin) for r, f, c, fin in s.pop_messages(3)]
+    assert got == o.messages
+    assert s.stats()["frames_emitted"] == sum(len(m[2]) for m in o.messages)
