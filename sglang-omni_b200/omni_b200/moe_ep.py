@@ -14,7 +14,8 @@ routes its own tokens with the replicated router.  Per layer:
             formed in bf16
   combine   the partial rows return by a second all-to-all; each token sums its
             partials in rank order, then adds the gated shared expert (computed
-            locally) and the residual, as the single-GPU combine does
+            locally, on a side stream that runs while the two all-to-alls and the
+            local experts run) and the residual, as the single-GPU combine does
 
 Fixed-size blocks keep every collective's split sizes constant, so no host
 synchronisation sits inside the layer.  The routed sum is rounded once per rank
@@ -102,6 +103,7 @@ class ExpertParallelMoE:
         self.row_bytes = packed_row_bytes(hidden, k)
         # tokens of this rank: norm, codes, routing, shared expert (single-GPU block buffers)
         self.local = MoEBlock(cfg, hidden, max_batch=max_tokens, device=dev)
+        self.side = torch.cuda.Stream(dev)  # the shared expert, overlapped with the all-to-alls
         self.send = torch.zeros(W * self.cap + 1, self.row_bytes, dtype=torch.uint8, device=dev)
         self.recv = torch.zeros(W * self.cap, self.row_bytes, dtype=torch.uint8, device=dev)
         n_recv = W * self.cap
@@ -139,6 +141,13 @@ class ExpertParallelMoE:
         ops.moe_rmsnorm_quant(h, ss, ss_parts, gain, eps, x, xq, xs)
         ops.linear_fused(x, w_local["gate"], m.router_logits[:T], epilogue=ops.EPI_ROUTER,
                          router={"topk_ids": ids, "topk_weights": tw})
+        # the gated shared expert runs on a side stream while the routed tokens go out,
+        # through the local experts and back: the two all-to-alls overlap it
+        main = torch.cuda.current_stream(h.device)
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            ops.linear_fused(x, w_local["shared_gate_up"], m.shared_act[:T], epilogue=ops.EPI_SWIGLU)
+            ops.linear_fused(m.shared_act[:T], w_local["shared_down"], m.shared_out[:T], epilogue=ops.EPI_STORE)
         has, pos, flat, local_ids = dispatch_plan(ids, W, self.e_local, cap)
         pack_rows(self.send, H, k, xq, xs, local_ids, tw, flat)
         self.dist.all_to_all_single(self.recv, self.send[: W * cap], group=self.group)
@@ -156,7 +165,6 @@ class ExpertParallelMoE:
                          self.y)
         ops.moe_partial_sum(self.y, self.slot_of, w_view, rb // 4, self.ret_send)
         self.dist.all_to_all_single(self.ret_recv, self.ret_send, group=self.group)
-        ops.linear_fused(x, w_local["shared_gate_up"], m.shared_act[:T], epilogue=ops.EPI_SWIGLU)
-        ops.linear_fused(m.shared_act[:T], w_local["shared_down"], m.shared_out[:T], epilogue=ops.EPI_STORE)
+        main.wait_stream(self.side)
         ops.moe_combine_parts(self.ret_recv, part_index(has, pos, cap), x, w_local["shared_expert_gate"],
                               m.shared_out[:T], h, ss)

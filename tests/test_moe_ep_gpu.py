@@ -1,6 +1,6 @@
-"""Expert-parallel MoE block on 2 GPUs (NCCL all-to-all over NVLink) against the
-single-GPU block on the same tokens: bf16 tolerance (cosine >= 0.999, max-abs <=
-2e-2 x scale).  Skipped with fewer than two GPUs."""
+"""Expert-parallel MoE block (NCCL all-to-all over NVLink) against the single-GPU
+block on the same tokens: bf16 tolerance (cosine >= 0.999, max-abs <= 2e-2 x scale).
+One rank on one GPU, and two ranks where two GPUs are present."""
 
 from __future__ import annotations
 
@@ -69,11 +69,14 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_moe_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("world", [1, 2])
+def test_ep_moe_matches_single_gpu(tmp_path, world):
+    """world 1 runs the same block (one NCCL rank, local all-to-alls, the shared expert
+    on its side stream) on one GPU; world 2 needs two."""
     import torch.multiprocessing as mp
 
-    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
     for r in range(world):
         cos, err, scale, cos_d, same_route = np.load(tmp_path / f"ep{r}.npy")
