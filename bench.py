@@ -172,6 +172,17 @@ def run_reference_arm(args, rank: int) -> None:
         return
     steps = max(1, min(args.steps, 5))
     warmup = 1
+    if args.config == 0:
+        cb = cpu_predictor_rate(steps)
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
+            "steps": steps, "warmup": warmup, "ms_per_step": 8000.0 / cb["value"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config0: code predictor alone, 8 streams, 15 codebooks"},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+            flush=True)
+        return
     rate, desc, times = cpu_step_rate(steps, warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
@@ -432,6 +443,153 @@ def run_vocoder(args) -> None:
                           "achieved_gbs": gbs, "peak_gbs": hbm, "frac": gbs / hbm, "peak_kind": kind}))
 
 
+def run_config0(args, world: int, rank: int, local_rank: int, dist) -> None:
+    """Config 0 (the reference's CPU-runnable case) on the GPU: the code predictor alone
+    for 8 streams (5 layers, 15 residual codebooks of 2048, T 0.9 / top-k 50 / top-p 0.8,
+    talker hidden ~ N(0, 1)), one frame a step, graph-replayed; the CPU leg times the
+    oracle restatement of the same predictor loop."""
+    from omni_b200 import _lib, ops
+    from omni_b200.config import CONFIG0_PREDICTOR
+    from omni_b200.predictor import CodePredictor, init_predictor_weights
+    from omni_b200.seed import derive_sampling_seed
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    pc, B = CONFIG0_PREDICTOR, 8
+    H, G, V0 = pc.hidden_size, pc.num_code_groups, 3072
+    pw = init_predictor_weights(pc, seed=1, device=dev)
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    emb0 = (torch.randn(V0, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    p = CodePredictor(pc, pw, max_batch=B, device=dev, layer0_embedding=emb0)
+    seeds = [derive_sampling_seed("subtalker", derive_sampling_seed("omni-b200", rank, f"req{i}")) for i in range(B)]
+    p.set_sampling(temperature=[0.9] * B, top_k=[50] * B, top_p=[0.8] * B, seeds=seeds, do_sample=[True] * B,
+                   batch=B)
+    c0 = torch.randint(0, V0, (B,), generator=g, device=dev)
+    hidden = torch.randn(B, H, generator=g, device=dev).to(torch.bfloat16)
+    norm = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    ss = hidden.float().view(B, H // 128, 128).pow(2).sum(-1).t().contiguous()
+    positions = torch.arange(B, device=dev) * 7
+
+    def step():
+        p.code_predictor_forward(c0, hidden, positions, final_norm=norm, final_ss=ss, final_eps=pc.rms_norm_eps)
+
+    step()
+    torch.cuda.synchronize()
+    n0 = _lib.launch_count()
+    s_ = torch.cuda.Stream(dev)
+    s_.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s_):
+        step()
+    torch.cuda.current_stream(dev).wait_stream(s_)
+    launches_per_step = _lib.launch_count() - n0
+    W, K = max(3, args.warmup), args.steps
+    for _ in range(W):
+        graph.replay()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)]
+    with ClockSampler(local_rank) as clocks:
+        ev[0].record(st)
+        for i in range(K):
+            graph.replay()
+            ev[i + 1].record(st)
+        torch.cuda.synchronize()
+    step_ms = [ev[i].elapsed_time(ev[i + 1]) for i in range(K)]
+    total_ms = ev[0].elapsed_time(ev[K])
+    # end to end: the inputs in from pinned host memory, the codes out, every step
+    c0_h = c0.cpu().pin_memory()
+    hid_h = hidden.cpu().pin_memory()
+    codes_h = torch.empty(B, G, dtype=torch.long).pin_memory()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(st)
+    for _ in range(K):
+        c0.copy_(c0_h, non_blocking=True)
+        hidden.copy_(hid_h, non_blocking=True)
+        graph.replay()
+        codes_h.copy_(p.output_codes[:B], non_blocking=True)
+        st.synchronize()
+    t1.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = t0.elapsed_time(t1)
+    # the dominant kernel: the predictor gate_up GEMM (+ folded norm, SwiGLU) over the 5 layers in turn
+    cyc = {"i": 0}
+    eps = pc.rms_norm_eps
+
+    def gate_up():
+        li = cyc["i"] % pc.num_hidden_layers
+        cyc["i"] += 1
+        ops.linear_fused(p.h[:B], p.folded[li]["gate_up"], p.act[:B], epilogue=ops.EPI_SWIGLU, ss_in=p.ss,
+                         ss_in_parts=H // 128, norm_eps=eps)
+
+    gu_s = time_kernel(gate_up, 60)
+    wgu = p.folded[0]["gate_up"]
+    gu_bytes = wgu.numel() * 2 + B * H * 2 + B * pc.intermediate_size * 2
+    params = sum(v.numel() for lw in pw["layers"] for k, v in lw.items() if k.endswith("proj"))
+    step_bytes = (G - 1) * (params + pc.vocab_size * H) * 2
+    from omni_b200.replicas import aggregate_step_times
+
+    total_max, e2e_max, frames = aggregate_step_times(total_ms, e2e_ms, float(B * K), dist, dev)
+    if rank == 0:
+        hbm, _, peak_kind = measured_peaks()
+        achieved = gu_bytes / gu_s / 1e9
+        line = {
+            "metric": METRIC, "value": frames / (total_max / 1000.0), "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": total_ms / K, "p50_step_us": 1000 * float(np.median(step_ms)),
+            "p99_step_us": 1000 * float(np.percentile(step_ms, 99)), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config0: code predictor alone, 8 streams (5 layers, H 1024, 16q/8kv hd 64, "
+                                   "SwiGLU 3072, 15 residual codebooks of 2048, T 0.9 / top-k 50 / top-p 0.8, "
+                                   "talker hidden N(0,1)), one frame a step",
+                       "streams_per_gpu": B, "parallelism": f"dp{world} replicas (no collective)",
+                       "step_bytes": step_bytes,
+                       "step_bandwidth_gbs": step_bytes / (total_ms / K / 1000.0) / 1e9,
+                       "l2": "weights 126 MB of predictor layers + 63 MB of lm_heads cycle each step (> L2)"},
+            "e2e": {"value": frames / (e2e_max / 1000.0), "unit": UNIT, "h2d_bytes_per_step": B * 8 + B * H * 2,
+                    "d2h_bytes_per_step": B * G * 8},
+            "gpu_launches": launches_per_step * K,
+            "roofline": {"bound": "hbm", "kernel": "gemm_kernel<2>: predictor gate_up + folded norm + SwiGLU "
+                                                   "(8 rows)",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                         "algorithmic_bytes": gu_bytes, "launch_us": gu_s * 1e6, "peak_kind": peak_kind},
+            "clocks": clocks.summary(),
+        }
+        if not args.no_cpu:
+            line["cpu_baseline"] = cpu_predictor_rate(args.cpu_steps)
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_predictor_rate(steps: int) -> dict:
+    """The oracle restatement of config 0's predictor loop (8 streams, fp32) on the host cores."""
+    from oracle.model import OracleTalker  # test infrastructure: the CPU baseline
+    from omni_b200.config import CONFIG0_PREDICTOR, TalkerConfig
+    from omni_b200.predictor import init_predictor_weights
+    from omni_b200.talker import init_talker_weights
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = TalkerConfig(num_hidden_layers=1, predictor=CONFIG0_PREDICTOR)
+    o = OracleTalker(cfg, init_talker_weights(cfg, seed=0, device="cpu"),
+                     init_predictor_weights(CONFIG0_PREDICTOR, seed=1, device="cpu"))
+    B = 8
+    g = torch.Generator().manual_seed(3)
+    c0 = torch.randint(0, cfg.vocab_size, (B,), generator=g)
+    hid = torch.randn(B, cfg.hidden_size, generator=g).bfloat16().float()
+    sub = dict(temperature=np.full(B, 0.9, np.float32), top_k=np.full(B, 50), top_p=np.full(B, 0.8, np.float32),
+               seed=np.arange(B) + 100, do_sample=np.ones(B, np.uint8), max_top_k=50, has_top_p=True)
+    times = []
+    for it in range(steps + 1):
+        t0 = time.perf_counter()
+        o.code_predictor(c0, hid, torch.arange(B) * 7, sub)
+        if it:
+            times.append(time.perf_counter() - t0)
+    return {"value": B * len(times) / sum(times), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(times)} config-0 predictor steps (8 streams, 15 codebooks) of the CPU restatement, "
+                      f"fp32 on {torch.get_num_threads()} threads, after 1 warm-up step"}
+
+
 def run_config4(args, world: int, rank: int, local_rank: int, dist) -> None:
     """Config 4: 2048 streams arriving by a Poisson process, sharded over the GPUs by
     request (round-robin binding, no collective), each GPU running the continuous-
@@ -563,8 +721,9 @@ def main() -> None:
                     help="with --config 3 under torchrun: experts sharded over the ranks (NCCL all-to-all)")
     ap.add_argument("--layers", type=int, default=0,
                     help="with --kernels: talker layers to build (0 = the config's 20); for small profiling runs")
-    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4],
-                    help="1: dense talker, 64 streams (the headline); 2: mixed prefill (16 new streams, prompts "
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4],
+                    help="0: the code predictor alone, 8 streams; "
+                         "1: dense talker, 64 streams (the headline); 2: mixed prefill (16 new streams, prompts "
                          "U[64, 4096]) + 112 decode streams; 3: MoE talker with FP8 experts, 256 streams; "
                          "4: continuous batching of Poisson arrivals over the config-3 model")
     ap.add_argument("--streams", type=int, default=2048, help="with --config 4: streams of the whole job")
@@ -596,6 +755,9 @@ def main() -> None:
 
     if args.config == 4:
         run_config4(args, world, rank, local_rank, dist)
+        return
+    if args.config == 0:
+        run_config0(args, world, rank, local_rank, dist)
         return
 
     from omni_b200 import _lib, ops
