@@ -71,6 +71,12 @@ SIGNATURES: dict[str, list] = {
     "omni_sched_row_rids": [_P, _P, _I64, _P],
     "omni_sched_request_state": [_P, _I64, _P, _P, _P, _I64, _P],
     "omni_sched_check": [_P],
+    # host-only codec-frame relay (include/omni_relay.h)
+    "omni_relay_open": [ctypes.c_char_p, _I64, _I32],
+    "omni_relay_close": [_P, _I32],
+    "omni_relay_push": [_P, _I64, _I64, _I32, _I32, _I32, _P],
+    "omni_relay_pop": [_P, _P, _P, _P, _P, _P, _P, _I64],
+    "omni_relay_stats": [_P, _P, _I32],
     "omni_moe_rmsnorm_quant": [_P, _I64, _P, _I32, _I64, _P, _F32, _I64, _I32, _P, _I64, _P, _P, _P],
     "omni_moe_chunk_capacity": [_I64, _I32, _I32],
     "omni_moe_align_gather": [_P, _I64, _I32, _I32, _P, _P, _I32, _P, _P, _P, _P, _P, _I64, _P, _P],
@@ -100,6 +106,8 @@ _RESTYPES = {
     "omni_moe_chunk_capacity": ctypes.c_int64,
     "omni_sched_create": ctypes.c_void_p,
     "omni_sched_destroy": None,
+    "omni_relay_open": ctypes.c_void_p,
+    "omni_relay_close": None,
 }
 
 _lock = threading.Lock()
@@ -166,8 +174,9 @@ def check(rc: int, name: str) -> None:
 
 # Entry points that launch kernels (counted by launch_count()), one kernel each but
 # the paged decode attention (the attention and the merge of split rows).
-_LAUNCHERS = {n for n in SIGNATURES if not n.endswith("_bytes") and not n.startswith("omni_sched_") and n not in (
-    "omni_version", "omni_last_error", "omni_device_status")}
+_HOST_ONLY = ("omni_version", "omni_last_error", "omni_device_status")
+_LAUNCHERS = {n for n in SIGNATURES
+              if not n.endswith("_bytes") and not n.startswith(("omni_sched_", "omni_relay_")) and n not in _HOST_ONLY}
 _KERNELS_PER_CALL = {"omni_paged_decode_attention": 2, "omni_paged_decode_attention_noalloc": 2}
 _launches = 0
 

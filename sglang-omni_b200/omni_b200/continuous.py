@@ -357,6 +357,18 @@ class ContinuousTalkerRunner:
         finished = self.sched.process_batch_result(codes)
         return StepOutput(plan.mode, rids, codes, finished)
 
+    def forward_messages(self, relay, backlog: list | None = None) -> list:
+        """Hand the ready code chunks to the vocoder stage through a CodecRelay
+        (omni_b200.relay), oldest first; what does not fit in the ring stays in the
+        returned backlog for the next call (the talker never blocks on the vocoder)."""
+        backlog = list(backlog or []) + self.pop_messages()
+        sent = 0
+        for m in backlog:
+            if not relay.push(*m):
+                break
+            sent += 1
+        return backlog[sent:]
+
     def pop_messages(self) -> list[tuple[int, int, np.ndarray, bool]]:
         """The code chunks ready for the vocoder stage (scheduler emit_messages on):
         (rid, first frame, codes [frames, G], final), in emission order."""

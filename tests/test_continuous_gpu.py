@@ -147,10 +147,28 @@ def test_continuous_trace_runs_every_stream_to_its_end():
     want = {rid: F for v in arrivals.values() for rid, _, F in v}
     frames = run_to_end(cr, arrivals, check_state=True)
     assert {rid: len(f) for rid, f in frames.items()} == want
-    # the vocoder messages carry every stream's frames, in order, the last one final
+    # the vocoder messages, through the shared-memory relay, carry every stream's
+    # frames in order, the last one final
+    import os
+    import uuid
+
+    from omni_b200.relay import CodecRelay
+
+    name = f"/omni_relay_gpu_{os.getpid()}_{uuid.uuid4().hex[:6]}"
+    tx, rx = CodecRelay(name, create=True), CodecRelay(name, create=False)
     msgs: dict[int, list] = {}
-    for rid, first, codes, final in cr.pop_messages():
-        msgs.setdefault(rid, []).append((first, codes, final))
+    backlog: list = []
+    try:
+        while True:
+            backlog = cr.forward_messages(tx, backlog)
+            while (m := rx.pop()) is not None:
+                rid, first, codes, final = m
+                msgs.setdefault(rid, []).append((first, codes, final))
+            if not backlog:
+                break
+    finally:
+        rx.close()
+        tx.close()
     for rid, f in frames.items():
         got = msgs[rid]
         np.testing.assert_array_equal(np.concatenate([c for _, c, _ in got]), np.stack(f))
