@@ -95,7 +95,17 @@ struct PagedAttnParams {
   int* counters;     // [B][Hkv]
 };
 
-// First page of CTA c's range: pages [bound(c), bound(c + 1)) of the flattened list.
+// The flattened page list is cut in a virtual space where every row is preceded by
+// w units (the fixed cost of a row piece: its queries, the warps' combine and the
+// store), so that CTAs whose ranges hold many short rows get fewer pages: row b's
+// pages sit at virtual positions [pptr[b] + (b + 1) w, pptr[b + 1] + (b + 1) w).
+// w = kRowWeight once the batch has more pages than ranges; with fewer, every range is
+// one page (w = 0) and a row's split does not depend on the other rows.
+#ifndef OMNI_ATTN_ROW_WEIGHT
+#define OMNI_ATTN_ROW_WEIGHT 4
+#endif
+constexpr int kRowWeight = OMNI_ATTN_ROW_WEIGHT;
+// First virtual position of CTA c's range: [bound(c), bound(c + 1)).
 OMNI_DEVINL int range_bound(int c, int total, int ctas) { return (int)(((int64_t)total * c) / ctas); }
 // CTA whose range holds flattened page `pos` (ranges are non-empty: ctas <= total).
 OMNI_DEVINL int cta_of(int pos, int total, int ctas) {
@@ -135,19 +145,21 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_ker
   __syncthreads();
   const int* pptr = ptr_in_smem ? s_ptr : p.page_indptr;
   const int total = pptr[p.rows];
-  // at most one CTA per page, so that every range is non-empty
+  // at most one CTA per page (ctas <= total <= the virtual length): every range is non-empty
   const int ctas = min(p.ctas, total);
   if (c >= ctas) {
     griddep_wait();
     griddep_launch();
     return;
   }
-  const int a0 = range_bound(c, total, ctas), a1 = range_bound(c + 1, total, ctas);
-  int lo = 0, hi = p.rows - 1;  // first row of the range: last b with page_indptr[b] <= a0
+  const int rw = total > p.ctas ? kRowWeight : 0;
+  const int tv = total + p.rows * rw;  // virtual length
+  const int a0 = range_bound(c, tv, ctas), a1 = range_bound(c + 1, tv, ctas);
+  int lo = 0, hi = p.rows - 1;  // first row of the range: first b whose virtual end passes a0
   while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (pptr[mid] <= a0) lo = mid;
-    else hi = mid - 1;
+    const int mid = (lo + hi) >> 1;
+    if (pptr[mid + 1] + (mid + 1) * rw > a0) hi = mid;
+    else lo = mid + 1;
   }
   uint8_t* wring = smem + warp * (kWarpStages * kStageBytes);
   // combine area of warp w: the last stage of its ring ([8][kCombStride] o, then m[8],
@@ -157,9 +169,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) paged_decode_attention_ker
 
   // the next row piece of the range from row bb on: (b, r0, r1) with r0 < r1
   auto find_piece = [&](int bb, int& b, int& r0, int& r1) -> bool {
-    for (b = bb; b < p.rows && pptr[b] < a1; ++b) {
-      r0 = max(a0, pptr[b]);
-      r1 = min(a1, pptr[b + 1]);
+    for (b = bb; b < p.rows && pptr[b] + (b + 1) * rw < a1; ++b) {
+      const int off = (b + 1) * rw;  // virtual - page position in row b
+      r0 = max(a0 - off, pptr[b]);
+      r1 = min(a1 - off, pptr[b + 1]);
       if (r0 < r1) return true;
     }
     return false;
@@ -404,7 +417,9 @@ __global__ void __launch_bounds__(kGroup * 16) paged_attention_merge_kernel(cons
   griddep_launch();
   if (rp0 >= rp1) return;
   const int ctas = min(p.ctas, total);
-  const int c_lo = cta_of(rp0, total, ctas), c_hi = cta_of(rp1 - 1, total, ctas);
+  const int rw = total > p.ctas ? kRowWeight : 0;
+  const int tv = total + p.rows * rw, off = (b + 1) * rw;
+  const int c_lo = cta_of(rp0 + off, tv, ctas), c_hi = cta_of(rp1 - 1 + off, tv, ctas);
   const int nseg = c_hi - c_lo + 1;
   if (nseg == 1) return;
   const int hg = threadIdx.x >> 4;        // head within group
