@@ -468,14 +468,17 @@ OMNI_API int omni_extend_prepare(int64_t rows, const int64_t* prefix_lens, const
 
 /* Causal extend attention (RadixAttention extend, thinker_model.py:373-379) over
  * the paged pool: the extend rows of stream s are q[qo_indptr[s] ..
- * qo_indptr[s+1]) and query j sees keys [0, prefix + j] of the stream's pages;
- * out has the rows of q.  Grid of max_tiles x Hq CTAs (tiles of 64 queries; the
- * tiles past tile_indptr[streams] exit).  head_dim 128, page 16. */
-OMNI_API int omni_prefill_attention(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
-                                   const int32_t* qo_indptr, const int64_t* seq_lens, const int32_t* page_indptr,
-                                   const int32_t* page_indices, const int32_t* tile_indptr, int64_t streams,
-                                   int64_t max_tiles, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-                                   int32_t page_size, float sm_scale, void* out, int64_t out_stride, void* stream);
+ * qo_indptr[s+1]) (q_rows rows in all) and query j sees keys [0, prefix + j] of the
+ * stream's pages; out has the rows of q.  Grid of max_tiles x Hq CTAs (tiles of 128
+ * queries, tile_indptr from omni_extend_prepare with q_tile 128; the tiles past
+ * tile_indptr[streams] exit).  head_dim 128, page 16; k_cache / v_cache hold
+ * num_slots slots.  tcgen05 tensor cores: S and O accumulate in tensor memory. */
+OMNI_API int omni_prefill_attention(const void* q, int64_t q_stride, int64_t q_rows, const void* k_cache,
+                                   const void* v_cache, int64_t num_slots, const int32_t* qo_indptr,
+                                   const int64_t* seq_lens, const int32_t* page_indptr, const int32_t* page_indices,
+                                   const int32_t* tile_indptr, int64_t streams, int64_t max_tiles,
+                                   int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                                   float sm_scale, void* out, int64_t out_stride, void* stream);
 
 /* ======================================================================== */
 /* Streaming vocoder (code2wav) step                                        */

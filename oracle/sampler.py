@@ -182,7 +182,7 @@ def decode_rollback(seq_lens, req_pool_indices, req_to_token, page_size, out_cac
     return sl, r2t, freed[:n]
 
 
-def extend_prepare(prefix_lens, extend_lens, req_pool_indices, req_to_token, page_size, q_tile=64):
+def extend_prepare(prefix_lens, extend_lens, req_pool_indices, req_to_token, page_size, q_tile=128):
     """Returns (seq_lens, qo_indptr, out_cache_loc, positions, page_indptr, page_indices, tile_indptr)."""
     pre = _c(prefix_lens, np.int64)
     ext = _c(extend_lens, np.int64)

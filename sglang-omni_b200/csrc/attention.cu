@@ -1,25 +1,16 @@
 // Attention kernels of the decode step.
 //
 // paged_decode_attention_kernel — GQA decode over the paged KV pool (L1:
-//   RadixAttention decode, thinker_model.py:373-379).  One work item is
-//   (request row, chunk of up to `pages_per_chunk` pages) x one KV head; the
-//   work list is built once per step by the packing kernel and shared by every
-//   layer.  The 4 warps of a CTA take the item's pages in turn; each warp
-//   streams whole pages (16 tokens x head_dim, K and V) with 16-byte cp.async
-//   into a swizzled double buffer and runs
-//   S = Q K^T and O += P V on mma.sync m16n8k16 (the 8 query heads of the
-//   group in the M tile), with an online base-2 softmax.  Warps combine in
-//   shared memory; chunks of one row are merged by the last CTA of the row to
-//   finish (deterministic order, no spinning).
+//   RadixAttention decode, thinker_model.py:373-379).  The batch's flattened page
+//   list is cut into equal ranges (row pieces weighted by their fixed cost), two
+//   CTAs per SM over the KV heads; the 4 warps of a CTA take a piece's pages in
+//   turn, each streaming whole pages (16 tokens x head_dim, K and V) with 16-byte
+//   cp.async into a swizzled ring, and run S = K Q^T and O^T += V^T P^T on mma.sync
+//   m16n8k16 (the group's 8 query heads), with an online base-2 softmax.  Warps
+//   combine in shared memory; rows spread over several ranges are merged by
+//   paged_attention_merge_kernel in segment order (deterministic).
 //
-// prefill_attention_kernel — causal attention of an extend batch (the talker's
-//   prefill, RadixAttention extend, thinker_model.py:373-379) over the paged
-//   pool that the qkv epilogue has just written: CTA = 64 query rows of one
-//   stream x one query head; key tiles of 64 (4 pages) stream through a
-//   cp.async double buffer; per warp 16 query rows, S = Q K^T and O += P V on
-//   mma.sync m16n8k16 with the online base-2 softmax (P stays in registers as
-//   the A operand of P V); query j of a stream with prefix p sees keys
-//   [0, p + j].
+// The causal extend (prefill) attention is in prefill_attention.cu.
 //
 // predictor_attention_kernel — the code predictor's attention over its <= G+1
 //   per-request cache slots (predictor_cached_self_attention,
@@ -466,216 +457,6 @@ __global__ void __launch_bounds__(kGroup * 16) paged_attention_merge_kernel(cons
                  pack_bf2(sum[4] * iw, sum[5] * iw), pack_bf2(sum[6] * iw, sum[7] * iw));
 }
 
-// ---------------------------------------------------------------------------
-// Prefill (extend) attention
-// ---------------------------------------------------------------------------
-constexpr int kPfWarps = 4;
-constexpr int kPfRows = 16 * kPfWarps;  // query rows per CTA
-constexpr int kPfKeys = 64;             // keys per tile (4 pages)
-constexpr int kPfTileBytes = kPfKeys * kD * 2;  // 16 KB
-
-struct PrefillParams {
-  const uint16_t* q;  // [extend rows, Hq, D]
-  int64_t q_stride;
-  const uint16_t* k_cache;
-  const uint16_t* v_cache;
-  const int32_t* qo_indptr;    // [streams + 1]
-  const int64_t* seq_lens;     // [streams] prefix + extend
-  const int32_t* page_indptr;  // [streams + 1]
-  const int32_t* page_indices;
-  const int32_t* tile_indptr;  // [streams + 1] query tiles of 64
-  int streams, hq, hkv;
-  float scale_log2;
-  uint16_t* out;
-  int64_t out_stride;
-};
-
-__global__ void __launch_bounds__(kPfWarps * 32) prefill_attention_kernel(const __grid_constant__ PrefillParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* qbuf = smem;                           // [64][256 B]
-  uint8_t* kvbuf = smem + kPfRows * kD * 2;       // [stage][K | V][64][256 B]
-  griddep_wait();
-  griddep_launch();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int tile = blockIdx.x, hh = blockIdx.y;
-  if (tile >= p.tile_indptr[p.streams]) return;
-  int lo = 0, hi = p.streams - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (p.tile_indptr[mid] <= tile) lo = mid;
-    else hi = mid - 1;
-  }
-  const int st = lo;
-  const int qs0 = p.qo_indptr[st], ext = p.qo_indptr[st + 1] - qs0;
-  const int64_t seq_len = p.seq_lens[st];
-  const int prefix = (int)(seq_len - ext);
-  const int q0 = (tile - p.tile_indptr[st]) * kPfRows;  // first query of the tile (within the extend)
-  const int nq = min(kPfRows, ext - q0);
-  const int kvh = hh / (p.hq / p.hkv);
-  const int pg0 = p.page_indptr[st], npages = p.page_indptr[st + 1] - pg0;
-  const int kmax = prefix + q0 + nq;  // keys needed by the tile
-  const int ntiles = (kmax + kPfKeys - 1) / kPfKeys;
-
-  // Q tile: rows q0.. of head hh (rows past the extend are zero)
-  for (int c = threadIdx.x; c < kPfRows * 16; c += kPfWarps * 32) {
-    const int r = c >> 4, ch = c & 15;
-    uint8_t* dst = qbuf + swz(r, ch);
-    if (r < nq)
-      cp_async16(dst, p.q + (int64_t)(qs0 + q0 + r) * p.q_stride + (int64_t)hh * kD + ch * 8);
-    else
-      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-  }
-  auto load_kv = [&](int kt, int stage) {
-    uint8_t* kd = kvbuf + stage * 2 * kPfTileBytes;
-    uint8_t* vd = kd + kPfTileBytes;
-    for (int c = threadIdx.x; c < kPfKeys * 16; c += kPfWarps * 32) {
-      const int r = c >> 4, ch = c & 15;
-      const int pgl = kt * (kPfKeys / kPage) + (r >> 4);
-      if (pgl < npages) {
-        const int64_t page = p.page_indices[pg0 + pgl];
-        const int64_t off = ((page * kPage + (r & 15)) * p.hkv + kvh) * kD + ch * 8;
-        cp_async16(kd + swz(r, ch), p.k_cache + off);
-        cp_async16(vd + swz(r, ch), p.v_cache + off);
-      } else {
-        *reinterpret_cast<uint4*>(kd + swz(r, ch)) = make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(vd + swz(r, ch)) = make_uint4(0, 0, 0, 0);
-      }
-    }
-    cp_async_commit();
-  };
-  load_kv(0, 0);
-  // Q fragments (A operand, rows 16 warp .. 16 warp + 15)
-  cp_async_wait<0>();
-  __syncthreads();
-  uint32_t qa[8][4];
-  {
-    const uint32_t qb = smem_u32(qbuf);
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int row = warp * 16 + (lane & 15);
-      const int ch = 2 * ks + (lane >> 4);
-      ldsm_x4(qb + swz(row, ch), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
-    }
-  }
-  float o[16][4];
-#pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-  const int qr0 = q0 + warp * 16 + g, qr1 = qr0 + 8;  // this thread's two query rows (extend index)
-  const int lim0 = prefix + qr0, lim1 = prefix + qr1;  // last visible key of each row
-  for (int kt = 0; kt < ntiles; ++kt) {
-    const int stage = kt & 1;
-    if (kt + 1 < ntiles) {
-      load_kv(kt + 1, stage ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    uint8_t* kd = kvbuf + stage * 2 * kPfTileBytes;
-    // keys past the sequence hold stale values: zero their V rows
-    const int kbase = kt * kPfKeys;
-    if (kbase + kPfKeys > seq_len) {
-      const int first = (int)max((int64_t)0, seq_len - kbase);
-      for (int c = first * 16 + threadIdx.x; c < kPfKeys * 16; c += kPfWarps * 32)
-        *reinterpret_cast<uint4*>(kd + kPfTileBytes + swz(c >> 4, c & 15)) = make_uint4(0, 0, 0, 0);
-      __syncthreads();
-    }
-    const uint32_t kb = smem_u32(kd), vb = kb + kPfTileBytes;
-    // S = Q K^T: 16 rows x 64 keys (8 n-tiles of 8)
-    float s[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-#pragma unroll
-      for (int pr = 0; pr < 4; ++pr) {
-        const int tok = 16 * pr + ((lane >> 4) << 3) + (lane & 7);
-        const int ch = 2 * ks + ((lane >> 3) & 1);
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4(kb + swz(tok, ch), r0, r1, r2, r3);
-        mma_bf16_16816(s[2 * pr], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], r0, r1);
-        mma_bf16_16816(s[2 * pr + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], r2, r3);
-      }
-    }
-    // causal mask + online softmax (rows qr0: elements 0,1; qr1: elements 2,3)
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int key = kbase + 8 * n + 2 * t + e;
-        s[n][e] = key <= lim0 ? s[n][e] * p.scale_log2 : -INFINITY;
-        s[n][2 + e] = key <= lim1 ? s[n][2 + e] * p.scale_log2 : -INFINITY;
-        mx0 = fmaxf(mx0, s[n][e]);
-        mx1 = fmaxf(mx1, s[n][2 + e]);
-      }
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float a0 = mn0 == -INFINITY ? 1.0f : exp2f(m0 - mn0);
-    const float a1 = mn1 == -INFINITY ? 1.0f : exp2f(m1 - mn1);
-    float rs0 = 0.0f, rs1 = 0.0f;
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        s[n][e] = s[n][e] == -INFINITY ? 0.0f : exp2f(s[n][e] - mn0);
-        s[n][2 + e] = s[n][2 + e] == -INFINITY ? 0.0f : exp2f(s[n][2 + e] - mn1);
-        rs0 += s[n][e];
-        rs1 += s[n][2 + e];
-      }
-    }
-    rs0 += __shfl_xor_sync(0xFFFFFFFFu, rs0, 1);
-    rs0 += __shfl_xor_sync(0xFFFFFFFFu, rs0, 2);
-    rs1 += __shfl_xor_sync(0xFFFFFFFFu, rs1, 1);
-    rs1 += __shfl_xor_sync(0xFFFFFFFFu, rs1, 2);
-    l0 = l0 * a0 + rs0;
-    l1 = l1 * a1 + rs1;
-    m0 = mn0;
-    m1 = mn1;
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      o[n][0] *= a0;
-      o[n][1] *= a0;
-      o[n][2] *= a1;
-      o[n][3] *= a1;
-    }
-    // O += P V: keys in 4 k-steps of 16 (P from the S accumulators), dims in 16 n-tiles
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const uint32_t pa0 = pack_bf2(s[2 * kk][0], s[2 * kk][1]);
-      const uint32_t pa1 = pack_bf2(s[2 * kk][2], s[2 * kk][3]);
-      const uint32_t pa2 = pack_bf2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      const uint32_t pa3 = pack_bf2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int tok = 16 * kk + ((lane >> 3) & 1) * 8 + (lane & 7);
-        const int ch = 2 * jj + (lane >> 4);
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4_t(vb + swz(tok, ch), r0, r1, r2, r3);
-        mma_bf16_16816(o[2 * jj], pa0, pa1, pa2, pa3, r0, r1);
-        mma_bf16_16816(o[2 * jj + 1], pa0, pa1, pa2, pa3, r2, r3);
-      }
-    }
-    __syncthreads();  // the buffer of this stage is refilled by the next iteration's load
-  }
-  const float inv0 = l0 > 0.0f ? 1.0f / l0 : 0.0f, inv1 = l1 > 0.0f ? 1.0f / l1 : 0.0f;
-#pragma unroll
-  for (int n = 0; n < 16; ++n) {
-    const int d = 8 * n + 2 * t;
-    if (qr0 < ext)
-      *reinterpret_cast<uint32_t*>(p.out + (int64_t)(qs0 + qr0) * p.out_stride + (int64_t)hh * kD + d) =
-          pack_bf2(o[n][0] * inv0, o[n][1] * inv0);
-    if (qr1 < ext)
-      *reinterpret_cast<uint32_t*>(p.out + (int64_t)(qs0 + qr1) * p.out_stride + (int64_t)hh * kD + d) =
-          pack_bf2(o[n][2] * inv1, o[n][3] * inv1);
-  }
-}
 
 // ---------------------------------------------------------------------------
 // Predictor attention: rows laid out (request, token); a row attends to the
@@ -982,42 +763,3 @@ extern "C" OMNI_API int omni_paged_decode_attention_noalloc(
                                      work_capacity, sm_scale, out, out_stride, scratch, need, grid_ctas, stream);
 }
 
-extern "C" OMNI_API int omni_prefill_attention(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
-                                              const int32_t* qo_indptr, const int64_t* seq_lens,
-                                              const int32_t* page_indptr, const int32_t* page_indices,
-                                              const int32_t* tile_indptr, int64_t streams, int64_t max_tiles,
-                                              int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-                                              int32_t page_size, float sm_scale, void* out, int64_t out_stride,
-                                              void* stream) {
-  if (streams < 0 || max_tiles < 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads)
-    return set_error(OMNI_ERR_INVALID, "bad prefill attention shape");
-  if (head_dim != kD || page_size != kPage)
-    return set_error(OMNI_ERR_UNSUPPORTED, "prefill attention supports head_dim 128 and pages of 16");
-  if ((reinterpret_cast<uintptr_t>(q) & 15) || q_stride % 8 || (reinterpret_cast<uintptr_t>(out) & 3) ||
-      out_stride % 2 || (reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15))
-    return set_error(OMNI_ERR_UNSUPPORTED, "misaligned prefill attention operands");
-  if (streams == 0 || max_tiles == 0) return OMNI_OK;
-  PrefillParams p{};
-  p.q = static_cast<const uint16_t*>(q);
-  p.q_stride = q_stride;
-  p.k_cache = static_cast<const uint16_t*>(k_cache);
-  p.v_cache = static_cast<const uint16_t*>(v_cache);
-  p.qo_indptr = qo_indptr;
-  p.seq_lens = seq_lens;
-  p.page_indptr = page_indptr;
-  p.page_indices = page_indices;
-  p.tile_indptr = tile_indptr;
-  p.streams = (int)streams;
-  p.hq = num_q_heads;
-  p.hkv = num_kv_heads;
-  p.scale_log2 = sm_scale * 1.4426950408889634f;
-  p.out = static_cast<uint16_t*>(out);
-  p.out_stride = out_stride;
-  const size_t smem = (size_t)kPfRows * kD * 2 + 2 * 2 * kPfTileBytes;  // 80 KB
-  static std::once_flag once;
-  std::call_once(once, [smem] {
-    cudaFuncSetAttribute(prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  });
-  return check_launch(launch(prefill_attention_kernel, dim3((unsigned)max_tiles, (unsigned)num_q_heads),
-                             dim3(kPfWarps * 32), smem, static_cast<cudaStream_t>(stream), p));
-}

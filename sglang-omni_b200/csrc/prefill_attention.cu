@@ -1,0 +1,413 @@
+// Causal extend (prefill) attention over the paged KV pool on the 5th-generation
+// tensor cores (RadixAttention extend, thinker_model.py:373-379; the extend rows of a
+// mixed batch attend causally over their stream's pages, which the qkv epilogue has
+// just written).
+//
+// CTA = 128 queries of one stream x one query head; the stream's keys go by in tiles of
+// 128 (8 pages).  Six warps:
+//   warp 0    TMA producer: the Q tile once (two 64-column halves, 128B swizzle), then
+//             per key tile the 8 pages of K and of V, one 16-row x 64-column box per
+//             lane (32 lanes, 32 boxes), into a two-stage ring; pages past the stream
+//             are loaded from beyond the pool (zero fill);
+//   warp 1    MMA issuer (one elected lane): S_j = Q K_j^T into one of two TMEM
+//             buffers (M 128 queries x N 128 keys, fp32), then O += P_{j-1} V_{j-1}
+//             (A = P from shared memory, K-major; B = V, MN-major: the key rows as they
+//             sit in the pool are the K dimension, the head dimension the N one) --
+//             the QK^T of a tile runs while the softmax works on the previous one;
+//   warps 2-5 softmax, one query row per thread (TMEM lane): row max over the visible
+//             keys (key <= prefix + query), the lazily rescaled running max (O and the
+//             running sum are rescaled only when the max grows by more than 2^8), P =
+//             exp2(s * scale * log2 e - max) written as bf16 into a swizzled P buffer,
+//             and at the end O / sum to the output row.
+// Every barrier wait is bounded; a wait that gives up records a status and ends the
+// role's loop.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "capi_util.h"
+#include "common.cuh"
+
+namespace omni {
+namespace {
+
+OMNI_DEFINE_STATUS(prefill_tc)
+
+constexpr int kD = 128;
+constexpr int kPage = 16;
+constexpr int kRows = 128;                 // queries per CTA = TMEM lanes
+constexpr int kKeys = 128;                 // keys per tile
+constexpr int kHalfBytes = 128 * 128;      // [128 rows][64 bf16]
+constexpr int kTileBytes = 2 * kHalfBytes;  // 32 KB
+constexpr int kThreads = 192;
+constexpr int kQOff = 0;
+constexpr int kKVOff = kTileBytes;                       // stage s: K at + s*64K, V at + s*64K + 32K
+constexpr int kPOff = kKVOff + 4 * kTileBytes;           // P buffer b at + b*32K
+constexpr int kBarOff = kPOff + 2 * kTileBytes;          // 224 KB
+constexpr size_t kSmemBytes = (size_t)kBarOff + 256 + 1024;  // + barriers + alignment slack
+constexpr float kRescaleLog2 = 8.0f;
+
+struct PrefillTcParams {
+  const int32_t* qo_indptr;
+  const int64_t* seq_lens;
+  const int32_t* page_indptr;
+  const int32_t* page_indices;
+  const int32_t* tile_indptr;
+  int streams, hq, hkv;
+  int64_t num_slots;
+  float scale_log2;
+  uint16_t* out;
+  int64_t out_stride;
+};
+
+struct Bars {
+  uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2], drain;
+  uint32_t tmem;
+};
+
+// K-major / MN-major 128B-swizzle operand descriptors.  MN-major (the V operand):
+// 64-element rows along N, 8-row groups along K 1024 B apart (SBO), the second
+// 64 columns of N 16 KB away (LBO).
+OMNI_DEVINL uint64_t desc_mn_sw128(const void* p) {
+  uint64_t addr = smem_u32(p);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;
+  d |= (uint64_t)(kHalfBytes >> 4) << 16;  // LBO: the next 64 elements of N
+  d |= (uint64_t)(1024 >> 4) << 32;        // SBO: the next 8 rows of K
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+OMNI_DEVINL void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+OMNI_DEVINL void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
+    const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+    const __grid_constant__ CUtensorMap tv, const __grid_constant__ PrefillTcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + kBarOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, hh = blockIdx.y;
+  griddep_wait();
+  griddep_launch();
+  if (tile >= p.tile_indptr[p.streams]) return;
+  int lo = 0, hi = p.streams - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.tile_indptr[mid] <= tile) lo = mid;
+    else hi = mid - 1;
+  }
+  const int st = lo;
+  const int qs0 = p.qo_indptr[st], ext = p.qo_indptr[st + 1] - qs0;
+  const int64_t seq_len = p.seq_lens[st];
+  const int prefix = (int)(seq_len - ext);
+  const int q0 = (tile - p.tile_indptr[st]) * kRows;  // first query of the tile (within the extend)
+  const int nq = min(kRows, ext - q0);
+  const int kvh = hh / (p.hq / p.hkv);
+  const int pg0 = p.page_indptr[st], npages = p.page_indptr[st + 1] - pg0;
+  const int nt = (prefix + q0 + nq + kKeys - 1) / kKeys;  // key tiles the tile needs
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->kv_full[i], 1);
+      mbar_init(&bars->kv_empty[i], 1);
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->s_free[i], 4 * 32);
+      mbar_init(&bars->p_full[i], 4 * 32);
+      mbar_init(&bars->pv_done[i], 1);
+    }
+    mbar_init(&bars->drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem;
+  const uint32_t tO = tbase + 256;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      mbar_arrive_expect_tx(&bars->q_full, kTileBytes);
+    }
+    __syncwarp();
+    if (lane < 2) tma_load_2d(smem + kQOff + lane * kHalfBytes, &tq, &bars->q_full, hh * kD + lane * 64, qs0 + q0);
+    for (int j = 0; j < nt; ++j) {
+      const int s = j & 1;
+      if (j >= 2 && !mbar_wait(&bars->kv_empty[s], ((j - 2) >> 1) & 1)) {
+        report_status(kDevTimeoutTma);
+        break;
+      }
+      if (lane == 0) mbar_arrive_expect_tx(&bars->kv_full[s], 2 * kTileBytes);
+      __syncwarp();
+      const int idx = lane & 15, pg = idx >> 1, half = idx & 1;
+      const int pgl = j * (kKeys / kPage) + pg;
+      const int64_t y = pgl < npages ? (int64_t)p.page_indices[pg0 + pgl] * kPage : p.num_slots;
+      uint8_t* dst = smem + kKVOff + s * 2 * kTileBytes + (lane < 16 ? 0 : kTileBytes) + half * kHalfBytes +
+                     pg * kPage * 128;
+      tma_load_2d(dst, lane < 16 ? (const void*)&tk : (const void*)&tv, &bars->kv_full[s], kvh * kD + half * 64,
+                  (int)y);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    const bool leader = elect_one();
+    const uint32_t idesc_qk = idesc_bf16_f32(kRows, kKeys);
+    const uint32_t idesc_pv = idesc_bf16_f32(kRows, kD) | (1u << 16);  // B MN-major
+    bool ok = mbar_wait(&bars->q_full, 0);
+    for (int j = 0; ok && j <= nt; ++j) {
+      if (j < nt) {
+        const int s = j & 1;
+        ok = mbar_wait(&bars->kv_full[s], (j >> 1) & 1) && (j < 2 || mbar_wait(&bars->s_free[s], ((j - 2) >> 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+        if (leader) {
+          const uint8_t* kt = smem + kKVOff + s * 2 * kTileBytes;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint64_t ad = smem_desc_sw128(smem + kQOff + (k >> 2) * kHalfBytes) + 2 * (k & 3);
+            const uint64_t bd = smem_desc_sw128(kt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
+            tc_mma_bf16(tbase + s * 128, ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+          }
+          tc_commit(&bars->s_full[s]);
+        }
+        __syncwarp();
+      }
+      if (j >= 1) {
+        const int i = j - 1, s = i & 1;
+        if (!mbar_wait(&bars->p_full[s], (i >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (leader) {
+          const uint8_t* pt = smem + kPOff + s * kTileBytes;
+          const uint8_t* vt = smem + kKVOff + s * 2 * kTileBytes + kTileBytes;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint64_t ad = smem_desc_sw128(pt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
+            const uint64_t bd = desc_mn_sw128(vt + k * 16 * 128);
+            tc_mma_bf16(tO, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&bars->pv_done[s]);
+          tc_commit(&bars->kv_empty[s]);
+        }
+        __syncwarp();
+      }
+    }
+    if (!ok) report_status(kDevTimeoutMma);
+    // every MMA of this warp has completed before the TMEM is freed
+    if (leader) tc_commit(&bars->drain);
+    __syncwarp();
+    mbar_wait(&bars->drain, 0);
+  } else {
+    // ---------------- softmax (one query row per thread) ----------------
+    const int q = warp & 3;                // TMEM lane quarter of this warp
+    const int r = q * 32 + lane;           // query row of the tile
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const int lim = prefix + q0 + r;       // last key this query sees
+    const float sl = p.scale_log2;
+    float m_use = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nt && ok; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait(&bars->s_full[s], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t ts = tbase + lane_off + s * 128;
+      // pass 1: the row max over the visible keys
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(ts + c * 32, v);
+        tc_wait_ld();
+        const int k0 = j * kKeys + c * 32;
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (k0 + e <= lim) mx = fmaxf(mx, __uint_as_float(v[e]));
+      }
+      const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl;
+      const float m_new = fmaxf(m_use, m_tile);
+      if (m_new != -INFINITY && (m_use == -INFINITY || m_new > m_use + kRescaleLog2)) {
+        const float alpha = m_use == -INFINITY ? 0.0f : exp2f(m_use - m_new);
+        if (j > 0 && l > 0.0f) {
+          // O holds tiles < j once the previous P V has completed
+          if (!mbar_wait(&bars->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tO + lane_off + c * 32, v);
+            tc_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+            tmem_st_32x32b_x32(tO + lane_off + c * 32, v);
+          }
+          tc_wait_st();
+        }
+        l *= alpha;
+        m_use = m_new;
+      }
+      // the P buffer of tile j - 2 is free once its P V has completed
+      if (j >= 2 && !mbar_wait(&bars->pv_done[s], ((j - 2) >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      // pass 2: P = exp2(s * scale - max) as bf16 into the swizzled P buffer
+      uint8_t* prow = smem + kPOff + s * kTileBytes + r * 128;
+      float rs = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(ts + c * 32, v);
+        tc_wait_ld();
+        const int k0 = j * kKeys + c * 32;
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float a = (k0 + e <= lim) ? exp2f(__uint_as_float(v[e]) * sl - m_use) : 0.0f;
+          const float b = (k0 + e + 1 <= lim) ? exp2f(__uint_as_float(v[e + 1]) * sl - m_use) : 0.0f;
+          rs += a + b;
+          pk[e >> 1] = pack_bf2(a, b);
+        }
+        // keys c*32 .. c*32+31: half (c >> 1), 16-byte chunks (c & 1) * 4 .. + 3 of the row
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int chunk = (c & 1) * 4 + u;
+          uint8_t* dst = prow + (c >> 1) * kHalfBytes + ((chunk ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+      }
+      l += rs;
+      tc_fence_before();
+      mbar_arrive(&bars->s_free[s]);
+      fence_proxy_async();  // the P stores, visible to the tensor core
+      mbar_arrive(&bars->p_full[s]);
+    }
+    if (ok && nt > 0 && mbar_wait(&bars->pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1)) {
+      tc_fence_after();
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+      uint16_t* orow = p.out + (int64_t)(qs0 + q0 + r) * p.out_stride + (int64_t)hh * kD;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tO + lane_off + c * 32, v);
+        tc_wait_ld();
+        if (r < nq) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2)
+            pk[e >> 1] = pack_bf2(__uint_as_float(v[e]) * inv, __uint_as_float(v[e + 1]) * inv);
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+      }
+    } else if (nt > 0) {
+      report_status(kDevTimeoutMma);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// bf16 [rows, cols] with row stride (elements), box {64, box_rows}, 128B swizzle.
+bool tmap_2d(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t stride, int box_rows) {
+  auto fn = encode_tiled();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)stride * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+}  // namespace omni
+
+using namespace omni;
+
+extern "C" OMNI_API int omni_prefill_attention(const void* q, int64_t q_stride, int64_t q_rows, const void* k_cache,
+                                              const void* v_cache, int64_t num_slots, const int32_t* qo_indptr,
+                                              const int64_t* seq_lens, const int32_t* page_indptr,
+                                              const int32_t* page_indices, const int32_t* tile_indptr,
+                                              int64_t streams, int64_t max_tiles, int32_t num_q_heads,
+                                              int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                                              float sm_scale, void* out, int64_t out_stride, void* stream) {
+  if (streams < 0 || max_tiles < 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || q_rows < 0 ||
+      num_slots <= 0)
+    return set_error(OMNI_ERR_INVALID, "bad prefill attention shape");
+  if (head_dim != kD || page_size != kPage)
+    return set_error(OMNI_ERR_UNSUPPORTED, "prefill attention supports head_dim 128 and pages of 16");
+  if ((reinterpret_cast<uintptr_t>(q) & 15) || q_stride % 8 || (reinterpret_cast<uintptr_t>(out) & 15) ||
+      out_stride % 8 || (reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15))
+    return set_error(OMNI_ERR_UNSUPPORTED, "misaligned prefill attention operands");
+  if (streams == 0 || max_tiles == 0 || q_rows == 0) return OMNI_OK;
+  CUtensorMap tq, tk, tv;
+  const int64_t kv_cols = (int64_t)num_kv_heads * kD;
+  if (!tmap_2d(&tq, q, q_rows, (int64_t)num_q_heads * kD, q_stride, kRows) ||
+      !tmap_2d(&tk, k_cache, num_slots, kv_cols, kv_cols, kPage) ||
+      !tmap_2d(&tv, v_cache, num_slots, kv_cols, kv_cols, kPage))
+    return set_error(OMNI_ERR_UNSUPPORTED, "tensor map encoding failed");
+  PrefillTcParams p{};
+  p.qo_indptr = qo_indptr;
+  p.seq_lens = seq_lens;
+  p.page_indptr = page_indptr;
+  p.page_indices = page_indices;
+  p.tile_indptr = tile_indptr;
+  p.streams = (int)streams;
+  p.hq = num_q_heads;
+  p.hkv = num_kv_heads;
+  p.num_slots = num_slots;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.out = static_cast<uint16_t*>(out);
+  p.out_stride = out_stride;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(prefill_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  });
+  return check_launch(launch(prefill_attention_tc_kernel, dim3((unsigned)max_tiles, (unsigned)num_q_heads),
+                             dim3(kThreads), kSmemBytes, static_cast<cudaStream_t>(stream), tq, tk, tv, p));
+}

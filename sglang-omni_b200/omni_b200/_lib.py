@@ -88,8 +88,8 @@ SIGNATURES: dict[str, list] = {
     "omni_moe_partial_sum": [_P, _I64, _P, _P, _I64, _I32, _I64, _I32, _P, _I64, _P],
     "omni_moe_combine_parts": [_P, _I64, _P, _I32, _P, _I64, _P, _P, _I64, _P, _I64, _P, _I64, _I64, _I32, _P],
     "omni_extend_prepare": [_I64, _P, _P, _P, _P, _I64, _I32, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P],
-    "omni_prefill_attention": [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _I32, _F32, _P,
-                               _I64, _P],
+    "omni_prefill_attention": [_P, _I64, _I64, _P, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32,
+                               _I32, _F32, _P, _I64, _P],
     "omni_bias_snake_beta": [_P, _I64, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I32, _P],
     "omni_clamped_single_output_conv": [_P, _I64, _P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I32, _I32, _P],
     "omni_history_exchange": [_P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _I64, _I32, _I32, _I32, _I32, _I32,

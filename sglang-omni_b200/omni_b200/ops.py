@@ -546,7 +546,7 @@ def moe_combine_parts(parts: torch.Tensor, part_index: torch.Tensor, x: torch.Te
               0 if ss_out is None else ss_out.stride(0), rows, hidden, _lib.stream_of(h.device))
 
 
-PREFILL_Q_TILE = 64
+PREFILL_Q_TILE = 128
 
 
 def extend_prepare(*, prefix_lens, extend_lens, req_pool_indices, req_to_token, page_size, seq_lens, qo_indptr,
@@ -564,8 +564,9 @@ def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
                       page_indptr, page_indices, tile_indptr, max_tiles: int, num_q_heads: int, num_kv_heads: int,
                       head_dim: int, page_size: int, sm_scale: float, out: torch.Tensor) -> torch.Tensor:
     """Causal extend attention over the paged pool; q/out rows are the extend rows (cu_seqlens qo_indptr)."""
-    _lib.call("omni_prefill_attention", q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
-              qo_indptr.data_ptr(), seq_lens.data_ptr(), page_indptr.data_ptr(), page_indices.data_ptr(),
+    _lib.call("omni_prefill_attention", q.data_ptr(), q.stride(0), q.shape[0], k_cache.data_ptr(),
+              v_cache.data_ptr(), k_cache.shape[0], qo_indptr.data_ptr(), seq_lens.data_ptr(),
+              page_indptr.data_ptr(), page_indices.data_ptr(),
               tile_indptr.data_ptr(), qo_indptr.shape[0] - 1, max_tiles, num_q_heads, num_kv_heads, head_dim,
               page_size, sm_scale, out.data_ptr(), out.stride(0), _lib.stream_of(q.device))
     return out

@@ -3,8 +3,9 @@
 - extend packing (slots, positions, cu_seqlens, page lists, q tiles): bit-exact
   against the oracle;
 - causal extend attention over the paged pool (pages randomly permuted, streams
-  with and without a prefix, lengths around the 64-row tile and 16-token page
-  edges) against a torch fp32 reference: cosine >= 0.999, max-abs <= 2e-2 x scale.
+  with and without a prefix, lengths around the 128-query tile, the 128-key tile and
+  16-token page edges) against a torch fp32 reference: cosine >= 0.999, max-abs <= 2e-2
+  x scale.
 """
 
 from __future__ import annotations
@@ -60,7 +61,8 @@ def _pack(streams, r2t, req):
     return out
 
 
-STREAMS = [(0, 1), (0, 63), (0, 64), (0, 65), (0, 200), (37, 50), (5, 1), (16, 16)]
+STREAMS = [(0, 1), (0, 63), (0, 64), (0, 65), (0, 127), (0, 128), (0, 129), (0, 200), (37, 50), (5, 1),
+           (16, 16), (100, 300), (250, 7)]
 
 
 def test_extend_prepare_matches_oracle():
@@ -90,7 +92,7 @@ def test_prefill_attention_matches_fp32(hq, hkv):
     total = sum(s[1] for s in STREAMS)
     q = torch.randn(total, hq * D, generator=g, device=DEV).to(torch.bfloat16)
     out = torch.full((total, hq * D), float("nan"), device=DEV, dtype=torch.bfloat16)
-    max_tiles = sum(math.ceil(s[1] / 64) for s in STREAMS)
+    max_tiles = sum(math.ceil(s[1] / ops.PREFILL_Q_TILE) for s in STREAMS)
     scale = 1 / math.sqrt(D)
     ops.prefill_attention(q, kc, vc, qo_indptr=pk["qo_indptr"], seq_lens=pk["seq_lens"],
                           page_indptr=pk["page_indptr"], page_indices=pk["page_indices"],
