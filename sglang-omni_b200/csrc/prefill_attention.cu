@@ -14,11 +14,12 @@
 //             (A = P from shared memory, K-major; B = V, MN-major: the key rows as they
 //             sit in the pool are the K dimension, the head dimension the N one) --
 //             the QK^T of a tile runs while the softmax works on the previous one;
-//   warps 2-5 softmax, one query row per thread (TMEM lane): row max over the visible
-//             keys (key <= prefix + query), the lazily rescaled running max (O and the
-//             running sum are rescaled only when the max grows by more than 2^8), P =
-//             exp2(s * scale * log2 e - max) written as bf16 into a swizzled P buffer,
-//             and at the end O / sum to the output row.
+//   warps 2-5 softmax, one query row per thread (TMEM lane): P = exp2(s * scale *
+//             log2 e - m) against the running max m in one pass over the tile (masking
+//             only the tiles that cross the causal diagonal), written as bf16 into a
+//             swizzled P buffer; the first tile, and a tile whose max passes m by more
+//             than 2^8, rescale O and the running sum and write P again; at the end
+//             O / sum goes to the output row.
 // Every barrier wait is bounded; a wait that gives up records a status and ends the
 // role's loop.
 #include <cuda.h>
@@ -92,6 +93,12 @@ OMNI_DEVINL void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
       : "memory");
 }
 OMNI_DEVINL void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// 2^x by the PTX ex2.approx instruction (flush-to-zero; 2^-inf = +0).
+OMNI_DEVINL float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
     const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -229,6 +236,40 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
     const float sl = p.scale_log2;
     float m_use = -INFINITY, l = 0.0f;
     bool ok = true;
+    // P = exp2(s * scale - m_use) for this row's keys of tile j into the swizzled P
+    // buffer (masked keys 0); returns the sum of the row's P and its raw max score
+    auto write_p = [&](uint32_t ts, uint8_t* prow, int j, bool masked, float& mx) -> float {
+      float rs = 0.0f;
+      mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(ts + c * 32, v);
+        tc_wait_ld();
+        const int k0 = j * kKeys + c * 32;
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float a = __uint_as_float(v[e]), b = __uint_as_float(v[e + 1]);
+          if (masked) {
+            a = k0 + e <= lim ? a : -INFINITY;
+            b = k0 + e + 1 <= lim ? b : -INFINITY;
+          }
+          mx = fmaxf(mx, fmaxf(a, b));
+          const float pa = ex2_approx(a * sl - m_use), pb = ex2_approx(b * sl - m_use);
+          rs += pa + pb;
+          pk[e >> 1] = pack_bf2(pa, pb);
+        }
+        // keys c*32 .. c*32+31: half (c >> 1), 16-byte chunks (c & 1) * 4 .. + 3 of the row
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int chunk = (c & 1) * 4 + u;
+          uint8_t* dst = prow + (c >> 1) * kHalfBytes + ((chunk ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+      }
+      return rs;
+    };
     for (int j = 0; j < nt && ok; ++j) {
       const int s = j & 1;
       if (!mbar_wait(&bars->s_full[s], (j >> 1) & 1)) {
@@ -237,22 +278,34 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
       }
       tc_fence_after();
       const uint32_t ts = tbase + lane_off + s * 128;
-      // pass 1: the row max over the visible keys
-      float mx = -INFINITY;
+      // the P buffer of tile j - 2 is free once its P V has completed
+      if (j >= 2 && !mbar_wait(&bars->pv_done[s], ((j - 2) >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      uint8_t* prow = smem + kPOff + s * kTileBytes + r * 128;
+      // every key of the tile is visible to every query of the CTA: no mask
+      const bool masked = j * kKeys + kKeys - 1 > prefix + q0;
+      float mx;
+      // one pass against the running max; the rare tile whose max passes it by more
+      // than 2^8 (and the first tile) rescales O and the sum and writes P again
+      float rs = m_use == -INFINITY ? 0.0f : write_p(ts, prow, j, masked, mx);
+      if (m_use == -INFINITY) {
+        mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(ts + c * 32, v);
-        tc_wait_ld();
-        const int k0 = j * kKeys + c * 32;
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(ts + c * 32, v);
+          tc_wait_ld();
+          const int k0 = j * kKeys + c * 32;
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (k0 + e <= lim) mx = fmaxf(mx, __uint_as_float(v[e]));
+          for (int e = 0; e < 32; ++e)
+            if (!masked || k0 + e <= lim) mx = fmaxf(mx, __uint_as_float(v[e]));
+        }
       }
       const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl;
-      const float m_new = fmaxf(m_use, m_tile);
-      if (m_new != -INFINITY && (m_use == -INFINITY || m_new > m_use + kRescaleLog2)) {
-        const float alpha = m_use == -INFINITY ? 0.0f : exp2f(m_use - m_new);
+      if (m_tile != -INFINITY && (m_use == -INFINITY || m_tile > m_use + kRescaleLog2)) {
+        const float alpha = m_use == -INFINITY ? 0.0f : ex2_approx(m_use - m_tile);
         if (j > 0 && l > 0.0f) {
           // O holds tiles < j once the previous P V has completed
           if (!mbar_wait(&bars->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
@@ -272,37 +325,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
           tc_wait_st();
         }
         l *= alpha;
-        m_use = m_new;
-      }
-      // the P buffer of tile j - 2 is free once its P V has completed
-      if (j >= 2 && !mbar_wait(&bars->pv_done[s], ((j - 2) >> 1) & 1)) {
-        ok = false;
-        break;
-      }
-      // pass 2: P = exp2(s * scale - max) as bf16 into the swizzled P buffer
-      uint8_t* prow = smem + kPOff + s * kTileBytes + r * 128;
-      float rs = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(ts + c * 32, v);
-        tc_wait_ld();
-        const int k0 = j * kKeys + c * 32;
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float a = (k0 + e <= lim) ? exp2f(__uint_as_float(v[e]) * sl - m_use) : 0.0f;
-          const float b = (k0 + e + 1 <= lim) ? exp2f(__uint_as_float(v[e + 1]) * sl - m_use) : 0.0f;
-          rs += a + b;
-          pk[e >> 1] = pack_bf2(a, b);
-        }
-        // keys c*32 .. c*32+31: half (c >> 1), 16-byte chunks (c & 1) * 4 .. + 3 of the row
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int chunk = (c & 1) * 4 + u;
-          uint8_t* dst = prow + (c >> 1) * kHalfBytes + ((chunk ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-        }
+        m_use = m_tile;
+        float unused;
+        rs = write_p(ts, prow, j, masked, unused);
       }
       l += rs;
       tc_fence_before();
