@@ -4,7 +4,7 @@
 // just written).
 //
 // CTA = 128 queries of one stream x one query head; the stream's keys go by in tiles of
-// 128 (8 pages).  Six warps:
+// 128 (8 pages).  Ten warps:
 //   warp 0    TMA producer: the Q tile once (two 64-column halves, 128B swizzle), then
 //             per key tile the 8 pages of K and of V, one 16-row x 64-column box per
 //             lane (32 lanes, 32 boxes), into a two-stage ring; pages past the stream
@@ -14,7 +14,8 @@
 //             (A = P from shared memory, K-major; B = V, MN-major: the key rows as they
 //             sit in the pool are the K dimension, the head dimension the N one) --
 //             the QK^T of a tile runs while the softmax works on the previous one;
-//   warps 2-5 softmax, one query row per thread (TMEM lane): P = exp2(s * scale *
+//   warps 2-9 softmax, two threads per query row (TMEM lane; 64 columns each, the row
+//             max and sum swapped through spare TMEM columns): P = exp2(s * scale *
 //             log2 e - m) against the running max m in one pass over the tile (masking
 //             only the tiles that cross the causal diagonal), written as bf16 into a
 //             swizzled P buffer; the first tile, and a tile whose max passes m by more
@@ -41,7 +42,7 @@ constexpr int kRows = 128;                 // queries per CTA = TMEM lanes
 constexpr int kKeys = 128;                 // keys per tile
 constexpr int kHalfBytes = 128 * 128;      // [128 rows][64 bf16]
 constexpr int kTileBytes = 2 * kHalfBytes;  // 32 KB
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // TMA warp, MMA warp, 8 softmax warps
 constexpr int kQOff = 0;
 constexpr int kKVOff = kTileBytes;                       // stage s: K at + s*64K, V at + s*64K + 32K
 constexpr int kPOff = kKVOff + 4 * kTileBytes;           // P buffer b at + b*32K
@@ -63,7 +64,7 @@ struct PrefillTcParams {
 };
 
 struct Bars {
-  uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2], drain;
+  uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], s_free[2], p_full[2], pv_done[2], drain, pair[4];
   uint32_t tmem;
 };
 
@@ -133,11 +134,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
       mbar_init(&bars->kv_full[i], 1);
       mbar_init(&bars->kv_empty[i], 1);
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_free[i], 4 * 32);
-      mbar_init(&bars->p_full[i], 4 * 32);
+      mbar_init(&bars->s_free[i], 8 * 32);
+      mbar_init(&bars->p_full[i], 8 * 32);
       mbar_init(&bars->pv_done[i], 1);
     }
     mbar_init(&bars->drain, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&bars->pair[i], 64);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -228,25 +230,48 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
     __syncwarp();
     mbar_wait(&bars->drain, 0);
   } else {
-    // ---------------- softmax (one query row per thread) ----------------
-    const int q = warp & 3;                // TMEM lane quarter of this warp
-    const int r = q * 32 + lane;           // query row of the tile
+    // ---------------- softmax: two threads per query row ----------------
+    // warps 2-5 take columns 0-63 of S, O and P, warps 6-9 columns 64-127, of the
+    // rows of their TMEM lane quarter; the two threads of a row swap their maxima
+    // (and at the end their sums) through two spare TMEM columns of the row.
+    const int q = warp & 3;                 // TMEM lane quarter of this warp
+    const int hc = (warp - 2) >> 2;         // column half
+    const int r = q * 32 + lane;            // query row of the tile
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    const int lim = prefix + q0 + r;       // last key this query sees
+    const uint32_t txch = tbase + lane_off + 384;  // exchange columns 384 .. 389
+    const int lim = prefix + q0 + r;        // last key this query sees
     const float sl = p.scale_log2;
     float m_use = -INFINITY, l = 0.0f;
     bool ok = true;
-    // P = exp2(s * scale - m_use) for this row's keys of tile j into the swizzled P
-    // buffer (masked keys 0); returns the sum of the row's P and its raw max score
-    auto write_p = [&](uint32_t ts, uint8_t* prow, int j, bool masked, float& mx) -> float {
+    uint32_t pair_phase = 0;
+    // this thread's value and its partner's, through the row's TMEM exchange columns
+    auto swap = [&](float mine, int slot) -> float {
+      uint32_t v1[1] = {__float_as_uint(mine)};
+      asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(txch + slot * 2 + hc), "r"(v1[0])
+                   : "memory");
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(&bars->pair[q]);
+      if (!mbar_wait(&bars->pair[q], pair_phase & 1)) ok = false;
+      ++pair_phase;
+      tc_fence_after();
+      uint32_t o1;
+      asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(o1) : "r"(txch + slot * 2 + (hc ^ 1))
+                   : "memory");
+      tc_wait_ld();
+      return __uint_as_float(o1);
+    };
+    // P = exp2(s * scale - m_use) for this thread's 64 keys of tile j into its half of
+    // the swizzled P buffer (masked keys 0); returns their sum and raw max score
+    auto write_p = [&](uint32_t ts, uint8_t* phalf, int j, bool masked, float& mx) -> float {
       float rs = 0.0f;
       mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(ts + c * 32, v);
         tc_wait_ld();
-        const int k0 = j * kKeys + c * 32;
+        const int k0 = j * kKeys + hc * 64 + c * 32;
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
@@ -260,11 +285,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
           rs += pa + pb;
           pk[e >> 1] = pack_bf2(pa, pb);
         }
-        // keys c*32 .. c*32+31: half (c >> 1), 16-byte chunks (c & 1) * 4 .. + 3 of the row
+        // keys hc*64 + c*32 .. + 31: 16-byte chunks c*4 .. c*4+3 of the row in half hc
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int chunk = (c & 1) * 4 + u;
-          uint8_t* dst = prow + (c >> 1) * kHalfBytes + ((chunk ^ (r & 7)) << 4);
+          const int chunk = c * 4 + u;
+          uint8_t* dst = phalf + ((chunk ^ (r & 7)) << 4);
           *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         }
       }
@@ -277,32 +302,36 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
         break;
       }
       tc_fence_after();
-      const uint32_t ts = tbase + lane_off + s * 128;
+      const uint32_t ts = tbase + lane_off + s * 128 + hc * 64;
       // the P buffer of tile j - 2 is free once its P V has completed
       if (j >= 2 && !mbar_wait(&bars->pv_done[s], ((j - 2) >> 1) & 1)) {
         ok = false;
         break;
       }
-      uint8_t* prow = smem + kPOff + s * kTileBytes + r * 128;
+      uint8_t* phalf = smem + kPOff + s * kTileBytes + hc * kHalfBytes + r * 128;
       // every key of the tile is visible to every query of the CTA: no mask
       const bool masked = j * kKeys + kKeys - 1 > prefix + q0;
       float mx;
       // one pass against the running max; the rare tile whose max passes it by more
       // than 2^8 (and the first tile) rescales O and the sum and writes P again
-      float rs = m_use == -INFINITY ? 0.0f : write_p(ts, prow, j, masked, mx);
+      float rs = 0.0f;
       if (m_use == -INFINITY) {
         mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(ts + c * 32, v);
           tc_wait_ld();
-          const int k0 = j * kKeys + c * 32;
+          const int k0 = j * kKeys + hc * 64 + c * 32;
 #pragma unroll
           for (int e = 0; e < 32; ++e)
             if (!masked || k0 + e <= lim) mx = fmaxf(mx, __uint_as_float(v[e]));
         }
+      } else {
+        rs = write_p(ts, phalf, j, masked, mx);
       }
+      mx = fmaxf(mx, swap(mx, j & 1));  // the row's max over both halves
+      if (!ok) break;
       const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl;
       if (m_tile != -INFINITY && (m_use == -INFINITY || m_tile > m_use + kRescaleLog2)) {
         const float alpha = m_use == -INFINITY ? 0.0f : ex2_approx(m_use - m_tile);
@@ -314,20 +343,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
           }
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
             uint32_t v[32];
-            tmem_ld_32x32b_x32(tO + lane_off + c * 32, v);
+            tmem_ld_32x32b_x32(tO + lane_off + hc * 64 + c * 32, v);
             tc_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            tmem_st_32x32b_x32(tO + lane_off + c * 32, v);
+            tmem_st_32x32b_x32(tO + lane_off + hc * 64 + c * 32, v);
           }
           tc_wait_st();
         }
         l *= alpha;
         m_use = m_tile;
         float unused;
-        rs = write_p(ts, prow, j, masked, unused);
+        rs = write_p(ts, phalf, j, masked, unused);
       }
       l += rs;
       tc_fence_before();
@@ -335,14 +364,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
       fence_proxy_async();  // the P stores, visible to the tensor core
       mbar_arrive(&bars->p_full[s]);
     }
+    const float l_row = ok ? l + swap(l, 2) : 0.0f;
     if (ok && nt > 0 && mbar_wait(&bars->pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1)) {
       tc_fence_after();
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-      uint16_t* orow = p.out + (int64_t)(qs0 + q0 + r) * p.out_stride + (int64_t)hh * kD;
+      const float inv = l_row > 0.0f ? 1.0f / l_row : 0.0f;
+      uint16_t* orow = p.out + (int64_t)(qs0 + q0 + r) * p.out_stride + (int64_t)hh * kD + hc * 64;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tO + lane_off + c * 32, v);
+        tmem_ld_32x32b_x32(tO + lane_off + hc * 64 + c * 32, v);
         tc_wait_ld();
         if (r < nq) {
           uint32_t pk[16];
