@@ -9,8 +9,10 @@
 //             per key tile the 8 pages of K and of V, one 16-row x 64-column box per
 //             lane (32 lanes, 32 boxes), into a two-stage ring; pages past the stream
 //             are loaded from beyond the pool (zero fill);
-//   warp 1    MMA issuer (one elected lane): S_j = Q K_j^T into one of two TMEM
-//             buffers (M 128 queries x N 128 keys, fp32), then O += P_{j-1} V_{j-1}
+//   warp 1    MMA issuer (one elected lane), whichever is ready first: S_j = Q K_j^T
+//             into one of two TMEM buffers (M 128 queries x N 128 keys, fp32), or
+//             O += P_{j-1} V_{j-1} (issued as soon as P is written, so that the K/V
+//             stage frees for the next load without waiting for the next tile's K)
 //             (A = P from shared memory, K-major; B = V, MN-major: the key rows as they
 //             sit in the pool are the K dimension, the head dimension the N one) --
 //             the QK^T of a tile runs while the softmax works on the previous one;
@@ -184,11 +186,40 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
     const uint32_t idesc_qk = idesc_bf16_f32(kRows, kKeys);
     const uint32_t idesc_pv = idesc_bf16_f32(kRows, kD) | (1u << 16);  // B MN-major
     bool ok = mbar_wait(&bars->q_full, 0);
-    for (int j = 0; ok && j <= nt; ++j) {
-      if (j < nt) {
-        const int s = j & 1;
-        ok = mbar_wait(&bars->kv_full[s], (j >> 1) & 1) && (j < 2 || mbar_wait(&bars->s_free[s], ((j - 2) >> 1) & 1));
-        if (!ok) break;
+    // Issue whichever MMA is ready: the P V of tile ip as soon as its P is written
+    // (its completion frees the K/V stage for the next load), the QK^T of tile jq as
+    // soon as its K has landed and its S buffer is free.  Lane 0 polls, the warp
+    // follows its decision.
+    auto ready = [&](uint64_t* bar, uint32_t parity) -> bool {
+      uint32_t r = lane == 0 ? (mbar_try_wait(bar, parity) ? 1u : 0u) : 0u;
+      return __shfl_sync(0xFFFFFFFFu, r, 0) != 0;
+    };
+    int jq = 0, ip = 0;
+    uint32_t idle = 0;
+    while (ok && ip < nt) {
+      bool progressed = false;
+      if (ip < jq && ready(&bars->p_full[ip & 1], (ip >> 1) & 1)) {
+        const int s = ip & 1;
+        tc_fence_after();
+        if (leader) {
+          const uint8_t* pt = smem + kPOff + s * kTileBytes;
+          const uint8_t* vt = smem + kKVOff + s * 2 * kTileBytes + kTileBytes;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint64_t ad = smem_desc_sw128(pt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
+            const uint64_t bd = desc_mn_sw128(vt + k * 16 * 128);
+            tc_mma_bf16(tO, ad, bd, idesc_pv, (ip > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&bars->pv_done[s]);
+          tc_commit(&bars->kv_empty[s]);
+        }
+        __syncwarp();
+        ++ip;
+        progressed = true;
+      }
+      if (jq < nt && jq <= ip + 1 && ready(&bars->kv_full[jq & 1], (jq >> 1) & 1) &&
+          (jq < 2 || ready(&bars->s_free[jq & 1], ((jq - 2) >> 1) & 1))) {
+        const int s = jq & 1;
         tc_fence_after();
         if (leader) {
           const uint8_t* kt = smem + kKVOff + s * 2 * kTileBytes;
@@ -201,28 +232,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
           tc_commit(&bars->s_full[s]);
         }
         __syncwarp();
+        ++jq;
+        progressed = true;
       }
-      if (j >= 1) {
-        const int i = j - 1, s = i & 1;
-        if (!mbar_wait(&bars->p_full[s], (i >> 1) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (leader) {
-          const uint8_t* pt = smem + kPOff + s * kTileBytes;
-          const uint8_t* vt = smem + kKVOff + s * 2 * kTileBytes + kTileBytes;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint64_t ad = smem_desc_sw128(pt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
-            const uint64_t bd = desc_mn_sw128(vt + k * 16 * 128);
-            tc_mma_bf16(tO, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
-          }
-          tc_commit(&bars->pv_done[s]);
-          tc_commit(&bars->kv_empty[s]);
-        }
-        __syncwarp();
-      }
+      if (progressed) idle = 0;
+      else if (++idle > 4 * kWaitLimit) ok = false;
     }
     if (!ok) report_status(kDevTimeoutMma);
     // every MMA of this warp has completed before the TMEM is freed
