@@ -223,3 +223,18 @@ def test_moe_continuous_mixed_steps():
     assert {rid: len(f) for rid, f in frames.items()} == want
     cr.sched.check()
     assert cr.sched.stats()["free_pages"] == 63 and cr.device_status() == 0
+
+
+def test_retraction_under_a_small_pool():
+    """A pool too small for every stream's full context with no reserve: the scheduler
+    retracts streams, their rows are compacted away, they come back as new prefills of
+    their whole context and still produce exactly their frames; every page returns."""
+    cr = build(max_batch=8, num_pages=24, max_prefill=256, reserve_ratio=0.0)
+    arrivals = {0: [(i, 40 + 9 * i, 14) for i in range(6)]}
+    want = {rid: F for v in arrivals.values() for rid, _, F in v}
+    frames = run_to_end(cr, arrivals, check_state=True, max_steps=600)
+    assert {rid: len(f) for rid, f in frames.items()} == want
+    st = cr.sched.stats()
+    assert st["retracted"] > 0
+    assert st["free_pages"] == 23 and st["finished"] == 6
+    assert cr.device_status() == 0
