@@ -441,6 +441,32 @@ def run_vocoder(args) -> None:
         gbs = nbytes / secs / 1e9
         print(json.dumps({"kernel": name, "shape": shape, "us": secs * 1e6, "algorithmic_bytes": nbytes,
                           "achieved_gbs": gbs, "peak_gbs": hbm, "frac": gbs / hbm, "peak_kind": kind}))
+    del xs, rs, outs, sums, pads
+
+    # the whole code2wav slot decode: Qwen3-Omni code2wav geometry (transformers' defaults:
+    # 8-layer pre-transformer, decoder_dim 1536, 16 quantizers of 2048), random bf16
+    # weights, 64 streams decoding 10 new frames each (the talker's steady codec chunk),
+    # graph-replayed
+    from transformers.models.qwen3_omni_moe.configuration_qwen3_omni_moe import Qwen3OmniMoeCode2WavConfig
+    from transformers.models.qwen3_omni_moe.modeling_qwen3_omni_moe import Qwen3OmniMoeCode2Wav
+    from omni_b200.code2wav import Qwen3OmniIncrementalCodec
+
+    cfg = Qwen3OmniMoeCode2WavConfig()
+    cfg._attn_implementation = "sdpa"
+    model = Qwen3OmniMoeCode2Wav(cfg).to(device=dev, dtype=bf).eval()
+    codec = Qwen3OmniIncrementalCodec(model)
+    S, NF = 64, 10
+    pool = codec.make_pool(num_slots=S, ring_frames=codec.layout.retained + NF)
+    slots = torch.arange(S, device=dev)
+    codes = torch.randint(0, cfg.codebook_size, (S, cfg.num_quantizers, NF), device=dev)
+    with torch.inference_mode():
+        codec.decode_slots(codes, pool, slots, first_decode=True)
+        t = time_kernel(lambda: codec.decode_slots(codes, pool, slots, first_decode=False), 8)
+    fps = S * NF / t
+    rate = 24000 / codec.samples_per_frame()
+    print(json.dumps({"step": "code2wav slot decode (warm)", "streams": S, "frames_per_decode": NF,
+                      "us": t * 1e6, "frames_per_s": fps, "audio_seconds_per_s": fps / rate,
+                      "state_bytes_per_slot": pool.bytes_per_slot}))
 
 
 def run_config0(args, world: int, rank: int, local_rank: int, dist) -> None:

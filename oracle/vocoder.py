@@ -24,19 +24,20 @@ import torch
 
 def snake_beta(conv_output: torch.Tensor, bias: torch.Tensor, alpha_scale: torch.Tensor,
                inverse_beta: torch.Tensor, residual: torch.Tensor | None = None):
-    """(out, sum) for [B, L, C] activations in bf16 / fp16."""
+    """(out, sum) for [B, L, C] activations in bf16 / fp16 (fp32 / fp64 also, unrounded)."""
     dt = conv_output.dtype
+    wide = torch.float64 if dt == torch.float64 else torch.float32
 
     def r(x: torch.Tensor) -> torch.Tensor:
-        return x.to(dt).float()
+        return x.to(dt).to(wide)
 
-    total = r(conv_output.float() + bias.float())
+    total = r(conv_output.to(wide) + bias.to(wide))
     if residual is not None:
-        total = r(total + residual.float())
-    phase = r(total * alpha_scale.float())
+        total = r(total + residual.to(wide))
+    phase = r(total * alpha_scale.to(wide))
     sine = r(torch.sin(phase))
     sq = r(sine * sine)
-    scaled = r(inverse_beta.float() * sq)
+    scaled = r(inverse_beta.to(wide) * sq)
     return (total + scaled).to(dt), total.to(dt)
 
 
@@ -71,5 +72,6 @@ def overlap_exchange(output: torch.Tensor, overlap_pool: torch.Tensor, slot_inde
     o = int(overlap_pool.shape[1])
     idx = slot_index.long()
     if not is_cold:
-        output[:, :o] = (output[:, :o].float() + overlap_pool.index_select(0, idx).float()).to(output.dtype)
+        wide = torch.float64 if output.dtype == torch.float64 else torch.float32
+        output[:, :o] = (output[:, :o].to(wide) + overlap_pool.index_select(0, idx).to(wide)).to(output.dtype)
     overlap_pool.index_copy_(0, idx, output[:, emitted_samples:emitted_samples + o].clone())
