@@ -513,6 +513,19 @@ OMNI_API int omni_clamped_single_output_conv(const void* padded, int64_t padded_
                                              const void* bias, void* out, int64_t batch, int64_t length,
                                              int64_t channels, int32_t taps, int32_t dtype, void* stream);
 
+/* The windows a causal conv reads, as the rows of its GEMM operand:
+ * out[r * length + t, j * channels + c] = padded[r, t + j * dilation, c] for taps j.
+ *   padded [rows, padded_samples, channels] channels-last (row stride padded_row_stride
+ *   elements, samples contiguous), padded_samples >= length + (taps - 1) * dilation;
+ *   out [rows * length, taps * channels] contiguous.  channels x element_bytes, the row
+ *   stride in bytes and both pointers are 16-byte multiples.  No counterpart in the
+ *   reference, whose convs run on cuDNN's channels-last convolution
+ *   (sglang_omni/utils/channels_last_conv.py); here the code2wav's causal convs run as one
+ *   cuBLAS GEMM over these windows. */
+OMNI_API int omni_conv_window_gather(const void* padded, int64_t padded_row_stride, int64_t padded_samples,
+                                     int64_t rows, int64_t length, int32_t taps, int32_t dilation, int32_t channels,
+                                     int32_t element_bytes, void* out, void* stream);
+
 /* Causal-conv state: padded [rows, history + new + tail, channels] gets each row's slot
  * history in front (zeros for a cold slot) and zeros after the new samples; the slot
  * keeps the last `history` samples of (history ++ new).  history <= 64.  Replaces

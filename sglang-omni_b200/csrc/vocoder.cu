@@ -19,6 +19,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "capi_util.h"
 #include "common.cuh"
 
@@ -270,6 +272,35 @@ __global__ void __launch_bounds__(kChannelBlock * 4) overlap_exchange_kernel(con
 
 bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
 
+// The taps-wide windows of a causal conv's channels-last input, laid out as the rows of
+// the conv's GEMM operand: out[r * length + t, j * C + c] = padded[r, t + j * dilation, c].
+// One 16-byte vector a thread (grid-stride); a window's reads of neighbouring outputs hit
+// L2, so the traffic is one read of the input and one write of the taps-times-larger output.
+struct WindowParams {
+  const uint8_t* padded;
+  uint8_t* out;
+  int64_t row_bytes;       // padded row stride in bytes
+  uint32_t total;          // vectors in out
+  uint32_t seg;            // vectors per sample (channels x element bytes / 16)
+  uint32_t taps, length, dil_bytes_vec;  // dil_bytes_vec: dilation x seg
+};
+
+__global__ void __launch_bounds__(256) conv_window_gather_kernel(const __grid_constant__ WindowParams p) {
+  griddep_wait();
+  griddep_launch();
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < p.total; i += gridDim.x * blockDim.x) {
+    const uint32_t v = i % p.seg;
+    uint32_t rest = i / p.seg;
+    const uint32_t j = rest % p.taps;
+    rest /= p.taps;
+    const uint32_t t = rest % p.length;
+    const uint32_t r = rest / p.length;
+    const uint4* src = reinterpret_cast<const uint4*>(p.padded + (int64_t)r * p.row_bytes) +
+                       ((size_t)t * p.seg + (size_t)j * p.dil_bytes_vec + v);
+    reinterpret_cast<uint4*>(p.out)[i] = *src;
+  }
+}
+
 }  // namespace
 }  // namespace omni
 
@@ -341,6 +372,36 @@ extern "C" OMNI_API int omni_clamped_single_output_conv(const void* padded, int6
   if (dtype == kBF16) return go(single_output_conv_kernel<kBF16>);
   if (dtype == kF16) return go(single_output_conv_kernel<kF16>);
   return go(single_output_conv_kernel<kF32>);
+}
+
+extern "C" OMNI_API int omni_conv_window_gather(const void* padded, int64_t padded_row_stride,
+                                                int64_t padded_samples, int64_t rows, int64_t length, int32_t taps,
+                                                int32_t dilation, int32_t channels, int32_t element_bytes, void* out,
+                                                void* stream) {
+  if (rows < 0 || length < 0 || taps <= 0 || dilation <= 0 || channels <= 0)
+    return set_error(OMNI_ERR_INVALID, "bad conv window shape");
+  if (element_bytes != 2 && element_bytes != 4) return set_error(OMNI_ERR_UNSUPPORTED, "2- or 4-byte elements");
+  if (length + (int64_t)(taps - 1) * dilation > padded_samples || padded_row_stride < padded_samples * channels)
+    return set_error(OMNI_ERR_INVALID, "padded rows must hold length + (taps - 1) x dilation samples");
+  const int64_t seg_bytes = (int64_t)channels * element_bytes;
+  if (seg_bytes % 16 != 0 || (padded_row_stride * element_bytes) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(padded) % 16 != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0)
+    return set_error(OMNI_ERR_UNSUPPORTED, "channels, row stride and pointers must be 16-byte multiples");
+  const int64_t total = rows * length * taps * (seg_bytes / 16);
+  if (total >= ((int64_t)1 << 31)) return set_error(OMNI_ERR_UNSUPPORTED, "output above 32 GiB");
+  if (total == 0) return OMNI_OK;
+  WindowParams p{};
+  p.padded = static_cast<const uint8_t*>(padded);
+  p.out = static_cast<uint8_t*>(out);
+  p.row_bytes = padded_row_stride * element_bytes;
+  p.total = (uint32_t)total;
+  p.seg = (uint32_t)(seg_bytes / 16);
+  p.taps = (uint32_t)taps;
+  p.length = (uint32_t)length;
+  p.dil_bytes_vec = (uint32_t)dilation * p.seg;
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 8);
+  return check_launch(launch(conv_window_gather_kernel, dim3((unsigned)blocks), dim3(256), 0,
+                             static_cast<cudaStream_t>(stream), p));
 }
 
 extern "C" OMNI_API int omni_history_exchange(void* padded, int64_t padded_row_stride, int64_t padded_sample_stride,

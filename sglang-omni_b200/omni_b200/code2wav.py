@@ -26,8 +26,9 @@ the whole-sequence forward trims it.
 Activations stay channels last ([rows, samples, channels]); every SnakeBeta runs fused
 with the bias and residual adds in front of it (`fused_bias_snake_beta`) and writes
 straight into the next conv's padded input; the last conv is the clamped
-single-output-channel kernel.  The GEMMs, convolutions and the windowed attention are
-cuBLAS / cuDNN / SDPA calls.
+single-output-channel kernel.  Ungrouped convs and transposed convs run as cuBLAS GEMMs
+over channels-last windows; the ConvNeXt depthwise conv is a cuDNN call and the windowed
+attention an SDPA call.
 """
 
 from __future__ import annotations
@@ -45,12 +46,13 @@ def default_kernels() -> SimpleNamespace:
     from omni_b200 import _lib
     from omni_b200.kernels.bias_snake_beta import SnakeBetaCoefficients, fused_bias_snake_beta
     from omni_b200.kernels.codec_state import history_exchange, overlap_exchange
+    from omni_b200.kernels.conv_window import conv_window_gather
     from omni_b200.kernels.single_output_conv import clamped_single_output_conv
 
     _lib.load()
     return SimpleNamespace(coefficients=SnakeBetaCoefficients.from_activation, snake=fused_bias_snake_beta,
                            history_exchange=history_exchange, overlap_exchange=overlap_exchange,
-                           single_output_conv=clamped_single_output_conv)
+                           single_output_conv=clamped_single_output_conv, conv_windows=conv_window_gather)
 
 
 @dataclass(frozen=True)
@@ -187,6 +189,7 @@ class Qwen3OmniIncrementalCodec:
             for s1, _, s2, _ in units:
                 acts += [s1, s2]
         self.snake = {id(a): self.k.coefficients(a) for a in acts}
+        self._weights: dict[int, torch.Tensor] = {}
 
     def make_pool(self, *, num_slots: int, ring_frames: int, device=None, dtype=None) -> CodecStatePool:
         p = next(self.codec.parameters())
@@ -235,21 +238,55 @@ class Qwen3OmniIncrementalCodec:
         buf = like.new_empty(rows, c.history + length, c.conv.in_channels)
         return buf, buf[:, c.history:]
 
+    def _gemm_weight(self, conv) -> torch.Tensor:
+        """A conv's weight as the [taps x C_in, C_out] (causal conv) or [C_in, taps x
+        C_out] (transposed conv) matrix of its GEMM form, made once."""
+        w = self._weights.get(id(conv))
+        if w is None:
+            if isinstance(conv, torch.nn.ConvTranspose1d):      # [C_in, C_out, taps]
+                w = conv.weight.permute(0, 2, 1).reshape(conv.in_channels, -1).contiguous()
+            else:                                               # [C_out, C_in, taps]
+                w = conv.weight.permute(2, 1, 0).reshape(-1, conv.out_channels).contiguous()
+            self._weights[id(conv)] = w
+        return w
+
     def _conv(self, c: _CausalConv, padded: torch.Tensor, pool, slots, length: int, cold: bool):
         """The causal conv's [rows, length, C_out] outputs without bias, its padded input's
-        history exchanged with the slots first."""
+        history exchanged with the slots first.  Ungrouped convs run as one GEMM over the
+        taps-wide window of the channels-last input (output t reads padded samples t,
+        t + dilation, ...), which keeps the activations channels last."""
         if c.history:
             self.k.history_exchange(padded, pool.histories[c.key], slots, new_samples=length, is_cold=cold)
         conv = c.conv
-        y = F.conv1d(padded.transpose(1, 2), conv.weight, None, 1, 0, conv.dilation, conv.groups)
-        return y.transpose(1, 2).contiguous()
+        if conv.groups != 1:
+            y = F.conv1d(padded.transpose(1, 2), conv.weight, None, 1, 0, conv.dilation, conv.groups)
+            return y.transpose(1, 2).contiguous()
+        rows, taps = padded.shape[0], conv.kernel_size[0]
+        window = padded if taps == 1 else self.k.conv_windows(padded, length, taps, conv.dilation[0])
+        y = window.reshape(rows * length, -1) @ self._gemm_weight(conv)
+        return y.view(rows, length, conv.out_channels)
 
     def _transconv(self, t: _TransConv, frames: torch.Tensor, pool, slots, cold: bool):
         """The transposed conv's emitted samples without bias: the slots' overlap added in
-        front, the samples past the emitted ones kept, the left pad dropped on a first decode."""
-        y = F.conv_transpose1d(frames.transpose(1, 2), t.conv.weight, None, t.stride)
-        y = y.transpose(1, 2).contiguous()
-        emitted = frames.shape[1] * t.stride
+        front, the samples past the emitted ones kept, the left pad dropped on a first decode.
+        One GEMM gives every input frame's taps x C_out contributions; with taps = 2 x stride
+        frame i writes output blocks i (first stride taps) and i + 1 (the rest), summed in
+        fp32 (fp64 for fp64 activations)."""
+        rows, n, _ = frames.shape
+        conv, s = t.conv, t.stride
+        taps, cout = conv.kernel_size[0], conv.out_channels
+        z = (frames.reshape(rows * n, -1) @ self._gemm_weight(conv)).view(rows, n, taps, cout)
+        if taps == s:
+            y = z.reshape(rows, n * s, cout)
+        elif taps == 2 * s:
+            wide = torch.float64 if z.dtype == torch.float64 else torch.float32
+            acc = z.new_zeros(rows, n + 1, s, cout, dtype=wide)
+            acc[:, :n] += z[:, :, :s]
+            acc[:, 1:] += z[:, :, s:]
+            y = acc.to(z.dtype).view(rows, (n + 1) * s, cout)
+        else:
+            raise ValueError("code2wav transposed convs have taps = stride or 2 x stride")
+        emitted = n * s
         if t.overlap:
             self.k.overlap_exchange(y, pool.overlaps[t.key], slots, emitted_samples=emitted, is_cold=cold)
         return y[:, (t.left_trim if cold else 0):emitted]

@@ -11,8 +11,10 @@ import torch
 from oracle import vocoder as ov
 
 
+# decoder_dim 128: the last decoder block has 8 channels, the fewest the library's
+# SnakeBeta kernel takes (16-byte vectors of bf16)
 def small_code2wav(seed: int = 0, *, hidden=64, heads=4, kv_heads=2, layers=2, window=8, quantizers=4,
-                   codebook=32, decoder_dim=96, rates=(8, 5, 4, 3), gain=1.0):
+                   codebook=32, decoder_dim=128, rates=(8, 5, 4, 3), gain=1.0):
     from transformers.models.qwen3_omni_moe.configuration_qwen3_omni_moe import Qwen3OmniMoeCode2WavConfig
     from transformers.models.qwen3_omni_moe.modeling_qwen3_omni_moe import Qwen3OmniMoeCode2Wav
 
@@ -61,8 +63,14 @@ def oracle_kernels() -> SimpleNamespace:
     def single(padded, conv, length):
         return ov.single_output_conv(padded, conv.weight, conv.bias, length)
 
+    def windows(padded, length, taps, dilation):
+        rows, samples, ch = padded.shape
+        view = padded.as_strided((rows, length, taps, ch), (padded.stride(0), ch, dilation * ch, 1),
+                                 padded.storage_offset())
+        return view.reshape(rows * length, taps * ch)
+
     return SimpleNamespace(coefficients=coefficients, snake=snake, history_exchange=ov.history_exchange,
-                           overlap_exchange=ov.overlap_exchange, single_output_conv=single)
+                           overlap_exchange=ov.overlap_exchange, single_output_conv=single, conv_windows=windows)
 
 
 def decode_in_chunks(codec, pool, codes: torch.Tensor, slots: torch.Tensor, splits) -> torch.Tensor:

@@ -136,3 +136,25 @@ def test_overlap_exchange_matches_the_oracle(overlap, emitted, dtype):
         torch.cuda.synchronize()
         assert torch.equal(dev.cpu(), out)
         assert torch.equal(pool_dev.cpu(), pool_ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("channels,taps,dilation", [(96, 7, 1), (384, 7, 3), (768, 7, 9), (8, 7, 9), (192, 1, 1)])
+def test_conv_window_gather_is_the_strided_window_copy(dtype, channels, taps, dilation):
+    from omni_b200.kernels.conv_window import conv_window_gather
+
+    torch.manual_seed(0)
+    rows, length = 5, 37
+    history = (taps - 1) * dilation
+    padded = torch.randn(rows, history + length, channels, device=DEV).to(dtype)
+    got = conv_window_gather(padded, length, taps, dilation)
+    want = padded.as_strided((rows, length, taps, channels), (padded.stride(0), channels, dilation * channels, 1))
+    assert torch.equal(got, want.reshape(rows * length, taps * channels))
+
+
+def test_conv_window_gather_rejects_a_short_input():
+    from omni_b200.kernels.conv_window import conv_window_gather
+
+    padded = torch.zeros(2, 10, 96, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        conv_window_gather(padded, 8, 7, 1)
