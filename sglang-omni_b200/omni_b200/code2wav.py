@@ -270,8 +270,9 @@ class Qwen3OmniIncrementalCodec:
         """The transposed conv's emitted samples without bias: the slots' overlap added in
         front, the samples past the emitted ones kept, the left pad dropped on a first decode.
         One GEMM gives every input frame's taps x C_out contributions; with taps = 2 x stride
-        frame i writes output blocks i (first stride taps) and i + 1 (the rest), summed in
-        fp32 (fp64 for fp64 activations)."""
+        frame i writes output blocks i (first stride taps) and i + 1 (the rest); the two
+        contributions are added once, in the activations' dtype (torch adds bf16 in fp32
+        and rounds once)."""
         rows, n, _ = frames.shape
         conv, s = t.conv, t.stride
         taps, cout = conv.kernel_size[0], conv.out_channels
@@ -279,11 +280,11 @@ class Qwen3OmniIncrementalCodec:
         if taps == s:
             y = z.reshape(rows, n * s, cout)
         elif taps == 2 * s:
-            wide = torch.float64 if z.dtype == torch.float64 else torch.float32
-            acc = z.new_zeros(rows, n + 1, s, cout, dtype=wide)
-            acc[:, :n] += z[:, :, :s]
-            acc[:, 1:] += z[:, :, s:]
-            y = acc.to(z.dtype).view(rows, (n + 1) * s, cout)
+            y = z.new_empty(rows, n + 1, s, cout)
+            y[:, :n].copy_(z[:, :, :s])
+            y[:, n].zero_()
+            y[:, 1:].add_(z[:, :, s:])
+            y = y.view(rows, (n + 1) * s, cout)
         else:
             raise ValueError("code2wav transposed convs have taps = stride or 2 x stride")
         emitted = n * s
