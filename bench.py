@@ -467,6 +467,17 @@ def run_vocoder(args) -> None:
     print(json.dumps({"step": "code2wav slot decode (warm)", "streams": S, "frames_per_decode": NF,
                       "us": t * 1e6, "frames_per_s": fps, "audio_seconds_per_s": fps / rate,
                       "state_bytes_per_slot": pool.bytes_per_slot}))
+    if args.profile:
+        # device time per kernel over 3 eager decodes (torch profiler, CUDA activity)
+        from torch.profiler import ProfilerActivity, profile
+
+        with torch.inference_mode():
+            torch.cuda.synchronize()
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                for _ in range(3):
+                    codec.decode_slots(codes, pool, slots, first_decode=False)
+                torch.cuda.synchronize()
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=16, max_name_column_width=60))
 
 
 def run_config0(args, world: int, rank: int, local_rank: int, dist) -> None:
@@ -757,6 +768,8 @@ def main() -> None:
                     help="with --config 4: prefill-coalescing gate (requests; <= 1 turns it off)")
     ap.add_argument("--vocoder", action="store_true",
                     help="time the streaming vocoder step's kernels (one JSON line each) and exit")
+    ap.add_argument("--profile", action="store_true",
+                    help="with --vocoder: print the code2wav decode's device time per kernel")
     args = ap.parse_args()
     if args.vocoder:
         run_vocoder(args)
