@@ -42,6 +42,10 @@ OMNI_API const char* omni_last_error(void);
 
 /* Sticky device status written by bounded waits that gave up (0 = none).
  * reset != 0 clears it.  Synchronous: reads device memory. */
+#define OMNI_DEV_TIMEOUT_TMA 0x100u  /* a wait for copies into shared memory gave up */
+#define OMNI_DEV_TIMEOUT_MMA 0x200u  /* a wait for tensor-core work gave up */
+#define OMNI_DEV_BAD_INDEX 0x300u    /* an index outside its table was skipped */
+#define OMNI_DEV_TIMEOUT_FLAG 0x400u /* a wait on a flag in global memory gave up */
 OMNI_API unsigned int omni_device_status(int reset);
 
 /* ======================================================================== */
@@ -270,6 +274,8 @@ OMNI_API int omni_qknorm_rope_store(const void* qkv, int64_t qkv_stride, int64_t
 /* Attention                                                                */
 /* ======================================================================== */
 
+/* Workspace bytes of omni_paged_decode_attention; -1 for negative sizes or a
+ * byte count beyond 2^60 (the entry points reject those with OMNI_ERR_INVALID). */
 OMNI_API int64_t omni_paged_attention_workspace_bytes(int64_t rows, int32_t num_kv_heads, int64_t work_capacity);
 
 /* Paged-KV GQA decode attention (RadixAttention decode, thinker_model.py:373-379).
@@ -281,8 +287,9 @@ OMNI_API int64_t omni_paged_attention_workspace_bytes(int64_t rows, int32_t num_
  *   second launch.  work_capacity = partial segments the workspace holds: at least
  *   rows + ranges - 1 (fewer ranges are used when it is smaller).  workspace:
  *   omni_paged_attention_workspace_bytes(rows, Hkv, work_capacity), 256-byte aligned.
- *   work_indptr and pages_per_chunk (the chunk list of omni_decode_prepare) are accepted
- *   for interface stability and not read.
+ *   work_indptr and pages_per_chunk are unused: they belonged to a fixed-size chunk
+ *   list that the range partition replaced; they stay in the signature so that
+ *   existing bindings keep working (pass NULL and any positive value).
  *   Programmatic dependent launch: the page table, seq_lens and every KV slot except
  *   each row's newest token are read before the kernel waits on its predecessor, so
  *   they must have been written before the previous kernel on the stream started (the
@@ -303,9 +310,11 @@ OMNI_API int omni_paged_decode_attention(const void* q, int64_t q_stride, const 
  * process exit.  Calls needing more than 8 MiB of scratch
  * (omni_paged_attention_workspace_bytes) fail with OMNI_ERR_CAPACITY.  All
  * calls on a device share the array: calls that overlap on the GPU race.
- * Each call zeroes the merge counters on its stream before the kernel.  The
- * first call on a device resolves the array's address (cudaGetSymbolAddress)
- * with that device current; make it before any stream capture. */
+ * Every call writes the partial outputs it reads in the same call, so the
+ * array needs no clearing between calls (its counter region is reserved and
+ * unused).  The first call on a device resolves the array's address
+ * (cudaGetSymbolAddress) with that device current; make it before any stream
+ * capture. */
 OMNI_API int omni_paged_decode_attention_noalloc(const void* q, int64_t q_stride, const void* k_cache,
                                                  const void* v_cache, const int32_t* page_indptr,
                                                  const int32_t* page_indices, const int64_t* seq_lens,
@@ -545,6 +554,20 @@ OMNI_API int omni_overlap_exchange(void* output, int64_t output_row_stride, int6
                                    int64_t pool_sample_stride, int64_t pool_channel_stride, const int64_t* slot_index,
                                    int64_t rows, int32_t overlap_samples, int32_t emitted_samples, int32_t channels,
                                    int32_t is_cold, int32_t dtype, void* stream);
+
+/* ======================================================================== */
+/* Test hooks                                                               */
+/* ======================================================================== */
+
+/* No counterpart in the reference.  Launches the bf16 store GEMM (omni_linear,
+ * epilogue 0, row-major x [rows, k], w [n, k]) with a producer that issues no
+ * copies and every mbarrier wait bounded by wait_limit polls, so that the waits
+ * run out.  The kernel records OMNI_DEV_TIMEOUT_TMA (or _MMA) in the status word
+ * read by omni_device_status and returns with nothing in flight; y is not
+ * written.  Exists so that tests can show a bounded device wait ending without
+ * faulting the GPU. */
+OMNI_API int omni_gemm_wait_probe(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
+                                  int32_t splits, uint32_t wait_limit, void* stream);
 
 #ifdef __cplusplus
 }

@@ -584,8 +584,14 @@ __global__ void __launch_bounds__(128) predictor_attention_kernel(const uint16_t
 
 using namespace omni;
 
+// -1 for a negative size or one whose byte count would not fit in 2^60.
 extern "C" OMNI_API int64_t omni_paged_attention_workspace_bytes(int64_t rows, int32_t num_kv_heads,
                                                                  int64_t work_capacity) {
+  constexpr int64_t kLimit = int64_t(1) << 60;
+  if (rows < 0 || num_kv_heads <= 0 || work_capacity < 0) return -1;
+  if (rows > kLimit / (4 * (int64_t)num_kv_heads) ||
+      work_capacity > kLimit / ((int64_t)num_kv_heads * kGroup * (kD + 1) * 4 + 256))
+    return -1;
   const int64_t ctr = (rows * num_kv_heads * 4 + 255) / 256 * 256;
   const int64_t lse = (work_capacity * num_kv_heads * kGroup * 4 + 255) / 256 * 256;
   return ctr + lse + work_capacity * num_kv_heads * kGroup * kD * 4;
@@ -605,17 +611,13 @@ extern "C" OMNI_API int omni_paged_decode_attention(const void* q, int64_t q_str
   if ((reinterpret_cast<uintptr_t>(out) & 15) || out_stride % 8 || (reinterpret_cast<uintptr_t>(q) & 3) ||
       q_stride % 2 || (reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15))
     return set_error(OMNI_ERR_UNSUPPORTED, "misaligned attention operands");
-  if (workspace_bytes < omni_paged_attention_workspace_bytes(rows, num_kv_heads, work_capacity) ||
-      (reinterpret_cast<uintptr_t>(workspace) & 255))
+  const int64_t need = omni_paged_attention_workspace_bytes(rows, num_kv_heads, work_capacity);
+  if (need < 0) return set_error(OMNI_ERR_INVALID, "attention workspace size out of range");
+  if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
     return set_error(OMNI_ERR_CAPACITY, "attention workspace too small or misaligned");
   if (rows == 0) return OMNI_OK;
   // one partial segment per (row, CTA page range) piece: at most ctas + rows - 1 of them
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0, v = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    sms = v;
-  }
+  const int sms = device_sm_count();
   // two CTAs per SM over all KV heads
   int64_t ctas = grid_ctas > 0 ? grid_ctas : (2 * sms) / num_kv_heads;
   if (ctas > work_capacity - rows + 1) ctas = work_capacity - rows + 1;
@@ -641,13 +643,11 @@ extern "C" OMNI_API int omni_paged_decode_attention(const void* q, int64_t q_str
   p.part_lse = reinterpret_cast<float*>(ws + ctr);
   p.part_o = reinterpret_cast<float*>(ws + ctr + lse);
   const size_t smem = (size_t)kAttnWarps * kWarpStages * kStageBytes;  // 96 KB of rings (+ combine area)
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return check_launch(e);
-    attr = true;
-  }
+  // the attribute belongs to the device that is current when it is set
+  const cudaError_t e = once_per_device(reinterpret_cast<const void*>(paged_decode_attention_kernel), kAttrSmem, [smem] {
+    return cudaFuncSetAttribute(paged_decode_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  });
+  if (e != cudaSuccess) return check_launch(e);
   (void)work_indptr;
   (void)pages_per_chunk;
   const int rc = check_launch(launch(paged_decode_attention_kernel, dim3((unsigned)ctas, (unsigned)num_kv_heads),
@@ -714,8 +714,10 @@ extern "C" OMNI_API int omni_predictor_attention(const void* q, int64_t q_stride
 //     the process exits;
 //   - all calls on a device share the array, so calls whose kernels overlap on
 //     the GPU (different streams without ordering) race on it; serialise them;
-//   - the scratch also holds per-row counters that the current kernels do not
-//     use (the layout is shared with omni_paged_attention_workspace_bytes).
+//   - the scratch layout is omni_paged_attention_workspace_bytes's: a per-row
+//     counter region that the current kernels neither read nor write, then the
+//     log-sum-exps and partial outputs, which every call rewrites before it
+//     reads them, so nothing needs clearing between calls.
 // The first call on each device looks up the array's device address with
 // cudaGetSymbolAddress while that device is current and caches it; make that
 // first call before any stream capture on the device.
@@ -737,6 +739,7 @@ extern "C" OMNI_API int omni_paged_decode_attention_noalloc(
     int64_t work_capacity, float sm_scale, void* out, int64_t out_stride, int32_t grid_ctas, void* stream) {
   if (rows < 0 || num_kv_heads <= 0 || work_capacity < 0) return set_error(OMNI_ERR_INVALID, "bad attention shape");
   const int64_t need = omni_paged_attention_workspace_bytes(rows, num_kv_heads, work_capacity);
+  if (need < 0) return set_error(OMNI_ERR_INVALID, "attention scratch size out of range");
   if (need > (int64_t)kNoAllocScratchBytes)
     return set_error(OMNI_ERR_CAPACITY,
                      "scratch need exceeds the 8 MiB built-in array of the allocation-free attention entry point");

@@ -3,8 +3,10 @@
 #include <cstdlib>
 #include <cstring>
 #include <cstdio>
+#include <map>
 #include <mutex>
-#include <unordered_set>
+#include <set>
+#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -50,17 +52,52 @@ bool pdl_enabled() {
   return enabled != 0;
 }
 
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return dev;
+}
+
+int device_sm_count() {
+  static std::mutex mu;
+  static std::map<int, int> sms;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> g(mu);
+  auto it = sms.find(dev);
+  if (it != sms.end()) return it->second;
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) {
+    cudaGetLastError();
+    return 148;  // not cached: asked again on the next call
+  }
+  sms[dev] = v;
+  return v;
+}
+
+cudaError_t once_per_device(const void* kernel, int what, const std::function<cudaError_t()>& set) {
+  static std::mutex mu;
+  static std::set<std::pair<std::pair<const void*, int>, int>> done;
+  const auto key = std::make_pair(std::make_pair(kernel, what), current_device());
+  std::lock_guard<std::mutex> g(mu);
+  if (done.count(key)) return cudaSuccess;
+  const cudaError_t e = set();
+  if (e == cudaSuccess) done.insert(key);
+  return e;
+}
+
 // Every kernel of the library asks for the largest shared-memory carveout, so
 // that all SMs keep one L1/shared split: an SM can only change its split while
 // it is idle, so kernels that prefer different splits cannot overlap through
 // programmatic dependent launch.
 void prefer_max_shared(const void* fn) {
-  static std::mutex mu;
-  static std::unordered_set<const void*> done;
-  std::lock_guard<std::mutex> g(mu);
-  if (!done.insert(fn).second) return;
-  cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-  cudaGetLastError();
+  const cudaError_t e = once_per_device(fn, kAttrCarveout, [fn] {
+    return cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                (int)cudaSharedmemCarveoutMaxShared);
+  });
+  if (e != cudaSuccess) cudaGetLastError();
 }
 
 }  // namespace omni

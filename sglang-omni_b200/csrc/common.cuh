@@ -122,8 +122,8 @@ OMNI_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait: about a second of polling at most (try_wait itself suspends
 // for a hardware-defined interval).  Returns false on timeout.
 constexpr uint32_t kWaitLimit = 1u << 22;
-OMNI_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+OMNI_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = kWaitLimit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
   }
   return false;

@@ -22,7 +22,8 @@
 // (Distributed shared memory moves about 12-16 bytes a cycle per SM here,
 // which made a shared-memory exchange of 32 KB per CTA cost about 1.5 us.)
 // The epilogue operands of the owned rows (RMSNorm scale, rotary position, KV
-// slot, residual) are fetched while the MMAs run.  No global scratch memory.
+// slot, residual) are fetched while the MMAs run.  The only global scratch is
+// the slab array above; the entry points take no workspace.
 //
 // Programmatic dependent launch: weights never depend on the previous kernel,
 // so the producer issues the first stages' weight loads before
@@ -36,7 +37,9 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "capi_util.h"
 #include "common.cuh"
@@ -95,6 +98,10 @@ struct GemmParams {
   int32_t* topk_ids;
   float* topk_w;
   int top_k;
+  // test hook (omni_gemm_wait_probe): polls per bounded wait (0 = kWaitLimit) and
+  // a producer that issues no copies, so that the waits run out
+  uint32_t wait_limit;
+  int withhold_loads;
 };
 
 OMNI_DEVINL uint32_t cluster_ctarank() {
@@ -211,7 +218,8 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   // (one wait for the MMA warp); later stages cycle through the ring on full /
   // empty, starting at phase 0.
   const int pre = nk < ST ? nk : ST;
-  if (warp == 0 && lane == 0) {
+  const uint32_t lim = p.wait_limit ? p.wait_limit : kWaitLimit;
+  if (warp == 0 && lane == 0 && !p.withhold_loads) {
     mbar_arrive_expect_tx(pre_bar, (uint32_t)pre * (a_bytes + b_bytes));
     for (int i = 0; i < pre; ++i) load_w(i, kb_begin + i, pre_bar);
   }
@@ -222,19 +230,19 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
     // producer: the whole warp walks the stages (warp-uniform addresses and
     // phases), one elected lane issues the copies
     const bool leader = elect_one();
-    if (leader)
+    if (leader && !p.withhold_loads)
       for (int i = 0; i < pre; ++i) tma_load_2d(b_smem + i * b_bytes, &tmap_x, pre_bar, (kb_begin + i) * kBK, row0);
     int s = 0;
     uint32_t ph = 0;
     for (int i = pre; i < nk; ++i) {
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&empty[s], ph))) {
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&empty[s], ph, lim))) {
         if (leader) {
           report_status(kDevTimeoutMma);
           flags[0] = 1;
         }
         break;
       }
-      if (leader) {
+      if (leader && !p.withhold_loads) {
         mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes);
         load_w(s, kb_begin + i, &full[s]);
         tma_load_2d(b_smem + s * b_bytes, &tmap_x, &full[s], (kb_begin + i) * kBK, row0);
@@ -251,7 +259,7 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
     // A = W (128 features on M), B = X (the tile's rows on N)
     const uint32_t idesc = idesc_bf16_f32(kTileN, Rt);
     const uint64_t wd0 = smem_desc_sw128(a_smem), xd0 = smem_desc_sw128(b_smem);
-    bool ok = nk == 0 || __all_sync(0xFFFFFFFFu, mbar_wait(pre_bar, 0));
+    bool ok = nk == 0 || __all_sync(0xFFFFFFFFu, mbar_wait(pre_bar, 0, lim));
     if (!ok && leader) {
       report_status(kDevTimeoutTma);
       flags[0] = 1;
@@ -259,7 +267,7 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
     int s = 0;
     uint32_t ph = 0;
     for (int i = 0; ok && i < nk; ++i) {
-      if (i >= pre && !__all_sync(0xFFFFFFFFu, mbar_wait(&full[s], ph))) {
+      if (i >= pre && !__all_sync(0xFFFFFFFFu, mbar_wait(&full[s], ph, lim))) {
         if (leader) {
           report_status(kDevTimeoutTma);
           flags[0] = 1;
@@ -319,7 +327,7 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   // ---- accumulators: TMEM -> this split's slab (S > 1) or shared memory (S = 1) ----
   const bool have_acc = nk > 0;
   if (have_acc) {
-    if (!mbar_wait(mma_done, 0)) {
+    if (!mbar_wait(mma_done, 0, lim)) {
       report_status(kDevTimeoutMma);
       flags[0] = 1;
     }
@@ -636,40 +644,32 @@ struct Plan {
   size_t smem;
 };
 
-int num_sms() {
-  static int n = [] {
-    int dev = 0, v = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    return v;
-  }();
-  return n;
-}
+int num_sms() { return device_sm_count(); }
 
+// Kernel attributes belong to the device that is current when they are set.
 template <int EPI>
 void set_kernel_attrs() {
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    prefer_max_shared(reinterpret_cast<const void*>(gemm_kernel<EPI>));
-  });
+  const void* k = reinterpret_cast<const void*>(gemm_kernel<EPI>);
+  if (once_per_device(k, kAttrSmem, [] {
+        return cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      }) != cudaSuccess)
+    cudaGetLastError();
+  if (once_per_device(k, kAttrCluster, [] {
+        return cudaFuncSetAttribute(gemm_kernel<EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      }) != cudaSuccess)
+    cudaGetLastError();
+  prefer_max_shared(k);
 }
 
 // Co-resident clusters of S CTAs with this much shared memory (cached).
 template <int EPI>
 int max_active_clusters(int S, size_t smem) {
   static std::mutex mu;
-  static int cache[kMaxSplits + 1][64];  // [S][smem KB / 4]
-  static bool init = false;
+  static std::map<std::pair<int, int>, int> cache;  // (device, S * 64 + smem KB / 4)
   std::lock_guard<std::mutex> g(mu);
-  if (!init) {
-    for (auto& row : cache)
-      for (int& v : row) v = -1;
-    init = true;
-  }
   const int key = (int)((smem + 4095) / 4096);
   if (key >= 64) return 0;
-  int& slot = cache[S][key];
+  int& slot = cache.emplace(std::make_pair(current_device(), S * 64 + key), -1).first->second;
   if (slot >= 0) return slot;
   set_kernel_attrs<EPI>();
   cudaLaunchConfig_t cfg = {};
@@ -906,7 +906,7 @@ using namespace omni;
 extern "C" OMNI_API int64_t omni_linear_workspace_bytes(int64_t rows, int64_t k, int64_t n, int32_t epilogue,
                                                         int32_t splits) {
   (void)rows, (void)k, (void)n, (void)epilogue, (void)splits;
-  return 0;  // split-K partials are reduced in the cluster's shared memory
+  return 0;  // split-K partials go through the library's own L2-resident slab array
 }
 
 extern "C" OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w,
@@ -958,4 +958,19 @@ extern "C" OMNI_API int omni_linear_fused(const OmniLinearArgs* a, void* stream)
   gp.top_k = a->top_k;
   return run_linear(a->x, a->rows, a->k, a->x_stride, a->w, a->n, a->epilogue, gp, a->splits,
                     static_cast<cudaStream_t>(stream));
+}
+
+// Test hook: the store GEMM with a producer that issues no copies and waits
+// bounded by wait_limit polls, so that every wait runs out.  The kernel must
+// record kDevTimeoutTma (or kDevTimeoutMma) in the status word and return with
+// nothing in flight; `y` is left unwritten.
+extern "C" OMNI_API int omni_gemm_wait_probe(const void* x, int64_t rows, int64_t k, const void* w, int64_t n,
+                                             void* y, int32_t splits, uint32_t wait_limit, void* stream) {
+  if (wait_limit == 0) return set_error(OMNI_ERR_INVALID, "the probe needs a positive wait limit");
+  GemmParams gp{};
+  gp.y = y;
+  gp.y_stride = n;
+  gp.wait_limit = wait_limit;
+  gp.withhold_loads = 1;
+  return run_linear(x, rows, k, k, w, n, kEpiStore, gp, splits, static_cast<cudaStream_t>(stream));
 }

@@ -700,14 +700,7 @@ bool make_tmap_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int num_sms_moe() {
-  static int n = [] {
-    int dev = 0, v = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    return v;
-  }();
-  return n;
-}
+int num_sms_moe() { return device_sm_count(); }
 
 template <int MODE>
 int launch_grouped(const void* a_q, int64_t rows_cap, int64_t k, const void* w, int64_t experts, int64_t w_rows,
@@ -726,11 +719,10 @@ int launch_grouped(const void* a_q, int64_t rows_cap, int64_t k, const void* w, 
   gp.slots = gp.tmem_cols / gp.slot_cols;
   if (gp.slots > 8) gp.slots = 8;
   const size_t smem = fixed + st * stage_bytes;
-  static std::once_flag once;
-  std::call_once(once, [smem] {
-    (void)smem;
-    cudaFuncSetAttribute(moe_grouped_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  const cudaError_t ae = once_per_device(reinterpret_cast<const void*>(moe_grouped_kernel<MODE>), kAttrSmem, [] {
+    return cudaFuncSetAttribute(moe_grouped_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
+  if (ae != cudaSuccess) return check_launch(ae);
   return check_launch(launch(moe_grouped_kernel<MODE>, dim3((unsigned)num_sms_moe()), dim3(kGroupedThreads), smem,
                              static_cast<cudaStream_t>(stream), tw, ta, gp));
 }
@@ -796,10 +788,10 @@ extern "C" OMNI_API int omni_moe_align_gather_strided(
   const int W = (int)((tokens + 31) / 32);
   const size_t smem = (size_t)experts * (W > 0 ? W : 1) * 4;
   if (smem > 48 * 1024) {
-    static std::once_flag once;
-    std::call_once(once, [] {
-      cudaFuncSetAttribute(moe_align_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    const cudaError_t ae = once_per_device(reinterpret_cast<const void*>(moe_align_gather_kernel), kAttrSmem, [] {
+      return cudaFuncSetAttribute(moe_align_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
     });
+    if (ae != cudaSuccess) return check_launch(ae);
   }
   const int grid = tokens > 0 ? (int)((tokens + 31) / 32) : 1;
   return check_launch(launch(moe_align_gather_kernel, dim3((unsigned)grid), dim3(1024), smem,

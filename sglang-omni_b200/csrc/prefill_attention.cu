@@ -473,10 +473,11 @@ extern "C" OMNI_API int omni_prefill_attention(const void* q, int64_t q_stride, 
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.out = static_cast<uint16_t*>(out);
   p.out_stride = out_stride;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(prefill_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  const cudaError_t ae = once_per_device(reinterpret_cast<const void*>(prefill_attention_tc_kernel), kAttrSmem, [] {
+    return cudaFuncSetAttribute(prefill_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kSmemBytes);
   });
+  if (ae != cudaSuccess) return check_launch(ae);
   return check_launch(launch(prefill_attention_tc_kernel, dim3((unsigned)max_tiles, (unsigned)num_q_heads),
                              dim3(kThreads), kSmemBytes, static_cast<cudaStream_t>(stream), tq, tk, tv, p));
 }

@@ -21,6 +21,12 @@ OMNI_ERR_INVALID = 2
 OMNI_ERR_CAPACITY = 3
 OMNI_ERR_CUDA = 4
 
+# status word of omni_device_status (include/omni_b200.h OMNI_DEV_*)
+OMNI_DEV_TIMEOUT_TMA = 0x100
+OMNI_DEV_TIMEOUT_MMA = 0x200
+OMNI_DEV_BAD_INDEX = 0x300
+OMNI_DEV_TIMEOUT_FLAG = 0x400
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int32
@@ -95,6 +101,7 @@ SIGNATURES: dict[str, list] = {
     "omni_conv_window_gather": [_P, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _P, _P],
     "omni_history_exchange": [_P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _I64, _I32, _I32, _I32, _I32, _I32,
                               _I32, _P],
+    "omni_gemm_wait_probe": [_P, _I64, _I64, _P, _I64, _P, _I32, _U32, _P],
     "omni_overlap_exchange": [_P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _I64, _I32, _I32, _I32, _I32, _I32,
                               _P],
 }

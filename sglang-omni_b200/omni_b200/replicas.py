@@ -10,22 +10,26 @@ reduction (max of the per-rank device times, sum of the frames).
 
 from __future__ import annotations
 
+import itertools
 import threading
+from collections import defaultdict
 
 
 class RoundRobinBinding:
-    """Thread-safe round-robin replica selection per process name."""
+    """Replica choice by arrival order: the i-th stream that a process (the talker
+    stage, say) hands out goes to replica i mod N, whatever its request id.  One
+    arrival counter per process name; safe to call from several threads."""
 
     def __init__(self) -> None:
-        self.counters: dict[str, int] = {}
-        self.lock = threading.Lock()
+        self._arrivals: defaultdict[str, itertools.count] = defaultdict(itertools.count)
+        self._mu = threading.Lock()
 
     def bind(self, process_name: str, num_replicas: int, request_id: str | None = None) -> int:
-        del request_id
-        with self.lock:
-            index = self.counters.get(process_name, 0)
-            self.counters[process_name] = index + 1
-        return index % num_replicas
+        if num_replicas < 1:
+            raise ValueError("num_replicas must be positive")
+        with self._mu:
+            arrival = next(self._arrivals[process_name])
+        return arrival % num_replicas
 
 
 def shard_streams(num_streams: int, world: int, rank: int) -> list[int]:
