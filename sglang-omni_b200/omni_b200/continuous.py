@@ -39,7 +39,7 @@ from omni_b200.config import SamplingParams
 from omni_b200.kv_cache import PageAllocator
 from omni_b200.model_runner import TalkerDecodeRunner
 from omni_b200.scheduler import DECODE, MIXED, OmniScheduler, StepPlan
-from omni_b200.seed import derive_sampling_seed
+from omni_b200.staging import TalkerRequest
 from omni_b200.talker import ExtendForwardBatch
 
 
@@ -155,12 +155,16 @@ class ContinuousTalkerRunner:
             p.output_embeds, p.sub_temperature_tensor, p.sub_top_k_tensor, p.sub_top_p_tensor,
             p.sub_sampling_seed_tensor, p.sub_do_sample_tensor,
         ])
-        ladder = (4, 8, 16, 32, 50, 64, 128, 256, 512, 1024)
-        t.max_top_k = next(w for w in ladder if w >= sampling.top_k)
-        # uniform residual-sampling flags for every row (set_sampling keeps per-row tensors)
-        p.set_sampling(temperature=[sampling.subtalker_temperature] * B, top_k=[sampling.subtalker_top_k] * B,
-                       top_p=[sampling.subtalker_top_p] * B, seeds=[0] * B,
-                       do_sample=[sampling.subtalker_dosample] * B, batch=B)
+        # the batch-wide sampler flags of every row (the per-row tensors are restaged at
+        # admission): the padding rows of a bucket carry this configuration too
+        runner.stage([TalkerRequest(rid=f"pad{i}", seed=0, sampling=sampling) for i in range(runner.max_batch)])
+        runner.requests = []
+        # per-stream request state by stream id: seeds, the layer-0 output ids so far (the
+        # repetition mask of a retracted stream's re-admission carries them), the suppress
+        # row without the leading-silence ids and whether those are still masked
+        self.streams: dict[int, TalkerRequest] = {}
+        self.base_suppress: dict[int, np.ndarray] = {}
+        self.silenced: set[int] = set()
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.graph_pool = None
         self.eager_steps = 0
@@ -178,9 +182,31 @@ class ContinuousTalkerRunner:
                 return b
         raise RuntimeError("batch above the largest decode bucket")
 
-    def _stream_seeds(self, rid: int) -> tuple[int, int]:
-        base = derive_sampling_seed("omni-b200", self.seed, f"req{rid}")
-        return derive_sampling_seed("semantic", base), derive_sampling_seed("subtalker", base)
+    def request(self, rid: int) -> TalkerRequest:
+        """The request state of stream `rid` (synthetic: public seed seed * 1_000_003 + rid)."""
+        rq = self.streams.get(rid)
+        if rq is None:
+            rq = TalkerRequest(rid=f"req{rid}", seed=self.seed * 1_000_003 + rid, sampling=self.sampling, output_ids=[])
+            self.streams[rid] = rq
+        return rq
+
+    def _after_step(self, rids: list[int], codes: np.ndarray, finished) -> None:
+        """Output-id history, leading-silence release and the end of finished streams."""
+        lim = self.runner.codec_control.leading_silence_mask_frames
+        release = []
+        for row, rid in enumerate(rids):
+            rq = self.request(int(rid))
+            rq.output_ids = list(rq.output_ids or []) + [int(codes[row, 0])]
+            if int(rid) in self.silenced and rq.frames >= lim:
+                release.append((row, int(rid)))
+        for row, rid in release:
+            self.runner.talker.suppress_mask[row].copy_(torch.from_numpy(self.base_suppress[rid]))
+            self.silenced.discard(rid)
+        for rid in finished:
+            rid = int(rid)
+            self.streams.pop(rid, None)
+            self.base_suppress.pop(rid, None)
+            self.silenced.discard(rid)
 
     def _stage_text(self, rids: list[int]) -> None:
         n = len(rids)
@@ -221,20 +247,16 @@ class ContinuousTalkerRunner:
         ops.admit_streams(rows=rows, slots=slots, prompt_lens=lens_d, page_indptr=indptr, pages=pages,
                           req_to_token=r.r2t.req_to_token, page_size=r.cfg.page_size, seq_lens=r.seq_lens,
                           req_pool_indices=r.req_pool_indices, status=r.status)
-        # sampling state of the new rows (prepare_decode_buffers for fresh requests)
-        sl = slice(Bd, Bd + n)
-        t.repetition_penalties[sl].fill_(sp.repetition_penalty)
-        t.repetition_mask[sl].zero_()
-        t.suppress_mask[sl].zero_()
-        t.sampling_temperatures[sl].fill_(sp.temperature)
-        t.sampling_top_ks[sl].fill_(sp.top_k)
-        t.sampling_top_ps[sl].fill_(sp.top_p)
-        t.sampling_min_ps[sl].fill_(sp.min_p)
-        seeds = [self._stream_seeds(int(rid)) for rid in plan.new_rid]
-        t.sampling_seeds[sl].copy_(self._h2d("seeds", [s[0] for s in seeds], n))
-        p.set_sampling(temperature=[sp.subtalker_temperature] * n, top_k=[sp.subtalker_top_k] * n,
-                       top_p=[sp.subtalker_top_p] * n, seeds=[s[1] for s in seeds],
-                       do_sample=[sp.subtalker_dosample] * n, batch=n, row0=Bd)
+        # sampling state of the new rows (prepare_decode_buffers): a re-admitted (retracted)
+        # stream's repetition mask carries its whole output history
+        reqs = [self.request(int(rid)) for rid in plan.new_rid]
+        st = r.stage_requests(reqs)
+        r.write_staging(st, row0=Bd)
+        self.h2d_bytes += n * (2 * r.cfg.vocab_size + 48)
+        for i, rid in enumerate(plan.new_rid.tolist()):
+            self.base_suppress[int(rid)] = st.base_suppress_mask[i].copy()
+            if st.silence_rows[i]:
+                self.silenced.add(int(rid))
         # prompt rows of the new streams (compose_prefill_embeds): each stream's rows
         # start at an offset of the host pool chosen by its id
         off = 0
@@ -355,6 +377,7 @@ class ContinuousTalkerRunner:
         rids = rids[:rows]
         codes = self.codes_h[:rows].numpy().copy()
         finished = self.sched.process_batch_result(codes)
+        self._after_step(rids, codes, finished)
         return StepOutput(plan.mode, rids, codes, finished)
 
     def forward_messages(self, relay, backlog: list | None = None) -> list:

@@ -31,7 +31,8 @@ from omni_b200 import ops
 from omni_b200.config import SamplingParams, TalkerConfig
 from omni_b200.kv_cache import PageAllocator, PagedKVPool, ReqToTokenPool
 from omni_b200.predictor import CodePredictor, init_predictor_weights
-from omni_b200.seed import derive_sampling_seed
+from omni_b200.staging import OMNI, TTS, CodecControl, TalkerRequest, layer0_top_k_width, stage_decode_buffers, \
+    synthetic_requests
 from omni_b200.talker import DecodeForwardBatch, DenseTalker, ExtendForwardBatch, init_talker_weights
 
 
@@ -49,10 +50,19 @@ class GenerationBatchResult:
 class TalkerDecodeRunner:
     def __init__(self, cfg: TalkerConfig, *, max_batch: int, num_pages: int, seed: int = 0, device="cuda",
                  pages_per_chunk: int = 32, weights: dict | None = None, predictor_weights: dict | None = None,
-                 expert_parallel: bool = False, max_prefill_tokens: int = 0):
+                 expert_parallel: bool = False, max_prefill_tokens: int = 0, flavor: str | None = None,
+                 codec_control: CodecControl | None = None):
         """max_batch: streams in a step (decode + newly admitted); max_prefill_tokens: extend rows of
-        a mixed step (0 = decode only)."""
+        a mixed step (0 = decode only).  flavor: how requests are staged (omni_b200.staging):
+        "tts" (Qwen3-TTS seeds and codec-control suppression; the default for the dense
+        talker) or "omni" (Qwen3-Omni seeds; the default for the MoE talker)."""
         self.cfg = cfg
+        self.flavor = flavor or (TTS if cfg.moe is None else OMNI)
+        self.codec_control = codec_control or CodecControl()
+        # host mirror of the staged requests of rows [0, len(requests))
+        self.requests: list[TalkerRequest] = []
+        self.silence_rows = np.zeros(0, dtype=bool)
+        self.base_suppress: np.ndarray | None = None
         self.device = torch.device(device)
         self.max_batch = max_batch
         self.pages_per_chunk = pages_per_chunk
@@ -97,13 +107,17 @@ class TalkerDecodeRunner:
     # request admission (synthetic prefill: random KV contents)
     # ------------------------------------------------------------------
     def admit(self, context_lens: list[int], *, sampling: SamplingParams = SamplingParams(), seed: int = 0,
-              request_seeds: list[int] | None = None, fill_kv: bool = True) -> None:
+              requests: list[TalkerRequest] | None = None, fill_kv: bool = True) -> None:
         """Admit len(context_lens) streams whose first context_lens[i] tokens are in the
-        KV pool (pages randomly permuted in the pool), with seeded random KV contents."""
+        KV pool (pages randomly permuted in the pool), with seeded random KV contents.
+        Their sampling state is staged from `requests` (default: seeded synthetic requests
+        with `sampling`, omni_b200.staging.synthetic_requests)."""
         cfg = self.cfg
         B = len(context_lens)
         if B > self.max_batch:
             raise RuntimeError("batch exceeds max_batch")
+        if requests is not None and len(requests) != B:
+            raise ValueError("one request per admitted stream")
         P = cfg.page_size
         rng = np.random.default_rng(seed)
         num_pages = self.kv.num_pages
@@ -129,26 +143,76 @@ class TalkerDecodeRunner:
             for li in range(cfg.num_hidden_layers):
                 self.kv.k_buffer[li].normal_(generator=g)
                 self.kv.v_buffer[li].normal_(generator=g)
-        # sampling state
-        t = self.talker
-        t.repetition_penalties[:B].fill_(sampling.repetition_penalty)
-        t.repetition_mask[:B].zero_()
-        t.suppress_mask[:B].zero_()
-        t.sampling_temperatures[:B].fill_(sampling.temperature)
-        t.sampling_top_ks[:B].fill_(sampling.top_k)
-        t.sampling_top_ps[:B].fill_(sampling.top_p)
-        t.sampling_min_ps[:B].fill_(sampling.min_p)
-        ladder = (4, 8, 16, 32, 50, 64, 128, 256, 512, 1024)
-        t.max_top_k = next(w for w in ladder if w >= sampling.top_k)
-        seeds = request_seeds or [derive_sampling_seed("omni-b200", seed, f"req{i}") for i in range(B)]
-        t.sampling_seeds[:B].copy_(torch.tensor([derive_sampling_seed("semantic", s) for s in seeds]))
-        self.predictor.set_sampling(
-            temperature=[sampling.subtalker_temperature] * B, top_k=[sampling.subtalker_top_k] * B,
-            top_p=[sampling.subtalker_top_p] * B,
-            seeds=[derive_sampling_seed("subtalker", s) for s in seeds],
-            do_sample=[sampling.subtalker_dosample] * B, batch=B)
+        self.requests = []
+        self.stage(requests if requests is not None else synthetic_requests(B, seed=seed, sampling=sampling))
         self.predictor.output_embeds[:B].zero_()
         self.graph = None
+
+    def stage(self, requests: list[TalkerRequest], *, row0: int = 0) -> None:
+        """prepare_decode_buffers for rows row0 .. row0 + len(requests): per-row layer-0
+        sampling parameters, seeds, repetition mask (prior output ids), suppress mask
+        (request tokens; for the TTS flavor the codec control range and leading silence)
+        and the residual sampling rows, per omni_b200.staging."""
+        n = len(requests)
+        if row0 + n > self.max_batch:
+            raise RuntimeError("staged rows exceed max_batch")
+        st = self.stage_requests(requests)
+        self.write_staging(st, row0=row0)
+        # host mirrors: the requests and the rows whose leading-silence ids are still masked
+        self.requests = self.requests[:row0] + list(requests)
+        V = self.cfg.vocab_size
+        base = np.zeros((row0 + n, V), dtype=np.uint8)
+        sil = np.zeros(row0 + n, dtype=bool)
+        if row0 > 0 and self.base_suppress is not None:
+            k = min(row0, self.base_suppress.shape[0])
+            base[:k] = self.base_suppress[:k]
+            sil[:k] = self.silence_rows[:k]
+        base[row0:] = st.base_suppress_mask
+        sil[row0:] = st.silence_rows
+        self.base_suppress, self.silence_rows = base, sil
+
+    def stage_requests(self, requests: list[TalkerRequest]):
+        """The host staging of `requests` under this runner's flavor (omni_b200.staging)."""
+        return stage_decode_buffers(requests, flavor=self.flavor, vocab=self.cfg.vocab_size,
+                                    predictor_vocab=self.cfg.predictor.vocab_size, control=self.codec_control)
+
+    def write_staging(self, st, *, row0: int = 0) -> None:
+        """Copy staged rows (omni_b200.staging.DecodeStaging) into rows row0.. of the
+        step's sampling tensors."""
+        n = st.seeds.shape[0]
+        t = self.talker
+        rows = slice(row0, row0 + n)
+
+        def put(dst, arr):
+            dst[rows].copy_(torch.from_numpy(np.ascontiguousarray(arr)).to(dst.dtype).view(dst[rows].shape),
+                            non_blocking=False)
+
+        put(t.repetition_penalties, st.repetition_penalties)
+        put(t.sampling_temperatures, st.temperatures)
+        put(t.sampling_top_ps, st.top_ps)
+        put(t.sampling_top_ks, st.top_ks)
+        put(t.sampling_min_ps, st.min_ps)
+        put(t.sampling_seeds, st.seeds)
+        put(t.repetition_mask, st.repetition_mask)
+        put(t.suppress_mask, st.suppress_mask)
+        widths = [int(k) for k in st.top_ks] + ([t.max_top_k] if row0 > 0 else [])
+        t.max_top_k = layer0_top_k_width(widths)
+        self.predictor.set_sampling(
+            temperature=st.sub_temperatures, top_k=st.sub_top_ks, top_p=st.sub_top_ps, seeds=st.sub_seeds,
+            do_sample=st.sub_do_sample, batch=n, row0=row0)
+
+    def note_frames(self, layer0_codes: np.ndarray) -> None:
+        """Host bookkeeping after a step: append each row's layer-0 code to its request's
+        output ids and lift the leading-silence mask of rows that have now emitted
+        leading_silence_mask_frames frames (apply_codec_suppress_tokens masks the silence
+        ids while fewer frames exist)."""
+        lim = self.codec_control.leading_silence_mask_frames
+        for i, c in enumerate(np.asarray(layer0_codes).reshape(-1).tolist()[: len(self.requests)]):
+            rq = self.requests[i]
+            rq.output_ids = list(rq.output_ids or []) + [int(c)]
+            if self.silence_rows.size > i and self.silence_rows[i] and rq.frames >= lim:
+                self.talker.suppress_mask[i].copy_(torch.from_numpy(self.base_suppress[i]))
+                self.silence_rows[i] = False
 
     # ------------------------------------------------------------------
     def forward_batch(self) -> DecodeForwardBatch:
@@ -198,7 +262,8 @@ class TalkerDecodeRunner:
     # mixed step: new streams prefilled in the same forward as the decode rows
     # ------------------------------------------------------------------
     def admit_prefill(self, prompt_lens: list[int], *, seed: int = 0,
-                      sampling: SamplingParams = SamplingParams()) -> None:
+                      sampling: SamplingParams = SamplingParams(),
+                      requests: list[TalkerRequest] | None = None) -> None:
         """Admit len(prompt_lens) new streams (rows after the decode streams) whose prompts
         (seeded N(0, 1) embeddings, the rows compose_prefill_embeds would produce) are
         prefilled by every following step's fused forward, their slots reserved in
@@ -243,21 +308,8 @@ class TalkerDecodeRunner:
                                          tile_indptr=self.ext_tiles, max_tiles=max_tiles)
         self.sel_positions = torch.zeros(Bd + n, **i64)
         # per-stream sampling state of the new rows
-        t = self.talker
-        rows = slice(Bd, Bd + n)
-        t.repetition_penalties[rows].fill_(sampling.repetition_penalty)
-        t.repetition_mask[rows].zero_()
-        t.suppress_mask[rows].zero_()
-        t.sampling_temperatures[rows].fill_(sampling.temperature)
-        t.sampling_top_ks[rows].fill_(sampling.top_k)
-        t.sampling_top_ps[rows].fill_(sampling.top_p)
-        t.sampling_min_ps[rows].fill_(sampling.min_p)
-        seeds = [derive_sampling_seed("omni-b200", seed, f"new{i}") for i in range(n)]
-        t.sampling_seeds[rows].copy_(torch.tensor([derive_sampling_seed("semantic", s_) for s_ in seeds]))
-        self.predictor.set_sampling(
-            temperature=[sampling.subtalker_temperature] * n, top_k=[sampling.subtalker_top_k] * n,
-            top_p=[sampling.subtalker_top_p] * n, seeds=[derive_sampling_seed("subtalker", s_) for s_ in seeds],
-            do_sample=[sampling.subtalker_dosample] * n, batch=n, row0=Bd)
+        self.stage(requests if requests is not None else
+                   synthetic_requests(n, seed=seed, sampling=sampling, prefix="new"), row0=Bd)
         self.graph = None
 
     def prepare_extend(self) -> ExtendForwardBatch:
@@ -344,4 +396,6 @@ class TalkerDecodeRunner:
             codes_host = torch.empty((n, self.cfg.predictor.num_code_groups), dtype=torch.long, pin_memory=True)
         codes_host.copy_(self.predictor.output_codes[:n], non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
+        if self.silence_rows.any():
+            self.note_frames(codes_host[:, 0].numpy())
         return codes_host

@@ -116,37 +116,42 @@ class CodePredictor:
     # ------------------------------------------------------------------
     def set_sampling(self, *, temperature, top_k, top_p, seeds, do_sample, batch: int, row0: int = 0) -> None:
         """Stage per-row residual sampling parameters of rows row0 .. row0 + batch
-        (prepare_decode_buffers); with row0 > 0 the batch-wide flags widen to cover both."""
-        dev = self.device
+        (the subtalker rows of prepare_decode_buffers, sglang_model.py:1162-1270): a
+        greedy row is staged as temperature 1, top-p 1, top-k 1, a sampled row's
+        temperature is clamped to at least 1e-5, and the batch signature (ladder width,
+        top-p flag) comes from the sampled rows.  With row0 > 0 the batch-wide flags
+        widen to cover both parts."""
+        from omni_b200.staging import predictor_signature
+
         rows = slice(row0, row0 + batch)
-        self.sub_temperature_tensor[rows].copy_(torch.as_tensor(temperature, dtype=torch.float32), non_blocking=True)
-        self.sub_top_k_tensor[rows].copy_(torch.as_tensor(top_k, dtype=torch.long), non_blocking=True)
-        self.sub_top_p_tensor[rows].copy_(torch.as_tensor(top_p, dtype=torch.float32), non_blocking=True)
+        ds = [bool(v) for v in torch.as_tensor(do_sample).reshape(-1).tolist()]
+        t_in = [float(v) for v in torch.as_tensor(temperature, dtype=torch.float64).reshape(-1).tolist()]
+        k_in = [int(v) for v in torch.as_tensor(top_k).reshape(-1).tolist()]
+        p_in = [float(v) for v in torch.as_tensor(top_p, dtype=torch.float64).reshape(-1).tolist()]
+        temps = [max(t, 1e-5) if d else 1.0 for t, d in zip(t_in, ds)]
+        ks = [k if d else 1 for k, d in zip(k_in, ds)]
+        ps = [p if d else 1.0 for p, d in zip(p_in, ds)]
+        self.sub_temperature_tensor[rows].copy_(torch.tensor(temps, dtype=torch.float32), non_blocking=True)
+        self.sub_top_k_tensor[rows].copy_(torch.tensor(ks, dtype=torch.long), non_blocking=True)
+        self.sub_top_p_tensor[rows].copy_(torch.tensor(ps, dtype=torch.float32), non_blocking=True)
         self.sub_sampling_seed_tensor[rows].copy_(torch.as_tensor(seeds, dtype=torch.long), non_blocking=True)
-        ds = torch.as_tensor(do_sample, dtype=torch.uint8)
-        self.sub_do_sample_tensor[rows].copy_(ds, non_blocking=True)
+        self.sub_do_sample_tensor[rows].copy_(torch.tensor(ds, dtype=torch.uint8), non_blocking=True)
         prev = (self.sub_has_sampled_rows, self.sub_has_argmax_rows, self.sub_sampled_max_top_k,
                 self.sub_sampled_has_top_p) if row0 > 0 else None
-        top_k_list = [int(k) for k in torch.as_tensor(top_k).reshape(-1).tolist()]
-        top_p_list = [float(p) for p in torch.as_tensor(top_p).reshape(-1).tolist()]
-        ds_list = [bool(v) for v in ds.reshape(-1).tolist()]
-        sampled = [i for i, d in enumerate(ds_list) if d]
-        self.sub_has_sampled_rows = bool(sampled)
-        self.sub_has_argmax_rows = len(sampled) != len(ds_list)
-        bounded = [top_k_list[i] for i in sampled if 0 < top_k_list[i] < self.cfg.vocab_size]
-        if len(bounded) != len(sampled):
+        sampled = [i for i, d in enumerate(ds) if d]
+        sig = predictor_signature([ks[i] for i in sampled], [ps[i] for i in sampled], self.cfg.vocab_size)
+        if sig["has_unbounded_top_k"]:
             raise ValueError("unbounded subtalker top_k is outside the fused sampler's contract")
-        widest = max(bounded, default=4)
-        ladder = (4, 8, 16, 32, 50, 64, 128, 256, 512, 1024)
-        self.sub_sampled_max_top_k = next(w for w in ladder if w >= widest)
-        self.sub_sampled_has_top_p = any(0.0 < top_p_list[i] < 1.0 for i in sampled)
+        self.sub_has_sampled_rows = bool(sampled)
+        self.sub_has_argmax_rows = len(sampled) != len(ds)
+        self.sub_sampled_max_top_k = sig["max_top_k"] if sampled else 4
+        self.sub_sampled_has_top_p = sig["has_top_p"]
         if prev is not None:
             self.sub_has_sampled_rows = self.sub_has_sampled_rows or prev[0]
             self.sub_has_argmax_rows = self.sub_has_argmax_rows or prev[1]
             self.sub_sampled_max_top_k = max(self.sub_sampled_max_top_k, prev[2])
             self.sub_sampled_has_top_p = self.sub_sampled_has_top_p or prev[3]
         assert fused_raw_logit_block_k(self.sub_sampled_max_top_k) is not None
-        del dev
 
     # ------------------------------------------------------------------
     def forward_tokens(self, x: torch.Tensor, x_ss: torch.Tensor, *, batch: int, tokens: int,

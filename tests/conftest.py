@@ -42,6 +42,17 @@ def golden():
     return json.loads((GOLDEN / "reference_golden.json").read_text())
 
 
+@pytest.fixture(scope="session")
+def staging_golden():
+    return json.loads((GOLDEN / "staging_golden.json").read_text())
+
+
+@pytest.fixture(scope="session")
+def sampler_scale_golden():
+    with np.load(GOLDEN / "sampler_scale_golden.npz") as z:
+        return {k: z[k].astype(np.int64) for k in z.files}
+
+
 def decode_bf16_b64(case) -> np.ndarray:
     raw = base64.b64decode(case["logits_bf16_b64"])
     return np.frombuffer(raw, dtype="<u2").reshape(case["shape"]).copy()

@@ -79,20 +79,26 @@ def test_extend_prepare_matches_oracle():
     assert got["tile_indptr"].cpu().numpy().tolist() == tp.tolist()
 
 
-@pytest.mark.parametrize("hq,hkv", [(16, 2), (8, 8)])
-def test_prefill_attention_matches_fp32(hq, hkv):
+# config 2's prompt lengths reach 4096: the key-tile ring wraps many times
+LONG_STREAMS = [(0, 4096), (0, 2048), (0, 3001), (300, 2500), (0, 64), (4000, 96)]
+
+
+@pytest.mark.parametrize("hq,hkv,streams", [(16, 2, STREAMS), (8, 8, STREAMS), (16, 2, LONG_STREAMS)],
+                         ids=["gqa", "mha", "long-prompts"])
+def test_prefill_attention_matches_fp32(hq, hkv, streams):
     from omni_b200 import ops
 
+    STREAMS_ = streams
     D = 128
-    r2t, req, num_pages = _reserve(STREAMS, 512, 1)
-    pk = _pack(STREAMS, r2t, req)
+    r2t, req, num_pages = _reserve(STREAMS_, 8192, 1)
+    pk = _pack(STREAMS_, r2t, req)
     g = torch.Generator(device=DEV).manual_seed(3)
     kc = torch.randn(num_pages * P, hkv, D, generator=g, device=DEV).to(torch.bfloat16)
     vc = torch.randn(num_pages * P, hkv, D, generator=g, device=DEV).to(torch.bfloat16)
-    total = sum(s[1] for s in STREAMS)
+    total = sum(s[1] for s in STREAMS_)
     q = torch.randn(total, hq * D, generator=g, device=DEV).to(torch.bfloat16)
     out = torch.full((total, hq * D), float("nan"), device=DEV, dtype=torch.bfloat16)
-    max_tiles = sum(math.ceil(s[1] / ops.PREFILL_Q_TILE) for s in STREAMS)
+    max_tiles = sum(math.ceil(s[1] / ops.PREFILL_Q_TILE) for s in STREAMS_)
     scale = 1 / math.sqrt(D)
     ops.prefill_attention(q, kc, vc, qo_indptr=pk["qo_indptr"], seq_lens=pk["seq_lens"],
                           page_indptr=pk["page_indptr"], page_indices=pk["page_indices"],
@@ -103,16 +109,16 @@ def test_prefill_attention_matches_fp32(hq, hkv):
     qf = q.float().cpu().view(total, hq, D)
     kf, vf = kc.float().cpu(), vc.float().cpu()
     q0 = 0
-    for i, (pre, ext) in enumerate(STREAMS):
+    for i, (pre, ext) in enumerate(STREAMS_):
         L = pre + ext
         slots = torch.from_numpy(r2t[req[i], :L].astype(np.int64))
-        k = kf[slots].repeat_interleave(hq // hkv, 1)  # [L, hq, D]
-        v = vf[slots].repeat_interleave(hq // hkv, 1)
-        qq = qf[q0: q0 + ext]  # [ext, hq, D]
-        s = torch.einsum("qhd,khd->hqk", qq, k) * scale
         mask = torch.arange(L)[None, :] > (pre + torch.arange(ext))[:, None]
-        s = s.masked_fill(mask[None], float("-inf"))
-        ref[q0: q0 + ext] = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v)
+        for h in range(hq):  # one head at a time keeps the [ext, L] scores small
+            k = kf[slots, h // (hq // hkv)]  # [L, D]
+            v = vf[slots, h // (hq // hkv)]
+            s_ = (qf[q0: q0 + ext, h] @ k.t()) * scale
+            s_ = s_.masked_fill(mask, float("-inf"))
+            ref[q0: q0 + ext, h] = torch.softmax(s_, -1) @ v
         q0 += ext
     got = out.float().cpu().view(total, hq, D)
     assert torch.isfinite(got).all()

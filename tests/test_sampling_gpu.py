@@ -105,6 +105,25 @@ def test_sampler_matches_reference_golden(golden):
         assert got.tolist() == case["tokens"], case["id"]
 
 
+@pytest.mark.parametrize("name", ["config0", "config3"])
+def test_sampler_reproduces_the_reference_at_scale(name, sampler_scale_golden):
+    """12 000 rows of untied random bf16 logits at the config-0 / config-3 sampling
+    parameters (tests/golden/scale_inputs.py): every token equals the one the
+    reference's own torch sampler drew (tests/golden/make_golden.py)."""
+    import sys
+
+    from conftest import GOLDEN
+
+    sys.path.insert(0, str(GOLDEN))
+    from scale_inputs import scale_case
+
+    bits, temps, top_ks, top_ps, seeds, positions, max_top_k = scale_case(name)
+    got = _run_gpu(bits, temps, top_ks, top_ps, seeds, positions, max_top_k, True)
+    want = sampler_scale_golden[name]
+    mism = np.nonzero(got != want)[0]
+    assert mism.size == 0, f"{mism.size} of {want.size} rows differ (first {mism[:10].tolist()})"
+
+
 def test_fused_sampler_at_uint32_max_hash():
     # test_sampling_kernels.py:151-186
     logits = np.full((1, 2048), -200.0, np.float32)

@@ -19,17 +19,12 @@ import pytest
 import torch
 
 from oracle import sampler as orc
-from oracle.model import OracleTalker, bits
+from oracle.model import OracleTalker
+from step_util import check_step_against_oracle, cos_err
 
 pytestmark = pytest.mark.gpu
 
 DEV = "cuda"
-
-
-def cos_err(a: torch.Tensor, b: torch.Tensor):
-    a, b = a.float().flatten().cpu(), b.float().flatten().cpu()
-    cos = torch.nn.functional.cosine_similarity(a, b, dim=0).item()
-    return cos, (a - b).abs().max().item(), b.abs().max().item()
 
 
 def make_runner(layers=2, lens=(16, 1, 33, 100, 200, 15, 64, 17), seed=0, max_batch=8, sampling=None, moe=False):
@@ -54,84 +49,8 @@ def make_runner(layers=2, lens=(16, 1, 33, 100, 200, 15, 64, 17), seed=0, max_ba
 def test_decode_step_matches_oracle(dosample, moe):
     from omni_b200.config import SamplingParams
 
-    sp = SamplingParams(subtalker_dosample=dosample)
-    r = make_runner(sampling=sp, moe=moe)
-    B = r.batch_size
-    cfg = r.cfg
-    # snapshot the pre-step state for the oracle
-    seq0 = r.seq_lens[:B].cpu().numpy()
-    r2t0 = r.r2t.req_to_token[:B].cpu().numpy()
-    free = r.allocator.free_pages.cpu().numpy()
-    head0 = int(r.allocator.free_head.item())
-    kpool = r.kv.k_buffer.float().cpu()
-    vpool = r.kv.v_buffer.float().cpu()
-    feedback = r.predictor.output_embeds[:B].clone().cpu()
-    text = r.text_embeds[:B].clone().cpu()
-    t = r.talker
-    l0_state = dict(penalties=t.repetition_penalties[:B].cpu().numpy(), rep_mask=t.repetition_mask[:B].cpu().numpy(),
-                    suppress_mask=t.suppress_mask[:B].cpu().numpy(), temperature=t.sampling_temperatures[:B].cpu().numpy(),
-                    top_k=t.sampling_top_ks[:B].cpu().numpy(), top_p=t.sampling_top_ps[:B].cpu().numpy(),
-                    min_p=t.sampling_min_ps[:B].cpu().numpy(), seed=t.sampling_seeds[:B].cpu().numpy(),
-                    max_top_k=t.max_top_k)
-    p = r.predictor
-    sub = dict(temperature=p.sub_temperature_tensor[:B].cpu().numpy(), top_k=p.sub_top_k_tensor[:B].cpu().numpy(),
-               top_p=p.sub_top_p_tensor[:B].cpu().numpy(), seed=p.sub_sampling_seed_tensor[:B].cpu().numpy(),
-               do_sample=p.sub_do_sample_tensor[:B].cpu().numpy(), max_top_k=p.sub_sampled_max_top_k,
-               has_top_p=p.sub_sampled_has_top_p)
-
-    r.step(use_graph=False)
-    torch.cuda.synchronize()
-
-    # ---- packing: bit-exact ----
-    sl, r2t1, loc, pos, _, _, pgp, pgi, head1 = orc.decode_prepare(seq0, np.arange(B), r2t0, cfg.page_size, free,
-                                                                   free_head=head0)
-    assert r.seq_lens[:B].cpu().numpy().tolist() == sl.tolist()
-    assert r.out_cache_loc[:B].cpu().numpy().tolist() == loc.tolist()
-    assert r.positions[:B].cpu().numpy().tolist() == pos.tolist()
-    assert r.page_indptr[: B + 1].cpu().numpy().tolist() == pgp.tolist()
-    assert r.page_indices[: pgp[-1]].cpu().numpy().tolist() == pgi.tolist()
-    assert np.array_equal(r.r2t.req_to_token[:B].cpu().numpy(), r2t1)
-    assert int(r.allocator.free_head.item()) == head1
-
-    # ---- talker: bf16 tolerance ----
-    o = OracleTalker(cfg, r.w, r.predictor.w)
-    logits_o, hidden_o = o.talker_forward(feedback, text, torch.from_numpy(pos), torch.from_numpy(loc),
-                                          torch.from_numpy(sl), torch.from_numpy(r2t1), kpool, vpool)
-    cos, err, scale = cos_err(t.hidden[:B], hidden_o)
-    assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0), (cos, err, scale)
-    cos, err, scale = cos_err(t.logits[:B], logits_o)
-    assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0), (cos, err, scale)
-    # K/V written at the new slots
-    kdev = r.kv.k_buffer[:, torch.from_numpy(loc).to(DEV)].float().cpu()
-    cos, err, scale = cos_err(kdev, kpool[:, torch.from_numpy(loc)])
-    assert cos >= 0.999, cos
-
-    # ---- layer-0 draw: bit-exact given the device logits ----
-    l0_state["positions"] = pos
-    c0 = t.sampled_token_ids[:B].cpu()
-    assert o.layer0(t.logits[:B].cpu(), l0_state).tolist() == c0.tolist()
-    # the drawn token is marked in the repetition mask
-    assert t.repetition_mask[torch.arange(B, device=DEV), c0.to(DEV)].all()
-
-    # ---- predictor: teacher-forced logits within tolerance, draws bit-exact ----
-    codes = p.output_codes[:B].cpu().numpy()
-    assert codes[:, 0].tolist() == c0.tolist()
-    codes_o, summed_o, logits_po = o.code_predictor(c0, t.hidden[:B].cpu(), torch.from_numpy(pos), sub,
-                                                    forced_codes=codes)
-    G = cfg.predictor.num_code_groups
-    for j in range(G - 1):
-        lg = p.codebook_logits(j, B)
-        cos, err, scale = cos_err(lg, logits_po[j])
-        # these logits are stored in bf16: on top of the 2e-2 tolerance, one rounding
-        # of the output may land on the neighbouring bf16 value (one ulp at the scale)
-        ulp = 2.0 ** (np.floor(np.log2(max(scale, 1.0))) - 7)
-        assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0) + ulp, (j, cos, err, scale)
-        drawn = orc.sample_topk_topp(bits(lg), sub["temperature"], sub["top_k"], sub["top_p"], sub["seed"],
-                                     pos * (G - 1) + (j + 1), max_top_k=sub["max_top_k"], has_top_p=sub["has_top_p"])
-        am = np.argmax(lg.float().cpu().numpy(), axis=1)
-        want = np.where(sub["do_sample"].astype(bool), drawn, am)
-        assert codes[:, j + 1].tolist() == want.tolist(), j
-    assert np.array_equal(bits(p.output_embeds[:B]), summed_o)
+    r = make_runner(sampling=SamplingParams(subtalker_dosample=dosample), moe=moe)
+    check_step_against_oracle(r, use_graph=False)
 
 
 @pytest.mark.parametrize("moe", [False, True])
@@ -257,3 +176,64 @@ def test_mixed_prefill_decode_step_matches_oracle():
     c0 = t.sampled_token_ids[:n].cpu()
     assert o.layer0(t.logits[:n].cpu(), l0_state).tolist() == c0.tolist()
     assert r.predictor.output_codes[:n, 0].cpu().tolist() == c0.tolist()
+
+
+def test_staged_requests_drive_the_layer0_draw():
+    """prepare_decode_buffers through the runner: requests with prior output ids,
+    repetition penalties, suppress lists and cold-start clones (Qwen3-TTS flavor:
+    control range but EOS, leading silence) are staged into the device tensors exactly
+    as omni_b200.staging stages them; the step's layer-0 draw is bit-exact against the
+    oracle under those masks and never lands on a suppressed id; a clone's silence ids
+    are released after leading_silence_mask_frames frames."""
+    from omni_b200.config import SamplingParams, TalkerConfig
+    from omni_b200.model_runner import TalkerDecodeRunner
+    from omni_b200.staging import TTS, CodecControl, TalkerRequest
+
+    lens = (16, 1, 33, 100, 200, 15, 64, 17)
+    cfg = TalkerConfig(num_hidden_layers=2, max_context=1024)
+    rng = np.random.default_rng(5)
+    silence = tuple(int(x) for x in rng.choice(2048, 24, replace=False))
+    ctl = CodecControl(codec_eos_token_id=2150, leading_silence_mask_frames=2, silence_codec_ids=silence)
+    pages = sum((L + 16) // 16 for L in lens) + 32
+    r = TalkerDecodeRunner(cfg, max_batch=8, num_pages=pages, seed=3, flavor=TTS, codec_control=ctl)
+    reqs = []
+    for i in range(8):
+        sp = SamplingParams(repetition_penalty=[1.05, 1.0, 1.5, 2.0][i % 4], temperature=[0.9, 0.7][i % 2],
+                            top_k=[50, 20, 64, 4][i % 4], top_p=[0.8, 1.0, 0.95][i % 3],
+                            subtalker_dosample=i != 3)
+        clone = i in (0, 2, 6)  # cold-start clones have emitted nothing yet
+        prior = [] if clone else [int(x) for x in rng.integers(0, 2048, int(rng.integers(0, 40)))]
+        reqs.append(TalkerRequest(rid=f"s{i}", seed=None if i == 5 else 100 + i, sampling=sp, output_ids=prior,
+                                  suppress_tokens=[int(x) for x in rng.integers(0, 3072, 5)] if i % 2 else None,
+                                  mask_leading_silence=clone))
+    r.admit(list(lens), requests=reqs, seed=4)
+    g = torch.Generator(device=DEV).manual_seed(9)
+    r.text_embeds.normal_(generator=g)
+    r.predictor.output_embeds.normal_(generator=g)
+    st = r.stage_requests(reqs)
+    t, p = r.talker, r.predictor
+    B = 8
+    assert np.array_equal(t.repetition_mask[:B].cpu().numpy(), st.repetition_mask)
+    assert np.array_equal(t.suppress_mask[:B].cpu().numpy(), st.suppress_mask)
+    assert t.sampling_seeds[:B].cpu().tolist() == st.seeds.tolist()
+    assert t.sampling_top_ks[:B].cpu().tolist() == st.top_ks.tolist()
+    assert p.sub_sampling_seed_tensor[:B].cpu().tolist() == st.sub_seeds.tolist()
+    assert p.sub_top_k_tensor[:B].cpu().tolist() == st.sub_top_ks.tolist()
+    assert p.sub_do_sample_tensor[:B].cpu().tolist() == st.sub_do_sample.tolist()
+    masked = [set(np.nonzero(st.suppress_mask[i])[0].tolist()) for i in range(B)]
+    assert r.silence_rows.tolist() == [i in (0, 2, 6) for i in range(B)]
+    assert all(set(silence) <= masked[i] for i in (0, 2, 6))
+    check_step_against_oracle(r, use_graph=False)  # bit-exact draw under the staged masks
+    c0 = t.sampled_token_ids[:B].cpu().tolist()
+    assert all(c not in masked[i] for i, c in enumerate(c0))
+    # the public decode API keeps the frame count (step() is the device-only path);
+    # the clones' silence ids stay masked for their first 2 frames, then are released
+    r.capture(warmup=1)
+    text = torch.randn(B, cfg.hidden_size).to(torch.bfloat16).pin_memory()
+    codes = r.decode(text)
+    assert all(int(codes[i, 0]) not in masked[i] for i in range(B))
+    assert r.silence_rows.tolist() == [i in (0, 2, 6) for i in range(B)]
+    codes = r.decode(text)
+    assert all(int(codes[i, 0]) not in masked[i] for i in range(B))
+    assert not r.silence_rows.any()
+    assert np.array_equal(t.suppress_mask[:B].cpu().numpy(), r.base_suppress[:B])
