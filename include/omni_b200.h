@@ -140,7 +140,10 @@ OMNI_API int omni_layer0_sample(const float* logits, int64_t rows, int64_t vocab
  * to pair row 2 r + 1 and to summed; codes[r * codes_stride] = layer0_codes[r];
  * pair_ss[2 r], pair_ss[2 r + 1] = the pair rows' sums of squares.
  *   talker_residual bf16 [rows, hidden]; table bf16 [vocab, hidden];
- *   pair bf16 [2 rows, hidden]; summed, hidden_out bf16 [rows, hidden]. */
+ *   pair bf16 [2 rows, hidden]; summed, hidden_out bf16 [rows, hidden].
+ *   final_norm_weight NULL: talker_residual is already the normalized hidden state
+ *   (the reference's code_predictor_forward input) and is copied unchanged; ss_in
+ *   is then not read. */
 OMNI_API int omni_predictor_pair_inputs(const int64_t* layer0_codes, const void* talker_residual,
                                         int64_t residual_stride, const void* final_norm_weight, const float* ss_in,
                                         int32_t ss_parts, int64_t ss_stride, float eps, void* hidden_out,

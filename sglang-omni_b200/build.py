@@ -20,6 +20,8 @@ CSRC = ROOT / "csrc"
 BUILD = ROOT / "_build"
 INCLUDE = ROOT.parent / "include"
 LIB = ROOT / "omni_b200" / "libomni_b200.so"
+TORCH_OPS_SRC = ROOT / "torch_ext" / "omni_torch_ops.cpp"
+TORCH_OPS_LIB = ROOT / "omni_b200" / "libomni_torch_ops.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -79,5 +81,31 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> Path:
     return LIB
 
 
+def build_torch_ops(verbose: bool = False) -> Path:
+    """The torch operator registration (torch_ext/omni_torch_ops.cpp, TORCH_LIBRARY): a
+    host-only C++ library over libomni_b200.so's C ABI, compiled against the installed
+    torch's headers and linked with an $ORIGIN rpath, next to libomni_b200.so."""
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    if not _stale(TORCH_OPS_LIB, [TORCH_OPS_SRC, LIB, *sorted(INCLUDE.glob("*.h"))]):
+        return TORCH_OPS_LIB
+    cuda_home = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+    incs = ce.include_paths() + [str(cuda_home / "include"), str(INCLUDE)]
+    torch_lib = Path(torch.__file__).resolve().parent / "lib"
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-DTORCH_EXTENSION_NAME=omni_torch_ops", *[f"-I{i}" for i in incs], str(TORCH_OPS_SRC),
+           f"-L{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", f"-Wl,-rpath,{torch_lib}",
+           f"-L{LIB.parent}", "-l:libomni_b200.so", "-Wl,-rpath,$ORIGIN", "-o", str(TORCH_OPS_LIB)]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"torch ops build failed:\n{proc.stderr[-6000:]}")
+    if verbose:
+        print(f"built {TORCH_OPS_LIB}")
+    return TORCH_OPS_LIB
+
+
 if __name__ == "__main__":
     build(verbose=True, extra=sys.argv[1:])
+    build_torch_ops(verbose=True)

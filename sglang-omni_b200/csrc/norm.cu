@@ -1,9 +1,10 @@
 // Normalisation and rotary kernels of the decode step.
 //
 // rmsnorm_kernel: one warp per row; lane t holds columns 8t + 256b + j (16-byte
-//   vectors), its squares are folded in (b, j) order and combined by an xor
-//   butterfly 1, 2, 4, 8, 16 — the reduction tree the reference's exact
-//   add-norm reproduces (sglang_omni/utils/predictor_layers.py:1-37, :104-142).
+//   vectors), its squares (each rounded, then added: no fused multiply-add) are
+//   folded in (b, j) order and combined by an xor butterfly 1, 2, 4, 8, 16 — the
+//   reduction tree and rounding of the reference's add_rmsnorm_rounded
+//   (sglang_omni/utils/predictor_layers.py:104-142, compiled without fp fusion).
 //   Optionally adds a second operand first (bf16 sum, written back to the
 //   residual stream): the fused add + RMSNorm of sglang's RMSNorm(x, residual).
 //
@@ -56,7 +57,7 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint16_t* __restrict
 #pragma unroll
   for (int c = 0; c < CHUNKS; ++c)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc = __fmaf_rn(v[c][j], v[c][j], acc);
+    for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, __fmul_rn(v[c][j], v[c][j]));
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
   const float rstd = rsqrtf(acc / (float)H + eps);

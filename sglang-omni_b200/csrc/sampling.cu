@@ -1101,9 +1101,14 @@ __global__ void __launch_bounds__(128) predictor_pair_inputs_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t code = c0[row];
   if (threadIdx.x == 0) codes[row * codes_stride] = code;
-  float tot = 0.0f;
-  for (int q = 0; q < ss_parts; ++q) tot += ss_in[q * ss_stride + row];
-  const float rstd = rsqrtf(tot / (float)H + eps);
+  // final_norm == nullptr: h is already the normalized hidden state (copied unchanged)
+  const bool norm = final_norm != nullptr;
+  float rstd = 1.0f;
+  if (norm) {
+    float tot = 0.0f;
+    for (int q = 0; q < ss_parts; ++q) tot += ss_in[q * ss_stride + row];
+    rstd = rsqrtf(tot / (float)H + eps);
+  }
   const uint4* e = reinterpret_cast<const uint4*>(table + code * H);
   const uint4* hs = reinterpret_cast<const uint4*>(h + row * h_stride);
   const uint4* gw = reinterpret_cast<const uint4*>(final_norm);
@@ -1113,12 +1118,12 @@ __global__ void __launch_bounds__(128) predictor_pair_inputs_kernel(
   uint4* ho = hidden_out ? reinterpret_cast<uint4*>(hidden_out + (int64_t)row * H) : nullptr;
   float ss0 = 0.0f, ss1 = 0.0f;
   for (int v = threadIdx.x; v < H / 8; v += 128) {
-    const uint4 hv = hs[v], gv = gw[v], w = e[v];
+    const uint4 hv = hs[v], gv = norm ? gw[v] : make_uint4(0u, 0u, 0u, 0u), w = e[v];
     const uint32_t hx[4] = {hv.x, hv.y, hv.z, hv.w}, gx[4] = {gv.x, gv.y, gv.z, gv.w}, wx[4] = {w.x, w.y, w.z, w.w};
     uint32_t nx[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      nx[q] = pack_bf2(bf_lo(hx[q]) * rstd * bf_lo(gx[q]), bf_hi(hx[q]) * rstd * bf_hi(gx[q]));
+      nx[q] = norm ? pack_bf2(bf_lo(hx[q]) * rstd * bf_lo(gx[q]), bf_hi(hx[q]) * rstd * bf_hi(gx[q])) : hx[q];
       ss0 = __fmaf_rn(bf_lo(nx[q]), bf_lo(nx[q]), ss0);
       ss0 = __fmaf_rn(bf_hi(nx[q]), bf_hi(nx[q]), ss0);
       ss1 = __fmaf_rn(bf_lo(wx[q]), bf_lo(wx[q]), ss1);
@@ -1151,7 +1156,8 @@ extern "C" OMNI_API int omni_predictor_pair_inputs(const int64_t* layer0_codes, 
                                                    float eps, void* hidden_out, const void* table, int64_t rows,
                                                    int64_t hidden, void* pair, void* summed, float* pair_ss,
                                                    int64_t* codes, int64_t codes_stride, void* stream) {
-  if (rows < 0 || hidden <= 0 || ss_parts <= 0 || !ss_in || !pair_ss) return omni::set_error(OMNI_ERR_INVALID, "bad shape");
+  if (rows < 0 || hidden <= 0 || !pair_ss || (final_norm_weight && (ss_parts <= 0 || !ss_in)))
+    return omni::set_error(OMNI_ERR_INVALID, "bad shape");
   auto mis = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
   if (hidden % 8 || residual_stride % 8 || mis(talker_residual) || mis(table) || mis(pair) || mis(summed) ||
       mis(final_norm_weight) || (hidden_out && mis(hidden_out)))

@@ -235,6 +235,22 @@ class TalkerDecodeRunner:
                            status=self.status)
         return self.forward_batch()
 
+    def build_forward_batch(self):
+        """Host page bookkeeping and the device packing of the next step (prepare_for_decode
+        + build_forward_batch, and prepare_for_extend when new streams are admitted) as the
+        ForwardBatch that omni_b200.talker_model.TalkerModel.forward takes."""
+        from omni_b200.talker_model import ForwardBatch, ForwardMode
+
+        self._host_reserve()
+        fb = self.prepare_decode()
+        B = fb.batch_size
+        if self.extend is None:
+            return ForwardBatch(ForwardMode.DECODE, B, fb.positions, fb)
+        ext = self.prepare_extend()
+        R = B + ext.tokens
+        return ForwardBatch(ForwardMode.MIXED, B, self.row_positions[:R], fb, ext, self.row_positions,
+                            self.row_cache_loc, self.select)
+
     def run_step(self) -> None:
         """The whole decode step on the current stream (capturable); a mixed step when
         extend streams are admitted."""

@@ -94,6 +94,7 @@ class CodePredictor:
         self.lm_head_folded = torch.stack([ops.fold_norm(weights["lm_head"][j], weights["norm"])
                                            for j in range(G - 1)])
         self.output_codes = torch.zeros(max_batch, G, dtype=torch.long, device=self.device)
+        self.zero_positions = torch.zeros(max_batch, dtype=torch.long, device=self.device)
         self.output_embeds = torch.zeros(max_batch, H, **bf)
         # per-row residual sampling state (sub_*_tensor of sglang_model.py:1115-1140)
         self.sub_temperature_tensor = torch.full((max_batch,), 0.9, dtype=torch.float32, device=self.device)
@@ -195,16 +196,21 @@ class CodePredictor:
         talker_hidden: torch.Tensor,
         semantic_positions: torch.Tensor | None = None,
         *,
-        final_norm: torch.Tensor,
-        final_ss: torch.Tensor,
+        final_norm: torch.Tensor | None = None,
+        final_ss: torch.Tensor | None = None,
         final_eps: float = 1e-6,
         hidden_out: torch.Tensor | None = None,
     ) -> tuple[torch.Tensor, torch.Tensor]:
-        """(layer0_codes [B, 1] i64, talker residual [B, 1, H] bf16, semantic_positions [B])
-        -> (codes [B, G, 1] i64, summed [B, 1, H] bf16) (sglang_model.py:1317-1346).
-        The talker's final RMSNorm (gain final_norm, row sums of squares final_ss
-        [parts, rows]) is applied to talker_hidden on the way in; the normalized hidden
-        states are written to hidden_out when given."""
+        """(layer0_codes [B, 1] i64, talker_hidden [B, 1, H] bf16, semantic_positions [B] or
+        None) -> (codes [B, G, 1] i64, summed [B, 1, H] bf16), the reference's
+        code_predictor_forward (sglang_model.py:1317-1346): talker_hidden is the talker's
+        normalized final hidden state.
+        Fast path of the fused decode step: with final_norm (gain) and final_ss (row sums
+        of squares [parts, rows] of the talker's last residual), talker_hidden is that
+        residual and the talker's final RMSNorm is applied on the way in; the normalized
+        rows then also go to hidden_out when given."""
+        if (final_norm is None) != (final_ss is None):
+            raise ValueError("final_norm and final_ss are given together")
         cfg = self.cfg
         if layer0_codes.ndim == 2:
             layer0_codes = layer0_codes[:, 0]
@@ -215,15 +221,23 @@ class CodePredictor:
             raise RuntimeError("code predictor buffers are too small for this batch")
         H, G = cfg.hidden_size, cfg.num_code_groups
         if semantic_positions is None:
-            semantic_positions = torch.zeros(B, dtype=torch.long, device=self.device)
+            # (the reference then samples unseeded; here every row draws at position 0)
+            semantic_positions = self.zero_positions[:B]
+        elif semantic_positions.ndim == 2:
+            semantic_positions = semantic_positions.reshape(-1)
         codes = self.output_codes[:B]
         summed = self.output_embeds[:B]
         pair = self.pair[: 2 * B]
         from omni_b200 import _lib
 
+        if talker_hidden.dtype is not torch.bfloat16 or talker_hidden.shape[-1] != H or talker_hidden.stride(-1) != 1:
+            raise ValueError("talker_hidden must be bf16 [B, 1, H] with unit feature stride")
+        if layer0_codes.dtype is not torch.long or not layer0_codes.is_contiguous():
+            layer0_codes = layer0_codes.to(torch.long).contiguous()
         _lib.call("omni_predictor_pair_inputs", layer0_codes.data_ptr(), talker_hidden.data_ptr(),
-                  talker_hidden.stride(0), final_norm.data_ptr(), final_ss.data_ptr(), final_ss.shape[0],
-                  final_ss.stride(0), float(final_eps), _lib.ptr(hidden_out), self.layer0_embedding.data_ptr(), B, H,
+                  talker_hidden.stride(0), _lib.ptr(final_norm), _lib.ptr(final_ss),
+                  final_ss.shape[0] if final_ss is not None else 0, final_ss.stride(0) if final_ss is not None else 0,
+                  float(final_eps), _lib.ptr(hidden_out), self.layer0_embedding.data_ptr(), B, H,
                   pair.data_ptr(), summed.data_ptr(), self.pair_ss.data_ptr(), codes.data_ptr(), codes.stride(0),
                   _lib.stream_of(self.device))
         h = self.forward_tokens(pair, self.pair_ss, batch=B, tokens=2, cache_len=0)
