@@ -26,9 +26,26 @@ def cos_err(a: torch.Tensor, b: torch.Tensor):
     return cos, (a - b).abs().max().item(), b.abs().max().item()
 
 
-def check_step_against_oracle(r, *, use_graph: bool = False, tol: float = 2e-2) -> dict:
+def err_quantile(a: torch.Tensor, b: torch.Tensor, q: float = 0.999) -> float:
+    d = (a.float().flatten().cpu() - b.float().flatten().cpu()).abs()
+    return torch.quantile(d, q).item() if d.numel() <= 16_000_000 else d.max().item()
+
+
+def bf16_ulp(scale: float) -> float:
+    """The spacing of bf16 values at magnitude `scale` (>= 1)."""
+    return 2.0 ** (np.floor(np.log2(max(scale, 1.0))) - 7)
+
+
+def check_step_against_oracle(r, *, use_graph: bool = False, tol: float = 2e-2, depth_ulps: int = 0) -> dict:
     """Runs one step of runner r (eager, or its captured graph) and checks it against the
-    oracle; returns the measured agreement figures."""
+    oracle; returns the measured agreement figures.
+
+    Hidden states and logits: cosine >= 0.999 and max-abs <= tol x scale, plus
+    depth_ulps bf16 steps at the scale for deep stacks (the GPU and the oracle round to
+    bf16 at the same storage points but accumulate in different orders, so a residual
+    value can land one bf16 step apart and the difference carries through the following
+    layers); with depth_ulps > 0 the 99.9th percentile of the error must still be within
+    tol x scale."""
     cfg = r.cfg
     B = r.batch_size
     # snapshot the pre-step state for the oracle
@@ -72,11 +89,15 @@ def check_step_against_oracle(r, *, use_graph: bool = False, tol: float = 2e-2) 
                                           torch.from_numpy(sl), torch.from_numpy(r2t1), kpool, vpool)
     figures = {}
     cos, err, scale = cos_err(t.hidden[:B], hidden_o)
-    figures["hidden"] = (cos, err, scale)
-    assert cos >= 0.999 and err <= tol * max(scale, 1.0), (cos, err, scale)
+    q999 = err_quantile(t.hidden[:B], hidden_o)
+    figures["hidden"] = (cos, err, scale, q999)
+    assert cos >= 0.999 and err <= tol * max(scale, 1.0) + depth_ulps * bf16_ulp(scale), (cos, err, scale, q999)
+    assert q999 <= tol * max(scale, 1.0), (cos, err, scale, q999)
     cos, err, scale = cos_err(t.logits[:B], logits_o)
-    figures["logits"] = (cos, err, scale)
-    assert cos >= 0.999 and err <= tol * max(scale, 1.0), (cos, err, scale)
+    q999 = err_quantile(t.logits[:B], logits_o)
+    figures["logits"] = (cos, err, scale, q999)
+    assert cos >= 0.999 and err <= tol * max(scale, 1.0) + depth_ulps * bf16_ulp(scale), (cos, err, scale, q999)
+    assert q999 <= tol * max(scale, 1.0), (cos, err, scale, q999)
     # K/V written at the new slots
     kdev = r.kv.k_buffer[:, torch.from_numpy(loc).to(DEV)].float().cpu()
     cos, err, scale = cos_err(kdev, kpool[:, torch.from_numpy(loc)])
