@@ -166,12 +166,147 @@ def cpu_step_rate(steps: int, warmup: int, seed: int = 0) -> tuple[float, dict, 
     return rate, desc, times
 
 
+def cpu_slice_rate(config: int, seed: int = 0) -> dict:
+    """The CPU restatement of a reduced slice of config 2 or 3, scaled to the full config
+    (a bounded sample of host work; the scaling is stated in the returned description).
+
+    config 3: the 256 streams through 1 of the 20 MoE layers (FP8 experts dequantised to
+    fp32) and the 31-codebook predictor; talker time x 20 + predictor time.
+    config 2: 2 new streams' prompts (two of the benchmark's prompt draw) with 14
+    decode streams through the 20 dense layers in one mixed forward, then the layer-0 draw and
+    the 15-codebook predictor for the 16 streams; forward time x (full token count / slice
+    token count) + predictor time x (128 / 16)."""
+    import dataclasses
+
+    from oracle.model import OracleTalker  # test infrastructure: the CPU baseline
+    from omni_b200.config import CONFIG1_DENSE, CONFIG3_MOE
+    from omni_b200.predictor import init_predictor_weights
+    from omni_b200.talker import init_talker_weights
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed + 7)
+    if config == 3:
+        cfg = dataclasses.replace(CONFIG3_MOE, num_hidden_layers=1)
+        B, B_full, layers_full = 256, 256, CONFIG3_MOE.num_hidden_layers
+    else:
+        cfg = CONFIG1_DENSE
+        B, B_full = 14, 112
+    tw = init_talker_weights(cfg, seed=seed, device="cpu")
+    pw = init_predictor_weights(cfg.predictor, seed=seed + 1, device="cpu")
+    o = OracleTalker(cfg, tw, pw)
+    lens = context_lengths(B, seed, headroom=8)
+    prompts = []
+    if config == 2:
+        prng = np.random.default_rng(100)
+        # two of the benchmark's 16 prompt lengths (its 3rd and 5th: 564 and 387 rows), which
+        # keep the slice to tens of seconds of host work
+        draw = [int(x) for x in prng.integers(64, 4097, 16)]
+        prompts = [draw[2], draw[4]]
+    slots = sum(L + 1 for L in lens) + sum(prompts)
+    kpool = torch.randn(cfg.num_hidden_layers, slots, cfg.num_key_value_heads, cfg.head_dim,
+                        generator=g).bfloat16().float()
+    vpool = torch.randn_like(kpool)
+    r2t = torch.zeros(B + len(prompts), max(lens + prompts) + 2, dtype=torch.int32)
+    off = 0
+    for i, L in enumerate(lens):
+        r2t[i, : L + 1] = torch.arange(off, off + L + 1, dtype=torch.int32)
+        off += L + 1
+    seq = torch.tensor(lens) + 1
+    pos = seq - 1
+    loc = r2t[torch.arange(B), pos].long()
+    feedback = torch.randn(B, cfg.hidden_size, generator=g).bfloat16()
+    t0 = time.perf_counter()
+    if config == 3:
+        logits, hidden = o.talker_forward(feedback, None, pos, loc, seq, r2t, kpool, vpool)
+        n = B
+        positions = pos
+    else:
+        ext_pos, ext_loc, ext_ctx = [], [], []
+        for j, L in enumerate(prompts):
+            sl = torch.arange(off, off + L)
+            r2t[B + j, :L] = sl.to(torch.int32)
+            off += L
+            ext_pos += list(range(L))
+            ext_loc += sl.tolist()
+            ext_ctx += [sl[: k + 1] for k in range(L)]
+        prompt = torch.randn(sum(prompts), cfg.hidden_size, generator=g).bfloat16()
+        select = torch.tensor(list(range(B)) + [B + int(x) for x in np.cumsum(prompts) - 1])
+        logits, hidden = o.mixed_forward(feedback, None, pos, loc, seq, r2t, prompt, ext_pos, ext_loc, ext_ctx,
+                                         select, kpool, vpool)
+        n = B + len(prompts)
+        positions = torch.cat([pos, torch.tensor([L - 1 for L in prompts])])
+    t_talker = time.perf_counter() - t0
+    l0 = dict(penalties=np.full(n, 1.05, np.float32), rep_mask=np.zeros((n, cfg.vocab_size), np.uint8),
+              suppress_mask=np.zeros((n, cfg.vocab_size), np.uint8), temperature=np.full(n, 0.9, np.float32),
+              top_k=np.full(n, 50), top_p=np.full(n, 0.8, np.float32), min_p=np.zeros(n, np.float32),
+              seed=np.arange(n) + 1, max_top_k=50, positions=positions.numpy())
+    sub = dict(temperature=np.full(n, 0.9, np.float32), top_k=np.full(n, 50), top_p=np.full(n, 0.8, np.float32),
+               seed=np.arange(n) + 100, do_sample=np.ones(n, np.uint8), max_top_k=50, has_top_p=True)
+    t0 = time.perf_counter()
+    c0 = torch.from_numpy(o.layer0(logits, l0))
+    o.code_predictor(c0, hidden, positions, sub)
+    t_pred = time.perf_counter() - t0
+    if config == 3:
+        step_s = t_talker * (B_full / B) * (layers_full / cfg.num_hidden_layers) + t_pred * (B_full / B)
+        frames = B_full
+        scaling = f"talker slice time x {layers_full // cfg.num_hidden_layers} (layers) + predictor time"
+        sample = f"one step of {B} streams through 1 MoE layer + the 31-codebook predictor"
+    else:
+        full_prompts = [int(x) for x in np.random.default_rng(100).integers(64, 4097, 16)]
+        tok_slice, tok_full = B + sum(prompts), B_full + sum(full_prompts)
+        step_s = t_talker * tok_full / tok_slice + t_pred * (B_full + 16) / n
+        frames = B_full + 16
+        scaling = (f"forward time x {tok_full}/{tok_slice} (token count) + predictor time x {B_full + 16}/{n} "
+                   "(streams)")
+        sample = (f"one mixed step: {B} decode streams + 2 prompts ({prompts[0]} + {prompts[1]} rows) through 20 "
+                  "layers, then the 15-codebook predictor for 16 streams")
+    return {"value": frames / step_s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": sample + f", fp32 on {torch.get_num_threads()} threads; scaled: {scaling}",
+            "slice_talker_s": t_talker, "slice_predictor_s": t_pred}
+
+
+EXTRA_CONFIGS = (0, 2, 3)
+
+
+def run_extra_configs(args) -> dict:
+    """Configs 0, 2 and 3 measured in the same invocation as the headline (each in a child
+    bench.py process on the same GPU, so that each starts with the device to itself): the
+    child's JSON line, condensed."""
+    out = {}
+    for c in EXTRA_CONFIGS:
+        steps = max(5, min(args.steps, 20))
+        cmd = [sys.executable, str(ROOT / "bench.py"), "--config", str(c), "--steps", str(steps), "--warmup",
+               str(max(3, args.warmup)), "--cpu-steps", "1"]
+        if args.no_cpu:
+            cmd.append("--no-cpu")
+        try:
+            proc = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+        except subprocess.TimeoutExpired:
+            out[f"config{c}"] = {"error": "timed out"}
+            continue
+        line = None
+        for ln in proc.stdout.splitlines():
+            if ln.startswith("{"):
+                line = json.loads(ln)
+        if proc.returncode != 0 or line is None:
+            out[f"config{c}"] = {"error": f"exit {proc.returncode}: {proc.stderr[-300:]}"}
+            continue
+        keep = ("value", "unit", "ms_per_step", "p50_step_us", "p99_step_us", "steps", "warmup", "gpu_launches",
+                "roofline", "roofline_attention", "roofline_prefill_attention", "cpu_baseline", "e2e", "clocks")
+        entry = {k: line[k] for k in keep if k in line}
+        entry["workload"] = line.get("config", {}).get("workload")
+        out[f"config{c}"] = entry
+    return out
+
+
 # ---------------------------------------------------------------------------
 def run_reference_arm(args, rank: int) -> None:
     if rank != 0:
         return
-    steps = max(1, min(args.steps, 5))
-    warmup = 1
+    # the step count and warm-up the driver asks for (at least 3 warm-ups; at most 50 steps,
+    # about half a second each on the host cores)
+    steps = max(1, min(args.steps, 50))
+    warmup = max(3, min(args.warmup, 10))
     if args.config == 0:
         cb = cpu_predictor_rate(steps)
         print(json.dumps({
@@ -752,6 +887,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="with --config 1 on one GPU: skip the configs 0 / 2 / 3 lines under 'configs'")
     ap.add_argument("--kernels", action="store_true", help="print the per-kernel time table and exit")
     ap.add_argument("--only", default=None, help="with --kernels: only the rows whose name contains this text")
     ap.add_argument("--ep", action="store_true",
@@ -1006,6 +1143,10 @@ def main() -> None:
         if not args.no_cpu and args.config == 1:
             rate, desc, _ = cpu_step_rate(args.cpu_steps, 1)
             line["cpu_baseline"] = {"value": rate, "unit": UNIT, **desc}
+        elif not args.no_cpu and args.config in (2, 3):
+            line["cpu_baseline"] = cpu_slice_rate(args.config)
+        if args.config == 1 and world == 1 and not args.no_extra:
+            line["configs"] = run_extra_configs(args)
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
