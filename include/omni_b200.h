@@ -449,8 +449,22 @@ OMNI_API int omni_moe_align_gather_strided(const int32_t* topk_ids, int64_t ids_
                                            float* permuted_s, int32_t* slot_of, int32_t* expert_offsets,
                                            void* chunks, int64_t chunk_capacity, int32_t* n_chunks, void* stream);
 
-/* Expert-parallel dispatch/combine (SURVEY-described EP variant of FusedMoE):
- * the partial routed sum of one received row over the experts this rank holds,
+/* Expert-parallel dispatch packing (the all-to-all send side of the EP variant of
+ * the reference's FusedMoE, talker.py:325-351 with experts sharded over the ranks).
+ * Rank d holds experts [d e, (d + 1) e), e = experts_per_rank.  Every token goes once
+ * to each rank holding at least one of its top_k experts, as one packed row of
+ * row_bytes: its e4m3 codes (hidden bytes), group scales (hidden / 128 floats), the k
+ * expert ids local to that rank (-1 for the others) and the k routing weights.  The
+ * row lands at send[d cap + j], j = the count of earlier tokens going to d (token
+ * order); the unused rows of every block get ids -1; part_index[t][d] = d cap + j or
+ * -1, the row of token t's returned partial.  tokens <= cap, world <= 32. */
+OMNI_API int omni_moe_ep_pack(const int32_t* topk_ids, const float* topk_weights, int64_t tokens, int32_t top_k,
+                              const void* xq, int64_t xq_stride, const float* xs, int64_t xs_stride, int32_t hidden,
+                              int32_t world, int32_t experts_per_rank, int64_t cap, void* send, int64_t row_bytes,
+                              int32_t* part_index, void* stream);
+
+/* Expert-parallel combine side: the partial routed sum of one received row over the
+ * experts this rank holds,
  * out[r] = bf16(sum_k w[r][k] * y[slot_of[r][k]]) over slot_of >= 0 (k order),
  * zero when none. */
 OMNI_API int omni_moe_partial_sum(const void* y, int64_t y_stride, const int32_t* slot_of, const float* weights,

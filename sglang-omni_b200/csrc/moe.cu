@@ -671,6 +671,79 @@ __global__ void __launch_bounds__(128) moe_partial_sum_kernel(const uint16_t* __
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Expert-parallel dispatch packing.  CTA t < tokens: the token's destination ranks
+// (a rank holds experts [d e, (d + 1) e)), its row in each destination's block (the
+// count of earlier tokens going there: every CTA re-counts the tokens before it, at
+// most a few thousand ids), the packed row (e4m3 codes, group scales, the k ids local
+// to that rank or -1, the k weights) and part_index[t][d] = d cap + row or -1.  CTA
+// tokens + d: clears the expert ids of block d's unused rows to -1.
+// ---------------------------------------------------------------------------
+constexpr int kEpMaxWorld = 32;
+
+__global__ void __launch_bounds__(256) moe_ep_pack_kernel(const int32_t* __restrict__ ids, const float* __restrict__ tw,
+                                                         int tokens, int top_k, const uint8_t* __restrict__ xq,
+                                                         int64_t xq_stride, const float* __restrict__ xs,
+                                                         int64_t xs_stride, int hidden, int world, int e_per_rank,
+                                                         int cap, uint8_t* __restrict__ send, int64_t row_bytes,
+                                                         int32_t* __restrict__ part_index) {
+  __shared__ int counts[kEpMaxWorld];
+  griddep_wait();
+  griddep_launch();
+  const int b = blockIdx.x;
+  const int groups = hidden / 128;
+  const int64_t off_ids = hidden + 4 * groups, off_w = off_ids + 4 * top_k;
+  if (threadIdx.x < kEpMaxWorld) counts[threadIdx.x] = 0;
+  __syncthreads();
+  // destinations of token u as a bit mask (ids outside [0, world e) are dropped)
+  auto dests = [&](int u) {
+    uint32_t m = 0u;
+    for (int k = 0; k < top_k; ++k) {
+      const int e = ids[(int64_t)u * top_k + k];
+      if (e >= 0 && e < world * e_per_rank) m |= 1u << (e / e_per_rank);
+    }
+    return m;
+  };
+  const int upto = b < tokens ? b : tokens;  // tokens counted: those before b (all for a clearing CTA)
+  for (int u = threadIdx.x; u < upto; u += blockDim.x) {
+    uint32_t m = dests(u);
+    while (m) {
+      const int d = __ffs(m) - 1;
+      m &= m - 1u;
+      atomicAdd(&counts[d], 1);
+    }
+  }
+  __syncthreads();
+  if (b >= tokens) {
+    // clear block d's rows past its count
+    const int d = b - tokens;
+    for (int r = counts[d] + threadIdx.x; r < cap; r += blockDim.x) {
+      int32_t* rid = reinterpret_cast<int32_t*>(send + ((int64_t)d * cap + r) * row_bytes + off_ids);
+      for (int k = 0; k < top_k; ++k) rid[k] = -1;
+    }
+    return;
+  }
+  const uint32_t mine = dests(b);
+  for (int d = 0; d < world; ++d) {
+    const bool go = (mine >> d) & 1u;
+    if (threadIdx.x == 0) part_index[(int64_t)b * world + d] = go ? d * cap + counts[d] : -1;
+    if (!go || counts[d] >= cap) continue;
+    uint8_t* row = send + ((int64_t)d * cap + counts[d]) * row_bytes;
+    const uint4* src = reinterpret_cast<const uint4*>(xq + (int64_t)b * xq_stride);
+    for (int v = threadIdx.x; v < hidden / 16; v += blockDim.x) reinterpret_cast<uint4*>(row)[v] = src[v];
+    float* rs = reinterpret_cast<float*>(row + hidden);
+    for (int gq = threadIdx.x; gq < groups; gq += blockDim.x) rs[gq] = xs[(int64_t)b * xs_stride + gq];
+    if (threadIdx.x < top_k) {
+      const int k = threadIdx.x;
+      const int e = ids[(int64_t)b * top_k + k];
+      const bool local = e >= d * e_per_rank && e < (d + 1) * e_per_rank;
+      reinterpret_cast<int32_t*>(row + off_ids)[k] = local ? e - d * e_per_rank : -1;
+      reinterpret_cast<float*>(row + off_w)[k] = tw[(int64_t)b * top_k + k];
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -904,4 +977,23 @@ extern "C" OMNI_API int omni_moe_partial_sum(const void* y, int64_t y_stride, co
                              static_cast<cudaStream_t>(stream), static_cast<const uint16_t*>(y), y_stride, slot_of,
                              weights, weights_stride, (int)top_k, (int)hidden, static_cast<uint16_t*>(out),
                              out_stride));
+}
+
+extern "C" OMNI_API int omni_moe_ep_pack(const int32_t* topk_ids, const float* topk_weights, int64_t tokens,
+                                         int32_t top_k, const void* xq, int64_t xq_stride, const float* xs,
+                                         int64_t xs_stride, int32_t hidden, int32_t world, int32_t experts_per_rank,
+                                         int64_t cap, void* send, int64_t row_bytes, int32_t* part_index,
+                                         void* stream) {
+  if (tokens < 0 || top_k < 1 || top_k > 32 || world < 1 || world > kEpMaxWorld || experts_per_rank < 1 ||
+      cap < tokens || hidden % 128 != 0 || hidden <= 0)
+    return set_error(OMNI_ERR_INVALID, "ep_pack: 1 <= top_k <= 32, 1 <= world <= 32, tokens <= cap, hidden % 128 == 0");
+  if (row_bytes < hidden + 4 * (hidden / 128) + 8 * top_k || row_bytes % 16)
+    return set_error(OMNI_ERR_INVALID, "ep_pack: row_bytes below the packed row or not a multiple of 16");
+  if (!al16(xq) || !al16(send) || xq_stride % 16 || tokens > 65535)
+    return set_error(OMNI_ERR_UNSUPPORTED, "ep_pack: 16-byte aligned rows, at most 65535 tokens");
+  const unsigned grid = (unsigned)(tokens + world);
+  return check_launch(launch(moe_ep_pack_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                             topk_ids, topk_weights, (int)tokens, (int)top_k, static_cast<const uint8_t*>(xq),
+                             xq_stride, xs, xs_stride, (int)hidden, (int)world, (int)experts_per_rank, (int)cap,
+                             static_cast<uint8_t*>(send), row_bytes, part_index));
 }

@@ -91,6 +91,7 @@ SIGNATURES: dict[str, list] = {
     "omni_moe_combine": [_P, _I64, _P, _P, _I32, _P, _I64, _P, _P, _I64, _P, _I64, _P, _I64, _I64, _I32, _P],
     "omni_moe_align_gather_strided": [_P, _I64, _I64, _I32, _I32, _P, _I64, _P, _I64, _I32, _P, _P, _P, _P, _P, _I64,
                                       _P, _P],
+    "omni_moe_ep_pack": [_P, _P, _I64, _I32, _P, _I64, _P, _I64, _I32, _I32, _I32, _I64, _P, _I64, _P, _P],
     "omni_moe_partial_sum": [_P, _I64, _P, _P, _I64, _I32, _I64, _I32, _P, _I64, _P],
     "omni_moe_combine_parts": [_P, _I64, _P, _I32, _P, _I64, _P, _P, _I64, _P, _I64, _P, _I64, _I64, _I32, _P],
     "omni_extend_prepare": [_I64, _P, _P, _P, _P, _I64, _I32, _P, _P, _P, _P, _P, _P, _P, _I32, _P, _P],

@@ -17,8 +17,15 @@ routes its own tokens with the replicated router.  Per layer:
             locally, on a side stream that runs while the two all-to-alls and the
             local experts run) and the residual, as the single-GPU combine does
 
-Fixed-size blocks keep every collective's split sizes constant, so no host
-synchronisation sits inside the layer.  The routed sum is rounded once per rank
+The send buffer, with each row's place in its destination block and the index of
+the partial each token gets back, is built by one kernel (omni_moe_ep_pack).
+Fixed-size blocks of `cap` rows keep every collective's split sizes constant, so no
+host synchronisation sits inside the layer and the layer stays inside the step's
+CUDA graph: NCCL's all-to-all takes its split sizes on the host, so blocks sized
+from a device-side count exchange would cost a device-to-host copy and a stream
+synchronisation per MoE layer (20 a step).  A rank receives cap rows from every peer
+whatever the routing; with top-8 routing over 128 experts a token reaches most
+ranks of an 8-GPU node, so the blocks are mostly full at the config-4 batch.  The routed sum is rounded once per rank
 (the partial rows are bf16), so results agree with the single-GPU block within
 the bf16 tolerance, not bit for bit.
 """
@@ -27,7 +34,7 @@ from __future__ import annotations
 
 import torch
 
-from omni_b200 import ops
+from omni_b200 import _lib, ops
 from omni_b200.config import MoEConfig
 from omni_b200.moe import MoEBlock
 
@@ -38,47 +45,17 @@ def packed_row_bytes(hidden: int, top_k: int) -> int:
     return (b + 15) // 16 * 16
 
 
-def dispatch_plan(topk_ids: torch.Tensor, world: int, experts_per_rank: int, cap: int):
-    """For tokens' global expert ids [T, k]: has[t, d] (token t goes to rank d), pos[t, d]
-    (its row in block d), flat[t, d] (row in the send buffer; world*cap = discarded) and
-    local_ids[t, d, k] (expert id on rank d, or -1)."""
+def ep_pack(send: torch.Tensor, hidden: int, top_k: int, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+            xq: torch.Tensor, xs: torch.Tensor, world: int, experts_per_rank: int, cap: int,
+            part_index: torch.Tensor) -> None:
+    """The dispatch send buffer in one launch (omni_moe_ep_pack): each token's packed row
+    in the block of every rank that holds one of its experts (rows in token order),
+    unused rows with expert ids -1, and part_index [T, world] (the row of each returned
+    partial, -1 for none)."""
     T = topk_ids.shape[0]
-    dev = topk_ids.device
-    ranks = torch.arange(world, device=dev)
-    dest = torch.div(topk_ids.long(), experts_per_rank, rounding_mode="floor")  # [T, k]
-    onehot = dest.unsqueeze(-1) == ranks  # [T, k, W]
-    has = onehot.any(1)  # [T, W]
-    pos = torch.cumsum(has.to(torch.int32), 0) - 1  # [T, W]
-    flat = torch.where(has, ranks * cap + pos, torch.full_like(pos, world * cap))
-    local = topk_ids.long().unsqueeze(1) - (ranks * experts_per_rank).view(1, world, 1)  # [T, W, k]
-    local_ids = torch.where(onehot.permute(0, 2, 1), local, torch.full_like(local, -1)).to(torch.int32)
-    del T
-    return has, pos, flat, local_ids
-
-
-def pack_rows(send: torch.Tensor, hidden: int, top_k: int, xq: torch.Tensor, xs: torch.Tensor,
-              local_ids: torch.Tensor, weights: torch.Tensor, flat: torch.Tensor) -> None:
-    """Writes the dispatched rows into send [world*cap + 1, row_bytes] (uint8); rows no
-    token lands in carry expert ids -1."""
-    T, W = flat.shape
-    G = hidden // 128
-    idx = flat.reshape(-1)
-    q = send[:, :hidden]
-    s = send[:, hidden: hidden + 4 * G].view(torch.float32)
-    ids = send[:, hidden + 4 * G: hidden + 4 * G + 4 * top_k].view(torch.int32)
-    w = send[:, hidden + 4 * G + 4 * top_k: hidden + 4 * G + 8 * top_k].view(torch.float32)
-    ids.fill_(-1)
-    q.index_copy_(0, idx, xq.unsqueeze(1).expand(T, W, hidden).reshape(T * W, hidden))
-    s.index_copy_(0, idx, xs.unsqueeze(1).expand(T, W, G).reshape(T * W, G))
-    ids.index_copy_(0, idx, local_ids.reshape(T * W, top_k))
-    w.index_copy_(0, idx, weights.unsqueeze(1).expand(T, W, top_k).reshape(T * W, top_k))
-
-
-def part_index(has: torch.Tensor, pos: torch.Tensor, cap: int) -> torch.Tensor:
-    """Row of the returned partial of token t from rank d (or -1), [T, W] int32."""
-    W = has.shape[1]
-    ranks = torch.arange(W, device=has.device)
-    return torch.where(has, ranks * cap + pos, torch.full_like(pos, -1)).to(torch.int32).contiguous()
+    _lib.call("omni_moe_ep_pack", topk_ids.data_ptr(), topk_weights.data_ptr(), T, top_k, xq.data_ptr(),
+              xq.stride(0), xs.data_ptr(), xs.stride(0), hidden, world, experts_per_rank, cap, send.data_ptr(),
+              send.stride(0), part_index.data_ptr(), _lib.stream_of(send.device))
 
 
 class ExpertParallelMoE:
@@ -104,7 +81,8 @@ class ExpertParallelMoE:
         # tokens of this rank: norm, codes, routing, shared expert (single-GPU block buffers)
         self.local = MoEBlock(cfg, hidden, max_batch=max_tokens, device=dev)
         self.side = torch.cuda.Stream(dev)  # the shared expert, overlapped with the all-to-alls
-        self.send = torch.zeros(W * self.cap + 1, self.row_bytes, dtype=torch.uint8, device=dev)
+        self.send = torch.zeros(W * self.cap, self.row_bytes, dtype=torch.uint8, device=dev)
+        self.part_index = torch.zeros(self.cap, W, dtype=torch.int32, device=dev)
         self.recv = torch.zeros(W * self.cap, self.row_bytes, dtype=torch.uint8, device=dev)
         n_recv = W * self.cap
         pairs_cap = n_recv * k + 64
@@ -148,9 +126,9 @@ class ExpertParallelMoE:
         with torch.cuda.stream(self.side):
             ops.linear_fused(x, w_local["shared_gate_up"], m.shared_act[:T], epilogue=ops.EPI_SWIGLU)
             ops.linear_fused(m.shared_act[:T], w_local["shared_down"], m.shared_out[:T], epilogue=ops.EPI_STORE)
-        has, pos, flat, local_ids = dispatch_plan(ids, W, self.e_local, cap)
-        pack_rows(self.send, H, k, xq, xs, local_ids, tw, flat)
-        self.dist.all_to_all_single(self.recv, self.send[: W * cap], group=self.group)
+        pidx = self.part_index[:T]
+        ep_pack(self.send, H, k, ids, tw, xq, xs, W, self.e_local, cap, pidx)
+        self.dist.all_to_all_single(self.recv, self.send, group=self.group)
         rb = self.row_bytes
         ids_view = self.recv[:, H + 4 * G:].view(torch.int32)
         xs_view = self.recv[:, H:].view(torch.float32)
@@ -166,5 +144,4 @@ class ExpertParallelMoE:
         ops.moe_partial_sum(self.y, self.slot_of, w_view, rb // 4, self.ret_send)
         self.dist.all_to_all_single(self.ret_recv, self.ret_send, group=self.group)
         main.wait_stream(self.side)
-        ops.moe_combine_parts(self.ret_recv, part_index(has, pos, cap), x, w_local["shared_expert_gate"],
-                              m.shared_out[:T], h, ss)
+        ops.moe_combine_parts(self.ret_recv, pidx, x, w_local["shared_expert_gate"], m.shared_out[:T], h, ss)

@@ -1,11 +1,13 @@
 """Expert-parallel MoE dispatch/combine plumbing on CPU: gloo, world size 2.
 
-The device path (moe_ep.ExpertParallelMoE) packs rows with moe_ep.dispatch_plan /
-pack_rows, exchanges fixed blocks with all_to_all_single and combines the returned
-partial rows through moe_ep.part_index.  Here the same functions run on CPU tensors
-with a stand-in expert (partial = sum_k w_k * (global expert id + 1)): every token
-must reach exactly the ranks that hold its experts, with its own row, ids and
-weights, and get back the sum over all of its experts.
+The device path (moe_ep.ExpertParallelMoE) packs its send buffer with the
+omni_moe_ep_pack kernel, whose CPU restatement is oracle.ep (dispatch_plan,
+pack_rows, part_index; tests/test_moe_ep_gpu.py holds the kernel to it bit for
+bit), exchanges fixed blocks with all_to_all_single and combines the returned
+partial rows through the part index.  Here the restatement runs on CPU tensors with
+a stand-in expert (partial = sum_k w_k * (global expert id + 1)): every token must
+reach exactly the ranks that hold its experts, with its own row, ids and weights,
+and get back the sum over all of its experts.
 """
 
 from __future__ import annotations
@@ -52,7 +54,8 @@ def _worker(rank: int, port: int, out_dir: str) -> None:
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=W)
     try:
-        from omni_b200.moe_ep import dispatch_plan, pack_rows, packed_row_bytes, part_index
+        from omni_b200.moe_ep import packed_row_bytes
+        from oracle.ep import dispatch_plan, pack_rows, part_index
 
         e_local = E // W
         ids, xq, xs, tw = _tokens(rank)

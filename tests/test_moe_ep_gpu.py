@@ -83,3 +83,38 @@ def test_ep_moe_matches_single_gpu(tmp_path, world):
         assert same_route == 1
         assert cos >= 0.999 and err <= 2e-2 * max(scale, 1.0), (r, cos, err, scale)
         assert cos_d >= 0.99, (r, cos_d)
+
+
+@pytest.mark.parametrize("world,tokens,cap", [(2, 64, 64), (8, 256, 256), (4, 37, 50), (1, 5, 8)])
+def test_ep_pack_kernel_matches_restatement(world, tokens, cap):
+    """omni_moe_ep_pack against oracle.ep: every used row, every unused row's ids and the
+    part index bit-exact (the config-3 shapes: hidden 1024, top-8 of 128 experts)."""
+    from oracle.ep import dispatch_plan, pack_rows, part_index
+
+    from omni_b200.moe_ep import ep_pack, packed_row_bytes
+
+    dev = torch.device("cuda", 0)
+    H, E, K = 1024, 128, 8
+    g = torch.Generator().manual_seed(world * 100 + tokens)
+    ids = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(tokens)]).to(torch.int32)
+    tw = torch.rand(tokens, K, generator=g)
+    xq = torch.randint(0, 256, (tokens, H), generator=g, dtype=torch.uint8)
+    xs = torch.rand(tokens, H // 128, generator=g)
+    rb = packed_row_bytes(H, K)
+    e_local = E // world
+    has, pos, flat, local_ids = dispatch_plan(ids, world, e_local, cap)
+    want = torch.zeros(world * cap + 1, rb, dtype=torch.uint8)
+    pack_rows(want, H, K, xq, xs, local_ids, tw, flat)
+    want_pidx = part_index(has, pos, cap)
+    send = torch.full((world * cap, rb), 0xAB, dtype=torch.uint8, device=dev)
+    pidx = torch.full((tokens, world), -7, dtype=torch.int32, device=dev)
+    ep_pack(send, H, K, ids.to(dev), tw.to(dev), xq.to(dev), xs.to(dev), world, e_local, cap, pidx)
+    torch.cuda.synchronize()
+    got = send.cpu()
+    assert torch.equal(pidx.cpu(), want_pidx)
+    G = H // 128
+    got_ids = got[:, H + 4 * G: H + 4 * G + 4 * K].view(torch.int32)
+    want_ids = want[: world * cap, H + 4 * G: H + 4 * G + 4 * K].view(torch.int32)
+    assert torch.equal(got_ids, want_ids)
+    used = want_pidx[want_pidx >= 0].long()
+    assert torch.equal(got[used, : H + 4 * G + 8 * K], want[used, : H + 4 * G + 8 * K])
