@@ -552,6 +552,23 @@ OMNI_API int omni_conv_window_gather(const void* padded, int64_t padded_row_stri
                                      int64_t rows, int64_t length, int32_t taps, int32_t dilation, int32_t channels,
                                      int32_t element_bytes, void* out, void* stream);
 
+/* Implicit-GEMM causal conv on tcgen05 (the code2wav's ungrouped convs,
+ * qwen3_omni/components/code2wav.py:326-460, transformers' Qwen3OmniMoeCausalConvNet):
+ *   out[r, t, n] = sum_{j < taps} sum_c padded[r, t + j dilation, c] weight[n, j * C_in + c]
+ * for t < length, channels last.  padded bf16 [rows, padded_positions, C_in] contiguous
+ * (padded_positions >= length + (taps - 1) dilation: the history in front); weight bf16
+ * [C_out, taps * C_in] (conv.weight [C_out, C_in, taps] permuted to [C_out, taps, C_in]);
+ * out rows r at out + r * out_batch_stride, positions C_out apart.  With taps = 1 it is the
+ * GEMM of a 1x1 conv or of a transposed conv's taps.  C_in, C_out multiples of 32.
+ * alpha_scale == NULL: out = bf16(conv).  Else, with bias, inverse_beta [C_out] and
+ * optionally residual / sum_out (contiguous [rows, length, C_out]), the vocoder's next
+ * SnakeBeta fused in: total = conv + bias (+ residual), sum_out = total, out = SnakeBeta
+ * (total), with the rounding points of omni_bias_snake_beta. */
+OMNI_API int omni_conv1d_gemm(const void* padded, int64_t rows, int64_t padded_positions, int32_t cin,
+                              const void* weight, int32_t cout, int32_t taps, int32_t dilation, int64_t length,
+                              void* out, int64_t out_batch_stride, const void* bias, const void* residual,
+                              void* sum_out, const void* alpha_scale, const void* inverse_beta, void* stream);
+
 /* Causal-conv state: padded [rows, history + new + tail, channels] gets each row's slot
  * history in front (zeros for a cold slot) and zeros after the new samples; the slot
  * keeps the last `history` samples of (history ++ new).  history <= 64.  Replaces

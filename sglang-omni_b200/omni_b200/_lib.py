@@ -99,6 +99,7 @@ SIGNATURES: dict[str, list] = {
                                _I32, _F32, _P, _I64, _P],
     "omni_bias_snake_beta": [_P, _I64, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I32, _P],
     "omni_clamped_single_output_conv": [_P, _I64, _P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I32, _I32, _P],
+    "omni_conv1d_gemm": [_P, _I64, _I64, _I32, _P, _I32, _I32, _I32, _I64, _P, _I64, _P, _P, _P, _P, _P, _P],
     "omni_conv_window_gather": [_P, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _P, _P],
     "omni_history_exchange": [_P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _I64, _I32, _I32, _I32, _I32, _I32,
                               _I32, _P],

@@ -23,12 +23,15 @@ What a slot carries between decodes:
 A stream's first decode reads no state and drops each transposed conv's left pad, as
 the whole-sequence forward trims it.
 
-Activations stay channels last ([rows, samples, channels]); every SnakeBeta runs fused
-with the bias and residual adds in front of it (`fused_bias_snake_beta`) and writes
-straight into the next conv's padded input; the last conv is the clamped
-single-output-channel kernel.  Ungrouped convs and transposed convs run as cuBLAS GEMMs
-over channels-last windows; the ConvNeXt depthwise conv is a cuDNN call and the windowed
-attention an SDPA call.
+Activations stay channels last ([rows, samples, channels]).  Ungrouped causal convs run
+on the implicit-GEMM tcgen05 kernel (omni_conv1d_gemm: no window is materialised) and the
+SnakeBeta that follows a conv (with its bias and residual adds) runs in that conv's
+epilogue, writing straight into the next conv's padded input; the SnakeBeta that follows
+a transposed conv (whose overlap is added after its GEMM) is the separate
+`fused_bias_snake_beta` kernel.  Transposed convs run their taps' GEMM on the same kernel
+(taps = 1).  The last conv is the clamped single-output-channel kernel.  The ConvNeXt
+depthwise conv is a cuDNN call, its pointwise layers and the pre-transformer's
+projections cuBLAS GEMMs, and the windowed attention an SDPA call.
 """
 
 from __future__ import annotations
@@ -50,9 +53,12 @@ def default_kernels() -> SimpleNamespace:
     from omni_b200.kernels.single_output_conv import clamped_single_output_conv
 
     _lib.load()
+    from omni_b200.ops import conv1d_gemm
+
     return SimpleNamespace(coefficients=SnakeBetaCoefficients.from_activation, snake=fused_bias_snake_beta,
                            history_exchange=history_exchange, overlap_exchange=overlap_exchange,
-                           single_output_conv=clamped_single_output_conv, conv_windows=conv_window_gather)
+                           single_output_conv=clamped_single_output_conv, conv_windows=conv_window_gather,
+                           conv_gemm=conv1d_gemm)
 
 
 @dataclass(frozen=True)
@@ -250,21 +256,51 @@ class Qwen3OmniIncrementalCodec:
             self._weights[id(conv)] = w
         return w
 
-    def _conv(self, c: _CausalConv, padded: torch.Tensor, pool, slots, length: int, cold: bool):
+    def _conv_weight(self, conv) -> torch.Tensor:
+        """A causal conv's weight as the [C_out, taps x C_in] matrix of the implicit GEMM."""
+        key = ("implicit", id(conv))
+        w = self._weights.get(key)
+        if w is None:
+            w = conv.weight.permute(0, 2, 1).reshape(conv.out_channels, -1).contiguous()
+            self._weights[key] = w
+        return w
+
+    def _conv(self, c: _CausalConv, padded: torch.Tensor, pool, slots, length: int, cold: bool, snake=None):
         """The causal conv's [rows, length, C_out] outputs without bias, its padded input's
-        history exchanged with the slots first.  Ungrouped convs run as one GEMM over the
-        taps-wide window of the channels-last input (output t reads padded samples t,
-        t + dilation, ...), which keeps the activations channels last."""
+        history exchanged with the slots first.  Ungrouped convs run as the implicit-GEMM
+        tcgen05 kernel (conv_gemm: the taps' windows are TMA boxes of the channels-last
+        input, nothing is gathered); kernel sets without it (the tests' oracle kernels)
+        take one GEMM over the gathered taps-wide window.
+        snake = (bias, SnakeBeta coefficients, dest, residual, sum_out): instead of
+        returning the conv, write SnakeBeta(conv + bias [+ residual]) to dest (and the sum
+        to sum_out) — fused into the conv's epilogue when the kernel is conv_gemm."""
         if c.history:
             self.k.history_exchange(padded, pool.histories[c.key], slots, new_samples=length, is_cold=cold)
         conv = c.conv
+        rows, taps = padded.shape[0], conv.kernel_size[0]
+        gemm = getattr(self.k, "conv_gemm", None)
         if conv.groups != 1:
             y = F.conv1d(padded.transpose(1, 2), conv.weight, None, 1, 0, conv.dilation, conv.groups)
-            return y.transpose(1, 2).contiguous()
-        rows, taps = padded.shape[0], conv.kernel_size[0]
-        window = padded if taps == 1 else self.k.conv_windows(padded, length, taps, conv.dilation[0])
-        y = window.reshape(rows * length, -1) @ self._gemm_weight(conv)
-        return y.view(rows, length, conv.out_channels)
+            y = y.transpose(1, 2).contiguous()
+        elif gemm is not None and conv.in_channels % 32 == 0 and conv.out_channels % 32 == 0:
+            w = self._conv_weight(conv)
+            if snake is None:
+                y = padded.new_empty(rows, length, conv.out_channels)
+                gemm(padded, w, taps=taps, dilation=conv.dilation[0], length=length, out=y)
+                return y
+            bias, coeff, dest, residual, sum_out = snake
+            gemm(padded, w, taps=taps, dilation=conv.dilation[0], length=length, out=dest, bias=bias,
+                 alpha_scale=coeff.alpha_scale, inverse_beta=coeff.inverse_beta, residual=residual,
+                 sum_out=sum_out)
+            return None
+        else:
+            window = padded if taps == 1 else self.k.conv_windows(padded, length, taps, conv.dilation[0])
+            y = (window.reshape(rows * length, -1) @ self._gemm_weight(conv)).view(rows, length, conv.out_channels)
+        if snake is None:
+            return y
+        bias, coeff, dest, residual, sum_out = snake
+        self.k.snake(y, bias, coeff, dest, residual=residual, sum_out=sum_out)
+        return None
 
     def _transconv(self, t: _TransConv, frames: torch.Tensor, pool, slots, cold: bool):
         """The transposed conv's emitted samples without bias: the slots' overlap added in
@@ -276,7 +312,18 @@ class Qwen3OmniIncrementalCodec:
         rows, n, _ = frames.shape
         conv, s = t.conv, t.stride
         taps, cout = conv.kernel_size[0], conv.out_channels
-        z = (frames.reshape(rows * n, -1) @ self._gemm_weight(conv)).view(rows, n, taps, cout)
+        gemm = getattr(self.k, "conv_gemm", None)
+        if gemm is not None and conv.in_channels % 32 == 0 and (taps * cout) % 32 == 0 and frames.is_contiguous():
+            key = ("transposed", id(conv))
+            w = self._weights.get(key)
+            if w is None:  # [taps x C_out, C_in]: the 1x1 conv form of the taps' GEMM
+                w = self._gemm_weight(conv).t().contiguous()
+                self._weights[key] = w
+            z = frames.new_empty(rows, n, taps * cout)
+            gemm(frames, w, taps=1, dilation=1, length=n, out=z)
+            z = z.view(rows, n, taps, cout)
+        else:
+            z = (frames.reshape(rows * n, -1) @ self._gemm_weight(conv)).view(rows, n, taps, cout)
         if taps == s:
             y = z.reshape(rows, n * s, cout)
         elif taps == 2 * s:
@@ -308,28 +355,41 @@ class Qwen3OmniIncrementalCodec:
         n = x.shape[1]
         padded, body = self._padded(L.decoder_in, rows, n, x)
         body.copy_(x)
-        out = self._conv(L.decoder_in, padded, pool, slots, n, cold)
+        # the conv whose output feeds the next SnakeBeta: run by that SnakeBeta's caller,
+        # so that the two fuse (conv + bias [+ residual] -> SnakeBeta in the conv epilogue)
+        pending = (L.decoder_in, padded, n)
         bias = L.decoder_in.conv.bias
         residual = None
+        channels = L.decoder_in.conv.out_channels
         for act, trans, units in L.blocks:
-            activated = out.new_empty(out.shape)
-            k.snake(out, bias, self.snake[id(act)], activated, residual=residual)
+            activated = x.new_empty(rows, n, channels)
+            pc, ppad, pn = pending
+            self._conv(pc, ppad, pool, slots, pn, cold, snake=(bias, self.snake[id(act)], activated, residual, None))
             frames = self._transconv(trans, activated, pool, slots, cold)
             n = frames.shape[1]
-            out, bias = frames, trans.conv.bias
-            residual_in, residual = None, frames.new_empty(frames.shape)
-            for s1, c1, s2, c2 in units:
-                # unit input = out + bias (+ the previous unit's input): SnakeBeta of it
-                # into conv1's padded input, the sum itself kept as the residual
-                padded, body = self._padded(c1, rows, n, frames)
-                k.snake(out, bias, self.snake[id(s1)], body, residual=residual_in, sum_out=residual)
-                y1 = self._conv(c1, padded, pool, slots, n, cold)
-                padded, body = self._padded(c2, rows, n, frames)
-                k.snake(y1, c1.conv.bias, self.snake[id(s2)], body)
-                out, bias = self._conv(c2, padded, pool, slots, n, cold), c2.conv.bias
-                residual_in = residual
-        padded, body = self._padded(L.final, rows, n, out)
-        k.snake(out, bias, self.snake[id(L.final_snake)], body, residual=residual)
+            channels = frames.shape[2]
+            # unit input = out + bias (+ the previous unit's input): SnakeBeta of it into
+            # conv1's padded input, the sum itself kept as the residual (one buffer a block,
+            # read and rewritten element by element)
+            residual = frames.new_empty(frames.shape)
+            s1, c1 = units[0][0], units[0][1]
+            padded1, body1 = self._padded(c1, rows, n, frames)
+            k.snake(frames, trans.conv.bias, self.snake[id(s1)], body1, residual=None, sum_out=residual)
+            for ui, (_, c1, s2, c2) in enumerate(units):
+                padded2, body2 = self._padded(c2, rows, n, frames)
+                self._conv(c1, padded1, pool, slots, n, cold,
+                           snake=(c1.conv.bias, self.snake[id(s2)], body2, None, None))
+                if ui + 1 < len(units):
+                    s1n, c1n = units[ui + 1][0], units[ui + 1][1]
+                    padded1, body1 = self._padded(c1n, rows, n, frames)
+                    self._conv(c2, padded2, pool, slots, n, cold,
+                               snake=(c2.conv.bias, self.snake[id(s1n)], body1, residual, residual))
+                else:
+                    pending = (c2, padded2, n)
+                    bias = c2.conv.bias
+        padded, body = self._padded(L.final, rows, n, x)
+        pc, ppad, pn = pending
+        self._conv(pc, ppad, pool, slots, pn, cold, snake=(bias, self.snake[id(L.final_snake)], body, residual, None))
         if L.final.history:
             k.history_exchange(padded, pool.histories[L.final.key], slots, new_samples=n, is_cold=cold)
         return k.single_output_conv(padded, L.final.conv, n)

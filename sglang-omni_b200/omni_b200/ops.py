@@ -570,3 +570,24 @@ def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
               tile_indptr.data_ptr(), qo_indptr.shape[0] - 1, max_tiles, num_q_heads, num_kv_heads, head_dim,
               page_size, sm_scale, out.data_ptr(), out.stride(0), _lib.stream_of(q.device))
     return out
+
+
+def conv1d_gemm(padded: torch.Tensor, weight_mat: torch.Tensor, *, taps: int, dilation: int, length: int,
+                out: torch.Tensor, bias: torch.Tensor | None = None, alpha_scale: torch.Tensor | None = None,
+                inverse_beta: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+                sum_out: torch.Tensor | None = None) -> torch.Tensor:
+    """Implicit-GEMM causal conv (omni_conv1d_gemm): padded [rows, positions, C_in] bf16 contiguous,
+    weight_mat [C_out, taps * C_in], out [rows, length, C_out] (row stride may exceed
+    length * C_out, as a padded buffer's body).  With alpha_scale: SnakeBeta(conv + bias
+    [+ residual]) fused, the sum to sum_out."""
+    rows, positions, cin = padded.shape
+    cout = weight_mat.shape[0]
+    if not padded.is_contiguous() or not weight_mat.is_contiguous() or weight_mat.shape[1] != taps * cin:
+        raise ValueError("conv1d_gemm needs a contiguous padded input and a [C_out, taps * C_in] weight")
+    if out.shape[-1] != cout or out.stride(-1) != 1 or (out.ndim == 3 and out.stride(1) != cout):
+        raise ValueError("conv1d_gemm output rows are [length, C_out] channels last")
+    _lib.call("omni_conv1d_gemm", padded.data_ptr(), rows, positions, cin, weight_mat.data_ptr(), cout, taps,
+              dilation, length, out.data_ptr(), out.stride(0), _lib.ptr(bias), _lib.ptr(residual),
+              _lib.ptr(sum_out), _lib.ptr(alpha_scale), _lib.ptr(inverse_beta), _lib.stream_of(padded.device))
+    return out
+
