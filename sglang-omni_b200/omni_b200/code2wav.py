@@ -282,7 +282,8 @@ class Qwen3OmniIncrementalCodec:
         if conv.groups != 1:
             y = F.conv1d(padded.transpose(1, 2), conv.weight, None, 1, 0, conv.dilation, conv.groups)
             y = y.transpose(1, 2).contiguous()
-        elif gemm is not None and conv.in_channels % 32 == 0 and conv.out_channels % 32 == 0:
+        elif (gemm is not None and conv.in_channels % 32 == 0 and conv.out_channels % 32 == 0
+              and padded.dtype is torch.bfloat16 and conv.weight.dtype is torch.bfloat16):
             w = self._conv_weight(conv)
             if snake is None:
                 y = padded.new_empty(rows, length, conv.out_channels)
@@ -313,7 +314,8 @@ class Qwen3OmniIncrementalCodec:
         conv, s = t.conv, t.stride
         taps, cout = conv.kernel_size[0], conv.out_channels
         gemm = getattr(self.k, "conv_gemm", None)
-        if gemm is not None and conv.in_channels % 32 == 0 and (taps * cout) % 32 == 0 and frames.is_contiguous():
+        if (gemm is not None and conv.in_channels % 32 == 0 and (taps * cout) % 32 == 0 and frames.is_contiguous()
+                and frames.dtype is torch.bfloat16 and conv.weight.dtype is torch.bfloat16):
             key = ("transposed", id(conv))
             w = self._weights.get(key)
             if w is None:  # [taps x C_out, C_in]: the 1x1 conv form of the taps' GEMM
