@@ -296,6 +296,23 @@ def run_extra_configs(args) -> dict:
         entry = {k: line[k] for k in keep if k in line}
         entry["workload"] = line.get("config", {}).get("workload")
         out[f"config{c}"] = entry
+    # the streaming vocoder that consumes the step's codes: the Qwen3-Omni code2wav slot
+    # decode (64 streams x 10 new frames, graph-replayed) and its kernels
+    try:
+        proc = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--vocoder"], capture_output=True, text=True,
+                              timeout=900)
+        kernels, decode = [], None
+        for ln in proc.stdout.splitlines():
+            if ln.startswith("{"):
+                d = json.loads(ln)
+                if "step" in d:
+                    decode = d
+                else:
+                    kernels.append(d)
+        out["code2wav"] = {"decode": decode, "kernels": kernels} if decode else {
+            "error": f"exit {proc.returncode}: {proc.stderr[-300:]}"}
+    except subprocess.TimeoutExpired:
+        out["code2wav"] = {"error": "timed out"}
     return out
 
 
@@ -577,6 +594,39 @@ def run_vocoder(args) -> None:
         print(json.dumps({"kernel": name, "shape": shape, "us": secs * 1e6, "algorithmic_bytes": nbytes,
                           "achieved_gbs": gbs, "peak_gbs": hbm, "frac": gbs / hbm, "peak_kind": kind}))
     del xs, rs, outs, sums, pads
+
+    # the implicit-GEMM causal conv (tcgen05) on code2wav decode shapes: the dilated 7-tap
+    # conv of a residual unit, plain and with the next SnakeBeta fused in its epilogue
+    from omni_b200 import ops
+
+    _, tflops_peak, _ = measured_peaks()
+    for rows, length, ch, dil, fused in ((64, 1600, 384, 3, False), (64, 1600, 384, 3, True),
+                                         (64, 6400, 192, 9, True), (64, 320, 768, 1, True)):
+        taps = 7
+        hist = (taps - 1) * dil
+        pads3 = [torch.randn(rows, hist + length, ch, device=dev, dtype=bf) for _ in range(2)]
+        w = (torch.randn(ch, taps * ch, device=dev) / (taps * ch) ** 0.5).to(bf)
+        ys = [torch.empty(rows, length, ch, device=dev, dtype=bf) for _ in range(2)]
+        cf = SnakeBetaCoefficients.from_activation(_Act(ch))
+        bch = torch.randn(ch, device=dev, dtype=bf)
+        cyc3 = {"i": 0}
+
+        def cgemm():
+            i = cyc3["i"] % 2
+            cyc3["i"] += 1
+            if fused:
+                ops.conv1d_gemm(pads3[i], w, taps=taps, dilation=dil, length=length, out=ys[i], bias=bch,
+                                alpha_scale=cf.alpha_scale, inverse_beta=cf.inverse_beta)
+            else:
+                ops.conv1d_gemm(pads3[i], w, taps=taps, dilation=dil, length=length, out=ys[i])
+
+        t = time_kernel(cgemm, 20)
+        flops = 2.0 * rows * length * ch * taps * ch
+        print(json.dumps({"kernel": "conv1d_gemm" + (" + SnakeBeta epilogue" if fused else ""),
+                          "shape": f"[{rows}, {hist}+{length}, {ch}] -> {ch}, 7 taps, dilation {dil}",
+                          "us": t * 1e6, "algorithmic_flops": flops, "achieved_tflops": flops / t / 1e12,
+                          "peak_tflops": tflops_peak, "frac": flops / t / 1e12 / tflops_peak, "peak_kind": kind}))
+        del pads3, ys
 
     # the whole code2wav slot decode: Qwen3-Omni code2wav geometry (transformers' defaults:
     # 8-layer pre-transformer, decoder_dim 1536, 16 quantizers of 2048), random bf16

@@ -14,9 +14,10 @@
 // TMA in the same stage.  KB = 64 channels (128-byte swizzle) when C_in is a multiple
 // of 64, else 32 (64-byte swizzle).
 //
-// Roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer (one elected
-// lane), warps 2..5 drain TMEM (warp w reads lanes 32 (w % 4) ..) and run the
-// epilogue: the bf16 conv output, or fused with the vocoder's next step
+// Roles (320 threads, two CTAs an SM so that one CTA's epilogue runs while the other
+// feeds the tensor cores): warp 0 = TMA producer, warp 1 = MMA issuer (one elected
+// lane), warps 2..9 drain TMEM (warp w reads lanes 32 (w % 4) .., half of the column
+// chunks each) and run the epilogue: the bf16 conv output, or fused with the vocoder's next step
 // SnakeBeta(conv + bias [+ residual]) with the same rounding points as
 // bias_snake_beta_kernel (vocoder.cu), the pre-activation sum optionally stored.
 #include <cuda.h>
@@ -32,7 +33,7 @@ namespace {
 OMNI_DEFINE_STATUS(conv_gemm)
 
 constexpr int kConvM = 128;       // output positions per CTA
-constexpr int kConvThreads = 192;
+constexpr int kConvThreads = 320;  // producer, MMA, 8 epilogue warps
 constexpr int kConvMaxStages = 8;
 constexpr int kConvMaxN = 256;
 
@@ -68,7 +69,7 @@ OMNI_DEVINL uint64_t smem_desc_sw64(const void* smem_ptr) {
 
 OMNI_DEVINL float rbf(float f) { return bf2f(f2bf(f)); }
 
-__global__ void __launch_bounds__(kConvThreads, 1)
+__global__ void __launch_bounds__(kConvThreads, 2)
     conv_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const __grid_constant__ ConvGemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -169,17 +170,19 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       else mbar_arrive(done);
     }
   } else {
-    // epilogue: warp w drains TMEM lanes 32 (w % 4) .. + 31 = positions t0 + that
+    // epilogue: warp w drains TMEM lanes 32 (w % 4) .. + 31 = positions t0 + that, the
+    // 32-column chunks 32 h, 32 h + 64, ... with h = (w - 2) / 4 (two warps a lane quarter)
     if (!mbar_wait(done, 0)) {
       report_status(kDevTimeoutMma);
       *abort_flag = 1;
     }
     tc_fence_after();
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int t = t0 + q * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     const bool aborted = *reinterpret_cast<volatile int*>(abort_flag) != 0;
-    for (int c = 0; c < p.n_tile && !aborted; c += 32) {
+    for (int c = half * 32; c < p.n_tile && !aborted; c += 64) {
       uint32_t r[32];
       tmem_ld_32x32b_x32(lane_base + (uint32_t)c, r);
       tc_wait_ld();
@@ -315,7 +318,8 @@ extern "C" OMNI_API int omni_conv1d_gemm(const void* padded, int64_t rows, int64
   p.b_bytes = (uint32_t)nt * p.kb * 2;
   const size_t fixed = 1024 + (2 * kConvMaxStages + 1) * 8 + 16;
   int st = kConvMaxStages;
-  while (st > 2 && fixed + (size_t)st * (p.a_bytes + p.b_bytes) > 200 * 1024) --st;
+  // two CTAs an SM (one's epilogue runs under the other's main loop): at most ~110 KB each
+  while (st > 2 && fixed + (size_t)st * (p.a_bytes + p.b_bytes) > 110 * 1024) --st;
   if (st > p.num_k) st = p.num_k < 2 ? 2 : p.num_k;
   p.stages = st;
   p.snake = snake ? 1 : 0;
@@ -332,7 +336,7 @@ extern "C" OMNI_API int omni_conv1d_gemm(const void* padded, int64_t rows, int64
     return set_error(OMNI_ERR_UNSUPPORTED, "conv1d_gemm: tensor map encoding failed");
   const size_t smem = fixed + (size_t)st * (p.a_bytes + p.b_bytes);
   const cudaError_t ae = once_per_device(reinterpret_cast<const void*>(conv_gemm_kernel), kAttrSmem, [] {
-    return cudaFuncSetAttribute(conv_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024 + 2048);
+    return cudaFuncSetAttribute(conv_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
   });
   if (ae != cudaSuccess) return check_launch(ae);
   const dim3 grid((unsigned)((length + kConvM - 1) / kConvM), (unsigned)rows, (unsigned)(cout / nt));
