@@ -7,8 +7,11 @@
 // GEMMs of its transposed convs).  The windows are never written to memory: a CTA
 // owns 128 output positions of one row (the MMA's M axis, TMEM lanes) and a tile of
 // output channels (N <= 256, TMEM columns); its K loop walks (tap j, channel block),
-// and the A tile of each step is the 128 x KB box of the channels-last input that
-// starts at position t0 + j * dil, one TMA copy of the 2D view [rows * Lp, C_in].
+// and the A tile of each step is the 128 x KB window of the channels-last input that
+// starts at position t0 + j * dil in the 2D view [rows * Lp, C_in].  When 128 +
+// (taps - 1) dil <= 256 one TMA box of that many positions per channel block serves
+// every tap (the MMA's descriptor starts j dil rows into it), which cuts the input's
+// reads from L2 by the tap count; otherwise each step loads its own 128-row box.
 // Positions past a row's L read the next row's samples or the fill value and are
 // never stored.  B tiles (KB x N of the [C_out, taps * C_in] weight matrix) come by
 // TMA in the same stage.  KB = 64 channels (128-byte swizzle) when C_in is a multiple
@@ -41,9 +44,11 @@ struct ConvGemmParams {
   int rows, length;        // batch rows, output positions per row
   int64_t lp;              // input positions per row (history + length)
   int cin, cout, taps, dil;
-  int kb, kb_per_tap, num_k;
-  int n_tile, stages, tmem_cols;
-  uint32_t a_bytes, b_bytes;
+  int kb, num_k;           // channels per K block; K steps = (C_in / kb) x taps, taps inner
+  int n_tile, tmem_cols;
+  int a_union;             // 1: one A box of 128 + (taps - 1) dil positions per channel block
+  int a_stages, b_stages;  // ring depths of the A and B tiles
+  uint32_t a_bytes, a_tx, b_bytes;  // A stage bytes (1024-aligned), A box bytes, B stage bytes
   int snake;               // 0: out = bf16(conv); 1: SnakeBeta(conv + bias [+ residual])
   const uint16_t* bias;
   const uint16_t* residual;  // contiguous [rows, length, cout] or null
@@ -76,19 +81,23 @@ __global__ void __launch_bounds__(kConvThreads, 2)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * kConvM, row = blockIdx.y, n0 = blockIdx.z * p.n_tile;
-  const int ST = p.stages;
+  const int SA = p.a_stages, SB = p.b_stages;
   uint8_t* a_smem = smem;
-  uint8_t* b_smem = smem + ST * p.a_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(b_smem + ST * p.b_bytes);
-  uint64_t* empty = full + kConvMaxStages;
-  uint64_t* done = empty + kConvMaxStages;
+  uint8_t* b_smem = smem + SA * p.a_bytes;
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(b_smem + SB * p.b_bytes);
+  uint64_t* empty_a = full_a + kConvMaxStages;
+  uint64_t* full_b = empty_a + kConvMaxStages;
+  uint64_t* empty_b = full_b + kConvMaxStages;
+  uint64_t* done = empty_b + kConvMaxStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < kConvMaxStages; ++s) {
+      mbar_init(&full_a[s], 1);
+      mbar_init(&empty_a[s], 1);
+      mbar_init(&full_b[s], 1);
+      mbar_init(&empty_b[s], 1);
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -108,62 +117,81 @@ __global__ void __launch_bounds__(kConvThreads, 2)
   griddep_launch();
 
   const int64_t a_row0 = (int64_t)row * p.lp + t0;
+  // K step i = (channel block cb, tap): cb = i / taps, tap = i % taps.  A tiles: one per
+  // step, or with a_union one per channel block (the box covers every tap's window; the
+  // MMA of tap j starts j x dil rows into it).  A step's A slot is its A index ka mod SA,
+  // its B slot i mod SB; a slot is refilled at round k once the MMAs of round k - 1 have
+  // released it.
   if (warp == 0) {
     const bool leader = elect_one();
-    int s = 0;
-    uint32_t ph = 0;
-    for (int i = 0; i < p.num_k; ++i) {
-      if (i >= ST && !__all_sync(0xFFFFFFFFu, mbar_wait(&empty[s], ph ^ 1u))) {
-        if (leader) {
-          report_status(kDevTimeoutMma);
-          *abort_flag = 1;
+    bool ok = true;
+    for (int i = 0; i < p.num_k && ok; ++i) {
+      const int cb = i / p.taps, tap = i - cb * p.taps;
+      if (!p.a_union || tap == 0) {
+        const int ka = p.a_union ? cb : i, sa = ka % SA;
+        if (ka >= SA && !__all_sync(0xFFFFFFFFu, mbar_wait(&empty_a[sa], (uint32_t)((ka / SA - 1) & 1)))) {
+          ok = false;
+          break;
         }
+        if (leader) {
+          mbar_arrive_expect_tx(&full_a[sa], p.a_tx);
+          tma_load_2d(a_smem + sa * p.a_bytes, &tmap_a, &full_a[sa], cb * p.kb,
+                      (int)(a_row0 + (p.a_union ? 0 : (int64_t)tap * p.dil)));
+        }
+      }
+      const int sb = i % SB;
+      if (i >= SB && !__all_sync(0xFFFFFFFFu, mbar_wait(&empty_b[sb], (uint32_t)((i / SB - 1) & 1)))) {
+        ok = false;
         break;
       }
       if (leader) {
-        const int tap = i / p.kb_per_tap, cb = i - tap * p.kb_per_tap;
-        mbar_arrive_expect_tx(&full[s], p.a_bytes + p.b_bytes);
-        tma_load_2d(a_smem + s * p.a_bytes, &tmap_a, &full[s], cb * p.kb, (int)(a_row0 + (int64_t)tap * p.dil));
-        tma_load_2d(b_smem + s * p.b_bytes, &tmap_b, &full[s], tap * p.cin + cb * p.kb, n0);
+        mbar_arrive_expect_tx(&full_b[sb], p.b_bytes);
+        tma_load_2d(b_smem + sb * p.b_bytes, &tmap_b, &full_b[sb], tap * p.cin + cb * p.kb, n0);
       }
       __syncwarp();
-      if (++s == ST) {
-        s = 0;
-        ph ^= 1u;
-      }
+    }
+    if (!ok && leader) {
+      report_status(kDevTimeoutMma);
+      *abort_flag = 1;
     }
   } else if (warp == 1) {
     const bool leader = elect_one();
     const uint32_t idesc = idesc_bf16_f32(kConvM, p.n_tile);
     const bool sw128 = p.kb == 64;
-    int s = 0;
-    uint32_t ph = 0;
+    const uint32_t row_bytes = (uint32_t)p.kb * 2;
     bool ok = true;
     for (int i = 0; i < p.num_k; ++i) {
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full[s], ph))) {
-        if (leader) {
-          report_status(kDevTimeoutTma);
-          *abort_flag = 1;
-        }
+      const int cb = i / p.taps, tap = i - cb * p.taps;
+      const int ka = p.a_union ? cb : i, sa = ka % SA, sb = i % SB;
+      if ((!p.a_union || tap == 0) && !__all_sync(0xFFFFFFFFu, mbar_wait(&full_a[sa], (uint32_t)((ka / SA) & 1)))) {
+        ok = false;
+        break;
+      }
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full_b[sb], (uint32_t)((i / SB) & 1)))) {
         ok = false;
         break;
       }
       tc_fence_after();
       if (leader) {
-        const uint8_t* as = a_smem + s * p.a_bytes;
-        const uint8_t* bs = b_smem + s * p.b_bytes;
-        const uint64_t ad = sw128 ? smem_desc_sw128(as) : smem_desc_sw64(as);
+        // tap j's window starts j x dil rows into the union box; the descriptor's base
+        // offset carries the row phase inside the swizzle pattern (bits 7.. of the start)
+        const uint8_t* as = a_smem + sa * p.a_bytes + (p.a_union ? (uint32_t)(tap * p.dil) * row_bytes : 0u);
+        const uint8_t* bs = b_smem + sb * p.b_bytes;
+        const uint32_t aaddr = smem_u32(as);
+        uint64_t ad = sw128 ? smem_desc_sw128(as) : smem_desc_sw64(as);
+        ad |= (uint64_t)((aaddr >> 7) & (sw128 ? 7u : 3u)) << 49;
         const uint64_t bd = sw128 ? smem_desc_sw128(bs) : smem_desc_sw64(bs);
         // 16 channels (32 bytes) per MMA: the start address advances by 2 16-byte units
         for (int kk = 0; kk < p.kb / 16; ++kk)
           tc_mma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&empty[s]);
+        tc_commit(&empty_b[sb]);
+        if (!p.a_union || tap == p.taps - 1) tc_commit(&empty_a[sa]);
       }
       __syncwarp();
-      if (++s == ST) {
-        s = 0;
-        ph ^= 1u;
-      }
+    }
+    if (!ok && leader) {
+      report_status(kDevTimeoutTma);
+      *abort_flag = 1;
     }
     if (leader) {
       if (ok) tc_commit(done);
@@ -301,8 +329,7 @@ extern "C" OMNI_API int omni_conv1d_gemm(const void* padded, int64_t rows, int64
   p.taps = taps;
   p.dil = dilation;
   p.kb = cin % 64 == 0 ? 64 : 32;
-  p.kb_per_tap = cin / p.kb;
-  p.num_k = taps * p.kb_per_tap;
+  p.num_k = taps * (cin / p.kb);
   // the output-channel tile: all of C_out when <= 256 (a multiple of 32), else the
   // widest multiple of 32 <= 256 that divides it
   int nt = cout;
@@ -314,14 +341,26 @@ extern "C" OMNI_API int omni_conv1d_gemm(const void* padded, int64_t rows, int64
   int tc = 32;
   while (tc < nt) tc <<= 1;
   p.tmem_cols = tc;
-  p.a_bytes = (uint32_t)kConvM * p.kb * 2;
   p.b_bytes = (uint32_t)nt * p.kb * 2;
-  const size_t fixed = 1024 + (2 * kConvMaxStages + 1) * 8 + 16;
-  int st = kConvMaxStages;
   // two CTAs an SM (one's epilogue runs under the other's main loop): at most ~110 KB each
-  while (st > 2 && fixed + (size_t)st * (p.a_bytes + p.b_bytes) > 110 * 1024) --st;
-  if (st > p.num_k) st = p.num_k < 2 ? 2 : p.num_k;
-  p.stages = st;
+  const size_t fixed = 1024 + (4 * kConvMaxStages + 1) * 8 + 16, budget = 110 * 1024;
+  const int union_rows = kConvM + (taps - 1) * dilation;
+  const uint32_t union_bytes = ((uint32_t)union_rows * p.kb * 2 + 1023u) & ~1023u;
+  // the union box when it fits a TMA box (<= 256 rows) and two A + two B slots fit
+  p.a_union = taps > 1 && union_rows <= 256 && fixed + 2 * (size_t)union_bytes + 2 * p.b_bytes <= budget;
+  if (p.a_union) {
+    p.a_bytes = union_bytes;
+    p.a_tx = (uint32_t)union_rows * p.kb * 2;
+    p.a_stages = 2;
+    int sb = kConvMaxStages;
+    while (sb > 2 && fixed + 2 * (size_t)union_bytes + (size_t)sb * p.b_bytes > budget) --sb;
+    p.b_stages = sb;
+  } else {
+    p.a_bytes = p.a_tx = (uint32_t)kConvM * p.kb * 2;
+    int st = kConvMaxStages;
+    while (st > 2 && fixed + (size_t)st * (p.a_bytes + p.b_bytes) > budget) --st;
+    p.a_stages = p.b_stages = st;
+  }
   p.snake = snake ? 1 : 0;
   p.bias = static_cast<const uint16_t*>(bias);
   p.residual = static_cast<const uint16_t*>(residual);
@@ -331,10 +370,10 @@ extern "C" OMNI_API int omni_conv1d_gemm(const void* padded, int64_t rows, int64
   p.out = static_cast<uint16_t*>(out);
   p.out_batch_stride = out_batch_stride;
   CUtensorMap ta, tb;
-  if (!conv_tmap(&ta, padded, rows * padded_positions, cin, cin, p.kb, kConvM) ||
+  if (!conv_tmap(&ta, padded, rows * padded_positions, cin, cin, p.kb, p.a_union ? union_rows : kConvM) ||
       !conv_tmap(&tb, weight, cout, (int64_t)taps * cin, (int64_t)taps * cin, p.kb, nt))
     return set_error(OMNI_ERR_UNSUPPORTED, "conv1d_gemm: tensor map encoding failed");
-  const size_t smem = fixed + (size_t)st * (p.a_bytes + p.b_bytes);
+  const size_t smem = fixed + (size_t)p.a_stages * p.a_bytes + (size_t)p.b_stages * p.b_bytes;
   const cudaError_t ae = once_per_device(reinterpret_cast<const void*>(conv_gemm_kernel), kAttrSmem, [] {
     return cudaFuncSetAttribute(conv_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
   });
