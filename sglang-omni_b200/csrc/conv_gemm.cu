@@ -173,13 +173,13 @@ __global__ void __launch_bounds__(kConvThreads, 2)
       }
       tc_fence_after();
       if (leader) {
-        // tap j's window starts j x dil rows into the union box; the descriptor's base
-        // offset carries the row phase inside the swizzle pattern (bits 7.. of the start)
+        // tap j's window starts j x dil rows into the union box: the swizzle is a function
+        // of the absolute shared-memory address (TMA wrote the box the same way), so a
+        // start inside a swizzle atom needs no base offset (measured: with the base-offset
+        // field set to the row phase the products were wrong, with 0 they match fp32)
         const uint8_t* as = a_smem + sa * p.a_bytes + (p.a_union ? (uint32_t)(tap * p.dil) * row_bytes : 0u);
         const uint8_t* bs = b_smem + sb * p.b_bytes;
-        const uint32_t aaddr = smem_u32(as);
-        uint64_t ad = sw128 ? smem_desc_sw128(as) : smem_desc_sw64(as);
-        ad |= (uint64_t)((aaddr >> 7) & (sw128 ? 7u : 3u)) << 49;
+        const uint64_t ad = sw128 ? smem_desc_sw128(as) : smem_desc_sw64(as);
         const uint64_t bd = sw128 ? smem_desc_sw128(bs) : smem_desc_sw64(bs);
         // 16 channels (32 bytes) per MMA: the start address advances by 2 16-byte units
         for (int kk = 0; kk < p.kb / 16; ++kk)
