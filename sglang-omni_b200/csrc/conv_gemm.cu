@@ -17,18 +17,15 @@
 // TMA in the same stage.  KB = 64 channels (128-byte swizzle) when C_in is a multiple
 // of 64, else 32 (64-byte swizzle).
 //
-// Persistent: a CTA walks tiles round robin with two TMEM accumulators, so that the
-// epilogue of one tile runs while the next tile's loads and MMAs go on (two CTAs an SM
-// when both CTAs' accumulators fit the 512 TMEM columns).  Roles (320 threads): warp
-// 0 = TMA producer, warp 1 = MMA issuer (one elected lane), warps 2..9 drain TMEM
-// (warp w reads lanes 32 (w % 4) .., half of the column chunks each) and run the
-// epilogue: the bf16 conv output, or fused with the vocoder's next step
+// Roles (320 threads, two CTAs an SM so that one CTA's epilogue runs while the other
+// feeds the tensor cores): warp 0 = TMA producer, warp 1 = MMA issuer (one elected
+// lane), warps 2..9 drain TMEM (warp w reads lanes 32 (w % 4) .., half of the column
+// chunks each) and run the epilogue: the bf16 conv output, or fused with the vocoder's next step
 // SnakeBeta(conv + bias [+ residual]) with the same rounding points as
 // bias_snake_beta_kernel (vocoder.cu), the pre-activation sum optionally stored.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include <algorithm>
 #include <mutex>
 
 #include "capi_util.h"
@@ -40,7 +37,6 @@ OMNI_DEFINE_STATUS(conv_gemm)
 
 constexpr int kConvM = 128;       // output positions per CTA
 constexpr int kConvThreads = 320;  // producer, MMA, 8 epilogue warps
-constexpr int kConvEpiWarps = 8;
 constexpr int kConvMaxStages = 8;
 constexpr int kConvMaxN = 256;
 
@@ -49,8 +45,7 @@ struct ConvGemmParams {
   int64_t lp;              // input positions per row (history + length)
   int cin, cout, taps, dil;
   int kb, num_k;           // channels per K block; K steps = (C_in / kb) x taps, taps inner
-  int n_tile, acc_cols;     // output channels per tile; TMEM columns of one accumulator (two)
-  int pos_tiles, n_tiles, total_tiles;
+  int n_tile, tmem_cols;
   int a_union;             // 1: one A box of 128 + (taps - 1) dil positions per channel block
   int a_stages, b_stages;  // ring depths of the A and B tiles
   uint32_t a_bytes, a_tx, b_bytes;  // A stage bytes (1024-aligned), A box bytes, B stage bytes
@@ -85,6 +80,7 @@ __global__ void __launch_bounds__(kConvThreads, 2)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * kConvM, row = blockIdx.y, n0 = blockIdx.z * p.n_tile;
   const int SA = p.a_stages, SB = p.b_stages;
   uint8_t* a_smem = smem;
   uint8_t* b_smem = smem + SA * p.a_bytes;
@@ -92,9 +88,8 @@ __global__ void __launch_bounds__(kConvThreads, 2)
   uint64_t* empty_a = full_a + kConvMaxStages;
   uint64_t* full_b = empty_a + kConvMaxStages;
   uint64_t* empty_b = full_b + kConvMaxStages;
-  uint64_t* acc_full = empty_b + kConvMaxStages;  // [2]: an accumulator's MMAs are done
-  uint64_t* acc_empty = acc_full + 2;             // [2]: the epilogue has drained it
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* done = empty_b + kConvMaxStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   if (threadIdx.x == 0) {
@@ -104,17 +99,14 @@ __global__ void __launch_bounds__(kConvThreads, 2)
       mbar_init(&full_b[s], 1);
       mbar_init(&empty_b[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], kConvEpiWarps);
-    }
+    mbar_init(done, 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, (uint32_t)(2 * p.acc_cols));
+    tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -124,51 +116,39 @@ __global__ void __launch_bounds__(kConvThreads, 2)
   griddep_wait();
   griddep_launch();
 
-  // Tiles (row, 128-position block, channel block), channel blocks fastest, dealt out
-  // round robin over the CTAs.  Within a tile, K step i = (channel block cb of the input,
-  // tap) with cb = i / taps: A tiles one per step or, with a_union, one per cb (the box
-  // covers every tap's window, the MMA of tap j starts j x dil rows into it); the A and B
-  // rings and the two TMEM accumulators run on across the CTA's tiles, so a tile's
-  // epilogue overlaps the next tile's loads and MMAs.
-  auto tile_coords = [&](int tile, int& row, int& t0, int& n0) {
-    const int nt = tile % p.n_tiles, rest = tile / p.n_tiles;
-    t0 = (rest % p.pos_tiles) * kConvM;
-    row = rest / p.pos_tiles;
-    n0 = nt * p.n_tile;
-  };
+  const int64_t a_row0 = (int64_t)row * p.lp + t0;
+  // K step i = (channel block cb, tap): cb = i / taps, tap = i % taps.  A tiles: one per
+  // step, or with a_union one per channel block (the box covers every tap's window; the
+  // MMA of tap j starts j x dil rows into it).  A step's A slot is its A index ka mod SA,
+  // its B slot i mod SB; a slot is refilled at round k once the MMAs of round k - 1 have
+  // released it.
   if (warp == 0) {
     const bool leader = elect_one();
     bool ok = true;
-    uint32_t ga = 0, gb = 0;
-    for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x) {
-      int row, t0, n0;
-      tile_coords(tile, row, t0, n0);
-      const int64_t a_row0 = (int64_t)row * p.lp + t0;
-      for (int i = 0; i < p.num_k; ++i) {
-        const int cb = i / p.taps, tap = i - cb * p.taps;
-        if (!p.a_union || tap == 0) {
-          const uint32_t ka = ga++, sa = ka % SA;
-          if (ka >= (uint32_t)SA && !__all_sync(0xFFFFFFFFu, mbar_wait(&empty_a[sa], (ka / SA - 1) & 1u))) {
-            ok = false;
-            break;
-          }
-          if (leader) {
-            mbar_arrive_expect_tx(&full_a[sa], p.a_tx);
-            tma_load_2d(a_smem + sa * p.a_bytes, &tmap_a, &full_a[sa], cb * p.kb,
-                        (int)(a_row0 + (p.a_union ? 0 : (int64_t)tap * p.dil)));
-          }
-        }
-        const uint32_t kb2 = gb++, sb = kb2 % SB;
-        if (kb2 >= (uint32_t)SB && !__all_sync(0xFFFFFFFFu, mbar_wait(&empty_b[sb], (kb2 / SB - 1) & 1u))) {
+    for (int i = 0; i < p.num_k && ok; ++i) {
+      const int cb = i / p.taps, tap = i - cb * p.taps;
+      if (!p.a_union || tap == 0) {
+        const int ka = p.a_union ? cb : i, sa = ka % SA;
+        if (ka >= SA && !__all_sync(0xFFFFFFFFu, mbar_wait(&empty_a[sa], (uint32_t)((ka / SA - 1) & 1)))) {
           ok = false;
           break;
         }
         if (leader) {
-          mbar_arrive_expect_tx(&full_b[sb], p.b_bytes);
-          tma_load_2d(b_smem + sb * p.b_bytes, &tmap_b, &full_b[sb], tap * p.cin + cb * p.kb, n0);
+          mbar_arrive_expect_tx(&full_a[sa], p.a_tx);
+          tma_load_2d(a_smem + sa * p.a_bytes, &tmap_a, &full_a[sa], cb * p.kb,
+                      (int)(a_row0 + (p.a_union ? 0 : (int64_t)tap * p.dil)));
         }
-        __syncwarp();
       }
+      const int sb = i % SB;
+      if (i >= SB && !__all_sync(0xFFFFFFFFu, mbar_wait(&empty_b[sb], (uint32_t)((i / SB - 1) & 1)))) {
+        ok = false;
+        break;
+      }
+      if (leader) {
+        mbar_arrive_expect_tx(&full_b[sb], p.b_bytes);
+        tma_load_2d(b_smem + sb * p.b_bytes, &tmap_b, &full_b[sb], tap * p.cin + cb * p.kb, n0);
+      }
+      __syncwarp();
     }
     if (!ok && leader) {
       report_status(kDevTimeoutMma);
@@ -180,49 +160,32 @@ __global__ void __launch_bounds__(kConvThreads, 2)
     const bool sw128 = p.kb == 64;
     const uint32_t row_bytes = (uint32_t)p.kb * 2;
     bool ok = true;
-    uint32_t ga = 0, gb = 0, lt = 0;
-    for (int tile = blockIdx.x; tile < p.total_tiles && ok; tile += gridDim.x, ++lt) {
-      const uint32_t acc = lt & 1u;
-      if (lt >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&acc_empty[acc], (lt / 2 - 1) & 1u))) {
+    for (int i = 0; i < p.num_k; ++i) {
+      const int cb = i / p.taps, tap = i - cb * p.taps;
+      const int ka = p.a_union ? cb : i, sa = ka % SA, sb = i % SB;
+      if ((!p.a_union || tap == 0) && !__all_sync(0xFFFFFFFFu, mbar_wait(&full_a[sa], (uint32_t)((ka / SA) & 1)))) {
+        ok = false;
+        break;
+      }
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full_b[sb], (uint32_t)((i / SB) & 1)))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t dt = tmem + acc * (uint32_t)p.acc_cols;
-      for (int i = 0; i < p.num_k; ++i) {
-        const int cb = i / p.taps, tap = i - cb * p.taps;
-        const bool new_a = !p.a_union || tap == 0;
-        const uint32_t ka = new_a ? ga++ : ga - 1, sa = ka % SA;
-        const uint32_t kb2 = gb++, sb = kb2 % SB;
-        if (new_a && !__all_sync(0xFFFFFFFFu, mbar_wait(&full_a[sa], (ka / SA) & 1u))) {
-          ok = false;
-          break;
-        }
-        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full_b[sb], (kb2 / SB) & 1u))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (leader) {
-          // tap j's window starts j x dil rows into the union box: the swizzle is a function
-          // of the absolute shared-memory address (TMA wrote the box the same way), so a
-          // start inside a swizzle atom needs no base offset (measured: with the base-offset
-          // field set to the row phase the products were wrong, with 0 they match fp32)
-          const uint8_t* as = a_smem + sa * p.a_bytes + (p.a_union ? (uint32_t)(tap * p.dil) * row_bytes : 0u);
-          const uint8_t* bs = b_smem + sb * p.b_bytes;
-          const uint64_t ad = sw128 ? smem_desc_sw128(as) : smem_desc_sw64(as);
-          const uint64_t bd = sw128 ? smem_desc_sw128(bs) : smem_desc_sw64(bs);
-          // 16 channels (32 bytes) per MMA: the start address advances by 2 16-byte units
-          for (int kk = 0; kk < p.kb / 16; ++kk)
-            tc_mma_bf16(dt, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(&empty_b[sb]);
-          if (!p.a_union || tap == p.taps - 1) tc_commit(&empty_a[sa]);
-        }
-        __syncwarp();
-      }
       if (leader) {
-        if (ok) tc_commit(&acc_full[acc]);
-        else mbar_arrive(&acc_full[acc]);
+        // tap j's window starts j x dil rows into the union box: the swizzle is a function
+        // of the absolute shared-memory address (TMA wrote the box the same way), so a
+        // start inside a swizzle atom needs no base offset (measured: with the base-offset
+        // field set to the row phase the products were wrong, with 0 they match fp32)
+        const uint8_t* as = a_smem + sa * p.a_bytes + (p.a_union ? (uint32_t)(tap * p.dil) * row_bytes : 0u);
+        const uint8_t* bs = b_smem + sb * p.b_bytes;
+        const uint64_t ad = sw128 ? smem_desc_sw128(as) : smem_desc_sw64(as);
+        const uint64_t bd = sw128 ? smem_desc_sw128(bs) : smem_desc_sw64(bs);
+        // 16 channels (32 bytes) per MMA: the start address advances by 2 16-byte units
+        for (int kk = 0; kk < p.kb / 16; ++kk)
+          tc_mma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&empty_b[sb]);
+        if (!p.a_union || tap == p.taps - 1) tc_commit(&empty_a[sa]);
       }
       __syncwarp();
     }
@@ -230,84 +193,78 @@ __global__ void __launch_bounds__(kConvThreads, 2)
       report_status(kDevTimeoutTma);
       *abort_flag = 1;
     }
+    if (leader) {
+      if (ok) tc_commit(done);
+      else mbar_arrive(done);
+    }
   } else {
-    // epilogue: warp w drains TMEM lanes 32 (w % 4) .. + 31 (the tile's positions t0 + that),
-    // the 32-column chunks 32 h, 32 h + 64, ... with h = (w - 2) / 4 (two warps a lane quarter)
+    // epilogue: warp w drains TMEM lanes 32 (w % 4) .. + 31 = positions t0 + that, the
+    // 32-column chunks 32 h, 32 h + 64, ... with h = (w - 2) / 4 (two warps a lane quarter)
+    if (!mbar_wait(done, 0)) {
+      report_status(kDevTimeoutMma);
+      *abort_flag = 1;
+    }
+    tc_fence_after();
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
-    uint32_t lt = 0;
-    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++lt) {
-      const uint32_t acc = lt & 1u;
-      if (!mbar_wait(&acc_full[acc], (lt / 2) & 1u)) {
-        report_status(kDevTimeoutMma);
-        *abort_flag = 1;
-      }
-      tc_fence_after();
-      if (*reinterpret_cast<volatile int*>(abort_flag) != 0) break;
-      int row, t0, n0;
-      tile_coords(tile, row, t0, n0);
-      const int t = t0 + q * 32 + lane;
-      const uint32_t lane_base = tmem + acc * (uint32_t)p.acc_cols + ((uint32_t)(q * 32) << 16);
-      for (int c = half * 32; c < p.n_tile; c += 64) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(lane_base + (uint32_t)c, r);
-        tc_wait_ld();
-        const int nb = n0 + c;
-        if (t >= p.length || nb >= p.cout) continue;
-        const int64_t pos = (int64_t)row * p.length + t;  // contiguous [rows, length, cout]
-        uint16_t* dst = p.out + (int64_t)row * p.out_batch_stride + (int64_t)t * p.cout + nb;
-        const int cnt = min(32, p.cout - nb);  // a multiple of 8 (cout % 8 == 0)
-        for (int v = 0; v < cnt; v += 8) {
-          uint32_t o[4], sv[4];
-          uint4 rv = make_uint4(0, 0, 0, 0), bv = make_uint4(0, 0, 0, 0), av = bv, iv = bv;
-          if (p.snake) {
-            bv = *reinterpret_cast<const uint4*>(p.bias + nb + v);
-            av = *reinterpret_cast<const uint4*>(p.alpha_scale + nb + v);
-            iv = *reinterpret_cast<const uint4*>(p.inverse_beta + nb + v);
-            if (p.residual) rv = *reinterpret_cast<const uint4*>(p.residual + pos * p.cout + nb + v);
-          }
-          const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w}, aw[4] = {av.x, av.y, av.z, av.w};
-          const uint32_t iw[4] = {iv.x, iv.y, iv.z, iv.w}, rw[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            float y2[2], s2[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const float conv = rbf(__uint_as_float(r[v + 2 * h + e]));  // the conv's bf16 output
-              if (!p.snake) {
-                y2[e] = conv;
-                s2[e] = 0.0f;
-                continue;
-              }
-              const uint32_t pick = e ? 16u : 0u;
-              const float b = bf2f((uint16_t)(bw[h] >> pick)), a = bf2f((uint16_t)(aw[h] >> pick));
-              const float ib = bf2f((uint16_t)(iw[h] >> pick));
-              float total = rbf(conv + b);
-              if (p.residual) total = rbf(total + bf2f((uint16_t)(rw[h] >> pick)));
-              s2[e] = total;
-              const float phase = rbf(total * a);
-              const float sine = rbf(sinf(phase));
-              const float sq = rbf(sine * sine);
-              const float scaled = rbf(ib * sq);
-              y2[e] = total + scaled;
-            }
-            o[h] = pack_bf2(y2[0], y2[1]);
-            sv[h] = pack_bf2(s2[0], s2[1]);
-          }
-          *reinterpret_cast<uint4*>(dst + v) = make_uint4(o[0], o[1], o[2], o[3]);
-          if (p.snake && p.sum_out)
-            *reinterpret_cast<uint4*>(p.sum_out + pos * p.cout + nb + v) = make_uint4(sv[0], sv[1], sv[2], sv[3]);
+    const int t = t0 + q * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    const bool aborted = *reinterpret_cast<volatile int*>(abort_flag) != 0;
+    for (int c = half * 32; c < p.n_tile && !aborted; c += 64) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(lane_base + (uint32_t)c, r);
+      tc_wait_ld();
+      const int nb = n0 + c;
+      if (t >= p.length || nb >= p.cout) continue;
+      const int64_t pos = (int64_t)row * p.length + t;  // contiguous [rows, length, cout]
+      uint16_t* dst = p.out + (int64_t)row * p.out_batch_stride + (int64_t)t * p.cout + nb;
+      const int cnt = min(32, p.cout - nb);  // a multiple of 8 (cout % 8 == 0)
+      for (int v = 0; v < cnt; v += 8) {
+        uint32_t o[4], sv[4];
+        uint4 rv = make_uint4(0, 0, 0, 0), bv = make_uint4(0, 0, 0, 0), av = bv, iv = bv;
+        if (p.snake) {
+          bv = *reinterpret_cast<const uint4*>(p.bias + nb + v);
+          av = *reinterpret_cast<const uint4*>(p.alpha_scale + nb + v);
+          iv = *reinterpret_cast<const uint4*>(p.inverse_beta + nb + v);
+          if (p.residual) rv = *reinterpret_cast<const uint4*>(p.residual + pos * p.cout + nb + v);
         }
+        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w}, aw[4] = {av.x, av.y, av.z, av.w};
+        const uint32_t iw[4] = {iv.x, iv.y, iv.z, iv.w}, rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float y2[2], s2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float conv = rbf(__uint_as_float(r[v + 2 * h + e]));  // the conv's bf16 output
+            if (!p.snake) {
+              y2[e] = conv;
+              s2[e] = 0.0f;
+              continue;
+            }
+            const uint32_t pick = e ? 16u : 0u;
+            const float b = bf2f((uint16_t)(bw[h] >> pick)), a = bf2f((uint16_t)(aw[h] >> pick));
+            const float ib = bf2f((uint16_t)(iw[h] >> pick));
+            float total = rbf(conv + b);
+            if (p.residual) total = rbf(total + bf2f((uint16_t)(rw[h] >> pick)));
+            s2[e] = total;
+            const float phase = rbf(total * a);
+            const float sine = rbf(sinf(phase));
+            const float sq = rbf(sine * sine);
+            const float scaled = rbf(ib * sq);
+            y2[e] = total + scaled;
+          }
+          o[h] = pack_bf2(y2[0], y2[1]);
+          sv[h] = pack_bf2(s2[0], s2[1]);
+        }
+        *reinterpret_cast<uint4*>(dst + v) = make_uint4(o[0], o[1], o[2], o[3]);
+        if (p.snake && p.sum_out)
+          *reinterpret_cast<uint4*>(p.sum_out + pos * p.cout + nb + v) = make_uint4(sv[0], sv[1], sv[2], sv[3]);
       }
-      // this warp's share of the accumulator is read: one arrive per epilogue warp
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, (uint32_t)(2 * p.acc_cols));
+  if (warp == 1) tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn_conv() {
@@ -383,14 +340,10 @@ extern "C" OMNI_API int omni_conv1d_gemm(const void* padded, int64_t rows, int64
   p.n_tile = nt;
   int tc = 32;
   while (tc < nt) tc <<= 1;
-  p.acc_cols = tc;
+  p.tmem_cols = tc;
   p.b_bytes = (uint32_t)nt * p.kb * 2;
-  // two TMEM accumulators a CTA (2 tc columns): two CTAs an SM when both fit the 512
-  // columns (tc <= 128, then at most ~110 KB of shared memory each), else one CTA an SM
-  // with deeper rings (the shared-memory request itself keeps a second CTA off the SM)
-  const int per_sm = tc <= 128 ? 2 : 1;
-  const size_t fixed = 1024 + (4 * kConvMaxStages + 4) * 8 + 16;
-  const size_t budget = per_sm == 2 ? 110 * 1024 : 200 * 1024;
+  // two CTAs an SM (one's epilogue runs under the other's main loop): at most ~110 KB each
+  const size_t fixed = 1024 + (4 * kConvMaxStages + 1) * 8 + 16, budget = 110 * 1024;
   const int union_rows = kConvM + (taps - 1) * dilation;
   const uint32_t union_bytes = ((uint32_t)union_rows * p.kb * 2 + 1023u) & ~1023u;
   // the union box when it fits a TMA box (<= 256 rows) and two A + two B slots fit
@@ -408,11 +361,6 @@ extern "C" OMNI_API int omni_conv1d_gemm(const void* padded, int64_t rows, int64
     while (st > 2 && fixed + (size_t)st * (p.a_bytes + p.b_bytes) > budget) --st;
     p.a_stages = p.b_stages = st;
   }
-  p.pos_tiles = (int)((length + kConvM - 1) / kConvM);
-  p.n_tiles = cout / nt;
-  const int64_t total = rows * (int64_t)p.pos_tiles * p.n_tiles;
-  if (total >= (int64_t(1) << 31)) return set_error(OMNI_ERR_UNSUPPORTED, "conv1d_gemm: too many tiles");
-  p.total_tiles = (int)total;
   p.snake = snake ? 1 : 0;
   p.bias = static_cast<const uint16_t*>(bias);
   p.residual = static_cast<const uint16_t*>(residual);
@@ -425,15 +373,12 @@ extern "C" OMNI_API int omni_conv1d_gemm(const void* padded, int64_t rows, int64
   if (!conv_tmap(&ta, padded, rows * padded_positions, cin, cin, p.kb, p.a_union ? union_rows : kConvM) ||
       !conv_tmap(&tb, weight, cout, (int64_t)taps * cin, (int64_t)taps * cin, p.kb, nt))
     return set_error(OMNI_ERR_UNSUPPORTED, "conv1d_gemm: tensor map encoding failed");
-  size_t smem = fixed + (size_t)p.a_stages * p.a_bytes + (size_t)p.b_stages * p.b_bytes;
-  if (per_sm == 1 && smem < 120 * 1024) smem = 120 * 1024;
+  const size_t smem = fixed + (size_t)p.a_stages * p.a_bytes + (size_t)p.b_stages * p.b_bytes;
   const cudaError_t ae = once_per_device(reinterpret_cast<const void*>(conv_gemm_kernel), kAttrSmem, [] {
-    return cudaFuncSetAttribute(conv_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    return cudaFuncSetAttribute(conv_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
   });
   if (ae != cudaSuccess) return check_launch(ae);
-  prefer_max_shared(reinterpret_cast<const void*>(conv_gemm_kernel));
-  const int64_t ctas = std::min<int64_t>(total, (int64_t)per_sm * device_sm_count());
-  const dim3 grid((unsigned)ctas);
+  const dim3 grid((unsigned)((length + kConvM - 1) / kConvM), (unsigned)rows, (unsigned)(cout / nt));
   return check_launch(launch(conv_gemm_kernel, grid, dim3(kConvThreads), smem, static_cast<cudaStream_t>(stream),
                              ta, tb, p));
 }
