@@ -23,15 +23,16 @@ What a slot carries between decodes:
 A stream's first decode reads no state and drops each transposed conv's left pad, as
 the whole-sequence forward trims it.
 
-Activations stay channels last ([rows, samples, channels]).  Ungrouped causal convs run
-on the implicit-GEMM tcgen05 kernel (omni_conv1d_gemm: no window is materialised) and the
-SnakeBeta that follows a conv (with its bias and residual adds) runs in that conv's
-epilogue, writing straight into the next conv's padded input; the SnakeBeta that follows
-a transposed conv (whose overlap is added after its GEMM) is the separate
-`fused_bias_snake_beta` kernel.  Transposed convs run their taps' GEMM on the same kernel
-(taps = 1).  The last conv is the clamped single-output-channel kernel.  The ConvNeXt
-depthwise conv is a cuDNN call, its pointwise layers and the pre-transformer's
-projections cuBLAS GEMMs, and the windowed attention an SDPA call.
+Activations stay channels last ([rows, samples, channels]).  The dilated 7-tap convs of
+the decoder's residual units run on the implicit-GEMM tcgen05 kernel (omni_conv1d_gemm: no
+window is materialised) with the SnakeBeta that follows them (bias and residual adds
+included) in its epilogue, writing straight into the next conv's padded input.  The 1x1
+convs, the first conv and the transposed convs' taps run as cuBLAS GEMMs (over a gathered
+window where taps > 1), each followed by the separate `fused_bias_snake_beta` kernel: for
+those shapes that measured faster (`_implicit`).  The last conv is the clamped
+single-output-channel kernel.  The ConvNeXt depthwise conv is a cuDNN call, its pointwise
+layers and the pre-transformer's projections cuBLAS GEMMs, and the windowed attention an
+SDPA call.
 """
 
 from __future__ import annotations
@@ -265,6 +266,18 @@ class Qwen3OmniIncrementalCodec:
             self._weights[key] = w
         return w
 
+    @staticmethod
+    def _implicit(conv) -> bool:
+        """Which convs take the implicit-GEMM kernel: the dilated multi-tap convs of at most
+        768 channels, where (with the next SnakeBeta in its epilogue) it measured faster on a
+        B200 than the gathered window + cuBLAS GEMM + separate SnakeBeta (64 streams x 10
+        frames, per conv: 768 ch 196 vs 224 us, 384 ch 315 vs 384, 192 ch 437 vs 673, 96 ch
+        903 vs 993); the 1x1 convs (whose epilogue outweighs their short K loop: 384 ch 273
+        vs 123 us), the transposed convs' GEMMs and the first 1024 -> 1536 conv are faster
+        on cuBLAS."""
+        return (conv.groups == 1 and conv.kernel_size[0] > 1 and conv.in_channels <= 768
+                and conv.in_channels % 32 == 0 and conv.out_channels % 32 == 0)
+
     def _conv(self, c: _CausalConv, padded: torch.Tensor, pool, slots, length: int, cold: bool, snake=None):
         """The causal conv's [rows, length, C_out] outputs without bias, its padded input's
         history exchanged with the slots first.  Ungrouped convs run as the implicit-GEMM
@@ -282,8 +295,8 @@ class Qwen3OmniIncrementalCodec:
         if conv.groups != 1:
             y = F.conv1d(padded.transpose(1, 2), conv.weight, None, 1, 0, conv.dilation, conv.groups)
             y = y.transpose(1, 2).contiguous()
-        elif (gemm is not None and conv.in_channels % 32 == 0 and conv.out_channels % 32 == 0
-              and padded.dtype is torch.bfloat16 and conv.weight.dtype is torch.bfloat16):
+        elif (gemm is not None and self._implicit(conv) and padded.dtype is torch.bfloat16
+              and conv.weight.dtype is torch.bfloat16):
             w = self._conv_weight(conv)
             if snake is None:
                 y = padded.new_empty(rows, length, conv.out_channels)
@@ -313,19 +326,7 @@ class Qwen3OmniIncrementalCodec:
         rows, n, _ = frames.shape
         conv, s = t.conv, t.stride
         taps, cout = conv.kernel_size[0], conv.out_channels
-        gemm = getattr(self.k, "conv_gemm", None)
-        if (gemm is not None and conv.in_channels % 32 == 0 and (taps * cout) % 32 == 0 and frames.is_contiguous()
-                and frames.dtype is torch.bfloat16 and conv.weight.dtype is torch.bfloat16):
-            key = ("transposed", id(conv))
-            w = self._weights.get(key)
-            if w is None:  # [taps x C_out, C_in]: the 1x1 conv form of the taps' GEMM
-                w = self._gemm_weight(conv).t().contiguous()
-                self._weights[key] = w
-            z = frames.new_empty(rows, n, taps * cout)
-            gemm(frames, w, taps=1, dilation=1, length=n, out=z)
-            z = z.view(rows, n, taps, cout)
-        else:
-            z = (frames.reshape(rows * n, -1) @ self._gemm_weight(conv)).view(rows, n, taps, cout)
+        z = (frames.reshape(rows * n, -1) @ self._gemm_weight(conv)).view(rows, n, taps, cout)
         if taps == s:
             y = z.reshape(rows, n * s, cout)
         elif taps == 2 * s:
