@@ -234,6 +234,11 @@ typedef struct OmniLinearArgs {
   int32_t* topk_ids;
   float* topk_weights;
   int32_t top_k;
+  /* Optional L2 prefetch (nullable): the launch's CTAs prefetch these bytes into
+   * L2 at their start, for a later launch on the stream (the next projection's
+   * weights); 16-byte aligned, no effect on this GEMM's results. */
+  const void* l2_prefetch;
+  int64_t l2_prefetch_bytes;
 } OmniLinearArgs;
 
 OMNI_API int omni_linear_fused(const OmniLinearArgs* args, void* stream);

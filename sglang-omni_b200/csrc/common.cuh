@@ -157,6 +157,10 @@ OMNI_DEVINL void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar, in
       "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+// Bulk prefetch of [src, src + bytes) into L2 (bytes a multiple of 16, src 16-byte aligned).
+OMNI_DEVINL void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 OMNI_DEVINL void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

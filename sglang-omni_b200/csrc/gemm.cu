@@ -99,6 +99,10 @@ struct GemmParams {
   int32_t* topk_ids;
   float* topk_w;
   int top_k;
+  // bytes to prefetch into L2 for a later launch (e.g. the next GEMM's weights), each
+  // CTA its slice, issued at the start ahead of griddepcontrol.wait
+  const uint8_t* l2_prefetch;
+  int64_t l2_prefetch_bytes;
   // test hook (omni_gemm_wait_probe): polls per bounded wait (0 = kWaitLimit) and
   // a producer that issues no copies, so that the waits run out
   uint32_t wait_limit;
@@ -223,6 +227,15 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   if (warp == 0 && lane == 0 && !p.withhold_loads) {
     mbar_arrive_expect_tx(pre_bar, (uint32_t)pre * (a_bytes + b_bytes));
     for (int i = 0; i < pre; ++i) load_w(i, kb_begin + i, pre_bar);
+  }
+  if (p.l2_prefetch != nullptr && warp == 2 && lane == 0) {
+    // this CTA's 16-byte aligned slice of the range, in pieces of at most 64 KB
+    const int64_t ctas = (int64_t)gridDim.x * gridDim.y * gridDim.z;
+    const int64_t cid = ((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    const int64_t per = ((p.l2_prefetch_bytes + ctas - 1) / ctas + 15) & ~(int64_t)15;
+    const int64_t b0 = cid * per;
+    const int64_t b1 = min(p.l2_prefetch_bytes & ~(int64_t)15, b0 + per);
+    for (int64_t b = b0; b < b1; b += 65536) bulk_prefetch_l2(p.l2_prefetch + b, (uint32_t)min((int64_t)65536, b1 - b));
   }
   griddep_wait();
   griddep_launch();
@@ -970,6 +983,12 @@ extern "C" OMNI_API int omni_linear_fused(const OmniLinearArgs* a, void* stream)
   gp.topk_ids = a->topk_ids;
   gp.topk_w = a->topk_weights;
   gp.top_k = a->top_k;
+  if (a->l2_prefetch != nullptr) {
+    if ((reinterpret_cast<uintptr_t>(a->l2_prefetch) & 15) != 0 || a->l2_prefetch_bytes < 0)
+      return set_error(OMNI_ERR_INVALID, "l2_prefetch must be 16-byte aligned with a non-negative size");
+    gp.l2_prefetch = static_cast<const uint8_t*>(a->l2_prefetch);
+    gp.l2_prefetch_bytes = a->l2_prefetch_bytes;
+  }
   return run_linear(a->x, a->rows, a->k, a->x_stride, a->w, a->n, a->epilogue, gp, a->splits,
                     static_cast<cudaStream_t>(stream));
 }

@@ -37,6 +37,7 @@ class OmniLinearArgs(ctypes.Structure):
         ("tokens_per_req", ctypes.c_int32), ("slot_stride", ctypes.c_int32), ("slot_base", ctypes.c_int32),
         ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
         ("topk_ids", ctypes.c_void_p), ("topk_weights", ctypes.c_void_p), ("top_k", ctypes.c_int32),
+        ("l2_prefetch", ctypes.c_void_p), ("l2_prefetch_bytes", ctypes.c_int64),
     ]
 
 
@@ -54,13 +55,16 @@ def linear_fused(
     qkv: dict | None = None,
     router: dict | None = None,
     splits: int = 0,
+    l2_prefetch: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """out = epilogue(rstd * (x @ w.T)) with the RMSNorm folded into w (gain already
     multiplied into its columns) and rstd from ss_in [parts, rows_cap] sums of squares.
     ss_out [parts, rows_cap] receives the output's per-tile sums of squares.
     qkv: head geometry, norms, rotary table and caches for EPI_QKV_ROPE.
     router: {"topk_ids": i32 [rows, k], "topk_weights": f32 [rows, k]} for EPI_ROUTER
-    (out receives the bf16 router logits)."""
+    (out receives the bf16 router logits).
+    l2_prefetch: a tensor (the next projection's weight) that this launch's CTAs
+    prefetch into L2 at their start."""
     a = OmniLinearArgs()
     a.x = x.data_ptr()
     a.rows, a.k = x.shape
@@ -105,6 +109,9 @@ def linear_fused(
         a.topk_ids = router["topk_ids"].data_ptr()
         a.topk_weights = router["topk_weights"].data_ptr()
         a.top_k = router["topk_ids"].shape[1]
+    if l2_prefetch is not None:
+        a.l2_prefetch = l2_prefetch.data_ptr()
+        a.l2_prefetch_bytes = l2_prefetch.numel() * l2_prefetch.element_size()
     _lib.call("omni_linear_fused", ctypes.addressof(a), _lib.stream_of(x.device))
     return out
 

@@ -113,6 +113,9 @@ class CodePredictor:
                 ws = max(ws, ops.linear_workspace_bytes(rows, k, n, e))
         self.workspace = torch.zeros(max(ws, 256), dtype=torch.uint8, device=self.device)
         self.scale = 1.0 / math.sqrt(D)
+        # each projection prefetches into L2 the weight of the projection two launches
+        # later in the chain (qkv -> gate_up, o -> down, gate_up -> next qkv / lm_head, ...)
+        self.prefetch_l2 = True
 
     # ------------------------------------------------------------------
     def set_sampling(self, *, temperature, top_k, top_p, seeds, do_sample, batch: int, row0: int = 0) -> None:
@@ -155,12 +158,19 @@ class CodePredictor:
         assert fused_raw_logit_block_k(self.sub_sampled_max_top_k) is not None
 
     # ------------------------------------------------------------------
+    def _chain(self, after: list) -> list:
+        ws = []
+        for li, lw in enumerate(self.w["layers"]):
+            ws += [self.folded[li]["qkv"], lw["o_proj"], self.folded[li]["gate_up"], lw["down_proj"]]
+        return ws + list(after)
+
     def forward_tokens(self, x: torch.Tensor, x_ss: torch.Tensor, *, batch: int, tokens: int,
-                       cache_len: int) -> torch.Tensor:
+                       cache_len: int, after: list | None = None) -> torch.Tensor:
         """The predictor stack on rows (request, token) at slots cache_len.. with input
         sums of squares x_ss (one part); leaves the residual stream in self.h and its sums
         of squares in self.ss, the input of the folded final norm of the lm_head
-        (predictor_forward_tokens, sglang_model.py:2036-2098)."""
+        (predictor_forward_tokens, sglang_model.py:2036-2098).  after: the weights the
+        stream's next projections use (for the L2 prefetch of the last layers)."""
         cfg = self.cfg
         rows = batch * tokens
         H, D = cfg.hidden_size, cfg.head_dim
@@ -168,10 +178,15 @@ class CodePredictor:
         eps = cfg.rms_norm_eps
         h, q, attn, act = self.h[:rows], self.q[:rows], self.attn[:rows], self.act[:rows]
         parts = H // 128
+        chain = self._chain(after or []) if self.prefetch_l2 else []
+
+        def pf(i):
+            return chain[i + 2] if i + 2 < len(chain) else None
+
         resid, ss_in, ss_parts = x, x_ss, 1
         for li, lw in enumerate(self.w["layers"]):
             ops.linear_fused(resid, self.folded[li]["qkv"], q, epilogue=ops.EPI_QKV_ROPE, ss_in=ss_in,
-                             ss_in_parts=ss_parts, norm_eps=eps,
+                             ss_in_parts=ss_parts, norm_eps=eps, l2_prefetch=pf(4 * li),
                              qkv=dict(num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=lw["q_norm"],
                                       k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin, tokens_per_req=tokens,
                                       slot_stride=cfg.cache_len, slot_base=cache_len, k_cache=self.k_cache[li],
@@ -179,11 +194,13 @@ class CodePredictor:
             ops.predictor_attention(q, self.k_cache[li], self.v_cache[li], num_q_heads=hq, num_kv_heads=hkv,
                                     head_dim=D, tokens_per_req=tokens, slot_stride=cfg.cache_len,
                                     slot_base=cache_len, sm_scale=self.scale, out=attn)
-            ops.linear_fused(attn, lw["o_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=resid, ss_out=self.ss)
+            ops.linear_fused(attn, lw["o_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=resid, ss_out=self.ss,
+                             l2_prefetch=pf(4 * li + 1))
             resid, ss_in, ss_parts = h, self.ss, parts
             ops.linear_fused(h, self.folded[li]["gate_up"], act, epilogue=ops.EPI_SWIGLU, ss_in=self.ss,
-                             ss_in_parts=parts, norm_eps=eps)
-            ops.linear_fused(act, lw["down_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=self.ss)
+                             ss_in_parts=parts, norm_eps=eps, l2_prefetch=pf(4 * li + 2))
+            ops.linear_fused(act, lw["down_proj"], h, epilogue=ops.EPI_RESIDUAL, residual=h, ss_out=self.ss,
+                             l2_prefetch=pf(4 * li + 3))
         return h
 
     def codebook_logits(self, j: int, batch: int) -> torch.Tensor:
@@ -240,14 +257,18 @@ class CodePredictor:
                   float(final_eps), _lib.ptr(hidden_out), self.layer0_embedding.data_ptr(), B, H,
                   pair.data_ptr(), summed.data_ptr(), self.pair_ss.data_ptr(), codes.data_ptr(), codes.stride(0),
                   _lib.stream_of(self.device))
-        h = self.forward_tokens(pair, self.pair_ss, batch=B, tokens=2, cache_len=0)
+        w0 = self.w["layers"][0]
+        nxt = [self.folded[0]["qkv"], w0["o_proj"]]
+        h = self.forward_tokens(pair, self.pair_ss, batch=B, tokens=2, cache_len=0,
+                                after=[self.lm_head_folded[0]] + nxt)
         argmax_all = not self.sub_has_sampled_rows
         parts = H // 128
         eps = cfg.rms_norm_eps
         for j in range(G - 1):
             rows = 2 * B if j == 0 else B
             ops.linear_fused(h[:rows], self.lm_head_folded[j], self.logits[j, :rows], epilogue=ops.EPI_STORE,
-                             ss_in=self.ss, ss_in_parts=parts, norm_eps=eps)
+                             ss_in=self.ss, ss_in_parts=parts, norm_eps=eps,
+                             l2_prefetch=nxt[1] if self.prefetch_l2 and j < G - 2 else None)
             predictor_sample_step(
                 self.codebook_logits(j, B),
                 temperatures=self.sub_temperature_tensor[:B],
@@ -268,5 +289,6 @@ class CodePredictor:
                 gathered_ss=self.next_ss[:B],
             )
             if j < G - 2:
-                h = self.forward_tokens(self.next_in[:B], self.next_ss[:B], batch=B, tokens=1, cache_len=2 + j)
+                h = self.forward_tokens(self.next_in[:B], self.next_ss[:B], batch=B, tokens=1, cache_len=2 + j,
+                                        after=[self.lm_head_folded[j + 1]] + (nxt if j + 1 < G - 2 else []))
         return codes.unsqueeze(-1), summed.unsqueeze(1)

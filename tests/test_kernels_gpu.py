@@ -378,6 +378,12 @@ def test_linear_fused_folded_norm_and_sumsq(rows):
     gu = ref_rmsnorm(out, gain, 1e-6).bfloat16().float() @ wgu.float().t()
     ref_act = torch.nn.functional.silu(gu[:, :N].bfloat16().float()) * gu[:, N:].bfloat16().float()
     close(act, ref_act, rel=2e-2, cos_min=0.9995)
+    # an L2 prefetch of another weight (odd size) leaves the results unchanged
+    act2 = torch.empty_like(act)
+    ops.linear_fused(out, ops.fold_norm(wgu, gain), act2, epilogue=ops.EPI_SWIGLU, ss_in=ss8, ss_in_parts=8,
+                     norm_eps=1e-6, l2_prefetch=wo.view(-1)[: wo.numel() - 24])
+    torch.cuda.synchronize()
+    assert torch.equal(act2, act)
 
 
 @pytest.mark.parametrize("hq,hkv,d,implicit", [(16, 2, 128, False), (16, 8, 64, True)])
