@@ -119,6 +119,19 @@ OMNI_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of a phase (for a warp that polls several barriers: try_wait
+// may suspend the thread on one barrier while another is already complete).
+OMNI_DEVINL bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait: about a second of polling at most (try_wait itself suspends
 // for a hardware-defined interval).  Returns false on timeout.
 constexpr uint32_t kWaitLimit = 1u << 22;

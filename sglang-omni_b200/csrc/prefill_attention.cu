@@ -3,8 +3,10 @@
 // mixed batch attend causally over their stream's pages, which the qkv epilogue has
 // just written).
 //
-// CTA = 128 queries of one stream x one query head; the stream's keys go by in tiles of
-// 128 (8 pages).  Ten warps:
+// Two kernels: prefill_attention_pair_kernel (below) when the query heads of a KV head
+// come in pairs (a CTA serves two of them, each K / V tile loaded once for both), and
+// prefill_attention_tc_kernel for an odd group size: CTA = 128 queries of one stream x
+// one query head; the stream's keys go by in tiles of 128 (8 pages).  Ten warps:
 //   warp 0    TMA producer: the Q tile once (two 64-column halves, 128B swizzle), then
 //             per key tile the 8 pages of K and of V, one 16-row x 64-column box per
 //             lane (32 lanes, 32 boxes), into a two-stage ring; pages past the stream
@@ -191,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
     // soon as its K has landed and its S buffer is free.  Lane 0 polls, the warp
     // follows its decision.
     auto ready = [&](uint64_t* bar, uint32_t parity) -> bool {
-      uint32_t r = lane == 0 ? (mbar_try_wait(bar, parity) ? 1u : 0u) : 0u;
+      uint32_t r = lane == 0 ? (mbar_test_wait(bar, parity) ? 1u : 0u) : 0u;
       return __shfl_sync(0xFFFFFFFFu, r, 0) != 0;
     };
     int jq = 0, ip = 0;
@@ -407,6 +409,340 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
   if (warp == 1) tmem_dealloc(tbase, 512);
 }
 
+// ---------------------------------------------------------------------------
+// GQA pair kernel: CTA = 128 queries of one stream x two query heads of one KV
+// head, so each K / V tile is loaded once for both heads.  Ten warps:
+//   warp 0    TMA producer: both heads' Q tiles once; per key tile the 8 pages of K
+//             into a two-stage K ring and (one tile behind) the 8 pages of V into a
+//             single V stage, one 16-row x 64-column box per lane (measured against
+//             one K stage with two V stages, and a three-slot ring that K and V take
+//             in turn: 981 against 1054 and 1027 us at config 2);
+//   warp 1    MMA issuer (polling its barriers without blocking): S_h(j) = Q_h K_j^T
+//             into head h's TMEM S buffer once K_j has landed and the head's softmax
+//             has released S_h(j-1); O_h += P_h(j) V_j once P_h(j) is written and V_j
+//             has landed;
+//   warps 2-5 softmax of head 0, warps 6-9 of head 1: one thread per query row (TMEM
+//             lane) over all 128 columns of the tile, so a row's max and sum stay in
+//             one thread: P = exp2(s * scale * log2 e - m) against the running max m
+//             in one pass, into the head's swizzled P buffer (K-major A operand of
+//             P V); the first tile and a tile whose max passes m by more than 2^8
+//             rescale O and the running sum and write P again.
+// Measured schedule (clock64 timeline of one CTA, 32 key tiles): the two heads run in
+// step, their softmaxes overlapping (~4 200 cycles a tile, two warps a sub-partition
+// hiding each other's latency), then the MMAs (~2 000 cycles): ~5 900 cycles a tile
+// pair, the tensor pipe ~35 % busy.  Making the heads take turns (one softmax while the
+// tensor core serves the other head) lengthened each softmax to ~3 200 cycles (one warp
+// a sub-partition) and the period to ~7 000; computing a share of the exponentials by a
+// polynomial on the FMA pipe, or twelve warps with setmaxnreg (no register spills),
+// were slower too.
+// Shared memory: Q 2 x 32 KB, K 2 x 32 KB, V 32 KB, P 2 x 32 KB (224 KB).
+// TMEM: S_0, S_1 (128 columns each), O_0, O_1 (128 each).
+// ---------------------------------------------------------------------------
+constexpr int kPairQOff = 0;                            // head h: + h * 32 KB
+constexpr int kPairKOff = 2 * kTileBytes;               // stage s: + s * 32 KB
+constexpr int kPairVOff = 4 * kTileBytes;
+constexpr int kPairPOff = 5 * kTileBytes;               // head h: + h * 32 KB
+constexpr int kPairBarOff = 7 * kTileBytes;             // 224 KB
+constexpr size_t kPairSmemBytes = (size_t)kPairBarOff + 256 + 1024;
+
+struct PairBars {
+  uint64_t q_full, k_full[2], k_empty[2], v_full, v_empty, s_full[2], s_free[2], p_full[2], pv_done[2], drain;
+  uint32_t tmem;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
+    const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+    const __grid_constant__ CUtensorMap tv, const __grid_constant__ PrefillTcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PairBars* bars = reinterpret_cast<PairBars*>(smem + kPairBarOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, h0 = 2 * blockIdx.y;  // query heads h0, h0 + 1
+  griddep_wait();
+  griddep_launch();
+  if (tile >= p.tile_indptr[p.streams]) return;
+  int lo = 0, hi = p.streams - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.tile_indptr[mid] <= tile) lo = mid;
+    else hi = mid - 1;
+  }
+  const int st = lo;
+  const int qs0 = p.qo_indptr[st], ext = p.qo_indptr[st + 1] - qs0;
+  const int64_t seq_len = p.seq_lens[st];
+  const int prefix = (int)(seq_len - ext);
+  const int q0 = (tile - p.tile_indptr[st]) * kRows;
+  const int nq = min(kRows, ext - q0);
+  const int kvh = h0 / (p.hq / p.hkv);
+  const int pg0 = p.page_indptr[st], npages = p.page_indptr[st + 1] - pg0;
+  const int nt = (prefix + q0 + nq + kKeys - 1) / kKeys;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->k_full[i], 1);
+      mbar_init(&bars->k_empty[i], 1);
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->s_free[i], 4 * 32);
+      mbar_init(&bars->p_full[i], 4 * 32);
+      mbar_init(&bars->pv_done[i], 1);
+    }
+    mbar_init(&bars->v_full, 1);
+    mbar_init(&bars->v_empty, 1);
+    mbar_init(&bars->drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      mbar_arrive_expect_tx(&bars->q_full, 2 * kTileBytes);
+    }
+    __syncwarp();
+    if (lane < 4)
+      tma_load_2d(smem + kPairQOff + (lane >> 1) * kTileBytes + (lane & 1) * kHalfBytes, &tq, &bars->q_full,
+                  (h0 + (lane >> 1)) * kD + (lane & 1) * 64, qs0 + q0);
+    const int idx = lane & 15, pg = idx >> 1, half = idx & 1;
+    auto load_tile = [&](const void* map, uint8_t* base, uint64_t* bar, int j) {
+      if (lane == 0) mbar_arrive_expect_tx(bar, kTileBytes);
+      __syncwarp();
+      if (lane < 16) {
+        const int pgl = j * (kKeys / kPage) + pg;
+        const int64_t y = pgl < npages ? (int64_t)p.page_indices[pg0 + pgl] * kPage : p.num_slots;
+        tma_load_2d(base + half * kHalfBytes + pg * kPage * 128, map, bar, kvh * kD + half * 64, (int)y);
+      }
+    };
+    // K_j, then V_{j-1} (V is used a softmax later than K)
+    for (int j = 0; j <= nt; ++j) {
+      if (j < nt) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&bars->k_empty[s], ((j - 2) >> 1) & 1)) {
+          report_status(kDevTimeoutTma);
+          break;
+        }
+        load_tile(&tk, smem + kPairKOff + s * kTileBytes, &bars->k_full[s], j);
+      }
+      if (j >= 1) {
+        if (j >= 2 && !mbar_wait(&bars->v_empty, (j - 2) & 1)) {
+          report_status(kDevTimeoutTma);
+          break;
+        }
+        load_tile(&tv, smem + kPairVOff, &bars->v_full, j - 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    const bool leader = elect_one();
+    const uint32_t idesc_qk = idesc_bf16_f32(kRows, kKeys);
+    const uint32_t idesc_pv = idesc_bf16_f32(kRows, kD) | (1u << 16);  // B MN-major
+    bool ok = mbar_wait(&bars->q_full, 0);
+    auto ready = [&](uint64_t* bar, uint32_t parity) -> bool {
+      uint32_t r = lane == 0 ? (mbar_test_wait(bar, parity) ? 1u : 0u) : 0u;
+      return __shfl_sync(0xFFFFFFFFu, r, 0) != 0;
+    };
+    int jq[2] = {0, 0}, ip[2] = {0, 0};
+    uint32_t idle = 0;
+    while (ok && (ip[0] < nt || ip[1] < nt)) {
+      bool progressed = false;
+      // P V first: it frees the V stage (and lets the head's softmax go on)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i = ip[h];
+        if (i < jq[h] && ready(&bars->p_full[h], i & 1) && ready(&bars->v_full, i & 1)) {
+          tc_fence_after();
+          if (leader) {
+            const uint8_t* pt = smem + kPairPOff + h * kTileBytes;
+            const uint8_t* vt = smem + kPairVOff;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint64_t ad = smem_desc_sw128(pt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
+              const uint64_t bd = desc_mn_sw128(vt + k * 16 * 128);
+              tc_mma_bf16(tbase + 256 + h * 128, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+            }
+            tc_commit(&bars->pv_done[h]);
+            // the V stage is free once both heads' P V of this tile have completed
+            if (ip[h ^ 1] > i) tc_commit(&bars->v_empty);
+          }
+          __syncwarp();
+          ++ip[h];
+          progressed = true;
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = jq[h];
+        // S_h(j) overwrites S_h(j-1): after the head's softmax released it; at most
+        // one K tile ahead of the other head (two K stages)
+        if (j < nt && j <= ip[h] && j <= jq[h ^ 1] + 1 && ready(&bars->k_full[j & 1], (j >> 1) & 1) &&
+            (j == 0 || ready(&bars->s_free[h], (j - 1) & 1))) {
+          tc_fence_after();
+          if (leader) {
+            const uint8_t* qt = smem + kPairQOff + h * kTileBytes;
+            const uint8_t* kt = smem + kPairKOff + (j & 1) * kTileBytes;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint64_t ad = smem_desc_sw128(qt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
+              const uint64_t bd = smem_desc_sw128(kt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
+              tc_mma_bf16(tbase + h * 128, ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+            }
+            tc_commit(&bars->s_full[h]);
+            // the K stage is free once both heads' S of this tile have completed
+            if (jq[h ^ 1] > j) tc_commit(&bars->k_empty[j & 1]);
+          }
+          __syncwarp();
+          ++jq[h];
+          progressed = true;
+        }
+      }
+      if (progressed) idle = 0;
+      else if (++idle > 4 * kWaitLimit) ok = false;
+    }
+    if (!ok) report_status(kDevTimeoutMma);
+    if (leader) tc_commit(&bars->drain);
+    __syncwarp();
+    mbar_wait(&bars->drain, 0);
+  } else {
+    // ---------------- softmax: one thread per query row of one head ----------------
+    const int h = (warp - 2) >> 2;          // head of this warpgroup
+    const int q = warp & 3;                 // TMEM lane quarter of this warp
+    const int r = q * 32 + lane;            // query row of the tile
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const uint32_t tS = tbase + lane_off + h * 128;
+    const uint32_t tO = tbase + lane_off + 256 + h * 128;
+    const int lim = prefix + q0 + r;        // last key this query sees
+    const float sl = p.scale_log2;
+    uint8_t* prow = smem + kPairPOff + h * kTileBytes + r * 128;
+    float m_use = -INFINITY, l = 0.0f;
+    bool ok = true;
+    // P = exp2(s * scale - m_use) of the row's 128 keys of tile j into the P buffer
+    // (masked keys 0); returns their sum and the raw max score
+    auto write_p = [&](int j, bool masked, float& mx) -> float {
+      float rs = 0.0f;
+      mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tS + c * 32, v);
+        tc_wait_ld();
+        const int k0 = j * kKeys + c * 32;
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float a = __uint_as_float(v[e]), b = __uint_as_float(v[e + 1]);
+          if (masked) {
+            a = k0 + e <= lim ? a : -INFINITY;
+            b = k0 + e + 1 <= lim ? b : -INFINITY;
+          }
+          mx = fmaxf(mx, fmaxf(a, b));
+          const float pa = ex2_approx(a * sl - m_use), pb = ex2_approx(b * sl - m_use);
+          rs += pa + pb;
+          pk[e >> 1] = pack_bf2(pa, pb);
+        }
+        // keys c*32 .. c*32+31: half c / 2, 16-byte chunks (c & 1) * 4 .. + 3 of the row
+        uint8_t* hrow = prow + (c >> 1) * kHalfBytes;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int chunk = (c & 1) * 4 + u;
+          *reinterpret_cast<uint4*>(hrow + ((chunk ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+      }
+      return rs;
+    };
+    for (int j = 0; j < nt && ok; ++j) {
+      if (!mbar_wait(&bars->s_full[h], j & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // the P buffer of tile j - 1 is free once its P V has completed
+      if (j >= 1 && !mbar_wait(&bars->pv_done[h], (j - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      const bool masked = j * kKeys + kKeys - 1 > prefix + q0;
+      float mx, rs = 0.0f;
+      if (m_use == -INFINITY) {
+        mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tS + c * 32, v);
+          tc_wait_ld();
+          const int k0 = j * kKeys + c * 32;
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (!masked || k0 + e <= lim) mx = fmaxf(mx, __uint_as_float(v[e]));
+        }
+      } else {
+        rs = write_p(j, masked, mx);
+      }
+      const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl;
+      if (m_tile != -INFINITY && (m_use == -INFINITY || m_tile > m_use + kRescaleLog2)) {
+        const float alpha = m_use == -INFINITY ? 0.0f : ex2_approx(m_use - m_tile);
+        if (j > 0 && l > 0.0f) {
+          // O holds tiles < j: its last P V (tile j - 1) has completed (waited above)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tO + c * 32, v);
+            tc_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+            tmem_st_32x32b_x32(tO + c * 32, v);
+          }
+          tc_wait_st();
+        }
+        l *= alpha;
+        m_use = m_tile;
+        float unused;
+        rs = write_p(j, masked, unused);
+      }
+      l += rs;
+      tc_fence_before();
+      mbar_arrive(&bars->s_free[h]);
+      fence_proxy_async();  // the P stores, visible to the tensor core
+      mbar_arrive(&bars->p_full[h]);
+    }
+    if (ok && nt > 0 && mbar_wait(&bars->pv_done[h], (nt - 1) & 1)) {
+      tc_fence_after();
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+      uint16_t* orow = p.out + (int64_t)(qs0 + q0 + r) * p.out_stride + (int64_t)(h0 + h) * kD;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tO + c * 32, v);
+        tc_wait_ld();
+        if (r < nq) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2)
+            pk[e >> 1] = pack_bf2(__uint_as_float(v[e]) * inv, __uint_as_float(v[e + 1]) * inv);
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        }
+      }
+    } else if (nt > 0) {
+      report_status(kDevTimeoutMma);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tbase, 512);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -473,6 +809,18 @@ extern "C" OMNI_API int omni_prefill_attention(const void* q, int64_t q_stride, 
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.out = static_cast<uint16_t*>(out);
   p.out_stride = out_stride;
+  if ((num_q_heads / num_kv_heads) % 2 == 0) {
+    // two query heads of one KV head a CTA
+    const cudaError_t ae =
+        once_per_device(reinterpret_cast<const void*>(prefill_attention_pair_kernel), kAttrSmem, [] {
+          return cudaFuncSetAttribute(prefill_attention_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kPairSmemBytes);
+        });
+    if (ae != cudaSuccess) return check_launch(ae);
+    return check_launch(launch(prefill_attention_pair_kernel,
+                               dim3((unsigned)max_tiles, (unsigned)(num_q_heads / 2)), dim3(kThreads), kPairSmemBytes,
+                               static_cast<cudaStream_t>(stream), tq, tk, tv, p));
+  }
   const cudaError_t ae = once_per_device(reinterpret_cast<const void*>(prefill_attention_tc_kernel), kAttrSmem, [] {
     return cudaFuncSetAttribute(prefill_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)kSmemBytes);

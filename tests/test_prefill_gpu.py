@@ -5,7 +5,8 @@
 - causal extend attention over the paged pool (pages randomly permuted, streams
   with and without a prefix, lengths around the 128-query tile, the 128-key tile and
   16-token page edges) against a torch fp32 reference: cosine >= 0.999, max-abs <= 2e-2
-  x scale.
+  x scale; both kernels (two query heads of a KV head a CTA when the group size is
+  even, one head otherwise).
 """
 
 from __future__ import annotations
@@ -83,8 +84,9 @@ def test_extend_prepare_matches_oracle():
 LONG_STREAMS = [(0, 4096), (0, 2048), (0, 3001), (300, 2500), (0, 64), (4000, 96)]
 
 
-@pytest.mark.parametrize("hq,hkv,streams", [(16, 2, STREAMS), (8, 8, STREAMS), (16, 2, LONG_STREAMS)],
-                         ids=["gqa", "mha", "long-prompts"])
+@pytest.mark.parametrize("hq,hkv,streams", [(16, 2, STREAMS), (8, 4, STREAMS), (12, 4, STREAMS), (8, 8, STREAMS),
+                                             (16, 2, LONG_STREAMS)],
+                         ids=["gqa8-pairs", "gqa2-pairs", "gqa3-single", "mha-single", "long-prompts"])
 def test_prefill_attention_matches_fp32(hq, hkv, streams):
     from omni_b200 import ops
 
