@@ -148,6 +148,175 @@ OMNI_DEVINL RowBlock row_block(int rows_here, int S, int q) {
   return b;
 }
 
+// ---------------------------------------------------------------------------
+// Epilogue of four consecutive output features of one row (lane ln of the row's warp
+// holds features tile * 128 + 4 ln .. + 3, already scaled by the row's folded-norm
+// factor): the fp32, router, qkv, store and residual epilogues.  Shared by the
+// split-K kernel and the tile-loop kernel below; the whole warp calls it for one row.
+// ---------------------------------------------------------------------------
+// The global operands of one lane's four features, fetched ahead of the arithmetic so
+// that a warp can have several rows' loads in flight: the residual, or for the qkv
+// epilogue the rotary cos / sin of the features' pair dimensions and the head-norm gain.
+struct QuadIn {
+  uint2 rv;
+  float4 c4, s4;
+  uint2 gw;
+};
+template <int EPI>
+OMNI_DEVINL QuadIn quad_fetch(const GemmParams& p, int64_t grow, int tile, int ln, int64_t pos) {
+  QuadIn in;
+  in.rv = make_uint2(0u, 0u);
+  in.gw = make_uint2(0u, 0u);
+  in.c4 = in.s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int64_t col = (int64_t)tile * kTileN + ln * 4;
+  if (EPI == kEpiResidual) in.rv = *reinterpret_cast<const uint2*>(p.residual + grow * p.res_stride + col);
+  if (EPI == kEpiQKV) {
+    const int D = p.head_dim, half = D / 2;
+    const int gh = (int)(col / D), d = (int)(col % D), ii = d % half;
+    const float* cs = p.cos_sin + pos * D;
+    in.c4 = *reinterpret_cast<const float4*>(cs + ii);
+    in.s4 = *reinterpret_cast<const float4*>(cs + half + ii);
+    if (gh < p.hq + p.hkv) in.gw = *reinterpret_cast<const uint2*>((gh < p.hq ? p.q_norm : p.k_norm) + d);
+  }
+  return in;
+}
+
+template <int EPI>
+OMNI_DEVINL void quad_epilogue(const GemmParams& p, int64_t grow, int tile, int ln, float (&o)[4], const QuadIn& in,
+                               int64_t loc) {
+  const int f = ln * 4;
+  const int64_t col = (int64_t)tile * kTileN + f;
+  const uint2 rv = in.rv;
+  if (EPI == kEpiF32) {
+    float* Y = static_cast<float*>(p.y);
+    *reinterpret_cast<float4*>(Y + grow * p.y_stride + col) = make_float4(o[0], o[1], o[2], o[3]);
+  } else if (EPI == kEpiRouter) {
+    // bf16 router logits (the gate projection's output), then the fp32 softmax over
+    // the 128 experts of the row: lane l holds experts 4l..4l+3, partial sums in index
+    // order, xor butterfly 16..1; top-k by (prob desc, index asc); weights renormalised
+    // by their sum in selection order
+    const uint2 packed = make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
+    uint16_t* Y = static_cast<uint16_t*>(p.y);
+    *reinterpret_cast<uint2*>(Y + grow * p.y_stride + col) = packed;
+    const float lg[4] = {bf_lo(packed.x), bf_hi(packed.x), bf_lo(packed.y), bf_hi(packed.y)};
+    float mx = fmaxf(fmaxf(lg[0], lg[1]), fmaxf(lg[2], lg[3]));
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+    float ex[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ex[j] = det_expf(__fsub_rn(lg[j], mx));
+    float z = __fadd_rn(__fadd_rn(__fadd_rn(ex[0], ex[1]), ex[2]), ex[3]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) z = __fadd_rn(z, __shfl_xor_sync(0xFFFFFFFFu, z, off));
+    unsigned long long key[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t pb = __float_as_uint(__fdiv_rn(ex[j], z));
+      const uint32_t ord = (pb >> 31) ? ~pb : (pb | 0x80000000u);
+      key[j] = ((unsigned long long)ord << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)(f + j));
+    }
+    float wsum = 0.0f, wsel = 0.0f;
+    int idsel = 0;
+    for (int kk = 0; kk < p.top_k; ++kk) {
+      unsigned long long best = 0ull;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) best = key[j] > best ? key[j] : best;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        const unsigned long long o2 = __shfl_xor_sync(0xFFFFFFFFu, best, off);
+        best = o2 > best ? o2 : best;
+      }
+      const int e = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu));
+      const uint32_t ob = (uint32_t)(best >> 32);
+      const float pe = __uint_as_float((ob >> 31) ? (ob & 0x7FFFFFFFu) : ~ob);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (f + j == e) key[j] = 0ull;
+      wsum = kk == 0 ? pe : __fadd_rn(wsum, pe);
+      if (ln == kk) {
+        wsel = pe;
+        idsel = e;
+      }
+    }
+    if (ln < p.top_k) {
+      p.topk_ids[grow * p.top_k + ln] = idsel;
+      p.topk_w[grow * p.top_k + ln] = __fdiv_rn(wsel, wsum);
+    }
+  } else if (EPI == kEpiQKV) {
+    const int D = p.head_dim;
+    const int gh = (int)(col / D);  // global head of these 4 features
+    const int d = (int)(col % D);   // first dimension within the head
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = bf2f(f2bf(o[j]));  // the qkv projection's bf16 output
+    const bool is_q = gh < p.hq, is_k = !is_q && gh < p.hq + p.hkv;
+    // lanes sharing a head: D/4 consecutive lanes (the whole warp for D = 128)
+    const int head_lanes = D / 4;
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss = __fmaf_rn(o[j], o[j], ss);
+    for (int off = 1; off < head_lanes; off <<= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
+    if (is_q || is_k) {
+      const float hr = rsqrtf(ss / (float)D + p.qk_eps);
+      const uint2 wv = in.gw;
+      const float gw4[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = bf2f(f2bf(o[j] * hr * gw4[j]));
+    }
+    // neox rotation pairs d with d + D/2, held by lane ^ (D/8); every lane joins the shuffle
+    const int half = D / 2;
+    const float c4[4] = {in.c4.x, in.c4.y, in.c4.z, in.c4.w}, s4[4] = {in.s4.x, in.s4.y, in.s4.z, in.s4.w};
+    float y4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float other = __shfl_xor_sync(0xFFFFFFFFu, o[j], D / 8);
+      const int dd = d + j;
+      const float c = c4[j], sn = s4[j];
+      y4[j] = dd < half ? o[j] * c - other * sn : o[j] * c + other * sn;
+    }
+    const uint2 packed_rot = make_uint2(pack_bf2(y4[0], y4[1]), pack_bf2(y4[2], y4[3]));
+    if (is_q) {
+      uint16_t* Y = static_cast<uint16_t*>(p.y);
+      *reinterpret_cast<uint2*>(Y + grow * p.y_stride + col) = packed_rot;
+    } else if (is_k) {
+      const int kh = gh - p.hq;
+      *reinterpret_cast<uint2*>(p.k_cache + (loc * p.hkv + kh) * D + d) = packed_rot;
+    } else {
+      const int vh = gh - p.hq - p.hkv;
+      *reinterpret_cast<uint2*>(p.v_cache + (loc * p.hkv + vh) * D + d) =
+          make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
+    }
+  } else {
+    if (EPI == kEpiResidual) {
+      o[0] += bf_lo(rv.x);
+      o[1] += bf_hi(rv.x);
+      o[2] += bf_lo(rv.y);
+      o[3] += bf_hi(rv.y);
+    }
+    uint16_t* Y = static_cast<uint16_t*>(p.y);
+    const uint2 packed = make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
+    *reinterpret_cast<uint2*>(Y + grow * p.y_stride + col) = packed;
+    if (p.ss_out) {
+      float ss = 0.0f;
+      const float q4[4] = {bf_lo(packed.x), bf_hi(packed.x), bf_lo(packed.y), bf_hi(packed.y)};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ss = __fmaf_rn(q4[j], q4[j], ss);
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
+      if (ln == 0) p.ss_out[tile * p.ss_out_stride + grow] = ss;
+    }
+  }
+}
+
+// SwiGLU of four outputs (out_col .. + 3) of one row from the gate and up sums.
+OMNI_DEVINL void swiglu_quad(const GemmParams& p, int64_t grow, int64_t out_col, float4 gt, float4 up, float sc) {
+  const float gg[4] = {gt.x, gt.y, gt.z, gt.w}, uu[4] = {up.x, up.y, up.z, up.w};
+  float o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o[j] = silu(bf2f(f2bf(gg[j] * sc))) * bf2f(f2bf(uu[j] * sc));
+  uint16_t* Y = static_cast<uint16_t*>(p.y);
+  *reinterpret_cast<uint2*>(Y + grow * p.y_stride + out_col) = make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
+}
+
 // Two CTAs fit on an SM (<= 128 registers a thread) for every epilogue but the fp32
 // one (the codec head, once a step), so that with programmatic dependent launch the
 // next GEMM's CTAs can start, and stream their weights, beside the CTAs of the
@@ -433,11 +602,9 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
   const int items = aborted ? 0 : mine.count;
   if (EPI == kEpiSwiGLU) {
     // features 0..63: gate, 64..127: up, for outputs tile*64 .. tile*64+63
-    uint16_t* Y = static_cast<uint16_t*>(p.y);
     for (int idx = threadIdx.x; idx < items * 16; idx += kThreadsG) {
       const int i = idx >> 4;
       const int g = (idx & 15) * 4;
-      const float sc = row_info[i];
       // gate and up summed side by side in split order (two CTAs per SM leave no
       // registers for all S slots of both in flight)
       const int r = mine.begin + i;
@@ -462,12 +629,7 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
         up.z += b.z;
         up.w += b.w;
       }
-      const float gg[4] = {gt.x, gt.y, gt.z, gt.w}, uu[4] = {up.x, up.y, up.z, up.w};
-      float o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) o[j] = silu(bf2f(f2bf(gg[j] * sc))) * bf2f(f2bf(uu[j] * sc));
-      *reinterpret_cast<uint2*>(Y + (int64_t)(row0 + mine.begin + i) * p.y_stride + tile * 64 + g) =
-          make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
+      swiglu_quad(p, row0 + mine.begin + i, tile * 64 + g, gt, up, row_info[i]);
     }
     return;
   }
@@ -492,136 +654,269 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
     if (idx >= items * 32) break;  // warp-uniform: items * 32 is a multiple of 32
     const int i = idx >> 5;
     const int ln = idx & 31;
-    const int f = ln * 4;
-    const int64_t grow = row0 + mine.begin + i;
-    const int64_t col = (int64_t)tile * kTileN + f;
     const float sc = row_info[i];
-    const float4 a = acc4(i, f);
+    const float4 a = acc4(i, ln * 4);
     float o[4] = {a.x * sc, a.y * sc, a.z * sc, a.w * sc};
-    if (EPI == kEpiF32) {
-      float* Y = static_cast<float*>(p.y);
-      *reinterpret_cast<float4*>(Y + grow * p.y_stride + col) = make_float4(o[0], o[1], o[2], o[3]);
-    } else if (EPI == kEpiRouter) {
-      // bf16 router logits (the gate projection's output), then the fp32 softmax over
-      // the 128 experts of the row: lane l holds experts 4l..4l+3, partial sums in index
-      // order, xor butterfly 16..1; top-k by (prob desc, index asc); weights renormalised
-      // by their sum in selection order
-      const uint2 packed = make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
-      uint16_t* Y = static_cast<uint16_t*>(p.y);
-      *reinterpret_cast<uint2*>(Y + grow * p.y_stride + col) = packed;
-      const float lg[4] = {bf_lo(packed.x), bf_hi(packed.x), bf_lo(packed.y), bf_hi(packed.y)};
-      float mx = fmaxf(fmaxf(lg[0], lg[1]), fmaxf(lg[2], lg[3]));
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
-      float ex[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) ex[j] = det_expf(__fsub_rn(lg[j], mx));
-      float z = __fadd_rn(__fadd_rn(__fadd_rn(ex[0], ex[1]), ex[2]), ex[3]);
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) z = __fadd_rn(z, __shfl_xor_sync(0xFFFFFFFFu, z, off));
-      unsigned long long key[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t pb = __float_as_uint(__fdiv_rn(ex[j], z));
-        const uint32_t ord = (pb >> 31) ? ~pb : (pb | 0x80000000u);
-        key[j] = ((unsigned long long)ord << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)(f + j));
-      }
-      float wsum = 0.0f, wsel = 0.0f;
-      int idsel = 0;
-      for (int kk = 0; kk < p.top_k; ++kk) {
-        unsigned long long best = 0ull;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) best = key[j] > best ? key[j] : best;
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-          const unsigned long long o2 = __shfl_xor_sync(0xFFFFFFFFu, best, off);
-          best = o2 > best ? o2 : best;
-        }
-        const int e = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu));
-        const uint32_t ob = (uint32_t)(best >> 32);
-        const float pe = __uint_as_float((ob >> 31) ? (ob & 0x7FFFFFFFu) : ~ob);
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (f + j == e) key[j] = 0ull;
-        wsum = kk == 0 ? pe : __fadd_rn(wsum, pe);
-        if (ln == kk) {
-          wsel = pe;
-          idsel = e;
-        }
-      }
-      if (ln < p.top_k) {
-        p.topk_ids[grow * p.top_k + ln] = idsel;
-        p.topk_w[grow * p.top_k + ln] = __fdiv_rn(wsel, wsum);
-      }
-    } else if (EPI == kEpiQKV) {
-      const int D = p.head_dim;
-      const int gh = (int)(col / D);  // global head of these 4 features
-      const int d = (int)(col % D);   // first dimension within the head
-#pragma unroll
-      for (int j = 0; j < 4; ++j) o[j] = bf2f(f2bf(o[j]));  // the qkv projection's bf16 output
-      const int64_t pos = reinterpret_cast<const int*>(row_info)[mine.per + i];
-      const int64_t loc = reinterpret_cast<const int*>(row_info)[2 * mine.per + i];
-      const bool is_q = gh < p.hq, is_k = !is_q && gh < p.hq + p.hkv;
-      // lanes sharing a head: D/4 consecutive lanes (the whole warp for D = 128)
-      const int head_lanes = D / 4;
-      float ss = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) ss = __fmaf_rn(o[j], o[j], ss);
-      for (int off = 1; off < head_lanes; off <<= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
-      if (is_q || is_k) {
-        const uint16_t* gw = is_q ? p.q_norm : p.k_norm;
-        const float hr = rsqrtf(ss / (float)D + p.qk_eps);
-        const uint2 wv = *reinterpret_cast<const uint2*>(gw + d);
-        const float gw4[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o[j] = bf2f(f2bf(o[j] * hr * gw4[j]));
-      }
-      // neox rotation pairs d with d + D/2, held by lane ^ (D/8); every lane joins the shuffle
-      const int half = D / 2;
-      const float* cs = p.cos_sin + pos * D;
-      float y4[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float other = __shfl_xor_sync(0xFFFFFFFFu, o[j], D / 8);
-        const int dd = d + j;
-        const int ii = dd % half;
-        const float c = cs[ii], sn = cs[half + ii];
-        y4[j] = dd < half ? o[j] * c - other * sn : o[j] * c + other * sn;
-      }
-      const uint2 packed_rot = make_uint2(pack_bf2(y4[0], y4[1]), pack_bf2(y4[2], y4[3]));
-      if (is_q) {
-        uint16_t* Y = static_cast<uint16_t*>(p.y);
-        *reinterpret_cast<uint2*>(Y + grow * p.y_stride + col) = packed_rot;
-      } else if (is_k) {
-        const int kh = gh - p.hq;
-        *reinterpret_cast<uint2*>(p.k_cache + (loc * p.hkv + kh) * D + d) = packed_rot;
-      } else {
-        const int vh = gh - p.hq - p.hkv;
-        *reinterpret_cast<uint2*>(p.v_cache + (loc * p.hkv + vh) * D + d) =
-            make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
-      }
+    int64_t pos = 0, loc = 0;
+    if (EPI == kEpiQKV) {
+      pos = reinterpret_cast<const int*>(row_info)[mine.per + i];
+      loc = reinterpret_cast<const int*>(row_info)[2 * mine.per + i];
+    }
+    QuadIn in;
+    if (EPI == kEpiResidual) {
+      in.rv = rv[u];
     } else {
-      if (EPI == kEpiResidual) {
-        o[0] += bf_lo(rv[u].x);
-        o[1] += bf_hi(rv[u].x);
-        o[2] += bf_lo(rv[u].y);
-        o[3] += bf_hi(rv[u].y);
-      }
-      uint16_t* Y = static_cast<uint16_t*>(p.y);
-      const uint2 packed = make_uint2(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]));
-      *reinterpret_cast<uint2*>(Y + grow * p.y_stride + col) = packed;
-      if (p.ss_out) {
-        float ss = 0.0f;
-        const float q4[4] = {bf_lo(packed.x), bf_hi(packed.x), bf_lo(packed.y), bf_hi(packed.y)};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) ss = __fmaf_rn(q4[j], q4[j], ss);
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
-        if (ln == 0) p.ss_out[tile * p.ss_out_stride + grow] = ss;
+      in = quad_fetch<EPI>(p, row0 + mine.begin + i, tile, ln, pos);
+    }
+    quad_epilogue<EPI>(p, row0 + mine.begin + i, tile, ln, o, in, loc);
+  }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Prefill-sized batches: a persistent tile loop, one CTA per SM.  The CTA walks the
+// (row tile of 128, feature tile of 128) pairs c, c + grid, ... (feature tile fastest,
+// so neighbouring CTAs share an activation block in L2).  Warp 0 streams W and X
+// k-steps through a five-stage ring across tile boundaries; warp 1 issues each tile's
+// MMAs into one of two TMEM accumulators; two epilogue groups of four warps take the
+// tiles in turn (group g the accumulator g), so that a tile's epilogue runs while the
+// next tile's MMAs do.  An epilogue group drains its accumulator 32 rows at a time
+// into a 16 KB staging buffer (lane = feature as TMEM holds it, row-contiguous in
+// shared memory), then a warp per row applies the same fused epilogue as the split-K
+// kernel.  No split: every tile sums its whole K in TMEM.
+// ---------------------------------------------------------------------------
+constexpr int kLoopThreads = 320;
+constexpr int kLoopRows = 128;
+constexpr int kLoopStages = 5;
+constexpr int kLoopWBytes = kTileN * kBK * 2;                 // 16 KB
+constexpr int kLoopStageBytes = kLoopWBytes + kLoopRows * kBK * 2;  // 32 KB
+constexpr int kLoopStagingBytes = 32 * kTileN * 4;            // 16 KB: 32 rows x 128 fp32
+constexpr int kLoopStagingOff = kLoopStages * kLoopStageBytes;
+constexpr int kLoopInfoOff = kLoopStagingOff + 2 * kLoopStagingBytes;
+constexpr int kLoopBarOff = kLoopInfoOff + 2 * 3 * kLoopRows * 4;
+constexpr size_t kLoopSmem = (size_t)kLoopBarOff + 256 + 1024;
+
+struct LoopBars {
+  uint64_t full[kLoopStages], empty[kLoopStages], acc_full[2], acc_empty[2];
+  uint32_t tmem;
+};
+
+OMNI_DEVINL void group_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+// Barrier of the group's 128 threads that also ANDs a predicate over them (so that the
+// group leaves a wait that ran out together).
+OMNI_DEVINL bool group_all(int id, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id)
+      : "memory");
+  return r != 0;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kLoopThreads, 1)
+    gemm_loop_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                     const __grid_constant__ GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  LoopBars* bars = reinterpret_cast<LoopBars*>(smem + kLoopBarOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_n = EPI == kEpiSwiGLU ? p.swiglu_half / (kTileN / 2) : p.N / kTileN;
+  const int total = tiles_n * ((p.rows + kLoopRows - 1) / kLoopRows);
+  const int nk = p.num_kb;
+  const uint32_t lim = kWaitLimit;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kLoopStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->acc_full[b], 1);
+      mbar_init(&bars->acc_empty[b], 128);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem, 2 * kLoopRows);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem;
+  griddep_wait();
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    const bool leader = elect_one();
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+      const int t = tile % tiles_n, row0 = (tile / tiles_n) * kLoopRows;
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = it % kLoopStages;
+        if (it >= kLoopStages &&
+            !__all_sync(0xFFFFFFFFu, mbar_wait(&bars->empty[s], ((it / kLoopStages) - 1) & 1, lim))) {
+          if (leader) report_status(kDevTimeoutMma);
+          tile = total;
+          break;
+        }
+        if (leader) {
+          uint8_t* st = smem + s * kLoopStageBytes;
+          mbar_arrive_expect_tx(&bars->full[s], kLoopStageBytes);
+          if (EPI == kEpiSwiGLU) {
+            tma_load_2d(st, &tmap_w, &bars->full[s], kb * kBK, t * (kTileN / 2));
+            tma_load_2d(st + (kTileN / 2) * kBK * 2, &tmap_w, &bars->full[s], kb * kBK, p.swiglu_half + t * (kTileN / 2));
+          } else {
+            tma_load_2d(st, &tmap_w, &bars->full[s], kb * kBK, t * kTileN);
+          }
+          tma_load_2d(st + kLoopWBytes, &tmap_x, &bars->full[s], kb * kBK, row0);
+        }
+        __syncwarp();
       }
     }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    const bool leader = elect_one();
+    const uint32_t idesc = idesc_bf16_f32(kTileN, kLoopRows);
+    int it = 0, i = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x, ++i) {
+      const int b = i & 1;
+      if (i >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars->acc_empty[b], ((i >> 1) - 1) & 1, lim))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int s = it % kLoopStages;
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->full[s], (it / kLoopStages) & 1, lim))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint8_t* st = smem + s * kLoopStageBytes;
+        const uint64_t wd = smem_desc_sw128(st), xd = smem_desc_sw128(st + kLoopWBytes);
+        if (leader) {
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc_mma_bf16(tmem + b * kLoopRows, wd + 2 * kk, xd + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&bars->empty[s]);
+        }
+        __syncwarp();
+      }
+      if (ok && leader) tc_commit(&bars->acc_full[b]);
+      __syncwarp();
+    }
+    if (!ok && leader) report_status(kDevTimeoutTma);
+  } else {
+    // ---------------- epilogue groups ----------------
+    const int g = (warp - 2) >> 2;           // group: accumulator g, tiles i = g (mod 2)
+    const int wl = (warp - 2) & 3;           // warp within the group
+    const int q = warp & 3;                  // TMEM lane quarter: features 32 q .. 32 q + 31
+    const int gt = wl * 32 + lane;           // thread within the group
+    float* staging = reinterpret_cast<float*>(smem + kLoopStagingOff + g * kLoopStagingBytes);
+    float* info = reinterpret_cast<float*>(smem + kLoopInfoOff) + g * 3 * kLoopRows;
+    int* ipos = reinterpret_cast<int*>(info + kLoopRows);
+    int* iloc = reinterpret_cast<int*>(info + 2 * kLoopRows);
+    int i = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++i) {
+      if ((i & 1) != g) continue;
+      const int t = tile % tiles_n, row0 = (tile / tiles_n) * kLoopRows;
+      const int rows_here = min(kLoopRows, p.rows - row0);
+      // the tile's per-row operands while its MMAs run
+      for (int r = gt; r < rows_here; r += 128) {
+        const int64_t grow = row0 + r;
+        float rs = 1.0f;
+        if (p.ss_in != nullptr) {
+          float ssum = 0.0f;
+          for (int pp = 0; pp < p.ss_in_parts; ++pp) ssum += p.ss_in[pp * p.ss_in_stride + grow];
+          rs = rsqrtf(ssum / (float)p.norm_dim + p.norm_eps);
+        }
+        info[r] = rs;
+        if (EPI == kEpiQKV) {
+          int64_t pos, loc;
+          if (p.positions) {
+            pos = p.positions[grow];
+            loc = p.cache_loc[grow];
+          } else {
+            const int tt = (int)(grow % p.tokens_per_req);
+            pos = p.slot_base + tt;
+            loc = (grow / p.tokens_per_req) * p.slot_stride + p.slot_base + tt;
+          }
+          if (pos < 0 || pos >= p.max_pos) pos = 0;
+          ipos[r] = (int)pos;
+          iloc[r] = (int)loc;
+        }
+      }
+      if (!group_all(1 + g, mbar_wait(&bars->acc_full[g], (i >> 1) & 1, lim))) {
+        if (gt == 0) report_status(kDevTimeoutMma);
+        break;
+      }
+      tc_fence_after();
+      const int nchunks = (rows_here + 31) / 32;
+      for (int c = 0; c < nchunks; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + g * kLoopRows + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+        tc_wait_ld();
+        if (c == nchunks - 1) {
+          // every read of this accumulator is done: the MMA warp may refill it
+          tc_fence_before();
+          mbar_arrive(&bars->acc_empty[g]);
+        }
+        group_sync(1 + g);  // the previous chunk's rows are done with the staging buffer
+#pragma unroll
+        for (int j = 0; j < 32; ++j) staging[j * kTileN + q * 32 + lane] = __uint_as_float(v[j]);
+        group_sync(1 + g);
+        const int rmax = min(32, rows_here - c * 32);
+        if (EPI == kEpiSwiGLU) {
+          // two rows a warp: lanes 0-15 and 16-31, four outputs a lane
+          for (int rr = 2 * wl + (lane >> 4); rr < rmax; rr += 8) {
+            const int gq = (lane & 15) * 4;
+            const float4 gv = *reinterpret_cast<const float4*>(staging + rr * kTileN + gq);
+            const float4 uv = *reinterpret_cast<const float4*>(staging + rr * kTileN + 64 + gq);
+            swiglu_quad(p, row0 + c * 32 + rr, (int64_t)t * 64 + gq, gv, uv, info[c * 32 + rr]);
+          }
+        } else {
+          // rows wl, wl + 4, ... of the chunk, four at a time: their global operands
+          // first (four rows' loads in flight), then the arithmetic and the stores
+          for (int r0 = wl; r0 < rmax; r0 += 16) {
+            QuadIn in[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int rr = r0 + 4 * u;
+              if (rr < rmax) {
+                const int r = c * 32 + rr;
+                in[u] = quad_fetch<EPI>(p, row0 + r, t, lane, EPI == kEpiQKV ? ipos[r] : 0);
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int rr = r0 + 4 * u;
+              if (rr < rmax) {
+                const int r = c * 32 + rr;
+                const float4 a = *reinterpret_cast<const float4*>(staging + rr * kTileN + lane * 4);
+                const float sc = info[r];
+                float o[4] = {a.x * sc, a.y * sc, a.z * sc, a.w * sc};
+                quad_epilogue<EPI>(p, row0 + r, t, lane, o, in[u], EPI == kEpiQKV ? iloc[r] : 0);
+              }
+            }
+          }
+        }
+      }
+      group_sync(1 + g);  // the group's row info and staging are free for its next tile
+    }
   }
-  }
+  griddep_launch();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 2 * kLoopRows);
 }
 
 // ---------------------------------------------------------------------------
@@ -842,9 +1137,58 @@ Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
   return pl;
 }
 
+// Prefill-sized batches with enough (row tile, feature tile) pairs for every SM take the
+// tile loop; a call that asks for a split count (1 included) keeps the split-K kernel.
+template <int EPI>
+int launch_loop(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n, GemmParams gp,
+                int tiles, cudaStream_t st) {
+  CUtensorMap tw, tx;
+  const int wbox = EPI == kEpiSwiGLU ? kTileN / 2 : kTileN;
+  if (!make_tmap(&tw, w, n, k, k, wbox) || !make_tmap(&tx, x, rows, k, x_stride, kLoopRows))
+    return set_error(OMNI_ERR_UNSUPPORTED, "tensor map encoding failed");
+  gp.rows = (int)rows;
+  gp.K = (int)k;
+  gp.N = (int)n;
+  gp.row_tile = kLoopRows;
+  gp.num_kb = (int)(k / kBK);
+  gp.splits = 1;
+  gp.swiglu_half = (int)(n / 2);
+  const void* kern = reinterpret_cast<const void*>(gemm_loop_kernel<EPI>);
+  if (once_per_device(kern, kAttrSmem, [] {
+        return cudaFuncSetAttribute(gemm_loop_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)kLoopSmem);
+      }) != cudaSuccess)
+    return check_launch(cudaGetLastError());
+  const int64_t total = (int64_t)tiles * ((rows + kLoopRows - 1) / kLoopRows);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(total < num_sms() ? total : num_sms()));
+  cfg.blockDim = dim3(kLoopThreads);
+  cfg.dynamicSmemBytes = kLoopSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return check_launch(cudaLaunchKernelEx(&cfg, gemm_loop_kernel<EPI>, tw, tx, gp));
+}
+
 template <int EPI>
 int launch_gemm(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n, GemmParams gp,
                 int splits_req, cudaStream_t st) {
+  // the tile loop's two four-warp epilogue groups keep up with the store, residual and
+  // SwiGLU epilogues; the qkv one (head norms, rotary, K/V scatter) measured faster on
+  // the split-K kernel's sixteen epilogue warps an SM (38.7 k rows: 504 against 669 us),
+  // and the router and fp32 ones stay there too
+  if (EPI == kEpiStore || EPI == kEpiResidual || EPI == kEpiSwiGLU) {
+    const int tiles = (int)(EPI == kEpiSwiGLU ? (n / 2) / (kTileN / 2) : n / kTileN);
+    if (rows > 256 && splits_req == 0 && (int64_t)tiles * ((rows + kLoopRows - 1) / kLoopRows) >= num_sms())
+      return launch_loop<EPI>(x, rows, k, x_stride, w, n, gp, tiles, st);
+  }
   const Plan pl = make_plan<EPI>(rows, k, n, splits_req);
   if (pl.splits > kMaxSplits) return set_error(OMNI_ERR_UNSUPPORTED, "at most 16 K-splits");
   if (pl.smem > 227 * 1024) return set_error(OMNI_ERR_UNSUPPORTED, "GEMM tile does not fit in shared memory");

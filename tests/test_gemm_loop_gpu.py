@@ -1,0 +1,138 @@
+"""The persistent tile-loop GEMM (prefill-sized batches, one CTA per SM, two TMEM
+accumulators) against the split-K kernel at one split.
+
+Both sum each output's whole K in TMEM in the same k order and apply the same fused
+epilogue code, so the loop's epilogues must match bit for bit: store and residual with
+the row sums of squares (folded RMSNorm on the way in) and SwiGLU; the store case is also
+held to an fp32 reference.  The qkv, fp32 and router epilogues stay on the split-K
+kernel at these sizes; their cases check that the auto-planned and the one-split calls
+agree.  Row counts leave a partial last row tile; the auto-planned call (splits=0) takes
+the loop once the batch has at least one (row tile, feature tile) pair per SM.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _gen(seed):
+    return torch.Generator(device=DEV).manual_seed(seed)
+
+
+def _both(fn):
+    a = fn(0)
+    b = fn(1)
+    torch.cuda.synchronize()
+    return a, b
+
+
+@pytest.mark.parametrize("rows,k,n", [(2500, 1024, 1024), (4133, 3072, 1024), (1000, 2048, 3072)])
+def test_loop_store_and_residual_match_split_k(rows, k, n):
+    from omni_b200 import ops
+
+    g = _gen(rows + k)
+    x = torch.randn(rows, k, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    res = torch.randn(rows, n, generator=g, device=DEV).to(torch.bfloat16)
+    ss_in = x.float().view(rows, k // 128, 128).pow(2).sum(-1).t().contiguous()
+
+    def store(splits):
+        y = torch.empty(rows, n, device=DEV, dtype=torch.bfloat16)
+        ops.linear_fused(x, w, y, epilogue=ops.EPI_STORE, ss_in=ss_in, ss_in_parts=k // 128, splits=splits)
+        return y
+
+    def resid(splits):
+        y = torch.empty(rows, n, device=DEV, dtype=torch.bfloat16)
+        ss = torch.full((n // 128, rows), -1.0, device=DEV)
+        ops.linear_fused(x, w, y, epilogue=ops.EPI_RESIDUAL, residual=res, ss_out=ss, splits=splits)
+        return y, ss
+
+    a, b = _both(store)
+    assert torch.equal(a, b)
+    rstd = torch.rsqrt(ss_in.sum(0) / k + 1e-6)
+    ref = (x.float() @ w.float().t()) * rstd[:, None]
+    cos = torch.nn.functional.cosine_similarity(a.float().flatten(), ref.flatten(), dim=0).item()
+    assert cos >= 0.9999 and (a.float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item()
+    (ya, sa), (yb, sb) = _both(resid)
+    assert torch.equal(ya, yb) and torch.equal(sa, sb)
+    torch.testing.assert_close(sa.sum(0), ya.float().pow(2).sum(1), rtol=1e-4, atol=1e-2)
+
+
+def test_loop_swiglu_matches_split_k():
+    from omni_b200 import ops
+
+    rows, k, inter = 3001, 1024, 3072
+    g = _gen(5)
+    x = torch.randn(rows, k, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(2 * inter, k, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    ss_in = x.float().view(rows, 8, 128).pow(2).sum(-1).t().contiguous()
+
+    def run(splits):
+        y = torch.empty(rows, inter, device=DEV, dtype=torch.bfloat16)
+        ops.linear_fused(x, w, y, epilogue=ops.EPI_SWIGLU, ss_in=ss_in, ss_in_parts=8, splits=splits)
+        return y
+
+    a, b = _both(run)
+    assert torch.equal(a, b)
+
+
+def test_loop_qkv_rope_store_matches_split_k():
+    from omni_b200 import ops
+
+    rows, k, hq, hkv, D = 2777, 1024, 16, 2, 128
+    n = (hq + 2 * hkv) * D
+    g = _gen(9)
+    x = torch.randn(rows, k, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, generator=g, device=DEV)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, generator=g, device=DEV)).to(torch.bfloat16)
+    cos_sin = ops.rope_cos_sin_cache(8192, D, 1e6, torch.device(DEV))
+    positions = torch.randint(0, 8192, (rows,), generator=g, device=DEV)
+    slots = torch.randperm(rows + 100, generator=g, device=DEV)[:rows]
+    ss_in = x.float().view(rows, 8, 128).pow(2).sum(-1).t().contiguous()
+
+    def run(splits):
+        q = torch.empty(rows, hq * D, device=DEV, dtype=torch.bfloat16)
+        kc = torch.zeros(rows + 100, hkv, D, device=DEV, dtype=torch.bfloat16)
+        vc = torch.zeros(rows + 100, hkv, D, device=DEV, dtype=torch.bfloat16)
+        ops.linear_fused(x, w, q, epilogue=ops.EPI_QKV_ROPE, ss_in=ss_in, ss_in_parts=8, splits=splits,
+                         qkv=dict(num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=qn, k_norm=kn, eps=1e-6,
+                                  cos_sin=cos_sin, positions=positions, cache_loc=slots, k_cache=kc, v_cache=vc))
+        return q, kc, vc
+
+    (qa, ka, va), (qb, kb, vb) = _both(run)
+    assert torch.equal(qa, qb) and torch.equal(ka, kb) and torch.equal(va, vb)
+
+
+def test_loop_f32_and_router_match_split_k():
+    from omni_b200 import ops
+
+    g = _gen(11)
+    rows, k = 19000, 1024
+    x = torch.randn(rows, k, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(128, k, generator=g, device=DEV) * 0.05).to(torch.bfloat16)
+
+    def f32(splits):
+        y = torch.empty(rows, 128, device=DEV, dtype=torch.float32)
+        ops.linear_fused(x, w, y, epilogue=ops.EPI_F32, splits=splits)
+        return y
+
+    def router(splits):
+        y = torch.empty(rows, 128, device=DEV, dtype=torch.bfloat16)
+        ids = torch.full((rows, 8), -1, device=DEV, dtype=torch.int32)
+        tw = torch.zeros(rows, 8, device=DEV, dtype=torch.float32)
+        ops.linear_fused(x, w, y, epilogue=ops.EPI_ROUTER, splits=splits,
+                         router={"topk_ids": ids, "topk_weights": tw})
+        return y, ids, tw
+
+    a, b = _both(f32)
+    assert torch.equal(a, b)
+    (ya, ia, wa), (yb, ib, wb) = _both(router)
+    assert torch.equal(ya, yb) and torch.equal(ia, ib) and torch.equal(wa, wb)
+    from omni_b200 import device_status
+
+    assert device_status() == 0
