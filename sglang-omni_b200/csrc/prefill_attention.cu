@@ -411,44 +411,66 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
 
 // ---------------------------------------------------------------------------
 // GQA pair kernel: CTA = 128 queries of one stream x two query heads of one KV
-// head, so each K / V tile is loaded once for both heads.  Ten warps:
-//   warp 0    TMA producer: both heads' Q tiles once; per key tile the 8 pages of K
-//             into a two-stage K ring and (one tile behind) the 8 pages of V into a
-//             single V stage, one 16-row x 64-column box per lane (measured against
-//             one K stage with two V stages, and a three-slot ring that K and V take
-//             in turn: 981 against 1054 and 1027 us at config 2);
-//   warp 1    MMA issuer (polling its barriers without blocking): S_h(j) = Q_h K_j^T
-//             into head h's TMEM S buffer once K_j has landed and the head's softmax
-//             has released S_h(j-1); O_h += P_h(j) V_j once P_h(j) is written and V_j
-//             has landed;
+// head, so each K / V tile is loaded once for both heads.  Keys go by in tiles of 64
+// (4 pages), so that each head has two S buffers in TMEM (2 heads x 2 x 64 columns,
+// and the two O accumulators of 128 columns: 512): the tensor core computes S(j + 1)
+// and P V(j - 1) while the softmax warps work on tile j.  Ten warps:
+//   warp 0    TMA producer: both heads' Q tiles once; per key tile the 4 pages of K
+//             and of V (one 16-row x 64-column box per lane) into three-slot K and V
+//             rings;
+//   warp 1    MMA issuer: S_h(j) = Q_h K_j^T into S buffer j & 1 of head h once K_j
+//             has landed and the head's softmax has released that buffer (tile j - 2);
+//             O_h += P_h(j) V_j once P_h(j) is written and V_j has landed.  Eight lanes
+//             test the eight barriers a round depends on at once (non-blocking
+//             test_wait) and one ballot gathers them: polling them one after another
+//             left 500-1 000 cycles between MMA groups;
 //   warps 2-5 softmax of head 0, warps 6-9 of head 1: one thread per query row (TMEM
-//             lane) over all 128 columns of the tile, so a row's max and sum stay in
-//             one thread: P = exp2(s * scale * log2 e - m) against the running max m
-//             in one pass, into the head's swizzled P buffer (K-major A operand of
-//             P V); the first tile and a tile whose max passes m by more than 2^8
-//             rescale O and the running sum and write P again.
-// Measured schedule (clock64 timeline of one CTA, 32 key tiles): the two heads run in
-// step, their softmaxes overlapping (~4 200 cycles a tile, two warps a sub-partition
-// hiding each other's latency), then the MMAs (~2 000 cycles): ~5 900 cycles a tile
-// pair, the tensor pipe ~35 % busy.  Making the heads take turns (one softmax while the
-// tensor core serves the other head) lengthened each softmax to ~3 200 cycles (one warp
-// a sub-partition) and the period to ~7 000; computing a share of the exponentials by a
-// polynomial on the FMA pipe, or twelve warps with setmaxnreg (no register spills),
-// were slower too.
-// Shared memory: Q 2 x 32 KB, K 2 x 32 KB, V 32 KB, P 2 x 32 KB (224 KB).
-// TMEM: S_0, S_1 (128 columns each), O_0, O_1 (128 each).
+//             lane) over the tile's 64 columns, so a row's max and sum stay in one
+//             thread: P = exp2(s * scale * log2 e - m) against the running max m in one
+//             pass, into the head's swizzled P buffer j & 1 (K-major A operand of P V);
+//             the first tile and a tile whose max passes m by more than 2^8 rescale O
+//             (after the head's previous P V) and the running sum and write P again.
+// Shared memory: Q 2 x 32 KB, K and V rings 3 x 16 KB each, P 2 heads x 2 x 16 KB
+// (192 KB).  History at config 2 (TFLOP/s of causal QK^T + PV): one head a CTA with
+// 128-key tiles 409; two heads with 128-key tiles (one S buffer a head, softmax and MMAs
+// not overlapped) 495; 64-key tiles with two S buffers 507; with the ballot polling and
+// the MMA warp sleeping 32 ns between idle rounds (its spinning took issue slots from
+// the softmax warps of its sub-partition) 559.  Measured slower: a polynomial exp2 on the
+// FMA pipe for 4 to 16 of every 32 keys (933-1 049 against 882 us; the softmax is bound
+// by its dependency chains, not by the special-function pipe), twelve warps with
+// setmaxnreg, the two heads' softmaxes taking turns.
 // ---------------------------------------------------------------------------
+constexpr int kPKeys = 64;                              // keys per tile
+constexpr int kPHalf = kPKeys * 128;                    // [64 keys][64 bf16]: 8 KB
+constexpr int kPTile = 2 * kPHalf;                      // a K or V tile: 16 KB
+constexpr int kPSlots = 3;
+constexpr int kPPBytes = kRows * 128;                   // P: [128 queries][64 keys] bf16, 16 KB
 constexpr int kPairQOff = 0;                            // head h: + h * 32 KB
-constexpr int kPairKOff = 2 * kTileBytes;               // stage s: + s * 32 KB
-constexpr int kPairVOff = 4 * kTileBytes;
-constexpr int kPairPOff = 5 * kTileBytes;               // head h: + h * 32 KB
-constexpr int kPairBarOff = 7 * kTileBytes;             // 224 KB
-constexpr size_t kPairSmemBytes = (size_t)kPairBarOff + 256 + 1024;
+constexpr int kPairKOff = 2 * kTileBytes;               // slot s: + s * 16 KB
+constexpr int kPairVOff = kPairKOff + kPSlots * kPTile;
+constexpr int kPairPOff = kPairVOff + kPSlots * kPTile;  // (head, buffer): + (2 h + b) * 16 KB
+constexpr int kPairBarOff = kPairPOff + 4 * kPPBytes;   // 192 KB
+constexpr size_t kPairSmemBytes = (size_t)kPairBarOff + 512 + 1024;
 
 struct PairBars {
-  uint64_t q_full, k_full[2], k_empty[2], v_full, v_empty, s_full[2], s_free[2], p_full[2], pv_done[2], drain;
+  uint64_t q_full, k_full[kPSlots], k_empty[kPSlots], v_full[kPSlots], v_empty[kPSlots];
+  uint64_t s_full[2][2], s_free[2][2], p_full[2][2], pv_done[2][2], drain;
   uint32_t tmem;
 };
+
+// MN-major 128B-swizzle descriptor of a V tile of 64 keys: 64-element rows along N
+// (the head dimension), 8-row groups along K 1024 B apart, the second 64 columns of N
+// one 8 KB half away.
+OMNI_DEVINL uint64_t desc_mn_sw128_64(const void* p) {
+  uint64_t addr = smem_u32(p);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;
+  d |= (uint64_t)(kPHalf >> 4) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
 
 __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
     const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -475,20 +497,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
   const int nq = min(kRows, ext - q0);
   const int kvh = h0 / (p.hq / p.hkv);
   const int pg0 = p.page_indptr[st], npages = p.page_indptr[st + 1] - pg0;
-  const int nt = (prefix + q0 + nq + kKeys - 1) / kKeys;
+  const int nt = (prefix + q0 + nq + kPKeys - 1) / kPKeys;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kPSlots; ++i) {
       mbar_init(&bars->k_full[i], 1);
       mbar_init(&bars->k_empty[i], 1);
-      mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_free[i], 4 * 32);
-      mbar_init(&bars->p_full[i], 4 * 32);
-      mbar_init(&bars->pv_done[i], 1);
+      mbar_init(&bars->v_full[i], 1);
+      mbar_init(&bars->v_empty[i], 1);
     }
-    mbar_init(&bars->v_full, 1);
-    mbar_init(&bars->v_empty, 1);
+    for (int h = 0; h < 2; ++h)
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&bars->s_full[h][b], 1);
+        mbar_init(&bars->s_free[h][b], 4 * 32);
+        mbar_init(&bars->p_full[h][b], 4 * 32);
+        mbar_init(&bars->pv_done[h][b], 1);
+      }
     mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
@@ -513,66 +538,77 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
     if (lane < 4)
       tma_load_2d(smem + kPairQOff + (lane >> 1) * kTileBytes + (lane & 1) * kHalfBytes, &tq, &bars->q_full,
                   (h0 + (lane >> 1)) * kD + (lane & 1) * 64, qs0 + q0);
-    const int idx = lane & 15, pg = idx >> 1, half = idx & 1;
+    const int pg = lane >> 1, half = lane & 1;  // lanes 0-7: page pg of the tile, head-dim half
     auto load_tile = [&](const void* map, uint8_t* base, uint64_t* bar, int j) {
-      if (lane == 0) mbar_arrive_expect_tx(bar, kTileBytes);
+      if (lane == 0) mbar_arrive_expect_tx(bar, kPTile);
       __syncwarp();
-      if (lane < 16) {
-        const int pgl = j * (kKeys / kPage) + pg;
+      if (lane < 8) {
+        const int pgl = j * (kPKeys / kPage) + pg;
         const int64_t y = pgl < npages ? (int64_t)p.page_indices[pg0 + pgl] * kPage : p.num_slots;
-        tma_load_2d(base + half * kHalfBytes + pg * kPage * 128, map, bar, kvh * kD + half * 64, (int)y);
+        tma_load_2d(base + half * kPHalf + pg * kPage * 128, map, bar, kvh * kD + half * 64, (int)y);
       }
     };
-    // K_j, then V_{j-1} (V is used a softmax later than K)
-    for (int j = 0; j <= nt; ++j) {
-      if (j < nt) {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&bars->k_empty[s], ((j - 2) >> 1) & 1)) {
-          report_status(kDevTimeoutTma);
-          break;
-        }
-        load_tile(&tk, smem + kPairKOff + s * kTileBytes, &bars->k_full[s], j);
+    for (int j = 0; j < nt; ++j) {
+      const int s = j % kPSlots;
+      const uint32_t par = ((j / kPSlots) - 1) & 1;
+      if (j >= kPSlots && !mbar_wait(&bars->k_empty[s], par)) {
+        report_status(kDevTimeoutTma);
+        break;
       }
-      if (j >= 1) {
-        if (j >= 2 && !mbar_wait(&bars->v_empty, (j - 2) & 1)) {
-          report_status(kDevTimeoutTma);
-          break;
-        }
-        load_tile(&tv, smem + kPairVOff, &bars->v_full, j - 1);
+      load_tile(&tk, smem + kPairKOff + s * kPTile, &bars->k_full[s], j);
+      if (j >= kPSlots && !mbar_wait(&bars->v_empty[s], par)) {
+        report_status(kDevTimeoutTma);
+        break;
       }
+      load_tile(&tv, smem + kPairVOff + s * kPTile, &bars->v_full[s], j);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     const bool leader = elect_one();
-    const uint32_t idesc_qk = idesc_bf16_f32(kRows, kKeys);
+    const uint32_t idesc_qk = idesc_bf16_f32(kRows, kPKeys);
     const uint32_t idesc_pv = idesc_bf16_f32(kRows, kD) | (1u << 16);  // B MN-major
     bool ok = mbar_wait(&bars->q_full, 0);
-    auto ready = [&](uint64_t* bar, uint32_t parity) -> bool {
-      uint32_t r = lane == 0 ? (mbar_test_wait(bar, parity) ? 1u : 0u) : 0u;
-      return __shfl_sync(0xFFFFFFFFu, r, 0) != 0;
-    };
     int jq[2] = {0, 0}, ip[2] = {0, 0};
     uint32_t idle = 0;
     while (ok && (ip[0] < nt || ip[1] < nt)) {
+      // lanes 0-7 test the eight barriers this round can act on at once (one ballot
+      // instead of eight polls in turn): lane 2h / 2h+1: head h's P and V of tile
+      // ip[h]; lane 4+2h / 5+2h: K of tile jq[h] and head h's S buffer
+      bool c = false;
+      if (lane < 8) {
+        const int h = (lane >> 1) & 1;
+        if (lane < 4) {
+          const int i = ip[h];
+          if (i < jq[h])
+            c = (lane & 1) ? mbar_test_wait(&bars->v_full[i % kPSlots], (i / kPSlots) & 1)
+                           : mbar_test_wait(&bars->p_full[h][i & 1], (i >> 1) & 1);
+        } else {
+          const int j = jq[h];
+          if (j < nt)
+            c = (lane & 1) ? (j < 2 || mbar_test_wait(&bars->s_free[h][j & 1], ((j - 2) >> 1) & 1))
+                           : mbar_test_wait(&bars->k_full[j % kPSlots], (j / kPSlots) & 1);
+        }
+      }
+      const uint32_t m = __ballot_sync(0xFFFFFFFFu, c);
       bool progressed = false;
-      // P V first: it frees the V stage (and lets the head's softmax go on)
+      // P V first: it frees the V slot (and lets the head's softmax go on)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int i = ip[h];
-        if (i < jq[h] && ready(&bars->p_full[h], i & 1) && ready(&bars->v_full, i & 1)) {
+        const int s = i % kPSlots;
+        if (((m >> (2 * h)) & 3u) == 3u) {
           tc_fence_after();
           if (leader) {
-            const uint8_t* pt = smem + kPairPOff + h * kTileBytes;
-            const uint8_t* vt = smem + kPairVOff;
+            const uint8_t* pt = smem + kPairPOff + (2 * h + (i & 1)) * kPPBytes;
+            const uint8_t* vt = smem + kPairVOff + s * kPTile;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint64_t ad = smem_desc_sw128(pt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
-              const uint64_t bd = desc_mn_sw128(vt + k * 16 * 128);
+            for (int k = 0; k < kPKeys / 16; ++k) {
+              const uint64_t ad = smem_desc_sw128(pt) + 2 * k;
+              const uint64_t bd = desc_mn_sw128_64(vt + k * 16 * 128);
               tc_mma_bf16(tbase + 256 + h * 128, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
             }
-            tc_commit(&bars->pv_done[h]);
-            // the V stage is free once both heads' P V of this tile have completed
-            if (ip[h ^ 1] > i) tc_commit(&bars->v_empty);
+            tc_commit(&bars->pv_done[h][i & 1]);
+            if (ip[h ^ 1] > i) tc_commit(&bars->v_empty[s]);  // both heads' P V of tile i
           }
           __syncwarp();
           ++ip[h];
@@ -582,31 +618,34 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int j = jq[h];
-        // S_h(j) overwrites S_h(j-1): after the head's softmax released it; at most
-        // one K tile ahead of the other head (two K stages)
-        if (j < nt && j <= ip[h] && j <= jq[h ^ 1] + 1 && ready(&bars->k_full[j & 1], (j >> 1) & 1) &&
-            (j == 0 || ready(&bars->s_free[h], (j - 1) & 1))) {
+        const int s = j % kPSlots;
+        // S_h(j) into buffer j & 1, one tile ahead of the head's P V at most
+        if (((m >> (4 + 2 * h)) & 3u) == 3u && j <= ip[h] + 1) {
           tc_fence_after();
           if (leader) {
             const uint8_t* qt = smem + kPairQOff + h * kTileBytes;
-            const uint8_t* kt = smem + kPairKOff + (j & 1) * kTileBytes;
+            const uint8_t* kt = smem + kPairKOff + s * kPTile;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const uint64_t ad = smem_desc_sw128(qt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
-              const uint64_t bd = smem_desc_sw128(kt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
-              tc_mma_bf16(tbase + h * 128, ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+              const uint64_t bd = smem_desc_sw128(kt + (k >> 2) * kPHalf) + 2 * (k & 3);
+              tc_mma_bf16(tbase + h * 128 + (j & 1) * kPKeys, ad, bd, idesc_qk, k > 0 ? 1u : 0u);
             }
-            tc_commit(&bars->s_full[h]);
-            // the K stage is free once both heads' S of this tile have completed
-            if (jq[h ^ 1] > j) tc_commit(&bars->k_empty[j & 1]);
+            tc_commit(&bars->s_full[h][j & 1]);
+            if (jq[h ^ 1] > j) tc_commit(&bars->k_empty[s]);  // both heads' S of tile j
           }
           __syncwarp();
           ++jq[h];
           progressed = true;
         }
       }
-      if (progressed) idle = 0;
-      else if (++idle > 4 * kWaitLimit) ok = false;
+      if (progressed) {
+        idle = 0;
+      } else {
+        // leave the issue slots of this sub-partition to the softmax warps beside it
+        __nanosleep(32);
+        if (++idle > 4 * kWaitLimit) ok = false;
+      }
     }
     if (!ok) report_status(kDevTimeoutMma);
     if (leader) tc_commit(&bars->drain);
@@ -618,24 +657,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
     const int q = warp & 3;                 // TMEM lane quarter of this warp
     const int r = q * 32 + lane;            // query row of the tile
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    const uint32_t tS = tbase + lane_off + h * 128;
     const uint32_t tO = tbase + lane_off + 256 + h * 128;
     const int lim = prefix + q0 + r;        // last key this query sees
     const float sl = p.scale_log2;
-    uint8_t* prow = smem + kPairPOff + h * kTileBytes + r * 128;
     float m_use = -INFINITY, l = 0.0f;
     bool ok = true;
-    // P = exp2(s * scale - m_use) of the row's 128 keys of tile j into the P buffer
+    // P = exp2(s * scale - m_use) of the row's 64 keys of tile j into P buffer j & 1
     // (masked keys 0); returns their sum and the raw max score
-    auto write_p = [&](int j, bool masked, float& mx) -> float {
+    auto write_p = [&](uint32_t tS, uint8_t* prow, int j, bool masked, float& mx) -> float {
       float rs = 0.0f;
       mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tS + c * 32, v);
         tc_wait_ld();
-        const int k0 = j * kKeys + c * 32;
+        const int k0 = j * kPKeys + c * 32;
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
@@ -649,50 +686,57 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
           rs += pa + pb;
           pk[e >> 1] = pack_bf2(pa, pb);
         }
-        // keys c*32 .. c*32+31: half c / 2, 16-byte chunks (c & 1) * 4 .. + 3 of the row
-        uint8_t* hrow = prow + (c >> 1) * kHalfBytes;
+        // keys c*32 .. c*32+31: 16-byte chunks c*4 .. c*4+3 of the row
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int chunk = (c & 1) * 4 + u;
-          *reinterpret_cast<uint4*>(hrow + ((chunk ^ (r & 7)) << 4)) =
+          const int chunk = c * 4 + u;
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) =
               make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         }
       }
       return rs;
     };
     for (int j = 0; j < nt && ok; ++j) {
-      if (!mbar_wait(&bars->s_full[h], j & 1)) {
+      const int b = j & 1;
+      if (!mbar_wait(&bars->s_full[h][b], (j >> 1) & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      // the P buffer of tile j - 1 is free once its P V has completed
-      if (j >= 1 && !mbar_wait(&bars->pv_done[h], (j - 1) & 1)) {
+      const uint32_t tS = tbase + lane_off + h * 128 + b * kPKeys;
+      // P buffer b held tile j - 2: free once that P V has completed
+      if (j >= 2 && !mbar_wait(&bars->pv_done[h][b], ((j - 2) >> 1) & 1)) {
         ok = false;
         break;
       }
-      const bool masked = j * kKeys + kKeys - 1 > prefix + q0;
+      uint8_t* prow = smem + kPairPOff + (2 * h + b) * kPPBytes + r * 128;
+      const bool masked = j * kPKeys + kPKeys - 1 > prefix + q0;
       float mx, rs = 0.0f;
       if (m_use == -INFINITY) {
         mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tS + c * 32, v);
           tc_wait_ld();
-          const int k0 = j * kKeys + c * 32;
+          const int k0 = j * kPKeys + c * 32;
 #pragma unroll
           for (int e = 0; e < 32; ++e)
             if (!masked || k0 + e <= lim) mx = fmaxf(mx, __uint_as_float(v[e]));
         }
       } else {
-        rs = write_p(j, masked, mx);
+        rs = write_p(tS, prow, j, masked, mx);
       }
       const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl;
       if (m_tile != -INFINITY && (m_use == -INFINITY || m_tile > m_use + kRescaleLog2)) {
         const float alpha = m_use == -INFINITY ? 0.0f : ex2_approx(m_use - m_tile);
         if (j > 0 && l > 0.0f) {
-          // O holds tiles < j: its last P V (tile j - 1) has completed (waited above)
+          // O holds tiles < j once the head's P V of tile j - 1 has completed
+          if (!mbar_wait(&bars->pv_done[h][(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t v[32];
@@ -707,15 +751,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
         l *= alpha;
         m_use = m_tile;
         float unused;
-        rs = write_p(j, masked, unused);
+        rs = write_p(tS, prow, j, masked, unused);
       }
       l += rs;
       tc_fence_before();
-      mbar_arrive(&bars->s_free[h]);
+      mbar_arrive(&bars->s_free[h][b]);
       fence_proxy_async();  // the P stores, visible to the tensor core
-      mbar_arrive(&bars->p_full[h]);
+      mbar_arrive(&bars->p_full[h][b]);
     }
-    if (ok && nt > 0 && mbar_wait(&bars->pv_done[h], (nt - 1) & 1)) {
+    if (ok && nt > 0 && mbar_wait(&bars->pv_done[h][(nt - 1) & 1], ((nt - 1) >> 1) & 1)) {
       tc_fence_after();
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       uint16_t* orow = p.out + (int64_t)(qs0 + q0 + r) * p.out_stride + (int64_t)(h0 + h) * kD;
