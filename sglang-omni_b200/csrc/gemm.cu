@@ -256,7 +256,8 @@ OMNI_DEVINL void quad_epilogue(const GemmParams& p, int64_t grow, int tile, int 
     for (int j = 0; j < 4; ++j) ss = __fmaf_rn(o[j], o[j], ss);
     for (int off = 1; off < head_lanes; off <<= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
     if (is_q || is_k) {
-      const float hr = rsqrtf(ss / (float)D + p.qk_eps);
+      // D is 64 or 128: scaling by the exact reciprocal is the same rounding as the division
+      const float hr = rsqrtf(ss * (D == 128 ? 0.0078125f : 0.015625f) + p.qk_eps);
       const uint2 wv = in.gw;
       const float gw4[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
 #pragma unroll
