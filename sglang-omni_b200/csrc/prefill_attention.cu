@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
 //             the first tile and a tile whose max passes m by more than 2^8 rescale O
 //             (after the head's previous P V) and the running sum and write P again.
 // Shared memory: Q 2 x 32 KB, K and V rings 3 x 16 KB each, P 2 heads x 2 x 16 KB
-// (192 KB).  History at config 2 (TFLOP/s of causal QK^T + PV): one head a CTA with
+// (224 KB).  History at config 2 (TFLOP/s of causal QK^T + PV): one head a CTA with
 // 128-key tiles 409; two heads with 128-key tiles (one S buffer a head, softmax and MMAs
 // not overlapped) 495; 64-key tiles with two S buffers 507; with the ballot polling and
 // the MMA warp sleeping 32 ns between idle rounds (its spinning took issue slots from
@@ -449,7 +449,7 @@ constexpr int kPairQOff = 0;                            // head h: + h * 32 KB
 constexpr int kPairKOff = 2 * kTileBytes;               // slot s: + s * 16 KB
 constexpr int kPairVOff = kPairKOff + kPSlots * kPTile;
 constexpr int kPairPOff = kPairVOff + kPSlots * kPTile;  // (head, buffer): + (2 h + b) * 16 KB
-constexpr int kPairBarOff = kPairPOff + 4 * kPPBytes;   // 192 KB
+constexpr int kPairBarOff = kPairPOff + 4 * kPPBytes;   // 224 KB
 constexpr size_t kPairSmemBytes = (size_t)kPairBarOff + 512 + 1024;
 
 struct PairBars {
