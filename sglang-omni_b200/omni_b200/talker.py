@@ -150,6 +150,7 @@ class DenseTalker:
         self.codec_head_folded = ops.fold_norm(self.w["codec_head"], self.w["norm"])
         self.ss = torch.zeros(H // 128, R, dtype=torch.float32, device=self.device)
         self.ss_sel = torch.zeros(H // 128, B, dtype=torch.float32, device=self.device)
+        self.qkv_raw = None  # raw qkv rows of a prompt-sized mixed step (allocated at the first one)
 
     def ensure_attention_workspace(self, work_capacity: int) -> None:
         need = ops.paged_attention_workspace_bytes(self.max_batch, self.cfg.num_key_value_heads, work_capacity)
@@ -229,13 +230,28 @@ class DenseTalker:
             ops.add_sumsq(feedback, text, h[:Bd], ss[0, :Bd])
         ops.add_sumsq(prompt_embeds, None, h[Bd:R], ss[0, Bd:R])
         ss_parts = 1
+        # prompt-sized batches: the qkv projection as a plain GEMM (the tile-loop kernel)
+        # into a raw buffer, then the q/k head norms, rotary and K/V store as their own
+        # pass; the same values, rounded at the same points, as the fused qkv epilogue,
+        # whose per-row work measured slower at these sizes
+        split_qkv = R > 256
+        if split_qkv and (self.qkv_raw is None or self.qkv_raw.shape[0] < R):
+            self.qkv_raw = torch.empty(self.max_rows, (hq + 2 * hkv) * D, device=self.device, dtype=torch.bfloat16)
         for li, lw in enumerate(self.w["layers"]):
             kc, vc = self.kv.k_buffer[li], self.kv.v_buffer[li]
-            ops.linear_fused(h, self.folded[li]["qkv"], q, epilogue=ops.EPI_QKV_ROPE, ss_in=ss, ss_in_parts=ss_parts,
-                             norm_eps=eps, qkv=dict(num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=lw["q_norm"],
-                                                    k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin,
-                                                    positions=positions[:R], cache_loc=cache_loc[:R],
-                                                    k_cache=kc, v_cache=vc))
+            if split_qkv:
+                raw = self.qkv_raw[:R]
+                ops.linear_fused(h, self.folded[li]["qkv"], raw, epilogue=ops.EPI_STORE, ss_in=ss,
+                                 ss_in_parts=ss_parts, norm_eps=eps)
+                ops.qknorm_rope_store(raw, num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=lw["q_norm"],
+                                      k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin, q_out=q, k_cache=kc,
+                                      v_cache=vc, positions=positions[:R], cache_loc=cache_loc[:R])
+            else:
+                ops.linear_fused(h, self.folded[li]["qkv"], q, epilogue=ops.EPI_QKV_ROPE, ss_in=ss,
+                                 ss_in_parts=ss_parts, norm_eps=eps,
+                                 qkv=dict(num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=lw["q_norm"],
+                                          k_norm=lw["k_norm"], eps=eps, cos_sin=self.cos_sin,
+                                          positions=positions[:R], cache_loc=cache_loc[:R], k_cache=kc, v_cache=vc))
             if Bd > 0:
                 ops.paged_decode_attention(q[:Bd], kc, vc, page_indptr=fb.page_indptr, page_indices=fb.page_indices,
                                            seq_lens=fb.seq_lens, work_indptr=fb.work_indptr, num_q_heads=hq,

@@ -136,3 +136,41 @@ def test_loop_f32_and_router_match_split_k():
     from omni_b200 import device_status
 
     assert device_status() == 0
+
+
+def test_qkv_as_store_then_qknorm_pass_equals_fused_epilogue():
+    """The mixed step's prompt-sized path (plain GEMM into raw qkv rows, then the q/k head
+    norms, rotary and K/V store as their own pass) writes the same bits as the fused qkv
+    epilogue: both round the projection to bf16, sum the head's squares in the same order
+    and round the normed and rotated values at the same points."""
+    from omni_b200 import ops
+
+    rows, k, hq, hkv, D = 1500, 1024, 16, 2, 128
+    n = (hq + 2 * hkv) * D
+    g = _gen(21)
+    x = torch.randn(rows, k, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, generator=g, device=DEV)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, generator=g, device=DEV)).to(torch.bfloat16)
+    cos_sin = ops.rope_cos_sin_cache(8192, D, 1e6, torch.device(DEV))
+    positions = torch.randint(0, 8192, (rows,), generator=g, device=DEV)
+    slots = torch.randperm(rows + 64, generator=g, device=DEV)[:rows]
+    ss_in = x.float().view(rows, 8, 128).pow(2).sum(-1).t().contiguous()
+
+    def caches():
+        return (torch.zeros(rows + 64, hkv, D, device=DEV, dtype=torch.bfloat16),
+                torch.zeros(rows + 64, hkv, D, device=DEV, dtype=torch.bfloat16))
+
+    q1 = torch.empty(rows, hq * D, device=DEV, dtype=torch.bfloat16)
+    k1, v1 = caches()
+    ops.linear_fused(x, w, q1, epilogue=ops.EPI_QKV_ROPE, ss_in=ss_in, ss_in_parts=8,
+                     qkv=dict(num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=qn, k_norm=kn, eps=1e-6,
+                              cos_sin=cos_sin, positions=positions, cache_loc=slots, k_cache=k1, v_cache=v1))
+    raw = torch.empty(rows, n, device=DEV, dtype=torch.bfloat16)
+    ops.linear_fused(x, w, raw, epilogue=ops.EPI_STORE, ss_in=ss_in, ss_in_parts=8)
+    q2 = torch.empty(rows, hq * D, device=DEV, dtype=torch.bfloat16)
+    k2, v2 = caches()
+    ops.qknorm_rope_store(raw, num_q_heads=hq, num_kv_heads=hkv, head_dim=D, q_norm=qn, k_norm=kn, eps=1e-6,
+                          cos_sin=cos_sin, q_out=q2, k_cache=k2, v_cache=v2, positions=positions, cache_loc=slots)
+    torch.cuda.synchronize()
+    assert torch.equal(q1, q2) and torch.equal(k1, k2) and torch.equal(v1, v2)

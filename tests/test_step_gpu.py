@@ -111,15 +111,18 @@ def test_public_decode_api_round_trip():
     assert device_status() == 0
 
 
-def test_mixed_prefill_decode_step_matches_oracle():
+@pytest.mark.parametrize("prompts", [(20, 70), (150, 260)], ids=["fused-qkv", "prompt-sized"])
+def test_mixed_prefill_decode_step_matches_oracle(prompts):
     """Config 2's fused forward at small size: 3 decode streams + 2 new streams (prompts of
-    20 and 70 rows) in one forward; logits / hidden of the decode rows and of each new
-    stream's last prompt row within the bf16 tolerance, the prompts' KV in the pool, the
-    layer-0 draws bit-exact given the device logits."""
+    20 and 70 rows; or 150 and 260, over 256 rows, where the projections take the tile loop
+    and the qkv projection its separate norm / rotary / store pass) in one forward; logits /
+    hidden of the decode rows and of each new stream's last prompt row within the bf16
+    tolerance, the prompts' KV in the pool, the layer-0 draws bit-exact given the device
+    logits."""
     from omni_b200.config import SamplingParams, TalkerConfig
     from omni_b200.model_runner import TalkerDecodeRunner
 
-    lens, prompts = (16, 33, 100), (20, 70)
+    lens = (16, 33, 100)
     cfg = TalkerConfig(num_hidden_layers=2, max_context=1024)
     pages = sum((L + 16) // 16 for L in lens) + sum((L + 15) // 16 for L in prompts) + 32
     r = TalkerDecodeRunner(cfg, max_batch=5, num_pages=pages, seed=6, max_prefill_tokens=sum(prompts))
