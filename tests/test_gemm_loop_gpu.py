@@ -174,3 +174,33 @@ def test_qkv_as_store_then_qknorm_pass_equals_fused_epilogue():
                           cos_sin=cos_sin, q_out=q2, k_cache=k2, v_cache=v2, positions=positions, cache_loc=slots)
     torch.cuda.synchronize()
     assert torch.equal(q1, q2) and torch.equal(k1, k2) and torch.equal(v1, v2)
+
+
+@pytest.mark.parametrize("rows,k,n,epi", [
+    (2369, 64, 1024, "store"),       # one k-step; the last row tile holds one row
+    (18945, 128, 128, "residual"),   # one feature tile, 149 row tiles
+    (9473, 256, 256, "swiglu"),      # two SwiGLU output tiles of 64
+    (2433, 1024, 1024, "residual"),  # 152 tiles: barely more than one per SM
+])
+def test_loop_edges_match_split_k(rows, k, n, epi):
+    from omni_b200 import ops
+
+    g = _gen(rows + k + n)
+    x = torch.randn(rows, k, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g, device=DEV) * 0.05).to(torch.bfloat16)
+    res = torch.randn(rows, n, generator=g, device=DEV).to(torch.bfloat16)
+    code = {"store": ops.EPI_STORE, "residual": ops.EPI_RESIDUAL, "swiglu": ops.EPI_SWIGLU}[epi]
+    width = n // 2 if epi == "swiglu" else n
+
+    def run(splits):
+        y = torch.full((rows, width), float("nan"), device=DEV, dtype=torch.bfloat16)
+        ss = torch.full((max(n // 128, 1), rows), -1.0, device=DEV) if epi == "residual" else None
+        ops.linear_fused(x, w, y, epilogue=code, residual=res if epi == "residual" else None, ss_out=ss,
+                         splits=splits)
+        return y, ss
+
+    (ya, sa), (yb, sb) = _both(run)
+    assert torch.isfinite(ya.float()).all()
+    assert torch.equal(ya, yb)
+    if sa is not None:
+        assert torch.equal(sa, sb)
