@@ -687,18 +687,24 @@ __global__ void __launch_bounds__(kThreadsG, (EPI == kEpiF32) ? 1 : 2)
 // kernel.  No split: every tile sums its whole K in TMEM.
 // ---------------------------------------------------------------------------
 constexpr int kLoopThreads = 320;
-constexpr int kLoopRows = 128;
-constexpr int kLoopStages = 5;
-constexpr int kLoopWBytes = kTileN * kBK * 2;                 // 16 KB
-constexpr int kLoopStageBytes = kLoopWBytes + kLoopRows * kBK * 2;  // 32 KB
-constexpr int kLoopStagingBytes = 32 * kTileN * 4;            // 16 KB: 32 rows x 128 fp32
-constexpr int kLoopStagingOff = kLoopStages * kLoopStageBytes;
-constexpr int kLoopInfoOff = kLoopStagingOff + 2 * kLoopStagingBytes;
-constexpr int kLoopBarOff = kLoopInfoOff + 2 * 3 * kLoopRows * 4;
-constexpr size_t kLoopSmem = (size_t)kLoopBarOff + 256 + 1024;
+constexpr int kLoopWBytes = kTileN * kBK * 2;  // 16 KB
+// Row tile RT (the MMA's N): 128 rows with five 32 KB stages, drained 32 rows at a time;
+// or 256 rows with four 48 KB stages (twice the multiply-adds per staged byte), drained
+// 16 rows at a time so that the staging fits beside them.
+template <int RT>
+struct LoopCfg {
+  static constexpr int kStages = RT == 256 ? 4 : 5;
+  static constexpr int kChunk = RT == 256 ? 16 : 32;
+  static constexpr int kStageBytes = kLoopWBytes + RT * kBK * 2;
+  static constexpr int kStagingBytes = kChunk * kTileN * 4;
+  static constexpr int kStagingOff = kStages * kStageBytes;
+  static constexpr int kInfoOff = kStagingOff + 2 * kStagingBytes;
+  static constexpr int kBarOff = kInfoOff + 2 * 3 * RT * 4;
+  static constexpr size_t kSmem = (size_t)kBarOff + 256 + 1024;
+};
 
 struct LoopBars {
-  uint64_t full[kLoopStages], empty[kLoopStages], acc_full[2], acc_empty[2];
+  uint64_t full[5], empty[5], acc_full[2], acc_empty[2];
   uint32_t tmem;
 };
 
@@ -718,10 +724,14 @@ OMNI_DEVINL bool group_all(int id, bool pred) {
   return r != 0;
 }
 
-template <int EPI>
+template <int EPI, int RT>
 __global__ void __launch_bounds__(kLoopThreads, 1)
     gemm_loop_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                      const __grid_constant__ GemmParams p) {
+  using C = LoopCfg<RT>;
+  constexpr int kLoopRows = RT, kLoopStages = C::kStages, kChunk = C::kChunk;
+  constexpr int kLoopStageBytes = C::kStageBytes, kLoopStagingBytes = C::kStagingBytes;
+  constexpr int kLoopStagingOff = C::kStagingOff, kLoopInfoOff = C::kInfoOff, kLoopBarOff = C::kBarOff;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   LoopBars* bars = reinterpret_cast<LoopBars*>(smem + kLoopBarOff);
@@ -861,10 +871,12 @@ __global__ void __launch_bounds__(kLoopThreads, 1)
         break;
       }
       tc_fence_after();
-      const int nchunks = (rows_here + 31) / 32;
+      const int nchunks = (rows_here + kChunk - 1) / kChunk;
       for (int c = 0; c < nchunks; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + g * kLoopRows + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+        uint32_t v[kChunk];
+        const uint32_t ta = tmem + g * kLoopRows + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * kChunk);
+        if constexpr (kChunk == 32) tmem_ld_32x32b_x32(ta, v);
+        else tmem_ld_32x32b_x16(ta, v);
         tc_wait_ld();
         if (c == nchunks - 1) {
           // every read of this accumulator is done: the MMA warp may refill it
@@ -873,16 +885,16 @@ __global__ void __launch_bounds__(kLoopThreads, 1)
         }
         group_sync(1 + g);  // the previous chunk's rows are done with the staging buffer
 #pragma unroll
-        for (int j = 0; j < 32; ++j) staging[j * kTileN + q * 32 + lane] = __uint_as_float(v[j]);
+        for (int j = 0; j < kChunk; ++j) staging[j * kTileN + q * 32 + lane] = __uint_as_float(v[j]);
         group_sync(1 + g);
-        const int rmax = min(32, rows_here - c * 32);
+        const int rmax = min(kChunk, rows_here - c * kChunk);
         if (EPI == kEpiSwiGLU) {
           // two rows a warp: lanes 0-15 and 16-31, four outputs a lane
           for (int rr = 2 * wl + (lane >> 4); rr < rmax; rr += 8) {
             const int gq = (lane & 15) * 4;
             const float4 gv = *reinterpret_cast<const float4*>(staging + rr * kTileN + gq);
             const float4 uv = *reinterpret_cast<const float4*>(staging + rr * kTileN + 64 + gq);
-            swiglu_quad(p, row0 + c * 32 + rr, (int64_t)t * 64 + gq, gv, uv, info[c * 32 + rr]);
+            swiglu_quad(p, row0 + c * kChunk + rr, (int64_t)t * 64 + gq, gv, uv, info[c * kChunk + rr]);
           }
         } else {
           // rows wl, wl + 4, ... of the chunk, four at a time: their global operands
@@ -893,7 +905,7 @@ __global__ void __launch_bounds__(kLoopThreads, 1)
             for (int u = 0; u < 4; ++u) {
               const int rr = r0 + 4 * u;
               if (rr < rmax) {
-                const int r = c * 32 + rr;
+                const int r = c * kChunk + rr;
                 in[u] = quad_fetch<EPI>(p, row0 + r, t, lane, EPI == kEpiQKV ? ipos[r] : 0);
               }
             }
@@ -901,7 +913,7 @@ __global__ void __launch_bounds__(kLoopThreads, 1)
             for (int u = 0; u < 4; ++u) {
               const int rr = r0 + 4 * u;
               if (rr < rmax) {
-                const int r = c * 32 + rr;
+                const int r = c * kChunk + rr;
                 const float4 a = *reinterpret_cast<const float4*>(staging + rr * kTileN + lane * 4);
                 const float sc = info[r];
                 float o[4] = {a.x * sc, a.y * sc, a.z * sc, a.w * sc};
@@ -1140,9 +1152,11 @@ Plan make_plan(int64_t rows, int64_t k, int64_t n, int splits_req) {
 
 // Prefill-sized batches with enough (row tile, feature tile) pairs for every SM take the
 // tile loop; a call that asks for a split count (1 included) keeps the split-K kernel.
-template <int EPI>
+template <int EPI, int RT>
 int launch_loop(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n, GemmParams gp,
                 int tiles, cudaStream_t st) {
+  constexpr int kLoopRows = RT;
+  constexpr size_t kLoopSmem = LoopCfg<RT>::kSmem;
   CUtensorMap tw, tx;
   const int wbox = EPI == kEpiSwiGLU ? kTileN / 2 : kTileN;
   if (!make_tmap(&tw, w, n, k, k, wbox) || !make_tmap(&tx, x, rows, k, x_stride, kLoopRows))
@@ -1154,10 +1168,10 @@ int launch_loop(const void* x, int64_t rows, int64_t k, int64_t x_stride, const 
   gp.num_kb = (int)(k / kBK);
   gp.splits = 1;
   gp.swiglu_half = (int)(n / 2);
-  const void* kern = reinterpret_cast<const void*>(gemm_loop_kernel<EPI>);
+  const void* kern = reinterpret_cast<const void*>(gemm_loop_kernel<EPI, RT>);
   if (once_per_device(kern, kAttrSmem, [] {
-        return cudaFuncSetAttribute(gemm_loop_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)kLoopSmem);
+        return cudaFuncSetAttribute(gemm_loop_kernel<EPI, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)LoopCfg<RT>::kSmem);
       }) != cudaSuccess)
     return check_launch(cudaGetLastError());
   const int64_t total = (int64_t)tiles * ((rows + kLoopRows - 1) / kLoopRows);
@@ -1175,7 +1189,7 @@ int launch_loop(const void* x, int64_t rows, int64_t k, int64_t x_stride, const 
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return check_launch(cudaLaunchKernelEx(&cfg, gemm_loop_kernel<EPI>, tw, tx, gp));
+  return check_launch(cudaLaunchKernelEx(&cfg, gemm_loop_kernel<EPI, RT>, tw, tx, gp));
 }
 
 template <int EPI>
@@ -1187,8 +1201,15 @@ int launch_gemm(const void* x, int64_t rows, int64_t k, int64_t x_stride, const 
   // and the router and fp32 ones stay there too
   if (EPI == kEpiStore || EPI == kEpiResidual || EPI == kEpiSwiGLU) {
     const int tiles = (int)(EPI == kEpiSwiGLU ? (n / 2) / (kTileN / 2) : n / kTileN);
-    if (rows > 256 && splits_req == 0 && (int64_t)tiles * ((rows + kLoopRows - 1) / kLoopRows) >= num_sms())
-      return launch_loop<EPI>(x, rows, k, x_stride, w, n, gp, tiles, st);
+    // 256-row tiles once they give every SM a tile (38.7 k rows: down 1 023 -> 1 215,
+    // qkv (store epilogue) 1 002 -> 1 160, o 973 -> 1 034 TFLOP/s; gate_up 912 either
+    // way), else 128-row tiles
+    if (rows > 256 && splits_req == 0) {
+      if ((int64_t)tiles * ((rows + 255) / 256) >= num_sms())
+        return launch_loop<EPI, 256>(x, rows, k, x_stride, w, n, gp, tiles, st);
+      if ((int64_t)tiles * ((rows + 127) / 128) >= num_sms())
+        return launch_loop<EPI, 128>(x, rows, k, x_stride, w, n, gp, tiles, st);
+    }
   }
   const Plan pl = make_plan<EPI>(rows, k, n, splits_req);
   if (pl.splits > kMaxSplits) return set_error(OMNI_ERR_UNSUPPORTED, "at most 16 K-splits");

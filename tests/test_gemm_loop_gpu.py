@@ -7,7 +7,9 @@ the row sums of squares (folded RMSNorm on the way in) and SwiGLU; the store cas
 held to an fp32 reference.  The qkv, fp32 and router epilogues stay on the split-K
 kernel at these sizes; their cases check that the auto-planned and the one-split calls
 agree.  Row counts leave a partial last row tile; the auto-planned call (splits=0) takes
-the loop once the batch has at least one (row tile, feature tile) pair per SM.
+the loop once the batch has at least one (row tile, feature tile) pair per SM, with
+256-row tiles when those are enough for every SM and 128-row tiles otherwise (the edge
+cases cover both).
 """
 
 from __future__ import annotations
@@ -177,10 +179,12 @@ def test_qkv_as_store_then_qknorm_pass_equals_fused_epilogue():
 
 
 @pytest.mark.parametrize("rows,k,n,epi", [
-    (2369, 64, 1024, "store"),       # one k-step; the last row tile holds one row
-    (18945, 128, 128, "residual"),   # one feature tile, 149 row tiles
-    (9473, 256, 256, "swiglu"),      # two SwiGLU output tiles of 64
-    (2433, 1024, 1024, "residual"),  # 152 tiles: barely more than one per SM
+    (2369, 64, 1024, "store"),       # 128-row tiles: one k-step; the last row tile holds one row
+    (18945, 128, 128, "residual"),   # 128-row tiles: one feature tile, 149 row tiles
+    (9473, 256, 256, "swiglu"),      # 128-row tiles: two SwiGLU output tiles of 64
+    (2433, 1024, 1024, "residual"),  # 128-row tiles: 152 tiles, barely more than one per SM
+    (4609, 64, 1024, "store"),       # 256-row tiles: 152 tiles, the last holding one row
+    (5000, 3072, 1024, "residual"),  # 256-row tiles: a partial last tile of 136 rows
 ])
 def test_loop_edges_match_split_k(rows, k, n, epi):
     from omni_b200 import ops
