@@ -265,13 +265,14 @@ def cpu_slice_rate(config: int, seed: int = 0) -> dict:
             "slice_talker_s": t_talker, "slice_predictor_s": t_pred}
 
 
-EXTRA_CONFIGS = (0, 2, 3)
+EXTRA_CONFIGS = (0, 2, 3, 4)
 
 
 def run_extra_configs(args) -> dict:
-    """Configs 0, 2 and 3 measured in the same invocation as the headline (each in a child
-    bench.py process on the same GPU, so that each starts with the device to itself): the
-    child's JSON line, condensed."""
+    """Configs 0, 2, 3 and 4 measured in the same invocation as the headline (each in a
+    child bench.py process on the same GPU, so that each starts with the device to itself):
+    the child's JSON line, condensed.  Config 4 runs its whole 2048-stream trace (its own
+    step count) whatever --steps says."""
     out = {}
     for c in EXTRA_CONFIGS:
         steps = max(5, min(args.steps, 20))
