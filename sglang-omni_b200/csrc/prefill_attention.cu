@@ -430,8 +430,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
 //             pass, into the head's swizzled P buffer j & 1 (K-major A operand of P V);
 //             the first tile and a tile whose max passes m by more than 2^8 rescale O
 //             (after the head's previous P V) and the running sum and write P again.
-// Shared memory: Q 2 x 32 KB, K and V rings 3 x 16 KB each, P 2 heads x 2 x 16 KB
-// (224 KB).  History at config 2 (TFLOP/s of causal QK^T + PV): one head a CTA with
+// Shared memory: Q 2 x 32 KB, K and V rings 3 x 16 KB each (160 KB); P stays in TMEM,
+// written by the softmax over the first 32 columns of the S buffer it has read and
+// read from there as the A operand of P V (the MMA warp issues P V(j) before S(j + 2)
+// into the same buffer).  History at config 2 (TFLOP/s of causal QK^T + PV): one head a CTA with
 // 128-key tiles 409; two heads with 128-key tiles (one S buffer a head, softmax and MMAs
 // not overlapped) 495; 64-key tiles with two S buffers 507; with the ballot polling and
 // the MMA warp sleeping 32 ns between idle rounds (its spinning took issue slots from
@@ -444,13 +446,22 @@ constexpr int kPKeys = 64;                              // keys per tile
 constexpr int kPHalf = kPKeys * 128;                    // [64 keys][64 bf16]: 8 KB
 constexpr int kPTile = 2 * kPHalf;                      // a K or V tile: 16 KB
 constexpr int kPSlots = 3;
-constexpr int kPPBytes = kRows * 128;                   // P: [128 queries][64 keys] bf16, 16 KB
 constexpr int kPairQOff = 0;                            // head h: + h * 32 KB
 constexpr int kPairKOff = 2 * kTileBytes;               // slot s: + s * 16 KB
 constexpr int kPairVOff = kPairKOff + kPSlots * kPTile;
-constexpr int kPairPOff = kPairVOff + kPSlots * kPTile;  // (head, buffer): + (2 h + b) * 16 KB
-constexpr int kPairBarOff = kPairPOff + 4 * kPPBytes;   // 224 KB
+constexpr int kPairBarOff = kPairVOff + kPSlots * kPTile;  // 160 KB
 constexpr size_t kPairSmemBytes = (size_t)kPairBarOff + 512 + 1024;
+
+// D[tmem] (+)= A[tmem] * B[smem], kind::f16: the A operand (here P, bf16 packed two
+// to a 32-bit column, M rows on the TMEM lanes) read from tensor memory.
+OMNI_DEVINL void tc_mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accum)
+      : "memory");
+}
 
 struct PairBars {
   uint64_t q_full, k_full[kPSlots], k_empty[kPSlots], v_full[kPSlots], v_empty[kPSlots];
@@ -599,13 +610,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
         if (((m >> (2 * h)) & 3u) == 3u) {
           tc_fence_after();
           if (leader) {
-            const uint8_t* pt = smem + kPairPOff + (2 * h + (i & 1)) * kPPBytes;
+            // P_h(i) sits in the first 32 columns of head h's S buffer i & 1 (16 keys a
+            // k-step: 8 columns)
+            const uint32_t pt = tbase + h * 128 + (i & 1) * kPKeys;
             const uint8_t* vt = smem + kPairVOff + s * kPTile;
 #pragma unroll
             for (int k = 0; k < kPKeys / 16; ++k) {
-              const uint64_t ad = smem_desc_sw128(pt) + 2 * k;
               const uint64_t bd = desc_mn_sw128_64(vt + k * 16 * 128);
-              tc_mma_bf16(tbase + 256 + h * 128, ad, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+              tc_mma_bf16_ts(tbase + 256 + h * 128, pt + k * 8, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
             }
             tc_commit(&bars->pv_done[h][i & 1]);
             if (ip[h ^ 1] > i) tc_commit(&bars->v_empty[s]);  // both heads' P V of tile i
@@ -662,9 +674,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
     const float sl = p.scale_log2;
     float m_use = -INFINITY, l = 0.0f;
     bool ok = true;
-    // P = exp2(s * scale - m_use) of the row's 64 keys of tile j into P buffer j & 1
-    // (masked keys 0); returns their sum and the raw max score
-    auto write_p = [&](uint32_t tS, uint8_t* prow, int j, bool masked, float& mx) -> float {
+    // P = exp2(s * scale - m_use) of the row's 64 keys of tile j into pk (bf16 pairs,
+    // masked keys 0); returns their sum and the raw max score
+    auto compute_p = [&](uint32_t tS, int j, bool masked, float& mx, uint32_t (&pk)[32]) -> float {
       float rs = 0.0f;
       mx = -INFINITY;
 #pragma unroll
@@ -673,7 +685,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
         tmem_ld_32x32b_x32(tS + c * 32, v);
         tc_wait_ld();
         const int k0 = j * kPKeys + c * 32;
-        uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           float a = __uint_as_float(v[e]), b = __uint_as_float(v[e + 1]);
@@ -684,14 +695,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
           mx = fmaxf(mx, fmaxf(a, b));
           const float pa = ex2_approx(a * sl - m_use), pb = ex2_approx(b * sl - m_use);
           rs += pa + pb;
-          pk[e >> 1] = pack_bf2(pa, pb);
-        }
-        // keys c*32 .. c*32+31: 16-byte chunks c*4 .. c*4+3 of the row
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int chunk = c * 4 + u;
-          *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+          pk[c * 16 + (e >> 1)] = pack_bf2(pa, pb);
         }
       }
       return rs;
@@ -709,10 +713,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
         ok = false;
         break;
       }
-      uint8_t* prow = smem + kPairPOff + (2 * h + b) * kPPBytes + r * 128;
       const bool masked = j * kPKeys + kPKeys - 1 > prefix + q0;
       float mx, rs = 0.0f;
+      uint32_t pk[32];
       if (m_use == -INFINITY) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pk[e] = 0u;  // a tile with no visible key leaves P zero
         mx = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
@@ -725,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
             if (!masked || k0 + e <= lim) mx = fmaxf(mx, __uint_as_float(v[e]));
         }
       } else {
-        rs = write_p(tS, prow, j, masked, mx);
+        rs = compute_p(tS, j, masked, mx, pk);
       }
       const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl;
       if (m_tile != -INFINITY && (m_use == -INFINITY || m_tile > m_use + kRescaleLog2)) {
@@ -751,12 +757,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
         l *= alpha;
         m_use = m_tile;
         float unused;
-        rs = write_p(tS, prow, j, masked, unused);
+        rs = compute_p(tS, j, masked, unused, pk);
       }
       l += rs;
+      // P over the S columns this thread has read (the buffer's first 32 columns)
+      tmem_st_32x32b_x32(tS, pk);
+      tc_wait_st();
       tc_fence_before();
       mbar_arrive(&bars->s_free[h][b]);
-      fence_proxy_async();  // the P stores, visible to the tensor core
       mbar_arrive(&bars->p_full[h][b]);
     }
     if (ok && nt > 0 && mbar_wait(&bars->pv_done[h][(nt - 1) & 1], ((nt - 1) >> 1) & 1)) {
