@@ -175,7 +175,10 @@ OMNI_API int64_t omni_linear_workspace_bytes(int64_t rows, int64_t k, int64_t n,
  *   splits: K-splits per 128-feature tile (one thread-block cluster each),
  *   0 = chosen by the library so that one wave covers the GPU, else 1..16
  *   (narrowed when a wide row tile exceeds shared memory or the grid's split
- *   partials exceed the scratch array).
+ *   partials exceed the scratch array).  With 0, a batch of more than 256 rows
+ *   with a (row tile, feature tile) pair for every SM runs a persistent
+ *   tile-loop kernel without split (store, residual and SwiGLU epilogues; the
+ *   same bits as one split).
  *   workspace / workspace_bytes: unused (may be NULL / 0). */
 OMNI_API int omni_linear(const void* x, int64_t rows, int64_t k, int64_t x_stride, const void* w, int64_t n,
                          int32_t epilogue, const void* residual, int64_t residual_stride, void* y, int64_t y_stride,
