@@ -1202,10 +1202,10 @@ int launch_gemm(const void* x, int64_t rows, int64_t k, int64_t x_stride, const 
   if (EPI == kEpiStore || EPI == kEpiResidual || EPI == kEpiSwiGLU) {
     const int tiles = (int)(EPI == kEpiSwiGLU ? (n / 2) / (kTileN / 2) : n / kTileN);
     // 256-row tiles once they give every SM a tile (38.7 k rows: down 1 023 -> 1 215,
-    // qkv (store epilogue) 1 002 -> 1 160, o 973 -> 1 034 TFLOP/s; gate_up 912 either
-    // way), else 128-row tiles
+    // qkv (store epilogue) 1 002 -> 1 160, o 973 -> 1 034 TFLOP/s), else 128-row tiles;
+    // SwiGLU keeps 128-row tiles (gate_up 937 against 913)
     if (rows > 256 && splits_req == 0) {
-      if ((int64_t)tiles * ((rows + 255) / 256) >= num_sms())
+      if (EPI != kEpiSwiGLU && (int64_t)tiles * ((rows + 255) / 256) >= num_sms())
         return launch_loop<EPI, 256>(x, rows, k, x_stride, w, n, gp, tiles, st);
       if ((int64_t)tiles * ((rows + 127) / 128) >= num_sms())
         return launch_loop<EPI, 128>(x, rows, k, x_stride, w, n, gp, tiles, st);
