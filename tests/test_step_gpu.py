@@ -240,3 +240,43 @@ def test_staged_requests_drive_the_layer0_draw():
     assert all(int(codes[i, 0]) not in masked[i] for i in range(B))
     assert not r.silence_rows.any()
     assert np.array_equal(t.suppress_mask[:B].cpu().numpy(), r.base_suppress[:B])
+
+
+@pytest.mark.parametrize("batch", [1, 3, 16])
+def test_pair_pass_matches_two_one_token_passes(batch):
+    """The predictor's opening two-token pass (rows (request, token), slots 0 and 1, causal)
+    against two one-token passes (slot 0, then slot 1 over the cached slot 0): the
+    residual stream of both tokens and the K/V of both slots within the bf16 GEMM rounding
+    tolerance the reference uses for the same check (atol 2^-6, rtol 2^-7;
+    test_predictor_cuda_graph.py:637-672)."""
+    import dataclasses
+
+    from omni_b200.config import CONFIG0_PREDICTOR
+    from omni_b200.predictor import CodePredictor, init_predictor_weights
+
+    dev = torch.device(DEV)
+    cfg = dataclasses.replace(CONFIG0_PREDICTOR, num_hidden_layers=2)
+    H, S = cfg.hidden_size, cfg.cache_len
+    w = init_predictor_weights(cfg, seed=batch, device=dev)
+    emb0 = torch.zeros(16, H, dtype=torch.bfloat16, device=dev)
+    pair = CodePredictor(cfg, w, max_batch=batch, device=dev, layer0_embedding=emb0)
+    serial = CodePredictor(cfg, w, max_batch=batch, device=dev, layer0_embedding=emb0)
+    g = torch.Generator(device=dev).manual_seed(batch)
+    embeds = torch.randn(batch, 2, H, generator=g, device=dev).to(torch.bfloat16)
+
+    def sumsq(x):
+        return x.float().pow(2).sum(-1).contiguous()
+
+    x2 = embeds.reshape(2 * batch, H).contiguous()
+    h_pair = pair.forward_tokens(x2, sumsq(x2), batch=batch, tokens=2, cache_len=0).clone()
+    x0 = embeds[:, 0].contiguous()
+    h0 = serial.forward_tokens(x0, sumsq(x0), batch=batch, tokens=1, cache_len=0).clone()
+    x1 = embeds[:, 1].contiguous()
+    h1 = serial.forward_tokens(x1, sumsq(x1), batch=batch, tokens=1, cache_len=1).clone()
+    torch.cuda.synchronize()
+    tol = dict(atol=2 ** -6, rtol=2 ** -7)
+    torch.testing.assert_close(h_pair.view(batch, 2, H)[:, 0].float(), h0.float(), **tol)
+    torch.testing.assert_close(h_pair.view(batch, 2, H)[:, 1].float(), h1.float(), **tol)
+    slots = (torch.arange(batch, device=dev)[:, None] * S + torch.arange(2, device=dev)[None, :]).reshape(-1)
+    for cache_p, cache_s in ((pair.k_cache, serial.k_cache), (pair.v_cache, serial.v_cache)):
+        torch.testing.assert_close(cache_p[:, slots].float(), cache_s[:, slots].float(), **tol)
