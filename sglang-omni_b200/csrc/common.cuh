@@ -79,6 +79,18 @@ OMNI_DEVINL uint32_t pack_bf2(float lo, float hi) {
   return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
 }
 
+// The same packing by integer round-to-nearest-even on the ALU, for FINITE
+// inputs only (a NaN is not kept quiet): bit-identical to pack_bf2 for every
+// finite value, subnormals included.  The softmax loops, whose special
+// function unit is already busy with ex2, pack P this way so that the
+// conversion leaves that unit.
+OMNI_DEVINL uint32_t pack_bf2_finite(float lo, float hi) {
+  uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
+  a += 0x7FFFu + ((a >> 16) & 1u);
+  b += 0x7FFFu + ((b >> 16) & 1u);
+  return __byte_perm(a, b, 0x7632);
+}
+
 // ---------------------------------------------------------------------------
 // Shared-memory / async-proxy primitives (PTX ISA 8.6+, sm_100a).
 // ---------------------------------------------------------------------------

@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
           mx = fmaxf(mx, fmaxf(a, b));
           const float pa = ex2_approx(a * sl - m_use), pb = ex2_approx(b * sl - m_use);
           rs += pa + pb;
-          pk[e >> 1] = pack_bf2(pa, pb);
+          pk[e >> 1] = pack_bf2_finite(pa, pb);
         }
         // keys hc*64 + c*32 .. + 31: 16-byte chunks c*4 .. c*4+3 of the row in half hc
 #pragma unroll
@@ -695,7 +695,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
           mx = fmaxf(mx, fmaxf(a, b));
           const float pa = ex2_approx(a * sl - m_use), pb = ex2_approx(b * sl - m_use);
           rs += pa + pb;
-          pk[c * 16 + (e >> 1)] = pack_bf2(pa, pb);
+          pk[c * 16 + (e >> 1)] = pack_bf2_finite(pa, pb);
         }
       }
       return rs;
