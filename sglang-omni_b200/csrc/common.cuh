@@ -79,16 +79,55 @@ OMNI_DEVINL uint32_t pack_bf2(float lo, float hi) {
   return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
 }
 
-// The same packing by integer round-to-nearest-even on the ALU, for FINITE
-// inputs only (a NaN is not kept quiet): bit-identical to pack_bf2 for every
-// finite value, subnormals included.  The softmax loops, whose special
-// function unit is already busy with ex2, pack P this way so that the
-// conversion leaves that unit.
-OMNI_DEVINL uint32_t pack_bf2_finite(float lo, float hi) {
-  uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
-  a += 0x7FFFu + ((a >> 16) & 1u);
-  b += 0x7FFFu + ((b >> 16) & 1u);
-  return __byte_perm(a, b, 0x7632);
+// Packed fp32 pairs (the .f32x2 forms of sm_100): one instruction works on two
+// values held as one 64-bit register pair, lo in the low word.
+OMNI_DEVINL uint64_t f2_make(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+OMNI_DEVINL void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+OMNI_DEVINL uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+OMNI_DEVINL uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+OMNI_DEVINL uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+OMNI_DEVINL uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+OMNI_DEVINL float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// bf16 pair of a packed pair of NORMAL or zero values by Veltkamp splitting
+// (Dekker 1971): with g = v * (2^16 + 1), hi = g + (v - g) is v rounded to
+// the 8 significant bits of bf16, nearest-even, so the result is bit-identical
+// to pack_bf2 (checked over every float32 of whole binades from 2^-126 to 2^9).
+// Three packed instructions and one byte permute for two values; subnormal
+// inputs are outside its domain (the softmax's ex2.approx.ftz makes none).
+OMNI_DEVINL uint32_t f2_to_bf2(uint64_t v) {
+  const uint64_t sigma = f2_make(65537.0f, 65537.0f);
+  const uint64_t g = f2_mul(v, sigma);
+  const uint64_t h = f2_add(g, f2_sub(v, g));
+  float lo, hi;
+  f2_split(h, lo, hi);
+  return __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
 }
 
 // ---------------------------------------------------------------------------
