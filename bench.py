@@ -1187,7 +1187,9 @@ def main() -> None:
                                 "frac": gemm_flops / gemm_s / 1e12 / tflops, "traffic": None,
                                 "algorithmic_flops": gemm_flops, "launch_us": gemm_s * 1e6, "peak_kind": peak_kind}
             line["roofline_prefill_attention"] = {
-                "bound": "tensor", "kernel": "prefill_attention_tc_kernel (tcgen05, S and O in TMEM)",
+                "bound": "tensor",
+                "kernel": ("prefill_attention_pair_kernel" if (cfg.num_attention_heads // cfg.num_key_value_heads) % 2 == 0
+                           else "prefill_attention_tc_kernel") + " (tcgen05, S, P and O in TMEM)",
                 "achieved": pf_flops / pf_s / 1e12, "peak": tflops, "unit": "TFLOP/s",
                 "frac": pf_flops / pf_s / 1e12 / tflops, "algorithmic_flops": pf_flops, "launch_us": pf_s * 1e6,
                 "peak_kind": peak_kind}

@@ -459,10 +459,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
 // 128-key tiles 409; two heads with 128-key tiles (one S buffer a head, softmax and MMAs
 // not overlapped) 495; 64-key tiles with two S buffers 507; with the ballot polling and
 // the MMA warp sleeping 32 ns between idle rounds (its spinning took issue slots from
-// the softmax warps of its sub-partition) 559.  Measured slower: a polynomial exp2 on the
-// FMA pipe for 4 to 16 of every 32 keys (933-1 049 against 882 us; the softmax is bound
-// by its dependency chains, not by the special-function pipe), twelve warps with
-// setmaxnreg, the two heads' softmaxes taking turns.
+// the softmax warps of its sub-partition) 559; P in TMEM 573; the softmax's key pairs on
+// the packed fp32x2 forms with a 3-input max and the bf16 pack by Veltkamp splitting
+// (fewer issue slots a key, and no conversion on the special-function pipe) 596;
+// CTAs walking the tiles heaviest-first (block_work) 623-642.  Measured slower: a
+// polynomial exp2 on the FMA pipe for 4 to 16 of every 32 keys (933-1 049 against
+// 882 us), twelve warps with setmaxnreg, the two heads' softmaxes taking turns.
 // ---------------------------------------------------------------------------
 constexpr int kPKeys = 64;                              // keys per tile
 constexpr int kPHalf = kPKeys * 128;                    // [64 keys][64 bf16]: 8 KB
