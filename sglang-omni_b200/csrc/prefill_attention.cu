@@ -451,7 +451,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
 //             thread: P = exp2(s * scale * log2 e - m) against the running max m in one
 //             pass, into the head's swizzled P buffer j & 1 (K-major A operand of P V);
 //             the first tile and a tile whose max passes m by more than 2^8 rescale O
-//             (after the head's previous P V) and the running sum and write P again.
+//             (after the head's previous P V) and the running sum and write P again --
+//             for the whole warp when any of its rows must (the tcgen05.ld / st are
+//             warp-collective; the other rows keep their max, alpha = 1); one arrival a
+//             warp on the head's barriers (128 arrivals a tile on one word had slowed
+//             the MMA warp's tests of it).  In the steady state the MMA warp issues
+//             P_0 V(i), then S_0(i + 2) interleaved with P_1 V(i), then S_1(i + 2): an S
+//             k-step alone wants more shared-memory bandwidth than the SM has.
 // Shared memory: Q 2 x 32 KB, K and V rings 3 x 16 KB each (160 KB); P stays in TMEM,
 // written by the softmax over the first 32 columns of the S buffer it has read and
 // read from there as the A operand of P V (the MMA warp issues P V(j) before S(j + 2)
@@ -462,9 +468,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
 // the softmax warps of its sub-partition) 559; P in TMEM 573; the softmax's key pairs on
 // the packed fp32x2 forms with a 3-input max and the bf16 pack by Veltkamp splitting
 // (fewer issue slots a key, and no conversion on the special-function pipe) 596;
-// CTAs walking the tiles heaviest-first (block_work) 623-642.  Measured slower: a
+// CTAs walking the tiles heaviest-first (block_work) 623-642; the interleaved steady-state
+// issue and one arrival a warp, 4.5 % on the kernel alone.  Measured slower: a
 // polynomial exp2 on the FMA pipe for 4 to 16 of every 32 keys (933-1 049 against
-// 882 us), twelve warps with setmaxnreg, the two heads' softmaxes taking turns.
+// 882 us; again with the packed forms, on the MMA warp's sub-partition only: 10-13 %
+// slower), twelve warps with setmaxnreg, the two heads' softmaxes taking turns, lane 0
+// waiting for its warp (14 % slower than every thread polling), the page table read
+// one tile ahead (no change).
 // ---------------------------------------------------------------------------
 constexpr int kPKeys = 64;                              // keys per tile
 constexpr int kPHalf = kPKeys * 128;                    // [64 keys][64 bf16]: 8 KB
@@ -546,8 +556,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
     for (int h = 0; h < 2; ++h)
       for (int b = 0; b < 2; ++b) {
         mbar_init(&bars->s_full[h][b], 1);
-        mbar_init(&bars->s_free[h][b], 4 * 32);
-        mbar_init(&bars->p_full[h][b], 4 * 32);
+        mbar_init(&bars->s_free[h][b], 4);  // one arrival per softmax warp of the head
+        mbar_init(&bars->p_full[h][b], 4);
         mbar_init(&bars->pv_done[h][b], 1);
       }
     mbar_init(&bars->drain, 1);
@@ -627,7 +637,54 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
       }
       const uint32_t m = __ballot_sync(0xFFFFFFFFu, c);
       bool progressed = false;
-      // P V first: it frees the V slot (and lets the head's softmax go on)
+      // Steady state (both heads' P(i) and V(i), K(i + 2) and both S buffers ready):
+      // P_0 V(i), then S_0(i + 2) with P_1 V(i) interleaved two k-steps to one, then
+      // S_1(i + 2).  An S k-step alone (N = 64) wants about 192 B/cycle of shared
+      // memory for its Q and K operands, more than the SM delivers; beside a P V
+      // k-step (V only) the pair averages about 125.  Each accumulator still sees its
+      // k-steps in order, so the results are the same bits as the one-by-one issue.
+      if (m == 0xFFu && ip[0] == ip[1] && jq[0] == ip[0] + 2 && jq[1] == ip[0] + 2) {
+        const int i = ip[0], j = i + 2, sv = i % kPSlots, sk = j % kPSlots;
+        tc_fence_after();
+        if (leader) {
+          const uint8_t* vt = smem + kPairVOff + sv * kPTile;
+          const uint8_t* kt = smem + kPairKOff + sk * kPTile;
+          auto pv_step = [&](int h, int k) {
+            const uint32_t pt = tbase + h * 128 + (i & 1) * kPKeys;
+            tc_mma_bf16_ts(tbase + 256 + h * 128, pt + k * 8, desc_mn_sw128_64(vt + k * 16 * 128), idesc_pv,
+                           (i > 0 || k > 0) ? 1u : 0u);
+          };
+          auto s_step = [&](int h, int k) {
+            const uint8_t* qt = smem + kPairQOff + h * kTileBytes;
+            const uint64_t ad = smem_desc_sw128(qt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
+            const uint64_t bd = smem_desc_sw128(kt + (k >> 2) * kPHalf) + 2 * (k & 3);
+            tc_mma_bf16(tbase + h * 128 + (j & 1) * kPKeys, ad, bd, idesc_qk, k > 0 ? 1u : 0u);
+          };
+#pragma unroll
+          for (int k = 0; k < 4; ++k) pv_step(0, k);
+          tc_commit(&bars->pv_done[0][i & 1]);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            s_step(0, 2 * k);
+            s_step(0, 2 * k + 1);
+            pv_step(1, k);
+          }
+          tc_commit(&bars->pv_done[1][i & 1]);
+          tc_commit(&bars->v_empty[sv]);
+          tc_commit(&bars->s_full[0][j & 1]);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) s_step(1, k);
+          tc_commit(&bars->s_full[1][j & 1]);
+          tc_commit(&bars->k_empty[sk]);
+        }
+        __syncwarp();
+        ip[0] = ip[1] = i + 1;
+        jq[0] = jq[1] = j + 1;
+        idle = 0;
+        continue;
+      }
+      // otherwise one by one, P V first: it frees the V slot (and lets the head's
+      // softmax go on)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int i = ip[h];
@@ -735,21 +792,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
     };
     for (int j = 0; j < nt && ok; ++j) {
       const int b = j & 1;
-      if (!mbar_wait(&bars->s_full[h][b], (j >> 1) & 1)) {
+      // (every branch of this loop is warp-uniform: the tcgen05.ld / st below are
+      // warp-collective)
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->s_full[h][b], (j >> 1) & 1))) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t tS = tbase + lane_off + h * 128 + b * kPKeys;
       // P buffer b held tile j - 2: free once that P V has completed
-      if (j >= 2 && !mbar_wait(&bars->pv_done[h][b], ((j - 2) >> 1) & 1)) {
+      if (j >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars->pv_done[h][b], ((j - 2) >> 1) & 1))) {
         ok = false;
         break;
       }
       const bool masked = j * kPKeys + kPKeys - 1 > prefix + q0;
       float mx, rs = 0.0f;
       uint32_t pk[32];
-      if (m_use == -INFINITY) {
+      if (j == 0) {  // m_use is -inf on every row until tile 0 (key 0 is visible to all rows)
 #pragma unroll
         for (int e = 0; e < 32; ++e) pk[e] = 0u;  // a tile with no visible key leaves P zero
         mx = -INFINITY;
@@ -767,11 +826,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
         rs = compute_p(tS, j, masked, mx, pk);
       }
       const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl;
-      if (m_tile != -INFINITY && (m_use == -INFINITY || m_tile > m_use + kRescaleLog2)) {
-        const float alpha = m_use == -INFINITY ? 0.0f : ex2_approx(m_use - m_tile);
-        if (j > 0 && l > 0.0f) {
+      const bool resc = m_tile != -INFINITY && (m_use == -INFINITY || m_tile > m_use + kRescaleLog2);
+      // the warp rescales if any of its rows must (the others with alpha = 1 and their
+      // running max kept, which rewrites the same P)
+      if (__any_sync(0xFFFFFFFFu, resc)) {
+        const float alpha = !resc ? 1.0f : m_use == -INFINITY ? 0.0f : ex2_approx(m_use - m_tile);
+        if (__any_sync(0xFFFFFFFFu, resc && j > 0 && l > 0.0f)) {
           // O holds tiles < j once the head's P V of tile j - 1 has completed
-          if (!mbar_wait(&bars->pv_done[h][(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+          if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->pv_done[h][(j - 1) & 1], ((j - 1) >> 1) & 1))) {
             ok = false;
             break;
           }
@@ -788,7 +850,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
           tc_wait_st();
         }
         l *= alpha;
-        m_use = m_tile;
+        if (resc) m_use = m_tile;
         float unused;
         rs = compute_p(tS, j, masked, unused, pk);
       }
@@ -797,10 +859,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
       tmem_st_32x32b_x32(tS, pk);
       tc_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars->s_free[h][b]);
-      mbar_arrive(&bars->p_full[h][b]);
+      __syncwarp();
+      if (lane == 0) {  // one arrival a warp
+        mbar_arrive(&bars->s_free[h][b]);
+        mbar_arrive(&bars->p_full[h][b]);
+      }
     }
-    if (ok && nt > 0 && mbar_wait(&bars->pv_done[h][(nt - 1) & 1], ((nt - 1) >> 1) & 1)) {
+    if (ok && nt > 0 && __all_sync(0xFFFFFFFFu, mbar_wait(&bars->pv_done[h][(nt - 1) & 1], ((nt - 1) >> 1) & 1))) {
       tc_fence_after();
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       uint16_t* orow = p.out + (int64_t)(qs0 + q0 + r) * p.out_stride + (int64_t)(h0 + h) * kD;
