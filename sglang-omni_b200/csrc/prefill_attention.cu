@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       mbar_arrive(&bars->pair[q]);
-      if (!mbar_wait(&bars->pair[q], pair_phase & 1)) ok = false;
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->pair[q], pair_phase & 1))) ok = false;
       ++pair_phase;
       tc_fence_after();
       uint32_t o1;
@@ -335,14 +335,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
     };
     for (int j = 0; j < nt && ok; ++j) {
       const int s = j & 1;
-      if (!mbar_wait(&bars->s_full[s], (j >> 1) & 1)) {
+      // (every branch of this loop is warp-uniform: the tcgen05.ld / st are
+      // warp-collective)
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->s_full[s], (j >> 1) & 1))) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t ts = tbase + lane_off + s * 128 + hc * 64;
       // the P buffer of tile j - 2 is free once its P V has completed
-      if (j >= 2 && !mbar_wait(&bars->pv_done[s], ((j - 2) >> 1) & 1)) {
+      if (j >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars->pv_done[s], ((j - 2) >> 1) & 1))) {
         ok = false;
         break;
       }
@@ -353,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
       // one pass against the running max; the rare tile whose max passes it by more
       // than 2^8 (and the first tile) rescales O and the sum and writes P again
       float rs = 0.0f;
-      if (m_use == -INFINITY) {
+      if (j == 0) {  // m_use is -inf on every row until tile 0 (key 0 is visible to all rows)
         mx = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
@@ -371,11 +373,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
       mx = fmaxf(mx, swap(mx, j & 1));  // the row's max over both halves
       if (!ok) break;
       const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl;
-      if (m_tile != -INFINITY && (m_use == -INFINITY || m_tile > m_use + kRescaleLog2)) {
-        const float alpha = m_use == -INFINITY ? 0.0f : ex2_approx(m_use - m_tile);
-        if (j > 0 && l > 0.0f) {
+      const bool resc = m_tile != -INFINITY && (m_use == -INFINITY || m_tile > m_use + kRescaleLog2);
+      // the warp rescales if any of its rows must (the others with alpha = 1 and their
+      // running max kept, which rewrites the same P); both threads of a row scale their
+      // O columns, whatever their own half of the sum
+      if (__any_sync(0xFFFFFFFFu, resc)) {
+        const float alpha = !resc ? 1.0f : m_use == -INFINITY ? 0.0f : ex2_approx(m_use - m_tile);
+        if (j > 0) {
           // O holds tiles < j once the previous P V has completed
-          if (!mbar_wait(&bars->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+          if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1))) {
             ok = false;
             break;
           }
@@ -392,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
           tc_wait_st();
         }
         l *= alpha;
-        m_use = m_tile;
+        if (resc) m_use = m_tile;
         float unused;
         rs = write_p(ts, phalf, j, masked, unused);
       }
@@ -403,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
       mbar_arrive(&bars->p_full[s]);
     }
     const float l_row = ok ? l + swap(l, 2) : 0.0f;
-    if (ok && nt > 0 && mbar_wait(&bars->pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1)) {
+    if (ok && nt > 0 && __all_sync(0xFFFFFFFFu, mbar_wait(&bars->pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1))) {
       tc_fence_after();
       const float inv = l_row > 0.0f ? 1.0f / l_row : 0.0f;
       uint16_t* orow = p.out + (int64_t)(qs0 + q0 + r) * p.out_stride + (int64_t)hh * kD + hc * 64;

@@ -84,10 +84,17 @@ def test_extend_prepare_matches_oracle():
 LONG_STREAMS = [(0, 4096), (0, 2048), (0, 3001), (300, 2500), (0, 64), (4000, 96)]
 
 
-@pytest.mark.parametrize("hq,hkv,streams", [(16, 2, STREAMS), (8, 4, STREAMS), (12, 4, STREAMS), (8, 8, STREAMS),
-                                             (16, 2, LONG_STREAMS)],
-                         ids=["gqa8-pairs", "gqa2-pairs", "gqa3-single", "mha-single", "long-prompts"])
-def test_prefill_attention_matches_fp32(hq, hkv, streams):
+@pytest.mark.parametrize("hq,hkv,streams,spike", [(16, 2, STREAMS, False), (8, 4, STREAMS, False),
+                                                   (12, 4, STREAMS, False), (8, 8, STREAMS, False),
+                                                   (16, 2, LONG_STREAMS, False), (16, 2, LONG_STREAMS, True),
+                                                   (12, 4, LONG_STREAMS, True)],
+                         ids=["gqa8-pairs", "gqa2-pairs", "gqa3-single", "mha-single", "long-prompts",
+                              "rescale-split-pairs", "rescale-split-single"])
+def test_prefill_attention_matches_fp32(hq, hkv, streams, spike):
+    """spike: the key at position 300 of every stream gets +40 in dimension 0 and every
+    query row +-4 there (random sign), so the rows with + see their running max jump by
+    about 20 (log2 units, past the 2^8 rescale threshold) at that key while the rows
+    beside them in the same warp do not: the rescale runs for part of a warp."""
     from omni_b200 import ops
 
     STREAMS_ = streams
@@ -99,6 +106,12 @@ def test_prefill_attention_matches_fp32(hq, hkv, streams):
     vc = torch.randn(num_pages * P, hkv, D, generator=g, device=DEV).to(torch.bfloat16)
     total = sum(s[1] for s in STREAMS_)
     q = torch.randn(total, hq * D, generator=g, device=DEV).to(torch.bfloat16)
+    if spike:
+        sign = torch.randint(0, 2, (total, hq), generator=g, device=DEV).to(torch.bfloat16) * 2 - 1
+        q.view(total, hq, D)[:, :, 0] = 4 * sign
+        for i, (pre, ext) in enumerate(STREAMS_):
+            if pre + ext > 300:
+                kc[int(r2t[req[i], 300]), :, 0] = 40.0
     out = torch.full((total, hq * D), float("nan"), device=DEV, dtype=torch.bfloat16)
     max_tiles = sum(math.ceil(s[1] / ops.PREFILL_Q_TILE) for s in STREAMS_)
     scale = 1 / math.sqrt(D)
