@@ -439,48 +439,48 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
 
 // ---------------------------------------------------------------------------
 // GQA pair kernel: CTA = 128 queries of one stream x two query heads of one KV
-// head, so each K / V tile is loaded once for both heads.  Keys go by in tiles of 64
-// (4 pages), so that each head has two S buffers in TMEM (2 heads x 2 x 64 columns,
-// and the two O accumulators of 128 columns: 512): the tensor core computes S(j + 1)
-// and P V(j - 1) while the softmax warps work on tile j.  Ten warps:
+// head, so each K / V tile is loaded once for both heads; keys go by in tiles of 64
+// (4 pages).  TMEM (512 columns): each head's Q (64 columns, bf16 pairs), its S
+// buffer (64), its O accumulator (128).  Q sits in TMEM as the A operand of S, so an S
+// k-step reads only K from shared memory: with Q from shared memory as well, the
+// operands of an N = 64 S k-step wanted about 192 B/cycle and the MMAs, not the
+// softmax, set the pace (an MMA warp blocked in issue for most of each round).  With
+// one S buffer a head the heads take turns on the tensor core: the head-1 softmax runs
+// on S_1(j) while the tensor core does P_0 V(j) and S_0(j + 1), and the other way round.
+// Ten warps:
 //   warp 0    TMA producer: both heads' Q tiles once; per key tile the 4 pages of K
 //             and of V (one 16-row x 64-column box per lane) into three-slot K and V
 //             rings;
-//   warp 1    MMA issuer: S_h(j) = Q_h K_j^T into S buffer j & 1 of head h once K_j
-//             has landed and the head's softmax has released that buffer (tile j - 2);
-//             O_h += P_h(j) V_j once P_h(j) is written and V_j has landed.  Eight lanes
-//             test the eight barriers a round depends on at once (non-blocking
-//             test_wait) and one ballot gathers them: polling them one after another
-//             left 500-1 000 cycles between MMA groups;
-//   warps 2-5 softmax of head 0, warps 6-9 of head 1: one thread per query row (TMEM
-//             lane) over the tile's 64 columns, so a row's max and sum stay in one
+//   warp 1    MMA issuer, in a fixed order: S_0(0), S_1(0), then per tile i
+//             P_0 V(i), S_0(i + 1), P_1 V(i), S_1(i + 1); each P V once the head's
+//             softmax has written P(i) and V(i) has landed, each S once K(i + 1) has;
+//             P_h(i) sits over the first 32 of the head's S columns, and S_h(i + 1) is
+//             issued after P_h V(i), which reads it first (MMAs execute in order);
+//   warps 2-5 softmax of head 0, warps 6-9 of head 1: first copy their row of Q from
+//             the swizzled shared tile into TMEM; then per tile one thread per query
+//             row (TMEM lane) over the 64 columns, so a row's max and sum stay in one
 //             thread: P = exp2(s * scale * log2 e - m) against the running max m in one
-//             pass, into the head's swizzled P buffer j & 1 (K-major A operand of P V);
-//             the first tile and a tile whose max passes m by more than 2^8 rescale O
-//             (after the head's previous P V) and the running sum and write P again --
-//             for the whole warp when any of its rows must (the tcgen05.ld / st are
-//             warp-collective; the other rows keep their max, alpha = 1); one arrival a
-//             warp on the head's barriers (128 arrivals a tile on one word had slowed
-//             the MMA warp's tests of it).  In the steady state the MMA warp issues
-//             P_0 V(i), then S_0(i + 2) interleaved with P_1 V(i), then S_1(i + 2): an S
-//             k-step alone wants more shared-memory bandwidth than the SM has.
-// Shared memory: Q 2 x 32 KB, K and V rings 3 x 16 KB each (160 KB); P stays in TMEM,
-// written by the softmax over the first 32 columns of the S buffer it has read and
-// read from there as the A operand of P V (the MMA warp issues P V(j) before S(j + 2)
-// into the same buffer).  History at config 2 (TFLOP/s of causal QK^T + PV): one head a CTA with
+//             pass; the first tile and a tile whose max passes m by more than 2^8
+//             rescale O and the running sum and write P again -- for the whole warp when
+//             any of its rows must (the tcgen05.ld / st are warp-collective; the other
+//             rows keep their max, alpha = 1).  The completion of S_h(j) covers every
+//             MMA issued before it, P_h V(j - 1) included, so the softmax never waits
+//             for P V inside the loop.  One barrier arrival a warp.
+// Shared memory: Q 2 x 32 KB (read once into TMEM), K and V rings 3 x 16 KB each
+// (160 KB).  History at config 2 (TFLOP/s of causal QK^T + PV): one head a CTA with
 // 128-key tiles 409; two heads with 128-key tiles (one S buffer a head, softmax and MMAs
-// not overlapped) 495; 64-key tiles with two S buffers 507; with the ballot polling and
-// the MMA warp sleeping 32 ns between idle rounds (its spinning took issue slots from
-// the softmax warps of its sub-partition) 559; P in TMEM 573; the softmax's key pairs on
-// the packed fp32x2 forms with a 3-input max and the bf16 pack by Veltkamp splitting
-// (fewer issue slots a key, and no conversion on the special-function pipe) 596;
-// CTAs walking the tiles heaviest-first (block_work) 623-642; the interleaved steady-state
-// issue and one arrival a warp, 4.5 % on the kernel alone.  Measured slower: a
-// polynomial exp2 on the FMA pipe for 4 to 16 of every 32 keys (933-1 049 against
-// 882 us; again with the packed forms, on the MMA warp's sub-partition only: 10-13 %
-// slower), twelve warps with setmaxnreg, the two heads' softmaxes taking turns, lane 0
+// not overlapped) 495; 64-key tiles with two S buffers a head and Q in shared memory
+// 507; the MMA warp polling eight barriers in one ballot and sleeping between idle
+// rounds 559; P in TMEM 573; the softmax's key pairs on the packed fp32x2 forms with a
+// 3-input max and the bf16 pack by Veltkamp splitting 596; CTAs walking the tiles
+// heaviest-first (block_work) 623-642; the second head's P V interleaved with the first
+// head's S and one arrival a warp 633-672; Q in TMEM with the heads taking turns
+// (this layout) 697.  Measured slower: a polynomial exp2 on the FMA pipe for 4 to 16 of
+// every 32 keys (933-1 049 against 882 us; again with the packed forms, on the MMA
+// warp's sub-partition only: 10-13 % slower), twelve warps with setmaxnreg, lane 0
 // waiting for its warp (14 % slower than every thread polling), the page table read
-// one tile ahead (no change).
+// one tile ahead (no change), the MMA warp testing four barriers with one lane instead
+// of eight with eight (no change).
 // ---------------------------------------------------------------------------
 constexpr int kPKeys = 64;                              // keys per tile
 constexpr int kPHalf = kPKeys * 128;                    // [64 keys][64 bf16]: 8 KB
@@ -504,8 +504,8 @@ OMNI_DEVINL void tc_mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc
 }
 
 struct PairBars {
-  uint64_t q_full, k_full[kPSlots], k_empty[kPSlots], v_full[kPSlots], v_empty[kPSlots];
-  uint64_t s_full[2][2], s_free[2][2], p_full[2][2], pv_done[2][2], drain;
+  uint64_t q_full, q_tmem, k_full[kPSlots], k_empty[kPSlots], v_full[kPSlots], v_empty[kPSlots];
+  uint64_t s_full[2], p_full[2], pv_done[2], drain;
   uint32_t tmem;
 };
 
@@ -553,19 +553,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
+    mbar_init(&bars->q_tmem, 8);  // one arrival per softmax warp
     for (int i = 0; i < kPSlots; ++i) {
       mbar_init(&bars->k_full[i], 1);
       mbar_init(&bars->k_empty[i], 1);
       mbar_init(&bars->v_full[i], 1);
       mbar_init(&bars->v_empty[i], 1);
     }
-    for (int h = 0; h < 2; ++h)
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(&bars->s_full[h][b], 1);
-        mbar_init(&bars->s_free[h][b], 4);  // one arrival per softmax warp of the head
-        mbar_init(&bars->p_full[h][b], 4);
-        mbar_init(&bars->pv_done[h][b], 1);
-      }
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&bars->s_full[h], 1);
+      mbar_init(&bars->p_full[h], 4);  // one arrival per softmax warp of the head
+      mbar_init(&bars->pv_done[h], 1);
+    }
     mbar_init(&bars->drain, 1);
     fence_barrier_init();
   }
@@ -615,136 +614,64 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
       load_tile(&tv, smem + kPairVOff + s * kPTile, &bars->v_full[s], j);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer: P_0 V(i), S_0(i + 1), P_1 V(i), S_1(i + 1), ... ----------------
     const bool leader = elect_one();
     const uint32_t idesc_qk = idesc_bf16_f32(kRows, kPKeys);
     const uint32_t idesc_pv = idesc_bf16_f32(kRows, kD) | (1u << 16);  // B MN-major
-    bool ok = mbar_wait(&bars->q_full, 0);
-    int jq[2] = {0, 0}, ip[2] = {0, 0};
-    uint32_t idle = 0;
-    while (ok && (ip[0] < nt || ip[1] < nt)) {
-      // lanes 0-7 test the eight barriers this round can act on at once (one ballot
-      // instead of eight polls in turn): lane 2h / 2h+1: head h's P and V of tile
-      // ip[h]; lane 4+2h / 5+2h: K of tile jq[h] and head h's S buffer
-      bool c = false;
-      if (lane < 8) {
-        const int h = (lane >> 1) & 1;
-        if (lane < 4) {
-          const int i = ip[h];
-          if (i < jq[h])
-            c = (lane & 1) ? mbar_test_wait(&bars->v_full[i % kPSlots], (i / kPSlots) & 1)
-                           : mbar_test_wait(&bars->p_full[h][i & 1], (i >> 1) & 1);
-        } else {
-          const int j = jq[h];
-          if (j < nt)
-            c = (lane & 1) ? (j < 2 || mbar_test_wait(&bars->s_free[h][j & 1], ((j - 2) >> 1) & 1))
-                           : mbar_test_wait(&bars->k_full[j % kPSlots], (j / kPSlots) & 1);
+    // S_h(j) = Q_h K_j^T: A = head h's Q from TMEM (columns h * 64, 8 a k-step of 16
+    // dimensions), B = K_j from shared memory, into head h's S columns 128 + h * 64
+    auto issue_s = [&](int h, int j) {
+      const int s = j % kPSlots;
+      const uint8_t* kt = smem + kPairKOff + s * kPTile;
+      if (leader) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint64_t bd = smem_desc_sw128(kt + (k >> 2) * kPHalf) + 2 * (k & 3);
+          tc_mma_bf16_ts(tbase + 128 + h * 64, tbase + h * 64 + k * 8, bd, idesc_qk, k > 0 ? 1u : 0u);
         }
+        tc_commit(&bars->s_full[h]);
+        if (h == 1) tc_commit(&bars->k_empty[s]);  // both heads' S of tile j
       }
-      const uint32_t m = __ballot_sync(0xFFFFFFFFu, c);
-      bool progressed = false;
-      // Steady state (both heads' P(i) and V(i), K(i + 2) and both S buffers ready):
-      // P_0 V(i), then S_0(i + 2) with P_1 V(i) interleaved two k-steps to one, then
-      // S_1(i + 2).  An S k-step alone (N = 64) wants about 192 B/cycle of shared
-      // memory for its Q and K operands, more than the SM delivers; beside a P V
-      // k-step (V only) the pair averages about 125.  Each accumulator still sees its
-      // k-steps in order, so the results are the same bits as the one-by-one issue.
-      if (m == 0xFFu && ip[0] == ip[1] && jq[0] == ip[0] + 2 && jq[1] == ip[0] + 2) {
-        const int i = ip[0], j = i + 2, sv = i % kPSlots, sk = j % kPSlots;
+      __syncwarp();
+    };
+    // O_h += P_h(i) V_i: A = P_h(i) over the first 32 of the head's S columns
+    auto issue_pv = [&](int h, int i) {
+      const int s = i % kPSlots;
+      const uint8_t* vt = smem + kPairVOff + s * kPTile;
+      if (leader) {
+#pragma unroll
+        for (int k = 0; k < kPKeys / 16; ++k)
+          tc_mma_bf16_ts(tbase + 256 + h * 128, tbase + 128 + h * 64 + k * 8, desc_mn_sw128_64(vt + k * 16 * 128),
+                         idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+        if (i == nt - 1) tc_commit(&bars->pv_done[h]);
+        if (h == 1) tc_commit(&bars->v_empty[s]);  // both heads' P V of tile i
+      }
+      __syncwarp();
+    };
+    bool ok = mbar_wait(&bars->q_tmem, 0) && (nt == 0 || mbar_wait(&bars->k_full[0], 0));
+    if (ok && nt > 0) {
+      tc_fence_after();
+      issue_s(0, 0);
+      issue_s(1, 0);
+    }
+    for (int i = 0; i < nt && ok; ++i) {
+      for (int h = 0; h < 2; ++h) {
+        // P_h(i) written (S_h(i) read) by the head's four softmax warps
+        if (!mbar_wait(&bars->p_full[h], i & 1) ||
+            (h == 0 && !mbar_wait(&bars->v_full[i % kPSlots], (i / kPSlots) & 1))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        if (leader) {
-          const uint8_t* vt = smem + kPairVOff + sv * kPTile;
-          const uint8_t* kt = smem + kPairKOff + sk * kPTile;
-          auto pv_step = [&](int h, int k) {
-            const uint32_t pt = tbase + h * 128 + (i & 1) * kPKeys;
-            tc_mma_bf16_ts(tbase + 256 + h * 128, pt + k * 8, desc_mn_sw128_64(vt + k * 16 * 128), idesc_pv,
-                           (i > 0 || k > 0) ? 1u : 0u);
-          };
-          auto s_step = [&](int h, int k) {
-            const uint8_t* qt = smem + kPairQOff + h * kTileBytes;
-            const uint64_t ad = smem_desc_sw128(qt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
-            const uint64_t bd = smem_desc_sw128(kt + (k >> 2) * kPHalf) + 2 * (k & 3);
-            tc_mma_bf16(tbase + h * 128 + (j & 1) * kPKeys, ad, bd, idesc_qk, k > 0 ? 1u : 0u);
-          };
-#pragma unroll
-          for (int k = 0; k < 4; ++k) pv_step(0, k);
-          tc_commit(&bars->pv_done[0][i & 1]);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            s_step(0, 2 * k);
-            s_step(0, 2 * k + 1);
-            pv_step(1, k);
+        issue_pv(h, i);
+        if (i + 1 < nt) {
+          if (h == 0 && !mbar_wait(&bars->k_full[(i + 1) % kPSlots], ((i + 1) / kPSlots) & 1)) {
+            ok = false;
+            break;
           }
-          tc_commit(&bars->pv_done[1][i & 1]);
-          tc_commit(&bars->v_empty[sv]);
-          tc_commit(&bars->s_full[0][j & 1]);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) s_step(1, k);
-          tc_commit(&bars->s_full[1][j & 1]);
-          tc_commit(&bars->k_empty[sk]);
+          // after P_h V(i) in issue order, so P_h(i) is read before S_h(i + 1) overwrites it
+          issue_s(h, i + 1);
         }
-        __syncwarp();
-        ip[0] = ip[1] = i + 1;
-        jq[0] = jq[1] = j + 1;
-        idle = 0;
-        continue;
-      }
-      // otherwise one by one, P V first: it frees the V slot (and lets the head's
-      // softmax go on)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int i = ip[h];
-        const int s = i % kPSlots;
-        if (((m >> (2 * h)) & 3u) == 3u) {
-          tc_fence_after();
-          if (leader) {
-            // P_h(i) sits in the first 32 columns of head h's S buffer i & 1 (16 keys a
-            // k-step: 8 columns)
-            const uint32_t pt = tbase + h * 128 + (i & 1) * kPKeys;
-            const uint8_t* vt = smem + kPairVOff + s * kPTile;
-#pragma unroll
-            for (int k = 0; k < kPKeys / 16; ++k) {
-              const uint64_t bd = desc_mn_sw128_64(vt + k * 16 * 128);
-              tc_mma_bf16_ts(tbase + 256 + h * 128, pt + k * 8, bd, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
-            }
-            tc_commit(&bars->pv_done[h][i & 1]);
-            if (ip[h ^ 1] > i) tc_commit(&bars->v_empty[s]);  // both heads' P V of tile i
-          }
-          __syncwarp();
-          ++ip[h];
-          progressed = true;
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int j = jq[h];
-        const int s = j % kPSlots;
-        // S_h(j) into buffer j & 1, one tile ahead of the head's P V at most
-        if (((m >> (4 + 2 * h)) & 3u) == 3u && j <= ip[h] + 1) {
-          tc_fence_after();
-          if (leader) {
-            const uint8_t* qt = smem + kPairQOff + h * kTileBytes;
-            const uint8_t* kt = smem + kPairKOff + s * kPTile;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint64_t ad = smem_desc_sw128(qt + (k >> 2) * kHalfBytes) + 2 * (k & 3);
-              const uint64_t bd = smem_desc_sw128(kt + (k >> 2) * kPHalf) + 2 * (k & 3);
-              tc_mma_bf16(tbase + h * 128 + (j & 1) * kPKeys, ad, bd, idesc_qk, k > 0 ? 1u : 0u);
-            }
-            tc_commit(&bars->s_full[h][j & 1]);
-            if (jq[h ^ 1] > j) tc_commit(&bars->k_empty[s]);  // both heads' S of tile j
-          }
-          __syncwarp();
-          ++jq[h];
-          progressed = true;
-        }
-      }
-      if (progressed) {
-        idle = 0;
-      } else {
-        // leave the issue slots of this sub-partition to the softmax warps beside it
-        __nanosleep(32);
-        if (++idle > 4 * kWaitLimit) ok = false;
       }
     }
     if (!ok) report_status(kDevTimeoutMma);
@@ -757,11 +684,35 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
     const int q = warp & 3;                 // TMEM lane quarter of this warp
     const int r = q * 32 + lane;            // query row of the tile
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const uint32_t tQ = tbase + lane_off + h * 64;
+    const uint32_t tS = tbase + lane_off + 128 + h * 64;
     const uint32_t tO = tbase + lane_off + 256 + h * 128;
     const int lim = prefix + q0 + r;        // last key this query sees
     const float sl = p.scale_log2;
     float m_use = -INFINITY, l = 0.0f;
-    bool ok = true;
+    // this row's Q (bf16 pairs, the dimensions in order) from the swizzled shared tile
+    // into the head's Q columns of TMEM, the A operand of every S
+    bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(&bars->q_full, 0));
+    if (ok) {
+      const uint8_t* qrow = smem + kPairQOff + h * kTileBytes + r * 128;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t v[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 x = *reinterpret_cast<const uint4*>(qrow + hf * kHalfBytes + ((c ^ (r & 7)) << 4));
+          v[4 * c] = x.x;
+          v[4 * c + 1] = x.y;
+          v[4 * c + 2] = x.z;
+          v[4 * c + 3] = x.w;
+        }
+        tmem_st_32x32b_x32(tQ + hf * 32, v);
+      }
+      tc_wait_st();
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars->q_tmem);
     // P = exp2(s * scale - m_use) of the row's 64 keys of tile j into pk (bf16 pairs,
     // masked keys 0); returns their sum and the raw max score
     // Key pairs go through the packed fp32x2 forms: one FMA for both arguments,
@@ -797,20 +748,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
       return ra + rb;
     };
     for (int j = 0; j < nt && ok; ++j) {
-      const int b = j & 1;
       // (every branch of this loop is warp-uniform: the tcgen05.ld / st below are
       // warp-collective)
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->s_full[h][b], (j >> 1) & 1))) {
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->s_full[h], j & 1))) {
         ok = false;
         break;
       }
+      // S_h(j) has completed, and with it every MMA issued before it: the head's
+      // P V(j - 1) too, so O holds tiles < j and P(j - 1) has been read
       tc_fence_after();
-      const uint32_t tS = tbase + lane_off + h * 128 + b * kPKeys;
-      // P buffer b held tile j - 2: free once that P V has completed
-      if (j >= 2 && !__all_sync(0xFFFFFFFFu, mbar_wait(&bars->pv_done[h][b], ((j - 2) >> 1) & 1))) {
-        ok = false;
-        break;
-      }
       const bool masked = j * kPKeys + kPKeys - 1 > prefix + q0;
       float mx, rs = 0.0f;
       uint32_t pk[32];
@@ -838,12 +784,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
       if (__any_sync(0xFFFFFFFFu, resc)) {
         const float alpha = !resc ? 1.0f : m_use == -INFINITY ? 0.0f : ex2_approx(m_use - m_tile);
         if (__any_sync(0xFFFFFFFFu, resc && j > 0 && l > 0.0f)) {
-          // O holds tiles < j once the head's P V of tile j - 1 has completed
-          if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->pv_done[h][(j - 1) & 1], ((j - 1) >> 1) & 1))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t v[32];
@@ -861,17 +801,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
         rs = compute_p(tS, j, masked, unused, pk);
       }
       l += rs;
-      // P over the S columns this thread has read (the buffer's first 32 columns)
+      // P over the S columns this thread has read (their first 32)
       tmem_st_32x32b_x32(tS, pk);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {  // one arrival a warp
-        mbar_arrive(&bars->s_free[h][b]);
-        mbar_arrive(&bars->p_full[h][b]);
-      }
+      if (lane == 0) mbar_arrive(&bars->p_full[h]);  // one arrival a warp
     }
-    if (ok && nt > 0 && __all_sync(0xFFFFFFFFu, mbar_wait(&bars->pv_done[h][(nt - 1) & 1], ((nt - 1) >> 1) & 1))) {
+    if (ok && nt > 0 && __all_sync(0xFFFFFFFFu, mbar_wait(&bars->pv_done[h], 0))) {
       tc_fence_after();
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       uint16_t* orow = p.out + (int64_t)(qs0 + q0 + r) * p.out_stride + (int64_t)(h0 + h) * kD;
