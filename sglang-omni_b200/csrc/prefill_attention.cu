@@ -620,15 +620,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
     const uint32_t idesc_pv = idesc_bf16_f32(kRows, kD) | (1u << 16);  // B MN-major
     // S_h(j) = Q_h K_j^T: A = head h's Q from TMEM (columns h * 64, 8 a k-step of 16
     // dimensions), B = K_j from shared memory, into head h's S columns 128 + h * 64
+    // (descriptors from one base a tile plus constant offsets, computed by the whole
+    // warp: the elected lane only issues)
     auto issue_s = [&](int h, int j) {
       const int s = j % kPSlots;
-      const uint8_t* kt = smem + kPairKOff + s * kPTile;
+      const uint64_t kd = smem_desc_sw128(smem + kPairKOff + s * kPTile);
+      const uint32_t ta = tbase + h * 64, td = tbase + 128 + h * 64;
       if (leader) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint64_t bd = smem_desc_sw128(kt + (k >> 2) * kPHalf) + 2 * (k & 3);
-          tc_mma_bf16_ts(tbase + 128 + h * 64, tbase + h * 64 + k * 8, bd, idesc_qk, k > 0 ? 1u : 0u);
-        }
+        for (int k = 0; k < 8; ++k)
+          tc_mma_bf16_ts(td, ta + k * 8, kd + (uint64_t)(((k >> 2) * kPHalf) >> 4) + 2 * (k & 3), idesc_qk,
+                         k > 0 ? 1u : 0u);
         tc_commit(&bars->s_full[h]);
         if (h == 1) tc_commit(&bars->k_empty[s]);  // both heads' S of tile j
       }
@@ -637,12 +639,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
     // O_h += P_h(i) V_i: A = P_h(i) over the first 32 of the head's S columns
     auto issue_pv = [&](int h, int i) {
       const int s = i % kPSlots;
-      const uint8_t* vt = smem + kPairVOff + s * kPTile;
+      const uint64_t vd = desc_mn_sw128_64(smem + kPairVOff + s * kPTile);
+      const uint32_t ta = tbase + 128 + h * 64, td = tbase + 256 + h * 128;
       if (leader) {
 #pragma unroll
-        for (int k = 0; k < kPKeys / 16; ++k)
-          tc_mma_bf16_ts(tbase + 256 + h * 128, tbase + 128 + h * 64 + k * 8, desc_mn_sw128_64(vt + k * 16 * 128),
-                         idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < kPKeys / 16; ++k)  // 16 keys a k-step: 16 rows of V, 2 KB on
+          tc_mma_bf16_ts(td, ta + k * 8, vd + (uint64_t)((k * 16 * 128) >> 4), idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
         if (i == nt - 1) tc_commit(&bars->pv_done[h]);
         if (h == 1) tc_commit(&bars->v_empty[s]);  // both heads' P V of tile i
       }
@@ -655,23 +657,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
       issue_s(1, 0);
     }
     for (int i = 0; i < nt && ok; ++i) {
+      // V(i) and K(i + 1) land long before the softmax has written P(i) (their loads
+      // wait only for MMAs issued rounds ago): wait for them first, so that P V and
+      // S go out the moment P is in
+      if (!mbar_wait(&bars->v_full[i % kPSlots], (i / kPSlots) & 1) ||
+          (i + 1 < nt && !mbar_wait(&bars->k_full[(i + 1) % kPSlots], ((i + 1) / kPSlots) & 1))) {
+        ok = false;
+        break;
+      }
       for (int h = 0; h < 2; ++h) {
         // P_h(i) written (S_h(i) read) by the head's four softmax warps
-        if (!mbar_wait(&bars->p_full[h], i & 1) ||
-            (h == 0 && !mbar_wait(&bars->v_full[i % kPSlots], (i / kPSlots) & 1))) {
+        if (!mbar_wait(&bars->p_full[h], i & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
         issue_pv(h, i);
-        if (i + 1 < nt) {
-          if (h == 0 && !mbar_wait(&bars->k_full[(i + 1) % kPSlots], ((i + 1) / kPSlots) & 1)) {
-            ok = false;
-            break;
-          }
-          // after P_h V(i) in issue order, so P_h(i) is read before S_h(i + 1) overwrites it
-          issue_s(h, i + 1);
-        }
+        // after P_h V(i) in issue order, so P_h(i) is read before S_h(i + 1) overwrites it
+        if (i + 1 < nt) issue_s(h, i + 1);
       }
     }
     if (!ok) report_status(kDevTimeoutMma);
