@@ -725,11 +725,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
       const uint64_t sl2 = f2_make(sl, sl), nm2 = f2_make(-m_use, -m_use);
       uint64_t rs2 = f2_make(0.0f, 0.0f);
       mx = -INFINITY;
+      uint32_t vv[2][32];
+      tmem_ld_32x32b_x32(tS, vv[0]);
+      tmem_ld_32x32b_x32(tS + 32, vv[1]);
+      tc_wait_ld();
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tS + c * 32, v);
-        tc_wait_ld();
+        const uint32_t (&v)[32] = vv[c];
         const int k0 = j * kPKeys + c * 32;
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
