@@ -97,6 +97,14 @@ OMNI_DEVINL void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+OMNI_DEVINL void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 OMNI_DEVINL void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // 2^x by the PTX ex2.approx instruction (flush-to-zero; 2^-inf = +0).
 OMNI_DEVINL float ex2_approx(float x) {
@@ -452,20 +460,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
 //             and of V (one 16-row x 64-column box per lane) into three-slot K and V
 //             rings;
 //   warp 1    MMA issuer, in a fixed order: S_0(0), S_1(0), then per tile i
-//             P_0 V(i), S_0(i + 1), P_1 V(i), S_1(i + 1); each P V once the head's
-//             softmax has written P(i) and V(i) has landed, each S once K(i + 1) has;
+//             P_0 V(i), S_0(i + 1), P_1 V(i), S_1(i + 1); each half of a P V once the
+//             head's softmax has written that half of P(i), after V(i) and K(i + 1)
+//             have landed;
 //             P_h(i) sits over the first 32 of the head's S columns, and S_h(i + 1) is
 //             issued after P_h V(i), which reads it first (MMAs execute in order);
 //   warps 2-5 softmax of head 0, warps 6-9 of head 1: first copy their row of Q from
 //             the swizzled shared tile into TMEM; then per tile one thread per query
 //             row (TMEM lane) over the 64 columns, so a row's max and sum stay in one
-//             thread: P = exp2(s * scale * log2 e - m) against the running max m in one
-//             pass; the first tile and a tile whose max passes m by more than 2^8
-//             rescale O and the running sum and write P again -- for the whole warp when
-//             any of its rows must (the tcgen05.ld / st are warp-collective; the other
-//             rows keep their max, alpha = 1).  The completion of S_h(j) covers every
-//             MMA issued before it, P_h V(j - 1) included, so the softmax never waits
-//             for P V inside the loop.  One barrier arrival a warp.
+//             thread: the tile's max first; the first tile and a tile whose max passes
+//             the running max m by more than 2^8 rescale O and the running sum (the
+//             whole warp when any of its rows must: the tcgen05.ld / st are
+//             warp-collective; the other rows keep their max, alpha = 1); then P =
+//             exp2(s * scale * log2 e - m) 32 keys at a time, each half written over
+//             the S columns just read and handed to the MMA warp at once, so that its
+//             two P V k-steps run under the next half (13 % on the kernel against one
+//             hand-off a tile).  The completion of S_h(j) covers every MMA issued
+//             before it, P_h V(j - 1) included, so the softmax never waits for P V
+//             inside the loop.  One barrier arrival a warp.
 // Shared memory: Q 2 x 32 KB (read once into TMEM), K and V rings 3 x 16 KB each
 // (160 KB).  History at config 2 (TFLOP/s of causal QK^T + PV): one head a CTA with
 // 128-key tiles 409; two heads with 128-key tiles (one S buffer a head, softmax and MMAs
@@ -475,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_tc_kernel(
 // 3-input max and the bf16 pack by Veltkamp splitting 596; CTAs walking the tiles
 // heaviest-first (block_work) 623-642; the second head's P V interleaved with the first
 // head's S and one arrival a warp 633-672; Q in TMEM with the heads taking turns
-// (this layout) 697.  Measured slower: a polynomial exp2 on the FMA pipe for 4 to 16 of
+// (this layout) 697-702; P handed over in halves 851.  Measured slower: a polynomial exp2 on the FMA pipe for 4 to 16 of
 // every 32 keys (933-1 049 against 882 us; again with the packed forms, on the MMA
 // warp's sub-partition only: 10-13 % slower), twelve warps with setmaxnreg, lane 0
 // waiting for its warp (14 % slower than every thread polling), the page table read
@@ -505,7 +517,7 @@ OMNI_DEVINL void tc_mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc
 
 struct PairBars {
   uint64_t q_full, q_tmem, k_full[kPSlots], k_empty[kPSlots], v_full[kPSlots], v_empty[kPSlots];
-  uint64_t s_full[2], p_full[2], pv_done[2], drain;
+  uint64_t s_full[2], p_full[2][2], pv_done[2], drain;
   uint32_t tmem;
 };
 
@@ -562,7 +574,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(&bars->s_full[h], 1);
-      mbar_init(&bars->p_full[h], 4);  // one arrival per softmax warp of the head
+      mbar_init(&bars->p_full[h][0], 4);  // one arrival per softmax warp of the head
+      mbar_init(&bars->p_full[h][1], 4);
       mbar_init(&bars->pv_done[h], 1);
     }
     mbar_init(&bars->drain, 1);
@@ -636,17 +649,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
       }
       __syncwarp();
     };
-    // O_h += P_h(i) V_i: A = P_h(i) over the first 32 of the head's S columns
-    auto issue_pv = [&](int h, int i) {
+    // O_h += P_h(i) V_i, keys 32 * half .. + 31 (k-steps 2 * half, 2 * half + 1): A = P_h(i)
+    // over the first 32 of the head's S columns, 16 keys a k-step
+    auto issue_pv = [&](int h, int i, int half) {
       const int s = i % kPSlots;
       const uint64_t vd = desc_mn_sw128_64(smem + kPairVOff + s * kPTile);
       const uint32_t ta = tbase + 128 + h * 64, td = tbase + 256 + h * 128;
       if (leader) {
 #pragma unroll
-        for (int k = 0; k < kPKeys / 16; ++k)  // 16 keys a k-step: 16 rows of V, 2 KB on
+        for (int kk = 0; kk < 2; ++kk) {
+          const int k = 2 * half + kk;  // 16 rows of V, 2 KB on
           tc_mma_bf16_ts(td, ta + k * 8, vd + (uint64_t)((k * 16 * 128) >> 4), idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
-        if (i == nt - 1) tc_commit(&bars->pv_done[h]);
-        if (h == 1) tc_commit(&bars->v_empty[s]);  // both heads' P V of tile i
+        }
+        if (half == 1 && i == nt - 1) tc_commit(&bars->pv_done[h]);
+        if (half == 1 && h == 1) tc_commit(&bars->v_empty[s]);  // both heads' P V of tile i
       }
       __syncwarp();
     };
@@ -665,16 +681,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
         ok = false;
         break;
       }
-      for (int h = 0; h < 2; ++h) {
-        // P_h(i) written (S_h(i) read) by the head's four softmax warps
-        if (!mbar_wait(&bars->p_full[h], i & 1)) {
-          ok = false;
-          break;
+      for (int h = 0; h < 2 && ok; ++h) {
+        // each half of P_h(i) once the head's four softmax warps have written it (the
+        // first half after S_h(i) has been read)
+        for (int half = 0; half < 2; ++half) {
+          if (!mbar_wait(&bars->p_full[h][half], i & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(h, i, half);
         }
-        tc_fence_after();
-        issue_pv(h, i);
         // after P_h V(i) in issue order, so P_h(i) is read before S_h(i + 1) overwrites it
-        if (i + 1 < nt) issue_s(h, i + 1);
+        if (ok && i + 1 < nt) issue_s(h, i + 1);
       }
     }
     if (!ok) report_status(kDevTimeoutMma);
@@ -716,42 +735,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&bars->q_tmem);
-    // P = exp2(s * scale - m_use) of the row's 64 keys of tile j into pk (bf16 pairs,
-    // masked keys 0); returns their sum and the raw max score
-    // Key pairs go through the packed fp32x2 forms: one FMA for both arguments,
-    // one add into a two-lane row sum, one 3-input max and a 4-instruction bf16
-    // pack, so the issue slots per key stay below the ex2 unit's rate.
-    auto compute_p = [&](uint32_t tS, int j, bool masked, float& mx, uint32_t (&pk)[32]) -> float {
-      const uint64_t sl2 = f2_make(sl, sl), nm2 = f2_make(-m_use, -m_use);
-      uint64_t rs2 = f2_make(0.0f, 0.0f);
-      mx = -INFINITY;
-      uint32_t vv[2][32];
-      tmem_ld_32x32b_x32(tS, vv[0]);
-      tmem_ld_32x32b_x32(tS + 32, vv[1]);
-      tc_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const uint32_t (&v)[32] = vv[c];
-        const int k0 = j * kPKeys + c * 32;
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float a = __uint_as_float(v[e]), b = __uint_as_float(v[e + 1]);
-          if (masked) {
-            a = k0 + e <= lim ? a : -INFINITY;
-            b = k0 + e + 1 <= lim ? b : -INFINITY;
-          }
-          mx = fmax3(mx, a, b);
-          float ta, tb;
-          f2_split(f2_fma(f2_make(a, b), sl2, nm2), ta, tb);
-          const uint64_t pp = f2_make(ex2_approx(ta), ex2_approx(tb));
-          rs2 = f2_add(rs2, pp);
-          pk[c * 16 + (e >> 1)] = f2_to_bf2(pp);
-        }
-      }
-      float ra, rb;
-      f2_split(rs2, ra, rb);
-      return ra + rb;
-    };
     for (int j = 0; j < nt && ok; ++j) {
       // (every branch of this loop is warp-uniform: the tcgen05.ld / st below are
       // warp-collective)
@@ -763,29 +746,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
       // P V(j - 1) too, so O holds tiles < j and P(j - 1) has been read
       tc_fence_after();
       const bool masked = j * kPKeys + kPKeys - 1 > prefix + q0;
-      float mx, rs = 0.0f;
-      uint32_t pk[32];
-      if (j == 0) {  // m_use is -inf on every row until tile 0 (key 0 is visible to all rows)
+      // the row's 64 scores (keys past the diagonal -inf), and their max first
+      uint32_t vv[2][32];
+      tmem_ld_32x32b_x32(tS, vv[0]);
+      tmem_ld_32x32b_x32(tS + 32, vv[1]);
+      tc_wait_ld();
+      if (masked) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) pk[e] = 0u;  // a tile with no visible key leaves P zero
-        mx = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tS + c * 32, v);
-          tc_wait_ld();
-          const int k0 = j * kPKeys + c * 32;
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e)
-            if (!masked || k0 + e <= lim) mx = fmaxf(mx, __uint_as_float(v[e]));
-        }
-      } else {
-        rs = compute_p(tS, j, masked, mx, pk);
+            if (j * kPKeys + c * 32 + e > lim) vv[c][e] = __float_as_uint(-INFINITY);
       }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) mx = fmax3(mx, __uint_as_float(vv[c][e]), __uint_as_float(vv[c][e + 1]));
       const float m_tile = mx == -INFINITY ? -INFINITY : mx * sl;
       const bool resc = m_tile != -INFINITY && (m_use == -INFINITY || m_tile > m_use + kRescaleLog2);
       // the warp rescales if any of its rows must (the others with alpha = 1 and their
-      // running max kept, which rewrites the same P)
+      // running max kept)
       if (__any_sync(0xFFFFFFFFu, resc)) {
         const float alpha = !resc ? 1.0f : m_use == -INFINITY ? 0.0f : ex2_approx(m_use - m_tile);
         if (__any_sync(0xFFFFFFFFu, resc && j > 0 && l > 0.0f)) {
@@ -802,16 +783,34 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attention_pair_kernel(
         }
         l *= alpha;
         if (resc) m_use = m_tile;
-        float unused;
-        rs = compute_p(tS, j, masked, unused, pk);
       }
-      l += rs;
-      // P over the S columns this thread has read (their first 32)
-      tmem_st_32x32b_x32(tS, pk);
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[h]);  // one arrival a warp
+      // P = exp2(s * scale - m_use), 32 keys at a time over the S columns just read
+      // (bf16 pairs: 16 columns a half), each half handed to the MMA warp as soon as
+      // it is written so that its P V k-steps run under the next half.  Key pairs go
+      // through the packed fp32x2 forms: one FMA for both arguments, one add into a
+      // two-lane row sum and a 4-instruction bf16 pack.
+      const uint64_t sl2 = f2_make(sl, sl), nm2 = f2_make(-m_use, -m_use);
+      uint64_t rs2 = f2_make(0.0f, 0.0f);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float ta, tb;
+          f2_split(f2_fma(f2_make(__uint_as_float(vv[c][e]), __uint_as_float(vv[c][e + 1])), sl2, nm2), ta, tb);
+          const uint64_t pp = f2_make(ex2_approx(ta), ex2_approx(tb));
+          rs2 = f2_add(rs2, pp);
+          pk[e >> 1] = f2_to_bf2(pp);
+        }
+        tmem_st_32x32b_x16(tS + c * 16, pk);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->p_full[h][c]);  // one arrival a warp
+      }
+      float ra, rb;
+      f2_split(rs2, ra, rb);
+      l += ra + rb;
     }
     if (ok && nt > 0 && __all_sync(0xFFFFFFFFu, mbar_wait(&bars->pv_done[h], 0))) {
       tc_fence_after();
